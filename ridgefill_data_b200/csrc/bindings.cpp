@@ -1,0 +1,89 @@
+// Python bindings of the sm_100a kernels (torch tensors -> raw pointers + the current stream).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "gemm.h"
+#include "kernels.h"
+
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bf16")
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// One int32 error word per device: kernels with bounded waits record a code here on timeout.
+torch::Tensor& err_word(int dev) {
+  static std::vector<torch::Tensor> words(64);
+  if (!words[dev].defined())
+    words[dev] = torch::zeros({1}, torch::dtype(torch::kInt32).device(torch::kCUDA, dev));
+  return words[dev];
+}
+
+int* err_ptr(const torch::Tensor& like) { return err_word(like.get_device()).data_ptr<int>(); }
+
+torch::Tensor error_word(int64_t dev) { return err_word((int)dev); }
+
+// out = epilogue(A x B^T). A: [M, K] (a_mn: [K, M]); B: [N, K] (b_mn: [K, N]); leading stride of each
+// operand may exceed its logical width (row pitch = stride(0)).
+void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<torch::Tensor> bias,
+          c10::optional<torch::Tensor> residual, int64_t epi, int64_t bn, bool a_mn, bool b_mn, int64_t k_splits,
+          int64_t k_chunk, int64_t max_ctas) {
+  CHECK_CUDA(a); CHECK_CUDA(b); CHECK_CUDA(out);
+  CHECK_BF16(a); CHECK_BF16(b);
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm: 2-D operands");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1, "gemm: unit inner stride");
+  c10::cuda::CUDAGuard g(a.device());
+  rf::GemmOperands op;
+  op.A = a.data_ptr(); op.lda = a.stride(0); op.a_mn = a_mn;
+  op.B = b.data_ptr(); op.ldb = b.stride(0); op.b_mn = b_mn;
+  rf::GemmArgs args{};
+  args.M = (int)(a_mn ? a.size(1) : a.size(0));
+  args.K = (int)(a_mn ? a.size(0) : a.size(1));
+  args.N = (int)(b_mn ? b.size(1) : b.size(0));
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == args.K, "gemm: K mismatch");
+  args.k_splits = (int)k_splits;
+  args.k_chunk = (int)k_chunk;
+  args.out = out.data_ptr();
+  args.ldo = out.stride(0);
+  const int64_t out_cols = epi == rf::kEpiSwiGLU ? args.N / 2 : args.N;
+  TORCH_CHECK(out.size(0) == args.M && out.size(1) == out_cols, "gemm: output shape");
+  if (epi == rf::kEpiStore || epi == rf::kEpiSwiGLU) CHECK_BF16(out);
+  if (epi == rf::kEpiF32) TORCH_CHECK(out.scalar_type() == at::kFloat, "gemm: fp32 output");
+  if (epi == rf::kEpiF64Acc) TORCH_CHECK(out.scalar_type() == at::kDouble, "gemm: fp64 output");
+  bool vec = (reinterpret_cast<uintptr_t>(args.out) % 16 == 0) && ((args.ldo * out.element_size()) % 16 == 0);
+  if (bias.has_value()) {
+    CHECK_BF16(*bias);
+    TORCH_CHECK(bias->is_contiguous() && bias->numel() == args.N, "gemm: bias [N]");
+    args.bias = reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr());
+  }
+  if (residual.has_value()) {
+    CHECK_BF16(*residual);
+    TORCH_CHECK(residual->dim() == 2 && residual->stride(1) == 1 && residual->size(0) == args.M &&
+                    residual->size(1) == args.N, "gemm: residual [M, N]");
+    args.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    args.ldr = residual->stride(0);
+    vec = vec && (reinterpret_cast<uintptr_t>(args.residual) % 16 == 0) && ((args.ldr * 2) % 16 == 0);
+  }
+  args.vec_ok = vec ? 1 : 0;
+  args.err = err_ptr(a);
+  rf::gemm_bf16(op, args, (int)epi, (int)bn, (int)max_ctas, stream());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int64_t sm_count(int64_t dev) { return rf::num_sms((int)dev); }
+
+}  // namespace
+
+void register_ops(pybind11::module_& m);   // bind_ops.cpp
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "ridgefill_data_b200 sm_100a kernels";
+  m.def("error_word", &error_word);
+  m.def("sm_count", &sm_count);
+  m.def("gemm", &gemm, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("bias") = py::none(),
+        py::arg("residual") = py::none(), py::arg("epi") = 0, py::arg("bn") = 256, py::arg("a_mn") = false,
+        py::arg("b_mn") = false, py::arg("k_splits") = 1, py::arg("k_chunk") = 0, py::arg("max_ctas") = 0);
+  register_ops(m);
+}

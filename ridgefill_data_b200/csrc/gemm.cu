@@ -1,0 +1,437 @@
+// Persistent tcgen05 GEMM for sm_100a: C = A x B^T (+ epilogue), bf16 operands, fp32 TMEM accumulators.
+//
+// Roles per CTA (192 threads, one CTA per SM):
+//   warp 0      TMA producer: A/B tiles into a STAGES-deep shared-memory ring (128-byte swizzle)
+//   warp 1      TMEM owner + UMMA issuer: one elected lane issues tcgen05.mma (M=128, N=BN, K=16)
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32*(w%4)..+31), apply
+//               the epilogue and write global memory
+// Two TMEM accumulator buffers (2 x BN columns) let the epilogue of tile t overlap the MMAs of t+1.
+//
+// Operand majors: A is K-major ([M, K] row-major) or MN-major ([K, M] row-major); same for B
+// ([N, K] or [K, N]). The MN-major forms serve the ridge Gram X^T Y, which reads row-major
+// activations without a transpose.
+//
+// Epilogues: kEpiStore (bf16 out, optional bias[n] and residual[m, n]), kEpiSwiGLU (columns
+// [0, BN/2) of each tile are gate rows, [BN/2, BN) the matching up rows: out = silu(g) * u),
+// kEpiF32 (fp32 out), kEpiF64Acc (fp64 out += acc, split-K chunks added with atomics: the
+// fp32-per-block, fp64-across-blocks accumulation of the ridge sufficient statistics).
+#include "gemm.h"
+#include "ptx.cuh"
+
+#include <cudaTypedefs.h>
+#include <cstdio>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+namespace rf {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kGemmThreads = 192;
+constexpr int kGroupM = 16;   // rasterisation: consecutive tiles walk 16 M-blocks per N-block
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+};
+
+struct TileCoord {
+  int mb, nb, ks;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(int t, int num_mb, int num_nb, int k_splits) {
+  TileCoord c;
+  c.ks = t % k_splits;
+  int t2 = t / k_splits;
+  int per_group = kGroupM * num_nb;
+  int group = t2 / per_group;
+  int first = group * kGroupM;
+  int gsize = min(num_mb - first, kGroupM);
+  int r = t2 % per_group;
+  c.mb = first + r % gsize;
+  c.nb = r / gsize;
+  return c;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int BN, int EPI, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int num_mb = (args.M + BM - 1) / BM;
+  const int num_nb = (args.N + BN - 1) / BN;
+  const int num_tiles = num_mb * num_nb * args.k_splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      uint32_t issued = 0, last_par = 0;   // per stage: a load was issued / parity of its phase
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        TileCoord tc = tile_coord(t, num_mb, num_nb, args.k_splits);
+        const int k0 = tc.ks * args.k_chunk;
+        const int k1 = min(args.K, k0 + args.k_chunk);
+        const int nkb = (k1 - k0 + BK - 1) / BK;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1u, args.err, kErrTimeoutProducer)) {
+            ok = false;
+            *abort_flag = 1;
+            break;
+          }
+          issued |= 1u << stage;
+          last_par = (last_par & ~(1u << stage)) | (phase << stage);
+          mbar_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          uint8_t* sA = smem + stage * Cfg::STAGE_BYTES;
+          uint8_t* sB = sA + Cfg::A_BYTES;
+          const int kc = k0 + kb * BK;
+          if (!A_MN) {
+            tma_load_2d(sA, &tmA, &full[stage], kc, tc.mb * BM);
+          } else {
+#pragma unroll
+            for (int h = 0; h < BM / 64; ++h) tma_load_2d(sA + h * 8192, &tmA, &full[stage], tc.mb * BM + h * 64, kc);
+          }
+          if (!B_MN) {
+            tma_load_2d(sB, &tmB, &full[stage], kc, tc.nb * BN);
+          } else {
+#pragma unroll
+            for (int h = 0; h < BN / 64; ++h) tma_load_2d(sB + h * 8192, &tmB, &full[stage], tc.nb * BN + h * 64, kc);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: the last load issued into every stage must land before the CTA may exit.
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) mbar_wait(&full[s], (last_par >> s) & 1u, args.err, kErrTimeoutDrain);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ UMMA issuer
+    uint32_t stage = 0, phase = 0;
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+      TileCoord tc = tile_coord(t, num_mb, num_nb, args.k_splits);
+      const int k0 = tc.ks * args.k_chunk;
+      const int k1 = min(args.K, k0 + args.k_chunk);
+      const int nkb = (k1 - k0 + BK - 1) / BK;
+      const uint32_t buf = it & 1;
+      const uint32_t aphase = (it >> 1) & 1;
+      if (*abort_flag || !mbar_wait(&tempty[buf], aphase ^ 1u, args.err, kErrTimeoutMma)) {
+        ok = false;
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * BN;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (*abort_flag || !mbar_wait(&full[stage], phase, args.err, kErrTimeoutMma)) {
+          ok = false;
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a_addr + k * 2048, 8192, 1024) : sdesc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b_addr + k * 2048, 8192, 1024) : sdesc_sw128(b_addr + k * 32, 16, 1024);
+            umma_f16(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (lane == 0) umma_commit(&tfull[buf]);
+      __syncwarp();
+    }
+    if (!ok) {
+      // Wait (bounded) for MMAs already issued before TMEM is released.
+      if (lane == 0) umma_commit(&tfull[0]);
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      TileCoord tc = tile_coord(t, num_mb, num_nb, args.k_splits);
+      const uint32_t buf = it & 1;
+      const uint32_t aphase = (it >> 1) & 1;
+      if (*abort_flag || !mbar_wait(&tfull[buf], aphase, args.err, kErrTimeoutEpilogue)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = tc.mb * BM + row_in_tile;
+      const bool row_ok = row < args.M;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * BN;
+
+      if constexpr (EPI == kEpiSwiGLU) {
+        constexpr int HALF = BN / 2;
+        const int ncols_out = args.N / 2;
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+#pragma unroll 1
+        for (int c = 0; c < HALF; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tbase + c, g);
+          tmem_ld32(tbase + HALF + c, u);
+          tmem_wait_ld();
+          const int col0 = tc.nb * HALF + c;
+          if (row_ok) {
+            __nv_bfloat16* dst = out + (size_t)row * args.ldo + col0;
+            if (col0 + 32 <= ncols_out && args.vec_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 v;
+                v.x = pack_bf16x2(silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]),
+                                  silu_f(__uint_as_float(g[j + 1])) * __uint_as_float(u[j + 1]));
+                v.y = pack_bf16x2(silu_f(__uint_as_float(g[j + 2])) * __uint_as_float(u[j + 2]),
+                                  silu_f(__uint_as_float(g[j + 3])) * __uint_as_float(u[j + 3]));
+                v.z = pack_bf16x2(silu_f(__uint_as_float(g[j + 4])) * __uint_as_float(u[j + 4]),
+                                  silu_f(__uint_as_float(g[j + 5])) * __uint_as_float(u[j + 5]));
+                v.w = pack_bf16x2(silu_f(__uint_as_float(g[j + 6])) * __uint_as_float(u[j + 6]),
+                                  silu_f(__uint_as_float(g[j + 7])) * __uint_as_float(u[j + 7]));
+                *reinterpret_cast<uint4*>(dst + j) = v;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < ncols_out)
+                  dst[j] = __float2bfloat16(silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]));
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c, r);
+          tmem_wait_ld();
+          const int col0 = tc.nb * BN + c;
+          if (!row_ok || col0 >= args.N) continue;
+          const bool full_chunk = (col0 + 32 <= args.N);
+          if constexpr (EPI == kEpiStore) {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col0;
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            if (args.bias != nullptr) {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.N) v[j] += __bfloat162float(args.bias[col0 + j]);
+            }
+            if (args.residual != nullptr) {
+              const __nv_bfloat16* res = args.residual + (size_t)row * args.ldr + col0;
+              if (full_chunk && args.vec_ok) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                  uint4 w = *reinterpret_cast<const uint4*>(res + j);
+                  v[j] += bf16_lo(w.x); v[j + 1] += bf16_hi(w.x);
+                  v[j + 2] += bf16_lo(w.y); v[j + 3] += bf16_hi(w.y);
+                  v[j + 4] += bf16_lo(w.z); v[j + 5] += bf16_hi(w.z);
+                  v[j + 6] += bf16_lo(w.w); v[j + 7] += bf16_hi(w.w);
+                }
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (col0 + j < args.N) v[j] += __bfloat162float(res[j]);
+              }
+            }
+            if (full_chunk && args.vec_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 w;
+                w.x = pack_bf16x2(v[j], v[j + 1]);
+                w.y = pack_bf16x2(v[j + 2], v[j + 3]);
+                w.z = pack_bf16x2(v[j + 4], v[j + 5]);
+                w.w = pack_bf16x2(v[j + 6], v[j + 7]);
+                *reinterpret_cast<uint4*>(dst + j) = w;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.N) dst[j] = __float2bfloat16(v[j]);
+            }
+          } else if constexpr (EPI == kEpiF32) {
+            float* dst = reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + col0;
+            if (full_chunk && args.vec_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<uint4*>(dst + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.N) dst[j] = __uint_as_float(r[j]);
+            }
+          } else {  // kEpiF64Acc
+            double* dst = reinterpret_cast<double*>(args.out) + (size_t)row * args.ldo + col0;
+            if (args.k_splits == 1) {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.N) dst[j] += (double)__uint_as_float(r[j]);
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.N) atomicAdd(dst + j, (double)__uint_as_float(r[j]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ============================================================================== host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || p == nullptr)
+      throw std::runtime_error("cuTensorMapEncodeTiled entry point unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix [outer, inner] with row pitch `pitch_elems`.
+CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t pitch_elems,
+                              uint32_t box_inner, uint32_t box_outer) {
+  CUtensorMap tm;
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) throw std::runtime_error("TMA base must be 16-byte aligned");
+  if ((pitch_elems * 2) % 16 != 0) throw std::runtime_error("TMA row pitch must be a multiple of 16 bytes");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch_elems * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return tm;
+}
+
+int num_sms(int device) {
+  static int cached[64] = {0};
+  if (device < 0 || device >= 64) return 148;
+  if (cached[device] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
+    cached[device] = v > 0 ? v : 148;
+  }
+  return cached[device];
+}
+
+template <int BN, int EPI, bool A_MN, bool B_MN>
+static void launch_gemm(const GemmOperands& op, GemmArgs args, int max_ctas, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  auto kernel = gemm_kernel<BN, EPI, A_MN, B_MN>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    attr_set[dev & 63] = true;
+  }
+  CUtensorMap ta = A_MN ? make_tmap_bf16_2d(op.A, args.M, args.K, op.lda, 64, 64)
+                        : make_tmap_bf16_2d(op.A, args.K, args.M, op.lda, 64, BM);
+  CUtensorMap tb = B_MN ? make_tmap_bf16_2d(op.B, args.N, args.K, op.ldb, 64, 64)
+                        : make_tmap_bf16_2d(op.B, args.K, args.N, op.ldb, 64, BN);
+  const int num_tiles = ((args.M + BM - 1) / BM) * ((args.N + BN - 1) / BN) * args.k_splits;
+  int ctas = num_sms(dev);
+  if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
+  if (num_tiles < ctas) ctas = num_tiles;
+  if (ctas <= 0) return;
+  kernel<<<ctas, kGemmThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, args);
+}
+
+void gemm_bf16(const GemmOperands& op, GemmArgs args, int epi, int bn, int max_ctas, cudaStream_t stream) {
+  if (args.M <= 0 || args.N <= 0 || args.K <= 0) return;
+  if (args.k_splits <= 0) args.k_splits = 1;
+  if (args.k_chunk <= 0 || args.k_splits == 1) args.k_chunk = args.K;
+  if (args.k_splits > 1 && args.k_chunk % BK != 0) throw std::runtime_error("split-K chunk must be a multiple of 64");
+  if (epi == kEpiSwiGLU && (args.N % bn != 0)) throw std::runtime_error("SwiGLU GEMM needs N % BN == 0");
+  if (epi != kEpiF64Acc && args.k_splits != 1) throw std::runtime_error("split-K only with the fp64 epilogue");
+#define RF_GEMM_CASE(BN_, EPI_, AM_, BMJ_)                                               \
+  if (bn == BN_ && epi == EPI_ && op.a_mn == AM_ && op.b_mn == BMJ_) {                   \
+    launch_gemm<BN_, EPI_, AM_, BMJ_>(op, args, max_ctas, stream);                       \
+    return;                                                                              \
+  }
+  RF_GEMM_CASE(256, kEpiStore, false, false)
+  RF_GEMM_CASE(128, kEpiStore, false, false)
+  RF_GEMM_CASE(256, kEpiSwiGLU, false, false)
+  RF_GEMM_CASE(128, kEpiSwiGLU, false, false)
+  RF_GEMM_CASE(256, kEpiF32, false, false)
+  RF_GEMM_CASE(128, kEpiF32, false, false)
+  RF_GEMM_CASE(256, kEpiF64Acc, true, true)
+  RF_GEMM_CASE(128, kEpiF64Acc, true, true)
+  RF_GEMM_CASE(256, kEpiF64Acc, false, false)
+  RF_GEMM_CASE(256, kEpiStore, true, true)
+#undef RF_GEMM_CASE
+  throw std::runtime_error("gemm_bf16: unsupported (bn, epilogue, majors) combination");
+}
+
+}  // namespace rf

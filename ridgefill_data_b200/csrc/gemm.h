@@ -1,0 +1,39 @@
+// tcgen05 GEMM interface (see gemm.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace rf {
+
+enum GemmEpilogue : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiF32 = 2, kEpiF64Acc = 3 };
+
+struct GemmOperands {
+  const void* A;   // bf16; [M, K] (K-major) or [K, M] (MN-major), row pitch lda elements
+  long lda;
+  bool a_mn;
+  const void* B;   // bf16; [N, K] (K-major) or [K, N] (MN-major), row pitch ldb elements
+  long ldb;
+  bool b_mn;
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int k_splits;                     // split-K chunks (fp64 epilogue only); 1 otherwise
+  int k_chunk;                      // K elements per chunk (multiple of 64)
+  void* out;                        // bf16 / fp32 / fp64 by epilogue
+  long ldo;                         // output row pitch in elements
+  const __nv_bfloat16* bias;        // [N] or nullptr (kEpiStore)
+  const __nv_bfloat16* residual;    // [M, N] or nullptr (kEpiStore); may alias out
+  long ldr;
+  int vec_ok;                       // out/residual pitches and bases allow 16-byte vector access
+  int* err;                         // device error word (bounded waits), may be nullptr
+};
+
+void gemm_bf16(const GemmOperands& op, GemmArgs args, int epi, int bn, int max_ctas, cudaStream_t stream);
+CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t pitch_elems,
+                              uint32_t box_inner, uint32_t box_outer);
+int num_sms(int device);
+
+}  // namespace rf

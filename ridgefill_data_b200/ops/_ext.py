@@ -1,0 +1,46 @@
+"""Loads the in-tree sm_100a extension (ridgefill_data_b200/_C*.so, built by `python setup.py
+build_ext --inplace` or __graft_entry__.build()).
+
+There is no fallback: on a machine with a CUDA device, a missing or stale extension raises at
+first use, so a GPU run can never silently take a slower PyTorch path."""
+import importlib
+
+_mod = None
+_err = None
+
+
+class ExtensionMissing(RuntimeError):
+    pass
+
+
+def ext():
+    global _mod, _err
+    if _mod is not None:
+        return _mod
+    try:
+        _mod = importlib.import_module("ridgefill_data_b200._C")
+    except ImportError as e:  # pragma: no cover - depends on the build
+        _err = e
+        raise ExtensionMissing(
+            "the sm_100a extension ridgefill_data_b200._C is not built; run `python setup.py build_ext --inplace`"
+        ) from e
+    return _mod
+
+
+def available():
+    try:
+        ext()
+        return True
+    except ExtensionMissing:
+        return False
+
+
+def check_errors(device=None):
+    """Raise if any kernel recorded a bounded-wait timeout in the device error word; clears it."""
+    import torch
+    dev = torch.cuda.current_device() if device is None else torch.device(device).index or 0
+    w = ext().error_word(dev)
+    code = int(w.item())
+    if code:
+        w.zero_()
+        raise RuntimeError(f"sm_100a kernel reported error code {code} (bounded wait timed out)")

@@ -1,0 +1,81 @@
+"""tcgen05 GEMM vs a plain PyTorch fp32 reference of the same op."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(x, w):
+    return x.float() @ w.float().T
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 512), (1000, 384, 200), (37, 4096, 4096),
+                                   (4096, 4096, 4096), (300, 128, 1024)])
+def test_linear(m, n, k):
+    from ridgefill_data_b200.ops import gemm
+    torch.manual_seed(0)
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05
+    got = gemm.linear(x, w).float()
+    ref = _ref(x, w)
+    err = (got - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, err
+
+
+def test_linear_bias_residual_inplace():
+    from ridgefill_data_b200.ops import gemm
+    torch.manual_seed(1)
+    m, n, k = 513, 768, 320
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05
+    b = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+    h = torch.randn(m, n, device="cuda", dtype=torch.bfloat16)
+    ref = _ref(x, w) + b.float() + h.float()
+    gemm.linear(x, w, bias=b, residual=h, out=h)
+    err = (h.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-2, err
+
+
+def test_linear_bn128_and_f32():
+    from ridgefill_data_b200.ops import gemm
+    torch.manual_seed(2)
+    x = torch.randn(640, 512, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(200, 512, device="cuda", dtype=torch.bfloat16)
+    ref = _ref(x, w)
+    got = gemm.linear_f32(x, w, bn=128)
+    assert torch.allclose(got, ref, rtol=1e-4, atol=1e-2)
+    got16 = gemm.linear(x, w, bn=128).float()
+    assert (got16 - ref).abs().max().item() / ref.abs().max().item() < 1e-2
+
+
+def test_swiglu():
+    from ridgefill_data_b200.ops import gemm
+    torch.manual_seed(3)
+    m, f, k = 700, 512, 256
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    g = torch.randn(f, k, device="cuda", dtype=torch.bfloat16) * 0.1
+    u = torch.randn(f, k, device="cuda", dtype=torch.bfloat16) * 0.1
+    got = gemm.swiglu_linear(x, gemm.pack_gate_up(g, u)).float()
+    gr, ur = _ref(x, g), _ref(x, u)
+    ref = torch.nn.functional.silu(gr) * ur
+    assert (got - ref).abs().max().item() / ref.abs().max().item() < 1e-2
+
+
+def test_gram_fp64_split_k():
+    from ridgefill_data_b200.ops import gemm
+    torch.manual_seed(4)
+    n, dx, dy = 5000, 384, 256
+    x = torch.randn(n, dx, device="cuda", dtype=torch.bfloat16)
+    y = torch.randn(n, dy, device="cuda", dtype=torch.bfloat16)
+    acc = torch.zeros(dx, dy, device="cuda", dtype=torch.float64)
+    gemm.gram_acc(acc, x, y, k_chunk=1024)
+    ref = x.double().T @ y.double()
+    assert (acc - ref).abs().max().item() < 1e-3 * ref.abs().max().item()
+    gemm.gram_acc(acc, x, y, k_chunk=8192)
+    assert (acc - 2 * ref).abs().max().item() < 2e-3 * ref.abs().max().item()
+
+
+def test_no_error_recorded():
+    from ridgefill_data_b200.ops._ext import check_errors
+    torch.cuda.synchronize()
+    check_errors()
