@@ -1,0 +1,96 @@
+"""Arm: one prefill configuration (code/kva/kva.py:79-118 semantics).
+
+Fills of a late layer's prefix rows [0, P) (P = N - tail):
+  exact           no approximation (P = 0)
+  proj            ridge projector x_i = W_i b + c_i (b = the row's split-layer input)
+  identity        x_i = b for every late layer
+  none            prefix rows never reach the layer (plain layer skip)
+  oracle          the true layer inputs (all rows: reproduces exact prefill; a diagnostic)
+  swiftkv         SwiftKV's distilled K/V for prefix rows; tail and decode exact
+  swiftkv_native  SwiftKV as released: every row's late K/V from SwiftKV, queries through q_proj_swiftkv
+  kvfold          attention layers' pre-RoPE K/V straight from the unit-RMS boundary state
+  by_type         fill_by_type = {'attention': f, 'gdn': g}
+Options: st (terminal-state corrections {layer: dS} added after a GDN layer's prefix fill), f1 (row 0 uses
+its exact late inputs), context (projector input [b, c_{S-1}, .., c_{S-K}]), refresh (run layer R in full on
+the filled prefix rows, then a refresh projector of split R+1), tail_bias_from / tail_bias_skip_last (the
+tail's mean projector residual added to prefix fills), exact_part ('k' | 'v' from the true inputs),
+rescale (knorm | kdir | vnorm oracle, ktail | vtail deployable) with rescale_skip_last, tail_from
+('continuation': the tail is the scored rows).
+"""
+from __future__ import annotations
+
+import dataclasses
+from dataclasses import dataclass, field
+
+ORACLE_RESCALE = ("knorm", "kdir", "vnorm")
+TAIL_RESCALE = ("ktail", "vtail")
+FILLS = ("exact", "proj", "identity", "none", "oracle", "swiftkv", "swiftkv_native", "kvfold", "by_type")
+ENGINE_MIN_TAIL = 512   # a block-granular engine never runs a shorter exact tail
+
+
+@dataclass
+class Arm:
+    name: str
+    split: int | None = None
+    tail: int = 0
+    fill: str = "exact"
+    projector: object = None
+    st: dict | None = None
+    f1: bool = False
+    fill_by_type: dict | None = None
+    kvfold: object = None
+    context: int = 0
+    refresh: int | None = None
+    refresh_projector: object = None
+    tail_bias_from: int | None = None
+    tail_bias_skip_last: int = 0
+    exact_part: str | None = None
+    rescale: str | None = None
+    rescale_skip_last: int = 0
+    tail_from: str | None = None
+    meta: dict = field(default_factory=dict)
+
+    def __post_init__(self):
+        if self.fill not in FILLS:
+            raise ValueError(f"fill {self.fill!r} (one of {FILLS})")
+        if self.fill_by_type is not None:
+            self.fill = "by_type"
+
+    def prefix_len(self, n):
+        if self.fill == "exact":
+            return 0
+        if self.fill == "swiftkv_native":
+            return n
+        return max(0, n - self.tail)
+
+    def fill_of(self, layer_type):
+        if self.fill_by_type is None:
+            return self.fill
+        return self.fill_by_type["attention" if layer_type == "attn" else layer_type]
+
+    def uses(self, fill):
+        return fill in (self.fill_by_type.values() if self.fill_by_type else (self.fill,))
+
+    def uses_oracle(self):
+        return self.uses("oracle") or self.exact_part is not None or self.rescale in ORACLE_RESCALE
+
+
+def pop_split(n_layers):
+    """POP's split: prefill prunes the last floor(L / 3) layers, S = L - floor(L / 3)."""
+    return n_layers - n_layers // 3
+
+
+def rounded_tail(n, base, block):
+    """Tail length when the prefix boundary is rounded down to a block multiple (tail >= base)."""
+    return n - max(0, (n - base) // block * block)
+
+
+def exclude_scored(arm, scored):
+    """The arm with its tail statistics (ktail / vtail scale, tail bias) kept off the last `scored` rows."""
+    if scored <= 0:
+        return arm
+    if arm.rescale in TAIL_RESCALE and arm.rescale_skip_last < scored:
+        arm = dataclasses.replace(arm, rescale_skip_last=scored)
+    if arm.tail_bias_from is not None and arm.tail_bias_skip_last < scored:
+        arm = dataclasses.replace(arm, tail_bias_skip_last=scored)
+    return arm

@@ -1,0 +1,138 @@
+"""Shifted sufficient statistics of the ridge regressions x -> y_i (code/kva/ridge.py:19-75).
+
+For boundary rows x [n, d] and each late layer's true inputs y_i [n, d]:
+  n, sx = sum(x - cx), sxx = sum((x - cx)(x - cx)^T), sy_i = sum(y_i - cy_i), sxy_i = sum((x - cx)(y_i - cy_i)^T)
+with fixed shifts cx, cy_i (the first block's means) for numerical stability. Products are summed in
+fp32 within row blocks and the blocks added into fp64 accumulators.
+
+On a CUDA device the products run on the tcgen05 Gram kernel: the centred rows are split as
+hi + lo (two bf16 terms, ~16 mantissa bits) and X^T Y is accumulated as hi^T hi + hi^T lo + lo^T hi
+in one MN-major GEMM over the concatenated rows, fp32 per k-chunk and fp64 across chunks
+(ops.gemm.gram_acc). On the CPU the products are plain fp32 matmuls.
+
+Row weights: add(..., w) makes every sum weighted (n holds sum(w)); w=None is unweighted.
+"""
+from __future__ import annotations
+
+import torch
+
+BLOCK = 8192
+
+
+def split_bf16(xc):
+    """fp32 rows -> (hi, lo) bf16 with hi + lo ~= xc to ~2^-16 relative."""
+    hi = xc.to(torch.bfloat16)
+    lo = (xc - hi.float()).to(torch.bfloat16)
+    return hi, lo
+
+
+def cross_acc(acc, a, b, block=BLOCK):
+    """acc [da, db] fp64 += a^T b for fp32 rows a [n, da], b [n, db]."""
+    if a.is_cuda:
+        from ..ops import gemm
+        ah, al = split_bf16(a)
+        if b is a:
+            bh, bl = ah, al
+        else:
+            bh, bl = split_bf16(b)
+        lhs = torch.cat((ah, ah, al), 0)
+        rhs = torch.cat((bh, bl, bh), 0)
+        if acc.is_cuda and acc.is_contiguous():
+            gemm.gram_acc(acc, lhs, rhs, k_chunk=block)
+        else:
+            tmp = torch.zeros(acc.shape, dtype=torch.float64, device=a.device)
+            gemm.gram_acc(tmp, lhs, rhs, k_chunk=block)
+            acc += tmp.to(acc.device)
+        return acc
+    acc += (a.T @ b).to(acc.device, torch.float64)
+    return acc
+
+
+class RidgeStats:
+    """Accumulators for one split over its late layers (fp64, on `device`)."""
+
+    def __init__(self, split, layers, dim, device="cpu", out_dim=None):
+        self.split, self.layers, self.dim, self.device = split, list(layers), dim, torch.device(device)
+        out_dim = dim if out_dim is None else out_dim
+        f64 = dict(dtype=torch.float64, device=self.device)
+        self.n = 0.0
+        self.cx = None
+        self.cy = {}
+        self.sx = torch.zeros(dim, **f64)
+        self.sxx = torch.zeros(dim, dim, **f64)
+        self.sy = {i: torch.zeros(out_dim, **f64) for i in self.layers}
+        self.sxy = {i: torch.zeros(dim, out_dim, **f64) for i in self.layers}
+        self._x = None
+
+    @torch.no_grad()
+    def begin(self, x, block=BLOCK, w=None):
+        """Boundary rows x [n, d] of one document; follow with add_layer for every layer."""
+        if self.cx is None:
+            self.cx = x[:block].float().mean(0)
+        self._x, self._block = x, block
+        self._w = None if w is None else w.to(x.device, torch.float32)[:, None]
+        self.n += x.shape[0] if w is None else float(w.double().sum())
+        for r in range(0, x.shape[0], block):
+            xc = x[r:r + block].float() - self.cx.to(x.device)
+            xw = xc if self._w is None else xc * self._w[r:r + xc.shape[0]]
+            self.sx += xw.sum(0).double().to(self.device)
+            cross_acc(self.sxx, xw, xc, block)
+
+    @torch.no_grad()
+    def add_layer(self, i, y):
+        if i not in self.cy:
+            self.cy[i] = y[:self._block].float().mean(0)
+        for r in range(0, y.shape[0], self._block):
+            xc = self._x[r:r + self._block].float() - self.cx.to(y.device)
+            xw = xc if self._w is None else xc * self._w[r:r + xc.shape[0]]
+            yc = y[r:r + self._block].float() - self.cy[i].to(y.device)
+            yw = yc if self._w is None else yc * self._w[r:r + yc.shape[0]]
+            self.sy[i] += yw.sum(0).double().to(self.device)
+            cross_acc(self.sxy[i], xw, yc, self._block)
+
+    def add(self, x, ys, block=BLOCK, w=None):
+        self.begin(x, block, w)
+        for i in self.layers:
+            self.add_layer(i, ys[i])
+
+    def state(self):
+        cpu = lambda t: t.detach().cpu()  # noqa: E731
+        return dict(split=self.split, layers=self.layers, dim=self.dim, n=self.n, cx=cpu(self.cx).double(),
+                    cy={i: cpu(v).double() for i, v in self.cy.items()}, sx=cpu(self.sx), sxx=cpu(self.sxx),
+                    sy={i: cpu(v) for i, v in self.sy.items()}, sxy={i: cpu(v) for i, v in self.sxy.items()})
+
+
+def residual(state):
+    """Statistics of the target y - x (ridge towards the identity map): shifts cy - cx, sums sy - sx,
+    sxy - sxx (code/kva/ridge.py:134-139)."""
+    sx, sxx = state["sx"].double(), state["sxx"].double()
+    return dict(state, sx=sx, sxx=sxx, cy={i: state["cy"][i] - state["cx"] for i in state["layers"]},
+                sy={i: state["sy"][i].double() - sx for i in state["layers"]},
+                sxy={i: state["sxy"][i].double() - sxx for i in state["layers"]})
+
+
+def combine(a, b, w=1.0):
+    """Statistics of a's rows plus w times b's rows, b re-expressed about a's shifts
+    (code/kva/ridge.py:142-156). Both are state() dicts over the same split and layers."""
+    d = b["cx"] - a["cx"]
+    out = dict(a, n=a["n"] + w * b["n"])
+    sxb = b["sx"] + b["n"] * d
+    out["sx"] = a["sx"] + w * sxb
+    out["sxx"] = a["sxx"] + w * (b["sxx"] + torch.outer(b["sx"], d) + torch.outer(d, b["sx"])
+                                 + b["n"] * torch.outer(d, d))
+    out["sy"], out["sxy"] = {}, {}
+    for i in a["layers"]:
+        e = b["cy"][i] - a["cy"][i]
+        out["sy"][i] = a["sy"][i] + w * (b["sy"][i] + b["n"] * e)
+        out["sxy"][i] = a["sxy"][i] + w * (b["sxy"][i] + torch.outer(b["sx"], e) + torch.outer(d, b["sy"][i])
+                                           + b["n"] * torch.outer(d, e))
+    return out
+
+
+def raw_moments(state, i):
+    """Uncentred sum(x x^T) and sum(x y_i^T) (fp64) reconstructed from the shifted sums."""
+    n, cx, sx = state["n"], state["cx"].double(), state["sx"].double()
+    cy, sy = state["cy"][i].double(), state["sy"][i].double()
+    xx = state["sxx"].double() + torch.outer(sx, cx) + torch.outer(cx, sx) + n * torch.outer(cx, cx)
+    xy = state["sxy"][i].double() + torch.outer(sx, cy) + torch.outer(cx, sy) + n * torch.outer(cx, cy)
+    return xx, xy

@@ -1,0 +1,111 @@
+"""Ridge statistics and fits: shifted sums vs naive sums, eigen vs Cholesky vs a direct solve,
+residual/combine identities, the plain (uncentred) form, map file format."""
+import pytest
+import torch
+
+from ridgefill_data_b200.ridge import fit as rfit
+from ridgefill_data_b200.ridge import projector as rp
+from ridgefill_data_b200.ridge.stats import RidgeStats, combine, raw_moments, residual
+
+
+def _data(n=300, d=12, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(n, d, generator=g) * 2 + 5
+    ys = {i: x @ torch.randn(d, d, generator=g) * 0.3 + torch.randn(n, d, generator=g) * 0.1 + i
+          for i in (3, 4)}
+    return x, ys
+
+
+def test_stats_match_naive_sums():
+    x, ys = _data()
+    st = RidgeStats(3, [3, 4], 12)
+    st.add(x[:100], {i: y[:100] for i, y in ys.items()}, block=64)
+    st.add(x[100:], {i: y[100:] for i, y in ys.items()}, block=64)
+    s = st.state()
+    xx, xy = raw_moments(s, 4)
+    assert torch.allclose(xx, x.double().T @ x.double(), rtol=1e-5)
+    assert torch.allclose(xy, x.double().T @ ys[4].double(), rtol=1e-5)
+
+
+def test_eigen_matches_cholesky_and_direct():
+    x, ys = _data()
+    st = RidgeStats(3, [3, 4], 12)
+    st.add(x, ys)
+    s = st.state()
+    lam = 0.03
+    e = rfit.EigenFit(s).layer(4, [lam])[lam]
+    c = rfit.CholeskyFit(s).layer(4, [lam])[lam]
+    xd, yd = x.double(), ys[4].double()
+    xc, yc = xd - xd.mean(0), yd - yd.mean(0)
+    cxx = xc.T @ xc
+    w = torch.linalg.solve(cxx + lam * cxx.diagonal().mean() * torch.eye(12, dtype=torch.float64), xc.T @ yc)
+    b = yd.mean(0) - xd.mean(0) @ w
+    for got in (e, c):
+        assert torch.allclose(got[0].double(), w.T, atol=1e-4)
+        assert torch.allclose(got[1].double(), b, atol=1e-3)
+
+
+def test_plain_form_uncentred():
+    x, ys = _data()
+    st = RidgeStats(3, [3, 4], 12)
+    st.add(x, ys)
+    s = st.state()
+    xd, yd = x.double(), ys[3].double()
+    xtx = xd.T @ xd
+    lam = 1e-2
+    w = torch.linalg.solve(xtx + lam * xtx.trace() / 12 * torch.eye(12, dtype=torch.float64), xd.T @ yd)
+    for cls in (rfit.EigenFit, rfit.CholeskyFit):
+        got_w, got_b = cls(s, center=False).layer(3, [lam])[lam]
+        assert torch.allclose(got_w.double(), w.T, atol=1e-4) and float(got_b.abs().max()) == 0.0
+
+
+def test_residual_and_combine():
+    x, ys = _data()
+    a = RidgeStats(3, [3, 4], 12)
+    a.add(x[:150], {i: y[:150] for i, y in ys.items()})
+    b = RidgeStats(3, [3, 4], 12)
+    b.add(x[150:], {i: y[150:] for i, y in ys.items()})
+    full = RidgeStats(3, [3, 4], 12)
+    full.add(x, ys)
+    c = combine(a.state(), b.state(), 1.0)
+    for i in (3, 4):
+        ref = raw_moments(full.state(), i)[1]
+        assert (raw_moments(c, i)[1] - ref).abs().max() < 1e-6 * ref.abs().max()
+    r = residual(full.state())
+    xy = raw_moments(r, 4)[1]
+    ref = x.double().T @ (ys[4] - x).double()
+    assert (xy - ref).abs().max() < 1e-6 * ref.abs().max()
+
+
+def test_projector_roundtrip_and_refusals(tmp_path):
+    W = {5: torch.randn(8, 8), 6: torch.randn(8, 8)}
+    B = {5: torch.randn(8), 6: torch.randn(8)}
+    p = rp.Projector(5, W, B)
+    path = tmp_path / "m.safetensors"
+    p.save(path, dict(model="t", lam=0.03, rows=10))
+    assert rp.meta_of(path)["split"] == "5" and rp.meta_of(path)["rows"] == "10"
+    q = rp.Projector.load(path, dtype=torch.float32)
+    assert q.split == 5 and torch.allclose(q.W[6], W[6].bfloat16().float())
+    bad = rp.Projector(5, {5: torch.full((2, 2), 2e4)}, {5: torch.zeros(2)})
+    with pytest.raises(ValueError):
+        bad.save(tmp_path / "bad.safetensors", {})
+    from ridgefill_data_b200.utils.integrity import IntegrityError
+    with pytest.raises(IntegrityError):
+        rp.Projector.load(path, sha256="0" * 64)
+
+
+def test_i8_roundtrip(tmp_path):
+    from safetensors.torch import save_file
+    w = torch.randn(16, 256) * 0.05
+    b = torch.randn(16)
+    codes, scale, bias = rp.quant_i8(w, b)
+    save_file({"proj.7.codes": codes, "proj.7.scale": scale, "proj.7.bias": bias}, str(tmp_path / "p7.safetensors"))
+    p = rp.Projector.load_i8({7: tmp_path / "p7.safetensors"}, split=7, dtype=torch.float32)
+    assert (p.W[7] - w).abs().max() < 2e-3
+
+
+def test_st_roundtrip(tmp_path):
+    st = {9: torch.randn(4, 8, 6)}
+    rp.save_st(tmp_path / "c.safetensors", st)
+    got = rp.load_st(tmp_path / "c.safetensors")
+    assert torch.equal(got[9], st[9])
