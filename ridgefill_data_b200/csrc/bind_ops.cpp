@@ -1,8 +1,235 @@
-// Python bindings of the non-GEMM kernels (kernels.h).
+// Python bindings of the non-GEMM kernels (kernels.h). Tensors are checked for device, dtype and the
+// contiguity each kernel assumes; strides that kernels take explicitly are passed from Python.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
 #include "kernels.h"
 
-void register_ops(pybind11::module_& m) { (void)m; }
+namespace {
+
+using at::Tensor;
+using OptT = c10::optional<Tensor>;
+
+cudaStream_t cur() { return at::cuda::getCurrentCUDAStream().stream(); }
+const __nv_bfloat16* cbf(const Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); }
+__nv_bfloat16* bf(const Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+
+void need(const Tensor& t, at::ScalarType st, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == st, name, " has dtype ", t.scalar_type(), ", expected ", st);
+}
+
+void rmsnorm(Tensor x, Tensor w, Tensor out, double eps, bool zero_centred) {
+  need(x, at::kBFloat16, "x");
+  need(w, at::kBFloat16, "w");
+  need(out, at::kBFloat16, "out");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "rmsnorm: 2-D rows");
+  const int d = (int)x.size(1);
+  TORCH_CHECK(d % 8 == 0 && d <= 8192 && w.numel() == d, "rmsnorm: d % 8 == 0, d <= 8192");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && out.stride(0) % 8 == 0, "rmsnorm: row pitch % 8");
+  c10::cuda::CUDAGuard g(x.device());
+  rf::rmsnorm(cbf(x), x.stride(0), cbf(w), bf(out), out.stride(0), (int)x.size(0), d, (float)eps, zero_centred ? 1 : 0,
+              cur());
+}
+
+void head_norm_rope(Tensor src, int64_t src_row_stride, int64_t src_head_stride, int64_t n_heads, int64_t head_dim,
+                    int64_t n_rows, OptT norm_w, int64_t norm_mode, double eps, OptT cos, OptT sin, int64_t rot,
+                    OptT pos, int64_t pos_offset, Tensor dst, int64_t dst_head_stride, int64_t dst_row_stride) {
+  need(src, at::kBFloat16, "src");
+  need(dst, at::kBFloat16, "dst");
+  TORCH_CHECK(head_dim % 32 == 0 && head_dim <= 256, "head_norm_rope: head_dim % 32 == 0, <= 256");
+  TORCH_CHECK(rot == 0 || ((rot / 2) % (head_dim / 32) == 0 && rot <= head_dim), "head_norm_rope: rot layout");
+  c10::cuda::CUDAGuard g(src.device());
+  rf::HeadNormRopeArgs a{};
+  a.src = cbf(src);
+  a.src_row_stride = src_row_stride;
+  a.src_head_stride = src_head_stride;
+  a.n_heads = (int)n_heads;
+  a.head_dim = (int)head_dim;
+  a.n_rows = (int)n_rows;
+  a.norm_w = norm_w.has_value() ? cbf(*norm_w) : nullptr;
+  a.norm_mode = norm_w.has_value() ? (int)norm_mode : -1;
+  a.eps = (float)eps;
+  a.rot = (int)rot;
+  if (rot > 0) {
+    TORCH_CHECK(cos.has_value() && sin.has_value(), "head_norm_rope: cos/sin tables");
+    need(*cos, at::kBFloat16, "cos");
+    a.cos = cbf(*cos);
+    a.sin = cbf(*sin);
+  }
+  if (pos.has_value()) {
+    need(*pos, at::kInt, "pos");
+    a.pos = pos->data_ptr<int>();
+  }
+  a.pos_offset = (int)pos_offset;
+  a.dst = bf(dst);
+  a.dst_head_stride = dst_head_stride;
+  a.dst_row_stride = dst_row_stride;
+  rf::head_norm_rope(a, cur());
+}
+
+void gated_rmsnorm(Tensor o, Tensor z, int64_t ldz, Tensor w, Tensor out, int64_t heads, int64_t dv, double eps) {
+  need(o, at::kBFloat16, "o");
+  need(z, at::kBFloat16, "z");
+  need(w, at::kBFloat16, "w");
+  need(out, at::kBFloat16, "out");
+  TORCH_CHECK(dv % 32 == 0 && dv <= 256, "gated_rmsnorm: dv");
+  c10::cuda::CUDAGuard g(o.device());
+  rf::gated_rmsnorm(cbf(o), o.stride(0), cbf(z), ldz, cbf(w), bf(out), out.stride(0), (int)o.size(0), (int)heads,
+                    (int)dv, (float)eps, cur());
+}
+
+void embed_gather(Tensor table, Tensor ids, Tensor out) {
+  need(table, at::kBFloat16, "table");
+  need(ids, at::kLong, "ids");
+  need(out, at::kBFloat16, "out");
+  TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && ids.is_contiguous(), "embed_gather: contiguous");
+  TORCH_CHECK(table.size(1) % 8 == 0, "embed_gather: d % 8");
+  c10::cuda::CUDAGuard g(table.device());
+  rf::embed_gather(cbf(table), ids.data_ptr<int64_t>(), bf(out), (int)ids.numel(), (int)table.size(1),
+                   (long)table.size(0), cur());
+}
+
+void flash_attention(Tensor q, int64_t q_head_stride, Tensor k, Tensor v, int64_t kv_head_stride, Tensor out,
+                     int64_t hq, int64_t hkv, int64_t hd, int64_t nq, int64_t nk, OptT qpos, int64_t q_start,
+                     double scale, OptT gate, int64_t gate_row, int64_t gate_head) {
+  need(q, at::kBFloat16, "q");
+  need(k, at::kBFloat16, "k");
+  need(v, at::kBFloat16, "v");
+  need(out, at::kBFloat16, "out");
+  TORCH_CHECK(hd == 64 || hd == 128 || hd == 256, "flash_attention: head_dim 64/128/256");
+  TORCH_CHECK(hq % hkv == 0, "flash_attention: GQA");
+  TORCH_CHECK(out.stride(1) == 1, "flash_attention: out rows");
+  c10::cuda::CUDAGuard g(q.device());
+  rf::AttnArgs a{};
+  a.q = cbf(q);
+  a.q_head_stride = q_head_stride;
+  a.k = cbf(k);
+  a.v = cbf(v);
+  a.kv_head_stride = kv_head_stride;
+  a.hq = (int)hq;
+  a.hkv = (int)hkv;
+  a.hd = (int)hd;
+  a.nq = (int)nq;
+  a.nk = (int)nk;
+  if (qpos.has_value()) {
+    need(*qpos, at::kInt, "qpos");
+    a.qpos = qpos->data_ptr<int>();
+  }
+  a.q_start = (int)q_start;
+  a.scale = (float)scale;
+  if (gate.has_value()) {
+    need(*gate, at::kBFloat16, "gate");
+    a.gate = cbf(*gate);
+    a.gate_row = gate_row;
+    a.gate_head = gate_head;
+  }
+  a.out = bf(out);
+  a.out_row = out.stride(0);
+  rf::flash_attention(a, cur());
+}
+
+void gdn_prep(Tensor proj, int64_t b_off, int64_t a_off, Tensor conv_w, OptT conv_state, Tensor A_log,
+              Tensor dt_bias, int64_t n, int64_t nk, int64_t nv, int64_t dk, int64_t dv, int64_t K, Tensor q, Tensor k,
+              Tensor v, Tensor beta, Tensor g) {
+  need(proj, at::kBFloat16, "proj");
+  need(conv_w, at::kBFloat16, "conv_w");
+  need(A_log, at::kFloat, "A_log");
+  need(dt_bias, at::kFloat, "dt_bias");
+  need(q, at::kBFloat16, "q");
+  need(k, at::kBFloat16, "k");
+  need(v, at::kBFloat16, "v");
+  need(beta, at::kFloat, "beta");
+  need(g, at::kFloat, "g");
+  TORCH_CHECK(proj.stride(1) == 1 && conv_w.is_contiguous(), "gdn_prep: layouts");
+  TORCH_CHECK(dk % 32 == 0 && dv % 32 == 0 && dk <= 256 && dv <= 256 && K <= 8, "gdn_prep: dims");
+  c10::cuda::CUDAGuard gd(proj.device());
+  rf::GdnPrepArgs a{};
+  a.proj = cbf(proj);
+  a.proj_row = proj.stride(0);
+  a.b_off = (int)b_off;
+  a.a_off = (int)a_off;
+  a.conv_w = cbf(conv_w);
+  if (conv_state.has_value()) {
+    need(*conv_state, at::kBFloat16, "conv_state");
+    a.conv_state = cbf(*conv_state);
+  }
+  a.A_log = A_log.data_ptr<float>();
+  a.dt_bias = dt_bias.data_ptr<float>();
+  a.n = (int)n;
+  a.nk = (int)nk;
+  a.nv = (int)nv;
+  a.dk = (int)dk;
+  a.dv = (int)dv;
+  a.K = (int)K;
+  a.q = bf(q);
+  a.k = bf(k);
+  a.v = bf(v);
+  a.beta = beta.data_ptr<float>();
+  a.g = g.data_ptr<float>();
+  rf::gdn_prep(a, cur());
+}
+
+void gdn_conv_state_update(Tensor proj, Tensor state, int64_t n, int64_t C, int64_t K) {
+  need(proj, at::kBFloat16, "proj");
+  need(state, at::kBFloat16, "state");
+  TORCH_CHECK(state.is_contiguous() && K <= 8, "gdn_conv_state_update: layout");
+  c10::cuda::CUDAGuard g(proj.device());
+  rf::gdn_conv_state_update(cbf(proj), proj.stride(0), bf(state), (int)n, (int)C, (int)K, cur());
+}
+
+void gdn_chunk_scan(OptT q, Tensor k, Tensor v, Tensor beta, Tensor g, Tensor state, OptT out, Tensor w_buf,
+                    Tensor u_buf, int64_t n, int64_t nk, int64_t nv, int64_t dk, int64_t dv, Tensor err) {
+  need(k, at::kBFloat16, "k");
+  need(v, at::kBFloat16, "v");
+  need(beta, at::kFloat, "beta");
+  need(g, at::kFloat, "g");
+  need(state, at::kFloat, "state");
+  need(w_buf, at::kBFloat16, "w_buf");
+  need(u_buf, at::kBFloat16, "u_buf");
+  TORCH_CHECK(dk == 128 && dv % 64 == 0 && dv <= 128 && nv % nk == 0, "gdn_chunk_scan: dk 128, dv 64|128");
+  const int64_t n_pad = (n + 63) / 64 * 64;
+  TORCH_CHECK(w_buf.numel() >= nv * n_pad * dk && u_buf.numel() >= nv * n_pad * dv, "gdn_chunk_scan: scratch size");
+  TORCH_CHECK(state.is_contiguous() && state.numel() == nv * dk * dv, "gdn_chunk_scan: state [nv, dk, dv]");
+  c10::cuda::CUDAGuard gd(k.device());
+  rf::GdnScanArgs a{};
+  if (q.has_value()) {
+    need(*q, at::kBFloat16, "q");
+    a.q = cbf(*q);
+    TORCH_CHECK(out.has_value(), "gdn_chunk_scan: output mode needs out");
+  }
+  a.k = cbf(k);
+  a.v = cbf(v);
+  a.beta = beta.data_ptr<float>();
+  a.g = g.data_ptr<float>();
+  a.state = state.data_ptr<float>();
+  if (out.has_value()) {
+    need(*out, at::kBFloat16, "out");
+    a.out = bf(*out);
+    a.out_row = out->stride(0);
+  }
+  a.w_buf = bf(w_buf);
+  a.u_buf = bf(u_buf);
+  a.n = (int)n;
+  a.nk = (int)nk;
+  a.nv = (int)nv;
+  a.dk = (int)dk;
+  a.dv = (int)dv;
+  a.err = err.data_ptr<int>();
+  rf::gdn_chunk_scan(a, cur());
+}
+
+}  // namespace
+
+void register_ops(pybind11::module_& m) {
+  namespace py = pybind11;
+  m.def("rmsnorm", &rmsnorm);
+  m.def("head_norm_rope", &head_norm_rope);
+  m.def("gated_rmsnorm", &gated_rmsnorm);
+  m.def("embed_gather", &embed_gather);
+  m.def("flash_attention", &flash_attention);
+  m.def("gdn_prep", &gdn_prep);
+  m.def("gdn_conv_state_update", &gdn_conv_state_update);
+  m.def("gdn_chunk_scan", &gdn_chunk_scan);
+}

@@ -1,8 +1,92 @@
-// Launchers of the non-GEMM sm_100a kernels (norms, RoPE, attention, Gated DeltaNet, ridge linear
-// algebra, MoE routing, peer-memory collectives). Raw pointers + a stream; no torch types.
+// Launchers of the non-GEMM sm_100a kernels. Raw pointers + a stream; no torch types.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
-namespace rf {}  // namespace rf
+namespace rf {
+
+// ---- norm.cu
+void rmsnorm(const __nv_bfloat16* x, long ldx, const __nv_bfloat16* w, __nv_bfloat16* y, long ldy, int rows, int d,
+             float eps, int zero_centred, cudaStream_t stream);
+
+struct HeadNormRopeArgs {
+  const __nv_bfloat16* src;   // head h of row t at src + t * src_row_stride + h * src_head_stride
+  long src_row_stride;
+  long src_head_stride;
+  int n_heads, head_dim, n_rows;
+  const __nv_bfloat16* norm_w;  // [head_dim] or nullptr
+  int norm_mode;                // -1 none, 0 plain RMSNorm, 1 zero-centred
+  float eps;
+  const __nv_bfloat16* cos;     // [max_pos, rot / 2] bf16 tables
+  const __nv_bfloat16* sin;
+  int rot;                      // rotated dims (0: no RoPE)
+  const int* pos;               // [n_rows] positions, or nullptr: row + pos_offset
+  int pos_offset;
+  __nv_bfloat16* dst;           // head h of row t at dst + h * dst_head_stride + t * dst_row_stride
+  long dst_head_stride;
+  long dst_row_stride;
+};
+void head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t stream);
+
+void gated_rmsnorm(const __nv_bfloat16* o, long ldo, const __nv_bfloat16* z, long ldz, const __nv_bfloat16* w,
+                   __nv_bfloat16* y, long ldy, int rows, int heads, int dv, float eps, cudaStream_t stream);
+
+void embed_gather(const __nv_bfloat16* table, const int64_t* ids, __nv_bfloat16* out, int rows, int d, long vocab,
+                  cudaStream_t stream);
+
+// ---- attention.cu
+struct AttnArgs {
+  const __nv_bfloat16* q;   // [hq, nq, hd] (head-major; row pitch hd, head pitch q_head_stride)
+  long q_head_stride;
+  const __nv_bfloat16* k;   // [hkv, *, hd] cache (head pitch kv_head_stride, row pitch hd)
+  const __nv_bfloat16* v;
+  long kv_head_stride;
+  int hq, hkv, hd, nq, nk;
+  const int* qpos;          // [nq] sorted query positions, or nullptr: q_start + row
+  int q_start;
+  float scale;
+  const __nv_bfloat16* gate;   // optional output gate: gate of (row t, head h) at gate + t * gate_row + h * gate_head
+  long gate_row, gate_head;
+  __nv_bfloat16* out;          // [nq, hq * hd] (row pitch out_row)
+  long out_row;
+};
+void flash_attention(const AttnArgs& a, cudaStream_t stream);
+
+// ---- gdn.cu
+struct GdnPrepArgs {
+  const __nv_bfloat16* proj;   // [n, *] in-projection rows: [q | k | v] conv channels at col 0, b at b_off, a at a_off
+  long proj_row;
+  int b_off, a_off;
+  const __nv_bfloat16* conv_w;  // [C, K]
+  const __nv_bfloat16* conv_state;  // [K-1, C] previous pre-conv rows (zeros at the start)
+  const float* A_log;           // [nv]
+  const float* dt_bias;         // [nv]
+  int n, nk, nv, dk, dv, K;
+  __nv_bfloat16* q;             // [nk, n, dk] l2-normed, scaled by dk^-0.5
+  __nv_bfloat16* k;             // [nk, n, dk] l2-normed
+  __nv_bfloat16* v;             // [nv, n, dv]
+  float* beta;                  // [nv, n]
+  float* g;                     // [nv, n]
+};
+void gdn_prep(const GdnPrepArgs& a, cudaStream_t stream);
+void gdn_conv_state_update(const __nv_bfloat16* proj, long proj_row, __nv_bfloat16* state, int n, int C, int K,
+                           cudaStream_t stream);
+
+struct GdnScanArgs {
+  const __nv_bfloat16* q;   // [nk, n, dk] (nullptr: fill mode, no output)
+  const __nv_bfloat16* k;   // [nk, n, dk]
+  const __nv_bfloat16* v;   // [nv, n, dv]
+  const float* beta;        // [nv, n]
+  const float* g;           // [nv, n]
+  float* state;             // [nv, dk, dv] fp32, read and updated in place
+  __nv_bfloat16* out;       // [n, nv, dv] (row pitch out_row) or nullptr
+  long out_row;
+  __nv_bfloat16* w_buf;     // scratch [nv, n_pad, dk]
+  __nv_bfloat16* u_buf;     // scratch [nv, n_pad, dv]
+  int n, nk, nv, dk, dv;
+  int* err;
+};
+void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream);
+
+}  // namespace rf

@@ -1,0 +1,212 @@
+// Row-wise kernels of the prefill path (memory-bound; one pass each):
+//   rmsnorm           y = RMSNorm(x) with the plain (HF order: normalise fp32, round, times w) or
+//                     zero-centred ((1 + w) in fp32, one rounding) weight
+//   head_norm_rope    per (row, head): optional head RMSNorm, rotate-half RoPE on the first `rot` dims from a
+//                     bf16 cos/sin table, written head-major (queries, or straight into the K/V cache)
+//   gated_rmsnorm     Gated DeltaNet output: per-head RMSNorm, times w, times silu(z)
+//   embed_gather      rows of the embedding table
+#include "kernels.h"
+
+#include <cuda_bf16.h>
+
+namespace rf {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+// ------------------------------------------------------------------------------------- rmsnorm
+// One CTA (256 threads) per row; the row (d <= 8192) is held in registers between the two passes.
+template <int MODE>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long ldx,
+                                                      const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
+                                                      long ldy, int d, float eps) {
+  constexpr int MAXV = 4;  // up to 4 x 8 elements per thread: d <= 8192
+  const long row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * ldx;
+  __nv_bfloat16* yr = y + row * ldy;
+  const int nvec = d / 8;
+  uint4 buf[MAXV];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int v = threadIdx.x + j * 256;
+    if (v < nvec) {
+      buf[j] = *reinterpret_cast<const uint4*>(xr + v * 8);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&buf[j]);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float f = __bfloat162float(e[q]);
+        ss += f * f;
+      }
+    }
+  }
+  __shared__ float red[8];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < 8 ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)d + eps);
+#pragma unroll
+  for (int j = 0; j < MAXV; ++j) {
+    const int v = threadIdx.x + j * 256;
+    if (v < nvec) {
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&buf[j]);
+      uint4 wv = *reinterpret_cast<const uint4*>(w + v * 8);
+      const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+      uint4 out;
+      __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&out);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float f = __bfloat162float(e[q]) * inv;
+        if (MODE == 0)
+          oe[q] = __float2bfloat16(bfr(f) * __bfloat162float(we[q]));
+        else
+          oe[q] = __float2bfloat16(f * (1.0f + __bfloat162float(we[q])));
+      }
+      *reinterpret_cast<uint4*>(yr + v * 8) = out;
+    }
+  }
+}
+
+void rmsnorm(const __nv_bfloat16* x, long ldx, const __nv_bfloat16* w, __nv_bfloat16* y, long ldy, int rows, int d,
+             float eps, int zero_centred, cudaStream_t stream) {
+  if (rows <= 0) return;
+  if (zero_centred)
+    rmsnorm_kernel<1><<<rows, 256, 0, stream>>>(x, ldx, w, y, ldy, d, eps);
+  else
+    rmsnorm_kernel<0><<<rows, 256, 0, stream>>>(x, ldx, w, y, ldy, d, eps);
+}
+
+// ----------------------------------------------------------------------------- head_norm_rope
+// One warp per (row, head); head_dim <= 256 (8 elements per lane).
+__global__ void __launch_bounds__(256) head_norm_rope_kernel(HeadNormRopeArgs a) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int row = warp / a.n_heads;
+  const int head = warp % a.n_heads;
+  if (row >= a.n_rows) return;
+  const int hd = a.head_dim;
+  const int per = hd / 32;  // elements per lane (hd multiple of 32)
+  const __nv_bfloat16* src = a.src + (long)row * a.src_row_stride + (long)head * a.src_head_stride;
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = 0.f;
+  // lane owns elements lane*per .. lane*per+per-1
+  for (int j = 0; j < per; ++j) v[j] = __bfloat162float(src[lane * per + j]);
+  if (a.norm_mode >= 0) {
+    float ss = 0.f;
+    for (int j = 0; j < per; ++j) ss += v[j] * v[j];
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / (float)hd + a.eps);
+    for (int j = 0; j < per; ++j) {
+      const float wj = __bfloat162float(a.norm_w[lane * per + j]);
+      const float f = v[j] * inv;
+      v[j] = (a.norm_mode == 0) ? bfr(bfr(f) * wj) : bfr(f * (1.0f + wj));
+    }
+  }
+  if (a.rot > 0) {
+    // rotate-half over [0, rot): out[i] = x[i] cos[i] - x[i + h] sin[i] (i < h), out[i] = x[i] cos[i - h] + x[i - h] sin
+    const int h = a.rot / 2;
+    const int p = a.pos != nullptr ? a.pos[row] : row + a.pos_offset;
+    const __nv_bfloat16* cs = a.cos + (long)p * h;
+    const __nv_bfloat16* sn = a.sin + (long)p * h;
+    float out[8];
+    for (int j = 0; j < per; ++j) out[j] = v[j];
+    // partner exchange: element i pairs with i +- h; h is a multiple of per when rot % (2*per) == 0
+    const int loff = h / per;
+    for (int j = 0; j < per; ++j) {
+      const int i = lane * per + j;
+      const float up = __shfl_down_sync(0xffffffffu, v[j], loff);  // value at i + h
+      const float dn = __shfl_up_sync(0xffffffffu, v[j], loff);    // value at i - h
+      if (i < a.rot) {
+        if (i < h) {
+          const float c = __bfloat162float(cs[i]), s = __bfloat162float(sn[i]);
+          out[j] = bfr(bfr(v[j] * c) + bfr(-up * s));
+        } else {
+          const float c = __bfloat162float(cs[i - h]), s = __bfloat162float(sn[i - h]);
+          out[j] = bfr(bfr(v[j] * c) + bfr(dn * s));
+        }
+      }
+    }
+    for (int j = 0; j < per; ++j) v[j] = out[j];
+  }
+  __nv_bfloat16* dst = a.dst + (long)head * a.dst_head_stride + (long)row * a.dst_row_stride;
+  for (int j = 0; j < per; ++j) dst[lane * per + j] = __float2bfloat16(v[j]);
+}
+
+void head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t stream) {
+  if (a.n_rows <= 0 || a.n_heads <= 0) return;
+  const long warps = (long)a.n_rows * a.n_heads;
+  const int blocks = (int)((warps * 32 + 255) / 256);
+  head_norm_rope_kernel<<<blocks, 256, 0, stream>>>(a);
+}
+
+// ------------------------------------------------------------------------------ gated_rmsnorm
+// y[row, head, :] = bf16( bf16(w * bf16(norm(o))) * silu(z) ); one warp per (row, head), dv <= 256.
+__global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ o, long ldo,
+                                                            const __nv_bfloat16* __restrict__ z, long ldz,
+                                                            const __nv_bfloat16* __restrict__ w,
+                                                            __nv_bfloat16* __restrict__ y, long ldy, int rows,
+                                                            int heads, int dv, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int row = warp / heads;
+  const int head = warp % heads;
+  if (row >= rows) return;
+  const int per = dv / 32;
+  const __nv_bfloat16* orow = o + (long)row * ldo + head * dv;
+  const __nv_bfloat16* zrow = z + (long)row * ldz + head * dv;
+  float v[8];
+  float ss = 0.f;
+  for (int j = 0; j < per; ++j) {
+    v[j] = __bfloat162float(orow[lane * per + j]);
+    ss += v[j] * v[j];
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)dv + eps);
+  __nv_bfloat16* yrow = y + (long)row * ldy + head * dv;
+  for (int j = 0; j < per; ++j) {
+    const int i = lane * per + j;
+    const float t = bfr(__bfloat162float(w[i]) * bfr(v[j] * inv));
+    const float zz = __bfloat162float(zrow[i]);
+    const float sz = zz / (1.0f + expf(-zz));
+    yrow[i] = __float2bfloat16(t * sz);
+  }
+}
+
+void gated_rmsnorm(const __nv_bfloat16* o, long ldo, const __nv_bfloat16* z, long ldz, const __nv_bfloat16* w,
+                   __nv_bfloat16* y, long ldy, int rows, int heads, int dv, float eps, cudaStream_t stream) {
+  if (rows <= 0) return;
+  const long warps = (long)rows * heads;
+  gated_rmsnorm_kernel<<<(int)((warps * 32 + 255) / 256), 256, 0, stream>>>(o, ldo, z, ldz, w, y, ldy, rows, heads,
+                                                                            dv, eps);
+}
+
+// ------------------------------------------------------------------------------- embed_gather
+__global__ void embed_gather_kernel(const __nv_bfloat16* __restrict__ table, const int64_t* __restrict__ ids,
+                                    __nv_bfloat16* __restrict__ out, int d, long vocab) {
+  const long row = blockIdx.x;
+  long id = ids[row];
+  if (id < 0 || id >= vocab) id = 0;
+  const uint4* src = reinterpret_cast<const uint4*>(table + id * (long)d);
+  uint4* dst = reinterpret_cast<uint4*>(out + row * (long)d);
+  for (int v = threadIdx.x; v < d / 8; v += blockDim.x) dst[v] = src[v];
+}
+
+void embed_gather(const __nv_bfloat16* table, const int64_t* ids, __nv_bfloat16* out, int rows, int d, long vocab,
+                  cudaStream_t stream) {
+  if (rows <= 0) return;
+  embed_gather_kernel<<<rows, 128, 0, stream>>>(table, ids, out, d, vocab);
+}
+
+}  // namespace rf

@@ -27,6 +27,8 @@ def run_lower(model, ids, splits, hs_device=None, hook=None, mix=None):
         splits = [splits]
     ids = ids.to(model.device)
     pos = torch.arange(ids.shape[0], device=model.device)
+    if hasattr(model, "reserve"):
+        model.reserve(ids.shape[0] + 64)
     cache = model.new_cache()
     h = model.embed(ids)
     hs = {}
@@ -137,6 +139,8 @@ def finish(model, ids, h_split, lower_cache, arm, keep, oracle=None, keep_cache=
     split = arm.split
     P = arm.prefix_len(n)
     pos = torch.arange(n, device=model.device)
+    if hasattr(model, "reserve"):
+        model.reserve(n + 64)
     h_split = h_split.to(model.device)
     cache = [dict(c) for c in lower_cache[:split]] + [dict() for _ in range(model.n_layers - split)]
     if arm.fill == "swiftkv_native":

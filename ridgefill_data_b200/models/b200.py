@@ -1,0 +1,293 @@
+"""B200 models: the layer math of models/llama.py and models/hybrid.py on the sm_100a kernels.
+
+Weights are packed at load for the fused kernels:
+  attention   qkv_p = [q (q|gate per head when gated) ; k ; v] rows -> one tcgen05 GEMM; the K/V rows are a
+              contiguous row slice (the cache-only fill's GEMM)
+  GDN         in_p = [in_proj_qkv ; in_proj_b ; in_proj_a ; in_proj_z] rows: the fill GEMM uses the prefix
+              without z
+  MLP         gu_p = gate/up interleaved per 128-row block -> one GEMM with a SwiGLU epilogue
+The torch names (q, k, v, qkv, b, a, z, ...) stay as views of the packed tensors, so the diagnostic paths
+inherited from the torch models (reads, queries, layer_rows, SwiftKV) keep working on the device.
+
+Hot path per exact layer: rmsnorm -> GEMM -> head-norm/RoPE straight into the K/V cache (or conv + gates
+-> chunked delta rule) -> flash attention with the gate epilogue (or gated rmsnorm) -> GEMM with the
+residual add fused -> rmsnorm -> SwiGLU GEMM -> down GEMM with the residual add fused.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..ops import gemm as G
+from ..ops import kernels as K
+from .base import KV_RESERVE
+from .hybrid import Hybrid
+from .llama import Llama
+
+
+class _B200:
+    """Kernel-backed overrides shared by the Llama-family and hybrid models."""
+
+    zero_centred = False
+    capacity_hint = 0
+
+    # ---- setup
+    def _kernel_setup(self):
+        if self.device.type != "cuda":
+            raise RuntimeError("the B200 backend needs a CUDA device")
+        from ..ops._ext import ext
+        ext()   # fail loudly when the extension is missing
+        self._rope_tables = None
+        self._span_cache = {}
+        self.lm_head_f = None
+
+    def rope(self, need):
+        """bf16 cos/sin tables covering positions < need (grown on demand)."""
+        if self._rope_tables is None or self._rope_tables[0].shape[0] < need:
+            n = max(need, 8192, 2 * (self._rope_tables[0].shape[0] if self._rope_tables else 0))
+            self._rope_tables = K.rope_tables(self.inv_freq, n, self.device)
+        return self._rope_tables
+
+    def reserve(self, n_tokens):
+        """Size new attention caches for n_tokens rows (prompt + decode reserve), so appends never copy."""
+        self.capacity_hint = int(n_tokens)
+
+    def _span(self, pos):
+        """(first position, int32 positions or None when pos is a contiguous range)."""
+        key = (pos.data_ptr(), pos.numel(), pos.device)
+        ent = self._span_cache.get(key)
+        hit = ent[1] if ent is not None else None
+        if hit is None:
+            p = pos.to("cpu", torch.long)
+            p0 = int(p[0]) if p.numel() else 0
+            contiguous = bool(torch.equal(p, torch.arange(p0, p0 + p.numel())))
+            hit = (p0, None if contiguous else pos.to(self.device, torch.int32).contiguous())
+            if len(self._span_cache) > 64:
+                self._span_cache.clear()
+            self._span_cache[key] = (pos, hit)   # holding pos keeps its address from being reused
+        return hit
+
+    def _norm(self, x, w):
+        return K.rmsnorm(x, w, self.eps, self.zero_centred)
+
+    # ---- common
+    def embed(self, ids):
+        return K.embed(self.embed_w, ids.to(self.device))
+
+    def final_norm(self, h):
+        return self._norm(h, self.norm_w)
+
+    def logits(self, h):
+        return G.linear_f32(self.final_norm(h), self.lm_head)
+
+    def mlp(self, i, h):
+        w = self.W[i]
+        if "gu_p" not in w:
+            return super().mlp(i, h)
+        x = K.rmsnorm(h, w["ln2"], self.eps, self.zero_centred)
+        act = G.swiglu_linear(x, w["gu_p"])
+        return G.linear(act, w["down"], residual=h)
+
+    def _pack_mlp(self, w):
+        if "gate" in w and w["gate"].shape[0] % 128 == 0:
+            w["gu_p"] = G.pack_gate_up(w["gate"], w["up"]).contiguous()
+            del w["gate"], w["up"]
+
+    # ---- attention
+    def _kv_reserve(self, c, m):
+        n = c.get("n", 0)
+        kb = c.get("kbuf")
+        if kb is None or n + m > kb.shape[1]:
+            cap = max(n + m + KV_RESERVE, self.capacity_hint)
+            shape = (self.n_kv, cap, self.head_dim)
+            nkb = torch.empty(shape, dtype=self.dtype, device=self.device)
+            nvb = torch.empty(shape, dtype=self.dtype, device=self.device)
+            if n:
+                nkb[:, :n] = c["kbuf"][:, :n]
+                nvb[:, :n] = c["vbuf"][:, :n]
+            c["kbuf"], c["vbuf"] = nkb, nvb
+        return n
+
+    def _commit_kv(self, c, n_new):
+        c["n"] = n_new
+        c["k"], c["v"] = c["kbuf"][:, :n_new], c["vbuf"][:, :n_new]
+
+    def _qk_mode(self):
+        if not self.cfg.qk_norm:
+            return -1
+        return 1 if self.zero_centred else 0
+
+    def _write_kv(self, i, kv_src, pos, c):
+        """K (head norm + RoPE) and V rows of kv_src [m, 2 * hkv * hd] into cache c at its end."""
+        w = self.W[i]
+        m = kv_src.shape[0]
+        hd, hkv = self.head_dim, self.n_kv
+        p0, parr = self._span(pos)
+        n0 = self._kv_reserve(c, m)
+        kb, vb = c["kbuf"], c["vbuf"]
+        cap = kb.shape[1]
+        tables = self.rope(p0 + m if parr is None else int(pos.max()) + 1)
+        K.head_norm_rope(kv_src, hkv, hd, hd, kb[:, n0:], cap * hd, hd, norm_w=w.get("k_norm"),
+                         norm_mode=self._qk_mode(), eps=self.eps, tables=tables, rot=self.cfg.rot_dim,
+                         pos=parr, pos_offset=p0)
+        K.head_norm_rope(kv_src[:, hkv * hd:], hkv, hd, hd, vb[:, n0:], cap * hd, hd)
+        self._commit_kv(c, n0 + m)
+        return n0
+
+    def _attn_mix(self, i, h, pos, cache):
+        """Attention block output added to h (new tensor) and the mixer output when asked."""
+        w = self.W[i]
+        n = h.shape[0]
+        hd, hq, hkv = self.head_dim, self.n_heads, self.n_kv
+        gated = self.cfg.gated_attn
+        qw = hq * hd * (2 if gated else 1)
+        x = self._norm(h, w["ln1"])
+        qkv = G.linear(x, w["qkv_p"])
+        p0, parr = self._span(pos)
+        c = cache[i]
+        n0 = self._write_kv(i, qkv[:, qw:], pos, c)
+        q = torch.empty(hq, n, hd, dtype=self.dtype, device=self.device)
+        tables = self.rope(p0 + n if parr is None else int(pos.max()) + 1)
+        K.head_norm_rope(qkv, hq, hd, 2 * hd if gated else hd, q, n * hd, hd, norm_w=w.get("q_norm"),
+                         norm_mode=self._qk_mode(), eps=self.eps, tables=tables, rot=self.cfg.rot_dim, pos=parr,
+                         pos_offset=p0)
+        o = torch.empty(n, hq * hd, dtype=self.dtype, device=self.device)
+        K.attention(q, c["kbuf"], c["vbuf"], n0 + n, self.scale, o, q_start=n0,
+                    gate=qkv[:, hd:] if gated else None, gate_head=2 * hd)
+        return o
+
+    # ---- per-layer API
+    def _mixer_out(self, i, h, pos, cache, need_out=True):
+        if self.layer_types[i] == "attn":
+            return self._attn_mix(i, h, pos, cache), self.W[i]["o"]
+        return self._gdn_mix(i, h, cache), self.W[i]["out"]
+
+    def layer(self, i, h, pos, cache, mix=None, gdn_checkpoint_every=None, **_):
+        if gdn_checkpoint_every and self.layer_types[i] == "gdn":
+            return super().layer(i, h, pos, cache, gdn_checkpoint_every=gdn_checkpoint_every, mix=mix)
+        y, wo = self._mixer_out(i, h, pos, cache)
+        if mix is not None:
+            a = G.linear(y, wo)
+            mix(i, a)
+            h2 = h + a
+        else:
+            h2 = G.linear(y, wo, residual=h)
+        return self.mlp(i, h2)
+
+    def fill(self, i, x, pos, cache, st=None, checkpoint_every=None, **_):
+        if checkpoint_every:
+            return super().fill(i, x, pos, cache, st=st, checkpoint_every=checkpoint_every)
+        w = self.W[i]
+        xn = self._norm(x, w["ln1"])
+        if self.layer_types[i] == "attn":
+            qw = self.n_heads * self.head_dim * (2 if self.cfg.gated_attn else 1)
+            kv = G.linear(xn, w["qkv_p"][qw:])
+            self._write_kv(i, kv, pos, cache[i])
+            return {}
+        self._gdn_fill(i, xn, cache)
+        if st is not None:
+            cache[i]["rec"] = cache[i]["rec"] + st.to(cache[i]["rec"])
+        return {}
+
+    def fill_batch(self, layers, b, pos, cache, projector=None):
+        """Cache-only fills of every late layer from the same boundary rows b: x_i = b W_i^T + c_i (tcgen05
+        GEMM with the bias epilogue; identity fill when projector is None), then the layer's fill."""
+        if projector is not None:
+            W, B = projector.device_maps(self.device)
+        for i in layers:
+            if projector is None:
+                x = b
+            else:
+                x = G.linear(b, W[i] if W[i].dtype == self.dtype else W[i].to(self.dtype),
+                             bias=B[i] if B[i].dtype == self.dtype else B[i].to(self.dtype))
+            self.fill(i, x, pos, cache)
+
+
+class B200Llama(_B200, Llama):
+    """Llama-3.1 / dense Qwen3 on the sm_100a kernels."""
+
+    zero_centred = False
+
+    def _setup(self):
+        super()._setup()
+        self._kernel_setup()
+
+    def _load_layer(self, i):
+        w = super()._load_layer(i)
+        qkv = torch.cat((w["q"], w["k"], w["v"])).contiguous()
+        qw, kw = w["q"].shape[0], w["k"].shape[0]
+        w.update(qkv_p=qkv, q=qkv[:qw], k=qkv[qw:qw + kw], v=qkv[qw + kw:])
+        self._pack_mlp(w)
+        return w
+
+    def _gdn_mix(self, i, h, cache):
+        raise RuntimeError("Llama-family models have no Gated DeltaNet layers")
+
+
+class B200Hybrid(_B200, Hybrid):
+    """The Qwen3.5-style hybrid (and its MoE variant) on the sm_100a kernels."""
+
+    zero_centred = True
+
+    def _setup(self):
+        super()._setup()
+        self._kernel_setup()
+        c = self.cfg
+        self.conv_dim = c.gdn_conv_dim
+        self.vd = c.gdn_nv * c.gdn_dv
+
+    def _load_layer(self, i):
+        w = super()._load_layer(i)
+        if self.layer_types[i] == "attn":
+            qkv = torch.cat((w["q"], w["k"], w["v"])).contiguous()
+            qw, kw = w["q"].shape[0], w["k"].shape[0]
+            w.update(qkv_p=qkv, q=qkv[:qw], k=qkv[qw:qw + kw], v=qkv[qw + kw:])
+        else:
+            C, nv = self.cfg.gdn_conv_dim, self.cfg.gdn_nv
+            p = torch.cat((w["qkv"], w["b"], w["a"], w["z"])).contiguous()
+            w.update(in_p=p, qkv=p[:C], b=p[C:C + nv], a=p[C + nv:C + 2 * nv], z=p[C + 2 * nv:],
+                     conv=w["conv"].contiguous(), A_log=w["A_log"].float().contiguous(),
+                     dt_bias=w["dt_bias"].float().contiguous())
+        if not self.cfg.moe:
+            self._pack_mlp(w)
+        return w
+
+    def _gdn_core_dev(self, i, proj, cache, need_out):
+        """Conv + gates + chunked delta rule over the rows of proj, continuing cache[i]'s states."""
+        w = self.W[i]
+        cfg = self.cfg
+        C, nv = self.conv_dim, cfg.gdn_nv
+        c = cache[i]
+        conv_state = c.get("conv")
+        q, k, v, beta, g = K.gdn_prep(proj, C, C + nv, w["conv"], conv_state, w["A_log"], w["dt_bias"],
+                                      cfg.gdn_nk, nv, cfg.gdn_dk, cfg.gdn_dv)
+        new_conv = (conv_state.clone() if conv_state is not None
+                    else torch.zeros(cfg.conv_k - 1, C, dtype=self.dtype, device=self.device))
+        K.gdn_conv_state_update(proj, new_conv, C)
+        rec = c.get("rec")
+        rec = (rec.float().clone() if rec is not None
+               else torch.zeros(nv, cfg.gdn_dk, cfg.gdn_dv, dtype=torch.float32, device=self.device))
+        out = None
+        if need_out:
+            out = torch.empty(proj.shape[0], self.vd, dtype=self.dtype, device=self.device)
+        K.gdn_scan(q if need_out else None, k, v, beta, g, rec, out)
+        c["conv"], c["rec"] = new_conv, rec
+        c["len"] = c.get("len", 0) + proj.shape[0]
+        return out
+
+    def _gdn_mix(self, i, h, cache):
+        w = self.W[i]
+        x = self._norm(h, w["ln1"])
+        proj = G.linear(x, w["in_p"])
+        o = self._gdn_core_dev(i, proj, cache, True)
+        z = proj[:, self.conv_dim + 2 * self.cfg.gdn_nv:]
+        return K.gated_rmsnorm(o, z, w["norm"], self.cfg.gdn_nv, self.cfg.gdn_dv, self.eps)
+
+    def _gdn_fill(self, i, xn, cache):
+        w = self.W[i]
+        proj = G.linear(xn, w["in_p"][:self.conv_dim + 2 * self.cfg.gdn_nv])
+        self._gdn_core_dev(i, proj, cache, False)
+
+    def mlp(self, i, h):
+        if self.cfg.moe:
+            return Hybrid.mlp(self, i, h)
+        return _B200.mlp(self, i, h)

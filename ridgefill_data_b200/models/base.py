@@ -19,7 +19,7 @@ import torch
 import torch.nn.functional as F
 
 from ..ops import oracle as ops
-from .checkpoint import Checkpoint, DictSource, random_weights
+from .checkpoint import Checkpoint, DictSource, RandomSource, random_weights
 from .config import ModelConfig
 
 MLP_ROWS = 4096      # MLP row block (bounds the [rows, FFN] intermediate)
@@ -200,8 +200,15 @@ def load(path, device="cpu", dtype=torch.bfloat16, backend="torch", verify=True,
 
 
 def from_config(cfg: ModelConfig, seed=0, device="cpu", dtype=torch.bfloat16, backend="torch", std=0.02,
-                weights=None, **kw):
-    """A random-init model of cfg (seeded; weights generated on the CPU in fp32, then cast)."""
+                weights=None, lazy=None, **kw):
+    """A random-init model of cfg. Default: every tensor drawn on the target device from a (seed, name)
+    generator (RandomSource: no host copy); weights= a state dict; lazy=False: the host-generated
+    random_weights (bitwise identical on every machine)."""
     cls = model_class(cfg, backend)
-    tensors = weights if weights is not None else random_weights(cfg, seed=seed, std=std)
-    return cls(cfg, DictSource(tensors), device=device, dtype=dtype, **kw)
+    if weights is not None:
+        src = DictSource(weights)
+    elif lazy is False:
+        src = DictSource(random_weights(cfg, seed=seed, std=std))
+    else:
+        src = RandomSource(cfg, seed=seed, std=std)
+    return cls(cfg, src, device=device, dtype=dtype, **kw)

@@ -168,3 +168,44 @@ def save_checkpoint(path, cfg: ModelConfig, tensors, shard_bytes=None):
         wmap.update({k: fn for k in sh})
     (path / "model.safetensors.index.json").write_text(json.dumps(dict(metadata={}, weight_map=wmap)))
     return path
+
+
+class RandomSource:
+    """Lazily generated seeded random weights (the Checkpoint interface), each tensor drawn on the target
+    device from its own generator seeded by (seed, name): no host copy of the whole model is ever built,
+    which is what lets a 27B-shaped model initialise straight into HBM."""
+
+    def __init__(self, cfg: ModelConfig, seed=0, std=0.02):
+        import zlib
+        self.cfg = cfg
+        self.seed = seed
+        self.std = std
+        self.shapes = hf_names(cfg)
+        self._crc = zlib.crc32
+
+    def __contains__(self, key):
+        return key in self.shapes
+
+    def keys(self):
+        return self.shapes.keys()
+
+    def get(self, key, device="cpu", dtype=None):
+        dev = torch.device(device)
+        s = (self.seed * 1000003 + self._crc(key.encode())) % (2**62)
+        gen = torch.Generator(device=dev).manual_seed(s)
+        shape = self.shapes[key]
+        cfg = self.cfg
+        if key.endswith("A_log"):
+            t = torch.empty(shape, device=dev).uniform_(1.0, 16.0, generator=gen).log()
+        elif key.endswith("dt_bias"):
+            t = 0.1 * torch.randn(shape, generator=gen, device=dev)
+        elif key.endswith("conv1d.weight"):
+            t = torch.randn(shape, generator=gen, device=dev) / cfg.conv_k ** 0.5
+        elif len(shape) == 1:
+            base = 0.0 if (cfg.zero_centred_norm and "linear_attn.norm" not in key) else 1.0
+            t = base + 0.1 * torch.randn(shape, generator=gen, device=dev)
+        else:
+            t = self.std * torch.randn(shape, generator=gen, device=dev)
+        if dtype is not None and not key.endswith(("A_log", "dt_bias")):
+            t = t.to(dtype)
+        return t

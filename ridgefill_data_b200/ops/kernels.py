@@ -1,0 +1,95 @@
+"""Tensor-level wrappers of the sm_100a kernels (csrc/norm.cu, attention.cu, gdn.cu).
+
+Every wrapper requires CUDA bf16 tensors in the layouts documented per function and raises if the
+extension is missing: there is no PyTorch fallback on the device path.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._ext import ext
+
+BF16 = torch.bfloat16
+
+
+def rmsnorm(x, w, eps, zero_centred, out=None):
+    """RMSNorm of rows x [n, d] (plain: HF order; zero-centred: (1 + w))."""
+    if out is None:
+        out = torch.empty(x.shape[0], x.shape[1], dtype=BF16, device=x.device)
+    ext().rmsnorm(x, w, out, float(eps), bool(zero_centred))
+    return out
+
+
+def rope_tables(inv_freq, max_pos, device, dtype=BF16):
+    """cos/sin [max_pos, rot/2]: angles pos * inv_freq in fp32, cast to the activation dtype (the same
+    values the oracle's rope_cos_sin produces, stored once per half)."""
+    pos = torch.arange(max_pos, device=device, dtype=torch.float32)
+    ang = pos[:, None] * inv_freq.to(device=device, dtype=torch.float32)[None, :]
+    return ang.cos().to(dtype).contiguous(), ang.sin().to(dtype).contiguous()
+
+
+def head_norm_rope(src, n_heads, head_dim, head_stride, dst, dst_head_stride, dst_row_stride, norm_w=None,
+                   norm_mode=-1, eps=1e-6, tables=None, rot=0, pos=None, pos_offset=0):
+    """Per (row, head) of src [n, *] (head h at column h * head_stride): optional head RMSNorm, RoPE on the
+    first rot dims at positions pos (int32 [n]) or pos_offset + row; written to dst + h * dst_head_stride +
+    row * dst_row_stride (element strides)."""
+    cos, sin = tables if tables is not None else (None, None)
+    ext().head_norm_rope(src, src.stride(0), head_stride, n_heads, head_dim, src.shape[0], norm_w, norm_mode,
+                         float(eps), cos, sin, rot, pos, pos_offset, dst, dst_head_stride, dst_row_stride)
+
+
+def gated_rmsnorm(o, z, w, heads, dv, eps, out=None):
+    """Gated DeltaNet output norm: o [n, heads * dv], z [n, heads * dv] (any row pitch)."""
+    if out is None:
+        out = torch.empty(o.shape[0], heads * dv, dtype=BF16, device=o.device)
+    ext().gated_rmsnorm(o, z, z.stride(0), w, out, heads, dv, float(eps))
+    return out
+
+
+def embed(table, ids):
+    out = torch.empty(ids.numel(), table.shape[1], dtype=BF16, device=table.device)
+    ext().embed_gather(table, ids.to(table.device, torch.long).contiguous(), out)
+    return out
+
+
+def attention(q, k_cache, v_cache, nk, scale, out, q_start=0, qpos=None, gate=None, gate_head=0):
+    """Causal GQA attention. q [hq, nq, hd] (any head pitch, row pitch hd); k_cache/v_cache [hkv, cap, hd]
+    (the first nk rows valid); queries at positions q_start + row (or qpos int32 [nq]); out [nq, hq * hd];
+    gate: a [nq, *] view whose head h starts at column h * gate_head (o * sigmoid(gate))."""
+    hq, nq, hd = q.shape
+    hkv = k_cache.shape[0]
+    ext().flash_attention(q, q.stride(0), k_cache, v_cache, k_cache.stride(0), out, hq, hkv, hd, nq, nk, qpos,
+                          q_start, float(scale), gate, gate.stride(0) if gate is not None else 0, gate_head)
+    return out
+
+
+def gdn_prep(proj, b_off, a_off, conv_w, conv_state, A_log, dt_bias, nk, nv, dk, dv):
+    """Conv + SiLU + l2norm + gates for the rows of proj [n, *]: returns q, k [nk, n, dk], v [nv, n, dv]
+    (bf16) and beta, g [nv, n] (fp32)."""
+    n = proj.shape[0]
+    dev = proj.device
+    q = torch.empty(nk, n, dk, dtype=BF16, device=dev)
+    k = torch.empty(nk, n, dk, dtype=BF16, device=dev)
+    v = torch.empty(nv, n, dv, dtype=BF16, device=dev)
+    beta = torch.empty(nv, n, dtype=torch.float32, device=dev)
+    g = torch.empty(nv, n, dtype=torch.float32, device=dev)
+    ext().gdn_prep(proj, b_off, a_off, conv_w, conv_state, A_log, dt_bias, n, nk, nv, dk, dv, conv_w.shape[1],
+                   q, k, v, beta, g)
+    return q, k, v, beta, g
+
+
+def gdn_conv_state_update(proj, state, channels):
+    ext().gdn_conv_state_update(proj, state, proj.shape[0], channels, state.shape[0] + 1)
+
+
+def gdn_scan(q, k, v, beta, g, state, out=None):
+    """Chunked gated delta rule continuing `state` [nv, dk, dv] fp32 (updated in place). q None: fill
+    mode (state only). out [n, nv * dv] bf16 (output mode)."""
+    nk, n, dk = k.shape
+    nv, _, dv = v.shape
+    n_pad = (n + 63) // 64 * 64
+    w_buf = torch.empty(nv, n_pad, dk, dtype=BF16, device=k.device)
+    u_buf = torch.empty(nv, n_pad, dv, dtype=BF16, device=k.device)
+    err = ext().error_word(k.device.index or 0)
+    ext().gdn_chunk_scan(q, k, v, beta, g, state, out, w_buf, u_buf, n, nk, nv, dk, dv, err)
+    return out

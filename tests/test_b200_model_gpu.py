@@ -1,0 +1,92 @@
+"""B200 models (sm_100a kernels) vs the torch models on the same random weights (bf16, cuda): exact
+forward logits, ridge-fill prefill through the engine, decode steps."""
+import pytest
+import torch
+
+from ridgefill_data_b200.engine.arm import Arm
+from ridgefill_data_b200.engine.prefill import finish, run_lower
+from ridgefill_data_b200.models.base import from_config
+from ridgefill_data_b200.models.config import ModelConfig, _hybrid_types
+from ridgefill_data_b200.ridge.projector import Projector
+
+pytestmark = pytest.mark.gpu
+
+HYB = ModelConfig(arch="qwen3_5", n_layers=8, hidden=512, vocab=1024, n_heads=4, n_kv=1, head_dim=256,
+                  intermediate=1024, eps=1e-6, rope_theta=1e7, partial_rotary=0.25, layer_types=_hybrid_types(8),
+                  gdn_nk=2, gdn_nv=4, gdn_dk=128, gdn_dv=128, conv_k=4, name="tiny-hybrid")
+LLAMA = ModelConfig(arch="llama", n_layers=4, hidden=512, vocab=1024, n_heads=8, n_kv=2, head_dim=64,
+                    intermediate=1536, eps=1e-5, rope_theta=5e5, rope_type="llama3",
+                    rope_llama3=dict(factor=8.0, low_freq_factor=1.0, high_freq_factor=4.0,
+                                     original_max_position_embeddings=8192), name="tiny-llama-gpu")
+QWEN3 = ModelConfig(arch="qwen3", n_layers=4, hidden=512, vocab=1024, n_heads=4, n_kv=2, head_dim=128,
+                    intermediate=1024, eps=1e-6, rope_theta=1e6, name="tiny-qwen3-gpu")
+
+
+def _pair(cfg):
+    ref = from_config(cfg, seed=0, device="cuda", std=0.05)
+    dut = from_config(cfg, seed=0, device="cuda", std=0.05, backend="b200")
+    return ref, dut
+
+
+def _fp32(cfg):
+    return from_config(cfg, seed=0, device="cuda", std=0.05, dtype=torch.float32)
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+
+@pytest.mark.parametrize("cfg", [HYB, LLAMA, QWEN3], ids=lambda c: c.name)
+def test_forward_exact_matches_torch(cfg):
+    ref, dut = _pair(cfg)
+    ids = torch.randint(0, cfg.vocab, (333,), generator=torch.Generator().manual_seed(1)).cuda()
+    keep = torch.arange(300, 333, device="cuda")
+    lr, _ = ref.forward_exact(ids, keep=keep)
+    ld, _ = dut.forward_exact(ids, keep=keep)
+    l32, _ = _fp32(cfg).forward_exact(ids, keep=keep)
+    # the kernel path is no further from fp32 than the torch bf16 path (plus a small margin)
+    assert _rel(ld, l32) < 1.5 * _rel(lr, l32) + 5e-3, (_rel(ld, l32), _rel(lr, l32))
+    assert (ld.argmax(-1) == l32.argmax(-1)).float().mean() > 0.8
+
+
+@pytest.mark.parametrize("cfg", [HYB, LLAMA], ids=lambda c: c.name)
+def test_ridge_fill_prefill_matches_torch(cfg):
+    ref, dut = _pair(cfg)
+    split = cfg.n_layers // 2
+    g = torch.Generator(device="cuda").manual_seed(3)
+    d = cfg.hidden
+    W = {i: (torch.eye(d, device="cuda") + 0.01 * torch.randn(d, d, device="cuda", generator=g)).bfloat16()
+         for i in range(split, cfg.n_layers)}
+    B = {i: (0.01 * torch.randn(d, device="cuda", generator=g)).bfloat16() for i in range(split, cfg.n_layers)}
+    arm = Arm("ridgefill", split=split, tail=100, fill="proj", projector=Projector(split, W, B))
+    ids = torch.randint(0, cfg.vocab, (400,), generator=torch.Generator().manual_seed(2)).cuda()
+    out = {}
+    for name, m in (("ref", ref), ("dut", dut), ("f32", _fp32(cfg))):
+        hs, lower = run_lower(m, ids, [split])
+        out[name] = finish(m, ids, hs[split], lower, arm, 4)
+    e_dut, e_ref = _rel(out["dut"][0], out["f32"][0]), _rel(out["ref"][0], out["f32"][0])
+    assert e_dut < 1.5 * e_ref + 5e-3, (e_dut, e_ref)
+    for i in range(split, cfg.n_layers):
+        cr, cd = out["ref"][1][i], out["dut"][1][i]
+        if cfg.layer_types[i] == "attn":
+            assert _rel(cd["k"], cr["k"]) < 3e-2 and _rel(cd["v"], cr["v"]) < 3e-2
+        else:
+            assert _rel(cd["rec"], cr["rec"]) < 5e-2
+
+
+def test_decode_steps_match_torch():
+    ref, dut = _pair(HYB)
+    f32 = _fp32(HYB)
+    ids = torch.randint(0, HYB.vocab, (130,), generator=torch.Generator().manual_seed(4)).cuda()
+    models = dict(ref=ref, dut=dut, f32=f32)
+    caches = {k: m.forward_exact(ids[:128])[1] for k, m in models.items()}
+    for t in (128, 129):
+        pos = torch.tensor([t], device="cuda")
+        lg = {}
+        for k, m in models.items():
+            h = m.embed(ids[t:t + 1])
+            for i in range(HYB.n_layers):
+                h = m.layer(i, h, pos, caches[k])
+            lg[k] = m.logits(h)
+        e_dut, e_ref = _rel(lg["dut"], lg["f32"]), _rel(lg["ref"], lg["f32"])
+        assert e_dut < 1.5 * e_ref + 5e-3, (t, e_dut, e_ref)

@@ -1,0 +1,116 @@
+"""sm_100a kernels vs the plain PyTorch fp32 oracle of the same op (ops/oracle.py)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from ridgefill_data_b200.ops import kernels as K
+from ridgefill_data_b200.ops import oracle as O
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30)).item()
+
+
+@pytest.mark.parametrize("zc", [False, True])
+def test_rmsnorm(zc):
+    torch.manual_seed(0)
+    x = torch.randn(37, 5120, device=dev).bfloat16()
+    w = (torch.randn(5120, device=dev) * 0.1 + (0 if zc else 1)).bfloat16()
+    got = K.rmsnorm(x, w, 1e-6, zc)
+    ref = (O.rms_norm_zc if zc else O.rms_norm)(x, w, 1e-6)
+    assert (got.float() - ref.float()).abs().max().item() <= 2 * ref.float().abs().max().item() / 128
+
+
+@pytest.mark.parametrize("hd,rot,mode", [(128, 128, 0), (256, 64, 1), (128, 128, -1)])
+def test_head_norm_rope(hd, rot, mode):
+    torch.manual_seed(1)
+    n, h = 50, 3
+    src = torch.randn(n, h * hd, device=dev).bfloat16()
+    w = (torch.randn(hd, device=dev) * 0.1 + (1 if mode == 0 else 0)).bfloat16()
+    inv = O.inv_freq_default(1e6, rot)
+    tables = K.rope_tables(inv, 4096, dev)
+    dst = torch.empty(h, n, hd, device=dev, dtype=torch.bfloat16)
+    K.head_norm_rope(src, h, hd, hd, dst, n * hd, hd, norm_w=w if mode >= 0 else None, norm_mode=mode, eps=1e-6,
+                     tables=tables, rot=rot, pos_offset=100)
+    x = src.view(n, h, hd)
+    if mode == 0:
+        x = O.rms_norm(x, w, 1e-6)
+    elif mode == 1:
+        x = O.rms_norm_zc(x, w, 1e-6)
+    cos, sin = O.rope_cos_sin(inv, torch.arange(100, 100 + n, device=dev), torch.bfloat16)
+    ref = O.apply_rope(x.transpose(0, 1), cos, sin)
+    assert _rel(dst, ref) < 1e-2
+
+
+@pytest.mark.parametrize("hd,hq,hkv,nq,nk,gated", [(128, 8, 2, 300, 300, False), (256, 6, 1, 200, 700, True),
+                                                    (64, 4, 4, 1, 513, False), (128, 4, 1, 130, 130, True)])
+def test_flash_attention(hd, hq, hkv, nq, nk, gated):
+    torch.manual_seed(2)
+    q = torch.randn(hq, nq, hd, device=dev).bfloat16()
+    k = torch.randn(hkv, nk + 64, hd, device=dev).bfloat16()
+    v = torch.randn(hkv, nk + 64, hd, device=dev).bfloat16()
+    gate = torch.randn(nq, hq * 2 * hd, device=dev).bfloat16()
+    out = torch.empty(nq, hq * hd, device=dev, dtype=torch.bfloat16)
+    K.attention(q, k, v, nk, hd ** -0.5, out, q_start=nk - nq, gate=gate[:, hd:] if gated else None,
+                gate_head=2 * hd)
+    ref = O.attend(q, k[:, :nk], v[:, :nk], hd ** -0.5)
+    if gated:
+        g = gate.view(nq, hq, 2 * hd)[..., hd:].reshape(nq, -1)
+        ref = ref * torch.sigmoid(g)
+    assert _rel(out, ref) < 2e-2
+
+
+def test_flash_attention_qpos():
+    torch.manual_seed(3)
+    hq, hkv, hd, nk = 4, 2, 128, 400
+    qpos = torch.tensor(sorted(set(torch.randint(0, nk, (90,)).tolist())), device=dev)
+    nq = qpos.numel()
+    q = torch.randn(hq, nq, hd, device=dev).bfloat16()
+    k = torch.randn(hkv, nk, hd, device=dev).bfloat16()
+    v = torch.randn(hkv, nk, hd, device=dev).bfloat16()
+    out = torch.empty(nq, hq * hd, device=dev, dtype=torch.bfloat16)
+    K.attention(q, k, v, nk, hd ** -0.5, out, qpos=qpos.int())
+    ref = O.attend_at(q, k, v, hd ** -0.5, qpos)
+    assert _rel(out, ref) < 2e-2
+
+
+@pytest.mark.parametrize("n,need_out,with_state", [(200, True, False), (64, True, True), (333, False, True),
+                                                   (1, True, True)])
+def test_gdn_prep_and_scan(n, need_out, with_state):
+    torch.manual_seed(4)
+    nk, nv, dk, dv, kk = 2, 6, 128, 128, 4
+    C = 2 * nk * dk + nv * dv
+    proj = (torch.randn(n, C + 2 * nv, device=dev) * 0.5).bfloat16()
+    conv_w = (torch.randn(C, kk, device=dev) / 2).bfloat16()
+    A_log = torch.empty(nv, device=dev).uniform_(0, 2.7)
+    dt = torch.randn(nv, device=dev) * 0.1
+    conv_state = (torch.randn(kk - 1, C, device=dev) * 0.5).bfloat16() if with_state else None
+    state = torch.randn(nv, dk, dv, device=dev) * 0.1 if with_state else torch.zeros(nv, dk, dv, device=dev)
+    q, k, v, beta, g = K.gdn_prep(proj, C, C + nv, conv_w, conv_state, A_log, dt, nk, nv, dk, dv)
+    # oracle
+    co, new_state = O.causal_conv(proj[:, :C], conv_state, conv_w)
+    rep = nv // nk
+    qo, ko, vo = co.split([nk * dk, nk * dk, nv * dv], -1)
+    qo = O.l2norm(qo.reshape(n, nk, dk).float()).transpose(0, 1) * dk ** -0.5
+    ko = O.l2norm(ko.reshape(n, nk, dk).float()).transpose(0, 1)
+    vo = vo.reshape(n, nv, dv).float().transpose(0, 1)
+    bo = torch.sigmoid(proj[:, C:C + nv]).float().T
+    go = (-A_log.exp() * F.softplus(proj[:, C + nv:].float() + dt)).T
+    assert _rel(q, qo) < 1e-2 and _rel(k, ko) < 1e-2 and _rel(v, vo) < 1e-2
+    assert _rel(beta, bo) < 1e-2 and _rel(g, go) < 1e-3
+    cs = conv_state.clone() if conv_state is not None else torch.zeros(kk - 1, C, device=dev, dtype=torch.bfloat16)
+    K.gdn_conv_state_update(proj, cs, C)
+    assert torch.equal(cs, new_state)
+    out = torch.empty(n, nv * dv, device=dev, dtype=torch.bfloat16) if need_out else None
+    st = state.clone()
+    K.gdn_scan(q if need_out else None, k, v, beta, g, st, out)
+    ro, rs, _ = O.delta_rule(qo.repeat_interleave(rep, 0), ko.repeat_interleave(rep, 0), vo, go, bo, state)
+    assert _rel(st, rs) < 3e-2
+    if need_out:
+        assert _rel(out.view(n, nv, dv).transpose(0, 1), ro) < 3e-2
+    from ridgefill_data_b200.ops._ext import check_errors
+    torch.cuda.synchronize()
+    check_errors()
