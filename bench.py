@@ -1,0 +1,245 @@
+#!/usr/bin/env python3
+"""Headline benchmark: RidgeFill prefill throughput (prompt tokens / TTFT) of the Qwen3.8-27B-shaped
+hybrid (64 layers, every 4th full attention, Gated DeltaNet elsewhere; d 5120) on B200.
+
+One step = one full prompt prefill through the public API (engine.prefill.run_lower + finish: layers
+< split exact on all rows, every later layer filled from its ridge map on the prefix rows, the exact
+tail through the full model) ending with the first-token logits. Random-init weights and maps of the
+named shapes, a seeded uniform-random prompt.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--seq 16384] [--tail 4096] [--split 32]
+  python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N      (one rank per GPU)
+  python bench.py --impl reference                                             (the reference arm)
+
+Multi-GPU: each rank prefills its own prompt (data parallel, weak scaling); the reported value is the
+whole-job tokens/s (sum over ranks of tokens / max-over-ranks device time).
+Timing: W untimed warm-up steps, then K steps bracketed by a barrier and torch.cuda.synchronize(),
+CUDA events on the launching stream, max over ranks. The weights (54 GB) exceed L2 (126 MB), so every
+step streams its inputs from HBM. SM clocks and throttle reasons are sampled with nvidia-smi during the
+timed region. e2e: the same metric timed on the host around the user-facing call, including the
+host->device copy of the prompt from pinned memory and the device->host read of the first token.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+# Published RidgeFill prompt time of the 27B hybrid at 16K tokens (llama.cpp fork, resident maps, split 16,
+# tail 4096, one A100 40 GB): 10.380 s -> tokens / s.
+BASELINE_TOK_S = {16384: 16384 / 10.380, 32768: 32768 / 21.112, 65536: 65536 / 46.284, 122880: 122880 / 100.014}
+METRIC = "prefill tok/s (RidgeFill TTFT), Qwen3.8-27B-shaped hybrid"
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of SM clock, max clock and throttle reasons while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=["nvidia-smi unavailable"])
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = list(self.rows)
+        if not rows:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=["no samples"])
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[3:]) if v.lower() == "active"})
+        return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=max(mx) if mx else None,
+                    reasons=reasons, samples=len(rows))
+
+
+def reference_arm(args):
+    msg = ("the reference (Approximate-Science/ridgefill-data) is a data release whose source tree has neither "
+           "setup.py nor pyproject.toml: pip reports 'Directory is not installable', so baseline/_ref cannot be "
+           "built")
+    if os.environ.get("RANK", "0") == "0":
+        print(json.dumps(dict(impl="reference", unavailable=msg)))
+
+
+def build_engine(args, device):
+    import torch
+    from ridgefill_data_b200.engine.arm import Arm
+    from ridgefill_data_b200.models.base import from_config
+    from ridgefill_data_b200.models.config import PRESETS
+    from ridgefill_data_b200.ridge.projector import Projector
+    cfg = PRESETS[args.model]
+    model = from_config(cfg, seed=0, device=device, backend="b200", std=0.02)
+    d = cfg.hidden
+    g = torch.Generator(device=device).manual_seed(123)
+    W, B = {}, {}
+    for i in range(args.split, cfg.n_layers):          # ridge maps of the right shape, near the identity
+        w = 0.01 * torch.randn(d, d, device=device, generator=g)
+        w.diagonal().add_(0.9)
+        W[i] = w.to(torch.bfloat16)
+        B[i] = (0.01 * torch.randn(d, device=device, generator=g)).to(torch.bfloat16)
+    arm = Arm("ridgefill", split=args.split, tail=args.tail, fill="proj", projector=Projector(args.split, W, B))
+    return cfg, model, arm
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--model", default="qwen3.8-27b")
+    ap.add_argument("--seq", type=int, default=16384)
+    ap.add_argument("--tail", type=int, default=4096)
+    ap.add_argument("--split", type=int, default=32)
+    ap.add_argument("--exact", action="store_true", help="also time full (exact) prefill for the speedup")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+    args.warmup = max(3, args.warmup)
+
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    from ridgefill_data_b200.engine.prefill import finish, run_lower
+    from ridgefill_data_b200.eval.data import uniform_prompt
+    from ridgefill_data_b200.ops._ext import check_errors, ext
+
+    cfg, model, arm = build_engine(args, device)
+    ids_host = uniform_prompt(args.seq, cfg.vocab, seed=2 + rank).pin_memory()
+    ids_dev = ids_host.to(device)
+    tok_host = torch.empty(1, dtype=torch.long).pin_memory()
+
+    def step(ids):
+        hs, lower = run_lower(model, ids, [arm.split])
+        logits, _, _ = finish(model, ids, hs[arm.split], lower, arm, keep=1, keep_cache=False)
+        return logits
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            step(ids_dev)
+        torch.cuda.synchronize()
+        check_errors(device)
+
+        # ---- device-timed region
+        sampler = ClockSampler(local)
+        sampler.start()
+        time.sleep(0.3)
+        barrier()
+        torch.cuda.synchronize()
+        launches0 = ext().launch_count()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            step(ids_dev)
+        t1.record()
+        torch.cuda.synchronize()
+        barrier()
+        launches = ext().launch_count() - launches0
+        clocks = sampler.stop()
+        ms = t0.elapsed_time(t1) / args.steps
+
+        # ---- end to end through the public API: pinned H2D of the prompt, prefill, D2H of the first token
+        barrier()
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        for _ in range(args.steps):
+            ids = ids_host.to(device, non_blocking=True)
+            logits = step(ids)
+            tok_host.copy_(logits[-1].argmax().view(1), non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        e2e_ms = (time.perf_counter() - w0) * 1e3 / args.steps
+        barrier()
+
+        exact_ms = None
+        if args.exact:
+            from ridgefill_data_b200.engine.arm import Arm
+            from ridgefill_data_b200.engine.prefill import prefill
+            ex = Arm("exact")
+            keep = torch.arange(args.seq - 1, args.seq, device=device)
+            prefill(model, ids_dev, ex)
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(max(1, args.steps // 2)):
+                model.forward_exact(ids_dev, keep=keep)
+            e1.record()
+            torch.cuda.synchronize()
+            exact_ms = e0.elapsed_time(e1) / max(1, args.steps // 2)
+        check_errors(device)
+
+    stats = torch.tensor([ms, e2e_ms, exact_ms or 0.0], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    ms_max, e2e_max, exact_max = stats.tolist()
+    tokens = args.seq * world
+    value = tokens / (ms_max / 1e3)
+    e2e_value = tokens / (e2e_max / 1e3)
+    base = BASELINE_TOK_S.get(args.seq)
+    if rank == 0:
+        line = dict(metric=METRIC, value=round(value, 1), unit="tokens/s", n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=round(ms_max, 3), higher_is_better=True,
+                    scaling="weak", vs_baseline=round(value / base, 3) if base else None, dtype="bf16",
+                    data="synthetic (seeded uniform prompt; random-init weights and ridge maps of the named shapes)",
+                    config=dict(model=args.model, global_batch=world, seq_len=args.seq, split=args.split,
+                                tail=args.tail, parallelism=f"dp{world}",
+                                l2="inputs larger than L2 (54 GB of weights streamed per step)"),
+                    clocks=clocks, gpu_launches=int(launches),
+                    e2e=dict(value=round(e2e_value, 1), unit="tokens/s", ms_per_step=round(e2e_max, 3),
+                             h2d_bytes_per_step=int(ids_host.numel() * ids_host.element_size()),
+                             d2h_bytes_per_step=int(tok_host.numel() * tok_host.element_size())),
+                    ttft_ms=round(ms_max, 3))
+        if exact_ms:
+            line.update(exact_prefill_ms=round(exact_max, 3), speedup_vs_exact=round(exact_max / ms_max, 3))
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

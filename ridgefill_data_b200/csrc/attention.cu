@@ -229,7 +229,7 @@ static void launch_fa(const AttnArgs& a, cudaStream_t stream) {
     set = true;
   }
   dim3 grid((a.nq + FA_BM - 1) / FA_BM, a.hq);
-  flash_attn_kernel<HD><<<grid, FA_THREADS, SMEM, stream>>>(a);
+  flash_attn_kernel<HD><<<grid, FA_THREADS, SMEM, stream>>>(a); count_launch();
 }
 
 void flash_attention(const AttnArgs& a, cudaStream_t stream) {

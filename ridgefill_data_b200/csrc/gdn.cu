@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(256) gdn_prep_kernel(GdnPrepArgs a) {
 
 void gdn_prep(const GdnPrepArgs& a, cudaStream_t stream) {
   if (a.n <= 0) return;
-  gdn_prep_kernel<<<a.n, 256, 0, stream>>>(a);
+  gdn_prep_kernel<<<a.n, 256, 0, stream>>>(a); count_launch();
 }
 
 // new state = last K-1 rows of [old state; proj rows]
@@ -106,7 +106,7 @@ __global__ void gdn_conv_state_kernel(const __nv_bfloat16* proj, long proj_row, 
 
 void gdn_conv_state_update(const __nv_bfloat16* proj, long proj_row, __nv_bfloat16* state, int n, int C, int K,
                            cudaStream_t stream) {
-  gdn_conv_state_kernel<<<(C + 255) / 256, 256, 0, stream>>>(proj, proj_row, state, n, C, K);
+  gdn_conv_state_kernel<<<(C + 255) / 256, 256, 0, stream>>>(proj, proj_row, state, n, C, K); count_launch();
 }
 
 // ------------------------------------------------------------------------------------ wy kernel
@@ -523,8 +523,8 @@ void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream) {
     cudaFuncSetAttribute(gdn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(ScanSmem));
     set = true;
   }
-  gdn_wy_kernel<<<dim3(n_chunks, a.nv), 128, sizeof(WySmem), stream>>>(a, n_pad);
-  gdn_scan_kernel<<<dim3(a.nv, a.dv / DVS), 128, sizeof(ScanSmem), stream>>>(a, n_pad);
+  gdn_wy_kernel<<<dim3(n_chunks, a.nv), 128, sizeof(WySmem), stream>>>(a, n_pad); count_launch();
+  gdn_scan_kernel<<<dim3(a.nv, a.dv / DVS), 128, sizeof(ScanSmem), stream>>>(a, n_pad); count_launch();
 }
 
 }  // namespace rf

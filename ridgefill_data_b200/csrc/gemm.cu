@@ -16,6 +16,7 @@
 // kEpiF32 (fp32 out), kEpiF64Acc (fp64 out += acc, split-K chunks added with atomics: the
 // fp32-per-block, fp64-across-blocks accumulation of the ridge sufficient statistics).
 #include "gemm.h"
+#include "kernels.h"
 #include "ptx.cuh"
 
 #include <cudaTypedefs.h>
@@ -406,6 +407,7 @@ static void launch_gemm(const GemmOperands& op, GemmArgs args, int max_ctas, cud
   if (num_tiles < ctas) ctas = num_tiles;
   if (ctas <= 0) return;
   kernel<<<ctas, kGemmThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, args);
+  count_launch();
 }
 
 void gemm_bf16(const GemmOperands& op, GemmArgs args, int epi, int bn, int max_ctas, cudaStream_t stream) {

@@ -4,7 +4,16 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
+#include <atomic>
+
 namespace rf {
+
+// Host-side count of kernel launches issued by this library (bench.py reports it per timed region).
+inline std::atomic<long>& launch_counter() {
+  static std::atomic<long> c{0};
+  return c;
+}
+inline void count_launch(long n = 1) { launch_counter().fetch_add(n, std::memory_order_relaxed); }
 
 // ---- norm.cu
 void rmsnorm(const __nv_bfloat16* x, long ldx, const __nv_bfloat16* w, __nv_bfloat16* y, long ldy, int rows, int d,

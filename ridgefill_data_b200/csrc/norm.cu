@@ -85,6 +85,7 @@ void rmsnorm(const __nv_bfloat16* x, long ldx, const __nv_bfloat16* w, __nv_bflo
     rmsnorm_kernel<1><<<rows, 256, 0, stream>>>(x, ldx, w, y, ldy, d, eps);
   else
     rmsnorm_kernel<0><<<rows, 256, 0, stream>>>(x, ldx, w, y, ldy, d, eps);
+  count_launch();
 }
 
 // ----------------------------------------------------------------------------- head_norm_rope
@@ -148,7 +149,7 @@ void head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t stream) {
   if (a.n_rows <= 0 || a.n_heads <= 0) return;
   const long warps = (long)a.n_rows * a.n_heads;
   const int blocks = (int)((warps * 32 + 255) / 256);
-  head_norm_rope_kernel<<<blocks, 256, 0, stream>>>(a);
+  head_norm_rope_kernel<<<blocks, 256, 0, stream>>>(a); count_launch();
 }
 
 // ------------------------------------------------------------------------------ gated_rmsnorm
@@ -189,7 +190,7 @@ void gated_rmsnorm(const __nv_bfloat16* o, long ldo, const __nv_bfloat16* z, lon
   if (rows <= 0) return;
   const long warps = (long)rows * heads;
   gated_rmsnorm_kernel<<<(int)((warps * 32 + 255) / 256), 256, 0, stream>>>(o, ldo, z, ldz, w, y, ldy, rows, heads,
-                                                                            dv, eps);
+                                                                            dv, eps); count_launch();
 }
 
 // ------------------------------------------------------------------------------- embed_gather
@@ -206,7 +207,7 @@ __global__ void embed_gather_kernel(const __nv_bfloat16* __restrict__ table, con
 void embed_gather(const __nv_bfloat16* table, const int64_t* ids, __nv_bfloat16* out, int rows, int d, long vocab,
                   cudaStream_t stream) {
   if (rows <= 0) return;
-  embed_gather_kernel<<<rows, 128, 0, stream>>>(table, ids, out, d, vocab);
+  embed_gather_kernel<<<rows, 128, 0, stream>>>(table, ids, out, d, vocab); count_launch();
 }
 
 }  // namespace rf
