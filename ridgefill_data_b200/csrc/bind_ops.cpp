@@ -143,7 +143,7 @@ void gdn_prep(Tensor proj, int64_t b_off, int64_t a_off, Tensor conv_w, OptT con
   need(beta, at::kFloat, "beta");
   need(g, at::kFloat, "g");
   TORCH_CHECK(proj.stride(1) == 1 && conv_w.is_contiguous(), "gdn_prep: layouts");
-  TORCH_CHECK(dk % 32 == 0 && dv % 32 == 0 && dk <= 256 && dv <= 256 && K <= 8, "gdn_prep: dims");
+  TORCH_CHECK(dk % 32 == 0 && dv % 32 == 0 && dk <= 128 && dv <= 128 && K <= 8, "gdn_prep: dims");
   c10::cuda::CUDAGuard gd(proj.device());
   rf::GdnPrepArgs a{};
   a.proj = cbf(proj);
@@ -180,7 +180,7 @@ void gdn_conv_state_update(Tensor proj, Tensor state, int64_t n, int64_t C, int6
 }
 
 void gdn_chunk_scan(OptT q, Tensor k, Tensor v, Tensor beta, Tensor g, Tensor state, OptT out, Tensor w_buf,
-                    Tensor u_buf, int64_t n, int64_t nk, int64_t nv, int64_t dk, int64_t dv, Tensor err) {
+                    Tensor u_buf, OptT s_buf, OptT vt_buf, int64_t n, int64_t nk, int64_t nv, int64_t dk, int64_t dv, Tensor err) {
   need(k, at::kBFloat16, "k");
   need(v, at::kBFloat16, "v");
   need(beta, at::kFloat, "beta");
@@ -188,7 +188,7 @@ void gdn_chunk_scan(OptT q, Tensor k, Tensor v, Tensor beta, Tensor g, Tensor st
   need(state, at::kFloat, "state");
   need(w_buf, at::kBFloat16, "w_buf");
   need(u_buf, at::kBFloat16, "u_buf");
-  TORCH_CHECK(dk == 128 && dv % 64 == 0 && dv <= 128 && nv % nk == 0, "gdn_chunk_scan: dk 128, dv 64|128");
+  TORCH_CHECK(dk == 128 && dv % 64 == 0 && dv <= 128 && nv % nk == 0, "gdn_chunk_scan: dk 128, dv 64 | 128");
   const int64_t n_pad = (n + 63) / 64 * 64;
   TORCH_CHECK(w_buf.numel() >= nv * n_pad * dk && u_buf.numel() >= nv * n_pad * dv, "gdn_chunk_scan: scratch size");
   TORCH_CHECK(state.is_contiguous() && state.numel() == nv * dk * dv, "gdn_chunk_scan: state [nv, dk, dv]");
@@ -197,7 +197,14 @@ void gdn_chunk_scan(OptT q, Tensor k, Tensor v, Tensor beta, Tensor g, Tensor st
   if (q.has_value()) {
     need(*q, at::kBFloat16, "q");
     a.q = cbf(*q);
-    TORCH_CHECK(out.has_value(), "gdn_chunk_scan: output mode needs out");
+    TORCH_CHECK(out.has_value() && s_buf.has_value() && vt_buf.has_value(),
+                "gdn_chunk_scan: output mode needs out, s_buf and vt_buf");
+    need(*s_buf, at::kBFloat16, "s_buf");
+    need(*vt_buf, at::kBFloat16, "vt_buf");
+    TORCH_CHECK(s_buf->numel() >= nv * (n_pad / 64) * dk * dv, "gdn_chunk_scan: s_buf size");
+    TORCH_CHECK(vt_buf->numel() >= nv * n_pad * dv, "gdn_chunk_scan: vt_buf size");
+    a.s_buf = bf(*s_buf);
+    a.vt_buf = bf(*vt_buf);
   }
   a.k = cbf(k);
   a.v = cbf(v);

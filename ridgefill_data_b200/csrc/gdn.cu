@@ -26,69 +26,114 @@ __device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log
 __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
 // ---------------------------------------------------------------------------------------- prep
-// grid: n tokens; block 256 threads (8 warps) loop over head tasks: [0, nk) q heads, [nk, 2nk) k heads,
-// [2nk, 2nk + nv) v heads.
-__global__ void __launch_bounds__(256) gdn_prep_kernel(GdnPrepArgs a) {
-  const int tkn = blockIdx.x;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
+// grid: (token blocks of 64, head tasks); head task [0, nk) q heads, [nk, 2nk) k heads, [2nk, 2nk + nv) v
+// heads. The CTA stages rows [t0 - (K-1), t0 + 64) of its head's channels in shared memory (earlier rows
+// from the conv state), then each warp produces 16 tokens: lane j owns channels 4j..4j+3.
+constexpr int PREP_T = 64;
+
+__global__ void __launch_bounds__(128) gdn_prep_kernel(GdnPrepArgs a) {
+  __shared__ __align__(16) __nv_bfloat16 rows[(PREP_T + 7) * 128];
+  __shared__ float wsh[128 * 8];
+  const int t0 = blockIdx.x * PREP_T;
+  const int task = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C = 2 * a.nk * a.dk + a.nv * a.dv;
-  const int tasks = 2 * a.nk + a.nv;
-  const __nv_bfloat16* prow = a.proj + (long)tkn * a.proj_row;
-  for (int task = warp; task < tasks; task += 8) {
-    int c0, dh;
-    if (task < 2 * a.nk) {
-      c0 = task * a.dk;
-      dh = a.dk;
-    } else {
-      c0 = 2 * a.nk * a.dk + (task - 2 * a.nk) * a.dv;
-      dh = a.dv;
+  int c0, dh;
+  if (task < 2 * a.nk) {
+    c0 = task * a.dk;
+    dh = a.dk;
+  } else {
+    c0 = 2 * a.nk * a.dk + (task - 2 * a.nk) * a.dv;
+    dh = a.dv;
+  }
+  const int K1 = a.K - 1;
+  const int nrows = min(PREP_T, a.n - t0) + K1;
+  // stage rows (16-byte vectors when the row pitches allow them)
+  const bool vec = (a.proj_row % 8 == 0) && (C % 8 == 0);
+  if (vec) {
+    for (int v = threadIdx.x; v < nrows * (dh / 8); v += 128) {
+      const int r = v / (dh / 8), c = (v % (dh / 8)) * 8;
+      const int src = t0 - K1 + r;
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (src >= 0)
+        val = *reinterpret_cast<const uint4*>(a.proj + (long)src * a.proj_row + c0 + c);
+      else if (a.conv_state != nullptr)
+        val = *reinterpret_cast<const uint4*>(a.conv_state + (long)(K1 + src) * C + c0 + c);
+      *reinterpret_cast<uint4*>(&rows[r * 128 + c]) = val;
     }
-    const int per = dh / 32;
-    float val[8];
+  } else {
+    for (int v = threadIdx.x; v < nrows * dh; v += 128) {
+      const int r = v / dh, c = v % dh;
+      const int src = t0 - K1 + r;
+      __nv_bfloat16 val = __float2bfloat16(0.f);
+      if (src >= 0)
+        val = a.proj[(long)src * a.proj_row + c0 + c];
+      else if (a.conv_state != nullptr)
+        val = a.conv_state[(long)(K1 + src) * C + c0 + c];
+      rows[r * 128 + c] = val;
+    }
+  }
+  // weights transposed to [tap][channel] so lanes (consecutive channels) hit distinct banks
+  for (int v = threadIdx.x; v < dh * a.K; v += 128) {
+    const int ch = v / a.K, tap = v % a.K;
+    wsh[tap * 128 + ch] = __bfloat162float(a.conv_w[(long)c0 * a.K + v]);
+  }
+  __syncthreads();
+  const int per = dh / 32;   // channels per lane: lane + 32 j
+  const bool is_qk = task < 2 * a.nk;
+  const bool is_q = task < a.nk;
+  const float qscale = rsqrtf((float)a.dk);
+  for (int tt = warp; tt < PREP_T; tt += 4) {
+    const int tkn = t0 + tt;
+    if (tkn >= a.n) break;
+    float val[4];
     float ss = 0.f;
-    for (int j = 0; j < per; ++j) {
-      const int c = c0 + lane * per + j;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j >= per) break;
+      const int ch = j * 32 + lane;
       float acc = 0.f;
-      for (int tap = 0; tap < a.K; ++tap) {
-        const int r = tkn - (a.K - 1) + tap;   // source row (negative: conv state)
-        float x;
-        if (r >= 0)
-          x = __bfloat162float(a.proj[(long)r * a.proj_row + c]);
-        else
-          x = a.conv_state != nullptr ? __bfloat162float(a.conv_state[(long)(a.K - 1 + r) * C + c]) : 0.f;
-        acc += x * __bfloat162float(a.conv_w[(long)c * a.K + tap]);
-      }
-      const float y = bf16r(acc / (1.f + expf(-acc)));
+      for (int tap = 0; tap < a.K; ++tap) acc += __bfloat162float(rows[(tt + tap) * 128 + ch]) * wsh[tap * 128 + ch];
+      const float y = bf16r(acc / (1.f + __expf(-acc)));
       val[j] = y;
       ss += y * y;
     }
-    if (task < 2 * a.nk) {
+    float scale = 1.f;
+    if (is_qk) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      float inv = rsqrtf(ss + 1e-6f);
-      const bool is_q = task < a.nk;
-      if (is_q) inv *= rsqrtf((float)a.dk);
-      const int hh = is_q ? task : task - a.nk;
-      __nv_bfloat16* dst = (is_q ? a.q : a.k) + ((long)hh * a.n + tkn) * a.dk;
-      for (int j = 0; j < per; ++j) dst[lane * per + j] = __float2bfloat16(val[j] * inv);
-    } else {
-      const int hh = task - 2 * a.nk;
-      __nv_bfloat16* dst = a.v + ((long)hh * a.n + tkn) * a.dv;
-      for (int j = 0; j < per; ++j) dst[lane * per + j] = __float2bfloat16(val[j]);
+      scale = rsqrtf(ss + 1e-6f) * (is_q ? qscale : 1.f);
     }
+    __nv_bfloat16* dst;
+    if (is_qk) {
+      const int hh = is_q ? task : task - a.nk;
+      dst = (is_q ? a.q : a.k) + ((long)hh * a.n + tkn) * a.dk;
+    } else {
+      dst = a.v + ((long)(task - 2 * a.nk) * a.n + tkn) * a.dv;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < per) dst[j * 32 + lane] = __float2bfloat16(val[j] * scale);
   }
-  for (int h = threadIdx.x; h < a.nv; h += blockDim.x) {
-    const float b = __bfloat162float(prow[a.b_off + h]);
-    const float av = __bfloat162float(prow[a.a_off + h]);
-    a.beta[(long)h * a.n + tkn] = bf16r(1.f / (1.f + expf(-b)));
-    a.g[(long)h * a.n + tkn] = -expf(a.A_log[h]) * softplus_f(av + a.dt_bias[h]);
+  if (task == 0) {   // gates of this token block
+    for (int v = threadIdx.x; v < PREP_T * a.nv; v += 128) {
+      const int tt = v / a.nv, h = v % a.nv;
+      const int tkn = t0 + tt;
+      if (tkn >= a.n) continue;
+      const __nv_bfloat16* prow = a.proj + (long)tkn * a.proj_row;
+      const float b = __bfloat162float(prow[a.b_off + h]);
+      const float av = __bfloat162float(prow[a.a_off + h]);
+      a.beta[(long)h * a.n + tkn] = bf16r(1.f / (1.f + expf(-b)));
+      a.g[(long)h * a.n + tkn] = -expf(a.A_log[h]) * softplus_f(av + a.dt_bias[h]);
+    }
   }
 }
 
 void gdn_prep(const GdnPrepArgs& a, cudaStream_t stream) {
   if (a.n <= 0) return;
-  gdn_prep_kernel<<<a.n, 256, 0, stream>>>(a); count_launch();
+  dim3 grid((a.n + PREP_T - 1) / PREP_T, 2 * a.nk + a.nv);
+  gdn_prep_kernel<<<grid, 128, 0, stream>>>(a);
+  count_launch();
 }
 
 // new state = last K-1 rows of [old state; proj rows]
@@ -112,16 +157,37 @@ void gdn_conv_state_update(const __nv_bfloat16* proj, long proj_row, __nv_bfloat
 // ------------------------------------------------------------------------------------ wy kernel
 constexpr int DK = 128;           // key head dim supported by the chunk kernels
 constexpr int PK = DK + 8;        // smem pitch of [64][dk] tiles
+constexpr int PA = GC + 1;        // fp32 [64][64] pitch
 
 struct WySmem {
   __nv_bfloat16 k[GC * PK];
-  __nv_bfloat16 kb[GC * PK];
-  __nv_bfloat16 vb[GC * PK];      // dv <= 128
-  __nv_bfloat16 t16[GC * (GC + 8)];
-  float A[GC * (GC + 1)];
+  __nv_bfloat16 v[GC * PK];       // dv <= 128
+  __nv_bfloat16 ta[GC * (GC + 8)];  // T diag(beta e^gam)
+  __nv_bfloat16 tb[GC * (GC + 8)];  // T diag(beta)
+  float A[GC * PA];               // strictly lower A, then scratch
+  float T[GC * PA];               // (I + A)^-1
   float gam[GC];
   float beta[GC];
+  float eg[GC];
 };
+
+// 16x16 fp32 block product: out (+)= sign * X_blk Y_blk; thread owns two adjacent outputs of one row.
+__device__ __forceinline__ void blk_mm(float* out, const float* X, const float* Y, int xb_r, int xb_c, int yb_r,
+                                       int yb_c, int ob_r, int ob_c, bool accumulate, float sign, int tid) {
+  const int r = tid >> 3, c = (tid & 7) * 2;
+  const float* xr = X + (xb_r * 16 + r) * PA + xb_c * 16;
+  const float* yc = Y + (yb_r * 16) * PA + yb_c * 16 + c;
+  float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float x = xr[k];
+    a0 += x * yc[k * PA];
+    a1 += x * yc[k * PA + 1];
+  }
+  float* o = out + (ob_r * 16 + r) * PA + ob_c * 16 + c;
+  o[0] = accumulate ? o[0] + sign * a0 : sign * a0;
+  o[1] = accumulate ? o[1] + sign * a1 : sign * a1;
+}
 
 __global__ void __launch_bounds__(128) gdn_wy_kernel(GdnScanArgs a, int n_pad) {
   extern __shared__ __align__(16) uint8_t wy_raw[];
@@ -135,7 +201,6 @@ __global__ void __launch_bounds__(128) gdn_wy_kernel(GdnScanArgs a, int n_pad) {
   const int rows = min(GC, a.n - r0);
   const int dv = a.dv;
 
-  // loads
   const __nv_bfloat16* kp = a.k + ((long)kh * a.n + r0) * DK;
   const __nv_bfloat16* vp = a.v + ((long)h * a.n + r0) * dv;
   for (int v = tid; v < GC * (DK / 8); v += 128) {
@@ -146,7 +211,7 @@ __global__ void __launch_bounds__(128) gdn_wy_kernel(GdnScanArgs a, int n_pad) {
   for (int v = tid; v < GC * (dv / 8); v += 128) {
     const int r = v / (dv / 8), c = (v % (dv / 8)) * 8;
     const bool ok = r < rows;
-    cp_async16(&s.vb[r * PK + c], ok ? vp + (long)r * dv + c : vp, ok);
+    cp_async16(&s.v[r * PK + c], ok ? vp + (long)r * dv + c : vp, ok);
   }
   cp_async_commit();
   if (tid < GC) {
@@ -156,22 +221,23 @@ __global__ void __launch_bounds__(128) gdn_wy_kernel(GdnScanArgs a, int n_pad) {
   }
   __syncthreads();
   if (warp == 0) {  // inclusive cumsum of 64 values, 2 per lane
-    float x0 = s.gam[2 * lane], x1 = s.gam[2 * lane + 1];
-    float pair = x0 + x1;
+    const float x0 = s.gam[2 * lane], x1 = s.gam[2 * lane + 1];
+    const float pair = x0 + x1;
     float incl = pair;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const float y = __shfl_up_sync(0xffffffffu, incl, o);
       if (lane >= o) incl += y;
     }
-    const float excl = incl - pair;
-    s.gam[2 * lane] = excl + x0;
+    s.gam[2 * lane] = incl - pair + x0;
     s.gam[2 * lane + 1] = incl;
+    s.eg[2 * lane] = __expf(incl - pair + x0);
+    s.eg[2 * lane + 1] = __expf(incl);
   }
   cp_async_wait<0>();
   __syncthreads();
 
-  // KK^T (16 rows per warp) -> A = strictly lower, beta_i * kk * exp(gam_i - gam_j)
+  // A = strictly lower(beta_i * k_i.k_j * exp(gam_i - gam_j)) from KK^T (16 rows per warp)
   {
     float acc[8][4];
 #pragma unroll
@@ -188,330 +254,439 @@ __global__ void __launch_bounds__(128) gdn_wy_kernel(GdnScanArgs a, int n_pad) {
         mma_bf16(acc[2 * j2 + 1], af, bf[2], bf[3]);
       }
     }
+    const int ra = warp * 16 + g, rb = ra + 8;
+    const float ba = s.beta[ra], bb = s.beta[rb], ga = s.gam[ra], gb = s.gam[rb];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int r = warp * 16 + g + (e >= 2 ? 8 : 0);
+        const int r = (e >= 2) ? rb : ra;
         const int c = j * 8 + 2 * t + (e & 1);
-        const float v = (r > c) ? s.beta[r] * acc[j][e] * expf(s.gam[r] - s.gam[c]) : 0.f;
-        s.A[r * (GC + 1) + c] = v;
+        const float v = (r > c) ? ((e >= 2) ? bb : ba) * acc[j][e] * __expf(((e >= 2) ? gb : ga) - s.gam[c]) : 0.f;
+        s.A[r * PA + c] = v;
+        s.T[r * PA + c] = 0.f;
       }
     }
   }
-  // scaled operands: kb = beta e^gam k, vb = beta v (in place over the loaded v)
-  for (int v = tid; v < GC * DK; v += 128) {
-    const int r = v / DK, c = v % DK;
-    s.kb[r * PK + c] = __float2bfloat16(s.beta[r] * expf(s.gam[r]) * __bfloat162float(s.k[r * PK + c]));
-  }
-  for (int v = tid; v < GC * dv; v += 128) {
-    const int r = v / dv, c = v % dv;
-    s.vb[r * PK + c] = __float2bfloat16(s.beta[r] * __bfloat162float(s.vb[r * PK + c]));
-  }
   __syncthreads();
-  // T = (I + A)^-1, column c by thread c: T[i][c] = [i == c] - sum_{c <= j < i} A[i][j] T[j][c]
-  if (tid < GC) {
-    const int c = tid;
-    float col[GC];
-#pragma unroll
-    for (int i = 0; i < GC; ++i) col[i] = 0.f;
-#pragma unroll
-    for (int i = 0; i < GC; ++i) {
-      if (i < c) continue;
-      float v = (i == c) ? 1.f : 0.f;
-#pragma unroll
-      for (int j = 0; j < i; ++j)
-        if (j >= c) v -= s.A[i * (GC + 1) + j] * col[j];
-      col[i] = v;
+  // (I + A)^-1, blocked 4 x 4 in 16 x 16 blocks. Diagonal blocks by forward substitution: warp w inverts
+  // block w, lane c < 16 owning column c.
+  if (lane < 16) {
+    const int b0 = warp * 16;
+    const int c = lane;
+    for (int r = 0; r < 16; ++r) {
+      float v = (r == c) ? 1.f : 0.f;
+      for (int j = c; j < r; ++j) v -= s.A[(b0 + r) * PA + b0 + j] * s.T[(b0 + j) * PA + b0 + c];
+      s.T[(b0 + r) * PA + b0 + c] = (r >= c) ? v : 0.f;
     }
-#pragma unroll
-    for (int i = 0; i < GC; ++i) s.t16[i * (GC + 8) + c] = __float2bfloat16(col[i]);
   }
   __syncthreads();
-  // W = T kb [64 x dk], U = T vb [64 x dv]
-  __nv_bfloat16* wdst = a.w_buf + ((long)h * n_pad + r0) * DK;
-  __nv_bfloat16* udst = a.u_buf + ((long)h * n_pad + r0) * dv;
+  // Off-diagonal blocks by distance: T_ij = -T_ii * sum_{k=j}^{i-1} A_ik T_kj (scratch X_ij in the zero
+  // upper triangle of A: block (j, i)).
+  for (int d = 1; d < 4; ++d) {
+    for (int j = 0; j + d < 4; ++j) {
+      const int i = j + d;
+      for (int k = j; k < i; ++k) blk_mm(s.A, s.A, s.T, i, k, k, j, j, i, k > j, 1.f, tid);
+    }
+    __syncthreads();
+    for (int j = 0; j + d < 4; ++j) {
+      const int i = j + d;
+      blk_mm(s.T, s.T, s.A, i, i, j, i, i, j, false, -1.f, tid);
+    }
+    __syncthreads();
+  }
+  // ta = T diag(beta e^gam), tb = T diag(beta) (bf16, lower triangle incl. diagonal)
+  for (int v = tid; v < GC * (GC / 2); v += 128) {
+    const int r = v / (GC / 2), c = (v % (GC / 2)) * 2;
+    const float t0 = r >= c ? s.T[r * PA + c] : 0.f;
+    const float t1 = r >= c + 1 ? s.T[r * PA + c + 1] : 0.f;
+    *reinterpret_cast<uint32_t*>(&s.ta[r * (GC + 8) + c]) =
+        pack2(t0 * s.beta[c] * s.eg[c], t1 * s.beta[c + 1] * s.eg[c + 1]);
+    *reinterpret_cast<uint32_t*>(&s.tb[r * (GC + 8) + c]) = pack2(t0 * s.beta[c], t1 * s.beta[c + 1]);
+  }
+  __syncthreads();
+  // W = ta k [64 x dk] -> w_buf rows; U^T = v^T tb^T [dv x 64] -> u_buf as per-chunk [dv][64] tiles
+  {
+    __nv_bfloat16* wdst = a.w_buf + ((long)h * n_pad + r0) * DK;
+    uint32_t af[4][4];
 #pragma unroll
-  for (int which = 0; which < 2; ++which) {
-    const __nv_bfloat16* B = which == 0 ? s.kb : s.vb;
-    const int ncols = which == 0 ? DK : dv;
-    __nv_bfloat16* dst = which == 0 ? wdst : udst;
-    for (int nb = 0; nb < ncols; nb += 64) {
+    for (int ks = 0; ks < GC / 16; ++ks) lda_row(af[ks], s.ta, GC + 8, warp * 16, ks * 16, lane);
+    for (int nb = 0; nb < DK; nb += 64) {
       float acc[8][4];
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 #pragma unroll
       for (int ks = 0; ks < GC / 16; ++ks) {
-        uint32_t af[4];
-        lda_row(af, s.t16, GC + 8, warp * 16, ks * 16, lane);
 #pragma unroll
         for (int j2 = 0; j2 < 4; ++j2) {
           uint32_t bf[4];
-          ldb_kn(bf, B, PK, nb + j2 * 16, ks * 16, lane);
-          mma_bf16(acc[2 * j2], af, bf[0], bf[1]);
-          mma_bf16(acc[2 * j2 + 1], af, bf[2], bf[3]);
+          ldb_kn(bf, s.k, PK, nb + j2 * 16, ks * 16, lane);
+          mma_bf16(acc[2 * j2], af[ks], bf[0], bf[1]);
+          mma_bf16(acc[2 * j2 + 1], af[ks], bf[2], bf[3]);
         }
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int r = warp * 16 + g;
         const int c = nb + j * 8 + 2 * t;
-        *reinterpret_cast<uint32_t*>(dst + (long)r * ncols + c) = pack2(acc[j][0], acc[j][1]);
-        *reinterpret_cast<uint32_t*>(dst + (long)(r + 8) * ncols + c) = pack2(acc[j][2], acc[j][3]);
+        *reinterpret_cast<uint32_t*>(wdst + (long)r * DK + c) = pack2(acc[j][0], acc[j][1]);
+        *reinterpret_cast<uint32_t*>(wdst + (long)(r + 8) * DK + c) = pack2(acc[j][2], acc[j][3]);
+      }
+    }
+  }
+  {
+    __nv_bfloat16* udst = a.u_buf + ((long)h * n_pad + r0) * dv;   // [dv][64] tile of this chunk
+    for (int mb = warp * 16; mb < dv; mb += 64) {
+      float acc[8][4];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < GC / 16; ++ks) {
+        uint32_t af[4];
+        lda_trans(af, s.v, PK, mb, ks * 16, lane);        // A = v^T [dv][rows]
+#pragma unroll
+        for (int j2 = 0; j2 < 4; ++j2) {
+          uint32_t bf[4];
+          ldb_nk(bf, s.tb, GC + 8, j2 * 16, ks * 16, lane);  // B[k][n] = tb[n][k]
+          mma_bf16(acc[2 * j2], af, bf[0], bf[1]);
+          mma_bf16(acc[2 * j2 + 1], af, bf[2], bf[3]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int m = mb + g;
+        const int c = j * 8 + 2 * t;
+        *reinterpret_cast<uint32_t*>(udst + (long)m * GC + c) = pack2(acc[j][0], acc[j][1]);
+        *reinterpret_cast<uint32_t*>(udst + (long)(m + 8) * GC + c) = pack2(acc[j][2], acc[j][3]);
       }
     }
   }
 }
 
-// ---------------------------------------------------------------------------------- scan kernel
-constexpr int DVS = 64;           // state columns per CTA
-constexpr int PV = DVS + 8;
+// ------------------------------------------------------------------------------ state pass kernel
+// Sequential over chunks, parallel over (value head, 64-row slice of S^T); 4 warps, each owning 16 rows of
+// the transposed state S^T [dv][dk] in mma accumulators. Per chunk, per warp (no inter-warp exchange):
+//   V'^T = U^T - S^T W^T          (A = S^T straight from the accumulators, B = W rows from smem)
+//   S^T  <- e^(gl) S^T + (V'^T diag(e^(gl - gam))) k     (A = scaled V'^T from the accumulators, B = k rows)
+// The C-fragment layout of one product is the A-fragment layout of the next, so S and V' never leave the
+// registers. Output mode stores the chunk-start S^T and the unscaled V'^T (bf16) for the output pass.
+// Inputs of chunk c+2 are fetched (cp.async, 3 stages) while chunk c computes.
+constexpr int SVS = 64;           // S^T rows (value dims) per CTA
+constexpr int SST = 3;            // pipeline stages
+constexpr int PU = GC + 8;        // pitch of the [dv][64] U^T tiles
 
-struct ScanSmem {
-  __nv_bfloat16 w[2][GC * PK];
-  __nv_bfloat16 k[2][GC * PK];
-  __nv_bfloat16 q[2][GC * PK];
-  __nv_bfloat16 u[2][GC * PV];
-  __nv_bfloat16 vn[GC * PV];
-  __nv_bfloat16 kd[GC * PK];
-  __nv_bfloat16 st[DK * PV];
-  float gam[2][GC];
+struct StateSmem {
+  __nv_bfloat16 w[SST][GC * PK];
+  __nv_bfloat16 k[SST][GC * PK];
+  __nv_bfloat16 ut[SST][SVS * PU];
+  float g[SST][GC];
 };
 
-__device__ __forceinline__ void scan_issue_loads(ScanSmem& s, const GdnScanArgs& a, int buf, int chunk, int h, int kh,
-                                                 int col0, int n_pad, int tid) {
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool pred) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  const int sz = pred ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(gmem), "r"(sz) : "memory");
+}
+
+__device__ __forceinline__ void state_issue_loads(StateSmem& s, const GdnScanArgs& a, int stage, int chunk, int h,
+                                                  int kh, int m0, int n_pad, int tid) {
   const int r0 = chunk * GC;
   const int rows = min(GC, a.n - r0);
   const __nv_bfloat16* wp = a.w_buf + ((long)h * n_pad + r0) * DK;
-  const __nv_bfloat16* up = a.u_buf + ((long)h * n_pad + r0) * a.dv + col0;
+  const __nv_bfloat16* up = a.u_buf + ((long)h * n_pad + r0) * a.dv + (long)m0 * GC;
   const __nv_bfloat16* kp = a.k + ((long)kh * a.n + r0) * DK;
-  const __nv_bfloat16* qp = a.q != nullptr ? a.q + ((long)kh * a.n + r0) * DK : nullptr;
   for (int v = tid; v < GC * (DK / 8); v += 128) {
     const int r = v / (DK / 8), c = (v % (DK / 8)) * 8;
-    cp_async16(&s.w[buf][r * PK + c], wp + (long)r * DK + c, true);   // padded rows hold zeros
+    cp_async16(&s.w[stage][r * PK + c], wp + (long)r * DK + c, true);   // padded rows hold zeros
     const bool ok = r < rows;
-    cp_async16(&s.k[buf][r * PK + c], ok ? kp + (long)r * DK + c : kp, ok);
-    if (qp != nullptr) cp_async16(&s.q[buf][r * PK + c], ok ? qp + (long)r * DK + c : qp, ok);
+    cp_async16(&s.k[stage][r * PK + c], ok ? kp + (long)r * DK + c : kp, ok);
   }
-  for (int v = tid; v < GC * (DVS / 8); v += 128) {
-    const int r = v / (DVS / 8), c = (v % (DVS / 8)) * 8;
-    cp_async16(&s.u[buf][r * PV + c], up + (long)r * a.dv + c, true);
+  for (int v = tid; v < SVS * (GC / 8); v += 128) {
+    const int r = v / (GC / 8), c = (v % (GC / 8)) * 8;
+    cp_async16(&s.ut[stage][r * PU + c], up + (long)r * GC + c, true);
   }
-  cp_async_commit();
+  if (tid < GC) {
+    const float* gp = a.g + (long)h * a.n + r0;
+    cp_async4(&s.g[stage][tid], tid < rows ? gp + tid : gp, tid < rows);
+  }
 }
 
-__global__ void __launch_bounds__(128, 1) gdn_scan_kernel(GdnScanArgs a, int n_pad) {
-  extern __shared__ __align__(16) uint8_t scan_raw[];
-  ScanSmem& s = *reinterpret_cast<ScanSmem*>(scan_raw);
+__global__ void __launch_bounds__(128, 1) gdn_state_kernel(GdnScanArgs a, int n_pad, __nv_bfloat16* s_buf,
+                                                           __nv_bfloat16* vt_buf) {
+  extern __shared__ __align__(16) uint8_t st_raw[];
+  StateSmem& s = *reinterpret_cast<StateSmem*>(st_raw);
   const int h = blockIdx.x;
-  const int col0 = blockIdx.y * DVS;
+  const int m0 = blockIdx.y * SVS;                 // first value dim of this CTA
   const int kh = h / (a.nv / a.nk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
+  const int mrow = warp * 16;                      // this warp's rows within the slice
   const int n_chunks = (a.n + GC - 1) / GC;
-  const bool out_mode = a.q != nullptr;
-  float* state = a.state + (long)h * DK * a.dv;
+  float* state = a.state + (long)h * DK * a.dv;    // S [dk][dv]
 
-  // state accumulators: warp rows [32w, 32w+32) (2 m-tiles) x 64 cols (8 n-tiles)
-  float S[2][8][4];
+  // S^T accumulators: rows m0 + mrow + (g, g+8), cols (dk) nt * 8 + 2t (+1)
+  float S[16][4];
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = warp * 32 + mt * 16 + g + (e >= 2 ? 8 : 0);
-        const int c = nt * 8 + 2 * t + (e & 1);
-        S[mt][nt][e] = state[(long)r * a.dv + col0 + c];
-      }
-
-  if (n_chunks > 0) scan_issue_loads(s, a, 0, 0, h, kh, col0, n_pad, tid);
+  for (int nt = 0; nt < 16; ++nt) {
+    const int m = m0 + mrow + g;
+    const int c = nt * 8 + 2 * t;
+    S[nt][0] = state[(long)c * a.dv + m];
+    S[nt][1] = state[(long)(c + 1) * a.dv + m];
+    S[nt][2] = state[(long)c * a.dv + m + 8];
+    S[nt][3] = state[(long)(c + 1) * a.dv + m + 8];
+  }
+  for (int p = 0; p < SST - 1; ++p) {
+    if (p < n_chunks) state_issue_loads(s, a, p, p, h, kh, m0, n_pad, tid);
+    cp_async_commit();
+  }
   for (int ch = 0; ch < n_chunks; ++ch) {
-    const int buf = ch & 1;
-    const int r0 = ch * GC;
-    const int rows = min(GC, a.n - r0);
-    // bf16 state copy + gamma of this chunk
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        const int r = warp * 32 + mt * 16 + g;
-        const int c = nt * 8 + 2 * t;
-        *reinterpret_cast<uint32_t*>(&s.st[r * PV + c]) = pack2(S[mt][nt][0], S[mt][nt][1]);
-        *reinterpret_cast<uint32_t*>(&s.st[(r + 8) * PV + c]) = pack2(S[mt][nt][2], S[mt][nt][3]);
-      }
-    if (warp == 0) {
-      const float x0 = (2 * lane < rows) ? a.g[(long)h * a.n + r0 + 2 * lane] : 0.f;
-      const float x1 = (2 * lane + 1 < rows) ? a.g[(long)h * a.n + r0 + 2 * lane + 1] : 0.f;
-      const float pair = x0 + x1;
-      float incl = pair;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      s.gam[buf][2 * lane] = incl - pair + x0;
-      s.gam[buf][2 * lane + 1] = incl;
-    }
-    if (ch + 1 < n_chunks) scan_issue_loads(s, a, buf ^ 1, ch + 1, h, kh, col0, n_pad, tid);
-    else cp_async_commit();
-    cp_async_wait<1>();
+    const int stage = ch % SST;
+    if (ch + SST - 1 < n_chunks) state_issue_loads(s, a, (ch + SST - 1) % SST, ch + SST - 1, h, kh, m0, n_pad, tid);
+    cp_async_commit();
+    cp_async_wait<SST - 1>();
     __syncthreads();
-    const float* gam = s.gam[buf];
-    const float gl = gam[GC - 1];
-
-    // V' = U - W S  (warp rows [16w, 16w + 16) x 64)
-    float vn[8][4];
+    // S^T as bf16 A fragments (k = dk in steps of 16: n-tiles 2ks, 2ks + 1)
+    uint32_t sa[8][4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) vn[j][0] = vn[j][1] = vn[j][2] = vn[j][3] = 0.f;
+    for (int ks = 0; ks < 8; ++ks) {
+      sa[ks][0] = pack2(S[2 * ks][0], S[2 * ks][1]);
+      sa[ks][1] = pack2(S[2 * ks][2], S[2 * ks][3]);
+      sa[ks][2] = pack2(S[2 * ks + 1][0], S[2 * ks + 1][1]);
+      sa[ks][3] = pack2(S[2 * ks + 1][2], S[2 * ks + 1][3]);
+    }
+    if (s_buf != nullptr) {   // chunk-start S^T, bf16 [dv][dk] per chunk
+      __nv_bfloat16* sb = s_buf + (((long)h * n_chunks + ch) * a.dv + m0 + mrow) * DK;
 #pragma unroll
-    for (int ks = 0; ks < DK / 16; ++ks) {
-      uint32_t af[4];
-      lda_row(af, s.w[buf], PK, warp * 16, ks * 16, lane);
+      for (int ks = 0; ks < 8; ++ks) {
+        const int c = ks * 16 + 2 * t;
+        *reinterpret_cast<uint32_t*>(sb + (long)g * DK + c) = sa[ks][0];
+        *reinterpret_cast<uint32_t*>(sb + (long)(g + 8) * DK + c) = sa[ks][1];
+        *reinterpret_cast<uint32_t*>(sb + (long)g * DK + c + 8) = sa[ks][2];
+        *reinterpret_cast<uint32_t*>(sb + (long)(g + 8) * DK + c + 8) = sa[ks][3];
+      }
+    }
+    // gates: every warp scans the chunk's log decays (lane l holds gam[2l], gam[2l + 1])
+    const float x0 = s.g[stage][2 * lane], x1 = s.g[stage][2 * lane + 1];
+    const float pair = x0 + x1;
+    float incl = pair;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const float gl = __shfl_sync(0xffffffffu, incl, 31);
+    const float f_even = __expf(gl - (incl - pair + x0)), f_odd = __expf(gl - incl);
+    // V'^T = U^T - S^T W^T: [16 x 64], n-tiles over chunk rows
+    float vt[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) vt[j][0] = vt[j][1] = vt[j][2] = vt[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
       for (int j2 = 0; j2 < 4; ++j2) {
         uint32_t bf[4];
-        ldb_kn(bf, s.st, PV, j2 * 16, ks * 16, lane);
-        mma_bf16(vn[2 * j2], af, bf[0], bf[1]);
-        mma_bf16(vn[2 * j2 + 1], af, bf[2], bf[3]);
+        ldb_nk(bf, s.w[stage], PK, j2 * 16, ks * 16, lane);   // B[k = dk][n = row] = W[row][dk]
+        mma_bf16(vt[2 * j2], sa[ks], bf[0], bf[1]);
+        mma_bf16(vt[2 * j2 + 1], sa[ks], bf[2], bf[3]);
+      }
+    }
+    const __nv_bfloat16* ut = s.ut[stage];
+    __nv_bfloat16* vtg = vt_buf != nullptr ? vt_buf + (((long)h * n_chunks + ch) * a.dv + m0 + mrow) * GC : nullptr;
+    uint32_t va[4][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = j * 8 + 2 * t;                      // chunk rows c, c + 1
+      const float2 u0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ut[(mrow + g) * PU + c]));
+      const float2 u1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ut[(mrow + g + 8) * PU + c]));
+      const float v0 = u0.x - vt[j][0], v1 = u0.y - vt[j][1], v2 = u1.x - vt[j][2], v3 = u1.y - vt[j][3];
+      if (vtg != nullptr) {
+        *reinterpret_cast<uint32_t*>(vtg + (long)g * GC + c) = pack2(v0, v1);
+        *reinterpret_cast<uint32_t*>(vtg + (long)(g + 8) * GC + c) = pack2(v2, v3);
+      }
+      // decay factors of chunk rows c, c + 1 (= lane (c >> 1)'s pair)
+      const float fc0 = __shfl_sync(0xffffffffu, f_even, c >> 1);
+      const float fc1 = __shfl_sync(0xffffffffu, f_odd, c >> 1);
+      const uint32_t lo = pack2(v0 * fc0, v1 * fc1), hi = pack2(v2 * fc0, v3 * fc1);
+      va[j >> 1][(j & 1) ? 2 : 0] = lo;
+      va[j >> 1][(j & 1) ? 3 : 1] = hi;
+    }
+    // S^T <- e^gl S^T + Vs^T k
+    const float cd = __expf(gl);
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      S[nt][0] *= cd;
+      S[nt][1] *= cd;
+      S[nt][2] *= cd;
+      S[nt][3] *= cd;
+    }
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+      for (int j2 = 0; j2 < 8; ++j2) {
+        uint32_t bf[4];
+        ldb_kn(bf, s.k[stage], PK, j2 * 16, ks * 16, lane);   // B[k = row][n = dk] = k[row][dk]
+        mma_bf16(S[2 * j2], va[ks], bf[0], bf[1]);
+        mma_bf16(S[2 * j2 + 1], va[ks], bf[2], bf[3]);
+      }
+    }
+    __syncthreads();   // this stage is refilled two iterations later
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    const int m = m0 + mrow + g;
+    const int c = nt * 8 + 2 * t;
+    state[(long)c * a.dv + m] = S[nt][0];
+    state[(long)(c + 1) * a.dv + m] = S[nt][1];
+    state[(long)c * a.dv + m + 8] = S[nt][2];
+    state[(long)(c + 1) * a.dv + m + 8] = S[nt][3];
+  }
+}
+
+// ---------------------------------------------------------------------------------- output pass
+// Parallel over (chunk, value head): O = (q e^gam) S_c + (q k^T * decay) V' for the chunk's rows, with
+// S_c^T [dv][dk] and V'^T [dv][64] from the state pass read as [N][K] B operands.
+struct OutSmem {
+  __nv_bfloat16 q[GC * PK];
+  __nv_bfloat16 k[GC * PK];
+  __nv_bfloat16 vt[128 * PU];     // V'^T [dv][64]
+  __nv_bfloat16 st[128 * PK];     // S_c^T [dv][dk]
+  float gam[GC];
+  float eg[GC];
+};
+
+__global__ void __launch_bounds__(128) gdn_output_kernel(GdnScanArgs a, int n_pad, const __nv_bfloat16* s_buf,
+                                                         const __nv_bfloat16* vt_buf) {
+  extern __shared__ __align__(16) uint8_t out_raw[];
+  OutSmem& s = *reinterpret_cast<OutSmem*>(out_raw);
+  const int chunk = blockIdx.x;
+  const int h = blockIdx.y;
+  const int kh = h / (a.nv / a.nk);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int r0 = chunk * GC;
+  const int rows = min(GC, a.n - r0);
+  const int dv = a.dv;
+  const int n_chunks = n_pad / GC;
+  const __nv_bfloat16* qp = a.q + ((long)kh * a.n + r0) * DK;
+  const __nv_bfloat16* kp = a.k + ((long)kh * a.n + r0) * DK;
+  const __nv_bfloat16* vp = vt_buf + ((long)h * n_chunks + chunk) * dv * GC;
+  const __nv_bfloat16* sp = s_buf + ((long)h * n_chunks + chunk) * dv * DK;
+  for (int v = tid; v < GC * (DK / 8); v += 128) {
+    const int r = v / (DK / 8), c = (v % (DK / 8)) * 8;
+    const bool ok = r < rows;
+    cp_async16(&s.q[r * PK + c], ok ? qp + (long)r * DK + c : qp, ok);
+    cp_async16(&s.k[r * PK + c], ok ? kp + (long)r * DK + c : kp, ok);
+  }
+  for (int v = tid; v < dv * (GC / 8); v += 128) {
+    const int r = v / (GC / 8), c = (v % (GC / 8)) * 8;
+    cp_async16(&s.vt[r * PU + c], vp + (long)r * GC + c, true);
+  }
+  for (int v = tid; v < dv * (DK / 8); v += 128) {
+    const int r = v / (DK / 8), c = (v % (DK / 8)) * 8;
+    cp_async16(&s.st[r * PK + c], sp + (long)r * DK + c, true);
+  }
+  cp_async_commit();
+  if (warp == 0) {
+    const float x0 = (2 * lane < rows) ? a.g[(long)h * a.n + r0 + 2 * lane] : 0.f;
+    const float x1 = (2 * lane + 1 < rows) ? a.g[(long)h * a.n + r0 + 2 * lane + 1] : 0.f;
+    const float pair = x0 + x1;
+    float incl = pair;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    s.gam[2 * lane] = incl - pair + x0;
+    s.gam[2 * lane + 1] = incl;
+    s.eg[2 * lane] = __expf(incl - pair + x0);
+    s.eg[2 * lane + 1] = __expf(incl);
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  const int ra = warp * 16 + g, rb = ra + 8;
+  float qk[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) qk[j][0] = qk[j][1] = qk[j][2] = qk[j][3] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < DK / 16; ++ks) {
+    uint32_t af[4];
+    lda_row(af, s.q, PK, warp * 16, ks * 16, lane);
+#pragma unroll
+    for (int j2 = 0; j2 < 4; ++j2) {
+      uint32_t bf[4];
+      ldb_nk(bf, s.k, PK, j2 * 16, ks * 16, lane);
+      mma_bf16(qk[2 * j2], af, bf[0], bf[1]);
+      mma_bf16(qk[2 * j2 + 1], af, bf[2], bf[3]);
+    }
+  }
+  const float ga = s.gam[ra], gb = s.gam[rb];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = (e >= 2) ? rb : ra;
+      const int c = j * 8 + 2 * t + (e & 1);
+      qk[j][e] = (r >= c) ? qk[j][e] * __expf(((e >= 2) ? gb : ga) - s.gam[c]) : 0.f;
+    }
+  uint32_t pf[4][4];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    pf[kk][0] = pack2(qk[2 * kk][0], qk[2 * kk][1]);
+    pf[kk][1] = pack2(qk[2 * kk][2], qk[2 * kk][3]);
+    pf[kk][2] = pack2(qk[2 * kk + 1][0], qk[2 * kk + 1][1]);
+    pf[kk][3] = pack2(qk[2 * kk + 1][2], qk[2 * kk + 1][3]);
+  }
+  uint32_t qa[8][4];
+  const float ea = s.eg[ra], eb = s.eg[rb];
+#pragma unroll
+  for (int ks = 0; ks < DK / 16; ++ks) {
+    lda_row(qa[ks], s.q, PK, warp * 16, ks * 16, lane);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float sc = (e & 1) ? eb : ea;
+      float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&qa[ks][e]));
+      qa[ks][e] = pack2(f.x * sc, f.y * sc);
+    }
+  }
+  for (int nb = 0; nb < dv; nb += 64) {
+    float o[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < DK / 16; ++ks) {
+#pragma unroll
+      for (int j2 = 0; j2 < 4; ++j2) {
+        uint32_t bf[4];
+        ldb_nk(bf, s.st, PK, nb + j2 * 16, ks * 16, lane);   // B[k = dk][n = dv] = S^T[dv][dk]
+        mma_bf16(o[2 * j2], qa[ks], bf[0], bf[1]);
+        mma_bf16(o[2 * j2 + 1], qa[ks], bf[2], bf[3]);
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int j2 = 0; j2 < 4; ++j2) {
+        uint32_t bf[4];
+        ldb_nk(bf, s.vt, PU, nb + j2 * 16, kk * 16, lane);   // B[k = row][n = dv] = V'^T[dv][row]
+        mma_bf16(o[2 * j2], pf[kk], bf[0], bf[1]);
+        mma_bf16(o[2 * j2 + 1], pf[kk], bf[2], bf[3]);
       }
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int r = warp * 16 + g;
-      const int c = j * 8 + 2 * t;
-      const __nv_bfloat16* ur = s.u[buf];
-      const float u0 = __bfloat162float(ur[r * PV + c]), u1 = __bfloat162float(ur[r * PV + c + 1]);
-      const float u2 = __bfloat162float(ur[(r + 8) * PV + c]), u3 = __bfloat162float(ur[(r + 8) * PV + c + 1]);
-      *reinterpret_cast<uint32_t*>(&s.vn[r * PV + c]) = pack2(u0 - vn[j][0], u1 - vn[j][1]);
-      *reinterpret_cast<uint32_t*>(&s.vn[(r + 8) * PV + c]) = pack2(u2 - vn[j][2], u3 - vn[j][3]);
+      const int c = nb + j * 8 + 2 * t;
+      if (ra < rows)
+        *reinterpret_cast<uint32_t*>(a.out + (long)(r0 + ra) * a.out_row + (long)h * dv + c) = pack2(o[j][0], o[j][1]);
+      if (rb < rows)
+        *reinterpret_cast<uint32_t*>(a.out + (long)(r0 + rb) * a.out_row + (long)h * dv + c) = pack2(o[j][2], o[j][3]);
     }
-    // Kd = k e^(gl - gam) (bf16)
-    for (int v = tid; v < GC * DK; v += 128) {
-      const int r = v / DK, c = v % DK;
-      s.kd[r * PK + c] = __float2bfloat16(__bfloat162float(s.k[buf][r * PK + c]) * expf(gl - gam[r]));
-    }
-    __syncthreads();
-
-    if (out_mode) {
-      // O = (q e^gam) S + (q k^T * decay) V'
-      float o[8][4];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-      const int ra = warp * 16 + g, rb = ra + 8;
-      const float ea = expf(gam[ra]), eb = expf(gam[rb]);
-#pragma unroll
-      for (int ks = 0; ks < DK / 16; ++ks) {
-        uint32_t af[4];
-        lda_row(af, s.q[buf], PK, warp * 16, ks * 16, lane);
-        // scale rows: a0, a2 -> row ra; a1, a3 -> row rb
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          __nv_bfloat162 p = *reinterpret_cast<__nv_bfloat162*>(&af[e]);
-          const float sc = (e & 1) ? eb : ea;
-          float2 f = __bfloat1622float2(p);
-          af[e] = pack2(f.x * sc, f.y * sc);
-        }
-#pragma unroll
-        for (int j2 = 0; j2 < 4; ++j2) {
-          uint32_t bf[4];
-          ldb_kn(bf, s.st, PV, j2 * 16, ks * 16, lane);
-          mma_bf16(o[2 * j2], af, bf[0], bf[1]);
-          mma_bf16(o[2 * j2 + 1], af, bf[2], bf[3]);
-        }
-      }
-      float qk[8][4];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) qk[j][0] = qk[j][1] = qk[j][2] = qk[j][3] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < DK / 16; ++ks) {
-        uint32_t af[4];
-        lda_row(af, s.q[buf], PK, warp * 16, ks * 16, lane);
-#pragma unroll
-        for (int j2 = 0; j2 < 4; ++j2) {
-          uint32_t bf[4];
-          ldb_nk(bf, s.k[buf], PK, j2 * 16, ks * 16, lane);
-          mma_bf16(qk[2 * j2], af, bf[0], bf[1]);
-          mma_bf16(qk[2 * j2 + 1], af, bf[2], bf[3]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int r = (e >= 2) ? rb : ra;
-          const int c = j * 8 + 2 * t + (e & 1);
-          qk[j][e] = (r >= c) ? qk[j][e] * expf(gam[r] - gam[c]) : 0.f;
-        }
-      }
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        uint32_t pf[4];
-        pf[0] = pack2(qk[2 * kk][0], qk[2 * kk][1]);
-        pf[1] = pack2(qk[2 * kk][2], qk[2 * kk][3]);
-        pf[2] = pack2(qk[2 * kk + 1][0], qk[2 * kk + 1][1]);
-        pf[3] = pack2(qk[2 * kk + 1][2], qk[2 * kk + 1][3]);
-#pragma unroll
-        for (int j2 = 0; j2 < 4; ++j2) {
-          uint32_t bf[4];
-          ldb_kn(bf, s.vn, PV, j2 * 16, kk * 16, lane);
-          mma_bf16(o[2 * j2], pf, bf[0], bf[1]);
-          mma_bf16(o[2 * j2 + 1], pf, bf[2], bf[3]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int c = col0 + j * 8 + 2 * t;
-        if (ra < rows)
-          *reinterpret_cast<uint32_t*>(a.out + (long)(r0 + ra) * a.out_row + (long)h * a.dv + c) =
-              pack2(o[j][0], o[j][1]);
-        if (rb < rows)
-          *reinterpret_cast<uint32_t*>(a.out + (long)(r0 + rb) * a.out_row + (long)h * a.dv + c) =
-              pack2(o[j][2], o[j][3]);
-      }
-    }
-
-    // S <- e^gl S + Kd^T V'
-    const float cd = expf(gl);
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) S[mt][nt][e] *= cd;
-#pragma unroll
-    for (int ks = 0; ks < GC / 16; ++ks) {
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        uint32_t af[4];
-        lda_trans(af, s.kd, PK, warp * 32 + mt * 16, ks * 16, lane);
-#pragma unroll
-        for (int j2 = 0; j2 < 4; ++j2) {
-          uint32_t bf[4];
-          ldb_kn(bf, s.vn, PV, j2 * 16, ks * 16, lane);
-          mma_bf16(S[mt][2 * j2], af, bf[0], bf[1]);
-          mma_bf16(S[mt][2 * j2 + 1], af, bf[2], bf[3]);
-        }
-      }
-    }
-    __syncthreads();
   }
-  cp_async_wait<0>();
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = warp * 32 + mt * 16 + g + (e >= 2 ? 8 : 0);
-        const int c = nt * 8 + 2 * t + (e & 1);
-        state[(long)r * a.dv + col0 + c] = S[mt][nt][e];
-      }
 }
 
 void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream) {
   if (a.n <= 0) return;
-  if (a.dk != DK || a.dv % DVS != 0 || a.dv > 128 || a.nv % a.nk != 0) {
+  if (a.dk != DK || a.dv % SVS != 0 || a.dv > 128 || a.nv % a.nk != 0 || (a.q != nullptr && (a.s_buf == nullptr || a.vt_buf == nullptr))) {
     if (a.err) cudaMemsetAsync(a.err, kErrBadShape, 1, stream);
     return;
   }
@@ -520,11 +695,18 @@ void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream) {
   static bool set = false;
   if (!set) {
     cudaFuncSetAttribute(gdn_wy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(WySmem));
-    cudaFuncSetAttribute(gdn_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(ScanSmem));
+    cudaFuncSetAttribute(gdn_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(StateSmem));
+    cudaFuncSetAttribute(gdn_output_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(OutSmem));
     set = true;
   }
-  gdn_wy_kernel<<<dim3(n_chunks, a.nv), 128, sizeof(WySmem), stream>>>(a, n_pad); count_launch();
-  gdn_scan_kernel<<<dim3(a.nv, a.dv / DVS), 128, sizeof(ScanSmem), stream>>>(a, n_pad); count_launch();
+  gdn_wy_kernel<<<dim3(n_chunks, a.nv), 128, sizeof(WySmem), stream>>>(a, n_pad);
+  gdn_state_kernel<<<dim3(a.nv, a.dv / SVS), 128, sizeof(StateSmem), stream>>>(a, n_pad, a.q ? a.s_buf : nullptr,
+                                                                               a.q ? a.vt_buf : nullptr);
+  count_launch(2);
+  if (a.q != nullptr) {
+    gdn_output_kernel<<<dim3(n_chunks, a.nv), 128, sizeof(OutSmem), stream>>>(a, n_pad, a.s_buf, a.vt_buf);
+    count_launch();
+  }
 }
 
 }  // namespace rf

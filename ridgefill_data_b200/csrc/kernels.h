@@ -92,7 +92,9 @@ struct GdnScanArgs {
   __nv_bfloat16* out;       // [n, nv, dv] (row pitch out_row) or nullptr
   long out_row;
   __nv_bfloat16* w_buf;     // scratch [nv, n_pad, dk]
-  __nv_bfloat16* u_buf;     // scratch [nv, n_pad, dv]
+  __nv_bfloat16* u_buf;     // scratch [nv, n_chunks, dv, 64]: U^T per chunk
+  __nv_bfloat16* s_buf;     // scratch [nv, n_chunks, dv, dk]: chunk-start S^T (output mode)
+  __nv_bfloat16* vt_buf;    // scratch [nv, n_chunks, dv, 64]: V'^T per chunk (output mode)
   int n, nk, nv, dk, dv;
   int* err;
 };

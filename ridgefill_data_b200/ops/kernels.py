@@ -90,6 +90,8 @@ def gdn_scan(q, k, v, beta, g, state, out=None):
     n_pad = (n + 63) // 64 * 64
     w_buf = torch.empty(nv, n_pad, dk, dtype=BF16, device=k.device)
     u_buf = torch.empty(nv, n_pad, dv, dtype=BF16, device=k.device)
+    s_buf = torch.empty(nv, n_pad // 64, dv, dk, dtype=BF16, device=k.device) if q is not None else None
+    vt_buf = torch.empty(nv, n_pad, dv, dtype=BF16, device=k.device) if q is not None else None
     err = ext().error_word(k.device.index or 0)
-    ext().gdn_chunk_scan(q, k, v, beta, g, state, out, w_buf, u_buf, n, nk, nv, dk, dv, err)
+    ext().gdn_chunk_scan(q, k, v, beta, g, state, out, w_buf, u_buf, s_buf, vt_buf, n, nk, nv, dk, dv, err)
     return out
