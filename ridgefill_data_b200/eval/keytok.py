@@ -1,0 +1,60 @@
+"""Token-level NLL readouts over a scored window: novel tokens and LongPPL-style key tokens
+(code/kva/keytok.py:26-78 semantics). Key tokens: the scored tokens whose exact-model log-prob drops by more
+than THRESHOLD nats when the prefix is removed (context [BOS] + the last T prompt tokens)."""
+from __future__ import annotations
+
+import torch
+
+from ..engine.scoring import score_tokens
+
+THRESHOLD = 2.0
+
+
+class KeyTokenReferenceMissing(ValueError):
+    pass
+
+
+def check_tail(n, scored, tail, bos):
+    usable = n - (1 if bos is not None else 0)
+    if not scored + 1 <= tail < usable:
+        raise ValueError(f"key-token tail {tail}: needs scored + 1 ({scored + 1}) <= tail < {usable}")
+
+
+@torch.no_grad()
+def exact_tail_only(model, ids, tail, bos, scored):
+    """Exact log-probs of the last `scored` tokens given only [BOS] + the last `tail` prompt tokens."""
+    check_tail(ids.shape[0], scored, tail, bos)
+    ctx = ids[-tail:]
+    if bos is not None:
+        ctx = torch.cat((ids[:1], ctx))
+    logits, _ = model.forward_exact(ctx.to(model.device),
+                                    keep=torch.arange(ctx.shape[0] - scored - 1, ctx.shape[0], device=model.device))
+    return score_tokens(logits, ctx, scored)
+
+
+def key_mask(lp_full, lp_tail, threshold=THRESHOLD):
+    return (lp_full.double() - lp_tail.double()) > threshold
+
+
+def nll_delta(lp_arm, lp_exact, mask=None):
+    d = (-lp_arm.double()) - (-lp_exact.double())
+    if mask is not None:
+        if int(mask.sum()) == 0:
+            return None, 0
+        d = d[mask]
+    return float(d.mean()), int(d.numel())
+
+
+def readout(rec, threshold=THRESHOLD):
+    """Per arm: NLL delta vs exact over all scored tokens, the novel tokens and the key tokens."""
+    if "tail_only" not in rec:
+        raise KeyTokenReferenceMissing("record lacks the exact tail-only log-probs")
+    exact = torch.as_tensor(rec["lp"]["exact"])
+    keys = key_mask(exact, torch.as_tensor(rec["tail_only"]), threshold)
+    novel = torch.as_tensor(rec["novel"], dtype=torch.bool) if "novel" in rec else None
+    out = {}
+    for arm, lp in rec["lp"].items():
+        lp = torch.as_tensor(lp)
+        out[arm] = dict(all=nll_delta(lp, exact), novel=nll_delta(lp, exact, novel) if novel is not None else None,
+                        key=nll_delta(lp, exact, keys))
+    return out

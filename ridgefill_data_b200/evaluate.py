@@ -1,0 +1,147 @@
+"""Evaluation CLI: arms x prompts x task, one atomic JSON record per prompt (resumable).
+
+  python -m ridgefill_data_b200.evaluate CONFIG.json TASK
+
+CONFIG: {"model": preset or checkpoint dir, "seed": 0, "backend": "b200"|"torch", "arms": [arm specs]
+(engine/spec.py), "prompts": {"kind": "uniform"|"zipf"|"niah", "lengths": [...], "count": k, "seed": s},
+"out": results dir, "keep": scored rows}.
+TASK:
+  quality  per arm: filled late-layer K/V (and GDN state) relative error vs exact prefill, next-token KL and
+           top-1 agreement of the last `keep` rows
+  ppl      per arm: mean NLL of the last `keep` prompt tokens
+  niah     greedy decode after each arm's prefill; correct iff the needle's value ids are reproduced
+  decode   decode agreement vs exact (teacher-forced KL, top-1, first divergence)
+  speed    per arm: device-timed TTFT (CUDA events) and tokens/s
+Validation happens before any model is built (engine/spec.py); results carry a provenance block.
+"""
+import argparse
+import json
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+
+def prompts_of(cfg, vocab):
+    from .eval.data import uniform_prompt, zipf_ids
+    from .eval.niah import DEPTHS, niah_prompt
+    p = cfg.get("prompts", {})
+    kind, seed = p.get("kind", "uniform"), p.get("seed", 2)
+    out = []
+    for n in p.get("lengths", [2048]):
+        for j in range(p.get("count", 1)):
+            if kind == "uniform":
+                out.append(dict(name=f"uniform-{n}-{j}", ids=uniform_prompt(n, vocab, seed=seed + j)))
+            elif kind == "zipf":
+                out.append(dict(name=f"zipf-{n}-{j}", ids=zipf_ids(n, vocab, seed=seed + j)))
+            elif kind == "niah":
+                d = DEPTHS[j % len(DEPTHS)]
+                rec = niah_prompt(n, vocab, d, seed=seed + j)
+                out.append(dict(name=f"niah-{n}-{d}-{j}", **rec))
+            else:
+                raise ValueError(f"prompt kind {kind!r}")
+    return out
+
+
+def _rel(a, b):
+    return float((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30))
+
+
+@torch.no_grad()
+def run_prompt(model, arms, prm, task, keep):
+    from .engine.decode import greedy
+    from .engine.prefill import finish, run_lower
+    from .engine.scoring import decode_agreement, kl, score_tokens, top1_agree
+    ids = prm["ids"].to(model.device)
+    n = ids.shape[0]
+    rec = dict(name=prm["name"], n=n, runs={})
+    exact_logits, exact_cache = model.forward_exact(ids, keep=torch.arange(n - keep, n, device=model.device))
+    splits = sorted({a.split for a in arms if a.split is not None})
+    lower = {S: run_lower(model, ids, [S]) for S in splits}
+    for arm in arms:
+        t0 = time.time()
+        if arm.fill == "exact":
+            logits, cache = exact_logits, exact_cache
+        else:
+            hs, lc = lower[arm.split]
+            logits, cache, _ = finish(model, ids, hs[arm.split], lc, arm, keep)
+        r = dict(wall_s=round(time.time() - t0, 4))
+        if task == "quality":
+            errs = {}
+            for i in range(arm.split or model.n_layers, model.n_layers):
+                c, e = cache[i], exact_cache[i]
+                if model.layer_types[i] == "attn":
+                    errs[i] = dict(k=_rel(c["k"], e["k"]), v=_rel(c["v"], e["v"]))
+                else:
+                    errs[i] = dict(state=_rel(c["rec"], e["rec"]))
+            r.update(kv_rel_err=errs, kl=float(kl(exact_logits, logits).mean()),
+                     top1=float(top1_agree(exact_logits, logits).mean()))
+        elif task == "ppl":
+            r["nll"] = float(-score_tokens(logits, ids, keep - 1).double().mean())
+        elif task == "niah":
+            from .eval.niah import niah_correct
+            gen, reason = greedy(model, ids, cache, logits, len(prm["value"]) + 4, arm)
+            r.update(gen=gen, finish_reason=reason, correct=niah_correct(gen, prm["value"]))
+        elif task == "decode":
+            r.update(decode_agreement(model, ids, exact_cache, exact_logits, cache, logits, steps=8))
+        rec["runs"][arm.name] = r
+    return rec
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("config")
+    ap.add_argument("task", choices=("quality", "ppl", "niah", "decode", "speed"))
+    a = ap.parse_args(argv)
+    from .engine import spec
+    from .models.base import from_config, load
+    from .models.config import PRESETS, ModelConfig
+    from .utils import prov
+    cfg = spec.load(a.config)
+    mcfg = PRESETS[cfg["model"]] if cfg["model"] in PRESETS else ModelConfig.from_dir(cfg["model"])
+    spec.validate(cfg, mcfg.n_layers)
+    dev = cfg.get("device", "cuda" if torch.cuda.is_available() else "cpu")
+    backend = cfg.get("backend", "b200" if dev.startswith("cuda") else "torch")
+    dtype = torch.float32 if cfg.get("dtype") == "fp32" else torch.bfloat16
+    if cfg["model"] in PRESETS:
+        model = from_config(mcfg, seed=cfg.get("seed", 0), device=dev, backend=backend, dtype=dtype)
+    else:
+        model = load(cfg["model"], device=dev, backend=backend, dtype=dtype)
+    cache = {}
+    arms = [spec.arm_of(s, dev, cache) for s in cfg["arms"]]
+    out = Path(cfg.get("out", "results")) / a.task
+    keep = cfg.get("keep", 16)
+    for prm in prompts_of(cfg, mcfg.vocab):
+        path = out / f"{prm['name']}.json"
+        if path.exists():
+            continue
+        if a.task == "speed":
+            rec = dict(name=prm["name"], runs={})
+            from .engine.prefill import prefill
+            ids = prm["ids"].to(dev)
+            for arm in arms:
+                prefill(model, ids, arm)
+                if dev.startswith("cuda"):
+                    torch.cuda.synchronize()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    prefill(model, ids, arm)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    ms = e0.elapsed_time(e1)
+                else:
+                    t0 = time.time()
+                    prefill(model, ids, arm)
+                    ms = (time.time() - t0) * 1e3
+                rec["runs"][arm.name] = dict(ttft_ms=ms, tok_s=ids.shape[0] / ms * 1e3)
+        else:
+            rec = run_prompt(model, arms, prm, a.task, keep)
+        rec["provenance"] = prov.provenance(cfg["model"], dict(task=a.task))
+        prov.write_json(path, rec)
+        print(json.dumps({k: v for k, v in rec.items() if k != "provenance"})[:400])
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
