@@ -11,8 +11,9 @@ named shapes, a seeded uniform-random prompt.
   python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N      (one rank per GPU)
   python bench.py --impl reference                                             (the reference arm)
 
-Multi-GPU: each rank prefills its own prompt (data parallel, weak scaling); the reported value is the
-whole-job tokens/s (sum over ranks of tokens / max-over-ranks device time).
+Multi-GPU (--parallel): tp (default) shards every layer over the N ranks (tensor parallel: one prompt per
+step, strong scaling; the reported value is prompt tokens / max-over-ranks step time); dp gives each rank its
+own prompt (weak scaling; value = sum of tokens / max-over-ranks step time).
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and torch.cuda.synchronize(),
 CUDA events on the launching stream, max over ranks. The weights (54 GB) exceed L2 (126 MB), so every
 step streams its inputs from HBM. SM clocks and throttle reasons are sampled with nvidia-smi during the
@@ -123,6 +124,8 @@ def main():
     ap.add_argument("--tail", type=int, default=4096)
     ap.add_argument("--split", type=int, default=32)
     ap.add_argument("--exact", action="store_true", help="also time full (exact) prefill for the speedup")
+    ap.add_argument("--parallel", default="tp", choices=("tp", "dp"))
+    ap.add_argument("--tp-comm", default="nccl", choices=("nccl", "fused"))
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -145,7 +148,11 @@ def main():
     from ridgefill_data_b200.ops._ext import check_errors, ext
 
     cfg, model, arm = build_engine(args, device)
-    ids_host = uniform_prompt(args.seq, cfg.vocab, seed=2 + rank).pin_memory()
+    tp_mode = world > 1 and args.parallel == "tp"
+    if tp_mode:
+        from ridgefill_data_b200.parallel.tp import TensorParallel, shard
+        shard(model, TensorParallel(mode=args.tp_comm))
+    ids_host = uniform_prompt(args.seq, cfg.vocab, seed=2 + (0 if tp_mode else rank)).pin_memory()
     ids_dev = ids_host.to(device)
     tok_host = torch.empty(1, dtype=torch.long).pin_memory()
 
@@ -217,17 +224,19 @@ def main():
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     ms_max, e2e_max, exact_max = stats.tolist()
-    tokens = args.seq * world
+    tokens = args.seq * (1 if tp_mode else world)
     value = tokens / (ms_max / 1e3)
     e2e_value = tokens / (e2e_max / 1e3)
     base = BASELINE_TOK_S.get(args.seq)
     if rank == 0:
         line = dict(metric=METRIC, value=round(value, 1), unit="tokens/s", n_gpus=world, steps=args.steps,
                     warmup=args.warmup, ms_per_step=round(ms_max, 3), higher_is_better=True,
-                    scaling="weak", vs_baseline=round(value / base, 3) if base else None, dtype="bf16",
+                    scaling="strong" if tp_mode else "weak", vs_baseline=round(value / base, 3) if base else None, dtype="bf16",
                     data="synthetic (seeded uniform prompt; random-init weights and ridge maps of the named shapes)",
-                    config=dict(model=args.model, global_batch=world, seq_len=args.seq, split=args.split,
-                                tail=args.tail, parallelism=f"dp{world}",
+                    config=dict(model=args.model, global_batch=1 if tp_mode else world, seq_len=args.seq,
+                                split=args.split, tail=args.tail,
+                                parallelism=(f"tp{world}" + ("" if args.tp_comm == "nccl" else "-fused")) if tp_mode
+                                else f"dp{world}",
                                 l2="inputs larger than L2 (54 GB of weights streamed per step)"),
                     clocks=clocks, gpu_launches=int(launches),
                     e2e=dict(value=round(e2e_value, 1), unit="tokens/s", ms_per_step=round(e2e_max, 3),

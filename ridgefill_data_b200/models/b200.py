@@ -29,6 +29,7 @@ class _B200:
 
     zero_centred = False
     capacity_hint = 0
+    tp = None          # parallel.tp.TensorParallel when the weights are sharded over ranks
 
     # ---- setup
     def _kernel_setup(self):
@@ -85,6 +86,8 @@ class _B200:
             return super().mlp(i, h)
         x = K.rmsnorm(h, w["ln2"], self.eps, self.zero_centred)
         act = G.swiglu_linear(x, w["gu_p"])
+        if self.tp is not None:
+            return self.tp.row_parallel(act, w["down"], h)
         return G.linear(act, w["down"], residual=h)
 
     def _pack_mlp(self, w):
@@ -165,7 +168,11 @@ class _B200:
         if gdn_checkpoint_every and self.layer_types[i] == "gdn":
             return super().layer(i, h, pos, cache, gdn_checkpoint_every=gdn_checkpoint_every, mix=mix)
         y, wo = self._mixer_out(i, h, pos, cache)
-        if mix is not None:
+        if self.tp is not None:
+            h2 = self.tp.row_parallel(y, wo, h)
+            if mix is not None:
+                mix(i, h2 - h)
+        elif mix is not None:
             a = G.linear(y, wo)
             mix(i, a)
             h2 = h + a
@@ -255,11 +262,11 @@ class B200Hybrid(_B200, Hybrid):
         """Conv + gates + chunked delta rule over the rows of proj, continuing cache[i]'s states."""
         w = self.W[i]
         cfg = self.cfg
-        C, nv = self.conv_dim, cfg.gdn_nv
+        C, nv = self.conv_dim, self.nv
         c = cache[i]
         conv_state = c.get("conv")
         q, k, v, beta, g = K.gdn_prep(proj, C, C + nv, w["conv"], conv_state, w["A_log"], w["dt_bias"],
-                                      cfg.gdn_nk, nv, cfg.gdn_dk, cfg.gdn_dv)
+                                      self.nk, nv, cfg.gdn_dk, cfg.gdn_dv)
         new_conv = (conv_state.clone() if conv_state is not None
                     else torch.zeros(cfg.conv_k - 1, C, dtype=self.dtype, device=self.device))
         K.gdn_conv_state_update(proj, new_conv, C)
@@ -279,12 +286,12 @@ class B200Hybrid(_B200, Hybrid):
         x = self._norm(h, w["ln1"])
         proj = G.linear(x, w["in_p"])
         o = self._gdn_core_dev(i, proj, cache, True)
-        z = proj[:, self.conv_dim + 2 * self.cfg.gdn_nv:]
-        return K.gated_rmsnorm(o, z, w["norm"], self.cfg.gdn_nv, self.cfg.gdn_dv, self.eps)
+        z = proj[:, self.conv_dim + 2 * self.nv:]
+        return K.gated_rmsnorm(o, z, w["norm"], self.nv, self.cfg.gdn_dv, self.eps)
 
     def _gdn_fill(self, i, xn, cache):
         w = self.W[i]
-        proj = G.linear(xn, w["in_p"][:self.conv_dim + 2 * self.cfg.gdn_nv])
+        proj = G.linear(xn, w["in_p"][:self.conv_dim + 2 * self.nv])
         self._gdn_core_dev(i, proj, cache, False)
 
     def mlp(self, i, h):

@@ -1,0 +1,128 @@
+"""Tensor parallelism for the B200 models (one rank per GPU).
+
+Sharding (column-parallel in, row-parallel out; activations replicated across ranks):
+  attention   query heads split evenly; each rank keeps the K/V heads its query heads read (KV heads are
+              replicated when there are fewer KV heads than ranks, e.g. 4 KV heads at TP 8); o_proj keeps the
+              columns of the local heads
+  GDN         key heads and value heads split evenly (value head h reads key head h // (nv / nk), so a rank's
+              value heads read only its own key heads); in_proj rows, conv channels, A_log / dt_bias and out_proj
+              columns follow
+  MLP         the packed gate/up rows in whole 128-row blocks, down_proj the matching columns
+  norms, embedding, lm_head and the ridge maps stay replicated
+Per layer the two row-parallel products (o_proj or out_proj, and down_proj) are summed over ranks:
+  nccl        GEMM (residual added on rank 0 only) then an NCCL all-reduce: the baseline
+  fused       GEMM whose epilogue stores each partial tile straight into the owner's receive slot over NVLink
+              peer memory, then the owner reduces its row block and writes it to every rank
+              (parallel/fused.py; falls back to nccl when the fused kernels are unavailable)
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..ops import gemm as G
+
+
+class TensorParallel:
+    def __init__(self, group=None, mode="nccl"):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.mode = mode
+        self.fused = None
+        if mode == "fused":
+            from .fused import FusedRowParallel
+            self.fused = FusedRowParallel(group)
+
+    def row_parallel(self, y, w, h):
+        """h + sum over ranks of y_r w_r^T (each rank holds its K-slice y_r, w_r)."""
+        if self.world == 1:
+            return G.linear(y, w, residual=h)
+        if self.fused is not None:
+            return self.fused(y, w, h)
+        a = G.linear(y, w, residual=h if self.rank == 0 else None)
+        dist.all_reduce(a, group=self.group)
+        return a
+
+
+def _span(total, world, rank, what):
+    if total % world:
+        raise ValueError(f"{what}: {total} is not divisible by {world} ranks")
+    per = total // world
+    return rank * per, (rank + 1) * per
+
+
+def shard_attention(w, cfg, rank, world):
+    """Slice one packed attention layer in place; returns (local q heads, local kv heads)."""
+    hd, hq, hkv = cfg.head_dim, cfg.n_heads, cfg.n_kv
+    qh = hd * (2 if cfg.gated_attn else 1)
+    h0, h1 = _span(hq, world, rank, "query heads")
+    rep = hq // hkv
+    k0, k1 = h0 // rep, (h1 - 1) // rep + 1
+    qkv = w["qkv_p"]
+    qw = hq * qh
+    q = qkv[h0 * qh:h1 * qh]
+    k = qkv[qw + k0 * hd:qw + k1 * hd]
+    v = qkv[qw + hkv * hd + k0 * hd:qw + hkv * hd + k1 * hd]
+    p = torch.cat((q, k, v)).contiguous()
+    nq = (h1 - h0) * qh
+    nkv = (k1 - k0) * hd
+    w.update(qkv_p=p, q=p[:nq], k=p[nq:nq + nkv], v=p[nq + nkv:], o=w["o"][:, h0 * hd:h1 * hd].contiguous())
+    return h1 - h0, k1 - k0
+
+
+def shard_gdn(w, cfg, rank, world):
+    """Slice one packed Gated DeltaNet layer in place; returns (local key heads, local value heads)."""
+    nk, nv, dk, dv = cfg.gdn_nk, cfg.gdn_nv, cfg.gdn_dk, cfg.gdn_dv
+    a0, a1 = _span(nk, world, rank, "GDN key heads")
+    v0, v1 = _span(nv, world, rank, "GDN value heads")
+    p = w["in_p"]
+    kd, vd = nk * dk, nv * dv
+    C = 2 * kd + vd
+    rows = [p[a0 * dk:a1 * dk], p[kd + a0 * dk:kd + a1 * dk], p[2 * kd + v0 * dv:2 * kd + v1 * dv],
+            p[C + v0:C + v1], p[C + nv + v0:C + nv + v1], p[C + 2 * nv + v0 * dv:C + 2 * nv + v1 * dv]]
+    conv = w["conv"]
+    conv_l = torch.cat((conv[a0 * dk:a1 * dk], conv[kd + a0 * dk:kd + a1 * dk],
+                        conv[2 * kd + v0 * dv:2 * kd + v1 * dv])).contiguous()
+    np_ = torch.cat(rows).contiguous()
+    nkl, nvl = a1 - a0, v1 - v0
+    Cl = 2 * nkl * dk + nvl * dv
+    w.update(in_p=np_, qkv=np_[:Cl], b=np_[Cl:Cl + nvl], a=np_[Cl + nvl:Cl + 2 * nvl], z=np_[Cl + 2 * nvl:],
+             conv=conv_l, A_log=w["A_log"][v0:v1].contiguous(), dt_bias=w["dt_bias"][v0:v1].contiguous(),
+             out=w["out"][:, v0 * dv:v1 * dv].contiguous())
+    return nkl, nvl
+
+
+def shard_mlp(w, rank, world, block=128):
+    gu = w["gu_p"]
+    nblk = gu.shape[0] // (2 * block)
+    b0, b1 = _span(nblk, world, rank, "FFN 128-row blocks")
+    w.update(gu_p=gu[b0 * 2 * block:b1 * 2 * block].contiguous(),
+             down=w["down"][:, b0 * block:b1 * block].contiguous())
+
+
+def shard(model, tp: TensorParallel):
+    """Shard a B200 model's weights for tp.rank of tp.world (in place) and attach the reduction."""
+    cfg = model.cfg
+    rank, world = tp.rank, tp.world
+    if world == 1:
+        model.tp = tp
+        return model
+    if cfg.moe:
+        raise ValueError("mixture-of-experts layers are expert-parallel (parallel/ep.py), not tensor-parallel")
+    local = {}
+    for i, w in enumerate(model.W):
+        if model.layer_types[i] == "attn":
+            local["attn"] = shard_attention(w, cfg, rank, world)
+        else:
+            local["gdn"] = shard_gdn(w, cfg, rank, world)
+        shard_mlp(w, rank, world)
+    if "attn" in local:
+        model.n_heads, model.n_kv = local["attn"]
+    if "gdn" in local:
+        model.nk, model.nv = local["gdn"]
+        model.conv_dim = 2 * model.nk * cfg.gdn_dk + model.nv * cfg.gdn_dv
+        model.vd = model.nv * cfg.gdn_dv
+    model.tp = tp
+    torch.cuda.empty_cache()
+    return model

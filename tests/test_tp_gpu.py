@@ -1,0 +1,78 @@
+"""Tensor parallelism on 2 GPUs (spawned NCCL ranks): the sharded B200 model reproduces the unsharded one's
+logits for exact forward and RidgeFill prefill. Skipped with fewer than 2 visible GPUs."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, mode, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from ridgefill_data_b200.engine.arm import Arm
+        from ridgefill_data_b200.engine.prefill import finish, run_lower
+        from ridgefill_data_b200.models.base import from_config
+        from ridgefill_data_b200.parallel.tp import TensorParallel, shard
+        from ridgefill_data_b200.ridge.projector import Projector
+        from test_b200_model_gpu import HYB, QWEN3
+        out = {}
+        for cfg in (HYB, QWEN3):
+            dev = torch.device("cuda", rank)
+            m = from_config(cfg, seed=0, device=dev, std=0.05, backend="b200")
+            ids = torch.randint(0, cfg.vocab, (300,), generator=torch.Generator().manual_seed(1)).to(dev)
+            keep = torch.arange(290, 300, device=dev)
+            split = cfg.n_layers // 2
+            W = {i: torch.eye(cfg.hidden, device=dev, dtype=torch.bfloat16) for i in range(split, cfg.n_layers)}
+            B = {i: torch.zeros(cfg.hidden, device=dev, dtype=torch.bfloat16) for i in range(split, cfg.n_layers)}
+            arm = Arm("rf", split=split, tail=64, fill="proj", projector=Projector(split, W, B))
+            with torch.no_grad():
+                ref, _ = m.forward_exact(ids, keep=keep)
+                hs, lower = run_lower(m, ids, [split])
+                ref_rf, _, _ = finish(m, ids, hs[split], lower, arm, 4)
+                shard(m, TensorParallel(mode=mode))
+                got, _ = m.forward_exact(ids, keep=keep)
+                hs, lower = run_lower(m, ids, [split])
+                got_rf, _, _ = finish(m, ids, hs[split], lower, arm, 4)
+            rel = lambda a, b: float((a - b).norm() / b.norm())  # noqa: E731
+            out[cfg.name] = (rel(got, ref), rel(got_rf, ref_rf))
+        q.put((rank, out))
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["nccl"])
+def test_tp2_matches_single_gpu(mode):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, out in res.items():
+        assert isinstance(out, dict), out
+        for name, (e_exact, e_rf) in out.items():
+            assert e_exact < 3e-2 and e_rf < 3e-2, (r, name, e_exact, e_rf)
