@@ -149,9 +149,11 @@ def main():
 
     cfg, model, arm = build_engine(args, device)
     tp_mode = world > 1 and args.parallel == "tp"
+    tp = None
     if tp_mode:
         from ridgefill_data_b200.parallel.tp import TensorParallel, shard
-        shard(model, TensorParallel(mode=args.tp_comm))
+        tp = TensorParallel(mode=args.tp_comm)
+        shard(model, tp)
     ids_host = uniform_prompt(args.seq, cfg.vocab, seed=2 + (0 if tp_mode else rank)).pin_memory()
     ids_dev = ids_host.to(device)
     tok_host = torch.empty(1, dtype=torch.long).pin_memory()
@@ -246,6 +248,10 @@ def main():
         if exact_ms:
             line.update(exact_prefill_ms=round(exact_max, 3), speedup_vs_exact=round(exact_max / ms_max, 3))
         print(json.dumps(line), flush=True)
+    if tp is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        tp.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -239,4 +239,139 @@ void register_ops(pybind11::module_& m) {
   m.def("gdn_prep", &gdn_prep);
   m.def("gdn_conv_state_update", &gdn_conv_state_update);
   m.def("gdn_chunk_scan", &gdn_chunk_scan);
+  void register_comm(pybind11::module_ & m);
+  register_comm(m);
+}
+
+// ---------------------------------------------------------------------------------- comm bindings
+#include "gemm.h"
+
+namespace {
+
+int64_t ipc_malloc_b(int64_t bytes) { return reinterpret_cast<int64_t>(rf::ipc_malloc((size_t)bytes)); }
+void ipc_free_b(int64_t p) { rf::ipc_free(reinterpret_cast<void*>(p)); }
+pybind11::bytes ipc_handle_b(int64_t p) { return pybind11::bytes(rf::ipc_handle(reinterpret_cast<void*>(p))); }
+int64_t ipc_open_b(pybind11::bytes h) { return reinterpret_cast<int64_t>(rf::ipc_open(std::string(h))); }
+void ipc_close_b(int64_t p) { rf::ipc_close(reinterpret_cast<void*>(p)); }
+
+// A non-owning tensor view of device memory at `ptr`.
+Tensor tensor_at(int64_t ptr, std::vector<int64_t> shape, int64_t dtype_code, int64_t device) {
+  const at::ScalarType st = dtype_code == 0 ? at::kBFloat16 : dtype_code == 1 ? at::kFloat : dtype_code == 2 ? at::kInt
+                                                                                                            : at::kDouble;
+  return torch::from_blob(reinterpret_cast<void*>(ptr), shape,
+                          torch::TensorOptions().dtype(st).device(torch::kCUDA, (int)device));
+}
+
+rf::PeerFlags flags_of(const std::vector<int64_t>& ptrs) {
+  rf::PeerFlags f{};
+  TORCH_CHECK(ptrs.size() <= rf::kMaxRanks, "at most 8 ranks");
+  f.n = (int)ptrs.size();
+  for (size_t i = 0; i < ptrs.size(); ++i) f.ptr[i] = reinterpret_cast<int*>(ptrs[i]);
+  return f;
+}
+
+void comm_signal_b(std::vector<int64_t> flag_ptrs, int64_t slot, int64_t value) {
+  rf::comm_signal(flags_of(flag_ptrs), (int)slot, (int)value, cur());
+}
+
+void comm_wait_b(int64_t flags, int64_t first, int64_t n, int64_t value, Tensor err) {
+  rf::comm_wait(reinterpret_cast<const int*>(flags), (int)first, (int)n, (int)value, err.data_ptr<int>(), cur());
+}
+
+void comm_reduce_rows_b(int64_t recv, int64_t slot_stride, c10::optional<Tensor> residual, int64_t red, int64_t rows,
+                        int64_t d, int64_t n_peers, int64_t my_rank, int64_t flags, int64_t arrive_slot,
+                        int64_t reduced_slot, int64_t value, int64_t counter, std::vector<int64_t> peer_flags,
+                        Tensor err) {
+  rf::ReduceRowsArgs a{};
+  a.recv = reinterpret_cast<const __nv_bfloat16*>(recv);
+  a.slot_stride = slot_stride;
+  if (residual.has_value()) {
+    need(*residual, at::kBFloat16, "residual");
+    a.residual = cbf(*residual);
+    a.ld_res = residual->stride(0);
+  }
+  a.red = reinterpret_cast<__nv_bfloat16*>(red);
+  a.rows = (int)rows;
+  a.d = (int)d;
+  a.n_peers = (int)n_peers;
+  a.my_rank = (int)my_rank;
+  a.flags = reinterpret_cast<const int*>(flags);
+  a.arrive_slot = (int)arrive_slot;
+  a.reduced_slot = (int)reduced_slot;
+  a.value = (int)value;
+  a.counter = reinterpret_cast<int*>(counter);
+  a.peer_flags = flags_of(peer_flags);
+  a.err = err.data_ptr<int>();
+  TORCH_CHECK(d % 8 == 0, "comm_reduce_rows: d % 8");
+  rf::comm_reduce_rows(a, cur());
+}
+
+void comm_gather_rows_b(std::vector<int64_t> peer_red, int64_t row_chunk, int64_t total_rows, int64_t d, Tensor out,
+                        int64_t flags, int64_t reduced_slot, int64_t value, Tensor err) {
+  need(out, at::kBFloat16, "out");
+  rf::GatherRowsArgs a{};
+  TORCH_CHECK(peer_red.size() <= rf::kMaxRanks, "at most 8 ranks");
+  for (size_t i = 0; i < peer_red.size(); ++i) a.peer_red[i] = reinterpret_cast<const __nv_bfloat16*>(peer_red[i]);
+  a.n_peers = (int)peer_red.size();
+  a.row_chunk = (int)row_chunk;
+  a.total_rows = (int)total_rows;
+  a.d = (int)d;
+  a.out = bf(out);
+  a.ld_out = out.stride(0);
+  a.flags = reinterpret_cast<const int*>(flags);
+  a.reduced_slot = (int)reduced_slot;
+  a.value = (int)value;
+  a.err = err.data_ptr<int>();
+  rf::comm_gather_rows(a, cur());
+}
+
+// tcgen05 GEMM whose epilogue stores bf16 tiles into peer buffers (gemm.h: PeerArgs).
+void gemm_peer_b(Tensor a, Tensor b, c10::optional<Tensor> bias, std::vector<int64_t> peers, int64_t mode,
+                 int64_t slot, int64_t row_chunk, int64_t slot_stride, int64_t ld, int64_t col_off, int64_t bn,
+                 Tensor err) {
+  need(a, at::kBFloat16, "a");
+  need(b, at::kBFloat16, "b");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1, "gemm_peer: unit inner stride");
+  TORCH_CHECK(peers.size() >= 1 && peers.size() <= rf::kMaxPeers, "gemm_peer: 1..8 peers");
+  c10::cuda::CUDAGuard g(a.device());
+  rf::GemmOperands op{a.data_ptr(), a.stride(0), false, b.data_ptr(), b.stride(0), false};
+  rf::GemmArgs args{};
+  args.M = (int)a.size(0);
+  args.K = (int)a.size(1);
+  args.N = (int)b.size(0);
+  TORCH_CHECK(b.size(1) == args.K, "gemm_peer: K mismatch");
+  args.k_splits = 1;
+  if (bias.has_value()) {
+    need(*bias, at::kBFloat16, "bias");
+    TORCH_CHECK(bias->is_contiguous() && bias->numel() == args.N, "gemm_peer: bias [N]");
+    args.bias = cbf(*bias);
+  }
+  args.vec_ok = (ld % 8 == 0 && col_off % 8 == 0 && slot_stride % 8 == 0) ? 1 : 0;
+  args.err = err.data_ptr<int>();
+  args.peer.n_peers = (int)peers.size();
+  for (size_t i = 0; i < peers.size(); ++i) args.peer.peer[i] = reinterpret_cast<void*>(peers[i]);
+  args.peer.mode = (int)mode;
+  args.peer.slot = (int)slot;
+  args.peer.row_chunk = (int)row_chunk;
+  args.peer.slot_stride = slot_stride;
+  args.peer.ld = ld;
+  args.peer.col_off = col_off;
+  rf::gemm_bf16(op, args, rf::kEpiPeer, (int)bn, 0, cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+void register_comm(pybind11::module_& m) {
+  m.def("ipc_malloc", &ipc_malloc_b);
+  m.def("ipc_free", &ipc_free_b);
+  m.def("ipc_handle", &ipc_handle_b);
+  m.def("ipc_open", &ipc_open_b);
+  m.def("ipc_close", &ipc_close_b);
+  m.def("tensor_at", &tensor_at);
+  m.def("comm_signal", &comm_signal_b);
+  m.def("comm_wait", &comm_wait_b);
+  m.def("comm_reduce_rows", &comm_reduce_rows_b);
+  m.def("comm_gather_rows", &comm_gather_rows_b);
+  m.def("gemm_peer", &gemm_peer_b);
 }

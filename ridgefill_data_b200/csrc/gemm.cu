@@ -307,6 +307,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               for (int j = 0; j < 32; ++j)
                 if (col0 + j < args.N) dst[j] = __float2bfloat16(v[j]);
             }
+          } else if constexpr (EPI == kEpiPeer) {
+            const PeerArgs& pa = args.peer;
+            if (pa.mode == 0) {
+              const int q = row / pa.row_chunk;
+              __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(pa.peer[q]) + (size_t)pa.slot * pa.slot_stride +
+                                   (size_t)(row - q * pa.row_chunk) * pa.ld + col0;
+              if (full_chunk && args.vec_ok) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8)
+                  *reinterpret_cast<uint4*>(dst + j) =
+                      make_uint4(pack_bf16x2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])),
+                                 pack_bf16x2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])),
+                                 pack_bf16x2(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5])),
+                                 pack_bf16x2(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7])));
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (col0 + j < args.N) dst[j] = __float2bfloat16(__uint_as_float(r[j]));
+              }
+            } else {
+              if (args.bias != nullptr) {
+                for (int j = 0; j < 32; ++j)
+                  if (col0 + j < args.N)
+                    r[j] = __float_as_uint(__uint_as_float(r[j]) + __bfloat162float(args.bias[col0 + j]));
+              }
+              uint4 packed[4];
+#pragma unroll
+              for (int j = 0; j < 32; j += 8)
+                packed[j / 8] = make_uint4(pack_bf16x2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])),
+                                           pack_bf16x2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])),
+                                           pack_bf16x2(__uint_as_float(r[j + 4]), __uint_as_float(r[j + 5])),
+                                           pack_bf16x2(__uint_as_float(r[j + 6]), __uint_as_float(r[j + 7])));
+              for (int q = 0; q < pa.n_peers; ++q) {
+                __nv_bfloat16* dst =
+                    reinterpret_cast<__nv_bfloat16*>(pa.peer[q]) + (size_t)row * pa.ld + pa.col_off + col0;
+                if (full_chunk && args.vec_ok) {
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(dst + 8 * j) = packed[j];
+                } else {
+                  for (int j = 0; j < 32; ++j)
+                    if (col0 + j < args.N) dst[j] = __float2bfloat16(__uint_as_float(r[j]));
+                }
+              }
+            }
           } else if constexpr (EPI == kEpiF32) {
             float* dst = reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + col0;
             if (full_chunk && args.vec_ok) {
@@ -432,6 +475,8 @@ void gemm_bf16(const GemmOperands& op, GemmArgs args, int epi, int bn, int max_c
   RF_GEMM_CASE(128, kEpiF64Acc, true, true)
   RF_GEMM_CASE(256, kEpiF64Acc, false, false)
   RF_GEMM_CASE(256, kEpiStore, true, true)
+  RF_GEMM_CASE(256, kEpiPeer, false, false)
+  RF_GEMM_CASE(128, kEpiPeer, false, false)
 #undef RF_GEMM_CASE
   throw std::runtime_error("gemm_bf16: unsupported (bn, epilogue, majors) combination");
 }

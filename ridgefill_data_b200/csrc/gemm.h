@@ -7,7 +7,24 @@
 
 namespace rf {
 
-enum GemmEpilogue : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiF32 = 2, kEpiF64Acc = 3 };
+enum GemmEpilogue : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiF32 = 2, kEpiF64Acc = 3, kEpiPeer = 4 };
+
+constexpr int kMaxPeers = 8;
+
+// Peer-store epilogue (kEpiPeer): bf16 tiles written straight into other GPUs' buffers (CUDA IPC mappings).
+//  mode 0 (scatter to row owner): rows are split in n_peers chunks of row_chunk; the tile of row r goes to
+//          peer[r / row_chunk] + slot * slot_stride + (r % row_chunk) * ld + col
+//  mode 1 (broadcast): every peer gets the tile at peer[q] + r * ld + col_off + col
+struct PeerArgs {
+  void* peer[kMaxPeers];
+  int n_peers;
+  int mode;
+  int slot;
+  int row_chunk;
+  long slot_stride;
+  long ld;
+  long col_off;
+};
 
 struct GemmOperands {
   const void* A;   // bf16; [M, K] (K-major) or [K, M] (MN-major), row pitch lda elements
@@ -29,6 +46,7 @@ struct GemmArgs {
   long ldr;
   int vec_ok;                       // out/residual pitches and bases allow 16-byte vector access
   int* err;                         // device error word (bounded waits), may be nullptr
+  PeerArgs peer;                    // kEpiPeer only
 };
 
 void gemm_bf16(const GemmOperands& op, GemmArgs args, int epi, int bn, int max_ctas, cudaStream_t stream);

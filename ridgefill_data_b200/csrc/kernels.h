@@ -5,6 +5,7 @@
 #include <cstdint>
 
 #include <atomic>
+#include <string>
 
 namespace rf {
 
@@ -99,5 +100,50 @@ struct GdnScanArgs {
   int* err;
 };
 void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream);
+
+// ---- comm.cu (peer-memory collectives; pointers are CUDA IPC mappings of the peers' buffers)
+constexpr int kMaxRanks = 8;
+
+struct PeerFlags {
+  int* ptr[kMaxRanks];   // every rank's flag array (this rank's own included)
+  int n;
+};
+
+struct ReduceRowsArgs {
+  const __nv_bfloat16* recv;       // [n_peers slots][rows][d] partials of this rank's row block
+  long slot_stride;                // elements between slots
+  const __nv_bfloat16* residual;   // [rows][d] (row pitch ld_res) or nullptr
+  long ld_res;
+  __nv_bfloat16* red;              // [rows][d] reduced rows (this rank's IPC buffer)
+  int rows, d, n_peers, my_rank;
+  const int* flags;                // this rank's flag array
+  int arrive_slot;                 // flags[arrive_slot + s]: rank s's partials have arrived
+  int reduced_slot;                // flags[reduced_slot + q]: owner q's rows are reduced (set on every rank)
+  int value;                       // the epoch of this call
+  int* counter;                    // zero-initialised completion counter (this rank)
+  PeerFlags peer_flags;
+  int* err;
+};
+
+struct GatherRowsArgs {
+  const __nv_bfloat16* peer_red[kMaxRanks];   // every owner's reduced rows
+  int n_peers, row_chunk, total_rows, d;
+  __nv_bfloat16* out;              // [total_rows][d] (row pitch ld_out)
+  long ld_out;
+  const int* flags;
+  int reduced_slot;
+  int value;
+  int* err;
+};
+
+void comm_signal(const PeerFlags& f, int slot, int value, cudaStream_t stream);
+void comm_wait(const int* flags, int first, int n, int value, int* err, cudaStream_t stream);
+void comm_reduce_rows(const ReduceRowsArgs& a, cudaStream_t stream);
+void comm_gather_rows(const GatherRowsArgs& a, cudaStream_t stream);
+void* ipc_malloc(size_t bytes);
+void ipc_free(void* p);
+std::string ipc_handle(void* p);
+void* ipc_open(const std::string& handle);
+void ipc_close(void* p);
 
 }  // namespace rf

@@ -204,8 +204,9 @@ class _B200:
             if projector is None:
                 x = b
             else:
-                x = G.linear(b, W[i] if W[i].dtype == self.dtype else W[i].to(self.dtype),
-                             bias=B[i] if B[i].dtype == self.dtype else B[i].to(self.dtype))
+                w = W[i] if W[i].dtype == self.dtype else W[i].to(self.dtype)
+                c = B[i] if B[i].dtype == self.dtype else B[i].to(self.dtype)
+                x = self.tp.map_fill(b, w, c) if self.tp is not None else G.linear(b, w, bias=c)
             self.fill(i, x, pos, cache)
 
 

@@ -8,12 +8,15 @@ Sharding (column-parallel in, row-parallel out; activations replicated across ra
               value heads read only its own key heads); in_proj rows, conv channels, A_log / dt_bias and out_proj
               columns follow
   MLP         the packed gate/up rows in whole 128-row blocks, down_proj the matching columns
-  norms, embedding, lm_head and the ridge maps stay replicated
-Per layer the two row-parallel products (o_proj or out_proj, and down_proj) are summed over ranks:
-  nccl        GEMM (residual added on rank 0 only) then an NCCL all-reduce: the baseline
-  fused       GEMM whose epilogue stores each partial tile straight into the owner's receive slot over NVLink
-              peer memory, then the owner reduces its row block and writes it to every rank
-              (parallel/fused.py; falls back to nccl when the fused kernels are unavailable)
+  ridge maps  column-sharded: each rank computes output features [r d / N, (r + 1) d / N) of x_l = h_S W_l^T + c_l
+              and the full x_l is gathered on every rank before the layer's RMSNorm + K/V / GDN projections
+  norms, embedding and lm_head stay replicated
+Communication per layer (the two row-parallel products, o_proj or out_proj and down_proj, summed over ranks; the
+map fill's column gather in late layers):
+  nccl        GEMM (residual added on rank 0 only) then an NCCL all-reduce; map slice then NCCL all-gather: the
+              baseline
+  fused       parallel/fused.py: GEMM epilogues store their tiles straight into peer memory (partials into the row
+              owner's receive slot; map columns into every rank's x_l), the owner reduces, every rank gathers
 """
 from __future__ import annotations
 
@@ -30,9 +33,11 @@ class TensorParallel:
         self.world = dist.get_world_size(group)
         self.mode = mode
         self.fused = None
-        if mode == "fused":
-            from .fused import FusedRowParallel
+        self.fused_fill = None
+        if mode == "fused" and self.world > 1:
+            from .fused import FusedMapFill, FusedRowParallel
             self.fused = FusedRowParallel(group)
+            self.fused_fill = FusedMapFill(group)
 
     def row_parallel(self, y, w, h):
         """h + sum over ranks of y_r w_r^T (each rank holds its K-slice y_r, w_r)."""
@@ -43,6 +48,26 @@ class TensorParallel:
         a = G.linear(y, w, residual=h if self.rank == 0 else None)
         dist.all_reduce(a, group=self.group)
         return a
+
+    def map_fill(self, b, W, B):
+        """x = b W^T + c with the map column-sharded over ranks (this rank computes output features
+        [r d / N, (r + 1) d / N)); returns the full [rows, d] on every rank."""
+        d = W.shape[0]
+        if self.world == 1:
+            return G.linear(b, W, bias=B)
+        c0, c1 = self.rank * d // self.world, (self.rank + 1) * d // self.world
+        if self.fused_fill is not None:
+            return self.fused_fill(b, W[c0:c1], B[c0:c1], d)
+        part = G.linear(b, W[c0:c1], bias=B[c0:c1])
+        out = torch.empty(self.world * b.shape[0], c1 - c0, dtype=part.dtype, device=part.device)
+        dist.all_gather_into_tensor(out, part, group=self.group)
+        return out.view(self.world, b.shape[0], c1 - c0).permute(1, 0, 2).reshape(b.shape[0], d)
+
+    def close(self):
+        for f in (self.fused, self.fused_fill):
+            if f is not None:
+                f.close()
+        self.fused = self.fused_fill = None
 
 
 def _span(total, world, rank, what):

@@ -46,10 +46,15 @@ def _worker(rank, world, port, mode, q):
                 ref, _ = m.forward_exact(ids, keep=keep)
                 hs, lower = run_lower(m, ids, [split])
                 ref_rf, _, _ = finish(m, ids, hs[split], lower, arm, 4)
-                shard(m, TensorParallel(mode=mode))
+                tp = TensorParallel(mode=mode)
+                shard(m, tp)
                 got, _ = m.forward_exact(ids, keep=keep)
                 hs, lower = run_lower(m, ids, [split])
                 got_rf, _, _ = finish(m, ids, hs[split], lower, arm, 4)
+                torch.cuda.synchronize()
+                from ridgefill_data_b200.ops._ext import check_errors
+                check_errors(dev)
+                tp.close()
             rel = lambda a, b: float((a - b).norm() / b.norm())  # noqa: E731
             out[cfg.name] = (rel(got, ref), rel(got_rf, ref_rf))
         q.put((rank, out))
@@ -59,7 +64,7 @@ def _worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["nccl"])
+@pytest.mark.parametrize("mode", ["nccl", "fused"])
 def test_tp2_matches_single_gpu(mode):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
