@@ -362,7 +362,61 @@ void gemm_peer_b(Tensor a, Tensor b, c10::optional<Tensor> bias, std::vector<int
 
 }  // namespace
 
+void router_topk_b(Tensor logits, int64_t E, int64_t k, Tensor idx, Tensor wts, bool norm) {
+  need(logits, at::kFloat, "logits");
+  need(idx, at::kInt, "idx");
+  need(wts, at::kFloat, "wts");
+  TORCH_CHECK(E <= 1024 && k <= 16 && logits.stride(1) == 1, "router_topk: E <= 1024, k <= 16");
+  rf::router_topk(logits.data_ptr<float>(), logits.stride(0), (int)logits.size(0), (int)E, (int)k,
+                  idx.data_ptr<int>(), wts.data_ptr<float>(), norm ? 1 : 0, cur());
+}
+
+void moe_align_b(Tensor idx, int64_t e0, int64_t E, Tensor counts, Tensor rank, Tensor seg_start, Tensor tile_start, Tensor pos,
+                 Tensor x, Tensor xp) {
+  need(idx, at::kInt, "idx");
+  need(x, at::kBFloat16, "x");
+  need(xp, at::kBFloat16, "xp");
+  TORCH_CHECK(E <= 4096 && x.size(1) % 8 == 0 && x.stride(1) == 1, "moe_align: E <= 4096, d % 8");
+  const int n = (int)idx.size(0), k = (int)idx.size(1);
+  rf::moe_align(idx.data_ptr<int>(), n, k, (int)e0, (int)E, counts.data_ptr<int>(), rank.data_ptr<int>(),
+                seg_start.data_ptr<int>(), tile_start.data_ptr<int>(), pos.data_ptr<int>(), cbf(x), x.stride(0), bf(xp),
+                (int)x.size(1), cur());
+}
+
+void grouped_gemm_b(Tensor xp, Tensor w, Tensor seg_start, Tensor tile_start, Tensor out, bool swiglu, Tensor err) {
+  need(xp, at::kBFloat16, "xp");
+  need(w, at::kBFloat16, "w");
+  need(out, at::kBFloat16, "out");
+  TORCH_CHECK(w.dim() == 3 && w.is_contiguous() && xp.is_contiguous(), "grouped_gemm: w [E, N, K] contiguous");
+  TORCH_CHECK(w.size(2) == xp.size(1), "grouped_gemm: K mismatch");
+  c10::cuda::CUDAGuard g(xp.device());
+  rf::grouped_gemm(cbf(xp), xp.size(0), cbf(w), (int)w.size(0), (int)w.size(1), (int)w.size(2),
+                   seg_start.data_ptr<int>(), tile_start.data_ptr<int>(), bf(out), out.stride(0), swiglu ? 1 : 0,
+                   err.data_ptr<int>(), cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void moe_combine_b(c10::optional<Tensor> h_opt, Tensor y, Tensor pos, Tensor w, c10::optional<Tensor> ys,
+                   c10::optional<Tensor> gate_logit, Tensor out) {
+  need(out, at::kBFloat16, "out");
+  const __nv_bfloat16* hp = h_opt.has_value() ? cbf(*h_opt) : nullptr;
+  const long ldh = h_opt.has_value() ? h_opt->stride(0) : 0;
+  const Tensor& h = out;
+  need(y, at::kBFloat16, "y");
+  need(out, at::kBFloat16, "out");
+  const int n = (int)h.size(0), k = (int)pos.size(1), d = (int)h.size(1);
+  const __nv_bfloat16* ysp = ys.has_value() ? cbf(*ys) : nullptr;
+  const float* gl = gate_logit.has_value() ? gate_logit->data_ptr<float>() : nullptr;
+  const long ldg = gate_logit.has_value() ? gate_logit->stride(0) : 0;
+  rf::moe_combine(hp, ldh, cbf(y), pos.data_ptr<int>(), w.data_ptr<float>(), n, k, ysp, gl, ldg, bf(out), d,
+                  cur());
+}
+
 void register_comm(pybind11::module_& m) {
+  m.def("router_topk", &router_topk_b);
+  m.def("moe_align", &moe_align_b);
+  m.def("grouped_gemm", &grouped_gemm_b);
+  m.def("moe_combine", &moe_combine_b);
   m.def("ipc_malloc", &ipc_malloc_b);
   m.def("ipc_free", &ipc_free_b);
   m.def("ipc_handle", &ipc_handle_b);

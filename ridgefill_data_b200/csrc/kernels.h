@@ -101,6 +101,18 @@ struct GdnScanArgs {
 };
 void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream);
 
+// ---- moe.cu
+void router_topk(const float* logits, long ld, int n, int E, int k, int* idx, float* wts, int norm,
+                 cudaStream_t stream);
+void moe_align(const int* idx, int n, int k, int e0, int E, int* counts, int* rank, int* seg_start, int* tile_start,
+               int* pos, const __nv_bfloat16* x, long ldx, __nv_bfloat16* xp, int d, cudaStream_t stream);
+void grouped_gemm(const __nv_bfloat16* xp, long rows_cap, const __nv_bfloat16* w, int E, int N, int K,
+                  const int* seg_start, const int* tile_start, __nv_bfloat16* out, long ldo, int swiglu, int* err,
+                  cudaStream_t stream);
+void moe_combine(const __nv_bfloat16* h, long ldh, const __nv_bfloat16* y, const int* pos, const float* w, int n,
+                 int k, const __nv_bfloat16* ys, const float* gate_logit, long ldg, __nv_bfloat16* out, int d,
+                 cudaStream_t stream);
+
 // ---- comm.cu (peer-memory collectives; pointers are CUDA IPC mappings of the peers' buffers)
 constexpr int kMaxRanks = 8;
 

@@ -30,6 +30,7 @@ class _B200:
     zero_centred = False
     capacity_hint = 0
     tp = None          # parallel.tp.TensorParallel when the weights are sharded over ranks
+    ep = None          # parallel.ep.ExpertParallel when the experts are spread over ranks
 
     # ---- setup
     def _kernel_setup(self):
@@ -255,9 +256,25 @@ class B200Hybrid(_B200, Hybrid):
             w.update(in_p=p, qkv=p[:C], b=p[C:C + nv], a=p[C + nv:C + 2 * nv], z=p[C + 2 * nv:],
                      conv=w["conv"].contiguous(), A_log=w["A_log"].float().contiguous(),
                      dt_bias=w["dt_bias"].float().contiguous())
-        if not self.cfg.moe:
+        if self.cfg.moe:
+            self._pack_moe(w)
+        else:
             self._pack_mlp(w)
         return w
+
+    def _pack_moe(self, w):
+        """Router rows extended by the shared-expert gate (padded to a multiple of 8 rows), each expert's gate/up
+        interleaved per 128-row block for the grouped SwiGLU GEMM, the shared expert packed like a dense MLP."""
+        E, d = self.cfg.n_experts, self.hidden
+        pad = (-(E + 1)) % 8
+        w["router_ext"] = torch.cat((w["router"], w["sh_gate_w"],
+                                     torch.zeros(pad, d, dtype=self.dtype, device=self.device))).contiguous()
+        F = self.cfg.moe_intermediate
+        gu = w["experts_gu"]
+        w["experts_gu_p"] = torch.stack([G.pack_gate_up(gu[e, :F], gu[e, F:]) for e in range(E)]).contiguous()
+        w["experts_down"] = w["experts_down"].contiguous()
+        del w["experts_gu"]
+        w["sh_gu_p"] = G.pack_gate_up(w["sh_gate"], w["sh_up"]).contiguous()
 
     def _gdn_core_dev(self, i, proj, cache, need_out):
         """Conv + gates + chunked delta rule over the rows of proj, continuing cache[i]'s states."""
@@ -297,5 +314,22 @@ class B200Hybrid(_B200, Hybrid):
 
     def mlp(self, i, h):
         if self.cfg.moe:
-            return Hybrid.mlp(self, i, h)
+            return self._moe_mlp(i, h)
         return _B200.mlp(self, i, h)
+
+    def _moe_mlp(self, i, h):
+        """Routed experts on the expert-grouped tcgen05 GEMM plus the gated shared expert, combined with the
+        residual in one pass (ops/moe.py)."""
+        from ..ops import moe as MO
+        w = self.W[i]
+        E, k = self.cfg.n_experts, self.cfg.top_k
+        x = K.rmsnorm(h, w["ln2"], self.eps, self.zero_centred)
+        logits = G.linear_f32(x, w["router_ext"])
+        if self.ep is not None:
+            return self.ep.moe(self, w, h, x, logits)
+        idx, wts = MO.router_topk(logits, E, k)
+        xp, pos, seg, tiles = MO.align(idx, E, x)
+        act = MO.grouped(xp, w["experts_gu_p"], seg, tiles, swiglu=True)
+        y = MO.grouped(act, w["experts_down"], seg, tiles, swiglu=False)
+        ys = G.linear(G.swiglu_linear(x, w["sh_gu_p"]), w["sh_down"])
+        return MO.combine(h, y, pos, wts, ys, logits[:, E])

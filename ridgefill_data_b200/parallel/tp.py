@@ -133,15 +133,17 @@ def shard(model, tp: TensorParallel):
     if world == 1:
         model.tp = tp
         return model
-    if cfg.moe:
-        raise ValueError("mixture-of-experts layers are expert-parallel (parallel/ep.py), not tensor-parallel")
     local = {}
     for i, w in enumerate(model.W):
         if model.layer_types[i] == "attn":
             local["attn"] = shard_attention(w, cfg, rank, world)
         else:
             local["gdn"] = shard_gdn(w, cfg, rank, world)
-        shard_mlp(w, rank, world)
+        if not cfg.moe:
+            shard_mlp(w, rank, world)
+    if cfg.moe:       # the MoE MLPs are expert-parallel over the same ranks
+        from .ep import ExpertParallel
+        ExpertParallel(tp.group, tp).shard(model)
     if "attn" in local:
         model.n_heads, model.n_kv = local["attn"]
     if "gdn" in local:

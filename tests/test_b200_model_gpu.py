@@ -90,3 +90,29 @@ def test_decode_steps_match_torch():
             lg[k] = m.logits(h)
         e_dut, e_ref = _rel(lg["dut"], lg["f32"]), _rel(lg["ref"], lg["f32"])
         assert e_dut < 1.5 * e_ref + 5e-3, (t, e_dut, e_ref)
+
+
+MOE = ModelConfig(arch="qwen3_5_moe", n_layers=4, hidden=512, vocab=1024, n_heads=4, n_kv=1, head_dim=256,
+                  intermediate=0, eps=1e-6, rope_theta=1e7, partial_rotary=0.25, layer_types=_hybrid_types(4),
+                  gdn_nk=2, gdn_nv=4, gdn_dk=128, gdn_dv=128, conv_k=4, n_experts=16, top_k=4,
+                  moe_intermediate=256, shared_intermediate=256, name="tiny-moe")
+
+
+def test_router_topk_matches_torch():
+    from ridgefill_data_b200.ops import moe as MO
+    from ridgefill_data_b200.ops.oracle import router_topk
+    torch.manual_seed(0)
+    logits = torch.randn(300, 520, device="cuda")
+    idx, w = MO.router_topk(logits, 512, 10)
+    rw, ri = router_topk(logits[:, :512], 10)
+    assert torch.equal(idx.long(), ri) and torch.allclose(w, rw, atol=1e-6)
+
+
+def test_moe_forward_matches_torch():
+    ref, dut = _pair(MOE)
+    ids = torch.randint(0, MOE.vocab, (333,), generator=torch.Generator().manual_seed(1)).cuda()
+    keep = torch.arange(300, 333, device="cuda")
+    lr, _ = ref.forward_exact(ids, keep=keep)
+    ld, _ = dut.forward_exact(ids, keep=keep)
+    l32, _ = _fp32(MOE).forward_exact(ids, keep=keep)
+    assert _rel(ld, l32) < 1.5 * _rel(lr, l32) + 5e-3, (_rel(ld, l32), _rel(lr, l32))
