@@ -34,8 +34,13 @@ sys.path.insert(0, ROOT)
 
 # Published RidgeFill prompt time of the 27B hybrid at 16K tokens (llama.cpp fork, resident maps, split 16,
 # tail 4096, one A100 40 GB): 10.380 s -> tokens / s.
-BASELINE_TOK_S = {16384: 16384 / 10.380, 32768: 32768 / 21.112, 65536: 65536 / 46.284, 122880: 122880 / 100.014}
-METRIC = "prefill tok/s (RidgeFill TTFT), Qwen3.8-27B-shaped hybrid"
+BASELINE_TOK_S = {"qwen3.8-27b": {16384: 16384 / 10.380, 32768: 32768 / 21.112, 65536: 65536 / 46.284,
+                                   122880: 122880 / 100.014},
+                  # Flash-Next RidgeFill TTFT medians (vLLM fork, TP2 on 2x AMD R9700): 9K / 16K / 32K
+                  "flash-next": {9216: 9216 / 10.178, 16384: 16384 / 16.463, 32768: 32768 / 31.180}}
+METRIC = {"qwen3.8-27b": "prefill tok/s (RidgeFill TTFT), Qwen3.8-27B-shaped hybrid",
+          "flash-next": "prefill tok/s (RidgeFill TTFT), Flash-Next-shaped MoE hybrid"}
+DEFAULT_SPLIT_TAIL = {"qwen3.8-27b": (32, 4096), "flash-next": (24, 2048)}
 
 
 class ClockSampler:
@@ -121,14 +126,17 @@ def main():
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--model", default="qwen3.8-27b")
     ap.add_argument("--seq", type=int, default=16384)
-    ap.add_argument("--tail", type=int, default=4096)
-    ap.add_argument("--split", type=int, default=32)
+    ap.add_argument("--tail", type=int)
+    ap.add_argument("--split", type=int)
     ap.add_argument("--exact", action="store_true", help="also time full (exact) prefill for the speedup")
     ap.add_argument("--parallel", default="tp", choices=("tp", "dp"))
     ap.add_argument("--tp-comm", default="nccl", choices=("nccl", "fused"))
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
+    dsplit, dtail = DEFAULT_SPLIT_TAIL.get(args.model, (32, 4096))
+    args.split = dsplit if args.split is None else args.split
+    args.tail = dtail if args.tail is None else args.tail
     args.warmup = max(3, args.warmup)
 
     import torch
@@ -229,9 +237,9 @@ def main():
     tokens = args.seq * (1 if tp_mode else world)
     value = tokens / (ms_max / 1e3)
     e2e_value = tokens / (e2e_max / 1e3)
-    base = BASELINE_TOK_S.get(args.seq)
+    base = BASELINE_TOK_S.get(args.model, {}).get(args.seq)
     if rank == 0:
-        line = dict(metric=METRIC, value=round(value, 1), unit="tokens/s", n_gpus=world, steps=args.steps,
+        line = dict(metric=METRIC.get(args.model, f"prefill tok/s (RidgeFill TTFT), {args.model}"), value=round(value, 1), unit="tokens/s", n_gpus=world, steps=args.steps,
                     warmup=args.warmup, ms_per_step=round(ms_max, 3), higher_is_better=True,
                     scaling="strong" if tp_mode else "weak", vs_baseline=round(value / base, 3) if base else None, dtype="bf16",
                     data="synthetic (seeded uniform prompt; random-init weights and ridge maps of the named shapes)",
@@ -239,7 +247,7 @@ def main():
                                 split=args.split, tail=args.tail,
                                 parallelism=(f"tp{world}" + ("" if args.tp_comm == "nccl" else "-fused")) if tp_mode
                                 else f"dp{world}",
-                                l2="inputs larger than L2 (54 GB of weights streamed per step)"),
+                                l2="inputs larger than L2 (the weights, tens of GB, are streamed every step)"),
                     clocks=clocks, gpu_launches=int(launches),
                     e2e=dict(value=round(e2e_value, 1), unit="tokens/s", ms_per_step=round(e2e_max, 3),
                              h2d_bytes_per_step=int(ids_host.numel() * ids_host.element_size()),

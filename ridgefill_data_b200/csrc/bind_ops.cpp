@@ -412,7 +412,18 @@ void moe_combine_b(c10::optional<Tensor> h_opt, Tensor y, Tensor pos, Tensor w, 
                   cur());
 }
 
+void cholesky_solve_b(Tensor a, Tensor b, double shift, Tensor err) {
+  need(a, at::kDouble, "a");
+  need(b, at::kDouble, "b");
+  TORCH_CHECK(a.dim() == 2 && a.size(0) == a.size(1) && a.stride(1) == 1 && b.stride(1) == 1 &&
+                  b.size(0) == a.size(0), "cholesky_solve: a [n, n], b [n, R]");
+  c10::cuda::CUDAGuard g(a.device());
+  rf::cholesky_solve(a.data_ptr<double>(), (int)a.size(0), a.stride(0), shift, b.data_ptr<double>(), b.stride(0),
+                     (int)b.size(1), err.data_ptr<int>(), cur());
+}
+
 void register_comm(pybind11::module_& m) {
+  m.def("cholesky_solve", &cholesky_solve_b);
   m.def("router_topk", &router_topk_b);
   m.def("moe_align", &moe_align_b);
   m.def("grouped_gemm", &grouped_gemm_b);

@@ -113,6 +113,9 @@ void moe_combine(const __nv_bfloat16* h, long ldh, const __nv_bfloat16* y, const
                  int k, const __nv_bfloat16* ys, const float* gate_logit, long ldg, __nv_bfloat16* out, int d,
                  cudaStream_t stream);
 
+// ---- linalg.cu
+void cholesky_solve(double* a, int n, long lda, double shift, double* b, long ldb, int R, int* err, cudaStream_t s);
+
 // ---- comm.cu (peer-memory collectives; pointers are CUDA IPC mappings of the peers' buffers)
 constexpr int kMaxRanks = 8;
 
