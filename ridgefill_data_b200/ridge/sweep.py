@@ -35,11 +35,39 @@ def stale_projectors(paths, rows):
     return [(p, meta_of(p).get("rows")) for p in paths if Path(p).exists() and meta_of(p).get("rows") != str(rows)]
 
 
-def capture(model, docs, splits, device=None, log=print):
-    """{S: RidgeStats} over the documents (forward_exact with a capture hook)."""
+def _common_shifts(model, doc, splits, group):
+    """Shifts (first-block means of the boundary and every late layer's input) taken from one document on rank 0
+    and broadcast, so every rank's sums share them and can simply be added."""
+    import torch.distributed as dist
+    L, H = model.n_layers, model.hidden
+    lo = min(splits)
+    buf = torch.zeros(L - lo + 1, H, dtype=torch.float32, device=model.device)
+    if dist.get_rank(group) == 0:
+        got = {}
+        with torch.no_grad():
+            model.forward_exact(torch.as_tensor(doc["ids"]).to(model.device),
+                                hook=lambda i, h: got.__setitem__(i, h[:8192].float().mean(0)) if i != "final" else None)
+        for i in range(lo, L):
+            buf[i - lo] = got[i]
+    dist.broadcast(buf, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+    return {i: buf[i - lo] for i in range(lo, L)}
+
+
+def capture(model, docs, splits, device=None, log=print, group=None):
+    """{S: RidgeStats} over the documents (forward_exact with a capture hook). With a process group the documents
+    are split over the ranks (data parallel), every rank uses rank 0's shifts, and the fp64 sums are added over
+    the ranks at the end (one reduction per statistic: each rank keeps its partial sums on the device until then)."""
     L, H = model.n_layers, model.hidden
     dev = device or model.device
     stats = {S: RidgeStats(S, range(S, L), H, dev) for S in splits}
+    if group is not None:
+        import torch.distributed as dist
+        shifts = _common_shifts(model, docs[0], splits, group)
+        for S, st in stats.items():
+            st.cx = shifts[S].to(dev)
+            st.cy = {i: shifts[i].to(dev) for i in range(S, L)}
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        docs = docs[rank::world]
     t0 = time.time()
     with torch.no_grad():
         for j, d in enumerate(docs):
@@ -54,6 +82,14 @@ def capture(model, docs, splits, device=None, log=print):
             model.forward_exact(torch.as_tensor(d["ids"]).to(model.device), hook=hook)
             if log and (j % 10 == 0 or j == len(docs) - 1):
                 log(f"capture {j + 1}/{len(docs)} rows {int(stats[splits[0]].n)} ({time.time() - t0:.0f}s)")
+    if group is not None:
+        import torch.distributed as dist
+        for st in stats.values():
+            n = torch.tensor([st.n], dtype=torch.float64, device=st.sx.device)
+            dist.all_reduce(n, group=group)
+            st.n = float(n.item())
+            for t in [st.sx, st.sxx] + list(st.sy.values()) + list(st.sxy.values()):
+                dist.all_reduce(t, group=group)
     return stats
 
 
@@ -104,7 +140,7 @@ def fit_split(stats_state, S, L, lams, solver="eigen", center=True, device=None)
 
 
 def fit(model, docs, splits, lambdas=LAMBDAS, held=None, out_dir=None, name=None, solver=None, center=True,
-        save_stats=False, log=print, meta_extra=None):
+        save_stats=False, log=print, meta_extra=None, group=None):
     """Fit maps for every split. Returns {S: dict(projector, lambda_star, mean_read_cos, per_layer_read_cos,
     record)}; writes files when out_dir is given."""
     splits = sorted(int(s) for s in splits)
@@ -119,7 +155,7 @@ def fit(model, docs, splits, lambdas=LAMBDAS, held=None, out_dir=None, name=None
         if stale:
             raise StaleProjector("fitted on another calibration list: " + ", ".join(f"{p} ({r})" for p, r in stale))
     solver = solver or ("cholesky" if model.device.type == "cuda" else "eigen")
-    stats = capture(model, docs, splits, log=log)
+    stats = capture(model, docs, splits, log=log, group=group)
     results = {}
     for S in sorted(splits, reverse=True):
         t0 = time.time()
@@ -140,7 +176,8 @@ def fit(model, docs, splits, lambdas=LAMBDAS, held=None, out_dir=None, name=None
         proj = Projector(S, W, B, {k: str(v) for k, v in dict(meta, split=S).items()})
         record = dict(rows=rows, docs=len(docs), lambda_star=best, mean_read_cos=mean,
                       per_layer_read_cos=per_layer, solver=solver, center=center)
-        if out_dir:
+        write = out_dir is not None and (group is None or __import__("torch.distributed").distributed.get_rank(group) == 0)
+        if write:
             path = proj_path(S)
             proj.save(path, meta)
             record.update(provenance=prov.provenance(name, dict(split=S, lambdas=list(lambdas), sweep_splits=splits,

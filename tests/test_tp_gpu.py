@@ -86,3 +86,46 @@ def test_tp2_matches_single_gpu(mode):
             # the sharded run is no further from fp32 than the unsharded bf16 run (plus a margin)
             assert e_tp < 1.5 * e_single + 5e-3, (r, name, e_tp, e_single)
             assert e_rf < 5e-2, (r, name, e_rf)
+
+
+def _fit_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from ridgefill_data_b200.eval.data import zipf_docs
+        from ridgefill_data_b200.models.base import from_config
+        from ridgefill_data_b200.ridge import sweep
+        from test_b200_model_gpu import HYB
+        m = from_config(HYB, seed=0, device=torch.device("cuda", rank), std=0.05, backend="b200")
+        docs = zipf_docs(6, 256, HYB.vocab, seed=1)
+        dp = sweep.fit(m, docs, [4], lambdas=(0.03,), log=None, group=dist.group.WORLD)
+        single = sweep.fit(m, docs, [4], lambdas=(0.03,), log=None)
+        errs = []
+        for i in range(4, HYB.n_layers):
+            a, b = dp[4]["maps"][0.03][i][0], single[4]["maps"][0.03][i][0]
+            errs.append(float((a.cpu() - b.cpu()).norm() / b.cpu().norm()))
+        q.put((rank, max(errs)))
+    except Exception as e:  # pragma: no cover
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_data_parallel_fit_matches_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fit_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for r, err in res.items():
+        assert isinstance(err, float) and err < 1e-3, (r, err)
