@@ -9,6 +9,7 @@
 #include "mma.cuh"
 
 #include <cfloat>
+#include <stdexcept>
 
 namespace rf {
 
@@ -234,6 +235,8 @@ static void launch_fa(const AttnArgs& a, cudaStream_t stream) {
 
 void flash_attention(const AttnArgs& a, cudaStream_t stream) {
   if (a.nq <= 0) return;
+  if (a.impl != 1 && flash_attention_tc(a, stream)) return;
+  if (a.impl == 2) throw std::runtime_error("flash_attention: the tcgen05 path does not cover this call");
   switch (a.hd) {
     case 64: launch_fa<64>(a, stream); break;
     case 128: launch_fa<128>(a, stream); break;

@@ -1,0 +1,387 @@
+// Flash prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM), for queries at contiguous
+// positions q_start .. q_start + nq - 1 over keys 0 .. nk - 1 (query at position p sees keys j <= p).
+//
+// CTA = 128 query rows of one query head (GQA: K/V of head / (hq / hkv)); 192 threads:
+//   warp 0      TMA: Q once, K and V tiles of BN keys into a 2-stage ring (3-D tensor maps [heads][rows][hd], so
+//               keys past nk read as zeros)
+//   warp 1      UMMA issuer: S_j = Q K_j^T into one of two TMEM S buffers, then O += P_{j-1} V_{j-1} into the TMEM
+//               O accumulator (P from shared memory, V as an MN-major B operand)
+//   warps 2..5  softmax: thread = query row; S row from TMEM, causal mask, exp2 with the scale folded in, row sum;
+//               O is rescaled in TMEM only when the row max grows by more than 2^8 (otherwise the stale max stays
+//               exact for both O and l); P rounded to bf16 into shared memory in the 128-byte-swizzled K-major
+//               layout; finally O / l (times sigmoid(gate)) to global memory
+// Every mbarrier wait is bounded (ptx.cuh); the kernel records an error code instead of hanging.
+#include "kernels.h"
+#include "ptx.cuh"
+
+#include <cudaTypedefs.h>
+#include <stdexcept>
+#include <string>
+
+namespace rf {
+
+template <int HD, int BN>
+struct TcFaCfg {
+  static constexpr int Q_BYTES = 128 * HD * 2;
+  static constexpr int K_BYTES = BN * HD * 2;
+  static constexpr int V_BYTES = BN * HD * 2;
+  static constexpr int P_BYTES = 128 * BN * 2;
+  static constexpr int BAR_BYTES = 8 * 16 + 16;
+  static constexpr int SMEM = 1024 + Q_BYTES + 2 * (K_BYTES + V_BYTES) + P_BYTES + BAR_BYTES;
+  static constexpr int O_COL = 2 * BN;
+};
+
+struct TcFaArgs {
+  int hq, hkv, nq, nk, q_start;
+  float scale_log2;
+  const __nv_bfloat16* gate;
+  long gate_row, gate_head;
+  __nv_bfloat16* out;
+  long out_row;
+  int* err;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <int HD, int BN>
+__global__ void __launch_bounds__(192, 1)
+    tc_flash_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, TcFaArgs a) {
+  using Cfg = TcFaCfg<HD, BN>;
+  constexpr uint32_t IDESC_S = idesc_bf16_f32(128, BN, false, false);
+  constexpr uint32_t IDESC_O = idesc_bf16_f32(128, HD, false, true);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + Cfg::Q_BYTES;
+  uint8_t* sV = sK + 2 * Cfg::K_BYTES;
+  uint8_t* sP = sV + 2 * Cfg::V_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + Cfg::P_BYTES);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* v_full = bars + 3;    // [2]
+  uint64_t* k_empty = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* s_free = bars + 11;   // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* p_free = bars + 14;
+  uint64_t* o_final = bars + 15;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int qt = gridDim.x - 1 - blockIdx.x;   // late (heavy) query tiles first
+  const int head = blockIdx.y;
+  const int kvh = head / (a.hq / a.hkv);
+  const int q0 = qt * 128;
+  const int rows_valid = min(128, a.nq - q0);
+  const int n_keys = min(a.nk, a.q_start + q0 + rows_valid);
+  const int ntiles = (n_keys + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(p_free, 1);
+    mbar_init(o_final, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_expect_tx(q_full, Cfg::Q_BYTES);
+#pragma unroll
+      for (int b = 0; b < HD / 64; ++b) tma_load_3d(sQ + b * 128 * 128, &tmQ, q_full, b * 64, q0, head);
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j & 1;
+        const uint32_t par = ((j >> 1) & 1) ^ 1u;
+        if (*abort_flag || !mbar_wait(&k_empty[st], par, a.err, kErrTimeoutProducer)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_expect_tx(&k_full[st], Cfg::K_BYTES);
+#pragma unroll
+        for (int b = 0; b < HD / 64; ++b)
+          tma_load_3d(sK + st * Cfg::K_BYTES + b * BN * 128, &tmK, &k_full[st], b * 64, j * BN, kvh);
+        if (!mbar_wait(&v_empty[st], par, a.err, kErrTimeoutProducer)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_expect_tx(&v_full[st], Cfg::V_BYTES);
+#pragma unroll
+        for (int b = 0; b < HD / 64; ++b)
+          tma_load_3d(sV + st * Cfg::V_BYTES + b * BN * 128, &tmV, &v_full[st], b * 64, j * BN, kvh);
+      }
+    }
+  } else if (warp == 1) {
+    bool ok = mbar_wait(q_full, 0, a.err, kErrTimeoutMma);
+    tc_fence_after();
+    const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+    auto issue_pv = [&](int jj) -> bool {
+      const int st = jj & 1;
+      if (!mbar_wait(p_full, jj & 1, a.err, kErrTimeoutMma)) return false;
+      if (!mbar_wait(&v_full[st], (jj >> 1) & 1, a.err, kErrTimeoutMma)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t v_addr = smem_u32(sV + st * Cfg::V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t ad = sdesc_sw128(p_addr + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, BN * 128, 1024);
+          umma_f16(tmem + Cfg::O_COL, ad, bd, IDESC_O, (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(p_free);
+        umma_commit(&v_empty[st]);
+      }
+      __syncwarp();
+      return true;
+    };
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int st = j & 1;
+      if (*abort_flag || !mbar_wait(&k_full[st], (j >> 1) & 1, a.err, kErrTimeoutMma)) {
+        ok = false;
+        break;
+      }
+      if (j >= 2 && !mbar_wait(&s_free[st], ((j - 2) >> 1) & 1, a.err, kErrTimeoutMma)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t k_addr = smem_u32(sK + st * Cfg::K_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t ad = sdesc_sw128(q_addr + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(k_addr + (kk >> 2) * BN * 128 + (kk & 3) * 32, 16, 1024);
+          umma_f16(tmem + st * BN, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[st]);
+        umma_commit(&k_empty[st]);
+      }
+      __syncwarp();
+      if (j >= 1 && !issue_pv(j - 1)) {
+        ok = false;
+        break;
+      }
+    }
+    if (ok && ntiles > 0) ok = issue_pv(ntiles - 1);
+    if (lane == 0) umma_commit(o_final);   // also drains whatever was issued on the abort path
+    __syncwarp();
+    if (!ok) *abort_flag = 1;
+  } else {
+    // ---------------------------------------------------------------- softmax + epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int pos = a.q_start + q0 + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j & 1;
+      if (*abort_flag || !mbar_wait(&s_full[st], (j >> 1) & 1, a.err, kErrTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[BN];
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + st * BN + c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) x[c + e] = __uint_as_float(v[e]) * a.scale_log2;
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[st]);
+      const int key0 = j * BN;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < BN; ++e) {
+        const int key = key0 + e;
+        if (key > pos || key >= n_keys) x[e] = -INFINITY;
+        mt = fmaxf(mt, x[e]);
+      }
+      float m_new = fmaxf(m_used, mt);
+      bool rescale = false;
+      float factor = 1.f;
+      if (m_used == -INFINITY) {
+        m_used = m_new;
+      } else if (m_new > m_used + 8.f) {
+        rescale = true;
+        factor = exp2f(m_used - m_new);
+        m_used = m_new;
+      }
+      const float base = m_used == -INFINITY ? 0.f : m_used;
+      float sum = 0.f;
+#pragma unroll
+      for (int e = 0; e < BN; ++e) {
+        x[e] = exp2f(x[e] - base);
+        sum += x[e];
+      }
+      l = l * factor + sum;
+      if (j >= 1) {
+        if (!mbar_wait(p_free, (j - 1) & 1, a.err, kErrTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int c = 0; c < HD; c += 32) {
+            uint32_t v[32];
+            tmem_ld32(tmem + lane_off + Cfg::O_COL + c, v);
+            tmem_wait_ld();
+            uint32_t w16a[16], w16b[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              w16a[e] = __float_as_uint(__uint_as_float(v[e]) * factor);
+              w16b[e] = __float_as_uint(__uint_as_float(v[16 + e]) * factor);
+            }
+            tmem_st16(tmem + lane_off + Cfg::O_COL + c, w16a);
+            tmem_st16(tmem + lane_off + Cfg::O_COL + c + 16, w16b);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P row -> shared memory, 128-byte swizzle, K-major (keys along K), 64-key column blocks
+#pragma unroll
+      for (int c = 0; c < BN; c += 8) {
+        uint4 pk;
+        pk.x = pack_bf16x2(x[c], x[c + 1]);
+        pk.y = pack_bf16x2(x[c + 2], x[c + 3]);
+        pk.z = pack_bf16x2(x[c + 4], x[c + 5]);
+        pk.w = pack_bf16x2(x[c + 6], x[c + 7]);
+        const int blk = c >> 6, chunk = (c & 63) >> 3;
+        uint8_t* dst = sP + blk * 128 * 128 + r * 128 + ((chunk ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = pk;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // epilogue
+    if (ok && mbar_wait(o_final, 0, a.err, kErrTimeoutEpilogue)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const long qrow = q0 + r;
+      const bool row_ok = r < rows_valid;
+      __nv_bfloat16* dst = a.out + qrow * a.out_row + (long)head * HD;
+      const __nv_bfloat16* gt = a.gate != nullptr ? a.gate + qrow * a.gate_row + (long)head * a.gate_head : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + Cfg::O_COL + c, v);
+        tmem_wait_ld();
+        if (!row_ok) continue;
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          float o[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) o[q] = __bfloat162float(__float2bfloat16(__uint_as_float(v[e + q]) * inv));
+          if (gt != nullptr) {
+            uint4 gv = *reinterpret_cast<const uint4*>(gt + c + e);
+            const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gv);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float z = __bfloat162float(ge[q]);
+              o[q] *= __bfloat162float(__float2bfloat16(1.f / (1.f + expf(-z))));
+            }
+          }
+          uint4 w;
+          w.x = pack_bf16x2(o[0], o[1]);
+          w.y = pack_bf16x2(o[2], o[3]);
+          w.z = pack_bf16x2(o[4], o[5]);
+          w.w = pack_bf16x2(o[6], o[7]);
+          *reinterpret_cast<uint4*>(dst + c + e) = w;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fa() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess || p == nullptr)
+      throw std::runtime_error("cuTensorMapEncodeTiled entry point unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 3-D map over [heads][rows][hd] (row pitch hd, head pitch head_stride elements), box {64, box_rows, 1}
+static CUtensorMap tmap3(const void* base, int hd, int rows, int heads, long head_stride, int box_rows) {
+  CUtensorMap tm;
+  cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)rows, (cuuint64_t)heads};
+  cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)head_stride * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fa()(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("tc_flash: tensor map encode failed " + std::to_string((int)r));
+  return tm;
+}
+
+template <int HD, int BN>
+static void launch_tc(const AttnArgs& x, cudaStream_t stream) {
+  using Cfg = TcFaCfg<HD, BN>;
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(tc_flash_kernel<HD, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    set = true;
+  }
+  CUtensorMap tq = tmap3(x.q, HD, x.nq, x.hq, x.q_head_stride, 128);
+  CUtensorMap tk = tmap3(x.k, HD, x.nk, x.hkv, x.kv_head_stride, BN);
+  CUtensorMap tv = tmap3(x.v, HD, x.nk, x.hkv, x.kv_head_stride, BN);
+  TcFaArgs a{x.hq, x.hkv, x.nq, x.nk, x.q_start, x.scale * 1.4426950408889634f, x.gate, x.gate_row, x.gate_head,
+             x.out, x.out_row, x.err};
+  dim3 grid((x.nq + 127) / 128, x.hq);
+  tc_flash_kernel<HD, BN><<<grid, 192, Cfg::SMEM, stream>>>(tq, tk, tv, a);
+  count_launch();
+}
+
+bool flash_attention_tc(const AttnArgs& x, cudaStream_t stream) {
+  if (x.qpos != nullptr || x.nq <= 0) return false;
+  if (reinterpret_cast<uintptr_t>(x.q) % 16 || reinterpret_cast<uintptr_t>(x.k) % 16 ||
+      reinterpret_cast<uintptr_t>(x.v) % 16)
+    return false;
+  if (x.gate != nullptr && (x.gate_row % 8 || x.gate_head % 8 || reinterpret_cast<uintptr_t>(x.gate) % 16))
+    return false;
+  if (x.out_row % 8) return false;
+  switch (x.hd) {
+    case 128: launch_tc<128, 128>(x, stream); return true;
+    case 256: launch_tc<256, 64>(x, stream); return true;
+    default: return false;
+  }
+}
+
+}  // namespace rf

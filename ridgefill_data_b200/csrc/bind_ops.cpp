@@ -93,7 +93,7 @@ void embed_gather(Tensor table, Tensor ids, Tensor out) {
 
 void flash_attention(Tensor q, int64_t q_head_stride, Tensor k, Tensor v, int64_t kv_head_stride, Tensor out,
                      int64_t hq, int64_t hkv, int64_t hd, int64_t nq, int64_t nk, OptT qpos, int64_t q_start,
-                     double scale, OptT gate, int64_t gate_row, int64_t gate_head) {
+                     double scale, OptT gate, int64_t gate_row, int64_t gate_head, int64_t impl, Tensor err) {
   need(q, at::kBFloat16, "q");
   need(k, at::kBFloat16, "k");
   need(v, at::kBFloat16, "v");
@@ -127,6 +127,8 @@ void flash_attention(Tensor q, int64_t q_head_stride, Tensor k, Tensor v, int64_
   }
   a.out = bf(out);
   a.out_row = out.stride(0);
+  a.err = err.data_ptr<int>();
+  a.impl = (int)impl;
   rf::flash_attention(a, cur());
 }
 

@@ -60,8 +60,11 @@ struct AttnArgs {
   long gate_row, gate_head;
   __nv_bfloat16* out;          // [nq, hq * hd] (row pitch out_row)
   long out_row;
+  int* err;                    // bounded-wait error word (tcgen05 path)
+  int impl;                    // 0 auto (tcgen05 when possible), 1 mma.sync kernel, 2 tcgen05 only
 };
 void flash_attention(const AttnArgs& a, cudaStream_t stream);
+bool flash_attention_tc(const AttnArgs& a, cudaStream_t stream);
 
 // ---- gdn.cu
 struct GdnPrepArgs {

@@ -52,14 +52,18 @@ def embed(table, ids):
     return out
 
 
-def attention(q, k_cache, v_cache, nk, scale, out, q_start=0, qpos=None, gate=None, gate_head=0):
+ATTN_IMPL = {"auto": 0, "mma": 1, "tcgen05": 2}
+
+
+def attention(q, k_cache, v_cache, nk, scale, out, q_start=0, qpos=None, gate=None, gate_head=0, impl="auto"):
     """Causal GQA attention. q [hq, nq, hd] (any head pitch, row pitch hd); k_cache/v_cache [hkv, cap, hd]
     (the first nk rows valid); queries at positions q_start + row (or qpos int32 [nq]); out [nq, hq * hd];
     gate: a [nq, *] view whose head h starts at column h * gate_head (o * sigmoid(gate))."""
     hq, nq, hd = q.shape
     hkv = k_cache.shape[0]
     ext().flash_attention(q, q.stride(0), k_cache, v_cache, k_cache.stride(0), out, hq, hkv, hd, nq, nk, qpos,
-                          q_start, float(scale), gate, gate.stride(0) if gate is not None else 0, gate_head)
+                          q_start, float(scale), gate, gate.stride(0) if gate is not None else 0, gate_head,
+                          ATTN_IMPL[impl], ext().error_word(q.device.index or 0))
     return out
 
 

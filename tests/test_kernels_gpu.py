@@ -45,22 +45,30 @@ def test_head_norm_rope(hd, rot, mode):
     assert _rel(dst, ref) < 1e-2
 
 
+@pytest.mark.parametrize("impl", ["mma", "auto"])
 @pytest.mark.parametrize("hd,hq,hkv,nq,nk,gated", [(128, 8, 2, 300, 300, False), (256, 6, 1, 200, 700, True),
-                                                    (64, 4, 4, 1, 513, False), (128, 4, 1, 130, 130, True)])
-def test_flash_attention(hd, hq, hkv, nq, nk, gated):
+                                                    (64, 4, 4, 1, 513, False), (128, 4, 1, 130, 130, True),
+                                                    (256, 3, 1, 1000, 1000, True), (128, 4, 2, 64, 2000, False),
+                                                    (256, 2, 2, 129, 4100, False)])
+def test_flash_attention(hd, hq, hkv, nq, nk, gated, impl):
     torch.manual_seed(2)
     q = torch.randn(hq, nq, hd, device=dev).bfloat16()
     k = torch.randn(hkv, nk + 64, hd, device=dev).bfloat16()
     v = torch.randn(hkv, nk + 64, hd, device=dev).bfloat16()
     gate = torch.randn(nq, hq * 2 * hd, device=dev).bfloat16()
     out = torch.empty(nq, hq * hd, device=dev, dtype=torch.bfloat16)
+    k[:, nk:] = float("nan")           # rows past nk must never be read into the result
+    v[:, nk:] = float("nan")
     K.attention(q, k, v, nk, hd ** -0.5, out, q_start=nk - nq, gate=gate[:, hd:] if gated else None,
-                gate_head=2 * hd)
+                gate_head=2 * hd, impl=impl)
     ref = O.attend(q, k[:, :nk], v[:, :nk], hd ** -0.5)
     if gated:
         g = gate.view(nq, hq, 2 * hd)[..., hd:].reshape(nq, -1)
         ref = ref * torch.sigmoid(g)
     assert _rel(out, ref) < 2e-2
+    from ridgefill_data_b200.ops._ext import check_errors
+    torch.cuda.synchronize()
+    check_errors()
 
 
 def test_flash_attention_qpos():
