@@ -304,8 +304,10 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_holder;
 
   auto decode = [&](int t, int& e, int& row0, int& rows, int& nb) {
-    nb = t / total_mt;
-    const int g = t % total_mt;
+    // N tiles innermost: the num_nb CTAs of one row tile run together (A read from DRAM once, then L2), and an
+    // expert's few row tiles sit num_nb apart (its weight tiles shared through L2 as well)
+    const int g = t / num_nb;
+    nb = t % num_nb;
     e = find_expert(args.tile_start, args.E, g);
     row0 = args.seg_start[e] + (g - args.tile_start[e]) * GBM;
     rows = min(GBM, args.seg_start[e + 1] - row0);
