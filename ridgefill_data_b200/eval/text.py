@@ -1,0 +1,323 @@
+"""Text prompt sets re-tokenised per model (code/kva/data.py): tokenizer helpers, the copy / novel-token masks,
+chat-template pieces, the graded prompts, the K20 needle-in-a-haystack generator, end-of-sequence ids and the
+calibration document lists.
+
+Data files live under a data root (RF_DATA, default <repo>/data):
+  inputs/plan-grade.json, plan-train.json, plan-held.json, plan-sterm.json, swap_summary.json   prompt plans
+  corpus/<source>.txt                                                                      NIAH haystack texts
+  calibration-exclude.json                                                                 {list: [doc names]}
+None of them ship with the framework; every function that needs one names the missing file.
+
+Kept alike on purpose, so results compare with the reference's: the masks' token-id rule, the chat-template
+split, the capping rule (drop from the left after the BOS), and the K20 generator's seeded draws (one
+random.Random(20260930) stream over lengths x sources x depths, haystack start, key and 7-digit value).
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import random
+import re
+from pathlib import Path
+
+from ..utils import paths
+
+MAX_LEN = 32768
+SCORED = 512
+COPY_SPAN = 8
+
+
+def data_root():
+    return paths.DATA
+
+
+def inputs_dir():
+    return data_root() / "inputs"
+
+
+def _need(path):
+    path = Path(path)
+    if not path.exists():
+        raise FileNotFoundError(f"{path}: data file missing (set RF_DATA to the data root)")
+    return path
+
+
+# ------------------------------------------------------------------------------------- tokenizer helpers
+
+def tokenizer(model_path):
+    from transformers import AutoTokenizer
+    return AutoTokenizer.from_pretrained(str(model_path))
+
+
+def bos_ids(tok):
+    """[BOS] when the tokenizer's default encoding starts with one (Llama), else [] (Qwen)."""
+    ids = tok("a").input_ids
+    return ids[:1] if tok.bos_token_id is not None and ids and ids[0] == tok.bos_token_id else []
+
+
+def encode(tok, text):
+    return list(tok(text, add_special_tokens=False).input_ids)
+
+
+def cap(ids, head, max_len=MAX_LEN):
+    """At most max_len ids: drop from the left, after the `head` ids, so the scored end survives."""
+    if len(ids) <= max_len:
+        return ids
+    return head + ids[len(ids) - (max_len - len(head)):]
+
+
+def copy_mask(ids, span=COPY_SPAN):
+    """True at every token inside a window of `span` ids that already occurred verbatim starting at an earlier
+    position (a window's first occurrence is not marked; overlapping repeats mark the union)."""
+    seen = {}
+    mask = [False] * len(ids)
+    for s in range(len(ids) - span + 1):
+        w = tuple(ids[s:s + span])
+        if w in seen:
+            mask[s:s + span] = [True] * span
+        else:
+            seen[w] = s
+    return mask
+
+
+def novel_mask(ids, scored, span=COPY_SPAN):
+    """Novel-token mask of the last `scored` ids: a token is novel unless copy_mask marks it (a token-id rule)."""
+    return [not m for m in copy_mask(ids, span)[-scored:]]
+
+
+def chat_pieces(tok):
+    """(user-turn open ids, assistant-turn open ids) of the model's chat template around one user message, with
+    thinking off where the template has the switch."""
+    mark = "\x00DOC\x00"
+    rendered = tok.apply_chat_template([{"role": "user", "content": mark}], tokenize=False,
+                                       add_generation_prompt=True, enable_thinking=False)
+    pre, post = rendered.split(mark)
+    return encode(tok, pre), encode(tok, post)
+
+
+def eos_ids(model_path, tok):
+    """The tokenizer's EOS plus every eos_token_id of generation_config.json / config.json (text_config too)."""
+    out = {tok.eos_token_id} if tok.eos_token_id is not None else set()
+    for name in ("generation_config.json", "config.json"):
+        f = Path(model_path) / name
+        if f.exists():
+            c = json.loads(f.read_text())
+            e = c.get("eos_token_id", c.get("text_config", {}).get("eos_token_id"))
+            out |= set(e) if isinstance(e, list) else ({e} if e is not None else set())
+    return out
+
+
+# ----------------------------------------------------------------------------------------- graded set
+CHAT_ASK = "\n\nContinue the text above from exactly where it stops."
+
+
+def grade_prompts(tok, fmt="raw", drop_bos=False, plan=None, helps=None):
+    """The graded prompts: scored on the last SCORED tokens, novel tokens primary.
+    raw: BOS + the text. chat: the text minus its last SCORED tokens plus CHAT_ASK as the user turn, then the
+    assistant header, then those SCORED tokens as the reply (joined as ids, so the scored ids equal raw's).
+    Capping drops from the left after the head. drop_bos: the same prompts without their (required) BOS.
+    plan / helps default to inputs/plan-grade.json and inputs/swap_summary.json."""
+    if plan is None:
+        plan = json.loads(_need(inputs_dir() / "plan-grade.json").read_text())
+    if helps is None:
+        f = inputs_dir() / "swap_summary.json"
+        helps = {r["name"]: r["helps"] for r in json.loads(f.read_text())["rows"]} if f.exists() else {}
+    bos = bos_ids(tok)
+    if fmt == "raw":
+        head = bos
+
+        def build(text):
+            return bos + encode(tok, text)
+    elif fmt == "chat":
+        head, reply_open = chat_pieces(tok)
+        ask = encode(tok, CHAT_ASK)
+
+        def build(text):
+            doc = encode(tok, text)
+            return head + doc[:-SCORED] + ask + reply_open + doc[-SCORED:]
+    else:
+        raise ValueError(f"unknown grade format {fmt!r}")
+    out = []
+    for p in plan:
+        full = build(p["text"])
+        ids = cap(full, head)
+        short = build(p["text"][p["short_start"]:])
+        rec = dict(name=p["name"], kind=p["kind"], ids=ids, full_len=len(full), truncated=len(full) > len(ids),
+                   short_ids=short, short_tail_match=short[-SCORED:] == ids[-SCORED:],
+                   novel=novel_mask(ids[1:], SCORED), helps16=helps.get(p["name"]), format=fmt)
+        if drop_bos:
+            if not bos or ids[0] != bos[0] or short[0] != bos[0]:
+                raise ValueError(f"drop_bos: prompt {p['name']} does not start with a BOS")
+            rec.update(ids=ids[1:], short_ids=short[1:], bos_dropped=True)
+        out.append(rec)
+    return out
+
+
+# ------------------------------------------------------------------------------------------ K20 NIAH
+NIAH_LENGTHS = (8704, 16384, 32768)
+NIAH_DEPTHS = (0.1, 0.3, 0.5, 0.7, 0.9)
+NIAH_SOURCES = ("prose", "docs", "code", "rust")
+NIAH_SEED = 20260930
+NIAH_KEYS = ("amber-falcon", "quiet-harbor", "silver-lantern", "crimson-meadow", "paper-comet", "iron-willow",
+             "velvet-canyon", "frozen-orchid", "hollow-summit", "golden-reef", "misty-anchor", "rapid-thistle")
+CHARS_PER_TOKEN = 7
+
+
+def corpus(root=None):
+    """{source: text} from <data root>/corpus/*.txt."""
+    root = Path(root) if root is not None else data_root() / "corpus"
+    return {p.stem: p.read_text() for p in sorted(root.glob("*.txt"))}
+
+
+def k20_cells(text_of, lengths=NIAH_LENGTHS, sources=NIAH_SOURCES):
+    """Per (length, source) cell: the haystack's character range and, per depth, (depth, key, value): one seeded
+    stream of draws, in the generator's order."""
+    rng = random.Random(NIAH_SEED)
+    cells = []
+    for L in lengths:
+        for si, src in enumerate(sources):
+            span = L * CHARS_PER_TOKEN
+            start = max(0, len(text_of[src]) - span - si * 1000 - rng.randrange(20000))
+            needles = [(d, rng.choice(NIAH_KEYS), str(rng.randrange(1_000_000, 10_000_000))) for d in NIAH_DEPTHS]
+            cells.append(dict(length=L, source=src, char_start=start, char_end=start + span, needles=needles))
+    return cells
+
+
+def niah_question(fmt, key):
+    if fmt == "chat":
+        return (f"\n\nWhat is the special magic number for {key} mentioned in the text above? "
+                f"Answer with the 7-digit number only.")
+    return (f"\n\nWhat is the special magic number for {key} mentioned in the text above? "
+            f"The special magic number for {key} is")
+
+
+def niah_needle(key, value):
+    return f"\nThe special magic number for {key} is {value}.\n"
+
+
+def _frame(tok, fmt):
+    """(head ids, tail ids) around a NIAH body: raw BOS / nothing; chat the template's user and assistant opens."""
+    if fmt == "chat":
+        mark = "\x00NIAH\x00"
+        pre, post = tok.apply_chat_template([{"role": "user", "content": mark}], tokenize=False,
+                                            add_generation_prompt=True).split(mark)
+        return encode(tok, pre), encode(tok, post)
+    return bos_ids(tok), []
+
+
+def niah_prompts(tok, fmt="raw", variant=None, text_of=None, lengths=NIAH_LENGTHS, sources=NIAH_SOURCES):
+    """K20 prompts: haystack tokens, the needle sentence (encoded alone) spliced at int(depth * len(body)), the
+    question at the end (raw: ending in 'The special magic number for KEY is'; chat: the user turn with an
+    answer-format instruction, then the assistant header). variant 'mk4': plus 3 distractor needles (other keys
+    and values) at 3 of the other depths, drawn from a per-prompt RNG so the target is unchanged."""
+    text_of = corpus() if text_of is None else text_of
+    head, tail = _frame(tok, fmt)
+    out = []
+    for c in k20_cells(text_of, lengths, sources):
+        L, src = c["length"], c["source"]
+        hay = encode(tok, text_of[src][c["char_start"]:c["char_end"]])
+        if len(hay) < L:
+            raise RuntimeError(f"NIAH haystack {src}: {len(hay)} tokens < {L}")
+        for d, key, value in c["needles"]:
+            name = f"niah-{L}-{src}-{int(d * 100)}"
+            placed = [(d, key, value, True)]
+            if variant == "mk4":
+                r2 = random.Random(f"{name}-mk4")
+                keys = r2.sample([k for k in NIAH_KEYS if k != key], 3)
+                depths = r2.sample([x for x in NIAH_DEPTHS if x != d], 3)
+                placed += [(dd, kk, str(r2.randrange(1_000_000, 10_000_000)), False) for dd, kk in zip(depths, keys)]
+            elif variant is not None:
+                raise ValueError(f"unknown NIAH variant {variant!r}")
+            coded = sorted(((dd, encode(tok, niah_needle(kk, vv)), tgt) for dd, kk, vv, tgt in placed),
+                           key=lambda x: x[0])
+            q = encode(tok, niah_question(fmt, key))
+            body = hay[:L - sum(len(n) for _, n, _ in coded) - len(q)]
+            ids, prev = list(head), 0
+            start = end = None
+            for dd, n, tgt in coded:
+                at = int(dd * len(body))
+                ids += body[prev:at]
+                if tgt:
+                    start, end = len(ids), len(ids) + len(n)
+                ids += n
+                prev = at
+            ids += body[prev:] + q + tail
+            rec = dict(name=name, length=L, source=src, depth=d, key=key, value=value, format=fmt,
+                       char_start=c["char_start"], char_end=c["char_end"], needle_start=start, needle_end=end, ids=ids)
+            if variant:
+                rec.update(variant=variant, distractors=[dict(depth=dd, key=kk, value=vv)
+                                                         for dd, kk, vv, tgt in placed if not tgt])
+            out.append(rec)
+    return out
+
+
+def niah_correct(text, value):
+    """The first standalone 7-digit number, after dropping any think block, equals the value."""
+    text = re.sub(r"<think>.*?(</think>|$)", "", text, flags=re.S)
+    m = re.search(r"(?<!\d)\d{7}(?!\d)", text)
+    return bool(m and m.group(0) == value)
+
+
+# ---------------------------------------------------------------------------------- calibration sets
+# held documents left out of lambda selection, by the sha256 of their (non-public) name
+HELD_EXCLUDE_SHA256 = {"84f57b5fa277a7ed4af11992762af87605d6b02b1d71b0589743ac4a29d9c73d"}
+
+
+def name_sha256(name):
+    return hashlib.sha256(name.encode()).hexdigest()
+
+
+def calib_exclude(which, path=None):
+    """Names excluded from the 'train' / 'held' / 'sterm' list (calibration-exclude.json; required)."""
+    path = _need(path or data_root() / "calibration-exclude.json")
+    return set(json.loads(path.read_text()).get(which, []))
+
+
+def calib_docs(which):
+    """[{name, text}]: train = plan-train's 'calib' documents; held = plan-held's documents of >= 1024 tokens;
+    sterm = plan-sterm's; minus the exclusion list (and the held hash list)."""
+    ex = calib_exclude(which)
+    if which == "train":
+        rows = json.loads(_need(inputs_dir() / "plan-train.json").read_text())
+        keep = [x for x in rows if x["kind"] == "calib"]
+    elif which == "held":
+        rows = json.loads(_need(inputs_dir() / "plan-held.json").read_text())
+        keep = [x for x in rows if x["tokens"] >= 1024 and name_sha256(x["name"]) not in HELD_EXCLUDE_SHA256]
+    elif which == "sterm":
+        keep = json.loads(_need(inputs_dir() / "plan-sterm.json").read_text())
+    else:
+        raise ValueError(which)
+    return [dict(name=x["name"], text=x["text"]) for x in keep if x["name"] not in ex]
+
+
+def calib_ids(tok, which, limit=None):
+    bos = bos_ids(tok)
+    docs = calib_docs(which)[:limit] if limit else calib_docs(which)
+    return [dict(name=d["name"], ids=cap(bos + encode(tok, d["text"]), bos)) for d in docs]
+
+
+GRAM = 50
+
+
+def grams(ids, n=GRAM):
+    return {tuple(ids[i:i + n]) for i in range(len(ids) - n + 1)}
+
+
+def adapt_docs(tok, slices, eval_prompts):
+    """Adaptation documents: corpus slices {source: [(start, end)]} kept only when they share no token 50-gram
+    with any evaluation prompt's ids. Returns (docs, dropped names)."""
+    text_of = corpus()
+    bos = bos_ids(tok)
+    taken = set()
+    for p in eval_prompts:
+        taken |= grams(p["ids"])
+    docs, dropped = [], []
+    for src, spans in slices.items():
+        for s, e in spans:
+            ids = bos + encode(tok, text_of[src][s:e])
+            name = f"adapt-{src}-{s}"
+            if grams(ids) & taken:
+                dropped.append(name)
+            else:
+                docs.append(dict(name=name, source=f"corpus/{src}.txt[{s}:{e}]", ids=ids))
+    return docs, dropped
