@@ -414,6 +414,34 @@ void moe_combine_b(c10::optional<Tensor> h_opt, Tensor y, Tensor pos, Tensor w, 
                   cur());
 }
 
+void score_rows_b(Tensor logits, c10::optional<Tensor> ref, c10::optional<Tensor> targets, Tensor logprob, Tensor lse,
+                  Tensor argmax, Tensor ref_argmax, Tensor kl) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == torch::kFloat32 && logits.dim() == 2 && logits.stride(1) == 1,
+              "score_rows: fp32 [rows, V] logits with unit column stride");
+  const int rows = (int)logits.size(0), V = (int)logits.size(1);
+  rf::ScoreArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.ld = logits.stride(0);
+  a.rows = rows;
+  a.V = V;
+  if (ref.has_value()) {
+    TORCH_CHECK(ref->scalar_type() == torch::kFloat32 && ref->size(0) == rows && ref->size(1) == V && ref->stride(1) == 1,
+                "score_rows: ref must match logits");
+    a.ref = ref->data_ptr<float>();
+    a.ld_ref = ref->stride(0);
+    a.kl = kl.data_ptr<double>();
+    a.ref_argmax = ref_argmax.data_ptr<int>();
+  }
+  if (targets.has_value()) {
+    TORCH_CHECK(targets->scalar_type() == torch::kInt64 && targets->numel() == rows, "score_rows: int64 targets [rows]");
+    a.targets = targets->data_ptr<int64_t>();
+    a.logprob = logprob.data_ptr<double>();
+  }
+  a.lse = lse.data_ptr<double>();
+  a.argmax = argmax.data_ptr<int>();
+  rf::score_rows(a, at::cuda::getCurrentCUDAStream());
+}
+
 void cholesky_solve_b(Tensor a, Tensor b, double shift, Tensor err) {
   need(a, at::kDouble, "a");
   need(b, at::kDouble, "b");
@@ -426,6 +454,7 @@ void cholesky_solve_b(Tensor a, Tensor b, double shift, Tensor err) {
 
 void register_comm(pybind11::module_& m) {
   m.def("cholesky_solve", &cholesky_solve_b);
+  m.def("score_rows", &score_rows_b);
   m.def("router_topk", &router_topk_b);
   m.def("moe_align", &moe_align_b);
   m.def("grouped_gemm", &grouped_gemm_b);

@@ -119,6 +119,22 @@ void moe_combine(const __nv_bfloat16* h, long ldh, const __nv_bfloat16* y, const
 // ---- linalg.cu
 void cholesky_solve(double* a, int n, long lda, double shift, double* b, long ldb, int R, int* err, cudaStream_t s);
 
+// vocabulary reductions of fp32 logits rows: lse (fp64), argmax, target log-prob, KL(ref || logits)
+struct ScoreArgs {
+  const float* logits;
+  long ld;
+  int rows, V;
+  const float* ref;       // optional reference rows (KL, reference argmax)
+  long ld_ref;
+  const long* targets;    // optional [rows]
+  double* logprob;        // [rows] (with targets)
+  double* lse;            // optional [rows]
+  int* argmax;            // optional [rows]
+  int* ref_argmax;        // optional [rows]
+  double* kl;             // optional [rows] (with ref)
+};
+void score_rows(const ScoreArgs& a, cudaStream_t stream);
+
 // ---- comm.cu (peer-memory collectives; pointers are CUDA IPC mappings of the peers' buffers)
 constexpr int kMaxRanks = 8;
 

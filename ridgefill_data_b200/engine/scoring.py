@@ -15,10 +15,18 @@ def check_finite(logits, where):
     return logits
 
 
+def _device_scorer(*tensors):
+    """The sm_100a vocabulary-reduction kernel applies when every tensor is on a CUDA device."""
+    return all(t.is_cuda for t in tensors)
+
+
 def score_tokens(logits, ids, keep_targets):
-    """Log-probs of the last keep_targets prompt tokens; logits = the last keep_targets + 1 rows."""
-    lp = torch.log_softmax(logits[:-1].float(), -1)
-    tgt = ids[-keep_targets:].to(lp.device)
+    """Log-probs (fp64) of the last keep_targets prompt tokens; logits = the last keep_targets + 1 rows."""
+    tgt = ids[-keep_targets:].to(logits.device)
+    if _device_scorer(logits):
+        from ..ops.kernels import score_rows
+        return score_rows(logits[:-1], targets=tgt)["logprob"].cpu()
+    lp = torch.log_softmax(logits[:-1].double(), -1)
     return lp.gather(1, tgt[:, None])[:, 0].cpu()
 
 
@@ -27,7 +35,10 @@ def mean_nll(logits, ids, keep_targets):
 
 
 def kl(p_logits, q_logits):
-    """KL(p || q) per row, fp64 log-softmax."""
+    """KL(p || q) per row, fp64 log-softmax (the device kernel on CUDA)."""
+    if _device_scorer(p_logits, q_logits):
+        from ..ops.kernels import score_rows
+        return score_rows(q_logits, ref=p_logits)["kl"]
     lp = torch.log_softmax(p_logits.double(), -1)
     lq = torch.log_softmax(q_logits.double(), -1)
     return (lp.exp() * (lp - lq)).sum(-1)

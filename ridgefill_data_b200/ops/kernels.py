@@ -99,3 +99,24 @@ def gdn_scan(q, k, v, beta, g, state, out=None):
     err = ext().error_word(k.device.index or 0)
     ext().gdn_chunk_scan(q, k, v, beta, g, state, out, w_buf, u_buf, s_buf, vt_buf, n, nk, nv, dk, dv, err)
     return out
+
+
+def score_rows(logits, targets=None, ref=None):
+    """Vocabulary reductions of fp32 logits rows [rows, V] on the device (csrc/score.cu): dict(lse fp64, argmax
+    int32, logprob fp64 of `targets` (int64 [rows]) when given, and with `ref` (the reference arm's logits of
+    the same rows) kl = KL(ref || logits) fp64 and ref_argmax)."""
+    logits = logits.float().contiguous()
+    rows = logits.shape[0]
+    dev = logits.device
+    f64 = dict(dtype=torch.float64, device=dev)
+    i32 = dict(dtype=torch.int32, device=dev)
+    out = dict(lse=torch.empty(rows, **f64), argmax=torch.empty(rows, **i32),
+               logprob=torch.empty(rows, **f64), kl=torch.empty(rows, **f64), ref_argmax=torch.empty(rows, **i32))
+    tg = None if targets is None else targets.to(dev, torch.int64).contiguous()
+    rf = None if ref is None else ref.float().contiguous()
+    ext().score_rows(logits, rf, tg, out["logprob"], out["lse"], out["argmax"], out["ref_argmax"], out["kl"])
+    if targets is None:
+        del out["logprob"]
+    if ref is None:
+        del out["kl"], out["ref_argmax"]
+    return out

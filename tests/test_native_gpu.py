@@ -1,0 +1,62 @@
+"""Native checks on the GPU: the standalone identity-fill program (no Python inside) and the device scorer
+(log-sum-exp, argmax, target log-probs, KL) against an fp64 torch reference; the fill debug tap through a
+B200 prefill (identity fill bitwise, ridge maps within bf16 rounding)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def test_identity_check_program():
+    from ridgefill_data_b200.native import build_native, run
+    build_native(["identity_check"])
+    code, out = run("identity_check", 777, 1024)
+    assert code == 0, out
+    assert '"mismatches": 0' in out
+
+
+def test_score_rows_matches_fp64():
+    from ridgefill_data_b200.ops.kernels import score_rows
+    g = torch.Generator(device="cuda").manual_seed(0)
+    rows, V = 7, 248320
+    x = torch.randn(rows, V, device="cuda", generator=g) * 3
+    q = x + 0.3 * torch.randn(rows, V, device="cuda", generator=g)
+    x[2, 17] = x[2].max() + 1          # a clear argmax
+    x[3, 5] = x[3, 9] = x[3].max() + 2  # a tie: the lower index wins
+    t = torch.randint(0, V, (rows,), device="cuda", generator=g)
+    out = score_rows(x, targets=t, ref=q)
+    lp = torch.log_softmax(x.double(), -1)
+    lq = torch.log_softmax(q.double(), -1)
+    torch.testing.assert_close(out["lse"], torch.logsumexp(x.double(), -1), rtol=0, atol=1e-9)
+    torch.testing.assert_close(out["logprob"], lp.gather(1, t[:, None])[:, 0], rtol=0, atol=1e-9)
+    torch.testing.assert_close(out["kl"], (lq.exp() * (lq - lp)).sum(-1), rtol=1e-9, atol=1e-10)
+    assert out["argmax"][2].item() == 17 and out["argmax"][3].item() == 5
+    assert torch.equal(out["ref_argmax"].long(), q.argmax(-1))
+
+
+def test_fill_tap_identity_and_maps():
+    from ridgefill_data_b200.engine.arm import Arm
+    from ridgefill_data_b200.engine.prefill import prefill, run_lower
+    from ridgefill_data_b200.engine.taps import FillTap, attached
+    from ridgefill_data_b200.models.base import from_config
+    from ridgefill_data_b200.models.config import PRESETS
+    from ridgefill_data_b200.ridge.projector import Projector
+    cfg = PRESETS["qwen3.8-27b"].replace(n_layers=8, layer_types=["gdn", "gdn", "gdn", "attn"] * 2, vocab=4096)
+    m = from_config(cfg, backend="b200", device="cuda")
+    ids = torch.randint(0, cfg.vocab, (1024,), generator=torch.Generator().manual_seed(1))
+    split = 4
+    hs, _ = run_lower(m, ids, [split])
+    tap = FillTap(rows=112)
+    with attached(m, tap):
+        prefill(m, ids, Arm("id", split=split, tail=512, fill="identity"), keep=1)
+    assert sorted(tap.got) == list(range(split, 8))
+    assert all(v == 0 for v in tap.check_identity(hs[split]).values())
+    gen = torch.Generator().manual_seed(2)
+    d = cfg.hidden
+    W = {i: (torch.eye(d) + 0.01 * torch.randn(d, d, generator=gen)).bfloat16() for i in range(split, 8)}
+    B = {i: (0.01 * torch.randn(d, generator=gen)).bfloat16() for i in range(split, 8)}
+    proj = Projector(split, W, B)
+    tap = FillTap(rows=112)
+    with attached(m, tap):
+        prefill(m, ids, Arm("rf", split=split, tail=512, fill="proj", projector=proj), keep=1)
+    assert max(tap.check_maps(hs[split], proj).values()) < 2e-2
