@@ -130,7 +130,7 @@ def main():
     ap.add_argument("--split", type=int)
     ap.add_argument("--exact", action="store_true", help="also time full (exact) prefill for the speedup")
     ap.add_argument("--parallel", default="tp", choices=("tp", "dp"))
-    ap.add_argument("--tp-comm", default="nccl", choices=("nccl", "fused"))
+    ap.add_argument("--tp-comm", default="nccl", choices=("nccl", "fused", "nvls"))
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -245,7 +245,7 @@ def main():
                     data="synthetic (seeded uniform prompt; random-init weights and ridge maps of the named shapes)",
                     config=dict(model=args.model, global_batch=1 if tp_mode else world, seq_len=args.seq,
                                 split=args.split, tail=args.tail,
-                                parallelism=(f"tp{world}" + ("" if args.tp_comm == "nccl" else "-fused")) if tp_mode
+                                parallelism=(f"tp{world}" + ("" if args.tp_comm == "nccl" else f"-{args.tp_comm}")) if tp_mode
                                 else f"dp{world}",
                                 l2="inputs larger than L2 (the weights, tens of GB, are streamed every step)"),
                     clocks=clocks, gpu_launches=int(launches),

@@ -442,6 +442,69 @@ void score_rows_b(Tensor logits, c10::optional<Tensor> ref, c10::optional<Tensor
   rf::score_rows(a, at::cuda::getCurrentCUDAStream());
 }
 
+rf::NvlsFlags nvls_flags_of(int64_t local, const std::vector<int64_t>& peers, int64_t rank) {
+  rf::NvlsFlags f{};
+  TORCH_CHECK(peers.size() >= 1 && peers.size() <= rf::kMaxRanksNvls, "nvls: 1..8 ranks");
+  f.local = reinterpret_cast<int*>(local);
+  f.world = (int)peers.size();
+  f.rank = (int)rank;
+  for (size_t i = 0; i < peers.size(); ++i) f.peer[i] = reinterpret_cast<int*>(peers[i]);
+  return f;
+}
+
+void nvls_allreduce_b(int64_t mc_in, int64_t mc_out, int64_t out_local, c10::optional<Tensor> dst, int64_t rows,
+                      int64_t d, int64_t row0, int64_t row1, int64_t flags_local, std::vector<int64_t> flag_peers,
+                      int64_t rank, int64_t slot_in, int64_t slot_out, int64_t epoch, int64_t counter, Tensor err) {
+  TORCH_CHECK(d % 8 == 0, "nvls_allreduce: d must be a multiple of 8");
+  rf::NvlsAllReduceArgs a{};
+  a.mc_in = reinterpret_cast<const void*>(mc_in);
+  a.mc_out = reinterpret_cast<void*>(mc_out);
+  a.out_local = reinterpret_cast<const __nv_bfloat16*>(out_local);
+  if (dst.has_value()) {
+    TORCH_CHECK(dst->is_contiguous() && dst->scalar_type() == torch::kBFloat16 && dst->numel() == rows * d,
+                "nvls_allreduce: dst must be a contiguous bf16 [rows, d] tensor");
+    a.dst = reinterpret_cast<__nv_bfloat16*>(dst->data_ptr());
+  }
+  a.rows = (int)rows;
+  a.d = (int)d;
+  a.row0 = (int)row0;
+  a.row1 = (int)row1;
+  a.f = nvls_flags_of(flags_local, flag_peers, rank);
+  a.slot_in = (int)slot_in;
+  a.slot_out = (int)slot_out;
+  a.epoch = (int)epoch;
+  a.counter = reinterpret_cast<int*>(counter);
+  a.err = err.data_ptr<int>();
+  rf::nvls_allreduce(a, cur());
+}
+
+void nvls_allgather_b(Tensor src, int64_t mc_out, int64_t d, int64_t col_off, int64_t flags_local,
+                      std::vector<int64_t> flag_peers, int64_t rank, int64_t slot, int64_t epoch, int64_t counter,
+                      Tensor err) {
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == torch::kBFloat16 && src.dim() == 2 && src.stride(1) == 1 &&
+                  src.size(1) % 8 == 0 && src.stride(0) % 8 == 0 && col_off % 8 == 0 && d % 8 == 0,
+              "nvls_allgather: bf16 [rows, cols] slice, 16-byte aligned rows and offsets");
+  rf::NvlsAllGatherArgs a{};
+  a.src = reinterpret_cast<const __nv_bfloat16*>(src.data_ptr());
+  a.ld_src = src.stride(0);
+  a.mc_out = reinterpret_cast<void*>(mc_out);
+  a.rows = (int)src.size(0);
+  a.cols = (int)src.size(1);
+  a.d = (int)d;
+  a.col_off = (int)col_off;
+  a.f = nvls_flags_of(flags_local, flag_peers, rank);
+  a.slot = (int)slot;
+  a.epoch = (int)epoch;
+  a.counter = reinterpret_cast<int*>(counter);
+  a.err = err.data_ptr<int>();
+  rf::nvls_allgather(a, cur());
+}
+
+void nvls_barrier_b(int64_t flags_local, std::vector<int64_t> flag_peers, int64_t rank, int64_t slot, int64_t epoch,
+                    Tensor err) {
+  rf::nvls_barrier(nvls_flags_of(flags_local, flag_peers, rank), (int)slot, (int)epoch, err.data_ptr<int>(), cur());
+}
+
 void cholesky_solve_b(Tensor a, Tensor b, double shift, Tensor err) {
   need(a, at::kDouble, "a");
   need(b, at::kDouble, "b");
@@ -455,6 +518,9 @@ void cholesky_solve_b(Tensor a, Tensor b, double shift, Tensor err) {
 void register_comm(pybind11::module_& m) {
   m.def("cholesky_solve", &cholesky_solve_b);
   m.def("score_rows", &score_rows_b);
+  m.def("nvls_allreduce", &nvls_allreduce_b);
+  m.def("nvls_allgather", &nvls_allgather_b);
+  m.def("nvls_barrier", &nvls_barrier_b);
   m.def("router_topk", &router_topk_b);
   m.def("moe_align", &moe_align_b);
   m.def("grouped_gemm", &grouped_gemm_b);

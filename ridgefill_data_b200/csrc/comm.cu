@@ -12,39 +12,13 @@
 // kernel returns without touching the data, so the host can raise instead of hanging the GPU.
 #include "kernels.h"
 #include "ptx.cuh"
+#include "comm.cuh"
 
 #include <cstring>
 #include <stdexcept>
 #include <string>
 
 namespace rf {
-
-constexpr uint64_t kCommWaitNs = 10000000000ull;   // 10 s
-
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ bool wait_value(const int* flag, int value, int* err) {
-  if (ld_acquire_sys(flag) == value) return true;
-  const uint64_t t0 = global_timer_ns();
-  uint32_t spins = 0;
-  while (true) {
-    if (ld_acquire_sys(flag) == value) return true;
-    if ((++spins & 63u) == 0u) {
-      if (global_timer_ns() - t0 > kCommWaitNs) {
-        record_error(err, kErrTimeoutPeer);
-        return false;
-      }
-      __nanosleep(200);
-    }
-  }
-}
 
 __global__ void signal_kernel(PeerFlags f, int slot, int value) {
   if (threadIdx.x == 0 && blockIdx.x == 0) {

@@ -135,6 +135,38 @@ struct ScoreArgs {
 };
 void score_rows(const ScoreArgs& a, cudaStream_t stream);
 
+// NVSwitch multicast collectives (nvls.cu). Flag words: slot * kMaxRanks + source rank, epoch-stamped.
+constexpr int kMaxRanksNvls = 8;
+struct NvlsFlags {
+  int* local;                 // this rank's flag array
+  int* peer[kMaxRanksNvls];   // every rank's flag array (unicast mappings, this rank's own included)
+  int world, rank;
+};
+struct NvlsAllReduceArgs {
+  const void* mc_in;                // multicast address of the partial rows (bf16 [rows][d])
+  void* mc_out;                     // multicast address of the output rows
+  const __nv_bfloat16* out_local;   // this rank's output buffer (unicast)
+  __nv_bfloat16* dst;               // fresh [rows][d] result (nullptr: leave it in the output buffer)
+  int rows, d, row0, row1;
+  NvlsFlags f;
+  int slot_in, slot_out, epoch;
+  int* counter;                     // local grid counter (zero between launches)
+  int* err;
+};
+struct NvlsAllGatherArgs {
+  const __nv_bfloat16* src;         // this rank's column slice [rows][cols], row pitch ld_src
+  long ld_src;
+  void* mc_out;                     // multicast address of the full [rows][d] buffer
+  int rows, cols, d, col_off;
+  NvlsFlags f;
+  int slot, epoch;
+  int* counter;
+  int* err;
+};
+void nvls_allreduce(const NvlsAllReduceArgs& a, cudaStream_t stream);
+void nvls_allgather(const NvlsAllGatherArgs& a, cudaStream_t stream);
+void nvls_barrier(const NvlsFlags& f, int slot, int epoch, int* err, cudaStream_t stream);
+
 // ---- comm.cu (peer-memory collectives; pointers are CUDA IPC mappings of the peers' buffers)
 constexpr int kMaxRanks = 8;
 

@@ -1,0 +1,140 @@
+"""Tensor-parallel collectives through NVSwitch multicast (csrc/nvls.cu), on symmetric buffers bound to one
+multicast object (allocated and exchanged with torch's symmetric-memory plumbing).
+
+NvlsRowParallel  h + sum_r y_r w_r^T: the tcgen05 GEMM writes this rank's partial (the residual added on rank 0)
+                 into its symmetric buffer; one kernel then barriers the ranks, reduces its own 1/N of the rows in
+                 the switch (multimem.ld_reduce, fp32 accumulation), multicasts the sums to every rank
+                 (multimem.st), barriers again and copies the full result into a fresh tensor.
+NvlsMapFill      the column-sharded ridge-map fill: this rank's slice x_l[:, cols_r] from the GEMM (bias epilogue)
+                 is multicast into every rank's copy of x_l (one store per 16 bytes, the switch fans it out), then a
+                 barrier; buffers alternate by layer parity.
+Every wait is bounded; a timeout sets the device error word (ops._ext.check_errors raises).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..ops import gemm as G
+from ..ops._ext import ext
+
+SLOT_AR_IN, SLOT_AR_OUT, SLOT_AG, SLOT_BAR = 0, 1, 2, 3
+COUNTER_AR, COUNTER_AG = 56, 57
+FLAG_WORDS = 64
+
+
+class NvlsUnavailable(RuntimeError):
+    """The GPUs or the driver offer no multicast objects (no NVSwitch multicast)."""
+
+
+def _group_name(group):
+    return (group if group is not None else dist.group.WORLD).group_name
+
+
+class _Symm:
+    """One symmetric allocation: local tensor, every rank's unicast pointer and the multicast pointer."""
+
+    def __init__(self, numel, dtype, group, need_multicast=True):
+        import torch.distributed._symmetric_memory as symm
+        name = _group_name(group)
+        try:
+            symm.enable_symm_mem_for_group(name)
+        except Exception:                                            # noqa: BLE001 (already enabled / not needed)
+            pass
+        self.t = symm.empty(numel, dtype=dtype, device=torch.device("cuda", torch.cuda.current_device()))
+        self.h = symm.rendezvous(self.t, name)
+        self.ptrs = [int(p) for p in self.h.buffer_ptrs]
+        self.mc = int(self.h.multicast_ptr)
+        if need_multicast and self.mc == 0:
+            raise NvlsUnavailable("symmetric memory has no multicast address (NVLS unsupported here)")
+
+
+class _NvlsBase:
+    def __init__(self, group):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.flags = _Symm(FLAG_WORDS, torch.int32, group, need_multicast=False)
+        self.flags.t.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        self.flag_local = self.flags.ptrs[self.rank]
+        self.epoch = 0
+        self.err = ext().error_word(torch.cuda.current_device())
+
+    def counter(self, idx):
+        return self.flag_local + 4 * idx
+
+    def close(self):
+        torch.cuda.synchronize()
+        self.flags = None
+
+
+class NvlsRowParallel(_NvlsBase):
+    def __init__(self, group=None):
+        super().__init__(group)
+        self.cap = 0
+        self.d = None
+        self.part = self.out = None
+
+    def _ensure(self, rows, d):
+        if rows <= self.cap and d == self.d:
+            return
+        cap = 1 << (max(rows, 1024) - 1).bit_length()
+        self.part = _Symm(cap * d, torch.bfloat16, self.group)
+        self.out = _Symm(cap * d, torch.bfloat16, self.group)
+        self.cap, self.d = cap, d
+
+    def allreduce_(self, rows, d, dst):
+        """Sum over ranks of this rank's partial rows (already in the symmetric partial buffer) into dst."""
+        self.epoch += 1
+        chunk = -(-rows // self.world)
+        r0, r1 = min(rows, self.rank * chunk), min(rows, (self.rank + 1) * chunk)
+        ext().nvls_allreduce(self.part.mc, self.out.mc, self.out.ptrs[self.rank], dst, rows, d, r0, r1,
+                             self.flag_local, self.flags.ptrs, self.rank, SLOT_AR_IN, SLOT_AR_OUT, self.epoch,
+                             self.counter(COUNTER_AR), self.err)
+        return dst
+
+    def partial_view(self, rows, d):
+        self._ensure(rows, d)
+        return self.part.t[:rows * d].view(rows, d)
+
+    def __call__(self, y, w, h):
+        rows, d = y.shape[0], w.shape[0]
+        part = self.partial_view(rows, d)
+        G.linear(y, w, residual=h if self.rank == 0 else None, out=part)
+        return self.allreduce_(rows, d, torch.empty(rows, d, dtype=torch.bfloat16, device=y.device))
+
+
+class NvlsMapFill(_NvlsBase):
+    def __init__(self, group=None):
+        super().__init__(group)
+        self.cap = 0
+        self.d = None
+        self.buf = None
+
+    def _ensure(self, rows, d):
+        if rows <= self.cap and d == self.d:
+            return
+        cap = 1 << (max(rows, 1024) - 1).bit_length()
+        self.buf = _Symm(2 * cap * d, torch.bfloat16, self.group)
+        self.cap, self.d = cap, d
+
+    def __call__(self, b, w_local, bias_local, d):
+        """Full x = b W^T + c [rows, d] on every rank from this rank's column slice (w_local [d / N, H])."""
+        P = b.shape[0]
+        self._ensure(P, d)
+        self.epoch += 1
+        par = self.epoch & 1
+        cols = w_local.shape[0]
+        part = G.linear(b, w_local, bias=bias_local)
+        off = par * self.cap * d
+        ext().nvls_allgather(part, self.buf.mc + 2 * off, d, self.rank * cols, self.flag_local, self.flags.ptrs,
+                             self.rank, SLOT_AG, self.epoch, self.counter(COUNTER_AG), self.err)
+        return self.buf.t[off:off + P * d].view(P, d)
+
+
+def nccl_allreduce_reference(x, group=None):
+    y = x.clone()
+    dist.all_reduce(y, group=group)
+    return y

@@ -17,6 +17,9 @@ map fill's column gather in late layers):
               baseline
   fused       parallel/fused.py: GEMM epilogues store their tiles straight into peer memory (partials into the row
               owner's receive slot; map columns into every rank's x_l), the owner reduces, every rank gathers
+  nvls        parallel/nvls.py: NVSwitch multicast: partials reduced in the switch (multimem.ld_reduce) and the sums
+              multicast to every rank (multimem.st) by one kernel with its own cross-rank barriers; map slices
+              multicast into every rank's x_l
 """
 from __future__ import annotations
 
@@ -38,6 +41,12 @@ class TensorParallel:
             from .fused import FusedMapFill, FusedRowParallel
             self.fused = FusedRowParallel(group)
             self.fused_fill = FusedMapFill(group)
+        elif mode == "nvls" and self.world > 1:
+            from .nvls import NvlsMapFill, NvlsRowParallel
+            self.fused = NvlsRowParallel(group)
+            self.fused_fill = NvlsMapFill(group)
+        elif mode not in ("nccl", "fused", "nvls"):
+            raise ValueError(f"TP communication mode {mode!r} (nccl | fused | nvls)")
 
     def row_parallel(self, y, w, h):
         """h + sum over ranks of y_r w_r^T (each rank holds its K-slice y_r, w_r)."""
