@@ -454,7 +454,8 @@ rf::NvlsFlags nvls_flags_of(int64_t local, const std::vector<int64_t>& peers, in
 
 void nvls_allreduce_b(int64_t mc_in, int64_t mc_out, int64_t out_local, c10::optional<Tensor> dst, int64_t rows,
                       int64_t d, int64_t row0, int64_t row1, int64_t flags_local, std::vector<int64_t> flag_peers,
-                      int64_t rank, int64_t slot_in, int64_t slot_out, int64_t epoch, int64_t counter, Tensor err) {
+                      int64_t rank, int64_t slot_in, int64_t slot_out, int64_t epoch, int64_t counter, Tensor err,
+                      int64_t max_ctas, bool acc32) {
   TORCH_CHECK(d % 8 == 0, "nvls_allreduce: d must be a multiple of 8");
   rf::NvlsAllReduceArgs a{};
   a.mc_in = reinterpret_cast<const void*>(mc_in);
@@ -475,6 +476,8 @@ void nvls_allreduce_b(int64_t mc_in, int64_t mc_out, int64_t out_local, c10::opt
   a.epoch = (int)epoch;
   a.counter = reinterpret_cast<int*>(counter);
   a.err = err.data_ptr<int>();
+  a.max_ctas = (int)max_ctas;
+  a.acc32 = acc32 ? 1 : 0;
   rf::nvls_allreduce(a, cur());
 }
 

@@ -152,6 +152,8 @@ struct NvlsAllReduceArgs {
   int slot_in, slot_out, epoch;
   int* counter;                     // local grid counter (zero between launches)
   int* err;
+  int max_ctas;                     // 0: one CTA per SM
+  int acc32;                        // accumulate in fp32 in the switch (else bf16)
 };
 struct NvlsAllGatherArgs {
   const __nv_bfloat16* src;         // this rank's column slice [rows][cols], row pitch ld_src

@@ -24,11 +24,18 @@ namespace rf {
 constexpr int kNvlsThreads = 512;
 constexpr int kNvlsUnroll = 4;
 
+template <bool ACC32>
 __device__ __forceinline__ void mm_ld_reduce_bf16x8(const void* mc, uint4& v) {
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(mc)
-               : "memory");
+  if constexpr (ACC32)
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(mc)
+                 : "memory");
+  else
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(mc)
+                 : "memory");
 }
 __device__ __forceinline__ void mm_st_16(void* mc, const uint4& v) {
   asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
@@ -67,6 +74,7 @@ __device__ void last_cta_arrive(const NvlsFlags& f, int slot, int epoch, int* co
   }
 }
 
+template <bool ACC32>
 __global__ void __launch_bounds__(kNvlsThreads) nvls_allreduce_kernel(NvlsAllReduceArgs a) {
   __shared__ int s_ok;
   if (blockIdx.x == 0 && threadIdx.x == 0) arrive(a.f, a.slot_in, a.epoch);
@@ -83,7 +91,7 @@ __global__ void __launch_bounds__(kNvlsThreads) nvls_allreduce_kernel(NvlsAllRed
 #pragma unroll
       for (int k = 0; k < kNvlsUnroll; ++k) {
         const long u = u0 + k * stride;
-        if (u < n_units) mm_ld_reduce_bf16x8(in + (base + u) * 16, v[k]);
+        if (u < n_units) mm_ld_reduce_bf16x8<ACC32>(in + (base + u) * 16, v[k]);
       }
 #pragma unroll
       for (int k = 0; k < kNvlsUnroll; ++k) {
@@ -134,7 +142,12 @@ void nvls_allreduce(const NvlsAllReduceArgs& a, cudaStream_t stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   const long units = std::max((long)(a.row1 - a.row0) * (a.d / 8), (long)a.rows * (a.d / 8) / kNvlsUnroll);
-  nvls_allreduce_kernel<<<grid_for(units / kNvlsUnroll + 1, dev), kNvlsThreads, 0, stream>>>(a);
+  int grid = grid_for(units / kNvlsUnroll + 1, dev);
+  if (a.max_ctas > 0) grid = std::min(grid, a.max_ctas);
+  if (a.acc32)
+    nvls_allreduce_kernel<true><<<grid, kNvlsThreads, 0, stream>>>(a);
+  else
+    nvls_allreduce_kernel<false><<<grid, kNvlsThreads, 0, stream>>>(a);
   count_launch();
 }
 

@@ -33,13 +33,14 @@ def run_lower(model, ids, splits, hs_device=None, hook=None, mix=None):
     h = model.embed(ids)
     hs = {}
     top = max(splits)
+    stable = getattr(model, "stable", lambda t: t)
     for i in range(top):
         if i in splits:
-            hs[i] = h if hs_device is None else h.to(hs_device)
+            hs[i] = stable(h) if hs_device is None else h.to(hs_device)
         if hook is not None:
-            hook(i, h)
+            hook(i, stable(h))
         h = model.layer(i, h, pos, cache, mix=mix)
-    hs[top] = h if hs_device is None else h.to(hs_device)
+    hs[top] = stable(h) if hs_device is None else h.to(hs_device)
     return hs, cache
 
 
@@ -240,7 +241,7 @@ def finish(model, ids, h_split, lower_cache, arm, keep, oracle=None, keep_cache=
         if st is not None:
             cache[i]["rec"] = cache[i]["rec"] + st.to(cache[i]["rec"])
         if hook is not None:
-            hook(i, h)
+            hook(i, model.stable(h) if hasattr(model, "stable") else h)
         h = model.layer(i, h, pos[P:], cache)
         if not keep_cache:
             cache[i] = {}

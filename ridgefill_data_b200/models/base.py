@@ -146,6 +146,11 @@ class Model:
         cos, sin = ops.rope_cos_sin(self.inv_freq, pos, k.dtype)
         self._append_kv(cache[i], ops.apply_rope(k.transpose(0, 1), cos, sin), v.transpose(0, 1))
 
+    def stable(self, h):
+        """h itself, or a copy when h lives in a buffer that later layers reuse (tensor-parallel outputs)."""
+        tp = getattr(self, "tp", None)
+        return h.clone() if tp is not None and hasattr(tp, "owns") and tp.owns(h) else h
+
     def forward_exact(self, ids, hook=None, cache=None, keep=None, gdn_checkpoint_every=None, mix=None):
         """Exact forward over all rows. hook(i, h) sees each layer's input and hook('final', h) the
         final-norm input; mix(i, a) each layer's mixer output. keep: row indices whose logits to return."""
@@ -154,10 +159,10 @@ class Model:
         h = self.embed(ids)
         for i in range(self.n_layers):
             if hook is not None:
-                hook(i, h)
+                hook(i, self.stable(h))
             h = self.layer(i, h, pos, cache, gdn_checkpoint_every=gdn_checkpoint_every, mix=mix)
         if hook is not None:
-            hook("final", h)
+            hook("final", self.stable(h))
         out = self.logits(h[keep]) if keep is not None else None
         return out, cache
 

@@ -45,6 +45,7 @@ def main(argv=None):
     ap.add_argument("--rows", type=int, nargs="+", default=[16384, 4096])
     ap.add_argument("--d", type=int, default=5120)
     ap.add_argument("--k", type=int, default=3072, help="row-parallel GEMM K per rank (down_proj: 17408 / N)")
+    ap.add_argument("--sweep", action="store_true", help="all-reduce only: CTA count x switch accumulation sweep")
     a = ap.parse_args(argv)
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
@@ -56,6 +57,31 @@ def main(argv=None):
     rp, mf = NvlsRowParallel(), NvlsMapFill()
     out = []
     d = a.d
+    if a.sweep:
+        for rows in a.rows:
+            S = rows * d * 2
+            part = rp.partial_view(rows, d)
+            part.copy_(torch.randn(rows, d, device="cuda", generator=g).bfloat16())
+            dst = torch.empty(rows, d, dtype=torch.bfloat16, device="cuda")
+            for acc in (True, False):
+                for ctas in (16, 32, 64, 148):
+                    for copy in (False, True):
+                        rp.max_ctas, rp.acc32 = ctas, acc
+                        t = _time(lambda: rp.allreduce_(rows, d, dst if copy else None))
+                        out.append(dict(case="allreduce_sweep", rows=rows, world=world, acc32=acc, ctas=ctas,
+                                        copy=copy, ms=round(t, 4), frac_of_roofline=round(S / (LINK_GBS * 1e9) * 1e3 / t, 3)))
+            rp.max_ctas, rp.acc32 = 0, True
+            x = part.clone()
+            t = _time(lambda: dist.all_reduce(x))
+            out.append(dict(case="nccl_allreduce", rows=rows, world=world, ms=round(t, 4)))
+        if rank == 0:
+            for r in out:
+                print(json.dumps(r), flush=True)
+        rp.close()
+        mf.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     for rows in a.rows:
         S = rows * d * 2
         x = torch.randn(rows, d, device="cuda", generator=g).bfloat16()

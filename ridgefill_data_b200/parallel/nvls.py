@@ -4,7 +4,9 @@ multicast object (allocated and exchanged with torch's symmetric-memory plumbing
 NvlsRowParallel  h + sum_r y_r w_r^T: the tcgen05 GEMM writes this rank's partial (the residual added on rank 0)
                  into its symmetric buffer; one kernel then barriers the ranks, reduces its own 1/N of the rows in
                  the switch (multimem.ld_reduce, fp32 accumulation), multicasts the sums to every rank
-                 (multimem.st), barriers again and copies the full result into a fresh tensor.
+                 (multimem.st) and barriers again. The result is a view of one of OUT_BUFFERS rotating symmetric
+                 output buffers: valid until OUT_BUFFERS further reductions (the model's stable() clones a tensor
+                 that must live longer, e.g. the split state).
 NvlsMapFill      the column-sharded ridge-map fill: this rank's slice x_l[:, cols_r] from the GEMM (bias epilogue)
                  is multicast into every rank's copy of x_l (one store per 16 bytes, the switch fans it out), then a
                  barrier; buffers alternate by layer parity.
@@ -19,6 +21,7 @@ from ..ops import gemm as G
 from ..ops._ext import ext
 
 SLOT_AR_IN, SLOT_AR_OUT, SLOT_AG, SLOT_BAR = 0, 1, 2, 3
+OUT_BUFFERS = 4
 COUNTER_AR, COUNTER_AG = 56, 57
 FLAG_WORDS = 64
 
@@ -37,10 +40,6 @@ class _Symm:
     def __init__(self, numel, dtype, group, need_multicast=True):
         import torch.distributed._symmetric_memory as symm
         name = _group_name(group)
-        try:
-            symm.enable_symm_mem_for_group(name)
-        except Exception:                                            # noqa: BLE001 (already enabled / not needed)
-            pass
         self.t = symm.empty(numel, dtype=dtype, device=torch.device("cuda", torch.cuda.current_device()))
         self.h = symm.rendezvous(self.t, name)
         self.ptrs = [int(p) for p in self.h.buffer_ptrs]
@@ -71,29 +70,41 @@ class _NvlsBase:
 
 
 class NvlsRowParallel(_NvlsBase):
+    max_ctas = 32          # the all-reduce saturates the switch with 32 CTAs of 512 threads (measured at TP 2 / 8)
+    acc32 = True
+
     def __init__(self, group=None):
         super().__init__(group)
         self.cap = 0
         self.d = None
-        self.part = self.out = None
+        self.part = None
+        self.outs = []
+        self.turn = 0
 
     def _ensure(self, rows, d):
         if rows <= self.cap and d == self.d:
             return
         cap = 1 << (max(rows, 1024) - 1).bit_length()
         self.part = _Symm(cap * d, torch.bfloat16, self.group)
-        self.out = _Symm(cap * d, torch.bfloat16, self.group)
+        self.outs = [_Symm(cap * d, torch.bfloat16, self.group) for _ in range(OUT_BUFFERS)]
         self.cap, self.d = cap, d
 
-    def allreduce_(self, rows, d, dst):
-        """Sum over ranks of this rank's partial rows (already in the symmetric partial buffer) into dst."""
+    def owns(self, t):
+        base = t.untyped_storage().data_ptr()
+        return any(base == o.t.untyped_storage().data_ptr() for o in self.outs)
+
+    def allreduce_(self, rows, d, dst=None):
+        """Sum over ranks of this rank's partial rows (already in the symmetric partial buffer): into dst, or
+        (dst None) a view of the next rotating symmetric output buffer."""
         self.epoch += 1
         chunk = -(-rows // self.world)
         r0, r1 = min(rows, self.rank * chunk), min(rows, (self.rank + 1) * chunk)
-        ext().nvls_allreduce(self.part.mc, self.out.mc, self.out.ptrs[self.rank], dst, rows, d, r0, r1,
+        out = self.outs[self.turn]
+        self.turn = (self.turn + 1) % len(self.outs)
+        ext().nvls_allreduce(self.part.mc, out.mc, out.ptrs[self.rank], dst, rows, d, r0, r1,
                              self.flag_local, self.flags.ptrs, self.rank, SLOT_AR_IN, SLOT_AR_OUT, self.epoch,
-                             self.counter(COUNTER_AR), self.err)
-        return dst
+                             self.counter(COUNTER_AR), self.err, self.max_ctas, self.acc32)
+        return dst if dst is not None else out.t[:rows * d].view(rows, d)
 
     def partial_view(self, rows, d):
         self._ensure(rows, d)
@@ -103,7 +114,7 @@ class NvlsRowParallel(_NvlsBase):
         rows, d = y.shape[0], w.shape[0]
         part = self.partial_view(rows, d)
         G.linear(y, w, residual=h if self.rank == 0 else None, out=part)
-        return self.allreduce_(rows, d, torch.empty(rows, d, dtype=torch.bfloat16, device=y.device))
+        return self.allreduce_(rows, d)
 
 
 class NvlsMapFill(_NvlsBase):

@@ -72,6 +72,10 @@ class TensorParallel:
         dist.all_gather_into_tensor(out, part, group=self.group)
         return out.view(self.world, b.shape[0], c1 - c0).permute(1, 0, 2).reshape(b.shape[0], d)
 
+    def owns(self, t):
+        """True when t lives in a rotating communication buffer (reused a few layers later)."""
+        return self.fused is not None and hasattr(self.fused, "owns") and self.fused.owns(t)
+
     def close(self):
         for f in (self.fused, self.fused_fill):
             if f is not None:
