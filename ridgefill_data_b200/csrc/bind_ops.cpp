@@ -362,6 +362,53 @@ void gemm_peer_b(Tensor a, Tensor b, c10::optional<Tensor> bias, std::vector<int
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Row-parallel product fused with its all-reduce through NVSwitch multicast (kEpiNvlsAR): out_part is this
+// rank's symmetric partial buffer (unicast view), mc_part / mc_out the multicast addresses of the partial and
+// output buffers.
+void gemm_nvls_ar_b(Tensor a, Tensor b, c10::optional<Tensor> residual, Tensor out_part, int64_t mc_part,
+                    int64_t mc_out, int64_t flags_local, std::vector<int64_t> flag_peers, int64_t rank, int64_t epoch,
+                    Tensor counters, int64_t max_mb, int64_t bn, int64_t max_ctas, Tensor err) {
+  need(a, at::kBFloat16, "a");
+  need(b, at::kBFloat16, "b");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out_part.stride(1) == 1, "gemm_nvls_ar: unit inner stride");
+  TORCH_CHECK(flag_peers.size() >= 1 && flag_peers.size() <= rf::kMaxPeers, "gemm_nvls_ar: 1..8 ranks");
+  TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= max_mb + 1, "gemm_nvls_ar: counters");
+  c10::cuda::CUDAGuard g(a.device());
+  rf::GemmOperands op{a.data_ptr(), a.stride(0), false, b.data_ptr(), b.stride(0), false};
+  rf::GemmArgs args{};
+  args.M = (int)a.size(0);
+  args.K = (int)a.size(1);
+  args.N = (int)b.size(0);
+  TORCH_CHECK(b.size(1) == args.K && out_part.size(0) == args.M && out_part.size(1) == args.N, "gemm_nvls_ar: shapes");
+  TORCH_CHECK(args.N % 8 == 0 && out_part.stride(0) % 8 == 0, "gemm_nvls_ar: N and the row pitch must be multiples of 8");
+  TORCH_CHECK((args.M + 127) / 128 <= max_mb, "gemm_nvls_ar: more row blocks than the flag array holds");
+  args.k_splits = 1;
+  args.out = out_part.data_ptr();
+  args.ldo = out_part.stride(0);
+  if (residual.has_value()) {
+    need(*residual, at::kBFloat16, "residual");
+    TORCH_CHECK(residual->stride(1) == 1 && residual->size(0) == args.M && residual->size(1) == args.N,
+                "gemm_nvls_ar: residual [M, N]");
+    args.residual = cbf(*residual);
+    args.ldr = residual->stride(0);
+  }
+  args.vec_ok = (args.ldo % 8 == 0 && (!residual.has_value() || args.ldr % 8 == 0)) ? 1 : 0;
+  args.err = err.data_ptr<int>();
+  rf::NvlsGemmArgs& nv = args.nvls;
+  nv.mc_part = reinterpret_cast<const void*>(mc_part);
+  nv.mc_out = reinterpret_cast<void*>(mc_out);
+  nv.flags = reinterpret_cast<int*>(flags_local);
+  for (size_t i = 0; i < flag_peers.size(); ++i) nv.peer_flags[i] = reinterpret_cast<int*>(flag_peers[i]);
+  nv.world = (int)flag_peers.size();
+  nv.rank = (int)rank;
+  nv.epoch = (int)epoch;
+  nv.rb_count = counters.data_ptr<int>();
+  nv.done_count = counters.data_ptr<int>() + max_mb;
+  nv.max_mb = (int)max_mb;
+  rf::gemm_bf16(op, args, rf::kEpiNvlsAR, (int)bn, (int)max_ctas, cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace
 
 void router_topk_b(Tensor logits, int64_t E, int64_t k, Tensor idx, Tensor wts, bool norm) {
@@ -539,4 +586,5 @@ void register_comm(pybind11::module_& m) {
   m.def("comm_reduce_rows", &comm_reduce_rows_b);
   m.def("comm_gather_rows", &comm_gather_rows_b);
   m.def("gemm_peer", &gemm_peer_b);
+  m.def("gemm_nvls_ar", &gemm_nvls_ar_b);
 }

@@ -14,12 +14,18 @@
 // Epilogues: kEpiStore (bf16 out, optional bias[n] and residual[m, n]), kEpiSwiGLU (columns
 // [0, BN/2) of each tile are gate rows, [BN/2, BN) the matching up rows: out = silu(g) * u),
 // kEpiF32 (fp32 out), kEpiF64Acc (fp64 out += acc, split-K chunks added with atomics: the
-// fp32-per-block, fp64-across-blocks accumulation of the ridge sufficient statistics).
+// fp32-per-block, fp64-across-blocks accumulation of the ridge sufficient statistics), kEpiPeer (tiles
+// stored into other GPUs' buffers) and kEpiNvlsAR: the tensor-parallel row-parallel product fused with its
+// all-reduce. The CTA then has 8 warps: warps 6-7 (comm warps) reduce the row blocks this rank owns through the
+// NVSwitch (multimem.ld_reduce / multimem.st) as soon as every rank's epilogues have finished them, while the
+// other warps keep computing later tiles (tile order finishes row blocks in groups of 16).
 #include "gemm.h"
 #include "kernels.h"
 #include "ptx.cuh"
+#include "comm.cuh"
 
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 #include <stdexcept>
@@ -30,6 +36,11 @@ namespace rf {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kGemmThreads = 192;
+
+template <int EPI>
+struct GemmThreads {
+  static constexpr int value = EPI == kEpiNvlsAR ? 256 : kGemmThreads;
+};
 constexpr int kGroupM = 16;   // rasterisation: consecutive tiles walk 16 M-blocks per N-block
 
 template <int BN>
@@ -64,7 +75,7 @@ __device__ __forceinline__ TileCoord tile_coord(int t, int num_mb, int num_nb, i
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
 template <int BN, int EPI, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
@@ -78,6 +89,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  __shared__ int s_tile_warps[2];   // kEpiNvlsAR: epilogue warps done with the tile in accumulator buffer b
+  __shared__ int s_comm_ok;
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -95,6 +108,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tempty[b], 128);
     }
     *abort_flag = 0;
+    s_tile_warps[0] = s_tile_warps[1] = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -207,7 +221,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (lane == 0) umma_commit(&tfull[0]);
       __syncwarp();
     }
-  } else {
+  } else if (warp < 6) {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
@@ -268,7 +282,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int col0 = tc.nb * BN + c;
           if (!row_ok || col0 >= args.N) continue;
           const bool full_chunk = (col0 + 32 <= args.N);
-          if constexpr (EPI == kEpiStore) {
+          if constexpr (EPI == kEpiStore || EPI == kEpiNvlsAR) {
             __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col0;
             float v[32];
 #pragma unroll
@@ -372,8 +386,77 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
+      if constexpr (EPI == kEpiNvlsAR) {
+        // the fourth epilogue warp to finish this tile counts it for its row block; the block's last tile
+        // announces the block to every rank
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence();
+          if (atomicAdd(&s_tile_warps[buf], 1) == 3) {
+            atomicExch(&s_tile_warps[buf], 0);
+            const NvlsGemmArgs& nv = args.nvls;
+            if (atomicAdd(nv.rb_count + tc.mb, 1) == num_nb - 1) {
+              nv.rb_count[tc.mb] = 0;
+              __threadfence_system();
+              for (int q = 0; q < nv.world; ++q) st_release_sys(nv.peer_flags[q] + tc.mb * kMaxPeers + nv.rank, nv.epoch);
+            }
+          }
+        }
+      }
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
+    }
+  } else if constexpr (EPI == kEpiNvlsAR) {
+    // ------------------------------------------------------------------ comm warps (6..7)
+    const NvlsGemmArgs& nv = args.nvls;
+    const int ct = threadIdx.x - 6 * 32;
+    const int units_row = args.N / 8;
+    const char* in = reinterpret_cast<const char*>(nv.mc_part);
+    char* outp = reinterpret_cast<char*>(nv.mc_out);
+    bool ok = true;
+    for (int mb = nv.rank; mb < num_mb && ok; mb += nv.world) {
+      if (ct == 0) {
+        bool good = true;
+        for (int q = 0; q < nv.world && good; ++q) good = wait_value(nv.flags + mb * kMaxPeers + q, nv.epoch, args.err);
+        s_comm_ok = good ? 1 : 0;
+      }
+      named_bar_sync(1, 64);
+      ok = s_comm_ok != 0;
+      named_bar_sync(1, 64);
+      if (!ok) break;
+      const int r0 = mb * BM, r1 = min(args.M, r0 + BM);
+      const long n_units = (long)(r1 - r0) * units_row;
+      const long per = (n_units + gridDim.x - 1) / gridDim.x;
+      const long ub = (long)blockIdx.x * per, ue = min(n_units, ub + per);
+      for (long u0 = ub + ct; u0 < ue; u0 += 64 * 4) {
+        uint4 v[4];
+        long off[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const long u = u0 + k * 64;
+          off[k] = -1;
+          if (u < ue) {
+            const long r = r0 + u / units_row, c = (u % units_row) * 8;
+            off[k] = (r * args.ldo + c) * 2;
+            multimem_ld_reduce_bf16x8(in + off[k], v[k]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (off[k] >= 0) multimem_st_16(outp + off[k], v[k]);
+      }
+    }
+    // every CTA's sums are out: the last CTA announces this rank done; every CTA waits for all ranks
+    named_bar_sync(1, 64);
+    if (ct == 0) {
+      __threadfence_system();
+      const int done_off = nv.max_mb * kMaxPeers;
+      if (atomicAdd(nv.done_count, 1) == (int)gridDim.x - 1) {
+        *nv.done_count = 0;
+        for (int q = 0; q < nv.world; ++q) st_release_sys(nv.peer_flags[q] + done_off + nv.rank, nv.epoch);
+      }
+      bool good = true;
+      for (int q = 0; q < nv.world && good; ++q) good = wait_value(nv.flags + done_off + q, nv.epoch, args.err);
     }
   }
 
@@ -449,7 +532,11 @@ static void launch_gemm(const GemmOperands& op, GemmArgs args, int max_ctas, cud
   if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
   if (num_tiles < ctas) ctas = num_tiles;
   if (ctas <= 0) return;
-  kernel<<<ctas, kGemmThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, args);
+  if (EPI == kEpiNvlsAR && ctas != num_sms(dev) && num_tiles < num_sms(dev)) {
+    // every CTA takes part in the reduction: keep one CTA per SM even when there are fewer tiles
+    ctas = max_ctas > 0 ? std::min(max_ctas, num_sms(dev)) : num_sms(dev);
+  }
+  kernel<<<ctas, GemmThreads<EPI>::value, Cfg::SMEM_BYTES, stream>>>(ta, tb, args);
   count_launch();
 }
 
@@ -477,6 +564,8 @@ void gemm_bf16(const GemmOperands& op, GemmArgs args, int epi, int bn, int max_c
   RF_GEMM_CASE(256, kEpiStore, true, true)
   RF_GEMM_CASE(256, kEpiPeer, false, false)
   RF_GEMM_CASE(128, kEpiPeer, false, false)
+  RF_GEMM_CASE(256, kEpiNvlsAR, false, false)
+  RF_GEMM_CASE(128, kEpiNvlsAR, false, false)
 #undef RF_GEMM_CASE
   throw std::runtime_error("gemm_bf16: unsupported (bn, epilogue, majors) combination");
 }

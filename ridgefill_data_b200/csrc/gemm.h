@@ -7,7 +7,7 @@
 
 namespace rf {
 
-enum GemmEpilogue : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiF32 = 2, kEpiF64Acc = 3, kEpiPeer = 4 };
+enum GemmEpilogue : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiF32 = 2, kEpiF64Acc = 3, kEpiPeer = 4, kEpiNvlsAR = 5 };
 
 constexpr int kMaxPeers = 8;
 
@@ -24,6 +24,23 @@ struct PeerArgs {
   long slot_stride;
   long ld;
   long col_off;
+};
+
+// Fused all-reduce through NVSwitch multicast (kEpiNvlsAR): the epilogue stores this rank's partial tile into its
+// symmetric partial buffer (args.out, residual added when given) and counts finished tiles per 128-row block; the
+// last tile of a block announces it to every rank. Two extra warps per CTA (the comm warps) take the row blocks
+// this rank owns (mb % world == rank) as soon as every rank has announced them, reduce them in the switch
+// (multimem.ld_reduce) and multicast the sums (multimem.st) into every rank's output buffer; a final barrier
+// makes the whole result visible on every rank before the kernel ends.
+struct NvlsGemmArgs {
+  const void* mc_part;      // multicast address of the partial buffer (bf16 [M][ldo])
+  void* mc_out;             // multicast address of the output buffer
+  int* flags;               // this rank's flag words: [row block][rank] epochs, then done[rank]
+  int* peer_flags[kMaxPeers];
+  int world, rank, epoch;
+  int* rb_count;            // local per-row-block tile counters (zero between launches)
+  int* done_count;          // local CTA counter (zero between launches)
+  int max_mb;               // row blocks the flag array holds
 };
 
 struct GemmOperands {
@@ -47,6 +64,7 @@ struct GemmArgs {
   int vec_ok;                       // out/residual pitches and bases allow 16-byte vector access
   int* err;                         // device error word (bounded waits), may be nullptr
   PeerArgs peer;                    // kEpiPeer only
+  NvlsGemmArgs nvls;                // kEpiNvlsAR only
 };
 
 void gemm_bf16(const GemmOperands& op, GemmArgs args, int epi, int bn, int max_ctas, cudaStream_t stream);

@@ -225,6 +225,25 @@ __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v 
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
+
+// Named barrier `id` over `n` threads (warps of one role synchronise without the rest of the CTA).
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// NVSwitch multicast: 8 bf16 summed over every rank's copy (fp32 accumulation in the switch) / 16 bytes stored
+// into every rank's copy.
+__device__ __forceinline__ void multimem_ld_reduce_bf16x8(const void* mc, uint4& v) {
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(mc)
+               : "memory");
+}
+__device__ __forceinline__ void multimem_st_16(void* mc, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 
 }  // namespace rf

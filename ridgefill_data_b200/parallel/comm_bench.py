@@ -110,13 +110,24 @@ def main(argv=None):
             o = G.linear(y, w, residual=h if rank == 0 else None)
             dist.all_reduce(o)
         t1 = _time(nccl_gemm_ar)
+        rp.fused_gemm = False
+        t2s = _time(lambda: rp(y, w, h))
+        rp.fused_gemm = True
+        want = rp(y, w, h).float()
+        rp.fused_gemm = False
+        got_split = rp(y, w, h).float()
+        rp.fused_gemm = True
+        torch.cuda.synchronize()
+        check_errors()
+        ferr = float((want - got_split).abs().max() / got_split.abs().max())
         t2 = _time(lambda: rp(y, w, h))
         t_gemm = _time(lambda: G.linear(y, w))
         flops = 2 * rows * d * a.k
         roof2 = max(flops / (GEMM_TFLOPS * 1e12), S / (LINK_GBS * 1e9)) * 1e3
         out.append(dict(case="gemm+allreduce", rows=rows, d=d, k=a.k, world=world, gemm_ms=round(t_gemm, 4),
-                        nccl_ms=round(t1, 4), nvls_ms=round(t2, 4), roofline_ms=round(roof2, 4),
-                        nvls_frac_of_roofline=round(roof2 / t2, 3)))
+                        nccl_ms=round(t1, 4), nvls_two_kernels_ms=round(t2s, 4), nvls_fused_ms=round(t2, 4),
+                        fused_vs_two_kernel_max_rel_diff=ferr, roofline_ms=round(roof2, 4),
+                        nvls_fused_frac_of_roofline=round(roof2 / t2, 3)))
 
         cols = d // world
         b = torch.randn(rows, d, device="cuda", generator=g).bfloat16()

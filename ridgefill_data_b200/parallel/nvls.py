@@ -7,6 +7,9 @@ NvlsRowParallel  h + sum_r y_r w_r^T: the tcgen05 GEMM writes this rank's partia
                  (multimem.st) and barriers again. The result is a view of one of OUT_BUFFERS rotating symmetric
                  output buffers: valid until OUT_BUFFERS further reductions (the model's stable() clones a tensor
                  that must live longer, e.g. the split state).
+                 With fused_gemm (the default) the GEMM and the reduction are one kernel (csrc/gemm.cu kEpiNvlsAR):
+                 comm warps reduce each 128-row block as soon as every rank's epilogues have written it, while the
+                 tensor cores work on later blocks.
 NvlsMapFill      the column-sharded ridge-map fill: this rank's slice x_l[:, cols_r] from the GEMM (bias epilogue)
                  is multicast into every rank's copy of x_l (one store per 16 bytes, the switch fans it out), then a
                  barrier; buffers alternate by layer parity.
@@ -72,6 +75,7 @@ class _NvlsBase:
 class NvlsRowParallel(_NvlsBase):
     max_ctas = 32          # the all-reduce saturates the switch with 32 CTAs of 512 threads (measured at TP 2 / 8)
     acc32 = True
+    fused_gemm = True      # one kernel: GEMM tiles + per-row-block reduction by the comm warps (kEpiNvlsAR)
 
     def __init__(self, group=None):
         super().__init__(group)
@@ -80,6 +84,8 @@ class NvlsRowParallel(_NvlsBase):
         self.part = None
         self.outs = []
         self.turn = 0
+        self.ar_flags = None
+        self.ar_epoch = 0
 
     def _ensure(self, rows, d):
         if rows <= self.cap and d == self.d:
@@ -88,6 +94,14 @@ class NvlsRowParallel(_NvlsBase):
         self.part = _Symm(cap * d, torch.bfloat16, self.group)
         self.outs = [_Symm(cap * d, torch.bfloat16, self.group) for _ in range(OUT_BUFFERS)]
         self.cap, self.d = cap, d
+        self.max_mb = cap // 128
+        if self.ar_flags is None or self.ar_flags.t.numel() < self.max_mb * 8 + 64:
+            self.ar_flags = _Symm(self.max_mb * 8 + 64, torch.int32, self.group, need_multicast=False)
+            self.ar_flags.t.zero_()
+            self.ar_epoch = 0
+        self.counters = torch.zeros(self.max_mb + 1, dtype=torch.int32, device=self.part.t.device)
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
 
     def owns(self, t):
         base = t.untyped_storage().data_ptr()
@@ -113,8 +127,16 @@ class NvlsRowParallel(_NvlsBase):
     def __call__(self, y, w, h):
         rows, d = y.shape[0], w.shape[0]
         part = self.partial_view(rows, d)
-        G.linear(y, w, residual=h if self.rank == 0 else None, out=part)
-        return self.allreduce_(rows, d)
+        if not self.fused_gemm:
+            G.linear(y, w, residual=h if self.rank == 0 else None, out=part)
+            return self.allreduce_(rows, d)
+        self.ar_epoch += 1
+        out = self.outs[self.turn]
+        self.turn = (self.turn + 1) % len(self.outs)
+        ext().gemm_nvls_ar(y, w, h if self.rank == 0 else None, part, self.part.mc, out.mc,
+                           self.ar_flags.ptrs[self.rank], self.ar_flags.ptrs, self.rank, self.ar_epoch, self.counters,
+                           self.max_mb, 256 if d % 256 == 0 else 128, 0, self.err)
+        return out.t[:rows * d].view(rows, d)
 
 
 class NvlsMapFill(_NvlsBase):
