@@ -16,9 +16,10 @@
 // kEpiF32 (fp32 out), kEpiF64Acc (fp64 out += acc, split-K chunks added with atomics: the
 // fp32-per-block, fp64-across-blocks accumulation of the ridge sufficient statistics), kEpiPeer (tiles
 // stored into other GPUs' buffers) and kEpiNvlsAR: the tensor-parallel row-parallel product fused with its
-// all-reduce. The CTA then has 8 warps: warps 6-7 (comm warps) reduce the row blocks this rank owns through the
+// all-reduce. The CTA then has 10 warps: the comm warps reduce the row blocks this rank owns through the
 // NVSwitch (multimem.ld_reduce / multimem.st) as soon as every rank's epilogues have finished them, while the
-// other warps keep computing later tiles (tile order finishes row blocks in groups of 16).
+// other warps keep computing later tiles (tile order finishes row blocks in groups of 16). Warps 6-9 are the comm
+// warps.
 #include "gemm.h"
 #include "kernels.h"
 #include "ptx.cuh"
@@ -37,9 +38,13 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kGemmThreads = 192;
 
+constexpr int kCommWarps = 4;     // kEpiNvlsAR: warps 6..9 move the reduced rows
+constexpr int kCommUnroll = 8;    // 16-byte multimem loads in flight per comm thread
+constexpr int kCommBatch = 8;     // owned row blocks reduced in one pass when they are already complete
+
 template <int EPI>
 struct GemmThreads {
-  static constexpr int value = EPI == kEpiNvlsAR ? 256 : kGemmThreads;
+  static constexpr int value = EPI == kEpiNvlsAR ? kGemmThreads + 32 * kCommWarps : kGemmThreads;
 };
 constexpr int kGroupM = 16;   // rasterisation: consecutive tiles walk 16 M-blocks per N-block
 
@@ -407,47 +412,68 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
       mbar_arrive(&tempty[buf]);
     }
   } else if constexpr (EPI == kEpiNvlsAR) {
-    // ------------------------------------------------------------------ comm warps (6..7)
+    // ------------------------------------------------------------------ comm warps (6..9)
+    // Owned row blocks (mb % world == rank) in ascending order; each pass waits for the next one and takes up to
+    // kCommBatch following owned blocks that are already complete on every rank. Every CTA moves its own
+    // 1/gridDim slice of each block, so the whole grid shares every block.
+    constexpr int CT = 32 * kCommWarps;
     const NvlsGemmArgs& nv = args.nvls;
     const int ct = threadIdx.x - 6 * 32;
     const int units_row = args.N / 8;
+    const long slice = ((long)BM * units_row + gridDim.x - 1) / gridDim.x;
     const char* in = reinterpret_cast<const char*>(nv.mc_part);
     char* outp = reinterpret_cast<char*>(nv.mc_out);
+    __shared__ int s_batch;
     bool ok = true;
-    for (int mb = nv.rank; mb < num_mb && ok; mb += nv.world) {
+    int mb = nv.rank;
+    while (mb < num_mb && ok) {
       if (ct == 0) {
         bool good = true;
         for (int q = 0; q < nv.world && good; ++q) good = wait_value(nv.flags + mb * kMaxPeers + q, nv.epoch, args.err);
+        int nb = 1;
+        while (good && nb < kCommBatch && mb + nb * nv.world < num_mb) {
+          const int nxt = mb + nb * nv.world;
+          bool ready = true;
+          for (int q = 0; q < nv.world && ready; ++q) ready = ld_acquire_sys(nv.flags + nxt * kMaxPeers + q) == nv.epoch;
+          if (!ready) break;
+          ++nb;
+        }
         s_comm_ok = good ? 1 : 0;
+        s_batch = nb;
       }
-      named_bar_sync(1, 64);
+      named_bar_sync(1, CT);
       ok = s_comm_ok != 0;
-      named_bar_sync(1, 64);
+      const int nbatch = s_batch;
+      named_bar_sync(1, CT);
       if (!ok) break;
-      const int r0 = mb * BM, r1 = min(args.M, r0 + BM);
-      const long n_units = (long)(r1 - r0) * units_row;
-      const long per = (n_units + gridDim.x - 1) / gridDim.x;
-      const long ub = (long)blockIdx.x * per, ue = min(n_units, ub + per);
-      for (long u0 = ub + ct; u0 < ue; u0 += 64 * 4) {
-        uint4 v[4];
-        long off[4];
+      const long total = (long)nbatch * slice;
+      for (long j0 = ct; j0 < total; j0 += (long)CT * kCommUnroll) {
+        uint4 v[kCommUnroll];
+        long off[kCommUnroll];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const long u = u0 + k * 64;
+        for (int k = 0; k < kCommUnroll; ++k) {
+          const long j = j0 + (long)k * CT;
           off[k] = -1;
-          if (u < ue) {
-            const long r = r0 + u / units_row, c = (u % units_row) * 8;
-            off[k] = (r * args.ldo + c) * 2;
-            multimem_ld_reduce_bf16x8(in + off[k], v[k]);
+          if (j < total) {
+            const int b = (int)(j / slice);
+            const long u = (long)blockIdx.x * slice + (j - (long)b * slice);
+            const int blk = mb + b * nv.world;
+            const int r0 = blk * BM;
+            const long nu = (long)(min(args.M, r0 + BM) - r0) * units_row;
+            if (u < nu) {
+              off[k] = ((long)(r0 + u / units_row) * args.ldo + (u % units_row) * 8) * 2;
+              multimem_ld_reduce_bf16x8(in + off[k], v[k]);
+            }
           }
         }
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
+        for (int k = 0; k < kCommUnroll; ++k)
           if (off[k] >= 0) multimem_st_16(outp + off[k], v[k]);
       }
+      mb += nbatch * nv.world;
     }
     // every CTA's sums are out: the last CTA announces this rank done; every CTA waits for all ranks
-    named_bar_sync(1, 64);
+    named_bar_sync(1, CT);
     if (ct == 0) {
       __threadfence_system();
       const int done_off = nv.max_mb * kMaxPeers;
