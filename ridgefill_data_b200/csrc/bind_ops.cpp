@@ -409,6 +409,47 @@ void gemm_nvls_ar_b(Tensor a, Tensor b, c10::optional<Tensor> residual, Tensor o
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Column-sharded product fused with its all-gather through NVSwitch multicast (kEpiNvlsAG): this rank's columns
+// of x = a b^T + bias land in every rank's copy of the full [M, d] buffer (mc_full: its multicast address).
+void gemm_nvls_ag_b(Tensor a, Tensor b, c10::optional<Tensor> bias, int64_t mc_full, int64_t d, int64_t col_off,
+                    int64_t flags_local, std::vector<int64_t> flag_peers, int64_t rank, int64_t epoch, Tensor counters,
+                    int64_t bn, Tensor err) {
+  need(a, at::kBFloat16, "a");
+  need(b, at::kBFloat16, "b");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1, "gemm_nvls_ag: unit inner stride");
+  TORCH_CHECK(flag_peers.size() >= 1 && flag_peers.size() <= rf::kMaxPeers, "gemm_nvls_ag: 1..8 ranks");
+  c10::cuda::CUDAGuard g(a.device());
+  rf::GemmOperands op{a.data_ptr(), a.stride(0), false, b.data_ptr(), b.stride(0), false};
+  rf::GemmArgs args{};
+  args.M = (int)a.size(0);
+  args.K = (int)a.size(1);
+  args.N = (int)b.size(0);
+  TORCH_CHECK(b.size(1) == args.K, "gemm_nvls_ag: K mismatch");
+  TORCH_CHECK(args.N % 32 == 0 && d % 8 == 0 && col_off % 8 == 0 && col_off + args.N <= d,
+              "gemm_nvls_ag: column slice must be whole 32-column chunks inside d, 16-byte aligned");
+  args.k_splits = 1;
+  args.out = reinterpret_cast<void*>(mc_full + col_off * 2);
+  args.ldo = d;
+  if (bias.has_value()) {
+    need(*bias, at::kBFloat16, "bias");
+    TORCH_CHECK(bias->is_contiguous() && bias->numel() == args.N, "gemm_nvls_ag: bias [N]");
+    args.bias = cbf(*bias);
+  }
+  args.vec_ok = 1;
+  args.err = err.data_ptr<int>();
+  rf::NvlsGemmArgs& nv = args.nvls;
+  nv.flags = reinterpret_cast<int*>(flags_local);
+  for (size_t i = 0; i < flag_peers.size(); ++i) nv.peer_flags[i] = reinterpret_cast<int*>(flag_peers[i]);
+  nv.world = (int)flag_peers.size();
+  nv.rank = (int)rank;
+  nv.epoch = (int)epoch;
+  TORCH_CHECK(counters.scalar_type() == at::kInt && counters.numel() >= 1, "gemm_nvls_ag: counters");
+  nv.done_count = counters.data_ptr<int>();
+  nv.max_mb = 0;
+  rf::gemm_bf16(op, args, rf::kEpiNvlsAG, (int)bn, 0, cur());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace
 
 void router_topk_b(Tensor logits, int64_t E, int64_t k, Tensor idx, Tensor wts, bool norm) {
@@ -587,4 +628,5 @@ void register_comm(pybind11::module_& m) {
   m.def("comm_gather_rows", &comm_gather_rows_b);
   m.def("gemm_peer", &gemm_peer_b);
   m.def("gemm_nvls_ar", &gemm_nvls_ar_b);
+  m.def("gemm_nvls_ag", &gemm_nvls_ag_b);
 }

@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
           const int col0 = tc.nb * BN + c;
           if (!row_ok || col0 >= args.N) continue;
           const bool full_chunk = (col0 + 32 <= args.N);
-          if constexpr (EPI == kEpiStore || EPI == kEpiNvlsAR) {
+          if constexpr (EPI == kEpiStore || EPI == kEpiNvlsAR || EPI == kEpiNvlsAG) {
             __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col0;
             float v[32];
 #pragma unroll
@@ -320,7 +320,10 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
                 w.y = pack_bf16x2(v[j + 2], v[j + 3]);
                 w.z = pack_bf16x2(v[j + 4], v[j + 5]);
                 w.w = pack_bf16x2(v[j + 6], v[j + 7]);
-                *reinterpret_cast<uint4*>(dst + j) = w;
+                if constexpr (EPI == kEpiNvlsAG)
+                  multimem_st_16(dst + j, w);
+                else
+                  *reinterpret_cast<uint4*>(dst + j) = w;
               }
             } else {
               for (int j = 0; j < 32; ++j)
@@ -410,6 +413,22 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
+    }
+    if constexpr (EPI == kEpiNvlsAG) {
+      // every epilogue warp of every CTA is done storing: the last CTA announces this rank; one thread per CTA
+      // waits (bounded) for every rank, so the gathered tensor is complete when the kernel ends
+      named_bar_sync(2, 128);
+      if (warp == 2 && lane == 0) {
+        const NvlsGemmArgs& nv = args.nvls;
+        const int done_off = nv.max_mb * kMaxPeers;
+        __threadfence_system();
+        if (atomicAdd(nv.done_count, 1) == (int)gridDim.x - 1) {
+          *nv.done_count = 0;
+          for (int q = 0; q < nv.world; ++q) st_release_sys(nv.peer_flags[q] + done_off + nv.rank, nv.epoch);
+        }
+        bool good = true;
+        for (int q = 0; q < nv.world && good; ++q) good = wait_value(nv.flags + done_off + q, nv.epoch, args.err);
+      }
     }
   } else if constexpr (EPI == kEpiNvlsAR) {
     // ------------------------------------------------------------------ comm warps (6..9)
@@ -592,6 +611,8 @@ void gemm_bf16(const GemmOperands& op, GemmArgs args, int epi, int bn, int max_c
   RF_GEMM_CASE(128, kEpiPeer, false, false)
   RF_GEMM_CASE(256, kEpiNvlsAR, false, false)
   RF_GEMM_CASE(128, kEpiNvlsAR, false, false)
+  RF_GEMM_CASE(256, kEpiNvlsAG, false, false)
+  RF_GEMM_CASE(128, kEpiNvlsAG, false, false)
 #undef RF_GEMM_CASE
   throw std::runtime_error("gemm_bf16: unsupported (bn, epilogue, majors) combination");
 }

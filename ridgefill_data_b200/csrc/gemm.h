@@ -7,7 +7,7 @@
 
 namespace rf {
 
-enum GemmEpilogue : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiF32 = 2, kEpiF64Acc = 3, kEpiPeer = 4, kEpiNvlsAR = 5 };
+enum GemmEpilogue : int { kEpiStore = 0, kEpiSwiGLU = 1, kEpiF32 = 2, kEpiF64Acc = 3, kEpiPeer = 4, kEpiNvlsAR = 5, kEpiNvlsAG = 6 };
 
 constexpr int kMaxPeers = 8;
 
@@ -32,6 +32,10 @@ struct PeerArgs {
 // this rank owns (mb % world == rank) as soon as every rank has announced them, reduce them in the switch
 // (multimem.ld_reduce) and multicast the sums (multimem.st) into every rank's output buffer; a final barrier
 // makes the whole result visible on every rank before the kernel ends.
+// Fused all-gather through NVSwitch multicast (kEpiNvlsAG, the column-sharded map fill): args.out is the
+// multicast address of the full [M][ldo] buffer already offset to this rank's first column; every 16-byte store
+// of the epilogue (bias added) lands in every rank's copy; a final barrier (done flags at index
+// max_mb * kMaxPeers + rank) makes the gathered tensor complete on every rank before the kernel ends.
 struct NvlsGemmArgs {
   const void* mc_part;      // multicast address of the partial buffer (bf16 [M][ldo])
   void* mc_out;             // multicast address of the output buffer

@@ -139,16 +139,23 @@ def main(argv=None):
             full = torch.empty(world * rows, cols, dtype=part.dtype, device=part.device)
             dist.all_gather_into_tensor(full, part)
             return full.view(world, rows, cols).permute(1, 0, 2).reshape(rows, d)
-        got = mf(b, wl, bl, d)
+        got = mf(b, wl, bl, d).clone()
         want = nccl_fill()
+        mf.fused_gemm = False
+        got2 = mf(b, wl, bl, d).clone()
+        mf.fused_gemm = True
         torch.cuda.synchronize()
         check_errors()
-        same = bool(torch.equal(got, want))
+        same = bool(torch.equal(got, want)) and bool(torch.equal(got2, want))
         t3 = _time(nccl_fill)
+        mf.fused_gemm = False
+        t4s = _time(lambda: mf(b, wl, bl, d))
+        mf.fused_gemm = True
         t4 = _time(lambda: mf(b, wl, bl, d))
         flops3 = 2 * rows * d * cols
         roof3 = max(flops3 / (GEMM_TFLOPS * 1e12), S * (world - 1) / world / (LINK_GBS * 1e9)) * 1e3
-        out.append(dict(case="map_fill", rows=rows, d=d, world=world, nccl_ms=round(t3, 4), nvls_ms=round(t4, 4),
+        out.append(dict(case="map_fill", rows=rows, d=d, world=world, nccl_ms=round(t3, 4),
+                        nvls_two_kernels_ms=round(t4s, 4), nvls_ms=round(t4, 4),
                         bitwise_equal=same, roofline_ms=round(roof3, 4), nvls_frac_of_roofline=round(roof3 / t4, 3)))
     if rank == 0:
         for r in out:

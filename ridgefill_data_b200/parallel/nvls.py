@@ -12,7 +12,8 @@ NvlsRowParallel  h + sum_r y_r w_r^T: the tcgen05 GEMM writes this rank's partia
                  tensor cores work on later blocks.
 NvlsMapFill      the column-sharded ridge-map fill: this rank's slice x_l[:, cols_r] from the GEMM (bias epilogue)
                  is multicast into every rank's copy of x_l (one store per 16 bytes, the switch fans it out), then a
-                 barrier; buffers alternate by layer parity.
+                 barrier; buffers alternate by layer parity. With fused_gemm (the default) the epilogue itself
+                 issues the multicast stores and the barrier closes the same kernel (csrc/gemm.cu kEpiNvlsAG).
 Every wait is bounded; a timeout sets the device error word (ops._ext.check_errors raises).
 """
 from __future__ import annotations
@@ -140,11 +141,14 @@ class NvlsRowParallel(_NvlsBase):
 
 
 class NvlsMapFill(_NvlsBase):
+    fused_gemm = True      # one kernel: the GEMM epilogue stores each tile through the multicast address (kEpiNvlsAG)
+
     def __init__(self, group=None):
         super().__init__(group)
         self.cap = 0
         self.d = None
         self.buf = None
+        self.done = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", torch.cuda.current_device()))
 
     def _ensure(self, rows, d):
         if rows <= self.cap and d == self.d:
@@ -160,10 +164,15 @@ class NvlsMapFill(_NvlsBase):
         self.epoch += 1
         par = self.epoch & 1
         cols = w_local.shape[0]
-        part = G.linear(b, w_local, bias=bias_local)
         off = par * self.cap * d
-        ext().nvls_allgather(part, self.buf.mc + 2 * off, d, self.rank * cols, self.flag_local, self.flags.ptrs,
-                             self.rank, SLOT_AG, self.epoch, self.counter(COUNTER_AG), self.err)
+        if self.fused_gemm and cols % 32 == 0:
+            ext().gemm_nvls_ag(b, w_local, bias_local, self.buf.mc + 2 * off, d, self.rank * cols, self.flag_local,
+                               self.flags.ptrs, self.rank, self.epoch, self.done, 256 if cols % 256 == 0 else 128,
+                               self.err)
+        else:
+            part = G.linear(b, w_local, bias=bias_local)
+            ext().nvls_allgather(part, self.buf.mc + 2 * off, d, self.rank * cols, self.flag_local, self.flags.ptrs,
+                                 self.rank, SLOT_AG, self.epoch, self.counter(COUNTER_AG), self.err)
         return self.buf.t[off:off + P * d].view(P, d)
 
 
