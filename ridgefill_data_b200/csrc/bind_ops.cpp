@@ -425,8 +425,8 @@ void gemm_nvls_ag_b(Tensor a, Tensor b, c10::optional<Tensor> bias, int64_t mc_f
   args.K = (int)a.size(1);
   args.N = (int)b.size(0);
   TORCH_CHECK(b.size(1) == args.K, "gemm_nvls_ag: K mismatch");
-  TORCH_CHECK(args.N % 32 == 0 && d % 8 == 0 && col_off % 8 == 0 && col_off + args.N <= d,
-              "gemm_nvls_ag: column slice must be whole 32-column chunks inside d, 16-byte aligned");
+  TORCH_CHECK(args.N % 64 == 0 && d % 8 == 0 && col_off % 8 == 0 && col_off + args.N <= d,
+              "gemm_nvls_ag: column slice must be whole 64-column chunks inside d, 16-byte aligned");
   args.k_splits = 1;
   args.out = reinterpret_cast<void*>(mc_full + col_off * 2);
   args.ldo = d;

@@ -57,7 +57,17 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 8 * (2 * STAGES + 4) + 16;
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  // kEpiNvlsAG: per epilogue warp a 32-row x 64-column bf16 staging tile, so the multicast stores go out as
+  // 128-byte row segments instead of one 16-byte piece per row
+  static constexpr int STAGE_OFF = (STAGES * STAGE_BYTES + BAR_BYTES + 127) / 128 * 128;
+  static constexpr int AG_STAGING = 4 * 32 * 128;
+  static constexpr int SMEM_BYTES_AG = 1024 + STAGE_OFF + AG_STAGING;
 };
+
+template <int BN, int EPI>
+constexpr int gemm_smem_bytes() {
+  return EPI == kEpiNvlsAG ? GemmCfg<BN>::SMEM_BYTES_AG : GemmCfg<BN>::SMEM_BYTES;
+}
 
 struct TileCoord {
   int mb, nb, ks;
@@ -278,6 +288,48 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
             }
           }
         }
+      } else if constexpr (EPI == kEpiNvlsAG) {
+        // 64 columns at a time: bias, bf16, staged row-major (16-byte units XOR-swizzled by row), then each
+        // instruction multicasts 4 rows x 128 contiguous bytes
+        uint4* stg = reinterpret_cast<uint4*>(smem + Cfg::STAGE_OFF) + (size_t)q * 32 * 8;
+        const int row0 = tc.mb * BM + q * 32;
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.out);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(tbase + c, ra);
+          tmem_ld32(tbase + c + 32, rb);
+          tmem_wait_ld();
+          const int col0 = tc.nb * BN + c;
+          if (col0 >= args.N) continue;
+          float v[64];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            v[j] = __uint_as_float(ra[j]);
+            v[32 + j] = __uint_as_float(rb[j]);
+          }
+          if (args.bias != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] += __bfloat162float(args.bias[col0 + j]);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            uint4 w;
+            w.x = pack_bf16x2(v[8 * u], v[8 * u + 1]);
+            w.y = pack_bf16x2(v[8 * u + 2], v[8 * u + 3]);
+            w.z = pack_bf16x2(v[8 * u + 4], v[8 * u + 5]);
+            w.w = pack_bf16x2(v[8 * u + 6], v[8 * u + 7]);
+            stg[lane * 8 + (u ^ (lane & 7))] = w;
+          }
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int rr = k * 4 + (lane >> 3), u = lane & 7;
+            const uint4 w = stg[rr * 8 + (u ^ (rr & 7))];
+            if (row0 + rr < args.M) multimem_st_16(out + (size_t)(row0 + rr) * args.ldo + col0 + u * 8, w);
+          }
+          __syncwarp();
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -287,7 +339,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
           const int col0 = tc.nb * BN + c;
           if (!row_ok || col0 >= args.N) continue;
           const bool full_chunk = (col0 + 32 <= args.N);
-          if constexpr (EPI == kEpiStore || EPI == kEpiNvlsAR || EPI == kEpiNvlsAG) {
+          if constexpr (EPI == kEpiStore || EPI == kEpiNvlsAR) {
             __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.out) + (size_t)row * args.ldo + col0;
             float v[32];
 #pragma unroll
@@ -320,10 +372,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
                 w.y = pack_bf16x2(v[j + 2], v[j + 3]);
                 w.z = pack_bf16x2(v[j + 4], v[j + 5]);
                 w.w = pack_bf16x2(v[j + 6], v[j + 7]);
-                if constexpr (EPI == kEpiNvlsAG)
-                  multimem_st_16(dst + j, w);
-                else
-                  *reinterpret_cast<uint4*>(dst + j) = w;
+                *reinterpret_cast<uint4*>(dst + j) = w;
               }
             } else {
               for (int j = 0; j < 32; ++j)
@@ -565,7 +614,7 @@ static void launch_gemm(const GemmOperands& op, GemmArgs args, int max_ctas, cud
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes<BN, EPI>());
     attr_set[dev & 63] = true;
   }
   CUtensorMap ta = A_MN ? make_tmap_bf16_2d(op.A, args.M, args.K, op.lda, 64, 64)
@@ -581,7 +630,7 @@ static void launch_gemm(const GemmOperands& op, GemmArgs args, int max_ctas, cud
     // every CTA takes part in the reduction: keep one CTA per SM even when there are fewer tiles
     ctas = max_ctas > 0 ? std::min(max_ctas, num_sms(dev)) : num_sms(dev);
   }
-  kernel<<<ctas, GemmThreads<EPI>::value, Cfg::SMEM_BYTES, stream>>>(ta, tb, args);
+  kernel<<<ctas, GemmThreads<EPI>::value, gemm_smem_bytes<BN, EPI>(), stream>>>(ta, tb, args);
   count_launch();
 }
 

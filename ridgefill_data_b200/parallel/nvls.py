@@ -165,7 +165,7 @@ class NvlsMapFill(_NvlsBase):
         par = self.epoch & 1
         cols = w_local.shape[0]
         off = par * self.cap * d
-        if self.fused_gemm and cols % 32 == 0:
+        if self.fused_gemm and cols % 64 == 0:
             ext().gemm_nvls_ag(b, w_local, bias_local, self.buf.mc + 2 * off, d, self.rank * cols, self.flag_local,
                                self.flags.ptrs, self.rank, self.epoch, self.done, 256 if cols % 256 == 0 else 128,
                                self.err)
