@@ -182,7 +182,8 @@ void gdn_conv_state_update(Tensor proj, Tensor state, int64_t n, int64_t C, int6
 }
 
 void gdn_chunk_scan(OptT q, Tensor k, Tensor v, Tensor beta, Tensor g, Tensor state, OptT out, Tensor w_buf,
-                    Tensor u_buf, OptT s_buf, OptT vt_buf, int64_t n, int64_t nk, int64_t nv, int64_t dk, int64_t dv, Tensor err) {
+                    Tensor u_buf, OptT s_buf, OptT vt_buf, int64_t n, int64_t nk, int64_t nv, int64_t dk, int64_t dv, Tensor err,
+                    int64_t groups, OptT grp_buf, OptT start_buf) {
   need(k, at::kBFloat16, "k");
   need(v, at::kBFloat16, "v");
   need(beta, at::kFloat, "beta");
@@ -226,6 +227,17 @@ void gdn_chunk_scan(OptT q, Tensor k, Tensor v, Tensor beta, Tensor g, Tensor st
   a.dk = (int)dk;
   a.dv = (int)dv;
   a.err = err.data_ptr<int>();
+  if (groups > 1 && grp_buf.has_value()) {
+    need(*grp_buf, at::kFloat, "grp_buf");
+    TORCH_CHECK(grp_buf->numel() >= 2 * nv * groups * dv * dk, "gdn_chunk_scan: grp_buf size");
+    a.groups = (int)groups;
+    a.grp_buf = grp_buf->data_ptr<float>();
+    if (start_buf.has_value()) {
+      need(*start_buf, at::kFloat, "start_buf");
+      TORCH_CHECK(start_buf->numel() >= nv * groups * dv * dk, "gdn_chunk_scan: start_buf size");
+      a.start_buf = start_buf->data_ptr<float>();
+    }
+  }
   rf::gdn_chunk_scan(a, cur());
 }
 

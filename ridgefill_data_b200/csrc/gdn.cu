@@ -411,18 +411,32 @@ __device__ __forceinline__ void state_issue_loads(StateSmem& s, const GdnScanArg
   }
 }
 
+// MODE 0: sequential over every chunk from a.state (updated in place).
+// MODE 1 (two-level scan, pass 1): blockIdx.z = chunk group; blockIdx.y < dv / SVS: the group's end state from a
+//        zero start (R); blockIdx.y >= dv / SVS: the group's transfer matrix P (start from the identity, U = 0),
+//        since S_end = S_start P + R is linear in S_start. Both go to grp_buf.
+// MODE 2 (two-level scan, pass 3): blockIdx.z = chunk group, start from start_buf, output-mode stores only.
+template <int MODE>
 __global__ void __launch_bounds__(128, 1) gdn_state_kernel(GdnScanArgs a, int n_pad, __nv_bfloat16* s_buf,
                                                            __nv_bfloat16* vt_buf) {
   extern __shared__ __align__(16) uint8_t st_raw[];
   StateSmem& s = *reinterpret_cast<StateSmem*>(st_raw);
   const int h = blockIdx.x;
-  const int m0 = blockIdx.y * SVS;                 // first value dim of this CTA
+  const int slices = a.dv / SVS;
+  const bool transfer = MODE == 1 && (int)blockIdx.y >= slices;   // computing P (U = 0, identity start)
+  const int m0 = (MODE == 1 ? (int)blockIdx.y % slices : (int)blockIdx.y) * SVS;   // first value dim of this CTA
   const int kh = h / (a.nv / a.nk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const int mrow = warp * 16;                      // this warp's rows within the slice
-  const int n_chunks = (a.n + GC - 1) / GC;
+  const int n_chunks_all = (a.n + GC - 1) / GC;
+  const int per_group = MODE == 0 ? n_chunks_all : (n_chunks_all + a.groups - 1) / a.groups;
+  const int c_begin = MODE == 0 ? 0 : (int)blockIdx.z * per_group;
+  const int c_end = MODE == 0 ? n_chunks_all : min(n_chunks_all, c_begin + per_group);
+  const int n_chunks = n_chunks_all;               // chunk indexing of the scratch buffers
   float* state = a.state + (long)h * DK * a.dv;    // S [dk][dv]
+  const long grp_mat = (long)a.dv * DK;            // one [dv][dk] matrix
+  const long grp_idx = ((long)h * a.groups + blockIdx.z) * grp_mat;
 
   // S^T accumulators: rows m0 + mrow + (g, g+8), cols (dk) nt * 8 + 2t (+1)
   float S[16][4];
@@ -430,18 +444,32 @@ __global__ void __launch_bounds__(128, 1) gdn_state_kernel(GdnScanArgs a, int n_
   for (int nt = 0; nt < 16; ++nt) {
     const int m = m0 + mrow + g;
     const int c = nt * 8 + 2 * t;
-    S[nt][0] = state[(long)c * a.dv + m];
-    S[nt][1] = state[(long)(c + 1) * a.dv + m];
-    S[nt][2] = state[(long)c * a.dv + m + 8];
-    S[nt][3] = state[(long)(c + 1) * a.dv + m + 8];
+    if constexpr (MODE == 0) {
+      S[nt][0] = state[(long)c * a.dv + m];
+      S[nt][1] = state[(long)(c + 1) * a.dv + m];
+      S[nt][2] = state[(long)c * a.dv + m + 8];
+      S[nt][3] = state[(long)(c + 1) * a.dv + m + 8];
+    } else if constexpr (MODE == 1) {
+      S[nt][0] = (transfer && c == m) ? 1.f : 0.f;
+      S[nt][1] = (transfer && c + 1 == m) ? 1.f : 0.f;
+      S[nt][2] = (transfer && c == m + 8) ? 1.f : 0.f;
+      S[nt][3] = (transfer && c + 1 == m + 8) ? 1.f : 0.f;
+    } else {
+      const float* sp = a.start_buf + grp_idx;
+      S[nt][0] = sp[(long)m * DK + c];
+      S[nt][1] = sp[(long)m * DK + c + 1];
+      S[nt][2] = sp[(long)(m + 8) * DK + c];
+      S[nt][3] = sp[(long)(m + 8) * DK + c + 1];
+    }
   }
   for (int p = 0; p < SST - 1; ++p) {
-    if (p < n_chunks) state_issue_loads(s, a, p, p, h, kh, m0, n_pad, tid);
+    if (c_begin + p < c_end) state_issue_loads(s, a, p, c_begin + p, h, kh, m0, n_pad, tid);
     cp_async_commit();
   }
-  for (int ch = 0; ch < n_chunks; ++ch) {
-    const int stage = ch % SST;
-    if (ch + SST - 1 < n_chunks) state_issue_loads(s, a, (ch + SST - 1) % SST, ch + SST - 1, h, kh, m0, n_pad, tid);
+  for (int ch = c_begin; ch < c_end; ++ch) {
+    const int stage = (ch - c_begin) % SST;
+    if (ch + SST - 1 < c_end)
+      state_issue_loads(s, a, (ch - c_begin + SST - 1) % SST, ch + SST - 1, h, kh, m0, n_pad, tid);
     cp_async_commit();
     cp_async_wait<SST - 1>();
     __syncthreads();
@@ -496,8 +524,9 @@ __global__ void __launch_bounds__(128, 1) gdn_state_kernel(GdnScanArgs a, int n_
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int c = j * 8 + 2 * t;                      // chunk rows c, c + 1
-      const float2 u0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ut[(mrow + g) * PU + c]));
-      const float2 u1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ut[(mrow + g + 8) * PU + c]));
+      float2 u0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ut[(mrow + g) * PU + c]));
+      float2 u1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ut[(mrow + g + 8) * PU + c]));
+      if (transfer) u0 = u1 = make_float2(0.f, 0.f);
       const float v0 = u0.x - vt[j][0], v1 = u0.y - vt[j][1], v2 = u1.x - vt[j][2], v3 = u1.y - vt[j][3];
       if (vtg != nullptr) {
         *reinterpret_cast<uint32_t*>(vtg + (long)g * GC + c) = pack2(v0, v1);
@@ -532,10 +561,125 @@ __global__ void __launch_bounds__(128, 1) gdn_state_kernel(GdnScanArgs a, int n_
     __syncthreads();   // this stage is refilled two iterations later
   }
   cp_async_wait<0>();
+  if constexpr (MODE == 2) return;                 // the group-end state is known from pass 2
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt) {
     const int m = m0 + mrow + g;
     const int c = nt * 8 + 2 * t;
+    if constexpr (MODE == 0) {
+      state[(long)c * a.dv + m] = S[nt][0];
+      state[(long)(c + 1) * a.dv + m] = S[nt][1];
+      state[(long)c * a.dv + m + 8] = S[nt][2];
+      state[(long)(c + 1) * a.dv + m + 8] = S[nt][3];
+    } else {
+      float* dst = a.grp_buf + (transfer ? (long)a.nv * a.groups * grp_mat : 0) + grp_idx;
+      dst[(long)m * DK + c] = S[nt][0];
+      dst[(long)m * DK + c + 1] = S[nt][1];
+      dst[(long)(m + 8) * DK + c] = S[nt][2];
+      dst[(long)(m + 8) * DK + c + 1] = S[nt][3];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------- two-level scan, pass 2
+// Per (value head, 64-row slice of S^T): sequentially over the chunk groups, S_start(z + 1) = S_start(z) P_z + R_z
+// (written to start_buf for pass 3 in output mode); the last one is the final state. The product runs on the
+// tensor cores with split-bf16 operands (hi + lo; hi*hi + hi*lo + lo*hi), about fp32 accurate, so the state
+// never passes through a single bf16 rounding.
+constexpr int PP = DK + 8;        // pitch of the staged P halves
+struct PropSmem {
+  __nv_bfloat16 hi[DK * PP];
+  __nv_bfloat16 lo[DK * PP];
+};
+
+__global__ void __launch_bounds__(128, 1) gdn_group_prop_kernel(GdnScanArgs a, int write_starts) {
+  extern __shared__ __align__(16) uint8_t pp_raw[];
+  PropSmem& s = *reinterpret_cast<PropSmem*>(pp_raw);
+  const int h = blockIdx.x, m0 = blockIdx.y * SVS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int mrow = warp * 16;
+  float* state = a.state + (long)h * DK * a.dv;
+  const long mat = (long)a.dv * DK;
+  const float* R = a.grp_buf;
+  const float* P = a.grp_buf + (long)a.nv * a.groups * mat;
+  float S[16][4];
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    const int m = m0 + mrow + g, c = nt * 8 + 2 * t;
+    S[nt][0] = state[(long)c * a.dv + m];
+    S[nt][1] = state[(long)(c + 1) * a.dv + m];
+    S[nt][2] = state[(long)c * a.dv + m + 8];
+    S[nt][3] = state[(long)(c + 1) * a.dv + m + 8];
+  }
+  for (int z = 0; z < a.groups; ++z) {
+    const long idx = ((long)h * a.groups + z) * mat;
+    if (write_starts) {
+      float* sp = a.start_buf + idx;
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt) {
+        const int m = m0 + mrow + g, c = nt * 8 + 2 * t;
+        sp[(long)m * DK + c] = S[nt][0];
+        sp[(long)m * DK + c + 1] = S[nt][1];
+        sp[(long)(m + 8) * DK + c] = S[nt][2];
+        sp[(long)(m + 8) * DK + c + 1] = S[nt][3];
+      }
+    }
+    __syncthreads();   // the previous group's P halves are no longer read
+    for (int v = tid; v < DK * DK; v += 128) {
+      const int r = v / DK, c = v % DK;
+      const float x = P[idx + (long)r * DK + c];
+      const __nv_bfloat16 xh = __float2bfloat16(x);
+      s.hi[r * PP + c] = xh;
+      s.lo[r * PP + c] = __float2bfloat16(x - __bfloat162float(xh));
+    }
+    __syncthreads();
+    // A fragments of S^T (hi and lo), K = dk in 8 steps of 16
+    uint32_t ah[8][4], al[8][4];
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float* src = S[2 * ks + (e >> 1)];
+        const float x0 = src[(e & 1) * 2], x1 = src[(e & 1) * 2 + 1];
+        const __nv_bfloat16 h0 = __float2bfloat16(x0), h1 = __float2bfloat16(x1);
+        ah[ks][e] = pack2(__bfloat162float(h0), __bfloat162float(h1));
+        al[ks][e] = pack2(x0 - __bfloat162float(h0), x1 - __bfloat162float(h1));
+      }
+    }
+    float acc[16][4];
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const int m = m0 + mrow + g, c = nt * 8 + 2 * t;
+      const float* rr = R + idx;
+      acc[nt][0] = rr[(long)m * DK + c];
+      acc[nt][1] = rr[(long)m * DK + c + 1];
+      acc[nt][2] = rr[(long)(m + 8) * DK + c];
+      acc[nt][3] = rr[(long)(m + 8) * DK + c + 1];
+    }
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+      for (int j2 = 0; j2 < 8; ++j2) {
+        uint32_t bh[4], bl[4];
+        ldb_kn(bh, s.hi, PP, j2 * 16, ks * 16, lane);   // B[k = row of P][n = col of P]
+        ldb_kn(bl, s.lo, PP, j2 * 16, ks * 16, lane);
+        mma_bf16(acc[2 * j2], ah[ks], bh[0], bh[1]);
+        mma_bf16(acc[2 * j2 + 1], ah[ks], bh[2], bh[3]);
+        mma_bf16(acc[2 * j2], ah[ks], bl[0], bl[1]);
+        mma_bf16(acc[2 * j2 + 1], ah[ks], bl[2], bl[3]);
+        mma_bf16(acc[2 * j2], al[ks], bh[0], bh[1]);
+        mma_bf16(acc[2 * j2 + 1], al[ks], bh[2], bh[3]);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) S[nt][e] = acc[nt][e];
+  }
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    const int m = m0 + mrow + g, c = nt * 8 + 2 * t;
     state[(long)c * a.dv + m] = S[nt][0];
     state[(long)(c + 1) * a.dv + m] = S[nt][1];
     state[(long)c * a.dv + m + 8] = S[nt][2];
@@ -695,14 +839,32 @@ void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream) {
   static bool set = false;
   if (!set) {
     cudaFuncSetAttribute(gdn_wy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(WySmem));
-    cudaFuncSetAttribute(gdn_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(StateSmem));
+    cudaFuncSetAttribute(gdn_state_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(StateSmem));
+    cudaFuncSetAttribute(gdn_state_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(StateSmem));
+    cudaFuncSetAttribute(gdn_state_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(StateSmem));
+    cudaFuncSetAttribute(gdn_group_prop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PropSmem));
     cudaFuncSetAttribute(gdn_output_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(OutSmem));
     set = true;
   }
   gdn_wy_kernel<<<dim3(n_chunks, a.nv), 128, sizeof(WySmem), stream>>>(a, n_pad);
-  gdn_state_kernel<<<dim3(a.nv, a.dv / SVS), 128, sizeof(StateSmem), stream>>>(a, n_pad, a.q ? a.s_buf : nullptr,
-                                                                               a.q ? a.vt_buf : nullptr);
-  count_launch(2);
+  count_launch();
+  const bool two_level = a.groups > 1 && a.dv == DK && a.grp_buf != nullptr &&
+                         (a.q == nullptr || a.start_buf != nullptr) && n_chunks >= 2 * a.groups;
+  if (!two_level) {
+    gdn_state_kernel<0><<<dim3(a.nv, a.dv / SVS), 128, sizeof(StateSmem), stream>>>(a, n_pad, a.q ? a.s_buf : nullptr,
+                                                                                  a.q ? a.vt_buf : nullptr);
+    count_launch();
+  } else {
+    gdn_state_kernel<1><<<dim3(a.nv, 2 * a.dv / SVS, a.groups), 128, sizeof(StateSmem), stream>>>(a, n_pad, nullptr,
+                                                                                               nullptr);
+    gdn_group_prop_kernel<<<dim3(a.nv, a.dv / SVS), 128, sizeof(PropSmem), stream>>>(a, a.q != nullptr ? 1 : 0);
+    count_launch(2);
+    if (a.q != nullptr) {
+      gdn_state_kernel<2><<<dim3(a.nv, a.dv / SVS, a.groups), 128, sizeof(StateSmem), stream>>>(a, n_pad, a.s_buf,
+                                                                                              a.vt_buf);
+      count_launch();
+    }
+  }
   if (a.q != nullptr) {
     gdn_output_kernel<<<dim3(n_chunks, a.nv), 128, sizeof(OutSmem), stream>>>(a, n_pad, a.s_buf, a.vt_buf);
     count_launch();

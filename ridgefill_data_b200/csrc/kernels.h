@@ -101,6 +101,10 @@ struct GdnScanArgs {
   __nv_bfloat16* vt_buf;    // scratch [nv, n_chunks, dv, 64]: V'^T per chunk (output mode)
   int n, nk, nv, dk, dv;
   int* err;
+  int groups;               // > 1: two-level scan over this many chunk groups (dk == dv); else sequential
+  float* grp_buf;           // scratch [2][nv][groups][dv][dk]: per group the end state from zero (R) and the
+                            // transfer matrix (P), both in the transposed-state layout
+  float* start_buf;         // scratch [nv][groups][dv][dk]: group-start S^T (output mode)
 };
 void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream);
 

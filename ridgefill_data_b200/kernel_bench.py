@@ -37,7 +37,8 @@ def _attn(dev, a):
 
 def _gdn(dev, a):
     from .ops import kernels as K
-    n, nk, nv, dk, dv = a.n or 16384, 16, 48, 128, 128
+    nv = a.nv or 48
+    n, nk, dk, dv = a.n or 16384, max(1, nv // 3), 128, 128
     C = 2 * nk * dk + nv * dv
     proj = (torch.randn(n, C + 2 * nv, device=dev) * 0.5).bfloat16()
     conv_w = (torch.randn(C, 4, device=dev) / 2).bfloat16()
@@ -48,11 +49,13 @@ def _gdn(dev, a):
     out = torch.empty(n, nv * dv, device=dev, dtype=torch.bfloat16)
     fill = a.fill
 
+    groups = a.groups or None
+
     def run():
         st.zero_()
-        K.gdn_scan(None if fill else q, kk, v, beta, g, st, None if fill else out)
+        K.gdn_scan(None if fill else q, kk, v, beta, g, st, None if fill else out, groups=groups)
     # the recurrence's 4 nv dk dv MACs per token (the chunked form does more)
-    return run, dict(flops=2 * 4 * nv * dk * dv * n, shape=[n, nk, nv, dk, dv], fill=fill)
+    return run, dict(flops=2 * 4 * nv * dk * dv * n, shape=[n, nk, nv, dk, dv], fill=fill, groups=groups or "auto")
 
 
 def _moe(dev, a):
@@ -83,6 +86,8 @@ def main(argv=None):
     ap.add_argument("--impl", default="auto", help="attention: auto | mma | tcgen05")
     ap.add_argument("--fill", action="store_true", help="gdn: state-only (fill) mode")
     ap.add_argument("--down", action="store_true", help="moe: the down projection instead of gate/up")
+    ap.add_argument("--nv", type=int, default=0, help="gdn: value heads (48 = the 27B on one GPU, 6 = its TP 8 share)")
+    ap.add_argument("--groups", type=int, default=0, help="gdn: chunk groups of the two-level scan (0: automatic)")
     a = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     fn, info = WORKLOADS[a.workload](dev, a)

@@ -86,9 +86,20 @@ def gdn_conv_state_update(proj, state, channels):
     ext().gdn_conv_state_update(proj, state, proj.shape[0], channels, state.shape[0] + 1)
 
 
-def gdn_scan(q, k, v, beta, g, state, out=None):
+def scan_groups(nv, dv, n, sms=148):
+    """Chunk groups of the two-level delta-rule scan: enough (value head, 64-row slice, group) CTAs to fill about two
+    waves when the heads alone leave the GPU mostly idle (tensor parallelism shrinks the heads per GPU); 1 (the
+    sequential scan) when the heads already fill it."""
+    n_chunks = (n + 63) // 64
+    per_group_ctas = nv * 2 * (dv // 64)
+    groups = (2 * sms) // max(1, per_group_ctas)
+    return groups if groups > 1 and n_chunks >= 2 * groups else 1
+
+
+def gdn_scan(q, k, v, beta, g, state, out=None, groups=None):
     """Chunked gated delta rule continuing `state` [nv, dk, dv] fp32 (updated in place). q None: fill
-    mode (state only). out [n, nv * dv] bf16 (output mode)."""
+    mode (state only). out [n, nv * dv] bf16 (output mode). groups: chunk groups of the two-level scan
+    (None: scan_groups' choice; 1: sequential)."""
     nk, n, dk = k.shape
     nv, _, dv = v.shape
     n_pad = (n + 63) // 64 * 64
@@ -96,8 +107,15 @@ def gdn_scan(q, k, v, beta, g, state, out=None):
     u_buf = torch.empty(nv, n_pad, dv, dtype=BF16, device=k.device)
     s_buf = torch.empty(nv, n_pad // 64, dv, dk, dtype=BF16, device=k.device) if q is not None else None
     vt_buf = torch.empty(nv, n_pad, dv, dtype=BF16, device=k.device) if q is not None else None
+    if groups is None:
+        groups = scan_groups(nv, dv, n) if dv == dk else 1
+    grp_buf = start_buf = None
+    if groups > 1:
+        grp_buf = torch.empty(2, nv, groups, dv, dk, dtype=torch.float32, device=k.device)
+        start_buf = torch.empty(nv, groups, dv, dk, dtype=torch.float32, device=k.device) if q is not None else None
     err = ext().error_word(k.device.index or 0)
-    ext().gdn_chunk_scan(q, k, v, beta, g, state, out, w_buf, u_buf, s_buf, vt_buf, n, nk, nv, dk, dv, err)
+    ext().gdn_chunk_scan(q, k, v, beta, g, state, out, w_buf, u_buf, s_buf, vt_buf, n, nk, nv, dk, dv, err,
+                         groups, grp_buf, start_buf)
     return out
 
 

@@ -122,3 +122,42 @@ def test_gdn_prep_and_scan(n, need_out, with_state):
     from ridgefill_data_b200.ops._ext import check_errors
     torch.cuda.synchronize()
     check_errors()
+
+
+@pytest.mark.parametrize("groups", [3, 8])
+@pytest.mark.parametrize("need_out", [False, True])
+def test_gdn_two_level_scan_matches_sequential_and_oracle(groups, need_out):
+    """The chunk-parallel scan (group end states from zero, group transfer matrices, sequential propagation with
+    split-bf16 products, then the per-group rerun for outputs) against the sequential scan and the fp32 oracle."""
+    torch.manual_seed(5)
+    n, nk, nv, dk, dv = 1500, 1, 2, 128, 128
+    C = 2 * nk * dk + nv * dv
+    proj = (torch.randn(n, C + 2 * nv, device=dev) * 0.5).bfloat16()
+    conv_w = (torch.randn(C, 4, device=dev) / 2).bfloat16()
+    A_log = torch.empty(nv, device=dev).uniform_(0, 2.7)
+    dt = torch.randn(nv, device=dev) * 0.1
+    state = torch.randn(nv, dk, dv, device=dev) * 0.1
+    q, k, v, beta, g = K.gdn_prep(proj, C, C + nv, conv_w, None, A_log, dt, nk, nv, dk, dv)
+    outs, states = {}, {}
+    for grp in (1, groups):
+        out = torch.empty(n, nv * dv, device=dev, dtype=torch.bfloat16) if need_out else None
+        st = state.clone()
+        K.gdn_scan(q if need_out else None, k, v, beta, g, st, out, groups=grp)
+        outs[grp], states[grp] = out, st
+    from ridgefill_data_b200.ops._ext import check_errors
+    torch.cuda.synchronize()
+    check_errors()
+    assert _rel(states[groups], states[1]) < 5e-3
+    if need_out:
+        assert _rel(outs[groups].float(), outs[1].float()) < 1e-2
+    co, _ = O.causal_conv(proj[:, :C], None, conv_w)
+    qo, ko, vo = co.split([nk * dk, nk * dk, nv * dv], -1)
+    qo = O.l2norm(qo.reshape(n, nk, dk).float()).transpose(0, 1) * dk ** -0.5
+    ko = O.l2norm(ko.reshape(n, nk, dk).float()).transpose(0, 1)
+    vo = vo.reshape(n, nv, dv).float().transpose(0, 1)
+    bo = torch.sigmoid(proj[:, C:C + nv]).float().T
+    go = (-A_log.exp() * F.softplus(proj[:, C + nv:].float() + dt)).T
+    ro, rs, _ = O.delta_rule(qo.repeat_interleave(nv, 0), ko.repeat_interleave(nv, 0), vo, go, bo, state)
+    assert _rel(states[groups], rs) < 3e-2
+    if need_out:
+        assert _rel(outs[groups].view(n, nv, dv).transpose(0, 1), ro) < 3e-2
