@@ -571,12 +571,22 @@ __global__ void __launch_bounds__(128, 1) gdn_state_kernel(GdnScanArgs a, int n_
       state[(long)(c + 1) * a.dv + m] = S[nt][1];
       state[(long)c * a.dv + m + 8] = S[nt][2];
       state[(long)(c + 1) * a.dv + m + 8] = S[nt][3];
+    } else if (!transfer) {
+      float* dst = a.grp_buf + grp_idx;
+      *reinterpret_cast<float2*>(dst + (long)m * DK + c) = make_float2(S[nt][0], S[nt][1]);
+      *reinterpret_cast<float2*>(dst + (long)(m + 8) * DK + c) = make_float2(S[nt][2], S[nt][3]);
     } else {
-      float* dst = a.grp_buf + (transfer ? (long)a.nv * a.groups * grp_mat : 0) + grp_idx;
-      dst[(long)m * DK + c] = S[nt][0];
-      dst[(long)m * DK + c + 1] = S[nt][1];
-      dst[(long)(m + 8) * DK + c] = S[nt][2];
-      dst[(long)(m + 8) * DK + c + 1] = S[nt][3];
+      // P as split bf16 (hi [dk][dk] then lo [dk][dk]) in its fp32 slot: pass 2 streams it with cp.async
+      __nv_bfloat16* hi = reinterpret_cast<__nv_bfloat16*>(a.grp_buf + (long)a.nv * a.groups * grp_mat + grp_idx);
+      __nv_bfloat16* lo = hi + (long)DK * DK;
+      const float x[4] = {S[nt][0], S[nt][1], S[nt][2], S[nt][3]};
+      float hx[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) hx[e] = __bfloat162float(__float2bfloat16(x[e]));
+      *reinterpret_cast<uint32_t*>(hi + (long)m * DK + c) = pack2(hx[0], hx[1]);
+      *reinterpret_cast<uint32_t*>(hi + (long)(m + 8) * DK + c) = pack2(hx[2], hx[3]);
+      *reinterpret_cast<uint32_t*>(lo + (long)m * DK + c) = pack2(x[0] - hx[0], x[1] - hx[1]);
+      *reinterpret_cast<uint32_t*>(lo + (long)(m + 8) * DK + c) = pack2(x[2] - hx[2], x[3] - hx[3]);
     }
   }
 }
@@ -585,12 +595,21 @@ __global__ void __launch_bounds__(128, 1) gdn_state_kernel(GdnScanArgs a, int n_
 // Per (value head, 64-row slice of S^T): sequentially over the chunk groups, S_start(z + 1) = S_start(z) P_z + R_z
 // (written to start_buf for pass 3 in output mode); the last one is the final state. The product runs on the
 // tensor cores with split-bf16 operands (hi + lo; hi*hi + hi*lo + lo*hi), about fp32 accurate, so the state
-// never passes through a single bf16 rounding.
+// never passes through a single bf16 rounding. The next group's P halves stream in (cp.async, double buffer)
+// while the current group's product runs.
 constexpr int PP = DK + 8;        // pitch of the staged P halves
 struct PropSmem {
-  __nv_bfloat16 hi[DK * PP];
-  __nv_bfloat16 lo[DK * PP];
+  __nv_bfloat16 hi[2][DK * PP];
+  __nv_bfloat16 lo[2][DK * PP];
 };
+
+__device__ __forceinline__ void prop_issue(PropSmem& s, const __nv_bfloat16* src, int buf, int tid) {
+  for (int v = tid; v < DK * (DK / 8); v += 128) {
+    const int r = v / (DK / 8), c = (v % (DK / 8)) * 8;
+    cp_async16(&s.hi[buf][r * PP + c], src + (long)r * DK + c, true);
+    cp_async16(&s.lo[buf][r * PP + c], src + (long)DK * DK + (long)r * DK + c, true);
+  }
+}
 
 __global__ void __launch_bounds__(128, 1) gdn_group_prop_kernel(GdnScanArgs a, int write_starts) {
   extern __shared__ __align__(16) uint8_t pp_raw[];
@@ -602,7 +621,7 @@ __global__ void __launch_bounds__(128, 1) gdn_group_prop_kernel(GdnScanArgs a, i
   float* state = a.state + (long)h * DK * a.dv;
   const long mat = (long)a.dv * DK;
   const float* R = a.grp_buf;
-  const float* P = a.grp_buf + (long)a.nv * a.groups * mat;
+  const float* Pbase = a.grp_buf + (long)a.nv * a.groups * mat;
   float S[16][4];
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt) {
@@ -612,28 +631,34 @@ __global__ void __launch_bounds__(128, 1) gdn_group_prop_kernel(GdnScanArgs a, i
     S[nt][2] = state[(long)c * a.dv + m + 8];
     S[nt][3] = state[(long)(c + 1) * a.dv + m + 8];
   }
+  prop_issue(s, reinterpret_cast<const __nv_bfloat16*>(Pbase + (long)h * a.groups * mat), 0, tid);
+  cp_async_commit();
   for (int z = 0; z < a.groups; ++z) {
     const long idx = ((long)h * a.groups + z) * mat;
+    const int buf = z & 1;
+    if (z + 1 < a.groups)
+      prop_issue(s, reinterpret_cast<const __nv_bfloat16*>(Pbase + idx + mat), buf ^ 1, tid);
+    cp_async_commit();
     if (write_starts) {
       float* sp = a.start_buf + idx;
 #pragma unroll
       for (int nt = 0; nt < 16; ++nt) {
         const int m = m0 + mrow + g, c = nt * 8 + 2 * t;
-        sp[(long)m * DK + c] = S[nt][0];
-        sp[(long)m * DK + c + 1] = S[nt][1];
-        sp[(long)(m + 8) * DK + c] = S[nt][2];
-        sp[(long)(m + 8) * DK + c + 1] = S[nt][3];
+        *reinterpret_cast<float2*>(sp + (long)m * DK + c) = make_float2(S[nt][0], S[nt][1]);
+        *reinterpret_cast<float2*>(sp + (long)(m + 8) * DK + c) = make_float2(S[nt][2], S[nt][3]);
       }
     }
-    __syncthreads();   // the previous group's P halves are no longer read
-    for (int v = tid; v < DK * DK; v += 128) {
-      const int r = v / DK, c = v % DK;
-      const float x = P[idx + (long)r * DK + c];
-      const __nv_bfloat16 xh = __float2bfloat16(x);
-      s.hi[r * PP + c] = xh;
-      s.lo[r * PP + c] = __float2bfloat16(x - __bfloat162float(xh));
+    float acc[16][4];
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const int m = m0 + mrow + g, c = nt * 8 + 2 * t;
+      const float2 r0 = *reinterpret_cast<const float2*>(R + idx + (long)m * DK + c);
+      const float2 r1 = *reinterpret_cast<const float2*>(R + idx + (long)(m + 8) * DK + c);
+      acc[nt][0] = r0.x;
+      acc[nt][1] = r0.y;
+      acc[nt][2] = r1.x;
+      acc[nt][3] = r1.y;
     }
-    __syncthreads();
     // A fragments of S^T (hi and lo), K = dk in 8 steps of 16
     uint32_t ah[8][4], al[8][4];
 #pragma unroll
@@ -642,28 +667,20 @@ __global__ void __launch_bounds__(128, 1) gdn_group_prop_kernel(GdnScanArgs a, i
       for (int e = 0; e < 4; ++e) {
         const float* src = S[2 * ks + (e >> 1)];
         const float x0 = src[(e & 1) * 2], x1 = src[(e & 1) * 2 + 1];
-        const __nv_bfloat16 h0 = __float2bfloat16(x0), h1 = __float2bfloat16(x1);
-        ah[ks][e] = pack2(__bfloat162float(h0), __bfloat162float(h1));
-        al[ks][e] = pack2(x0 - __bfloat162float(h0), x1 - __bfloat162float(h1));
+        const float h0 = __bfloat162float(__float2bfloat16(x0)), h1 = __bfloat162float(__float2bfloat16(x1));
+        ah[ks][e] = pack2(h0, h1);
+        al[ks][e] = pack2(x0 - h0, x1 - h1);
       }
     }
-    float acc[16][4];
-#pragma unroll
-    for (int nt = 0; nt < 16; ++nt) {
-      const int m = m0 + mrow + g, c = nt * 8 + 2 * t;
-      const float* rr = R + idx;
-      acc[nt][0] = rr[(long)m * DK + c];
-      acc[nt][1] = rr[(long)m * DK + c + 1];
-      acc[nt][2] = rr[(long)(m + 8) * DK + c];
-      acc[nt][3] = rr[(long)(m + 8) * DK + c + 1];
-    }
+    cp_async_wait<1>();
+    __syncthreads();
 #pragma unroll
     for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
       for (int j2 = 0; j2 < 8; ++j2) {
         uint32_t bh[4], bl[4];
-        ldb_kn(bh, s.hi, PP, j2 * 16, ks * 16, lane);   // B[k = row of P][n = col of P]
-        ldb_kn(bl, s.lo, PP, j2 * 16, ks * 16, lane);
+        ldb_kn(bh, s.hi[buf], PP, j2 * 16, ks * 16, lane);   // B[k = row of P][n = col of P]
+        ldb_kn(bl, s.lo[buf], PP, j2 * 16, ks * 16, lane);
         mma_bf16(acc[2 * j2], ah[ks], bh[0], bh[1]);
         mma_bf16(acc[2 * j2 + 1], ah[ks], bh[2], bh[3]);
         mma_bf16(acc[2 * j2], ah[ks], bl[0], bl[1]);
@@ -672,11 +689,13 @@ __global__ void __launch_bounds__(128, 1) gdn_group_prop_kernel(GdnScanArgs a, i
         mma_bf16(acc[2 * j2 + 1], al[ks], bh[2], bh[3]);
       }
     }
+    __syncthreads();   // buffer `buf` is refilled by the next iteration's prefetch
 #pragma unroll
     for (int nt = 0; nt < 16; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) S[nt][e] = acc[nt][e];
   }
+  cp_async_wait<0>();
 #pragma unroll
   for (int nt = 0; nt < 16; ++nt) {
     const int m = m0 + mrow + g, c = nt * 8 + 2 * t;
