@@ -130,7 +130,9 @@ def main():
     ap.add_argument("--split", type=int)
     ap.add_argument("--exact", action="store_true", help="also time full (exact) prefill for the speedup")
     ap.add_argument("--parallel", default="tp", choices=("tp", "dp"))
-    ap.add_argument("--tp-comm", default="nccl", choices=("nccl", "fused", "nvls"))
+    ap.add_argument("--tp-comm", default="nvls", choices=("nccl", "fused", "nvls"),
+                    help="tensor-parallel collectives: nvls (fused GEMM + NVSwitch multicast kernels; falls back to "
+                         "nccl where the GPUs offer no multicast), nccl (baseline), fused (peer stores)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -160,7 +162,14 @@ def main():
     tp = None
     if tp_mode:
         from ridgefill_data_b200.parallel.tp import TensorParallel, shard
-        tp = TensorParallel(mode=args.tp_comm)
+        try:
+            tp = TensorParallel(mode=args.tp_comm)
+        except Exception as e:                       # no NVSwitch multicast here: the NCCL baseline
+            if args.tp_comm != "nvls":
+                raise
+            print(f"nvls unavailable ({e}); using nccl", file=sys.stderr)
+            args.tp_comm = "nccl"
+            tp = TensorParallel(mode="nccl")
         shard(model, tp)
     ids_host = uniform_prompt(args.seq, cfg.vocab, seed=2 + (0 if tp_mode else rank)).pin_memory()
     ids_dev = ids_host.to(device)

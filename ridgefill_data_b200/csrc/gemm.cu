@@ -18,7 +18,8 @@
 // stored into other GPUs' buffers) and kEpiNvlsAR: the tensor-parallel row-parallel product fused with its
 // all-reduce. The CTA then has 10 warps: the comm warps reduce the row blocks this rank owns through the
 // NVSwitch (multimem.ld_reduce / multimem.st) as soon as every rank's epilogues have finished them, while the
-// other warps keep computing later tiles (row blocks are computed in order). Warps 6-9 are the comm warps.
+// other warps keep computing later tiles (the grouped tile order finishes row blocks 16 at a time; a row-major
+// order measured slower). Warps 6-9 are the comm warps.
 #include "gemm.h"
 #include "kernels.h"
 #include "ptx.cuh"
@@ -86,23 +87,6 @@ __device__ __forceinline__ TileCoord tile_coord(int t, int num_mb, int num_nb, i
   return c;
 }
 
-// kEpiNvlsAR walks row blocks in order (all N tiles of row block 0, then 1, ...): blocks finish one after another
-// while the grid sweeps, so the comm warps start on the first block after about one wave instead of at the end
-// of a 16-block group; the weights stay in L2 across row blocks and a row block's A tile is shared by the N tiles
-// running at the same time.
-template <int EPI>
-__device__ __forceinline__ TileCoord tile_coord_for(int t, int num_mb, int num_nb, int k_splits) {
-  if constexpr (EPI == kEpiNvlsAR) {
-    TileCoord c;
-    c.ks = 0;
-    c.mb = t / num_nb;
-    c.nb = t % num_nb;
-    return c;
-  } else {
-    return tile_coord(t, num_mb, num_nb, k_splits);
-  }
-}
-
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
 template <int BN, int EPI, bool A_MN, bool B_MN>
@@ -160,7 +144,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
       uint32_t issued = 0, last_par = 0;   // per stage: a load was issued / parity of its phase
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        TileCoord tc = tile_coord_for<EPI>(t, num_mb, num_nb, args.k_splits);
+        TileCoord tc = tile_coord(t, num_mb, num_nb, args.k_splits);
         const int k0 = tc.ks * args.k_chunk;
         const int k1 = min(args.K, k0 + args.k_chunk);
         const int nkb = (k1 - k0 + BK - 1) / BK;
@@ -206,7 +190,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
     int it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
-      TileCoord tc = tile_coord_for<EPI>(t, num_mb, num_nb, args.k_splits);
+      TileCoord tc = tile_coord(t, num_mb, num_nb, args.k_splits);
       const int k0 = tc.ks * args.k_chunk;
       const int k1 = min(args.K, k0 + args.k_chunk);
       const int nkb = (k1 - k0 + BK - 1) / BK;
@@ -258,7 +242,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
     const int row_in_tile = q * 32 + lane;
     int it = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
-      TileCoord tc = tile_coord_for<EPI>(t, num_mb, num_nb, args.k_splits);
+      TileCoord tc = tile_coord(t, num_mb, num_nb, args.k_splits);
       const uint32_t buf = it & 1;
       const uint32_t aphase = (it >> 1) & 1;
       if (*abort_flag || !mbar_wait(&tfull[buf], aphase, args.err, kErrTimeoutEpilogue)) {
@@ -530,7 +514,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
       const int nbatch = s_batch;
       named_bar_sync(1, CT);
       if (!ok) break;
-      const long total = (long)nbatch * slice;
+      const long total = nv.comm_off ? 0 : (long)nbatch * slice;
       for (long j0 = ct; j0 < total; j0 += (long)CT * kCommUnroll) {
         uint4 v[kCommUnroll];
         long off[kCommUnroll];

@@ -45,6 +45,7 @@ struct NvlsGemmArgs {
   int* rb_count;            // local per-row-block tile counters (zero between launches)
   int* done_count;          // local CTA counter (zero between launches)
   int max_mb;               // row blocks the flag array holds
+  int comm_off;             // diagnostics: announce and barrier but move no data (times the GEMM part alone)
 };
 
 struct GemmOperands {

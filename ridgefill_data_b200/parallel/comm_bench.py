@@ -121,10 +121,15 @@ def main(argv=None):
         check_errors()
         ferr = float((want - got_split).abs().max() / got_split.abs().max())
         t2 = _time(lambda: rp(y, w, h))
+        rp.comm_off = True
+        t2_gemm_part = _time(lambda: rp(y, w, h))
+        rp.comm_off = False
+        t_gemm_symm = _time(lambda: G.linear(y, w, out=part))
         t_gemm = _time(lambda: G.linear(y, w))
         flops = 2 * rows * d * a.k
         roof2 = max(flops / (GEMM_TFLOPS * 1e12), S / (LINK_GBS * 1e9)) * 1e3
         out.append(dict(case="gemm+allreduce", rows=rows, d=d, k=a.k, world=world, gemm_ms=round(t_gemm, 4),
+                        gemm_into_symmetric_ms=round(t_gemm_symm, 4), fused_comm_off_ms=round(t2_gemm_part, 4),
                         nccl_ms=round(t1, 4), nvls_two_kernels_ms=round(t2s, 4), nvls_fused_ms=round(t2, 4),
                         fused_vs_two_kernel_max_rel_diff=ferr, roofline_ms=round(roof2, 4),
                         nvls_fused_frac_of_roofline=round(roof2 / t2, 3)))

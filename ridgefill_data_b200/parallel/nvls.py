@@ -57,7 +57,9 @@ class _NvlsBase:
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
-        self.flags = _Symm(FLAG_WORDS, torch.int32, group, need_multicast=False)
+        # the flag words need no multicast address, but asking for one fails here (at construction) on GPUs
+        # without NVSwitch multicast, so callers can fall back before any layer runs
+        self.flags = _Symm(FLAG_WORDS, torch.int32, group, need_multicast=True)
         self.flags.t.zero_()
         torch.cuda.synchronize()
         dist.barrier(group=group)
@@ -77,6 +79,7 @@ class NvlsRowParallel(_NvlsBase):
     max_ctas = 32          # the all-reduce saturates the switch with 32 CTAs of 512 threads (measured at TP 2 / 8)
     acc32 = True
     fused_gemm = True      # one kernel: GEMM tiles + per-row-block reduction by the comm warps (kEpiNvlsAR)
+    comm_off = False       # diagnostics only: the fused kernel moves no data (times its GEMM part)
 
     def __init__(self, group=None):
         super().__init__(group)
@@ -136,7 +139,7 @@ class NvlsRowParallel(_NvlsBase):
         self.turn = (self.turn + 1) % len(self.outs)
         ext().gemm_nvls_ar(y, w, h if self.rank == 0 else None, part, self.part.mc, out.mc,
                            self.ar_flags.ptrs[self.rank], self.ar_flags.ptrs, self.rank, self.ar_epoch, self.counters,
-                           self.max_mb, 256 if d % 256 == 0 else 128, 0, self.err)
+                           self.max_mb, 256 if d % 256 == 0 else 128, 0, self.err, self.comm_off)
         return out.t[:rows * d].view(rows, d)
 
 
