@@ -41,11 +41,11 @@ def grouped(xp, w, seg, tiles, swiglu):
     return out
 
 
-def combine(h, y, pos, w, ys=None, gate_logit=None, n=None, d=None):
-    """h (or zeros when h is None) + sum_k w y[pos] (+ sigmoid(gate) ys)."""
-    if h is not None:
+def combine(h, y, pos, w, ys=None, gate_logit=None, n=None, d=None, out=None):
+    """h (or zeros when h is None) + sum_k w y[pos] (+ sigmoid(gate) ys), into `out` when given."""
+    if out is None and h is not None:
         out = torch.empty_like(h)
-    else:
+    elif out is None:
         out = torch.empty(n, d, dtype=torch.bfloat16, device=y.device)
     ext().moe_combine(h, y, pos, w, ys, gate_logit, out)
     return out

@@ -5,7 +5,8 @@ Rank r owns experts [r E / N, (r + 1) E / N). Every rank routes all tokens (the 
 (token, slot) pairs whose expert it owns, gathers those rows expert-sorted, runs its experts on the grouped
 tcgen05 GEMM and forms its partial sum_k w y for every token; rank 0 also adds the residual and the gated shared
 expert. The partials are summed over ranks (the expert combine) with the tensor-parallel reduction: NCCL
-all-reduce, or the peer-memory reduce/gather of parallel/fused.py. With replicated activations this moves one
+all-reduce, or (nvls mode) the combine writes straight into the symmetric partial buffer and the NVSwitch multicast
+all-reduce of parallel/nvls.py sums it. With replicated activations this moves one
 [tokens, d] all-reduce per MoE layer instead of an all-to-all dispatch of up to top_k copies of each row.
 """
 from __future__ import annotations
@@ -44,11 +45,17 @@ class ExpertParallel:
         xp, pos, seg, tiles = MO.align(idx, self.E_local, x, e0=self.e0)
         act = MO.grouped(xp, w["experts_gu_p"], seg, tiles, swiglu=True)
         y = MO.grouped(act, w["experts_down"], seg, tiles, swiglu=False)
+        nvls = getattr(self.tp, "fused", None) if self.world > 1 else None
+        nvls = nvls if hasattr(nvls, "allreduce_") else None
+        rows, d = h.shape
+        out = nvls.partial_view(rows, d) if nvls is not None else None   # combine straight into the symmetric buffer
         if self.rank == 0:
             ys = G.linear(G.swiglu_linear(x, w["sh_gu_p"]), w["sh_down"])
-            part = MO.combine(h, y, pos, wts, ys, logits[:, E])
+            part = MO.combine(h, y, pos, wts, ys, logits[:, E], out=out)
         else:
-            part = MO.combine(None, y, pos, wts, n=h.shape[0], d=h.shape[1])
+            part = MO.combine(None, y, pos, wts, n=rows, d=d, out=out)
+        if nvls is not None:
+            return nvls.allreduce_(rows, d)                              # NVSwitch multicast all-reduce
         if self.world > 1:
             dist.all_reduce(part, group=self.group)
         return part
