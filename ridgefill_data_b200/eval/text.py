@@ -44,7 +44,32 @@ def _need(path):
 
 # ------------------------------------------------------------------------------------- tokenizer helpers
 
+class _Encoding(dict):
+    __getattr__ = dict.__getitem__
+
+
+class CharTokenizer:
+    """Dry-run tokenizer without files: one id per character (code point + 10, ids below 10 reserved: 1 BOS,
+    2 EOS), offsets, decode and a minimal chat template. For tiny random models only."""
+    bos_token_id, eos_token_id = 1, 2
+
+    def __call__(self, text, add_special_tokens=True, return_offsets_mapping=False):
+        enc = _Encoding(input_ids=([1] if add_special_tokens else []) + [ord(c) + 10 for c in text])
+        if return_offsets_mapping:
+            enc["offset_mapping"] = [(i, i + 1) for i in range(len(text))]
+        return enc
+
+    def decode(self, ids, skip_special_tokens=False):
+        return "".join(chr(int(i) - 10) for i in ids if int(i) >= 10)
+
+    def apply_chat_template(self, msgs, tokenize=False, add_generation_prompt=True, **_):
+        return "<u>" + msgs[0]["content"] + "</u><a>"
+
+
 def tokenizer(model_path):
+    """The model's tokenizer (transformers, local files); "char" gives the dry-run CharTokenizer."""
+    if str(model_path) == "char":
+        return CharTokenizer()
     from transformers import AutoTokenizer
     return AutoTokenizer.from_pretrained(str(model_path))
 

@@ -3,16 +3,25 @@
   python -m ridgefill_data_b200.evaluate CONFIG.json TASK
 
 CONFIG: {"model": preset or checkpoint dir, "seed": 0, "backend": "b200"|"torch", "arms": [arm specs]
-(engine/spec.py), "prompts": {"kind": "uniform"|"zipf"|"niah", "lengths": [...], "count": k, "seed": s},
-"out": results dir, "keep": scored rows}.
+(engine/spec.py), "prompts": {"kind": ..., "lengths": [...], "count": k, "seed": s}, "out": results dir, "keep":
+scored rows, "tokenizer": dir or "char" (text sets; default the model dir), "format": "raw"|"chat",
+"protocol": version (optional: the research-protocol checks of engine/protocol.py run first)}.
+Prompt kinds: token-id synthetic sets "uniform" | "zipf" | "niah" (no tokenizer), and the text sets "grade",
+"k20" (K20 NIAH; "variant": "mk4"), "niahg", "ruler", "longbench", "longppl", "twokey", "qfirst" (eval/text.py,
+eval/locked.py, eval/derived.py, eval/niahg.py; config keys of those modules: ruler_tasks, ruler_lengths,
+ruler_max_len, longbench_max_len, longppl_max_len, ...).
 TASK:
-  quality  per arm: filled late-layer K/V (and GDN state) relative error vs exact prefill, next-token KL and
-           top-1 agreement of the last `keep` rows
-  ppl      per arm: mean NLL of the last `keep` prompt tokens
-  niah     greedy decode after each arm's prefill; correct iff the needle's value ids are reproduced
-  decode   decode agreement vs exact (teacher-forced KL, top-1, first divergence)
-  speed    per arm: device-timed TTFT (CUDA events) and tokens/s
-Validation happens before any model is built (engine/spec.py); results carry a provenance block.
+  quality   per arm: filled late-layer K/V (and GDN state) relative error vs exact prefill, next-token KL and
+            top-1 agreement of the last `keep` rows
+  ppl       per arm: mean NLL of the last `keep` prompt tokens (graded prompts: the last 512, also over novel
+            tokens; long-prompt documents: the continuation)
+  niah      greedy decode after each arm's prefill; correct iff the needle's value is reproduced
+  generate  greedy decode up to the row's budget, decoded and scored by the set's metric (RULER, LongBench,
+            non-numeric NIAH, K20)
+  decode    decode agreement vs exact (teacher-forced KL, top-1, first divergence)
+  speed     per arm: device-timed TTFT (CUDA events) and tokens/s
+Validation happens before any model is built (engine/spec.py, engine/protocol.py); results carry a provenance
+block and are written atomically, one per prompt (a rerun skips finished prompts).
 """
 import argparse
 import json
@@ -23,11 +32,40 @@ from pathlib import Path
 import torch
 
 
-def prompts_of(cfg, vocab):
+TEXT_KINDS = ("grade", "k20", "niahg", "ruler", "longbench", "longppl", "twokey", "qfirst")
+
+
+def text_prompts(cfg, tok):
+    """Prompts of a text set for this tokenizer (ids as tensors)."""
+    from .eval import derived, locked, niahg
+    from .eval import text as TX
+    p = cfg.get("prompts", {})
+    kind, fmt = p["kind"], cfg.get("format", "raw")
+    if kind == "grade":
+        out = TX.grade_prompts(tok, fmt)
+    elif kind == "k20":
+        out = TX.niah_prompts(tok, fmt, variant=p.get("variant"))
+    elif kind == "niahg":
+        out = niahg.prompts(tok, fmt)
+    elif kind in ("twokey", "qfirst"):
+        man = locked.manifest()
+        out, _ = derived.prompts(kind, tok, fmt, man, cfg.get("ruler_max_len"), cfg.get("ruler_tasks"),
+                                 cfg.get("ruler_lengths"), cfg.get("ruler_max_new"))
+    else:
+        protocol = {"models": {Path(str(cfg["model"])).name: {"niah_format": fmt}}}
+        out, _ = locked.prompts(kind, tok, dict(cfg, niah_format=fmt), Path(str(cfg["model"])).name, protocol)
+    for q in out:
+        q["ids"] = torch.as_tensor(q["ids"], dtype=torch.long)
+    return out
+
+
+def prompts_of(cfg, vocab, tok=None):
     from .eval.data import uniform_prompt, zipf_ids
     from .eval.niah import DEPTHS, niah_prompt
     p = cfg.get("prompts", {})
     kind, seed = p.get("kind", "uniform"), p.get("seed", 2)
+    if kind in TEXT_KINDS:
+        return text_prompts(cfg, tok)
     out = []
     for n in p.get("lengths", [2048]):
         for j in range(p.get("count", 1)):
@@ -48,8 +86,19 @@ def _rel(a, b):
     return float((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-30))
 
 
+def score_generation(prm, text):
+    """The row's own metric on a decoded continuation."""
+    from .eval import locked, niahg
+    from .eval import text as TX
+    if prm.get("set") in ("ruler", "longbench"):
+        return locked.score(prm, text)
+    if "type" in prm:                                   # non-numeric NIAH
+        return niahg.score(text, prm["value"], prm["type"], prm.get("format", "raw"))
+    return dict(pred=text, score=float(TX.niah_correct(text, prm["value"])))
+
+
 @torch.no_grad()
-def run_prompt(model, arms, prm, task, keep):
+def run_prompt(model, arms, prm, task, keep, tok=None):
     from .engine.decode import greedy
     from .engine.prefill import finish, run_lower
     from .engine.scoring import decode_agreement, kl, score_tokens, top1_agree
@@ -78,7 +127,17 @@ def run_prompt(model, arms, prm, task, keep):
             r.update(kv_rel_err=errs, kl=float(kl(exact_logits, logits).mean()),
                      top1=float(top1_agree(exact_logits, logits).mean()))
         elif task == "ppl":
-            r["nll"] = float(-score_tokens(logits, ids, keep - 1).double().mean())
+            lp = score_tokens(logits, ids, keep - 1).double()
+            r["nll"] = float(-lp.mean())
+            novel = prm.get("novel")
+            if novel is not None and len(novel) == keep - 1:
+                m = torch.tensor(novel, dtype=torch.bool)
+                r["nll_novel"] = float(-lp[m].mean()) if bool(m.any()) else None
+        elif task == "generate":
+            steps = int(prm.get("max_new", 32))
+            gen, reason = greedy(model, ids, cache, logits, steps, arm, eos=tuple(getattr(model, "eos_ids", ()) or ()))
+            text = tok.decode(gen, skip_special_tokens=False) if tok is not None else ""
+            r.update(gen=gen, finish_reason=reason, **score_generation(prm, text))
         elif task == "niah":
             from .eval.niah import niah_correct
             gen, reason = greedy(model, ids, cache, logits, len(prm["value"]) + 4, arm)
@@ -92,7 +151,7 @@ def run_prompt(model, arms, prm, task, keep):
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("config")
-    ap.add_argument("task", choices=("quality", "ppl", "niah", "decode", "speed"))
+    ap.add_argument("task", choices=("quality", "ppl", "niah", "generate", "decode", "speed"))
     a = ap.parse_args(argv)
     from .engine import spec
     from .models.base import from_config, load
@@ -101,6 +160,14 @@ def main(argv=None):
     cfg = spec.load(a.config)
     mcfg = PRESETS[cfg["model"]] if cfg["model"] in PRESETS else ModelConfig.from_dir(cfg["model"])
     spec.validate(cfg, mcfg.n_layers)
+    stamp = None
+    if cfg.get("protocol"):
+        from .engine import protocol
+        stamp = protocol.validate(cfg, set_name=cfg.get("prompts", {}).get("kind"))
+    tok = None
+    if cfg.get("prompts", {}).get("kind") in TEXT_KINDS or a.task == "generate":
+        from .eval.text import tokenizer
+        tok = tokenizer(cfg.get("tokenizer", cfg["model"]))
     dev = cfg.get("device", "cuda" if torch.cuda.is_available() else "cpu")
     backend = cfg.get("backend", "b200" if dev.startswith("cuda") else "torch")
     dtype = torch.float32 if cfg.get("dtype") == "fp32" else torch.bfloat16
@@ -112,7 +179,14 @@ def main(argv=None):
     arms = [spec.arm_of(s, dev, cache) for s in cfg["arms"]]
     out = Path(cfg.get("out", "results")) / a.task
     keep = cfg.get("keep", 16)
-    for prm in prompts_of(cfg, mcfg.vocab):
+    prompts = prompts_of(cfg, mcfg.vocab, tok)
+    if cfg.get("prompts", {}).get("kind") == "longppl":        # every scored row inside every arm's exact tail
+        from .eval.locked import check_tails
+
+        def tail_of(arm):
+            return lambda q: len(q["ids"]) - (arm.prefix_len(len(q["ids"])) if arm.split is not None else 0)
+        check_tails(prompts, {arm.name: tail_of(arm) for arm in arms})
+    for prm in prompts:
         path = out / f"{prm['name']}.json"
         if path.exists():
             continue
@@ -136,8 +210,13 @@ def main(argv=None):
                     ms = (time.time() - t0) * 1e3
                 rec["runs"][arm.name] = dict(ttft_ms=ms, tok_s=ids.shape[0] / ms * 1e3)
         else:
-            rec = run_prompt(model, arms, prm, a.task, keep)
-        rec["provenance"] = prov.provenance(cfg["model"], dict(task=a.task))
+            k = keep
+            if a.task == "ppl" and "cont_len" in prm:
+                k = prm["cont_len"] + 1                   # long-prompt documents: the whole continuation
+            elif a.task == "ppl" and "novel" in prm:
+                k = len(prm["novel"]) + 1                 # graded prompts: the scored window
+            rec = run_prompt(model, arms, prm, a.task, k, tok)
+        rec["provenance"] = prov.provenance(cfg["model"], dict(task=a.task, protocol=stamp))
         prov.write_json(path, rec)
         print(json.dumps({k: v for k, v in rec.items() if k != "provenance"})[:400])
     return 0

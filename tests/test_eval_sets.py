@@ -199,3 +199,32 @@ def test_niahg_prompts_and_scoring():
     assert NG.score("<think>x</think>\n\"3F9A 77\"", "3f9a77", "hexid", "chat")["correct"]
     assert NG.score("", "x", "name", "chat")["form"] == "none"
     assert NG.edit_distance("kitten", "sitting") == 3
+
+
+def test_evaluate_cli_on_locked_sets(tmp_path, locked_root, tiny_llama):
+    """The evaluation CLI on the synthetic locked set with the dry-run character tokenizer: RULER generation
+    scored by RULER's metric and long-prompt NLL over the continuation, per arm, one result file per prompt."""
+    from ridgefill_data_b200 import evaluate
+    path, _ = tiny_llama
+    arms = [dict(name="exact"), dict(name="identity", split=2, tail=64, fill="identity")]
+    base = dict(model=str(path), tokenizer="char", device="cpu", backend="torch", dtype="fp32", arms=arms,
+                format="raw", ruler_tasks=["niah_multikey_1"], ruler_lengths=[8192],
+                ruler_max_new={"niah_multikey_1": 3})
+    cfg = dict(base, prompts=dict(kind="ruler"), out=str(tmp_path / "ruler"))
+    (tmp_path / "ruler.json").write_text(json.dumps(cfg))
+    assert evaluate.main([str(tmp_path / "ruler.json"), "generate"]) == 0
+    recs = sorted((tmp_path / "ruler" / "generate").glob("*.json"))
+    assert len(recs) == 3
+    r = json.loads(recs[0].read_text())
+    for arm in ("exact", "identity"):
+        run = r["runs"][arm]
+        assert len(run["gen"]) == 3 and run["metric"] == "string_match_all" and 0.0 <= run["score"] <= 1.0
+    cfg = dict(base, prompts=dict(kind="longppl"), out=str(tmp_path / "lp"))
+    (tmp_path / "lp.json").write_text(json.dumps(cfg))
+    with pytest.raises(SystemExit, match="exact tail"):        # tail 64 < continuation 200 + 1
+        evaluate.main([str(tmp_path / "lp.json"), "ppl"])
+    cfg["arms"] = [dict(name="exact"), dict(name="identity", split=2, tail=256, fill="identity")]
+    (tmp_path / "lp.json").write_text(json.dumps(cfg))
+    assert evaluate.main([str(tmp_path / "lp.json"), "ppl"]) == 0
+    r = json.loads(next((tmp_path / "lp" / "ppl").glob("*.json")).read_text())
+    assert all(r["runs"][a]["nll"] > 0 for a in ("exact", "identity"))
