@@ -609,6 +609,55 @@ void nvls_barrier_b(int64_t flags_local, std::vector<int64_t> flag_peers, int64_
   rf::nvls_barrier(nvls_flags_of(flags_local, flag_peers, rank), (int)slot, (int)epoch, err.data_ptr<int>(), cur());
 }
 
+void row_cosine_b(Tensor a, Tensor b, Tensor out, double eps) {
+  need(a, at::kBFloat16, "a");
+  need(b, at::kBFloat16, "b");
+  need(out, at::kFloat, "out");
+  TORCH_CHECK(a.dim() == 2 && b.sizes() == a.sizes() && a.stride(1) == 1 && b.stride(1) == 1 &&
+                  out.numel() == a.size(0),
+              "row_cosine: a, b [rows, d] with unit column stride, out [rows]");
+  rf::row_cosine(cbf(a), a.stride(0), cbf(b), b.stride(0), a.size(0), (int)a.size(1), (float)eps,
+                 out.data_ptr<float>(), cur());
+}
+
+void window_mass_b(Tensor q, Tensor k, Tensor qpos, double scale, Tensor mass, Tensor part_m, Tensor part_l, Tensor qm,
+                   Tensor ql) {
+  need(q, at::kBFloat16, "q");
+  need(k, at::kBFloat16, "k");
+  TORCH_CHECK(q.dim() == 3 && k.dim() == 3 && q.size(2) == k.size(2) && q.stride(2) == 1 && k.stride(2) == 1,
+              "window_mass: q [hq, w, hd], k [hkv, n, hd]");
+  const int hd = (int)q.size(2);
+  TORCH_CHECK(hd % 16 == 0 && hd <= 256 && q.stride(1) % 8 == 0 && q.stride(0) % 8 == 0 && k.stride(1) % 8 == 0 &&
+                  k.stride(0) % 8 == 0 && q.size(0) % k.size(0) == 0,
+              "window_mass: head_dim a multiple of 16 (<= 256), 16-byte aligned rows, GQA");
+  TORCH_CHECK(qpos.scalar_type() == at::kInt && qpos.numel() == q.size(1), "window_mass: int32 qpos [w]");
+  TORCH_CHECK(mass.scalar_type() == at::kDouble && mass.numel() >= k.size(1), "window_mass: fp64 mass [n]");
+  rf::WindowMassArgs a{};
+  a.q = cbf(q);
+  a.q_head_stride = q.stride(0);
+  a.q_row_stride = q.stride(1);
+  a.k = cbf(k);
+  a.k_head_stride = k.stride(0);
+  a.k_row_stride = k.stride(1);
+  a.qpos = qpos.data_ptr<int>();
+  a.hq = (int)q.size(0);
+  a.hkv = (int)k.size(0);
+  a.w = (int)q.size(1);
+  a.n = (int)k.size(1);
+  a.hd = hd;
+  a.scale = (float)scale;
+  const long nblk = (a.n + 63) / 64;
+  TORCH_CHECK(part_m.numel() >= (long)a.hq * a.w * nblk && part_l.numel() >= (long)a.hq * a.w * nblk &&
+                  qm.numel() >= (long)a.hq * a.w && ql.numel() >= (long)a.hq * a.w,
+              "window_mass: scratch sizes");
+  a.part_m = part_m.data_ptr<float>();
+  a.part_l = part_l.data_ptr<float>();
+  a.qm = qm.data_ptr<float>();
+  a.ql = ql.data_ptr<float>();
+  a.mass = mass.data_ptr<double>();
+  rf::window_mass(a, cur());
+}
+
 void cholesky_solve_b(Tensor a, Tensor b, double shift, Tensor err) {
   need(a, at::kDouble, "a");
   need(b, at::kDouble, "b");
@@ -622,6 +671,8 @@ void cholesky_solve_b(Tensor a, Tensor b, double shift, Tensor err) {
 void register_comm(pybind11::module_& m) {
   m.def("cholesky_solve", &cholesky_solve_b);
   m.def("score_rows", &score_rows_b);
+  m.def("row_cosine", &row_cosine_b);
+  m.def("window_mass", &window_mass_b);
   m.def("nvls_allreduce", &nvls_allreduce_b);
   m.def("nvls_allgather", &nvls_allgather_b);
   m.def("nvls_barrier", &nvls_barrier_b);

@@ -139,6 +139,25 @@ struct ScoreArgs {
 };
 void score_rows(const ScoreArgs& a, cudaStream_t stream);
 
+// reduce.cu: read cosine of the lambda selection, window attention mass of the selectors
+void row_cosine(const __nv_bfloat16* a, long lda, const __nv_bfloat16* b, long ldb, long rows, int d, float eps,
+                float* out, cudaStream_t stream);
+struct WindowMassArgs {
+  const __nv_bfloat16* q;     // window queries [hq][w][hd] (post-RoPE)
+  long q_head_stride, q_row_stride;
+  const __nv_bfloat16* k;     // keys [hkv][n][hd] (post-RoPE, as cached)
+  long k_head_stride, k_row_stride;
+  const int* qpos;            // [w] positions of the window rows
+  int hq, hkv, w, n, hd;
+  float scale;
+  float* part_m;              // scratch [hq * w][key blocks]
+  float* part_l;
+  float* qm;                  // scratch [hq * w]
+  float* ql;
+  double* mass;               // [n], accumulated
+};
+void window_mass(const WindowMassArgs& a, cudaStream_t stream);
+
 // NVSwitch multicast collectives (nvls.cu). Flag words: slot * kMaxRanks + source rank, epoch-stamped.
 constexpr int kMaxRanksNvls = 8;
 struct NvlsFlags {

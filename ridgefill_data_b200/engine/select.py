@@ -187,6 +187,11 @@ def window_mass(model, win, cache, layers, end=None):
         qpos = torch.arange(e - w, e, device=k.device)
         q = model.queries(L, model.in_norm(h, model.W[L]["ln1"]), qpos)
         rep = q.shape[0] // hkv
+        if k.is_cuda and k.dtype == torch.bfloat16 and q.shape[-1] % 16 == 0:
+            from ..ops.kernels import window_mass as wm_kernel      # two-pass tensor-core kernel (csrc/reduce.cu)
+            acc = wm_kernel(q.to(torch.bfloat16), k, qpos, model.scale)
+            mass = acc if mass is None else mass + acc
+            continue
         mask = torch.arange(n, device=k.device)[None, :] > qpos[:, None]
         acc = torch.zeros(n, dtype=torch.float64, device=k.device)
         for gi in range(hkv):

@@ -138,3 +138,31 @@ def score_rows(logits, targets=None, ref=None):
     if ref is None:
         del out["kl"], out["ref_argmax"]
     return out
+
+
+def row_cosine(a, b, eps=1e-8):
+    """Cosine similarity of matching rows of a, b [..., d] (bf16) in fp32 on the device (csrc/reduce.cu)."""
+    d = a.shape[-1]
+    a2, b2 = a.reshape(-1, d), b.reshape(-1, d)
+    if a2.dtype != BF16:
+        a2, b2 = a2.to(BF16), b2.to(BF16)
+    a2, b2 = a2.contiguous() if a2.stride(-1) != 1 else a2, b2.contiguous() if b2.stride(-1) != 1 else b2
+    out = torch.empty(a2.shape[0], dtype=torch.float32, device=a.device)
+    ext().row_cosine(a2, b2, out, float(eps))
+    return out.view(a.shape[:-1])
+
+
+def window_mass(q, k, qpos, scale, mass=None):
+    """Attention mass [n] (fp64) that window queries q [hq, w, hd] at positions qpos [w] give every key of
+    k [hkv, n, hd] (causal, summed over heads and window rows); added into `mass` when given."""
+    hq, w, hd = q.shape
+    n = k.shape[1]
+    nblk = (n + 63) // 64
+    dev = q.device
+    f32 = dict(dtype=torch.float32, device=dev)
+    if mass is None:
+        mass = torch.zeros(n, dtype=torch.float64, device=dev)
+    ext().window_mass(q, k, qpos.to(dev, torch.int32).contiguous(), float(scale), mass,
+                      torch.empty(hq * w * nblk, **f32), torch.empty(hq * w * nblk, **f32),
+                      torch.empty(hq * w, **f32), torch.empty(hq * w, **f32))
+    return mass

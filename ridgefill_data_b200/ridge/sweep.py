@@ -96,6 +96,9 @@ def capture(model, docs, splits, device=None, log=print, group=None):
 def read_cos(model, i, pred, true):
     """Mean over the layer's read tensors of the per-row-per-head cosine (code/scripts/fit_sweep.py:308-312)."""
     p, t = model.reads(i, pred), model.reads(i, true)
+    if all(p[r].is_cuda and p[r].dtype == torch.bfloat16 for r in t):
+        from ..ops.kernels import row_cosine                         # one warp per row (csrc/reduce.cu)
+        return sum(row_cosine(p[r], t[r]).mean().item() for r in t) / len(t)
     return sum(F.cosine_similarity(p[r].float(), t[r].float(), dim=-1).mean().item() for r in t) / len(t)
 
 

@@ -60,3 +60,30 @@ def test_fill_tap_identity_and_maps():
     with attached(m, tap):
         prefill(m, ids, Arm("rf", split=split, tail=512, fill="proj", projector=proj), keep=1)
     assert max(tap.check_maps(hs[split], proj).values()) < 2e-2
+
+
+def test_row_cosine_matches_torch():
+    from ridgefill_data_b200.ops.kernels import row_cosine
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn(1000, 4, 128, device="cuda", generator=g).bfloat16()
+    b = (a.float() + 0.5 * torch.randn(1000, 4, 128, device="cuda", generator=g)).bfloat16()
+    got = row_cosine(a, b)
+    want = torch.nn.functional.cosine_similarity(a.float(), b.float(), dim=-1)
+    torch.testing.assert_close(got, want, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("hq,hkv,hd,n,w", [(8, 2, 128, 1000, 64), (24, 4, 256, 777, 64), (4, 4, 64, 130, 17)])
+def test_window_mass_matches_softmax_column_sums(hq, hkv, hd, n, w):
+    from ridgefill_data_b200.ops.kernels import window_mass
+    g = torch.Generator(device="cuda").manual_seed(4)
+    q = torch.randn(hq, w, hd, device="cuda", generator=g).bfloat16()
+    kbuf = torch.randn(hkv, n + 37, hd, device="cuda", generator=g).bfloat16()    # cache buffer with spare rows
+    k = kbuf[:, :n]
+    qpos = torch.arange(n - w, n, device="cuda")
+    scale = hd ** -0.5
+    got = window_mass(q, k, qpos, scale)
+    rep = hq // hkv
+    s = (q.float() @ k.float().repeat_interleave(rep, 0).transpose(1, 2)) * scale
+    s = s.masked_fill(torch.arange(n, device="cuda")[None, :] > qpos[:, None], float("-inf"))
+    want = torch.softmax(s, -1).sum((0, 1)).double()
+    torch.testing.assert_close(got, want, rtol=2e-3, atol=2e-4)
