@@ -379,7 +379,8 @@ void gemm_peer_b(Tensor a, Tensor b, c10::optional<Tensor> bias, std::vector<int
 // output buffers.
 void gemm_nvls_ar_b(Tensor a, Tensor b, c10::optional<Tensor> residual, Tensor out_part, int64_t mc_part,
                     int64_t mc_out, int64_t flags_local, std::vector<int64_t> flag_peers, int64_t rank, int64_t epoch,
-                    Tensor counters, int64_t max_mb, int64_t bn, int64_t max_ctas, Tensor err, bool comm_off) {
+                    Tensor counters, int64_t max_mb, int64_t bn, int64_t max_ctas, Tensor err, bool comm_off,
+                    int64_t comm_ctas) {
   need(a, at::kBFloat16, "a");
   need(b, at::kBFloat16, "b");
   TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out_part.stride(1) == 1, "gemm_nvls_ar: unit inner stride");
@@ -418,6 +419,7 @@ void gemm_nvls_ar_b(Tensor a, Tensor b, c10::optional<Tensor> residual, Tensor o
   nv.done_count = counters.data_ptr<int>() + max_mb;
   nv.max_mb = (int)max_mb;
   nv.comm_off = comm_off ? 1 : 0;
+  nv.comm_ctas = (int)comm_ctas;
   rf::gemm_bf16(op, args, rf::kEpiNvlsAR, (int)bn, (int)max_ctas, cur());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

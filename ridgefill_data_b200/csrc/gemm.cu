@@ -112,6 +112,16 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
   const int num_mb = (args.M + BM - 1) / BM;
   const int num_nb = (args.N + BN - 1) / BN;
   const int num_tiles = num_mb * num_nb * args.k_splits;
+  // kEpiNvlsAR with comm_ctas > 0: the last comm_ctas CTAs only move reduced rows (no tiles), the others only
+  // compute tiles, so the reduction traffic does not share SM ports with the GEMM's TMA loads
+  int tile_ctas = gridDim.x, comm_first = 0;
+  if constexpr (EPI == kEpiNvlsAR) {
+    if (args.nvls.comm_ctas > 0 && args.nvls.comm_ctas < (int)gridDim.x) {
+      tile_ctas = gridDim.x - args.nvls.comm_ctas;
+      comm_first = tile_ctas;
+    }
+  }
+  const int tile_begin = (int)blockIdx.x < tile_ctas ? (int)blockIdx.x : num_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -143,7 +153,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
       uint32_t stage = 0, phase = 0;
       uint32_t issued = 0, last_par = 0;   // per stage: a load was issued / parity of its phase
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = tile_begin; t < num_tiles && ok; t += tile_ctas) {
         TileCoord tc = tile_coord(t, num_mb, num_nb, args.k_splits);
         const int k0 = tc.ks * args.k_chunk;
         const int k1 = min(args.K, k0 + args.k_chunk);
@@ -189,7 +199,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
     uint32_t stage = 0, phase = 0;
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+    for (int t = tile_begin; t < num_tiles && ok; t += tile_ctas, ++it) {
       TileCoord tc = tile_coord(t, num_mb, num_nb, args.k_splits);
       const int k0 = tc.ks * args.k_chunk;
       const int k1 = min(args.K, k0 + args.k_chunk);
@@ -241,7 +251,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
     int it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+    for (int t = tile_begin; t < num_tiles; t += tile_ctas, ++it) {
       TileCoord tc = tile_coord(t, num_mb, num_nb, args.k_splits);
       const uint32_t buf = it & 1;
       const uint32_t aphase = (it >> 1) & 1;
@@ -488,7 +498,9 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
     const NvlsGemmArgs& nv = args.nvls;
     const int ct = threadIdx.x - 6 * 32;
     const int units_row = args.N / 8;
-    const long slice = ((long)BM * units_row + gridDim.x - 1) / gridDim.x;
+    const int comm_ctas = (int)gridDim.x - comm_first;            // CTAs sharing every row block
+    const int comm_idx = (int)blockIdx.x - comm_first;            // < 0: this CTA computes tiles only
+    const long slice = ((long)BM * units_row + comm_ctas - 1) / comm_ctas;
     const char* in = reinterpret_cast<const char*>(nv.mc_part);
     char* outp = reinterpret_cast<char*>(nv.mc_out);
     __shared__ int s_batch;
@@ -514,7 +526,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
       const int nbatch = s_batch;
       named_bar_sync(1, CT);
       if (!ok) break;
-      const long total = nv.comm_off ? 0 : (long)nbatch * slice;
+      const long total = (nv.comm_off || comm_idx < 0) ? 0 : (long)nbatch * slice;
       for (long j0 = ct; j0 < total; j0 += (long)CT * kCommUnroll) {
         uint4 v[kCommUnroll];
         long off[kCommUnroll];
@@ -524,7 +536,7 @@ __global__ void __launch_bounds__(GemmThreads<EPI>::value, 1)
           off[k] = -1;
           if (j < total) {
             const int b = (int)(j / slice);
-            const long u = (long)blockIdx.x * slice + (j - (long)b * slice);
+            const long u = (long)comm_idx * slice + (j - (long)b * slice);
             const int blk = mb + b * nv.world;
             const int r0 = blk * BM;
             const long nu = (long)(min(args.M, r0 + BM) - r0) * units_row;

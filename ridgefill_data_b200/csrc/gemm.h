@@ -46,6 +46,7 @@ struct NvlsGemmArgs {
   int* done_count;          // local CTA counter (zero between launches)
   int max_mb;               // row blocks the flag array holds
   int comm_off;             // diagnostics: announce and barrier but move no data (times the GEMM part alone)
+  int comm_ctas;            // > 0: that many trailing CTAs only reduce (the others only compute tiles)
 };
 
 struct GemmOperands {

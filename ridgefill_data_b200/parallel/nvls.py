@@ -80,6 +80,7 @@ class NvlsRowParallel(_NvlsBase):
     acc32 = True
     fused_gemm = True      # one kernel: GEMM tiles + per-row-block reduction by the comm warps (kEpiNvlsAR)
     comm_off = False       # diagnostics only: the fused kernel moves no data (times its GEMM part)
+    comm_ctas = 0          # > 0: CTAs dedicated to the reduction (the rest compute tiles); 0: every CTA does both
 
     def __init__(self, group=None):
         super().__init__(group)
@@ -139,7 +140,7 @@ class NvlsRowParallel(_NvlsBase):
         self.turn = (self.turn + 1) % len(self.outs)
         ext().gemm_nvls_ar(y, w, h if self.rank == 0 else None, part, self.part.mc, out.mc,
                            self.ar_flags.ptrs[self.rank], self.ar_flags.ptrs, self.rank, self.ar_epoch, self.counters,
-                           self.max_mb, 256 if d % 256 == 0 else 128, 0, self.err, self.comm_off)
+                           self.max_mb, 256 if d % 256 == 0 else 128, 0, self.err, self.comm_off, self.comm_ctas)
         return out.t[:rows * d].view(rows, d)
 
 
