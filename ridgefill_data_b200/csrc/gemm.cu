@@ -39,7 +39,7 @@ constexpr int BK = 64;
 constexpr int kGemmThreads = 192;
 
 constexpr int kCommWarps = 4;     // kEpiNvlsAR: warps 6..9 move the reduced rows
-constexpr int kCommUnroll = 8;    // 16-byte multimem loads in flight per comm thread
+constexpr int kCommUnroll = 8;    // 16-byte multimem loads in flight per comm thread (16 measured no faster)
 constexpr int kCommBatch = 8;     // owned row blocks reduced in one pass when they are already complete
 
 template <int EPI>

@@ -125,7 +125,7 @@ def main(argv=None):
         t2_gemm_part = _time(lambda: rp(y, w, h))
         rp.comm_off = False
         dedicated = {}
-        for cc in (16, 24, 32, 48):
+        for cc in (32, 64):
             rp.comm_ctas = cc
             dedicated[cc] = round(_time(lambda: rp(y, w, h)), 4)
             torch.cuda.synchronize()
