@@ -6,6 +6,8 @@
 
 #include "kernels.h"
 
+torch::Tensor& err_word(int dev);   // bindings.cpp: the per-device error word
+
 namespace {
 
 using at::Tensor;
@@ -88,7 +90,7 @@ void embed_gather(Tensor table, Tensor ids, Tensor out) {
   TORCH_CHECK(table.size(1) % 8 == 0, "embed_gather: d % 8");
   c10::cuda::CUDAGuard g(table.device());
   rf::embed_gather(cbf(table), ids.data_ptr<int64_t>(), bf(out), (int)ids.numel(), (int)table.size(1),
-                   (long)table.size(0), cur());
+                   (long)table.size(0), cur(), err_word(table.device().index()).data_ptr<int>());
 }
 
 void flash_attention(Tensor q, int64_t q_head_stride, Tensor k, Tensor v, int64_t kv_head_stride, Tensor out,

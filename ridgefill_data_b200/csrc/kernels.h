@@ -43,7 +43,8 @@ void gated_rmsnorm(const __nv_bfloat16* o, long ldo, const __nv_bfloat16* z, lon
                    __nv_bfloat16* y, long ldy, int rows, int heads, int dv, float eps, cudaStream_t stream);
 
 void embed_gather(const __nv_bfloat16* table, const int64_t* ids, __nv_bfloat16* out, int rows, int d, long vocab,
-                  cudaStream_t stream);
+                  cudaStream_t stream,
+                  int* err = nullptr);
 
 // ---- attention.cu
 struct AttnArgs {

@@ -6,6 +6,7 @@
 //   gated_rmsnorm     Gated DeltaNet output: per-head RMSNorm, times w, times silu(z)
 //   embed_gather      rows of the embedding table
 #include "kernels.h"
+#include "ptx.cuh"
 
 #include <cuda_bf16.h>
 
@@ -194,20 +195,26 @@ void gated_rmsnorm(const __nv_bfloat16* o, long ldo, const __nv_bfloat16* z, lon
 }
 
 // ------------------------------------------------------------------------------- embed_gather
+// An id outside [0, vocab) records kErrBadIndex and writes a zero row (the host raises on check_errors).
 __global__ void embed_gather_kernel(const __nv_bfloat16* __restrict__ table, const int64_t* __restrict__ ids,
-                                    __nv_bfloat16* __restrict__ out, int d, long vocab) {
+                                    __nv_bfloat16* __restrict__ out, int d, long vocab, int* err) {
   const long row = blockIdx.x;
-  long id = ids[row];
-  if (id < 0 || id >= vocab) id = 0;
-  const uint4* src = reinterpret_cast<const uint4*>(table + id * (long)d);
+  const long id = ids[row];
   uint4* dst = reinterpret_cast<uint4*>(out + row * (long)d);
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0 && err != nullptr) atomicMax(err, (int)kErrBadIndex);
+    for (int v = threadIdx.x; v < d / 8; v += blockDim.x) dst[v] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + id * (long)d);
   for (int v = threadIdx.x; v < d / 8; v += blockDim.x) dst[v] = src[v];
 }
 
 void embed_gather(const __nv_bfloat16* table, const int64_t* ids, __nv_bfloat16* out, int rows, int d, long vocab,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, int* err) {
   if (rows <= 0) return;
-  embed_gather_kernel<<<rows, 128, 0, stream>>>(table, ids, out, d, vocab); count_launch();
+  embed_gather_kernel<<<rows, 128, 0, stream>>>(table, ids, out, d, vocab, err);
+  count_launch();
 }
 
 }  // namespace rf

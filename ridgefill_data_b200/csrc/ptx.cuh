@@ -24,6 +24,7 @@ enum ErrCode : int {
   kErrTimeoutPeer = 4,
   kErrTimeoutDrain = 5,
   kErrBadShape = 6,
+  kErrBadIndex = 7,   // a gather index outside its table (the row is written as zeros)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -35,12 +35,18 @@ def available():
         return False
 
 
+ERROR_CODES = {1: "TMA producer wait timed out", 2: "MMA issuer wait timed out", 3: "epilogue wait timed out",
+               4: "peer flag wait timed out (a rank did not arrive)", 5: "drain wait timed out",
+               6: "unsupported shape", 7: "gather index outside its table"}
+
+
 def check_errors(device=None):
-    """Raise if any kernel recorded a bounded-wait timeout in the device error word; clears it."""
+    """Raise if any kernel recorded an error (a bounded wait that timed out, a bad shape or index) in the device
+    error word; clears it."""
     import torch
     dev = torch.cuda.current_device() if device is None else torch.device(device).index or 0
     w = ext().error_word(dev)
     code = int(w.item())
     if code:
         w.zero_()
-        raise RuntimeError(f"sm_100a kernel reported error code {code} (bounded wait timed out)")
+        raise RuntimeError(f"sm_100a kernel reported error code {code}: {ERROR_CODES.get(code, 'unknown')}")

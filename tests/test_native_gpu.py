@@ -87,3 +87,54 @@ def test_window_mass_matches_softmax_column_sums(hq, hkv, hd, n, w):
     s = s.masked_fill(torch.arange(n, device="cuda")[None, :] > qpos[:, None], float("-inf"))
     want = torch.softmax(s, -1).sum((0, 1)).double()
     torch.testing.assert_close(got, want, rtol=2e-3, atol=2e-4)
+
+
+def test_embedding_gather_reports_bad_ids():
+    from ridgefill_data_b200.ops import kernels as K
+    from ridgefill_data_b200.ops._ext import check_errors
+    table = torch.randn(50, 64, device="cuda").bfloat16()
+    out = K.embed(table, torch.tensor([3, 7], device="cuda"))
+    torch.testing.assert_close(out, table[[3, 7]])
+    check_errors()
+    bad = K.embed(table, torch.tensor([3, 99], device="cuda"))
+    torch.cuda.synchronize()
+    assert torch.equal(bad[1], torch.zeros_like(bad[1]))
+    with pytest.raises(RuntimeError, match="gather index"):
+        check_errors()
+
+
+@pytest.mark.parametrize("what", ["gemm", "attention", "gdn"])
+def test_kernels_are_deterministic(what):
+    """Run twice, bitwise equal (the determinism the reference's bitwise canaries rely on)."""
+    from ridgefill_data_b200.eval.checks import rerun_bitwise
+    from ridgefill_data_b200.ops import gemm as G
+    from ridgefill_data_b200.ops import kernels as K
+    g = torch.Generator(device="cuda").manual_seed(9)
+    if what == "gemm":
+        x = torch.randn(1000, 512, device="cuda", generator=g).bfloat16()
+        w = torch.randn(768, 512, device="cuda", generator=g).bfloat16()
+        fn = lambda: G.linear(x, w)  # noqa: E731
+    elif what == "attention":
+        q = torch.randn(8, 300, 128, device="cuda", generator=g).bfloat16()
+        k = torch.randn(2, 300, 128, device="cuda", generator=g).bfloat16()
+        v = torch.randn_like(k)
+
+        def fn():
+            out = torch.empty(300, 8 * 128, device="cuda", dtype=torch.bfloat16)
+            K.attention(q, k, v, 300, 128 ** -0.5, out)
+            return out
+    else:
+        n, nk, nv = 700, 1, 2
+        C = 2 * nk * 128 + nv * 128
+        proj = (torch.randn(n, C + 2 * nv, device="cuda", generator=g) * 0.5).bfloat16()
+        conv_w = (torch.randn(C, 4, device="cuda", generator=g) / 2).bfloat16()
+        q, kk, v, beta, gg = K.gdn_prep(proj, C, C + nv, conv_w, None, torch.rand(nv, device="cuda"),
+                                        torch.zeros(nv, device="cuda"), nk, nv, 128, 128)
+
+        def fn():
+            st = torch.zeros(nv, 128, 128, device="cuda")
+            out = torch.empty(n, nv * 128, device="cuda", dtype=torch.bfloat16)
+            K.gdn_scan(q, kk, v, beta, gg, st, out, groups=3)
+            return torch.cat((out.float().flatten(), st.flatten()))
+    same, _ = rerun_bitwise(fn)
+    assert same
