@@ -130,6 +130,9 @@ def main():
     ap.add_argument("--split", type=int)
     ap.add_argument("--exact", action="store_true", help="also time full (exact) prefill for the speedup")
     ap.add_argument("--parallel", default="tp", choices=("tp", "dp"))
+    ap.add_argument("--stages", action="store_true",
+                    help="after the timed steps, one extra step with per-stage device times (lower layers, fill, "
+                         "late layers) printed to stderr, max over ranks")
     ap.add_argument("--tp-comm", default="nvls", choices=("nccl", "fused", "nvls"),
                     help="tensor-parallel collectives: nvls (fused GEMM + NVSwitch multicast kernels; falls back to "
                          "nccl where the GPUs offer no multicast), nccl (baseline), fused (peer stores)")
@@ -208,6 +211,18 @@ def main():
         launches = ext().launch_count() - launches0
         clocks = sampler.stop()
         ms = t0.elapsed_time(t1) / args.steps
+
+        if args.stages:                          # diagnostics outside the timed region
+            from ridgefill_data_b200.utils.trace import StageTimer
+            timer = StageTimer()
+            with timer.stage("lower"):
+                hs, lower = run_lower(model, ids_dev, [arm.split])
+            with timer.stage("late"):
+                finish(model, ids_dev, hs[arm.split], lower, arm, keep=1, keep_cache=False, timer=timer)
+            del hs, lower
+            rep = timer.report()
+            if rank == 0:
+                print(json.dumps(dict(stages_ms={k: round(v, 3) for k, v in rep.items()})), file=sys.stderr)
 
         # ---- end to end through the public API: pinned H2D of the prompt, prefill, D2H of the first token
         barrier()

@@ -133,7 +133,7 @@ def _plain_batchable(arm, model, P, rows, fill_reuse, row0, fill_store):
 
 
 def finish(model, ids, h_split, lower_cache, arm, keep, oracle=None, keep_cache=True, fill_store=None,
-           fill_reuse=None, exact_rows=None, row_inputs=None, hook=None, mix=None):
+           fill_reuse=None, exact_rows=None, row_inputs=None, hook=None, mix=None, timer=None):
     """Layers >= arm.split for one arm. keep: number of final rows whose logits to return. Returns
     (logits [keep, V] fp32, cache, P). See the module doc and engine/arm.py for the options."""
     n = ids.shape[0]
@@ -175,7 +175,11 @@ def finish(model, ids, h_split, lower_cache, arm, keep, oracle=None, keep_cache=
     batched = _plain_batchable(arm, model, P, rows, fill_reuse, row0, fill_store)
     if batched:
         late = list(range(split, model.n_layers))
-        model.fill_batch(late, b, pos[:P], cache, arm.projector if arm.fill == "proj" else None)
+        if timer is not None:
+            with timer.stage("fill"):
+                model.fill_batch(late, b, pos[:P], cache, arm.projector if arm.fill == "proj" else None)
+        else:
+            model.fill_batch(late, b, pos[:P], cache, arm.projector if arm.fill == "proj" else None)
 
     for i in range(split, model.n_layers):
         if P > 0 and fill_reuse is not None:
