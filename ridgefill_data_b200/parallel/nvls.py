@@ -71,8 +71,13 @@ class _NvlsBase:
         return self.flag_local + 4 * idx
 
     def close(self):
+        """Drop this object's symmetric buffers (call before destroy_process_group)."""
         torch.cuda.synchronize()
-        self.flags = None
+        for name in ("flags", "part", "buf", "ar_flags"):
+            if hasattr(self, name):
+                setattr(self, name, None)
+        if hasattr(self, "outs"):
+            self.outs = []
 
 
 class NvlsRowParallel(_NvlsBase):
