@@ -78,6 +78,7 @@ class _NvlsBase:
                 setattr(self, name, None)
         if hasattr(self, "outs"):
             self.outs = []
+        self.cap = 0
 
 
 class NvlsRowParallel(_NvlsBase):
