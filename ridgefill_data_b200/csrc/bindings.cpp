@@ -6,6 +6,15 @@
 #include "gemm.h"
 #include "kernels.h"
 
+// One int32 error word per device: kernels with bounded waits (and gather bounds checks) record a code here.
+// Outside the anonymous namespace: bind_ops.cpp uses it too.
+torch::Tensor& err_word(int dev) {
+  static std::vector<torch::Tensor> words(64);
+  if (!words[dev].defined())
+    words[dev] = torch::zeros({1}, torch::dtype(torch::kInt32).device(torch::kCUDA, dev));
+  return words[dev];
+}
+
 namespace {
 
 #define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
@@ -13,13 +22,6 @@ namespace {
 
 cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
-// One int32 error word per device: kernels with bounded waits record a code here on timeout.
-torch::Tensor& err_word(int dev) {
-  static std::vector<torch::Tensor> words(64);
-  if (!words[dev].defined())
-    words[dev] = torch::zeros({1}, torch::dtype(torch::kInt32).device(torch::kCUDA, dev));
-  return words[dev];
-}
 
 int* err_ptr(const torch::Tensor& like) { return err_word(like.get_device()).data_ptr<int>(); }
 
