@@ -71,3 +71,24 @@ def test_noninferiority():
     assert none_worse.lo == pytest.approx(-100 * (1 - 0.05 ** (1 / 96)))
     with pytest.raises(ST.StatsError):
         ST.noninferiority(good)
+
+
+def test_paired_tables(tmp_path):
+    import json
+    from ridgefill_data_b200.eval import tables as TB
+    rng = np.random.default_rng(7)
+    for j in range(30):
+        base = float(rng.normal(2.0, 0.3))
+        runs = {"exact": {"nll": base}, "ridgefill": {"nll": base + 0.01 + float(rng.normal(0, 0.005))},
+                "identity": {"nll": base + 0.3 + float(rng.normal(0, 0.05))}}
+        (tmp_path / f"p{j}.json").write_text(json.dumps(dict(name=f"p{j}", runs=runs)))
+    (tmp_path / "broken.json").write_text(json.dumps(dict(name="b", runs={"exact": {"nll": float("nan")}})))
+    rows = TB.paired_table(TB.load_records(tmp_path), "nll", "exact", n_resamples=1000, upper=0.05)
+    by = {r["arm"]: r for r in rows}
+    assert by["ridgefill"]["n"] == 30 and by["ridgefill"]["lo"] < 0.01 < by["ridgefill"]["hi"]
+    assert by["ridgefill"]["noninferior"] and not by["identity"]["noninferior"]
+    assert by["identity"]["p_holm"] < 0.01
+    md = TB.markdown(rows, "nll", "exact")
+    assert md.count("\n") == 3 and "ridgefill" in md
+    tex = TB.latex(rows, "nll", "exact")
+    assert tex.startswith("\\begin{tabular}") and "\\checkmark" in tex
