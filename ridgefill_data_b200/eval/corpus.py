@@ -138,3 +138,54 @@ def write_tsv(path, rows, fields=None):
         w = csv.DictWriter(f, fieldnames=fields or list(rows[0]), delimiter="\t", extrasaction="ignore")
         w.writeheader()
         w.writerows(rows)
+
+
+def overlap_report(calib, evaluation, n=GRAM):
+    """Calibration-vs-evaluation overlap (the calibration exclusion check): for every calibration document
+    {name: text}, the number of its distinct word n-grams that also occur in any evaluation text, and the share of
+    its grams. Returns rows sorted by shared count (largest first)."""
+    ref = np.unique(np.concatenate([grams(t, n) for t in evaluation.values()])) if evaluation else np.zeros(0, np.uint64)
+    rows = []
+    for name, text in calib.items():
+        g = grams(text, n)
+        k = shared(g, ref)
+        rows.append(dict(name=name, grams=int(len(np.unique(g))), shared=k,
+                         share=k / max(1, len(np.unique(g)))))
+    return sorted(rows, key=lambda r: (-r["shared"], r["name"]))
+
+
+def _texts(paths):
+    out = {}
+    for p in paths:
+        p = Path(p)
+        files = sorted(p.rglob("*")) if p.is_dir() else [p]
+        for f in files:
+            if f.is_file() and f.suffix in (".txt", ".json", ".jsonl"):
+                raw = f.read_text(encoding="utf-8", errors="ignore")
+                if f.suffix == ".json":
+                    raw = "\n".join(strings_of(json.loads(raw)))
+                elif f.suffix == ".jsonl":
+                    raw = "\n".join(s for line in raw.splitlines() if line.strip() for s in strings_of(json.loads(line)))
+                out[str(f)] = raw
+    return out
+
+
+def main(argv=None):
+    import argparse
+    ap = argparse.ArgumentParser(description="calibration-vs-evaluation word n-gram overlap")
+    ap.add_argument("--calib", nargs="+", required=True, help="calibration files or directories")
+    ap.add_argument("--eval", nargs="+", required=True, help="evaluation files or directories")
+    ap.add_argument("--n", type=int, default=GRAM)
+    ap.add_argument("--tsv")
+    a = ap.parse_args(argv)
+    rows = overlap_report(_texts(a.calib), _texts(a.eval), a.n)
+    if a.tsv:
+        write_tsv(a.tsv, rows)
+    for r in rows:
+        print(f"{r['shared']}\t{r['share']:.4f}\t{r['name']}")
+    return 0
+
+
+if __name__ == "__main__":
+    import sys
+    sys.exit(main())

@@ -37,3 +37,17 @@ def test_tiny_checkpoints_load(tmp_path):
         logits, _ = m.forward_exact(torch.arange(12), keep=torch.tensor([11]))
         assert logits.shape[-1] == m.cfg.vocab and torch.isfinite(logits).all(), name
     assert load(paths["llama-3.1-swiftkv-8b-instruct"]).cfg.swift_layers == 4
+
+
+def test_overlap_report(tmp_path):
+    words = [f"w{i}" for i in range(200)]
+    (tmp_path / "calib").mkdir()
+    (tmp_path / "eval").mkdir()
+    (tmp_path / "calib" / "a.txt").write_text(" ".join(words[:120]))
+    (tmp_path / "calib" / "b.txt").write_text(" ".join(f"x{i}" for i in range(120)))
+    (tmp_path / "eval" / "e.jsonl").write_text('{"text": "%s"}\n' % " ".join(words[60:200]))
+    rows = CP.overlap_report(CP._texts([tmp_path / "calib"]), CP._texts([tmp_path / "eval"]), n=50)
+    assert rows[0]["name"].endswith("a.txt") and rows[0]["shared"] == 11 and rows[1]["shared"] == 0
+    assert CP.main(["--calib", str(tmp_path / "calib"), "--eval", str(tmp_path / "eval"), "--tsv",
+                    str(tmp_path / "o.tsv")]) == 0
+    assert len(CP.read_tsv(tmp_path / "o.tsv")) == 2
