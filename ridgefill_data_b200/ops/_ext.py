@@ -17,6 +17,7 @@ def ext():
     global _mod, _err
     if _mod is not None:
         return _mod
+    import torch  # noqa: F401  (loads libc10 / libtorch, which the extension links against)
     try:
         _mod = importlib.import_module("ridgefill_data_b200._C")
     except ImportError as e:  # pragma: no cover - depends on the build
