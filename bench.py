@@ -39,8 +39,13 @@ BASELINE_TOK_S = {"qwen3.8-27b": {16384: 16384 / 10.380, 32768: 32768 / 21.112, 
                   # Flash-Next RidgeFill TTFT medians (vLLM fork, TP2 on 2x AMD R9700): 9K / 16K / 32K
                   "flash-next": {9216: 9216 / 10.178, 16384: 16384 / 16.463, 32768: 32768 / 31.180}}
 METRIC = {"qwen3.8-27b": "prefill tok/s (RidgeFill TTFT), Qwen3.8-27B-shaped hybrid",
-          "flash-next": "prefill tok/s (RidgeFill TTFT), Flash-Next-shaped MoE hybrid"}
-DEFAULT_SPLIT_TAIL = {"qwen3.8-27b": (32, 4096), "flash-next": (24, 2048)}
+          "flash-next": "prefill tok/s (RidgeFill TTFT), Flash-Next-shaped MoE hybrid",
+          "llama-3.1-8b": "prefill tok/s (RidgeFill TTFT), Llama-3.1-8B-shaped dense model",
+          "qwen3-8b": "prefill tok/s (RidgeFill TTFT), Qwen3-8B-shaped dense model"}
+# the benchmark plan's configurations: 27B split 32 / tail 4096; MoE split 24 / tail 2048; Llama-8B split 16 /
+# tail 4096; Qwen3-8B split 18 (of its 12 / 18 / 24 sweep) / tail 4096
+DEFAULT_SPLIT_TAIL = {"qwen3.8-27b": (32, 4096), "flash-next": (24, 2048), "llama-3.1-8b": (16, 4096),
+                      "qwen3-8b": (18, 4096)}
 
 
 class ClockSampler:
