@@ -6,7 +6,8 @@
 //               keys past nk read as zeros)
 //   warp 1      UMMA issuer: S_j = Q K_j^T into one of two TMEM S buffers, then O += P_{j-1} V_{j-1} into the TMEM
 //               O accumulator (P from shared memory, V as an MN-major B operand)
-//   warps 2..5  softmax: thread = query row; S row from TMEM, causal mask, exp2 with the scale folded in, row sum;
+//   warps 2..5  softmax: thread = query row; S row from TMEM, causal mask (diagonal tiles only), one FMA + one ex2
+//               (special-function unit) per score with the scale folded in, row sum;
 //               O is rescaled in TMEM only when the row max grows by more than 2^8 (otherwise the stale max stays
 //               exact for both O and l); P rounded to bf16 into shared memory in the 128-byte-swizzled K-major
 //               layout; finally O / l (times sigmoid(gate)) to global memory
@@ -43,6 +44,13 @@ struct TcFaArgs {
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 2^x on the special-function unit (PTX ex2.approx, flush-to-zero): one instruction per element, ex2(-inf) = 0.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 template <int HD, int BN>
@@ -202,6 +210,7 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
+      // raw scores; the scale (log2 e / sqrt(d)) is applied inside the exponent's FMA
       float x[BN];
 #pragma unroll
       for (int c = 0; c < BN; c += 32) {
@@ -209,33 +218,37 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld32(tmem + lane_off + st * BN + c, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) x[c + e] = __uint_as_float(v[e]) * a.scale_log2;
+        for (int e = 0; e < 32; ++e) x[c + e] = __uint_as_float(v[e]);
       }
       tc_fence_before();
       mbar_arrive(&s_free[st]);
       const int key0 = j * BN;
+      // only tiles that reach past this row's position (the diagonal) or past n_keys need the mask
+      if (key0 + BN - 1 > pos || key0 + BN > n_keys) {
+#pragma unroll
+        for (int e = 0; e < BN; ++e) {
+          const int key = key0 + e;
+          if (key > pos || key >= n_keys) x[e] = -INFINITY;
+        }
+      }
       float mt = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < BN; ++e) {
-        const int key = key0 + e;
-        if (key > pos || key >= n_keys) x[e] = -INFINITY;
-        mt = fmaxf(mt, x[e]);
-      }
-      float m_new = fmaxf(m_used, mt);
+      for (int e = 0; e < BN; ++e) mt = fmaxf(mt, x[e]);
+      const float m_new = fmaxf(m_used, mt * a.scale_log2);   // scale > 0: max commutes with it
       bool rescale = false;
       float factor = 1.f;
       if (m_used == -INFINITY) {
         m_used = m_new;
       } else if (m_new > m_used + 8.f) {
         rescale = true;
-        factor = exp2f(m_used - m_new);
+        factor = ex2(m_used - m_new);
         m_used = m_new;
       }
       const float base = m_used == -INFINITY ? 0.f : m_used;
       float sum = 0.f;
 #pragma unroll
       for (int e = 0; e < BN; ++e) {
-        x[e] = exp2f(x[e] - base);
+        x[e] = ex2(fmaf(x[e], a.scale_log2, -base));
         sum += x[e];
       }
       l = l * factor + sum;
