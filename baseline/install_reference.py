@@ -1,0 +1,58 @@
+#!/usr/bin/env python3
+"""Install the reference implementation into baseline/_ref (git-ignored) for `bench.py --impl reference`.
+
+1. The prescribed offline pip install (`pip install --no-index --no-build-isolation --find-links /opt/wheelhouse
+   --target baseline/_ref SRC`). The reference is a research repository without package metadata, so pip stops with
+   "not installable".
+2. Then the reference's importable package, `code/kva` (plain PyTorch; imports torch and safetensors only), is
+   copied file for file, unmodified, to baseline/_ref/kva, and baseline/_ref/INSTALL.json records the pip outcome and
+   every copied file's sha256 (the reference arm re-hashes them before it runs and refuses a modified copy).
+
+    python baseline/install_reference.py SRC        # SRC: the reference checkout (its root, holding code/kva)
+"""
+import hashlib
+import json
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+DST = HERE / "_ref"
+
+
+def sha256(p):
+    return hashlib.sha256(Path(p).read_bytes()).hexdigest()
+
+
+def main(argv):
+    if len(argv) != 1:
+        sys.exit(__doc__)
+    src = Path(argv[0]).resolve()
+    DST.mkdir(parents=True, exist_ok=True)
+    pip = subprocess.run([sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation",
+                          "--find-links", "/opt/wheelhouse", "--target", str(DST), str(src)],
+                         capture_output=True, text=True)
+    tail = (pip.stderr or pip.stdout).strip().splitlines()[-3:]
+    record = dict(pip_returncode=pip.returncode, pip_tail=tail, source="code/kva", files={})
+    pkg = src / "code" / "kva"
+    if pip.returncode != 0:
+        if not (pkg / "__init__.py").is_file():
+            sys.exit(f"pip failed and {pkg} holds no package: {tail}")
+        target = DST / "kva"
+        if target.exists():
+            shutil.rmtree(target)
+        for f in sorted(pkg.rglob("*.py")):
+            rel = f.relative_to(pkg)
+            (target / rel).parent.mkdir(parents=True, exist_ok=True)
+            shutil.copyfile(f, target / rel)
+            record["files"][rel.as_posix()] = sha256(f)
+        for extra in ("LICENSE",):
+            if (src / "code" / extra).is_file():
+                shutil.copyfile(src / "code" / extra, DST / extra)
+    (DST / "INSTALL.json").write_text(json.dumps(record, indent=1))
+    print(json.dumps(dict(pip_returncode=pip.returncode, pip=tail[-1] if tail else "", copied=len(record["files"]))))
+
+
+if __name__ == "__main__":
+    main(sys.argv[1:])

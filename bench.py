@@ -96,29 +96,22 @@ class ClockSampler:
 
 
 def reference_arm(args):
-    msg = ("the reference (Approximate-Science/ridgefill-data) is a data release whose source tree has neither "
-           "setup.py nor pyproject.toml: pip reports 'Directory is not installable', so baseline/_ref cannot be "
-           "built")
-    if os.environ.get("RANK", "0") == "0":
-        print(json.dumps(dict(impl="reference", unavailable=msg)))
+    """The reference's own RidgeFill prefill on the same model, prompt and maps (baseline/reference_arm.py)."""
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    import reference_arm as R
+    return R.run(args, METRIC.get(args.model, f"prefill tok/s (RidgeFill TTFT), {args.model}"), BASELINE_TOK_S,
+                 ClockSampler)
 
 
 def build_engine(args, device):
-    import torch
     from ridgefill_data_b200.engine.arm import Arm
     from ridgefill_data_b200.models.base import from_config
     from ridgefill_data_b200.models.config import PRESETS
     from ridgefill_data_b200.ridge.projector import Projector
+    from ridgefill_data_b200.eval.data import synthetic_maps
     cfg = PRESETS[args.model]
     model = from_config(cfg, seed=0, device=device, backend="b200", std=0.02)
-    d = cfg.hidden
-    g = torch.Generator(device=device).manual_seed(123)
-    W, B = {}, {}
-    for i in range(args.split, cfg.n_layers):          # ridge maps of the right shape, near the identity
-        w = 0.01 * torch.randn(d, d, device=device, generator=g)
-        w.diagonal().add_(0.9)
-        W[i] = w.to(torch.bfloat16)
-        B[i] = (0.01 * torch.randn(d, device=device, generator=g)).to(torch.bfloat16)
+    W, B = synthetic_maps(cfg.hidden, args.split, cfg.n_layers, device)   # ridge maps near the identity
     arm = Arm("ridgefill", split=args.split, tail=args.tail, fill="proj", projector=Projector(args.split, W, B))
     return cfg, model, arm
 
@@ -142,12 +135,12 @@ def main():
                     help="tensor-parallel collectives: nvls (fused GEMM + NVSwitch multicast kernels; falls back to "
                          "nccl where the GPUs offer no multicast), nccl (baseline), fused (peer stores)")
     args = ap.parse_args()
-    if args.impl == "reference":
-        return reference_arm(args)
     dsplit, dtail = DEFAULT_SPLIT_TAIL.get(args.model, (32, 4096))
     args.split = dsplit if args.split is None else args.split
     args.tail = dtail if args.tail is None else args.tail
     args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        return reference_arm(args)
 
     import torch
     import torch.distributed as dist
