@@ -8,6 +8,13 @@
 #include "kernels.h"
 #include "mma.cuh"
 
+// 2^x on the special-function unit (PTX ex2.approx, flush-to-zero): one instruction, ex2(-inf) = 0.
+__device__ __forceinline__ float ex2_sfu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 #include <cfloat>
 #include <stdexcept>
 
@@ -149,17 +156,17 @@ __global__ void __launch_bounds__(FA_THREADS) flash_attn_kernel(AttnArgs a) {
     const float mn_hi = fmaxf(m_hi, mx_hi);
     const float base_lo = (mn_lo == -INFINITY) ? 0.f : mn_lo * sl2;
     const float base_hi = (mn_hi == -INFINITY) ? 0.f : mn_hi * sl2;
-    const float corr_lo = exp2f(m_lo * sl2 - base_lo);
-    const float corr_hi = exp2f(m_hi * sl2 - base_hi);
+    const float corr_lo = ex2_sfu(fmaf(m_lo, sl2, -base_lo));
+    const float corr_hi = ex2_sfu(fmaf(m_hi, sl2, -base_hi));
     m_lo = mn_lo;
     m_hi = mn_hi;
     float rs_lo = 0.f, rs_hi = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      s[j][0] = exp2f(s[j][0] * sl2 - base_lo);
-      s[j][1] = exp2f(s[j][1] * sl2 - base_lo);
-      s[j][2] = exp2f(s[j][2] * sl2 - base_hi);
-      s[j][3] = exp2f(s[j][3] * sl2 - base_hi);
+      s[j][0] = ex2_sfu(fmaf(s[j][0], sl2, -base_lo));
+      s[j][1] = ex2_sfu(fmaf(s[j][1], sl2, -base_lo));
+      s[j][2] = ex2_sfu(fmaf(s[j][2], sl2, -base_hi));
+      s[j][3] = ex2_sfu(fmaf(s[j][3], sl2, -base_hi));
       rs_lo += s[j][0] + s[j][1];
       rs_hi += s[j][2] + s[j][3];
     }
