@@ -8,30 +8,38 @@ from .scoring import check_finite
 
 
 @torch.no_grad()
+def step(model, tok, position, cache, arm):
+    """One exact decode step: token `tok` at `position` through every layer over `cache` (appended in place).
+    Returns the next-token logits [1, V] fp32."""
+    native = arm is not None and arm.fill == "swiftkv_native"
+    pos = torch.tensor([position], device=model.device)
+    h = model.embed(torch.tensor([tok], device=model.device))
+    b = None
+    for i in range(model.n_layers):
+        if native and i >= arm.split:
+            if i == arm.split:
+                b = h
+            model.swift_fill(i, b, pos, cache)
+            h = model.swift_layer(i, h, pos, cache)
+        else:
+            h = model.layer(i, h, pos, cache)
+    return model.logits(h)
+
+
+@torch.no_grad()
 def greedy(model, ids, cache, first_logits, steps, arm, eos=()):
     """Greedy continuation of up to `steps` tokens, stopping after an EOS. Returns (tokens, 'stop' | 'length')."""
     out = []
     tok = int(check_finite(first_logits[-1], f"{arm.name} first token").argmax())
     n = ids.shape[0]
-    native = arm.fill == "swiftkv_native"
     for t in range(steps):
         out.append(tok)
         if tok in eos:
             return out, "stop"
         if t == steps - 1:
             break
-        pos = torch.tensor([n + t], device=model.device)
-        h = model.embed(torch.tensor([tok], device=model.device))
-        b = None
-        for i in range(model.n_layers):
-            if native and i >= arm.split:
-                if i == arm.split:
-                    b = h
-                model.swift_fill(i, b, pos, cache)
-                h = model.swift_layer(i, h, pos, cache)
-            else:
-                h = model.layer(i, h, pos, cache)
-        tok = int(check_finite(model.logits(h)[-1], f"{arm.name} decode step {t + 1}").argmax())
+        logits = step(model, tok, n + t, cache, arm)
+        tok = int(check_finite(logits[-1], f"{arm.name} decode step {t + 1}").argmax())
     return out, "length"
 
 

@@ -20,15 +20,17 @@ def context_input(b, mix, split, k):
     return torch.cat([b] + [mix[split - j].to(b.device, b.dtype) for j in range(1, k + 1)], -1)
 
 
-def run_lower(model, ids, splits, hs_device=None, hook=None, mix=None):
+def run_lower(model, ids, splits, hs_device=None, hook=None, mix=None, tick=None, reserve=64):
     """Exact forward up to max(splits). Returns ({split: h_split [N, H]}, cache with layers < max(splits)
-    filled). hook(i, h): every layer input; mix(i, a): every mixer output."""
+    filled). hook(i, h): every layer input; mix(i, a): every mixer output; tick(i): called before layer i with no
+    tensor (a scheduler's point to run other work between layers); reserve: cache rows kept free past the prompt
+    (decode steps append there without copying)."""
     if isinstance(splits, int):
         splits = [splits]
     ids = ids.to(model.device)
     pos = torch.arange(ids.shape[0], device=model.device)
     if hasattr(model, "reserve"):
-        model.reserve(ids.shape[0] + 64)
+        model.reserve(ids.shape[0] + reserve)
     cache = model.new_cache()
     h = model.embed(ids)
     hs = {}
@@ -39,6 +41,8 @@ def run_lower(model, ids, splits, hs_device=None, hook=None, mix=None):
             hs[i] = stable(h) if hs_device is None else h.to(hs_device)
         if hook is not None:
             hook(i, stable(h))
+        if tick is not None:
+            tick(i)
         h = model.layer(i, h, pos, cache, mix=mix)
     hs[top] = stable(h) if hs_device is None else h.to(hs_device)
     return hs, cache
@@ -133,9 +137,10 @@ def _plain_batchable(arm, model, P, rows, fill_reuse, row0, fill_store):
 
 
 def finish(model, ids, h_split, lower_cache, arm, keep, oracle=None, keep_cache=True, fill_store=None,
-           fill_reuse=None, exact_rows=None, row_inputs=None, hook=None, mix=None, timer=None):
+           fill_reuse=None, exact_rows=None, row_inputs=None, hook=None, mix=None, timer=None, tick=None):
     """Layers >= arm.split for one arm. keep: number of final rows whose logits to return. Returns
-    (logits [keep, V] fp32, cache, P). See the module doc and engine/arm.py for the options."""
+    (logits [keep, V] fp32, cache, P). tick(i): called before late layer i's tail rows run. See the module doc and
+    engine/arm.py for the options."""
     n = ids.shape[0]
     split = arm.split
     P = arm.prefix_len(n)
@@ -246,6 +251,8 @@ def finish(model, ids, h_split, lower_cache, arm, keep, oracle=None, keep_cache=
             cache[i]["rec"] = cache[i]["rec"] + st.to(cache[i]["rec"])
         if hook is not None:
             hook(i, model.stable(h) if hasattr(model, "stable") else h)
+        if tick is not None:
+            tick(i)
         h = model.layer(i, h, pos[P:], cache)
         if not keep_cache:
             cache[i] = {}

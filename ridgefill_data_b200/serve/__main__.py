@@ -1,0 +1,77 @@
+"""Completion server CLI.
+
+    python -m ridgefill_data_b200.serve --model qwen3.8-27b --synthetic-maps --port 8080          # random-init shape
+    python -m ridgefill_data_b200.serve --checkpoint DIR --maps maps.safetensors --tokenizer DIR   # a real model
+
+Modes per request (`ridgefill_mode`): "on" = RidgeFill (split / tail of the maps or the flags), "off" = exact
+prefill. Decoding is always exact and greedy.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+
+
+def build(args):
+    import torch
+    from ..engine.arm import Arm
+    from ..models.base import from_config, load
+    from ..models.config import PRESETS
+    from ..ridge.projector import Projector
+    device = torch.device(args.device)
+    if args.checkpoint:
+        model = load(args.checkpoint, device=device, backend=args.backend)
+        name = args.checkpoint
+    else:
+        model = from_config(PRESETS[args.model], seed=0, device=device, backend=args.backend, std=0.02)
+        name = args.model
+    if args.maps:
+        proj = Projector.load(args.maps, device)
+        split = proj.split
+    elif args.synthetic_maps:
+        from ..eval.data import synthetic_maps
+        split = args.split
+        W, B = synthetic_maps(model.hidden, split, model.n_layers, device)
+        proj = Projector(split, W, B)
+    else:
+        raise SystemExit("give --maps FILE (a fitted map file) or --synthetic-maps (benchmark shapes only)")
+    arms = {"off": Arm("exact"), "on": Arm("ridgefill", split=split, tail=args.tail, fill="proj", projector=proj)}
+    tok, eos = None, ()
+    if args.tokenizer:
+        from ..eval.text import eos_ids, tokenizer
+        tok = tokenizer(args.tokenizer)
+        eos = eos_ids(args.tokenizer, tok) if args.tokenizer != "char" else (tok.eos_token_id,)
+    vocab = model.cfg.vocab
+    props = dict(model=str(name), n_layers=model.n_layers, vocab=vocab, split=split, tail=args.tail,
+                 backend=args.backend, interleave=args.interleave)
+    return model, arms, tok, eos, props
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description="RidgeFill completion server")
+    ap.add_argument("--model", default="qwen3.8-27b", help="a preset shape (random init) when no --checkpoint")
+    ap.add_argument("--checkpoint")
+    ap.add_argument("--backend", default="b200", choices=("b200", "torch"))
+    ap.add_argument("--device", default="cuda")
+    ap.add_argument("--maps")
+    ap.add_argument("--synthetic-maps", action="store_true")
+    ap.add_argument("--split", type=int, default=32)
+    ap.add_argument("--tail", type=int, default=4096)
+    ap.add_argument("--tokenizer")
+    ap.add_argument("--interleave", type=int, default=4, help="decode round every this many prefill layers (0: off)")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8080)
+    a = ap.parse_args(argv)
+    from .app import Server, create_app
+    from .engine import Scheduler
+    model, arms, tok, eos, props = build(a)
+    sched = Scheduler(model, eos=eos, interleave=a.interleave).start()
+    try:
+        Server(create_app(sched, arms, tok, props), a.host, a.port, log_level="info").run()
+    finally:
+        sched.stop()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

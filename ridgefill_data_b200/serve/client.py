@@ -1,0 +1,236 @@
+"""Measurement clients for the `/completion` server (the roles of code/qwen38-27b-kit/timing.py and mix.py):
+
+* `timing`: TTFT of distinct prompts on a warm server: one short warm-up request, then each prompt once, with the
+  client-side TTFT (send -> first token event) next to the server's own prompt time.
+* `mix`: a fixed-arrival concurrency mix. Background requests start decoding; at a planned time an injector sends a
+  long prompt; every request's stream is recorded with arrival-relative timestamps. The summary gives the injector's
+  TTFT and the background streams' inter-token gaps before, during and after the injector's prefill: what a long
+  RidgeFill prefill costs the requests already being served.
+
+    python -m ridgefill_data_b200.serve.client timing --url http://127.0.0.1:8080 --length 16384 --prompts 3
+    python -m ridgefill_data_b200.serve.client mix --url http://127.0.0.1:8080 --concurrency 4 --injector-len 16384
+
+Only the standard library is used on the client side (urllib + threads), so it runs anywhere.
+"""
+from __future__ import annotations
+
+import json
+import threading
+import time
+import urllib.request
+
+import numpy as np
+
+
+# ------------------------------------------------------------------------------------------------ transport
+def post_json(url, path, body, timeout=600):
+    req = urllib.request.Request(url + path, data=json.dumps(body).encode(), headers={"Content-Type": "application/json"})
+    with urllib.request.urlopen(req, timeout=timeout) as r:
+        return json.load(r)
+
+
+def get_json(url, path, timeout=30):
+    with urllib.request.urlopen(url + path, timeout=timeout) as r:
+        return json.load(r)
+
+
+def stream(url, body, epoch=None, timeout=600):
+    """[{'t': seconds since epoch, 'data': event}] of one streamed completion, and the send time."""
+    epoch = time.monotonic() if epoch is None else epoch
+    body = dict(body, stream=True)
+    req = urllib.request.Request(url + "/completion", data=json.dumps(body).encode(),
+                                 headers={"Content-Type": "application/json"})
+    sent = time.monotonic() - epoch
+    events = []
+    with urllib.request.urlopen(req, timeout=timeout) as r:
+        for raw in r:
+            raw = raw.strip()
+            if not raw.startswith(b"data:"):
+                continue
+            raw = raw[5:].strip()
+            if raw == b"[DONE]":
+                break
+            ev = json.loads(raw)
+            events.append(dict(t=time.monotonic() - epoch, data=ev))
+            if ev.get("stop"):
+                break
+    return events, sent
+
+
+# ------------------------------------------------------------------------------------------------ metrics
+def distribution(xs):
+    xs = [float(x) for x in xs]
+    if not xs:
+        return dict(n=0)
+    a = np.asarray(xs)
+    return dict(n=len(xs), mean=float(a.mean()), p50=float(np.percentile(a, 50)), p90=float(np.percentile(a, 90)),
+                p99=float(np.percentile(a, 99)), max=float(a.max()))
+
+
+class StreamError(RuntimeError):
+    pass
+
+
+def token_metrics(events, expected):
+    """Per-token arrival times of one stream (a token counted once, at the event that delivered it), the gaps
+    between consecutive tokens, and the final event. Checks: no error event, monotone token counts, exactly one
+    final event, `expected` tokens delivered."""
+    delivered, times, final, coalesced = 0, [], None, 0
+    for ev in events:
+        d, t = ev["data"], ev["t"]
+        if "error" in d:
+            raise StreamError(f"server error: {d['error']}")
+        if d.get("stop"):
+            if final is not None:
+                raise StreamError("two final events")
+            final = d
+            continue
+        count = d.get("tokens_predicted", delivered + len(d.get("tokens", [])))
+        if count < delivered:
+            raise StreamError("token count went backwards")
+        if count > delivered:
+            coalesced += count - delivered - 1
+            times += [t] * (count - delivered)
+            delivered = count
+    if final is None:
+        raise StreamError("no final event")
+    if delivered != expected or final.get("tokens_predicted") != expected:
+        raise StreamError(f"{delivered} tokens delivered, {expected} expected")
+    gaps = [dict(begin=a, end=b, ms=1e3 * (b - a)) for a, b in zip(times, times[1:])]
+    return dict(first=times[0], last=times[-1], token_times=times, gaps=gaps, coalesced_tokens=coalesced,
+                itl_ms=distribution([g["ms"] for g in gaps]),
+                decode_tps=(expected - 1) / (times[-1] - times[0]) if expected > 1 and times[-1] > times[0] else None,
+                final=final)
+
+
+# ------------------------------------------------------------------------------------------------ timing
+def timing(url, prompts, mode="on", warmup_len=32):
+    """TTFT of each prompt (lists of ids) on a warm server, one at a time."""
+    post_json(url, "/completion", dict(prompt=prompts[0][:warmup_len], n_predict=2, ridgefill_mode=mode,
+                                       ignore_eos=True))
+    rows = []
+    for j, ids in enumerate(prompts):
+        events, sent = stream(url, dict(prompt=list(ids), n_predict=1, ridgefill_mode=mode, ignore_eos=True,
+                                        temperature=0, top_k=1, cache_prompt=False))
+        m = token_metrics(events, 1)
+        t = m["final"]["timings"]
+        if t["prompt_n"] != len(ids) or t["cache_n"] != 0:
+            raise StreamError(f"prompt {j}: the server evaluated {t['prompt_n']} of {len(ids)} tokens")
+        rows.append(dict(prompt=j, n=len(ids), client_ttft_ms=1e3 * (m["first"] - sent),
+                         server_prompt_ms=t["prompt_ms"], filled=t.get("prompt_filled_n", 0)))
+    return dict(mode=mode, rows=rows, client_ttft_ms=distribution([r["client_ttft_ms"] for r in rows]),
+                server_prompt_ms=distribution([r["server_prompt_ms"] for r in rows]))
+
+
+# ------------------------------------------------------------------------------------------------ mix
+def make_schedule(concurrency, vocab, background_len=1024, background_predict=64, injector_len=16384,
+                  injector_predict=8, inject_at_s=1.0, stagger_s=0.05, seed=0):
+    """A fixed-arrival plan: concurrency - 1 background requests arriving stagger_s apart from t = 0, then one
+    injector (a long prompt) at inject_at_s. Seeded uniform ids."""
+    if concurrency < 2:
+        raise ValueError("a mix needs at least one background request and the injector")
+    g = np.random.default_rng(seed)
+    plan = [dict(id=f"bg{j}", role="background", arrival_s=j * stagger_s, predict=background_predict,
+                 ids=g.integers(0, vocab, background_len).tolist()) for j in range(concurrency - 1)]
+    plan.append(dict(id="inj", role="injector", arrival_s=inject_at_s, predict=injector_predict,
+                     ids=g.integers(0, vocab, injector_len).tolist()))
+    return plan
+
+
+def run_mix(url, plan, mode="on", background_mode="off", timeout=900):
+    """Send every planned request at its arrival time (the injector with `mode`, the background with
+    `background_mode`), record the streams, return (results, summary)."""
+    out, errors, threads = [], [], []
+    epoch = time.monotonic() + 0.5
+
+    def one(item):
+        try:
+            body = dict(prompt=item["ids"], n_predict=item["predict"], ignore_eos=True, temperature=0, top_k=1,
+                        ridgefill_mode=mode if item["role"] == "injector" else background_mode)
+            time.sleep(max(0.0, epoch + item["arrival_s"] - time.monotonic()))
+            events, sent = stream(url, body, epoch, timeout)
+            m = token_metrics(events, item["predict"])
+            m.update(id=item["id"], role=item["role"], n_prompt=len(item["ids"]), predict=item["predict"], sent=sent,
+                     planned=item["arrival_s"], lateness_ms=1e3 * (sent - item["arrival_s"]),
+                     ttft_s=m["first"] - sent)
+            out.append(m)
+        except Exception as e:
+            errors.append(dict(id=item["id"], error=repr(e)))
+
+    for item in plan:
+        th = threading.Thread(target=one, args=(item,), daemon=True)
+        threads.append(th)
+        th.start()
+    for th in threads:
+        th.join(timeout)
+    if errors:
+        raise StreamError(f"mix requests failed: {errors}")
+    return out, summarize(out)
+
+
+def summarize(results):
+    inj = next(r for r in results if r["role"] == "injector")
+    bg = [r for r in results if r["role"] == "background"]
+    gaps = [g for r in bg for g in r["gaps"]]
+    during = [g for g in gaps if g["end"] >= inj["sent"] and g["begin"] <= inj["first"]]
+    before = [g for g in gaps if g["end"] <= inj["sent"]]
+    after = [g for g in gaps if g["begin"] >= inj["first"]]
+    wall = max(r["last"] for r in results) - min(r["sent"] for r in results)
+    busy = inj["first"] - inj["sent"]
+    return dict(
+        injector_ttft_s=inj["ttft_s"], injector_server_prompt_ms=inj["final"]["timings"]["prompt_ms"],
+        injector_filled=inj["final"]["timings"].get("prompt_filled_n", 0),
+        background_ttft_s=distribution([r["ttft_s"] for r in bg]),
+        background_itl_ms=distribution([g["ms"] for g in gaps]),
+        background_itl_before_ms=distribution([g["ms"] for g in before]),
+        background_itl_during_prefill_ms=distribution([g["ms"] for g in during]),
+        background_itl_after_ms=distribution([g["ms"] for g in after]),
+        background_tokens_during_prefill=sum(inj["sent"] <= t <= inj["first"] for r in bg for t in r["token_times"]),
+        background_active_at_injection=sum(r["first"] < inj["sent"] < r["last"] for r in bg),
+        background_tps_during_prefill=(sum(inj["sent"] <= t <= inj["first"] for r in bg for t in r["token_times"])
+                                       / busy if busy > 0 else None),
+        aggregate_tps=sum(r["predict"] for r in results) / wall if wall > 0 else None,
+        lateness_ms=distribution([r["lateness_ms"] for r in results]), workload_s=wall,
+        coalesced_tokens=sum(r["coalesced_tokens"] for r in results))
+
+
+def main(argv=None):
+    import argparse
+    ap = argparse.ArgumentParser(description="timing and concurrency-mix clients of the completion server")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    for name in ("timing", "mix"):
+        p = sub.add_parser(name)
+        p.add_argument("--url", default="http://127.0.0.1:8080")
+        p.add_argument("--mode", default="on", help="the prompt's (injector's) ridgefill_mode")
+        p.add_argument("--seed", type=int, default=0)
+        p.add_argument("--out")
+    t = sub.choices["timing"]
+    t.add_argument("--length", type=int, default=16384)
+    t.add_argument("--prompts", type=int, default=3)
+    m = sub.choices["mix"]
+    m.add_argument("--concurrency", type=int, default=4)
+    m.add_argument("--background-len", type=int, default=1024)
+    m.add_argument("--background-predict", type=int, default=64)
+    m.add_argument("--injector-len", type=int, default=16384)
+    m.add_argument("--injector-predict", type=int, default=8)
+    m.add_argument("--inject-at", type=float, default=1.0)
+    m.add_argument("--background-mode", default="off")
+    a = ap.parse_args(argv)
+    vocab = int(get_json(a.url, "/props").get("vocab", 32000))
+    g = np.random.default_rng(a.seed)
+    if a.cmd == "timing":
+        res = timing(a.url, [g.integers(0, vocab, a.length).tolist() for _ in range(a.prompts)], a.mode)
+    else:
+        plan = make_schedule(a.concurrency, vocab, a.background_len, a.background_predict, a.injector_len,
+                             a.injector_predict, a.inject_at, seed=a.seed)
+        _, res = run_mix(a.url, plan, a.mode, a.background_mode)
+    if a.out:
+        from ..utils.atomic import write_result
+        write_result(a.out, res)
+    print(json.dumps(res, indent=1))
+    return 0
+
+
+if __name__ == "__main__":
+    import sys
+    sys.exit(main())

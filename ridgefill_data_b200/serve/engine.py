@@ -1,0 +1,247 @@
+"""Request scheduler for serving one model on one device.
+
+One worker thread owns the model. Requests wait in a FIFO queue; the worker takes one at a time for prefill and
+keeps every started request in the decode set until it has produced its tokens. Each decode round advances every
+active request by one greedy token (an exact full-model step over its own cache). A long prefill does not stall
+the running streams: the engine's layer loop calls `tick(i)` before every layer, and every `interleave` layers the
+worker runs one decode round for the other requests, so their inter-token gap during a prefill is bounded by
+`interleave` layers of that prefill instead of all of it (the quantity the fixed-arrival mix measures). Under
+tensor parallelism the layer outputs live in rotating collective buffers, so interleaving is off there.
+
+Events are plain dicts handed to the request's `emit` callback from the worker thread, in the field layout of the
+llama.cpp server's `/completion` stream (kept alike so the 27B kit's clients read them unchanged):
+  token:  {"tokens": [id], "content": str, "tokens_predicted": k, "stop": false}
+  final:  {"tokens": [], "content": "", "stop": true, "stop_type": "eos" | "limit", "tokens_predicted": k,
+           "tokens_evaluated": n_prompt, "truncated": false, "timings": {prompt_n, prompt_ms, prompt_per_second,
+           predicted_n, predicted_ms, predicted_per_second, prompt_filled_n, cache_n, ridgefill: {...}}}
+  error:  {"error": message, "stop": true}
+"""
+from __future__ import annotations
+
+import itertools
+import queue
+import threading
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from ..engine import decode as D
+from ..engine.arm import Arm
+from ..engine.prefill import finish, run_lower
+
+
+@dataclass
+class Request:
+    ids: torch.Tensor                       # [n] int64 prompt ids (host)
+    n_predict: int
+    arm: Arm                                # the prefill arm (exact, or a RidgeFill arm)
+    emit: object                            # callable(event dict), called from the worker thread
+    ignore_eos: bool = False
+    rid: str = ""
+    detok: object = None                    # callable([id]) -> str, optional
+    t_submit: float = 0.0
+    # runtime state
+    cache: list = None
+    position: int = 0
+    tok: int = -1
+    produced: list = field(default_factory=list)
+    t_prefill0: float = 0.0
+    t_first: float = 0.0
+    t_last: float = 0.0
+    filled: int = 0
+    cancelled: bool = False
+
+
+class Scheduler:
+    def __init__(self, model, eos=(), interleave=4, max_active=64, sync=None):
+        self.model = model
+        self.eos = frozenset(int(e) for e in eos)
+        self.interleave = int(interleave)
+        self.max_active = int(max_active)
+        self.waiting = queue.Queue()
+        self.active = []
+        self._stop = threading.Event()
+        self._wake = threading.Event()
+        self._thread = None
+        self._ids = itertools.count()
+        self.sync = sync if sync is not None else (torch.cuda.synchronize if model.device.type == "cuda"
+                                                  else (lambda: None))
+        self.stats = dict(requests=0, completed=0, errors=0, prompt_tokens=0, predicted_tokens=0,
+                          filled_tokens=0, interleaved_rounds=0)
+        self.ttft_ms, self.prompt_ms = [], []
+        self._lock = threading.Lock()
+
+    # ---- control
+    def start(self):
+        if self._thread is None:
+            self._thread = threading.Thread(target=self._loop, name="rf-scheduler", daemon=True)
+            self._thread.start()
+        return self
+
+    def stop(self, timeout=30):
+        self._stop.set()
+        self._wake.set()
+        if self._thread is not None:
+            self._thread.join(timeout)
+            self._thread = None
+
+    def submit(self, req: Request):
+        if req.n_predict < 1:
+            raise ValueError("n_predict must be at least 1")
+        if req.ids.dim() != 1 or req.ids.numel() == 0:
+            raise ValueError("the prompt must be a non-empty 1-D id sequence")
+        req.rid = req.rid or f"req-{next(self._ids)}"
+        req.t_submit = time.perf_counter()
+        with self._lock:
+            self.stats["requests"] += 1
+        self.waiting.put(req)
+        self._wake.set()
+        return req.rid
+
+    @property
+    def load(self):
+        return dict(waiting=self.waiting.qsize(), active=len(self.active))
+
+    # ---- worker
+    def _loop(self):
+        while not self._stop.is_set():
+            started = False
+            if len(self.active) < self.max_active:
+                try:
+                    req = self.waiting.get_nowait()
+                except queue.Empty:
+                    req = None
+                if req is not None:
+                    started = True
+                    self._prefill(req)
+            if self.active:
+                self._decode_round()
+            elif not started:
+                self._wake.wait(0.05)
+                self._wake.clear()
+
+    def _tick_for(self, owner):
+        """tick(i) for the prefill of `owner`: a decode round of the running streams every `interleave` layers."""
+        if self.interleave <= 0 or getattr(self.model, "tp", None) is not None:
+            return None
+        count = itertools.count(1)
+
+        def tick(i):                      # the owner joins the decode set only after its prefill
+            if next(count) % self.interleave == 0 and self.active:
+                self.stats["interleaved_rounds"] += 1
+                self._decode_round()
+        return tick
+
+    def _emit(self, req, ev):
+        try:
+            req.emit(ev)
+        except Exception:            # a closed client must not stop the worker
+            req.cancelled = True
+
+    @torch.no_grad()
+    def _prefill(self, req: Request):
+        model, arm = self.model, req.arm
+        n = int(req.ids.numel())
+        req.t_prefill0 = time.perf_counter()
+        tick = self._tick_for(req)
+        try:
+            ids = req.ids.to(model.device)
+            if arm.fill == "exact" or arm.split is None:
+                hs, cache = run_lower(model, ids, [model.n_layers], tick=tick, reserve=req.n_predict + 64)
+                logits = model.logits(hs[model.n_layers][-1:])
+                req.filled = 0
+            else:
+                hs, lower = run_lower(model, ids, [arm.split], tick=tick, reserve=req.n_predict + 64)
+                logits, cache, P = finish(model, ids, hs[arm.split], lower, arm, keep=1, tick=tick)
+                req.filled = int(P)
+            del hs
+            tok = int(D.check_finite(logits[-1], f"{req.rid} first token").argmax())
+        except Exception as e:                         # report, drop the request, keep serving
+            self.stats["errors"] += 1
+            self._emit(req, {"error": f"{type(e).__name__}: {e}", "stop": True})
+            return
+        now = time.perf_counter()
+        req.cache, req.position, req.t_first, req.t_last = cache, n, now, now
+        self.prompt_ms.append(1e3 * (now - req.t_prefill0))
+        self.ttft_ms.append(1e3 * (now - req.t_submit))
+        self.stats["prompt_tokens"] += n
+        self.stats["filled_tokens"] += req.filled
+        self._deliver(req, tok)
+        if not self._done(req):
+            self.active.append(req)
+        else:
+            self._final(req)
+
+    def _deliver(self, req, tok):
+        req.produced.append(tok)
+        req.tok = tok
+        self.stats["predicted_tokens"] += 1
+        self._emit(req, {"tokens": [tok], "content": req.detok([tok]) if req.detok else "",
+                         "tokens_predicted": len(req.produced), "stop": False})
+
+    def _done(self, req):
+        return (req.cancelled or len(req.produced) >= req.n_predict
+                or (not req.ignore_eos and req.tok in self.eos))
+
+    @torch.no_grad()
+    def _decode_round(self):
+        keep = []
+        for req in list(self.active):
+            try:
+                logits = D.step(self.model, req.tok, req.position, req.cache, req.arm)
+                tok = int(D.check_finite(logits[-1], f"{req.rid} decode").argmax())
+            except Exception as e:
+                self.stats["errors"] += 1
+                self._emit(req, {"error": f"{type(e).__name__}: {e}", "stop": True})
+                req.cache = None
+                continue
+            req.position += 1
+            req.t_last = time.perf_counter()
+            self._deliver(req, tok)
+            if self._done(req):
+                self._final(req)
+            else:
+                keep.append(req)
+        self.active = keep
+
+    def _final(self, req):
+        n = int(req.ids.numel())
+        prompt_ms = 1e3 * (req.t_first - req.t_prefill0)
+        pred = len(req.produced)
+        pred_ms = 1e3 * (req.t_last - req.t_first)
+        stop_type = "eos" if (req.tok in self.eos and not req.ignore_eos) else "limit"
+        arm = req.arm
+        timings = dict(prompt_n=n, prompt_ms=round(prompt_ms, 3),
+                       prompt_per_second=round(n / max(prompt_ms, 1e-9) * 1e3, 3),
+                       predicted_n=pred, predicted_ms=round(pred_ms, 3),
+                       predicted_per_second=round((pred - 1) / (pred_ms / 1e3), 3) if pred > 1 and pred_ms > 0
+                       else None,
+                       prompt_filled_n=req.filled, cache_n=0,
+                       queue_ms=round(1e3 * (req.t_prefill0 - req.t_submit), 3))
+        if req.filled:
+            timings["ridgefill"] = dict(n_filled=req.filled, split=arm.split, tail=arm.tail, fill=arm.fill,
+                                        n_cached_exact_prefix=0)
+        req.cache = None
+        with self._lock:
+            self.stats["completed"] += 1
+        self._emit(req, {"tokens": [], "content": "", "stop": True, "stop_type": stop_type,
+                         "tokens_predicted": pred, "tokens_evaluated": n, "truncated": False, "id": req.rid,
+                         "timings": timings})
+
+    # ---- metrics (Prometheus text exposition)
+    def metrics_text(self):
+        s = dict(self.stats, **self.load)
+        lines = []
+        for k, v in sorted(s.items()):
+            name = f"ridgefill_{k}" + ("_total" if k not in ("waiting", "active") else "")
+            kind = "gauge" if k in ("waiting", "active") else "counter"
+            lines += [f"# TYPE {name} {kind}", f"{name} {v}"]
+        for name, xs in (("ridgefill_ttft_ms", self.ttft_ms), ("ridgefill_prompt_ms", self.prompt_ms)):
+            xs = sorted(xs)
+            lines.append(f"# TYPE {name} summary")
+            for q in (0.5, 0.9, 0.99):
+                v = xs[min(len(xs) - 1, int(q * len(xs)))] if xs else float("nan")
+                lines.append(f'{name}{{quantile="{q}"}} {v:.3f}')
+            lines += [f"{name}_count {len(xs)}", f"{name}_sum {sum(xs):.3f}"]
+        return "\n".join(lines) + "\n"

@@ -1,0 +1,150 @@
+"""Serving on the CPU (tiny hybrid on the torch backend): the scheduler's streams equal the engine's greedy decode
+for both modes, decode rounds interleave with a long prefill, the HTTP server speaks the /completion layout
+(non-streamed, SSE, errors), and the timing and concurrency-mix clients run against it end to end."""
+import json
+import threading
+import urllib.error
+import urllib.request
+
+import pytest
+import torch
+
+pytest.importorskip("fastapi")
+pytest.importorskip("uvicorn")
+
+from ridgefill_data_b200.engine.arm import Arm  # noqa: E402
+from ridgefill_data_b200.engine.decode import greedy  # noqa: E402
+from ridgefill_data_b200.engine.prefill import prefill  # noqa: E402
+from ridgefill_data_b200.eval.data import synthetic_maps, uniform_prompt  # noqa: E402
+from ridgefill_data_b200.models.base import from_config  # noqa: E402
+from ridgefill_data_b200.models.tiny import tiny_configs  # noqa: E402
+from ridgefill_data_b200.ridge.projector import Projector  # noqa: E402
+from ridgefill_data_b200.serve import client as C  # noqa: E402
+from ridgefill_data_b200.serve.app import Server, create_app  # noqa: E402
+from ridgefill_data_b200.serve.engine import Request, Scheduler  # noqa: E402
+
+CFG = tiny_configs(8, 64)["qwen3.5-9b"]
+SPLIT, TAIL = 4, 16
+
+
+@pytest.fixture(scope="module")
+def setup():
+    model = from_config(CFG, seed=0, device="cpu", dtype=torch.float32)
+    W, B = synthetic_maps(CFG.hidden, SPLIT, CFG.n_layers, "cpu", dtype=torch.float32)
+    arms = {"off": Arm("exact"), "on": Arm("ridgefill", split=SPLIT, tail=TAIL, fill="proj",
+                                            projector=Projector(SPLIT, W, B))}
+    return model, arms
+
+
+def _expected(model, arm, ids, n):
+    logits, cache, _ = prefill(model, ids, arm, keep=1)
+    toks, _ = greedy(model, ids, cache, logits, n, arm)
+    return toks
+
+
+def _collect(sched, ids, n, arm):
+    evs, done = [], threading.Event()
+
+    def emit(ev):
+        evs.append(ev)
+        if ev.get("stop"):
+            done.set()
+    sched.submit(Request(ids=ids, n_predict=n, arm=arm, emit=emit, ignore_eos=True))
+    return evs, done
+
+
+def test_scheduler_matches_greedy_and_interleaves(setup):
+    model, arms = setup
+    sched = Scheduler(model, interleave=1)
+    short = uniform_prompt(40, CFG.vocab, seed=5)
+    long = uniform_prompt(96, CFG.vocab, seed=6)
+    ev_a, done_a = _collect(sched, short, 12, arms["off"])      # queued before the worker starts: A prefills
+    ev_b, done_b = _collect(sched, long, 5, arms["on"])         # first, then B's prefill interleaves A's decode
+    sched.start()
+    try:
+        assert done_a.wait(60) and done_b.wait(60)
+    finally:
+        sched.stop()
+    assert sched.stats["interleaved_rounds"] > 0
+    toks_a = [t for e in ev_a if not e.get("stop") for t in e["tokens"]]
+    toks_b = [t for e in ev_b if not e.get("stop") for t in e["tokens"]]
+    assert toks_a == _expected(model, arms["off"], short, 12)
+    assert toks_b == _expected(model, arms["on"], long, 5)
+    fa, fb = ev_a[-1], ev_b[-1]
+    assert fa["stop"] and fa["tokens_predicted"] == 12 and fa["timings"]["prompt_filled_n"] == 0
+    assert fb["timings"]["prompt_filled_n"] == 96 - TAIL and fb["timings"]["ridgefill"]["split"] == SPLIT
+    assert fb["tokens_evaluated"] == 96 and fb["stop_type"] == "limit"
+    assert sched.stats["completed"] == 2 and sched.stats["errors"] == 0
+    assert "ridgefill_completed_total 2" in sched.metrics_text()
+
+
+def test_eos_and_bad_requests(setup):
+    model, arms = setup
+    ids = uniform_prompt(30, CFG.vocab, seed=7)
+    first = _expected(model, arms["off"], ids, 1)[0]
+    sched = Scheduler(model, eos=[first]).start()
+    try:
+        evs, done = [], threading.Event()
+        sched.submit(Request(ids=ids, n_predict=9, arm=arms["off"],
+                             emit=lambda e: (evs.append(e), e.get("stop") and done.set())))
+        assert done.wait(60)
+        assert evs[-1]["stop_type"] == "eos" and evs[-1]["tokens_predicted"] == 1
+        with pytest.raises(ValueError):
+            sched.submit(Request(ids=ids, n_predict=0, arm=arms["off"], emit=print))
+    finally:
+        sched.stop()
+
+
+@pytest.fixture(scope="module")
+def server(setup):
+    model, arms = setup
+    sched = Scheduler(model, interleave=2).start()
+    srv = Server(create_app(sched, arms, props=dict(vocab=CFG.vocab)), port=0).start()
+    yield f"http://127.0.0.1:{srv.port}", model, arms
+    srv.stop()
+    sched.stop()
+
+
+def test_http_completion(server):
+    url, model, arms = server
+    assert C.get_json(url, "/health")["status"] == "ok"
+    ids = uniform_prompt(64, CFG.vocab, seed=8)
+    r = C.post_json(url, "/completion", dict(prompt=ids.tolist(), n_predict=6, ridgefill_mode="on", ignore_eos=True))
+    assert r["tokens"] == _expected(model, arms["on"], ids, 6) and r["stop"] and r["tokens_evaluated"] == 64
+    events, sent = C.stream(url, dict(prompt=ids.tolist(), n_predict=6, ridgefill=False, ignore_eos=True))
+    m = C.token_metrics(events, 6)
+    assert [e["data"]["tokens"][0] for e in events[:-1]] == _expected(model, arms["off"], ids, 6)
+    assert m["final"]["timings"]["prompt_filled_n"] == 0 and m["itl_ms"]["n"] == 5
+    for bad in (dict(prompt=[], n_predict=2), dict(prompt=[1, 2], n_predict=2, temperature=0.7),
+                dict(prompt=[1, 2], ridgefill_mode="half"), dict(prompt="text without a tokenizer")):
+        with pytest.raises(urllib.error.HTTPError) as e:
+            C.post_json(url, "/completion", bad)
+        assert e.value.code == 400
+    text = urllib.request.urlopen(url + "/metrics").read().decode()
+    assert "ridgefill_requests_total" in text and 'ridgefill_ttft_ms{quantile="0.5"}' in text
+
+
+def test_timing_and_mix_clients(server):
+    url, _, _ = server
+    res = C.timing(url, [uniform_prompt(80, CFG.vocab, seed=s).tolist() for s in (1, 2)], mode="on")
+    assert len(res["rows"]) == 2 and all(r["filled"] == 80 - TAIL for r in res["rows"])
+    plan = C.make_schedule(3, CFG.vocab, background_len=24, background_predict=40, injector_len=128,
+                           injector_predict=3, inject_at_s=0.3, seed=1)
+    results, summary = C.run_mix(url, plan, mode="on")
+    assert len(results) == 3 and summary["injector_filled"] == 128 - TAIL
+    assert summary["background_itl_ms"]["n"] == 2 * 39
+    json.dumps(summary)
+
+
+def test_token_metrics_checks():
+    ev = [dict(t=0.1, data=dict(tokens=[5], tokens_predicted=1)), dict(t=0.3, data=dict(tokens=[6, 7],
+                                                                                          tokens_predicted=3)),
+          dict(t=0.4, data=dict(stop=True, tokens_predicted=3, timings={}))]
+    m = C.token_metrics(ev, 3)
+    assert m["coalesced_tokens"] == 1 and m["token_times"] == [0.1, 0.3, 0.3]
+    with pytest.raises(C.StreamError):
+        C.token_metrics(ev, 4)
+    with pytest.raises(C.StreamError):
+        C.token_metrics(ev[:2], 3)
+    with pytest.raises(C.StreamError):
+        C.token_metrics([dict(t=0, data=dict(error="x"))], 1)

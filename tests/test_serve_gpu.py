@@ -1,0 +1,57 @@
+"""The serving scheduler on the B200 backend: two queued requests (exact and RidgeFill), the second prefill
+interleaving decode rounds of the first, produce exactly the tokens of the engine's own prefill + greedy decode on
+the same model (the kernels are deterministic, so any state clobbered by the interleaving would show)."""
+import threading
+
+import pytest
+import torch
+
+from ridgefill_data_b200.engine.arm import Arm
+from ridgefill_data_b200.engine.decode import greedy
+from ridgefill_data_b200.engine.prefill import prefill
+from ridgefill_data_b200.eval.data import synthetic_maps
+from ridgefill_data_b200.models.base import from_config
+from ridgefill_data_b200.models.config import ModelConfig, _hybrid_types
+from ridgefill_data_b200.ridge.projector import Projector
+from ridgefill_data_b200.serve.engine import Request, Scheduler
+
+pytestmark = pytest.mark.gpu
+
+HYB = ModelConfig(arch="qwen3_5", n_layers=8, hidden=512, vocab=1024, n_heads=4, n_kv=1, head_dim=256,
+                  intermediate=1024, eps=1e-6, rope_theta=1e7, partial_rotary=0.25, layer_types=_hybrid_types(8),
+                  gdn_nk=2, gdn_nv=4, gdn_dk=128, gdn_dv=128, conv_k=4, name="tiny-hybrid")
+
+
+def test_scheduler_b200_interleaved_streams_match_engine():
+    model = from_config(HYB, seed=0, device="cuda", std=0.05, backend="b200")
+    W, B = synthetic_maps(HYB.hidden, 4, HYB.n_layers, "cuda")
+    arms = [Arm("exact"), Arm("ridgefill", split=4, tail=256, fill="proj", projector=Projector(4, W, B))]
+    g = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, HYB.vocab, (300,), generator=g), torch.randint(0, HYB.vocab, (1100,), generator=g)]
+    n_pred = [24, 6]
+    want = []
+    with torch.no_grad():
+        for ids, arm, n in zip(prompts, arms, n_pred):
+            logits, cache, _ = prefill(model, ids.cuda(), arm, keep=1)
+            want.append(greedy(model, ids.cuda(), cache, logits, n, arm)[0])
+    sched = Scheduler(model, interleave=1)
+    got, done = [[], []], [threading.Event(), threading.Event()]
+    for j in range(2):
+        def emit(ev, j=j):
+            got[j].append(ev)
+            if ev.get("stop"):
+                done[j].set()
+        sched.submit(Request(ids=prompts[j], n_predict=n_pred[j], arm=arms[j], emit=emit, ignore_eos=True))
+    sched.start()
+    try:
+        assert done[0].wait(120) and done[1].wait(120)
+    finally:
+        sched.stop()
+    for j in range(2):
+        assert "error" not in got[j][-1], got[j][-1]
+        assert [t for e in got[j] if not e.get("stop") for t in e["tokens"]] == want[j]
+    assert got[1][-1]["timings"]["prompt_filled_n"] == 1100 - 256
+    assert sched.stats["interleaved_rounds"] > 0
+    from ridgefill_data_b200.ops._ext import check_errors
+    torch.cuda.synchronize()
+    check_errors()
