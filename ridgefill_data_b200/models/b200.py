@@ -140,24 +140,57 @@ class _B200:
     def _attn_mix(self, i, h, pos, cache):
         """Attention block output added to h (new tensor) and the mixer output when asked."""
         w = self.W[i]
-        n = h.shape[0]
-        hd, hq, hkv = self.head_dim, self.n_heads, self.n_kv
-        gated = self.cfg.gated_attn
-        qw = hq * hd * (2 if gated else 1)
         x = self._norm(h, w["ln1"])
         qkv = G.linear(x, w["qkv_p"])
+        o = torch.empty(h.shape[0], self.n_heads * self.head_dim, dtype=self.dtype, device=self.device)
+        return self._attn_core(i, qkv, pos, cache[i], o)
+
+    def _attn_core(self, i, qkv, pos, c, o):
+        """From the projected rows qkv [n, q(+gate) | k | v] of one sequence: K/V appended to its cache c, q head
+        norm + RoPE, causal attention over the cache into o [n, hq * hd] (times the gate when the model has one)."""
+        w = self.W[i]
+        n = qkv.shape[0]
+        hd, hq = self.head_dim, self.n_heads
+        gated = self.cfg.gated_attn
+        qw = hq * hd * (2 if gated else 1)
         p0, parr = self._span(pos)
-        c = cache[i]
         n0 = self._write_kv(i, qkv[:, qw:], pos, c)
         q = torch.empty(hq, n, hd, dtype=self.dtype, device=self.device)
         tables = self.rope(p0 + n if parr is None else int(pos.max()) + 1)
         K.head_norm_rope(qkv, hq, hd, 2 * hd if gated else hd, q, n * hd, hd, norm_w=w.get("q_norm"),
                          norm_mode=self._qk_mode(), eps=self.eps, tables=tables, rot=self.cfg.rot_dim, pos=parr,
                          pos_offset=p0)
-        o = torch.empty(n, hq * hd, dtype=self.dtype, device=self.device)
         K.attention(q, c["kbuf"], c["vbuf"], n0 + n, self.scale, o, q_start=n0,
                     gate=qkv[:, hd:] if gated else None, gate_head=2 * hd)
         return o
+
+    def decode_batch(self, toks, positions, caches):
+        """R sequences advanced by one token each in one pass over the weights: the embedding, every projection,
+        MLP (or MoE) and the logits run on the R stacked rows; only the per-sequence parts (K/V append and
+        attention over that sequence's cache, the GDN conv and recurrent step on its state) run per row. Every
+        GEMM computes its rows independently, so each row equals the single-sequence step bitwise."""
+        if self.tp is not None or len(toks) == 1:
+            return super().decode_batch(toks, positions, caches)
+        R = len(toks)
+        h = self.embed(torch.tensor([int(t) for t in toks], device=self.device))
+        pos = [torch.tensor([int(p)], device=self.device) for p in positions]
+        for i in range(self.n_layers):
+            w = self.W[i]
+            x = self._norm(h, w["ln1"])
+            if self.layer_types[i] == "attn":
+                qkv = G.linear(x, w["qkv_p"])
+                y = torch.empty(R, self.n_heads * self.head_dim, dtype=self.dtype, device=self.device)
+                for r in range(R):
+                    self._attn_core(i, qkv[r:r + 1], pos[r], caches[r][i], y[r:r + 1])
+                wo = w["o"]
+            else:
+                proj = G.linear(x, w["in_p"])
+                o = torch.cat([self._gdn_core_dev(i, proj[r:r + 1], caches[r], True) for r in range(R)])
+                z = proj[:, self.conv_dim + 2 * self.nv:]
+                y = K.gated_rmsnorm(o, z, w["norm"], self.nv, self.cfg.gdn_dv, self.eps)
+                wo = w["out"]
+            h = self.mlp(i, G.linear(y, wo, residual=h))
+        return self.logits(h)
 
     # ---- per-layer API
     def _mixer_out(self, i, h, pos, cache, need_out=True):

@@ -151,6 +151,19 @@ class Model:
         tp = getattr(self, "tp", None)
         return h.clone() if tp is not None and hasattr(tp, "owns") and tp.owns(h) else h
 
+    def decode_batch(self, toks, positions, caches):
+        """Next-token logits [R, V] fp32 of R independent sequences advanced by one token each: token toks[r] at
+        position positions[r] over caches[r] (appended in place). This reference version runs the sequences one
+        after another; the B200 model batches every projection and MLP over the R rows."""
+        outs = []
+        for t, p, c in zip(toks, positions, caches):
+            pos = torch.tensor([int(p)], device=self.device)
+            h = self.embed(torch.tensor([int(t)], device=self.device))
+            for i in range(self.n_layers):
+                h = self.layer(i, h, pos, c)
+            outs.append(self.logits(h))
+        return torch.cat(outs)
+
     def forward_exact(self, ids, hook=None, cache=None, keep=None, gdn_checkpoint_every=None, mix=None):
         """Exact forward over all rows. hook(i, h) sees each layer's input and hook('final', h) the
         final-norm input; mix(i, a) each layer's mixer output. keep: row indices whose logits to return."""

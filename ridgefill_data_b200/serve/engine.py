@@ -2,7 +2,9 @@
 
 One worker thread owns the model. Requests wait in a FIFO queue; the worker takes one at a time for prefill and
 keeps every started request in the decode set until it has produced its tokens. Each decode round advances every
-active request by one greedy token (an exact full-model step over its own cache). A long prefill does not stall
+active request by one greedy token (an exact full-model step over its own cache); the requests of a round go
+through the model together (`decode_batch`: one pass over the weights, per-sequence attention and recurrent
+state), which is what makes concurrent streams cheap on a weight-bandwidth-bound decode. A long prefill does not stall
 the running streams: the engine's layer loop calls `tick(i)` before every layer, and every `interleave` layers the
 worker runs one decode round for the other requests, so their inter-token gap during a prefill is bounded by
 `interleave` layers of that prefill instead of all of it (the quantity the fixed-arrival mix measures). Under
@@ -54,11 +56,12 @@ class Request:
 
 
 class Scheduler:
-    def __init__(self, model, eos=(), interleave=4, max_active=64, sync=None):
+    def __init__(self, model, eos=(), interleave=4, max_active=64, max_batch=32, sync=None):
         self.model = model
         self.eos = frozenset(int(e) for e in eos)
         self.interleave = int(interleave)
         self.max_active = int(max_active)
+        self.max_batch = int(max_batch)
         self.waiting = queue.Queue()
         self.active = []
         self._stop = threading.Event()
@@ -68,7 +71,7 @@ class Scheduler:
         self.sync = sync if sync is not None else (torch.cuda.synchronize if model.device.type == "cuda"
                                                   else (lambda: None))
         self.stats = dict(requests=0, completed=0, errors=0, prompt_tokens=0, predicted_tokens=0,
-                          filled_tokens=0, interleaved_rounds=0)
+                          filled_tokens=0, interleaved_rounds=0, decode_batches=0)
         self.ttft_ms, self.prompt_ms = [], []
         self._lock = threading.Lock()
 
@@ -186,11 +189,36 @@ class Scheduler:
 
     @torch.no_grad()
     def _decode_round(self):
-        keep = []
-        for req in list(self.active):
+        """One token for every active request: the plain ones together through model.decode_batch (one pass over
+        the weights for all of them, up to max_batch rows at a time), SwiftKV-native ones alone (their late layers
+        run a different path)."""
+        reqs = list(self.active)
+        plain = [r for r in reqs if r.arm.fill != "swiftkv_native"]
+        toks = {}
+        for j in range(0, len(plain), self.max_batch):
+            grp = plain[j:j + self.max_batch]
             try:
-                logits = D.step(self.model, req.tok, req.position, req.cache, req.arm)
-                tok = int(D.check_finite(logits[-1], f"{req.rid} decode").argmax())
+                logits = self.model.decode_batch([r.tok for r in grp], [r.position for r in grp],
+                                                 [r.cache for r in grp])
+                self.stats["decode_batches"] += 1
+                for r, row in zip(grp, logits):
+                    toks[id(r)] = row
+            except Exception as e:          # a failed batch may have appended to some caches: end its requests
+                for r in grp:
+                    toks[id(r)] = e
+        for r in reqs:
+            if r.arm.fill == "swiftkv_native":
+                try:
+                    toks[id(r)] = D.step(self.model, r.tok, r.position, r.cache, r.arm)[-1]
+                except Exception as e:
+                    toks[id(r)] = e
+        keep = []
+        for req in reqs:
+            row = toks[id(req)]
+            try:
+                if isinstance(row, Exception):
+                    raise row
+                tok = int(D.check_finite(row, f"{req.rid} decode").argmax())
             except Exception as e:
                 self.stats["errors"] += 1
                 self._emit(req, {"error": f"{type(e).__name__}: {e}", "stop": True})

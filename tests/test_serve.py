@@ -148,3 +148,19 @@ def test_token_metrics_checks():
         C.token_metrics(ev[:2], 3)
     with pytest.raises(C.StreamError):
         C.token_metrics([dict(t=0, data=dict(error="x"))], 1)
+
+
+def test_decode_batch_matches_single_steps(setup):
+    """The model's batched decode (R sequences, one token each) equals R single steps."""
+    from ridgefill_data_b200.engine.decode import fork_cache, step
+    model, arms = setup
+    seqs = []
+    for s, n in ((11, 33), (12, 50), (13, 70)):
+        ids = uniform_prompt(n, CFG.vocab, seed=s)
+        logits, cache, _ = prefill(model, ids, arms["on"] if n > TAIL else arms["off"], keep=1)
+        seqs.append((int(logits[-1].argmax()), n, cache))
+    single = [step(model, t, p, fork_cache(c), None) for t, p, c in seqs]
+    batched = model.decode_batch([t for t, _, _ in seqs], [p for _, p, _ in seqs], [fork_cache(c) for _, _, c in seqs])
+    assert batched.shape == (3, CFG.vocab)
+    for r in range(3):
+        assert torch.equal(batched[r], single[r][-1])

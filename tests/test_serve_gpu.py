@@ -55,3 +55,25 @@ def test_scheduler_b200_interleaved_streams_match_engine():
     from ridgefill_data_b200.ops._ext import check_errors
     torch.cuda.synchronize()
     check_errors()
+
+
+@pytest.mark.parametrize("gated", [True, False])
+def test_decode_batch_b200_matches_single_steps(gated):
+    """decode_batch on the sm_100a model: every row bitwise equal to that sequence's single decode step."""
+    from ridgefill_data_b200.engine.decode import fork_cache, step
+    cfg = HYB if gated else ModelConfig(arch="llama", n_layers=4, hidden=512, vocab=1024, n_heads=8, n_kv=2,
+                                        head_dim=64, intermediate=1536, eps=1e-5, rope_theta=5e5,
+                                        name="tiny-llama-gpu")
+    model = from_config(cfg, seed=0, device="cuda", std=0.05, backend="b200")
+    g = torch.Generator().manual_seed(9)
+    seqs = []
+    with torch.no_grad():
+        for n in (200, 333, 517):
+            ids = torch.randint(0, cfg.vocab, (n,), generator=g).cuda()
+            logits, cache, _ = prefill(model, ids, Arm("exact"), keep=1)
+            seqs.append((int(logits[-1].argmax()), n, cache))
+        single = [step(model, t, p, fork_cache(c), None)[-1] for t, p, c in seqs]
+        batched = model.decode_batch([t for t, _, _ in seqs], [p for _, p, _ in seqs],
+                                     [fork_cache(c) for _, _, c in seqs])
+    for r in range(3):
+        assert torch.equal(batched[r], single[r]), (batched[r] - single[r]).abs().max()
