@@ -13,18 +13,59 @@ class ExtensionMissing(RuntimeError):
     pass
 
 
+class KernelError(RuntimeError):
+    def __init__(self, op, code):
+        super().__init__(f"{op}: sm_100a kernel reported error code {code}: {ERROR_CODES.get(code, 'unknown')}")
+        self.op, self.code = op, code
+
+
+class Checked:
+    """Debug proxy over the extension (RF_CHECK_EACH=1 in the environment): after every call it synchronizes the
+    device and reads the error word, so the first op whose kernel recorded an error (a timed-out bounded wait, a bad
+    shape or index) is named in the exception instead of surfacing at a later check. Slow: for debugging only."""
+
+    PASS = frozenset(("error_word", "launch_count"))
+
+    def __init__(self, mod, sync=None, device=None):
+        self._mod = mod
+        self._sync = sync
+        self._device = device
+
+    def __getattr__(self, name):
+        f = getattr(self._mod, name)
+        if not callable(f) or name in self.PASS:
+            return f
+
+        def call(*a, **k):
+            import torch
+            out = f(*a, **k)
+            (self._sync or torch.cuda.synchronize)()
+            dev = self._device() if self._device else torch.cuda.current_device()
+            w = self._mod.error_word(dev)
+            code = int(w.item())
+            if code:
+                w.zero_()
+                raise KernelError(name, code)
+            return out
+        call.__name__ = name
+        return call
+
+
 def ext():
     global _mod, _err
     if _mod is not None:
         return _mod
+    import os
+
     import torch  # noqa: F401  (loads libc10 / libtorch, which the extension links against)
     try:
-        _mod = importlib.import_module("ridgefill_data_b200._C")
+        mod = importlib.import_module("ridgefill_data_b200._C")
     except ImportError as e:  # pragma: no cover - depends on the build
         _err = e
         raise ExtensionMissing(
             "the sm_100a extension ridgefill_data_b200._C is not built; run `python setup.py build_ext --inplace`"
         ) from e
+    _mod = Checked(mod) if os.environ.get("RF_CHECK_EACH") == "1" else mod
     return _mod
 
 
