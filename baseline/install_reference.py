@@ -6,7 +6,8 @@
    "not installable".
 2. Then the reference's importable package, `code/kva` (plain PyTorch; imports torch and safetensors only), is
    copied file for file, unmodified, to baseline/_ref/kva, and baseline/_ref/INSTALL.json records the pip outcome and
-   every copied file's sha256 (the reference arm re-hashes them before it runs and refuses a modified copy).
+   every copied file's sha256 (the reference arm re-hashes them before it runs and refuses a modified copy). Its
+   protocol file and paper run configs are copied beside it as data for the configuration-compatibility tests.
 
     python baseline/install_reference.py SRC        # SRC: the reference checkout (its root, holding code/kva)
 """
@@ -47,9 +48,17 @@ def main(argv):
             (target / rel).parent.mkdir(parents=True, exist_ok=True)
             shutil.copyfile(f, target / rel)
             record["files"][rel.as_posix()] = sha256(f)
-        for extra in ("LICENSE",):
+        for extra in ("LICENSE", "protocol.json"):
             if (src / "code" / extra).is_file():
                 shutil.copyfile(src / "code" / extra, DST / extra)
+                record["files_data"] = dict(record.get("files_data", {}), **{extra: sha256(src / "code" / extra)})
+        cfg_src = src / "code" / "configs"           # the paper's run configs: compatibility test data
+        if cfg_src.is_dir():
+            if (DST / "configs").exists():
+                shutil.rmtree(DST / "configs")
+            shutil.copytree(cfg_src, DST / "configs")
+            for f in sorted((DST / "configs").rglob("*.json")):
+                record.setdefault("files_data", {})["configs/" + f.relative_to(DST / "configs").as_posix()] = sha256(f)
     (DST / "INSTALL.json").write_text(json.dumps(record, indent=1))
     print(json.dumps(dict(pip_returncode=pip.returncode, pip=tail[-1] if tail else "", copied=len(record["files"]))))
 

@@ -4,7 +4,8 @@ work (code/kva/protocol.py:182-284 role: refuse a bad config by name, early).
 A config JSON: {"model": preset name or checkpoint dir, "arms": [spec, ...], "prompts": {...}, "out": dir}.
 An arm spec: {"name", "split", "tail", "fill", "projector" (map file), "st" (correction file), "select",
 "fill_by_type", "context", "refresh", "refresh_projector", "tail_bias_from", "tail_bias_skip_last",
-"exact_part", "rescale", "rescale_skip_last", "tail_from", "f1", "kvfold"}.
+"exact_part", "rescale", "rescale_skip_last", "tail_from", "f1", "kvfold", "repair", "repair_by", "sets",
+"reuse_fill", "tail_round"}.
 """
 from __future__ import annotations
 
@@ -17,7 +18,8 @@ from .select import KINDS
 
 SPEC_KEYS = {"name", "split", "tail", "fill", "projector", "st", "select", "fill_by_type", "context", "refresh",
              "refresh_projector", "tail_bias_from", "tail_bias_skip_last", "exact_part", "rescale",
-             "rescale_skip_last", "tail_from", "f1", "kvfold", "repair", "repair_by"}
+             "rescale_skip_last", "tail_from", "f1", "kvfold", "repair", "repair_by", "sets", "reuse_fill",
+             "tail_round"}
 
 
 class ConfigError(ValueError):
@@ -37,7 +39,10 @@ def validate_spec(spec, n_layers):
         s = spec.get("split")
         if not isinstance(s, int) or not 0 < s < n_layers:
             raise ConfigError(f"arm {name}: split {s!r} must be an int in (0, {n_layers})")
-        if fill != "swiftkv_native" and (not isinstance(spec.get("tail"), int) or spec["tail"] < 1):
+        if spec.get("tail_from") is not None:
+            if spec["tail_from"] != "continuation" or "tail" in spec:
+                raise ConfigError(f"arm {name}: tail_from 'continuation' sets the tail per prompt (no 'tail')")
+        elif fill != "swiftkv_native" and (not isinstance(spec.get("tail"), int) or spec["tail"] < 1):
             raise ConfigError(f"arm {name}: tail must be a positive int")
     if fill == "proj" and "projector" not in spec:
         raise ConfigError(f"arm {name}: fill 'proj' needs a projector file")

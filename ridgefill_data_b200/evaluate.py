@@ -1,6 +1,13 @@
-"""Evaluation CLI: arms x prompts x task, one atomic JSON record per prompt (resumable).
+"""Evaluation CLI: arms x prompts, one atomic JSON record per prompt (resumable).
 
-  python -m ridgefill_data_b200.evaluate CONFIG.json TASK
+  python -m ridgefill_data_b200.evaluate CONFIG.json SET [--only a,b] [--limit k] [--canary check|accept|reset|off]
+
+Configs in the research harness's format (no "prompts" block; its arm keys, $KVA_DATA / $RF_DATA paths) run the
+harness's evaluation sets: SET = grade | niah | niahg | multiturn | ruler | longbench | longppl | decode
+(eval/harness.py: protocol validation, canary, shared lower layers, selectors, reuse_fill, tail_round, tail_from,
+oracle / context / refresh arms, key-token tails, per-prompt records with the harness's field names).
+
+Configs with a "prompts" block run this framework's synthetic-set tasks (TASK below):
 
 CONFIG: {"model": preset or checkpoint dir, "seed": 0, "backend": "b200"|"torch", "arms": [arm specs]
 (engine/spec.py), "prompts": {"kind": ..., "lengths": [...], "count": k, "seed": s}, "out": results dir, "keep":
@@ -148,16 +155,94 @@ def run_prompt(model, arms, prm, task, keep, tok=None):
     return rec
 
 
+TASKS = ("quality", "ppl", "niah", "generate", "decode", "speed")
+
+
+def harness_main(cfg, a):
+    """The research harness's sets (eval/harness.py) for a config in its format."""
+    import os
+
+    from .engine import protocol as PR
+    from .eval import harness as H
+    from .eval import text as TX
+    from .models.base import from_config, load
+    from .models.config import PRESETS
+    from .utils import canary, gpu, prov
+    if a.set not in H.SETS:
+        raise SystemExit(f"set {a.set!r}: one of {H.SETS} (configs without a 'prompts' block)")
+    source = a.set
+    if a.set == "decode":
+        source = cfg.get("decode_from")
+    if a.set == "multiturn" and cfg.get("multiturn_from", "mk4") == "ruler":
+        source = "ruler"
+    dry = os.environ.get("RF_CPU_DRYRUN") == "1"
+    stamp = None if (dry and "protocol" not in cfg) else PR.validate(cfg, set_name=source)
+    device, gpu_info = gpu.setup()
+    backend = cfg.get("backend", "b200" if device.type == "cuda" else "torch")
+    dtype = torch.float32 if cfg.get("dtype") == "fp32" else torch.bfloat16
+    tok_path = cfg.get("tokenizer", cfg["model"])
+    tok = TX.tokenizer(tok_path)
+    name = Path(str(cfg["model"])).name
+    if cfg["model"] in PRESETS:
+        model = from_config(PRESETS[cfg["model"]], seed=cfg.get("seed", 0), device=device, backend=backend,
+                            dtype=dtype)
+    else:
+        model = load(cfg["model"], device=device, backend=backend, dtype=dtype)
+    root = Path(cfg.get("out", "results"))
+    out = root / f"{a.set}-{cfg['name']}"
+    out.mkdir(parents=True, exist_ok=True)
+    eos = TX.eos_ids(tok_path, tok) if tok_path != "char" else (tok.eos_token_id,)
+    try:
+        h = H.Harness(model, tok, cfg, a.set, out, eos=eos)
+    except H.EvalError as e:
+        raise SystemExit(f"refusing: {e}")
+    if a.canary != "off":
+        split = min(x.split for x in h.arms if x.split is not None) if any(x.split for x in h.arms) else \
+            model.n_layers // 2
+        print(f"canary: {canary.check(model, root, split, 'record' if a.canary in ('accept', 'reset') else 'check')}")
+    try:
+        protocol = PR.load()
+    except OSError:
+        protocol = {"models": {name: {"niah_format": cfg.get("niah_format", "raw")}}}
+    prompts, extra = H.set_prompts(a.set, cfg, tok, name, protocol)
+    if a.set == "niahg":
+        trim = cfg.get("niahg_tail", max(x.tail for x in h.arms if x.split is not None))
+        prompts = [q for q in prompts if q["needle_end"] <= len(q["ids"]) - trim]
+        extra["niahg_tail"] = trim
+    only = a.only or cfg.get("only", "")
+    if only:
+        prompts = [q for q in prompts if q["name"] in only.split(",")]
+    if a.limit:
+        prompts = prompts[:a.limit]
+    run_cfg = dict(config=cfg, protocol=stamp, set=a.set, keep=H.KEEP, niah_steps=H.NIAH_STEPS,
+                   file_sha256=h.files.hashes, **extra)
+    try:
+        n = h.run(prompts, prov.provenance(cfg["model"], run_cfg, gpu_info))
+    except H.EvalError as e:
+        raise SystemExit(f"refusing: {e}")
+    print(f"done: {n} prompts run, {len(prompts) - n} already complete")
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("config")
-    ap.add_argument("task", choices=("quality", "ppl", "niah", "generate", "decode", "speed"))
+    ap.add_argument("set", help="harness set (grade niah niahg multiturn ruler longbench longppl decode) or, for "
+                                "configs with a 'prompts' block, a task (quality ppl niah generate decode speed)")
+    ap.add_argument("--only", default="")
+    ap.add_argument("--limit", type=int, default=0)
+    ap.add_argument("--canary", choices=("check", "accept", "reset", "off"), default="check")
     a = ap.parse_args(argv)
     from .engine import spec
     from .models.base import from_config, load
     from .models.config import PRESETS, ModelConfig
     from .utils import prov
     cfg = spec.load(a.config)
+    if "prompts" not in cfg:
+        return harness_main(cfg, a)
+    a.task = a.set
+    if a.task not in TASKS:
+        raise SystemExit(f"task {a.task!r}: one of {TASKS} (configs with a 'prompts' block)")
     mcfg = PRESETS[cfg["model"]] if cfg["model"] in PRESETS else ModelConfig.from_dir(cfg["model"])
     spec.validate(cfg, mcfg.n_layers)
     stamp = None
