@@ -42,6 +42,10 @@ def main(argv=None):
     ap.add_argument("--from-stats", nargs="+")
     ap.add_argument("--list-docs")
     ap.add_argument("--data-parallel", action="store_true")
+    ap.add_argument("--unitrms", action="store_true",
+                    help="also fit unit-RMS targets y / rms(y) (the raw fit becomes the control: -rawctl)")
+    ap.add_argument("--kvfold", action="store_true",
+                    help="also fit the K/V fold: late attention layers' pre-RoPE [k | v] from b / rms(b)")
     a = ap.parse_args(argv)
     if a.list_docs:
         st = torch.load(a.list_docs, map_location="cpu", weights_only=False)
@@ -100,9 +104,10 @@ def main(argv=None):
         print(f"weighted ({a.weight}) split {splits[0]}: {len(maps)} lambdas fitted")
         return 0
     res = sweep.fit(model, docs, splits, lams, held=held, out_dir=a.out, solver=a.solver, center=not a.plain,
-                    save_stats=a.save_stats, group=group)
+                    save_stats=a.save_stats, group=group, unitrms=a.unitrms, kvfold=a.kvfold)
     for S, r in sorted(res.items()):
-        print(f"split {S}: lambda* {r['lambda_star']}  maps for layers {S}..{model.n_layers - 1}")
+        extra = "".join(f"; {k} lambda* {r[k]['lambda_star']}" for k in ("unitrms", "kvfold") if k in r)
+        print(f"split {S}: lambda* {r['lambda_star']}  maps for layers {S}..{model.n_layers - 1}{extra}")
     return 0
 
 

@@ -53,13 +53,34 @@ def _common_shifts(model, doc, splits, group):
     return {i: buf[i - lo] for i in range(lo, L)}
 
 
-def capture(model, docs, splits, device=None, log=print, group=None):
+def unit_rms(model, h):
+    """h / rms(h) in fp32 (rms with the model's norm eps): the direction a late layer's input norm keeps."""
+    hf = h.float()
+    return hf * torch.rsqrt(hf.square().mean(-1, keepdim=True) + model.eps)
+
+
+def capture(model, docs, splits, device=None, log=print, group=None, unitrms=False, kvfold=False):
     """{S: RidgeStats} over the documents (forward_exact with a capture hook). With a process group the documents
     are split over the ranks (data parallel), every rank uses rank 0's shifts, and the fp64 sums are added over
-    the ranks at the end (one reduction per statistic: each rank keeps its partial sums on the device until then)."""
+    the ranks at the end (one reduction per statistic: each rank keeps its partial sums on the device until then).
+    unitrms / kvfold: also the sums of the extra targets (same capture pass), returned as stats["unitrms"][S] (x =
+    h_S, targets y_i / rms(y_i)) and stats["kvfold"][S] (x = h_S / rms(h_S), targets the pre-RoPE [k | v] of
+    every late attention layer, with their per-feature sums of squares "sq")."""
     L, H = model.n_layers, model.hidden
     dev = device or model.device
     stats = {S: RidgeStats(S, range(S, L), H, dev) for S in splits}
+    extra = {}
+    if (unitrms or kvfold) and group is not None:
+        raise ValueError("the unit-RMS and K/V-fold sums are captured on one process (no data-parallel capture)")
+    if unitrms:
+        extra["unitrms"] = {S: RidgeStats(S, range(S, L), H, dev) for S in splits}
+    if kvfold:
+        from ..engine.prefill import kv_target
+        kv_dim = 2 * model.n_kv * model.head_dim
+        extra["kvfold"] = {S: RidgeStats(S, [i for i in range(S, L) if model.layer_types[i] == "attn"], H, dev,
+                                         out_dim=kv_dim) for S in splits}
+        sq = {S: {i: torch.zeros(kv_dim, dtype=torch.float64, device=dev) for i in extra["kvfold"][S].layers}
+              for S in splits}
     if group is not None:
         import torch.distributed as dist
         shifts = _common_shifts(model, docs[0], splits, group)
@@ -76,9 +97,21 @@ def capture(model, docs, splits, device=None, log=print, group=None):
                     return
                 if i in stats:
                     stats[i].begin(h)
+                    if unitrms:
+                        extra["unitrms"][i].begin(h)
+                    if kvfold:
+                        extra["kvfold"][i].begin(unit_rms(model, h))
+                u = unit_rms(model, h) if unitrms else None
+                kv = kv_target(model, i, h) if kvfold and model.layer_types[i] == "attn" else None
                 for S, st in stats.items():
                     if S <= i:
                         st.add_layer(i, h)
+                        if unitrms:
+                            extra["unitrms"][S].add_layer(i, u)
+                        if kv is not None:
+                            extra["kvfold"][S].add_layer(i, kv)
+                            c = extra["kvfold"][S].cy[i].to(kv.device)
+                            sq[S][i] += (kv.float() - c).double().square().sum(0).to(dev)
             model.forward_exact(torch.as_tensor(d["ids"]).to(model.device), hook=hook)
             if log and (j % 10 == 0 or j == len(docs) - 1):
                 log(f"capture {j + 1}/{len(docs)} rows {int(stats[splits[0]].n)} ({time.time() - t0:.0f}s)")
@@ -90,6 +123,10 @@ def capture(model, docs, splits, device=None, log=print, group=None):
             st.n = float(n.item())
             for t in [st.sx, st.sxx] + list(st.sy.values()) + list(st.sxy.values()):
                 dist.all_reduce(t, group=group)
+    if kvfold:
+        for S, st in extra["kvfold"].items():
+            st.sq = sq[S]
+    stats.update(extra)
     return stats
 
 
@@ -142,29 +179,68 @@ def fit_split(stats_state, S, L, lams, solver="eigen", center=True, device=None)
     return fit.layers(late, lams)
 
 
+def select_lambda_kv(model, held, S, fold_maps, lams):
+    """K/V-fold lambda selection: per candidate, the mean over held documents, late attention layers and K / V of
+    the per-row-per-head cosine between the fold's prediction and the true pre-RoPE K / V."""
+    from ..engine.prefill import kv_target
+    late = [i for i in range(S, model.n_layers) if model.layer_types[i] == "attn"]
+    sums = {lam: {i: 0.0 for i in late} for lam in lams}
+    count = 0
+    hd = model.head_dim
+    with torch.no_grad():
+        for d in held:
+            got = {}
+            model.forward_exact(torch.as_tensor(d["ids"]).to(model.device),
+                                hook=lambda i, h: got.__setitem__(i, h) if i != "final" and i >= S else None)
+            u = unit_rms(model, got[S])
+            count += 1
+            for i in late:
+                true = kv_target(model, i, got[i]).float().unflatten(-1, (-1, hd))
+                for lam in lams:
+                    w, b = fold_maps[lam][i]
+                    pred = F.linear(u, w.to(u.device), b.to(u.device)).unflatten(-1, (-1, hd))
+                    sums[lam][i] += F.cosine_similarity(pred, true, dim=-1).mean().item()
+    per_layer = {str(lam): {i: v / count for i, v in s.items()} for lam, s in sums.items()}
+    mean = {c: sum(v.values()) / max(1, len(v)) for c, v in per_layer.items()}
+    return max(lams, key=lambda lam: mean[str(lam)]), mean, per_layer
+
+
 def fit(model, docs, splits, lambdas=LAMBDAS, held=None, out_dir=None, name=None, solver=None, center=True,
-        save_stats=False, log=print, meta_extra=None, group=None):
+        save_stats=False, log=print, meta_extra=None, group=None, unitrms=False, kvfold=False):
     """Fit maps for every split. Returns {S: dict(projector, lambda_star, mean_read_cos, per_layer_read_cos,
-    record)}; writes files when out_dir is given."""
+    record)}; writes files when out_dir is given. unitrms: also the unit-RMS-target maps of the same capture,
+    saved as <name>-sweep-s<S>-unitrms with the raw fit as its control <name>-sweep-s<S>-rawctl
+    (results[S]["unitrms"]); kvfold: also the K/V fold (pre-RoPE [k | v] of every late attention layer straight
+    from the unit-RMS boundary state), saved as <name>-kvfold-s<S> (results[S]["kvfold"])."""
     splits = sorted(int(s) for s in splits)
     name = name or model.cfg.name or "model"
     L = model.n_layers
     rows = sum(len(d["ids"]) for d in docs)
     out_dir = Path(out_dir) if out_dir else None
-    proj_path = (lambda S: out_dir / f"{name}-sweep-s{S}.safetensors") if out_dir else None
+    raw_suffix = "-rawctl" if (unitrms or kvfold) else ""
+    proj_path = (lambda S, sfx=raw_suffix: out_dir / f"{name}-sweep-s{S}{sfx}.safetensors") if out_dir else None
     if out_dir:
         out_dir.mkdir(parents=True, exist_ok=True)
-        stale = stale_projectors([proj_path(S) for S in splits], rows)
+        paths = [proj_path(S) for S in splits] + ([proj_path(S, "-unitrms") for S in splits] if unitrms else [])
+        stale = stale_projectors(paths, rows)
         if stale:
             raise StaleProjector("fitted on another calibration list: " + ", ".join(f"{p} ({r})" for p, r in stale))
     solver = solver or ("cholesky" if model.device.type == "cuda" else "eigen")
-    stats = capture(model, docs, splits, log=log, group=group)
+    stats = capture(model, docs, splits, log=log, group=group, unitrms=unitrms, kvfold=kvfold)
+    extra = {k: stats.pop(k) for k in ("unitrms", "kvfold") if k in stats}
     results = {}
     for S in sorted(splits, reverse=True):
         t0 = time.time()
         state = stats[S].state()
         if out_dir and save_stats:
-            torch.save(dict(state, dtype="float64", docs=[d["name"] for d in docs], model=name),
+            more = {}
+            if unitrms:
+                u = extra["unitrms"][S].state()
+                more["unitrms"] = dict(cy=u["cy"], sy=u["sy"], sxy=u["sxy"])
+            if kvfold:
+                more["kvfold"] = dict(extra["kvfold"][S].state(), sq={i: v.cpu() for i, v in
+                                                                      extra["kvfold"][S].sq.items()})
+            torch.save(dict(state, dtype="float64", docs=[d["name"] for d in docs], model=name, **more),
                        out_dir / f"{name}-s{S}.pt")
         maps = fit_split(state, S, L, lambdas, solver, center, model.device)
         if held:
@@ -192,4 +268,61 @@ def fit(model, docs, splits, lambdas=LAMBDAS, held=None, out_dir=None, name=None
                 f"(identity {mean.get('identity', float('nan')):.4f}) in {time.time() - t0:.1f}s")
         results[S] = dict(projector=proj, lambda_star=best, mean_read_cos=mean, per_layer_read_cos=per_layer,
                           record=record, maps=maps)
+        if unitrms:
+            results[S]["unitrms"] = _fit_extra(model, extra["unitrms"][S].state(), S, lambdas, held, solver, center,
+                                               "unitrms", name, rows, docs, meta, out_dir, proj_path, write, log)
+        if kvfold:
+            results[S]["kvfold"] = _fit_kvfold(model, extra["kvfold"][S], S, lambdas, held, name, rows, docs,
+                                               meta, out_dir, write, log)
     return results
+
+
+def _fit_extra(model, state, S, lambdas, held, solver, center, kind, name, rows, docs, meta, out_dir, proj_path,
+               write, log):
+    """The unit-RMS-target maps of split S: same grid and held-out selection as the raw fit."""
+    L = model.n_layers
+    maps = fit_split(state, S, L, lambdas, solver, center, model.device)
+    best, mean, per_layer = (select_lambda(model, held, S, maps, lambdas) if held
+                             else (lambdas[len(lambdas) // 2], {}, {}))
+    W = {i: maps[best][i][0].to(torch.bfloat16).cpu() for i in range(S, L)}
+    B = {i: maps[best][i][1].to(torch.bfloat16).cpu() for i in range(S, L)}
+    m = dict(meta, lam=best, target="y / rms(y)")
+    proj = Projector(S, W, B, {k: str(v) for k, v in dict(m, split=S).items()})
+    record = dict(rows=rows, docs=len(docs), lambda_star=best, mean_read_cos=mean, per_layer_read_cos=per_layer,
+                  target="y / rms(y)")
+    if write:
+        path = proj_path(S, "-unitrms")
+        proj.save(path, m)
+        record.update(projector=str(path), projector_sha256=prov.sha256(path))
+        prov.write_json(out_dir / f"fit-sweep-{name}-s{S}-{kind}.json", record)
+    if log:
+        log(f"S={S} {kind}: lambda* {best} read cos {mean.get(str(best), float('nan')):.4f}")
+    return dict(projector=proj, lambda_star=best, mean_read_cos=mean, record=record)
+
+
+def _fit_kvfold(model, st, S, lambdas, held, name, rows, docs, meta, out_dir, write, log):
+    """The K/V fold of split S: ridge from the unit-RMS boundary state to every late attention layer's pre-RoPE
+    [k | v] (EigenFit: the outputs are narrower than the input), lambda by held-out K / V cosine."""
+    from .projector import KVFold
+    state = st.state()
+    fit_ = EigenFit(state, center=True)
+    maps = {lam: {} for lam in lambdas}
+    for i in st.layers:
+        for lam, wb in fit_.layer(i, lambdas).items():
+            maps[lam][i] = wb
+    best, mean, per_layer = (select_lambda_kv(model, held, S, maps, lambdas) if held
+                             else (lambdas[len(lambdas) // 2], {}, {}))
+    W = {i: maps[best][i][0].to(torch.bfloat16).cpu() for i in st.layers}
+    B = {i: maps[best][i][1].to(torch.bfloat16).cpu() for i in st.layers}
+    m = dict(meta, lam=best, target="pre-RoPE [k | v] from b / rms(b)")
+    fold = KVFold(S, W, B, model.n_kv, model.eps, {k: str(v) for k, v in dict(m, split=S).items()})
+    record = dict(rows=rows, docs=len(docs), lambda_star=best, mean_kv_cos=mean, per_layer_kv_cos=per_layer,
+                  layers=st.layers)
+    if write:
+        path = out_dir / f"{name}-kvfold-s{S}.safetensors"
+        fold.save(path, m)
+        record.update(projector=str(path), projector_sha256=prov.sha256(path))
+        prov.write_json(out_dir / f"fit-kvfold-{name}-s{S}.json", record)
+    if log:
+        log(f"S={S} kvfold: lambda* {best} K/V cos {mean.get(str(best), float('nan')):.4f}")
+    return dict(projector=fold, lambda_star=best, mean_kv_cos=mean, record=record)

@@ -109,3 +109,37 @@ def test_st_roundtrip(tmp_path):
     rp.save_st(tmp_path / "c.safetensors", st)
     got = rp.load_st(tmp_path / "c.safetensors")
     assert torch.equal(got[9], st[9])
+
+
+def test_unitrms_and_kvfold_fits(tmp_path):
+    """--unitrms / --kvfold: one capture gives the raw control, the unit-RMS-target maps and the K/V fold; the fold
+    predicts the late attention layers' pre-RoPE K / V from the unit-RMS boundary state better than chance, and
+    the files load back (KVFold with its n_kv / eps)."""
+    import torch
+    from ridgefill_data_b200.engine.prefill import kv_target
+    from ridgefill_data_b200.eval.data import zipf_docs
+    from ridgefill_data_b200.models.base import from_config
+    from ridgefill_data_b200.models.tiny import tiny_configs
+    from ridgefill_data_b200.ridge import sweep
+    from ridgefill_data_b200.ridge.projector import KVFold, Projector
+    cfg = tiny_configs(8, 64)["qwen3.5-9b"]
+    model = from_config(cfg, seed=0, device="cpu", dtype=torch.float32)
+    docs = zipf_docs(6, 256, 4000, seed=3)
+    held = zipf_docs(2, 256, 4000, seed=4)
+    res = sweep.fit(model, docs, [4], (1e-3, 1e-1), held=held, out_dir=tmp_path, name="tiny", log=None,
+                    unitrms=True, kvfold=True)
+    r = res[4]
+    assert (tmp_path / "tiny-sweep-s4-rawctl.safetensors").exists()
+    assert (tmp_path / "tiny-sweep-s4-unitrms.safetensors").exists()
+    assert Projector.load(tmp_path / "tiny-sweep-s4-unitrms.safetensors").meta["target"] == "y / rms(y)"
+    fold = KVFold.load(tmp_path / "tiny-kvfold-s4.safetensors")
+    assert fold.n_kv == model.n_kv and sorted(fold.W) == [i for i in range(4, 8) if model.layer_types[i] == "attn"]
+    got = {}
+    ids = torch.as_tensor(held[0]["ids"])
+    model.forward_exact(ids, hook=lambda i, h: got.__setitem__(i, h) if i != "final" else None)
+    i = sorted(fold.W)[0]
+    k, v = fold.kv(i, got[4])
+    true = kv_target(model, i, got[i]).unflatten(-1, (2, model.n_kv, -1))
+    cos = torch.nn.functional.cosine_similarity(k.float(), true[:, 0].float(), dim=-1).mean()
+    assert cos > 0.3 and r["kvfold"]["mean_kv_cos"][str(r["kvfold"]["lambda_star"])] > 0.3
+    assert r["unitrms"]["lambda_star"] in (1e-3, 1e-1)
