@@ -52,6 +52,21 @@ def main(argv):
             if (src / "code" / extra).is_file():
                 shutil.copyfile(src / "code" / extra, DST / extra)
                 record["files_data"] = dict(record.get("files_data", {}), **{extra: sha256(src / "code" / extra)})
+        fin = src / "code" / "finals"               # the battery's cells and their schema: compatibility test data
+        if fin.is_dir():
+            dst_fin = DST / "finals"
+            if dst_fin.exists():
+                shutil.rmtree(dst_fin)
+            (dst_fin / "cells").mkdir(parents=True)
+            for f in sorted((fin / "cells").glob("*.json")) + [fin / "cell.schema.json"]:
+                if f.is_file():
+                    to = dst_fin / ("cells" if f.parent.name == "cells" else "") / f.name
+                    shutil.copyfile(f, to)
+                    record.setdefault("files_data", {})["finals/" + to.relative_to(dst_fin).as_posix()] = sha256(f)
+            (dst_fin / "lib").mkdir()                # its cell-to-config code, run as an oracle by the tests
+            for f in sorted((fin / "lib").glob("*.py")):
+                shutil.copyfile(f, dst_fin / "lib" / f.name)
+                record["files"]["../finals/lib/" + f.name] = sha256(f)
         cfg_src = src / "code" / "configs"           # the paper's run configs: compatibility test data
         if cfg_src.is_dir():
             if (DST / "configs").exists():

@@ -1,0 +1,281 @@
+"""Cells to harness runs on this engine (code/finals/lib/kvabackend.py:1-259 role).
+
+harness_configs(cell, protocol) builds one harness config (eval/harness.py, the evaluate CLI's config format) per
+(set, variant, model, tasks, lengths) group of a cell's runs, so one prompt's record holds every arm of every split
+of those runs and their one exact (the pairing unit). Arms are engine.protocol.template() specs for the arm's
+protocol kind, renamed <paper name>-s<layer>, map files under $RF_PROJ_DIR, matched controls pointing at the rows arm
+of the same run, nofill+tailbudget taking the cell's budget. Splits are fractions of the model's layers on the
+boundary below (floor(num x layers / den)); pop-native runs at the model's pop split, SwiftKV at 16.
+
+run_cell(cell, cell_dir) refuses by name before any model is loaded (HarnessGap / StaleProjector): a missing
+environment variable, a map file that is missing, not the bytes the cell pins, or fitted on another calibration list;
+a derived-set manifest that is not the cell's. Then per config: the config is written (canonical bytes, whose sha256
+a registration pins), the harness runs, and every record gets a sha256 sidecar.
+
+The `ttft` set (the speed cells), which the reference marks as having no engine path, runs here on the engine itself:
+per prompt length, each arm's prefill (run_lower + finish) timed on the device with CUDA events after a warm-up,
+`repeats` times, recorded per length with the median.
+"""
+from __future__ import annotations
+
+import dataclasses
+import json
+import os
+import statistics
+import time
+from pathlib import Path
+
+from ..utils import atomic
+
+PAPER = {"nofill": "skip", "identity": "noproj", "ridgefill": "kva", "pop-native": "pop-native",
+         "identity+rows": "noproj+qattn10", "ridgefill+rows": "kva+qattn10",
+         "identity+qblind": "noproj+qblind10", "ridgefill+qblind": "kva+qblind10",
+         "identity+random": "noproj+random", "ridgefill+random": "kva+random",
+         "identity+tailmatch": "noproj+tailmatch", "ridgefill+tailmatch": "kva+tailmatch",
+         "nofill+tailbudget": "skip+tailbudget",
+         "ridgefill+kexact": "kva+kexact", "ridgefill+vexact": "kva+vexact", "kvexact": "kvexact",
+         "ridgefill+ktail": "kva+ktail", "ridgefill+vtail": "kva+vtail",
+         "swiftkv": "swiftkv", "swiftkv-native": "swiftkv-native"}
+ROWS_OF = {"noproj": "identity+rows", "kva": "ridgefill+rows"}
+TTFT_LENGTHS = (8192, 16384, 32768, 65536)
+
+
+class HarnessGap(NotImplementedError):
+    """A named missing piece: the cell can not run until it exists."""
+
+
+class StaleProjector(RuntimeError):
+    """A map file that is not the refit the cell declares."""
+
+
+def layer_of(model_entry, frac):
+    num, den = (int(x) for x in frac.split("/"))
+    return num * model_entry["layers"] // den
+
+
+def _model_of(cell, run):
+    return cell["swiftkv_model"]["name"] if run.get("model") == "swiftkv" else cell["model"]["name"]
+
+
+def arm_spec(p, cell, run, paper, layer):
+    from ..engine import protocol as PR
+    kind = PAPER.get(paper)
+    if kind is None:
+        raise HarnessGap(f"unknown arm {paper!r}")
+    model = _model_of(cell, run)
+    m = p["models"][model]
+    split = m["pop_split"] if kind == "pop-native" else layer
+    tail = None if kind in PR.TAILLESS else cell["tail"]
+    spec = PR.template(kind, model, split, tail, p)
+    spec["name"] = f"{paper}-s{split}"
+    if "projector" in spec:
+        declared = {f["layer"]: f["file"] for f in cell.get("projector", {}).get("files", [])}
+        if declared.get(split) != spec["projector"]:
+            raise HarnessGap(f"cell {cell['name']}: arm {paper} at layer {split} reads {spec['projector']}, which the "
+                             f"cell's projector.files does not declare ({declared.get(split)})")
+        spec["projector"] = f"$RF_PROJ_DIR/{spec['projector']}"
+    sel = spec.get("select", {})
+    if "match" in sel:
+        sel["match"] = f"{ROWS_OF[kind.split('+')[0]]}-s{split}"
+    if kind == "skip+tailbudget":
+        sel["budget"] = cell["tailbudget"]["b"]
+    return spec
+
+
+def _group_key(run):
+    return (run["set"], run.get("variant"), run.get("model"), tuple(run.get("tasks", ())),
+            tuple(run.get("lengths", ())))
+
+
+def harness_config(cell, runs, p):
+    """(config, set) of runs sharing a set, variant, model and row selection."""
+    run = runs[0]
+    model = _model_of(cell, run)
+    m = p["models"][model]
+    arms, parts = [], []
+    for r in runs:
+        layer = 16 if r.get("model") == "swiftkv" else layer_of(m, r["split"])
+        if layer not in m["splits"]:
+            raise HarnessGap(f"split {r['split']} of {model} is layer {layer}, not one of the protocol's {m['splits']}")
+        arms += [arm_spec(p, cell, r, a, layer) for a in r["arms"] if a != "exact"]
+        parts.append(f"{r['id']} ({r['role']}, split {r['split']} = layer {layer})")
+    cfg = {"name": f"{cell['model']['name']}-{run['id']}", "protocol": cell["code_tag"].removeprefix("protocol-v"),
+           "registration": [cell["registration"]], "model": f"$RF_MODEL_DIR/{model}",
+           "tokenizer": f"$RF_MODEL_DIR/{cell['model']['name']}", "niah_format": m.get("niah_format"),
+           "note": f"cell {cell['name']}, set {run['set']}, runs {', '.join(parts)}; generated from the cell",
+           "arms": arms, **cell.get("caps", {})}
+    if run["set"] == "longppl":
+        cfg["keytoken_tail"] = cell["keytoken"]["tail"]
+    if "dataset" in cell:
+        cfg.update(dataset=cell["dataset"], dataset_manifest_sha256=cell["dataset_manifest_sha256"])
+    if run["set"] == "decode":
+        cfg.update(decode_from=cell["decode"]["from"], decode_steps=cell["decode"]["steps"],
+                   only=",".join(cell["decode"]["only"]))
+    if run["set"] == "multiturn":
+        cfg.update(multiturn_from=cell["secondq"]["from"], multiturn_turns=cell["secondq"]["turns"])
+    if run["set"] == "ttft":
+        cfg["ttft_lengths"] = list(cell.get("ttft_lengths", TTFT_LENGTHS))
+    if run.get("variant"):
+        cfg["ruler_variant"] = run["variant"]
+    if run.get("tasks"):
+        cfg["ruler_tasks"] = list(run["tasks"])
+    if run.get("lengths"):
+        cfg["ruler_lengths"] = list(run["lengths"])
+    names = [a["name"] for a in arms]
+    if len(set(names)) != len(names):
+        raise HarnessGap(f"cell {cell['name']}: an arm appears twice in {cfg['name']}: {names}")
+    return cfg, run["set"]
+
+
+def harness_configs(cell, p):
+    if cell["kind"] == "flashnext":
+        raise HarnessGap("the flashnext cell runs on the engine driver (bench / serve), not through harness configs")
+    groups = {}
+    for r in cell["runs"]:
+        groups.setdefault(_group_key(r), []).append(r)
+    return [harness_config(cell, runs, p) for runs in groups.values()]
+
+
+def config_bytes(cfg):
+    """The bytes a run writes for a config (the pinned form): sorted keys, indent 1, trailing newline."""
+    return json.dumps(cfg, indent=1, sort_keys=True).encode() + b"\n"
+
+
+# ------------------------------------------------------------------------------------------ preflight
+def check_projector(path, provenance, sha256=None):
+    from ..ridge.projector import meta_of
+    name = Path(path).name
+    if not Path(path).is_file():
+        raise StaleProjector(f"map file {path} does not exist ($RF_PROJ_DIR)")
+    if sha256 is not None and atomic.sha256_file(path) != sha256:
+        raise StaleProjector(f"StaleProjector: {name} is not the file the cell pins (sha256 {sha256[:16]})")
+    meta = meta_of(path)
+    if "docs" in meta and meta["docs"] != str(provenance["calib_docs"]):
+        raise StaleProjector(f"StaleProjector: {name} was fitted on {meta['docs']} documents, the cell declares "
+                             f"{provenance['calib_docs']}")
+    if meta.get("rows") != str(provenance["calib_rows"]):
+        raise StaleProjector(f"StaleProjector: {name} was fitted on {meta.get('rows')} rows, the cell declares "
+                             f"{provenance['calib_rows']}")
+    got = meta.get("calib_exclude_sha256")
+    if got and got != provenance["calib_exclude_sha256"]:
+        raise StaleProjector(f"StaleProjector: {name} was fitted with exclusion list {got[:12]}, the cell declares "
+                             f"{provenance['calib_exclude_sha256'][:12]}")
+
+
+def check_derived(cell, derived_dir):
+    for name, want in cell.get("derived", {}).items():
+        path = Path(derived_dir) / f"{name}.json"
+        got = atomic.sha256_file(path) if path.is_file() else None
+        if got != want:
+            raise HarnessGap(f"DerivedManifestMismatch: {path} hashes to {got}, the cell pins {want}")
+
+
+def preflight(cell, configs, env=os.environ, derived_dir=None):
+    for v in ("RF_MODEL_DIR", "RF_PROJ_DIR"):
+        if not env.get(v):
+            raise HarnessGap(f"{v} is not set: the configs read models and map files from it")
+    if derived_dir is not None:
+        check_derived(cell, derived_dir)
+    pinned = {f["file"]: f.get("sha256") for f in cell.get("projector", {}).get("files", [])}
+    for cfg, _ in configs:
+        for f in sorted({a["projector"] for a in cfg["arms"] if "projector" in a}):
+            name = Path(f).name
+            if not pinned.get(name):
+                raise StaleProjector(f"UnpinnedProjector: cell {cell['name']} declares no sha256 for {name}")
+            check_projector(f.replace("$RF_PROJ_DIR", env["RF_PROJ_DIR"]), cell["projector"]["provenance"],
+                            pinned[name])
+
+
+def expand_env(cfg, env=os.environ):
+    """The config with $RF_MODEL_DIR / $RF_PROJ_DIR replaced (the harness reads plain paths)."""
+    text = json.dumps(cfg)
+    for v in ("RF_MODEL_DIR", "RF_PROJ_DIR"):
+        if v in env:
+            text = text.replace("$" + v, env[v])
+    return json.loads(text)
+
+
+# ------------------------------------------------------------------------------------------ runs
+def run_ttft(cfg, out_dir, model=None, repeats=3, lengths=None, log=print):
+    """The speed set on this engine: for each length a seeded prompt, every arm's TTFT (device time of run_lower +
+    finish to the first-token logits; wall time on the CPU), `repeats` times after one warm-up."""
+    import torch
+    from ..engine.prefill import finish, run_lower
+    from ..eval.data import uniform_prompt
+    from .harness import Files, build_arm
+    if model is None:
+        from ..models.base import load
+        model = load(cfg["model"], device="cuda" if torch.cuda.is_available() else "cpu")
+    files = Files(model.device)
+    arms = [build_arm(s, files) for s in cfg["arms"]]
+    from ..engine.arm import Arm
+    split0 = max(a.split for a in arms if a.split is not None)
+    arms = [Arm("exact", split=split0)] + arms
+    out_dir = Path(out_dir)
+    out_dir.mkdir(parents=True, exist_ok=True)
+    cuda = model.device.type == "cuda"
+    n_done = 0
+    for L in lengths or cfg.get("ttft_lengths", TTFT_LENGTHS):
+        ids = uniform_prompt(L, model.cfg.vocab, seed=L).to(model.device)
+        rec = dict(name=f"ttft-{L}", n=L, runs={})
+        for a in arms:
+            a = a if not a.tail_from else dataclasses.replace(a, tail=1)      # pop-native: the last token
+            times = []
+            for rep in range(repeats + 1):
+                with torch.no_grad():
+                    if cuda:
+                        torch.cuda.synchronize()
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record()
+                    t0 = time.perf_counter()
+                    hs, lower = run_lower(model, ids, [a.split])
+                    _, _, P = finish(model, ids, hs[a.split], lower, a, 1, keep_cache=False)
+                    if cuda:
+                        e1.record()
+                        torch.cuda.synchronize()
+                        ms = e0.elapsed_time(e1)
+                    else:
+                        ms = 1e3 * (time.perf_counter() - t0)
+                del hs, lower
+                if rep:
+                    times.append(round(ms, 3))
+            rec["runs"][a.name] = dict(ttft_ms=times, median_ms=statistics.median(times), P=P, split=a.split,
+                                       tail=L - P, clock="device" if cuda else "wall")
+        ex = rec["runs"]["exact"]["median_ms"]
+        for r in rec["runs"].values():
+            r["speedup_vs_exact"] = round(ex / r["median_ms"], 4) if r["median_ms"] else None
+        from ..utils.prov import write_json
+        write_json(out_dir / f"{rec['name']}.json", rec)
+        log(f"ttft {L}: " + " ".join(f"{k}:{r['median_ms']:.1f}ms" for k, r in rec["runs"].items()))
+        n_done += 1
+    return n_done
+
+
+def run_cell(cell, cell_dir, p, env=os.environ, derived_dir=None, model=None, log=print):
+    """Preflight, then every config: write it, run it through the harness (or the TTFT runner), sidecar every record
+    it wrote. Returns the record count."""
+    configs = harness_configs(cell, p)
+    preflight(cell, configs, env, derived_dir)
+    cell_dir = Path(cell_dir)
+    n = 0
+    for cfg, set_name in configs:
+        cfg_path = cell_dir / f"harness-{cfg['name']}.json"
+        atomic.write_bytes(cfg_path, config_bytes(cfg))
+        plain = dict(expand_env(cfg, env), out=str(cell_dir / "work" / "results"))
+        out_dir = cell_dir / "work" / "results" / f"{set_name}-{cfg['name']}"
+        if set_name == "ttft":
+            run_ttft(plain, out_dir, model=model, log=log)
+        else:
+            from .. import evaluate as E
+            run_path = cell_dir / f"run-{cfg['name']}.json"
+            run_path.write_text(json.dumps(plain, indent=1))
+            rc = E.main([str(run_path), set_name])
+            if rc:
+                raise HarnessGap(f"the harness failed (exit {rc}) for {cfg['name']}")
+        records = sorted(p_ for p_ in out_dir.glob("*.json"))
+        if not records:
+            raise HarnessGap(f"the harness wrote no records in {out_dir}")
+        for r in records:
+            atomic.refresh_sidecar(r)
+        n += len(records)
+    return n
