@@ -279,3 +279,60 @@ def run_cell(cell, cell_dir, p, env=os.environ, derived_dir=None, model=None, lo
             atomic.refresh_sidecar(r)
         n += len(records)
     return n
+
+
+# ------------------------------------------------------------------------------------------ registration pins
+def canonical(obj):
+    return json.dumps(obj, indent=1, sort_keys=True).encode() + b"\n"
+
+
+def pins(cell, p):
+    """{'cell': {name: sha256 of the cell's canonical bytes}, 'config': {name: sha256 of each generated config's
+    bytes}}: what a FINAL- registration pins."""
+    import hashlib
+    return {"cell": {cell["name"]: hashlib.sha256(canonical(cell)).hexdigest()},
+            "config": {cfg["name"]: hashlib.sha256(config_bytes(cfg)).hexdigest()
+                       for cfg, _ in harness_configs(cell, p)}}
+
+
+def pins_text(pn):
+    """The pins as registration text: 'pins: cell NAME sha256=HEX; config NAME sha256=HEX; ...'."""
+    return "pins: " + "; ".join(f"{k} {n} sha256={h}" for k in ("cell", "config") for n, h in pn[k].items())
+
+
+def pins_of(text):
+    import re
+    got = {"cell": {}, "config": {}}
+    for k, name, h in re.findall(r"\b(cell|config) (\S+) sha256=([0-9a-f]{64})", text or ""):
+        got[k][name] = h
+    return got
+
+
+def superseded_label(rid):
+    return f"superseded-{rid}"
+
+
+def _ledger_records(ledger):
+    path = Path(ledger)
+    if not path.is_file():
+        return []
+    return [json.loads(s) for s in path.read_text().splitlines() if s.strip()]
+
+
+def check_record(cell, p, ledger):
+    """[] if the ledger's record for the cell's registration pins exactly this cell and the configs it generates and
+    the id is not superseded; else the problems, by name."""
+    want = pins(cell, p)
+    recs = _ledger_records(ledger)
+    rid = cell["registration"]
+    if any(r.get("id") == superseded_label(rid) or r.get("label") == superseded_label(rid) for r in recs):
+        return [f"Superseded: {rid} is superseded ({superseded_label(rid)} in {ledger})"]
+    rec = next((r for r in recs if r.get("type") == "hypothesis" and r.get("id") == rid), None)
+    if rec is None:
+        return [f"registration {rid} is not a hypothesis id in {ledger}: register the cell first"]
+    got = pins_of(rec.get("claim") or rec.get("text"))
+    problems = [f"ConfigNotRegistered: {k} {n} sha256 {h[:16]} is not what {rid} pins ({got[k].get(n, 'nothing')[:16]})"
+                for k in ("cell", "config") for n, h in want[k].items() if got[k].get(n) != h]
+    problems += [f"ConfigNotRegistered: {rid} pins {k} {n}, which this cell does not generate"
+                 for k in ("cell", "config") for n in got[k] if n not in want[k]]
+    return problems

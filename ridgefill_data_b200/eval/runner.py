@@ -10,7 +10,8 @@ names the reason.
      sidecar; finished samples are skipped, so a rerun resumes
   6. .done with the results tree hash
 The harness is a callable harness(cell, sample_id) -> dict; mock_harness is a deterministic stand-in whose
-results are never evidence.
+results are never evidence. Battery cells (a "runs" list: eval/cells.py) run instead through eval/backend.py on
+this engine, after their registration's pins (the sha256 of the cell and of every config it expands to) are checked.
 
     python -m ridgefill_data_b200.eval.runner CELL.json --harness package.module:function [--new-host]
 """
@@ -81,11 +82,8 @@ def mock_harness(cell, sid):
                                              for i, a in enumerate(cell.get("arms", ["exact"]))})
 
 
-def run_cell(cell, results_root, harness, ledger, new_host=False, locked_root=None, info=None):
-    check_registration(cell, ledger)
-    manifest = check_locked(cell, locked_root) if cell.get("dataset_manifest_sha256") else None
-    cell_dir = Path(results_root) / cell["name"]
-    info = info or host_info()
+def _claim_host(cell, cell_dir, info, new_host):
+    """Steps 3-4: host fingerprint (restart elsewhere only with new_host) and the frozen cell declaration."""
     fp = fingerprint(info)
     host_file = cell_dir / "host.json"
     if host_file.exists():
@@ -106,6 +104,36 @@ def run_cell(cell, results_root, harness, ledger, new_host=False, locked_root=No
             raise RunnerRefusal(f"cell.json in {cell_dir} differs from the declared cell: declare a new cell instead")
     else:
         atomic.write_result(decl, cell)
+
+
+def run_battery_cell(cell, results_root, ledger, protocol, new_host=False, locked_root=None, info=None, env=None,
+                     derived_dir=None, model=None):
+    """A battery cell (a list of harness runs, eval/cells.py format): registration and its pins (the cell's and
+    every generated config's sha256 must be what the FINAL- record pins), the locked set, host and declaration
+    checks, then eval/backend.run_cell (preflight, harness, sidecars) and .done with the results tree hash."""
+    from . import backend as BK
+    check_registration(cell, ledger)
+    problems = BK.check_record(cell, protocol, ledger)
+    if problems:
+        raise RunnerRefusal(f"cell {cell['name']}: " + "; ".join(problems))
+    if cell.get("dataset_manifest_sha256") and any(r["set"] in LK.SETS for r in cell["runs"]):
+        check_locked(cell, locked_root)
+    cell_dir = Path(results_root) / cell["name"]
+    _claim_host(cell, cell_dir, info or host_info(), new_host)
+    n = BK.run_cell(cell, cell_dir, protocol, env=env if env is not None else os.environ, derived_dir=derived_dir,
+                    model=model, log=log)
+    tree = atomic.treehash(cell_dir)
+    atomic.write_bytes(cell_dir / ".done", json.dumps(dict(cell=cell["name"], registration=cell["registration"],
+                                                            records=n, tree_sha256=tree)).encode())
+    log(f"cell {cell['name']} done: {n} records, tree {tree}")
+    return tree
+
+
+def run_cell(cell, results_root, harness, ledger, new_host=False, locked_root=None, info=None):
+    check_registration(cell, ledger)
+    manifest = check_locked(cell, locked_root) if cell.get("dataset_manifest_sha256") else None
+    cell_dir = Path(results_root) / cell["name"]
+    _claim_host(cell, cell_dir, info or host_info(), new_host)
     ids = sample_ids(cell, manifest)
     todo = [(s, cell_dir / "samples" / (s.replace("/", "__") + ".json")) for s in ids]
     todo = [(s, p) for s, p in todo if not atomic.finished(p)]
@@ -131,8 +159,14 @@ def main(argv=None):
     ap.add_argument("--results", default=os.environ.get("RF_RESULTS", "results/cells"))
     ap.add_argument("--ledger", default=os.environ.get("RF_LEDGER", "ledger.jsonl"))
     ap.add_argument("--new-host", action="store_true")
+    ap.add_argument("--protocol", help="protocol.json for battery cells (default $RF_PROTOCOL)")
     a = ap.parse_args(argv)
-    run_cell(json.loads(Path(a.cell).read_text()), a.results, _load_harness(a.harness), a.ledger, a.new_host)
+    cell = json.loads(Path(a.cell).read_text())
+    if "runs" in cell:                                     # a battery cell: harness runs on this engine
+        from ..engine import protocol as PR
+        run_battery_cell(cell, a.results, a.ledger, PR.load(a.protocol), a.new_host)
+        return
+    run_cell(cell, a.results, _load_harness(a.harness), a.ledger, a.new_host)
 
 
 if __name__ == "__main__":

@@ -140,3 +140,22 @@ def test_ttft_runner_on_a_tiny_model(tmp_path):
     assert rec["runs"]["identity-s4"]["P"] == 128 and rec["runs"]["pop-native-s6"]["P"] == 159
     assert all(len(r["ttft_ms"]) == 2 and r["median_ms"] > 0 for r in rec["runs"].values())
     assert rec["runs"]["exact"]["speedup_vs_exact"] == 1.0
+
+
+@needs_ref
+def test_registration_pins(tmp_path):
+    from ridgefill_data_b200.engine import protocol as P
+    from ridgefill_data_b200.release.ledger import Ledger
+    p = P.load(REF / "protocol.json")
+    cell = json.loads((REF / "finals" / "cells" / "qwen3-8b-ruler.json").read_text())
+    pn = B.pins(cell, p)
+    assert len(pn["config"]) == 3 and B.pins_of(B.pins_text(pn)) == pn
+    led = Ledger(tmp_path / "ledger")
+    path = tmp_path / "ledger" / "ledger.jsonl"
+    assert "not a hypothesis id" in B.check_record(cell, p, path)[0]
+    led.append(dict(type="hypothesis", id=cell["registration"], claim="claim text | " + B.pins_text(pn)))
+    assert B.check_record(cell, p, path) == []
+    changed = dict(cell, tail=2048)
+    assert any(s.startswith("ConfigNotRegistered") for s in B.check_record(changed, p, path))
+    led.append(dict(type="record", label=B.superseded_label(cell["registration"])))
+    assert B.check_record(cell, p, path)[0].startswith("Superseded")
