@@ -16,8 +16,8 @@ from __future__ import annotations
 
 import torch
 
-from ..engine import decode as D
-from ..engine.scoring import check_finite
+from . import decode as D
+from .scoring import check_finite
 
 
 @torch.no_grad()

@@ -10,7 +10,7 @@ the two).
   multiturn  mk4 prompts as k-turn chats over one carried cache, with deferred repair arms (eval/multiturn.py)
   ruler, longbench, longppl   the locked test set (eval/locked.py): greedy to the task's output length and the
              official metric; longppl the continuation's NLL
-  decode     exact vs every arm over decode_steps tokens (eval/agree.py), prompts from decode_from (grade | longppl)
+  decode     exact vs every arm over decode_steps tokens (engine/agree.py), prompts from decode_from (grade | longppl)
              without their scored tokens
 Per prompt: the lower layers run once and are shared; every arm runs finish() over them (largest split first),
 optionally with exact rows chosen by its selector (engine/select.py: digits, regex, verbatim, qattn, pred, freq,
@@ -29,11 +29,11 @@ from pathlib import Path
 
 import torch
 
+from ..engine import agree as AG
 from ..engine import select as SEL
 from ..engine.arm import ENGINE_MIN_TAIL, Arm, exclude_scored, rounded_tail
 from ..engine.prefill import finish, oracle_tap, run_lower
 from ..engine.scoring import check_finite, score_tokens
-from . import agree as AG
 from . import text as TX
 
 SETS = ("grade", "niah", "niahg", "multiturn", "ruler", "longbench", "longppl", "decode")

@@ -108,7 +108,10 @@ def score_generation(prm, text):
 def run_prompt(model, arms, prm, task, keep, tok=None):
     from .engine.decode import greedy
     from .engine.prefill import finish, run_lower
-    from .engine.scoring import decode_agreement, kl, score_tokens, top1_agree
+    from .engine import agree as AG
+    from .engine.arm import Arm
+    from .engine.decode import fork_cache
+    from .engine.scoring import kl, score_tokens, top1_agree
     ids = prm["ids"].to(model.device)
     n = ids.shape[0]
     rec = dict(name=prm["name"], n=n, runs={})
@@ -150,7 +153,8 @@ def run_prompt(model, arms, prm, task, keep, tok=None):
             gen, reason = greedy(model, ids, cache, logits, len(prm["value"]) + 4, arm)
             r.update(gen=gen, finish_reason=reason, correct=niah_correct(gen, prm["value"]))
         elif task == "decode":
-            r.update(decode_agreement(model, ids, exact_cache, exact_logits, cache, logits, steps=8))
+            fields, ref = AG.exact_record(model, n, fork_cache(exact_cache), exact_logits, 8, Arm("exact"))
+            r.update(AG.compare(model, n, cache, logits, 8, arm, *ref), exact_gen=fields["gen"])
         rec["runs"][arm.name] = r
     return rec
 

@@ -5,7 +5,9 @@ import torch
 
 from ridgefill_data_b200.engine.arm import Arm, exclude_scored, pop_split, rounded_tail
 from ridgefill_data_b200.engine.prefill import finish, oracle_tap, prefill, run_lower
-from ridgefill_data_b200.engine.scoring import decode_agreement, kl
+from ridgefill_data_b200.engine import agree as AG
+from ridgefill_data_b200.engine.decode import fork_cache
+from ridgefill_data_b200.engine.scoring import kl
 from ridgefill_data_b200.eval.data import zipf_docs
 from ridgefill_data_b200.models.base import load
 from ridgefill_data_b200.ridge import sweep
@@ -73,8 +75,11 @@ def test_exact_rows_and_decode(model, maps):
     l3, _, _ = finish(model, ids, hs[2], lower, arm, 1, exact_rows=list(range(70)))
     ref, cref = model.forward_exact(ids, keep=torch.tensor([99]))
     assert torch.allclose(l3, ref, atol=1e-4)
-    agree = decode_agreement(model, ids, cref, ref, c1, l1, steps=4)
-    assert len(agree["tokens"]) == 4 and agree["mean_kl"] >= 0
+    fields, (y, lp) = AG.exact_record(model, 100, fork_cache(cref), ref, 4, Arm("exact"))
+    agree = AG.compare(model, 100, c1, l1, 4, arm, y, lp)
+    assert len(fields["gen"]) == 4 and len(agree["kl"]) == 4 and agree["kl_mean"] >= 0
+    same, _ = AG.run(model, 100, fork_cache(cref), ref, 4, Arm("exact"))
+    assert same == y                                                 # the exact run is reproducible
 
 
 def test_arm_helpers():
