@@ -7,6 +7,14 @@ POST /completion  {"prompt": [ids] | "text", "n_predict": 16, "stream": false, "
                    top_k 1, seed, cache_prompt false, id_slot) are accepted and must mean greedy decoding.
   stream=false -> one JSON object: the final event with "tokens" = every generated id and "content" the text.
   stream=true  -> text/event-stream, one `data: {event}` per token and the final event (see serve/engine.py).
+OpenAI-compatible (the API the c5 kit's client and the LongBench v2 runner speak):
+  GET  /v1/models
+  POST /v1/completions       {"prompt": "text" | [ids], "max_tokens", "stream", "stop", "ridgefill_mode"}
+  POST /v1/chat/completions  {"messages": [...], "max_tokens", "stream", "stop", "ridgefill_mode"} (the tokenizer's
+                             chat template renders the prompt)
+  Responses carry choices[0].text / .message.content, finish_reason ("stop" | "length") and usage token counts;
+  streams are chunk objects ending with `data: [DONE]`. Greedy decoding only. Text is detokenized incrementally
+  (the decoded prefix grows; a trailing partial character is held back), so multi-byte pieces stream correctly.
 """
 from __future__ import annotations
 
@@ -54,12 +62,185 @@ def parse_body(body, arms, tokenizer=None):
     return torch.tensor(ids, dtype=torch.long), n_predict, arms[mode], bool(body.get("ignore_eos", False))
 
 
+class Detok:
+    """Incremental detokenizer: the text of all ids so far, emitted as deltas (a trailing U+FFFD, an unfinished
+    multi-byte character, is held back until the next token completes it)."""
+
+    def __init__(self, tokenizer):
+        self.tok = tokenizer
+        self.ids, self.sent = [], ""
+
+    def push(self, ids):
+        if self.tok is None:
+            return ""
+        self.ids += list(ids)
+        text = self.tok.decode(self.ids, skip_special_tokens=True)
+        if text.endswith("\ufffd"):
+            return ""
+        delta = text[len(self.sent):] if text.startswith(self.sent) else text
+        self.sent = text
+        return delta
+
+
+def _greedy_only(body):
+    if float(body.get("temperature", 0) or 0) != 0 or int(body.get("top_k", 1) or 1) not in (1, -1) \
+            or float(body.get("top_p", 1) or 1) != 1:
+        raise BadRequest("only greedy decoding (temperature 0) is served")
+
+
+def _mode(body, arms):
+    mode = body.get("ridgefill_mode", "on" if body.get("ridgefill", True) else "off")
+    if mode not in arms:
+        raise BadRequest(f"ridgefill_mode {mode!r}: one of {sorted(arms)}")
+    return arms[mode]
+
+
+def _stops(body):
+    st = body.get("stop")
+    if st is None:
+        return []
+    st = [st] if isinstance(st, str) else list(st)
+    if not all(isinstance(x, str) and x for x in st):
+        raise BadRequest("stop: a string or a list of non-empty strings")
+    return st
+
+
 def create_app(scheduler, arms, tokenizer=None, props=None):
+    import time
+    import uuid
+
     from fastapi import FastAPI
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
     app = FastAPI(title="ridgefill-b200")
-    detok = (lambda toks: tokenizer.decode(toks)) if tokenizer is not None else None
+    model_name = str((props or {}).get("model", "ridgefill"))
+
+    def bad(msg, code=400):
+        return JSONResponse({"error": {"code": code, "message": msg, "type": "invalid_request_error"}},
+                            status_code=code)
+
+    def submit(ids, n_predict, arm, ignore_eos=False):
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+        req = Request(ids=ids, n_predict=n_predict, arm=arm, ignore_eos=ignore_eos,
+                      emit=lambda ev: loop.call_soon_threadsafe(q.put_nowait, ev))
+        scheduler.submit(req)
+        return req, q
+
+    async def openai_run(ids, body, arm, kind):
+        """Shared core of /v1/completions and /v1/chat/completions."""
+        n_predict = int(body.get("max_tokens") or body.get("max_completion_tokens") or 16)
+        if n_predict < 1:
+            raise BadRequest("max_tokens must be at least 1")
+        stops = _stops(body)
+        req, q = submit(ids, n_predict, arm)
+        rid = ("chatcmpl-" if kind == "chat" else "cmpl-") + uuid.uuid4().hex[:24]
+        created = int(time.time())
+        obj = "chat.completion" if kind == "chat" else "text_completion"
+        dt = Detok(tokenizer)
+
+        def chunk(text, finish=None, first=False):
+            if kind == "chat":
+                delta = ({"role": "assistant"} if first else {})
+                if text:
+                    delta["content"] = text
+                choice = dict(index=0, delta=delta, finish_reason=finish)
+            else:
+                choice = dict(index=0, text=text, finish_reason=finish, logprobs=None)
+            return dict(id=rid, object=obj + ".chunk" if kind == "chat" else obj, created=created,
+                        model=model_name, choices=[choice])
+
+        async def pieces():
+            """(text delta, finish_reason or None, final event or None) as tokens arrive; applies stop strings."""
+            text, emitted = "", 0
+            while True:
+                ev = await q.get()
+                if "error" in ev:
+                    raise RuntimeError(ev["error"])
+                if ev.get("stop"):
+                    rest = text[emitted:]
+                    yield rest, ("stop" if ev.get("stop_type") == "eos" else "length"), ev
+                    return
+                text += dt.push(ev["tokens"])
+                hit = min((text.find(s_) for s_ in stops if s_ in text), default=-1)
+                if hit >= 0:
+                    req.cancelled = True
+                    text = text[:hit]
+                    ev2 = await _drain(q)
+                    yield text[emitted:], "stop", ev2
+                    return
+                hold = max((len(s_) - 1 for s_ in stops), default=0)
+                safe = max(emitted, len(text) - hold)
+                if safe > emitted:
+                    yield text[emitted:safe], None, None
+                    emitted = safe
+
+        def usage(final):
+            n_out = final.get("tokens_predicted", 0) if final else 0
+            return dict(prompt_tokens=int(ids.numel()), completion_tokens=n_out, total_tokens=int(ids.numel()) + n_out)
+
+        if body.get("stream"):
+            async def events():
+                first = True
+                try:
+                    async for delta, finish, final in pieces():
+                        if delta or first or finish:
+                            c = chunk(delta, finish, first)
+                            if finish:
+                                c["usage"] = usage(final)
+                            yield "data: " + json.dumps(c) + "\n\n"
+                            first = False
+                except RuntimeError as e:
+                    yield "data: " + json.dumps({"error": {"message": str(e)}}) + "\n\n"
+                yield "data: [DONE]\n\n"
+            return StreamingResponse(events(), media_type="text/event-stream")
+        out, finish, final = [], None, None
+        try:
+            async for delta, f, fin in pieces():
+                out.append(delta)
+                finish, final = f or finish, fin or final
+        except RuntimeError as e:
+            return bad(str(e), 500)
+        text = "".join(out)
+        choice = (dict(index=0, message=dict(role="assistant", content=text), finish_reason=finish)
+                  if kind == "chat" else dict(index=0, text=text, finish_reason=finish, logprobs=None))
+        return dict(id=rid, object=obj, created=created, model=model_name, choices=[choice], usage=usage(final))
+
+    @app.get("/v1/models")
+    def models():
+        return dict(object="list", data=[dict(id=model_name, object="model", owned_by="ridgefill-b200")])
+
+    @app.post("/v1/completions")
+    async def v1_completions(body: dict):
+        try:
+            _greedy_only(body)
+            arm = _mode(body, arms)
+            prompt = body.get("prompt")
+            if isinstance(prompt, list) and len(prompt) == 1 and isinstance(prompt[0], str):
+                prompt = prompt[0]
+            ids, _, _, _ = parse_body(dict(prompt=prompt, n_predict=1, ridgefill_mode="x"), {"x": arm}, tokenizer)
+            return await openai_run(ids, body, arm, "text")
+        except BadRequest as e:
+            return bad(str(e))
+
+    @app.post("/v1/chat/completions")
+    async def v1_chat(body: dict):
+        try:
+            _greedy_only(body)
+            arm = _mode(body, arms)
+            msgs = body.get("messages")
+            if tokenizer is None:
+                raise BadRequest("chat needs the server's --tokenizer (its chat template)")
+            if not isinstance(msgs, list) or not msgs or not all(isinstance(m, dict) and "content" in m for m in msgs):
+                raise BadRequest("messages: a non-empty list of {role, content}")
+            from ..eval.text import encode
+            rendered = tokenizer.apply_chat_template(msgs, tokenize=False, add_generation_prompt=True)
+            ids = torch.tensor(encode(tokenizer, rendered), dtype=torch.long)
+            if ids.numel() == 0:
+                raise BadRequest("the rendered chat prompt encodes to no tokens")
+            return await openai_run(ids, body, arm, "chat")
+        except BadRequest as e:
+            return bad(str(e))
 
     @app.get("/health")
     def health():
@@ -81,7 +262,8 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
             return JSONResponse({"error": {"code": 400, "message": str(e)}}, status_code=400)
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
-        req = Request(ids=ids, n_predict=n_predict, arm=arm, ignore_eos=ignore_eos, detok=detok,
+        req = Request(ids=ids, n_predict=n_predict, arm=arm, ignore_eos=ignore_eos,
+                      detok=Detok(tokenizer).push if tokenizer is not None else None,
                       emit=lambda ev: loop.call_soon_threadsafe(q.put_nowait, ev))
         try:
             scheduler.submit(req)
@@ -106,6 +288,14 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
             text.append(ev.get("content", ""))
 
     return app
+
+
+async def _drain(q):
+    """The final event of a request that was cancelled mid-stream (the scheduler ends it at its next round)."""
+    while True:
+        ev = await q.get()
+        if ev.get("stop"):
+            return ev
 
 
 class Server:

@@ -164,3 +164,59 @@ def test_decode_batch_matches_single_steps(setup):
     assert batched.shape == (3, CFG.vocab)
     for r in range(3):
         assert torch.equal(batched[r], single[r][-1])
+
+
+@pytest.fixture(scope="module")
+def text_server(setup):
+    from ridgefill_data_b200.eval.text import CharTokenizer
+    model, arms = setup
+    tok = CharTokenizer()
+    sched = Scheduler(model, interleave=2).start()
+    srv = Server(create_app(sched, arms, tokenizer=tok, props=dict(vocab=CFG.vocab, model="tiny")), port=0).start()
+    yield f"http://127.0.0.1:{srv.port}", model, arms, tok
+    srv.stop()
+    sched.stop()
+
+
+def _sse(url, path, body):
+    req = urllib.request.Request(url + path, data=json.dumps(dict(body, stream=True)).encode(),
+                                 headers={"Content-Type": "application/json"})
+    out = []
+    with urllib.request.urlopen(req, timeout=120) as r:
+        for raw in r:
+            raw = raw.strip()
+            if raw.startswith(b"data:"):
+                out.append(raw[5:].strip().decode())
+    return out
+
+
+def test_openai_endpoints(text_server):
+    url, model, arms, tok = text_server
+    assert C.get_json(url, "/v1/models")["data"][0]["id"] == "tiny"
+    prompt = "the river stone and the amber cloud " * 3
+    ids = torch.tensor([1] + [ord(c) + 10 for c in prompt])
+    want = tok.decode(_expected(model, arms["on"], ids, 8), skip_special_tokens=True)
+    r = C.post_json(url, "/v1/completions", dict(model="tiny", prompt=prompt, max_tokens=8, temperature=0))
+    assert r["object"] == "text_completion" and r["choices"][0]["text"] == want
+    assert r["usage"] == dict(prompt_tokens=ids.numel(), completion_tokens=8, total_tokens=ids.numel() + 8)
+    assert r["choices"][0]["finish_reason"] == "length"
+    chunks = _sse(url, "/v1/completions", dict(prompt=prompt, max_tokens=8))
+    assert chunks[-1] == "[DONE]"
+    assert "".join(json.loads(c)["choices"][0]["text"] for c in chunks[:-1]) == want
+    chat = C.post_json(url, "/v1/chat/completions", dict(messages=[dict(role="user", content=prompt)], max_tokens=5,
+                                                           ridgefill_mode="off"))
+    msg = chat["choices"][0]["message"]
+    assert chat["object"] == "chat.completion" and msg["role"] == "assistant" and isinstance(msg["content"], str)
+    cchunks = _sse(url, "/v1/chat/completions", dict(messages=[dict(role="user", content=prompt)], max_tokens=5,
+                                                      ridgefill_mode="off"))
+    parts = [json.loads(c) for c in cchunks[:-1]]
+    assert parts[0]["choices"][0]["delta"].get("role") == "assistant"
+    assert "".join(p["choices"][0]["delta"].get("content", "") for p in parts) == msg["content"]
+    if len(want) > 3:                                # a stop string cuts the text where it starts
+        stop = want[2:4]
+        r = C.post_json(url, "/v1/completions", dict(prompt=prompt, max_tokens=8, stop=[stop]))
+        assert r["choices"][0]["text"] == want[:want.find(stop)] and r["choices"][0]["finish_reason"] == "stop"
+    for bad in (dict(prompt=prompt, temperature=0.8), dict(prompt=prompt, ridgefill_mode="half")):
+        with pytest.raises(urllib.error.HTTPError) as e:
+            C.post_json(url, "/v1/completions", bad)
+        assert e.value.code == 400
