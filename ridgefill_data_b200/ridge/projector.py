@@ -14,6 +14,7 @@ code/c5/convert.py:96-104) and the Gated DeltaNet terminal-state correction `st.
 from __future__ import annotations
 
 import json
+from pathlib import Path
 
 import torch
 import torch.nn.functional as F
@@ -30,6 +31,18 @@ def check_weights(tensors, where):
             r, c = bad.nonzero()[0].tolist()
             raise ValueError(f"{where}: {k} has {int(bad.sum())} non-finite or |w| > {MAX_ABS_WEIGHT:g} weights "
                              f"(first at row {r}, col {c}: {t[r, c].item():.4g}); refusing")
+
+
+def stable_safetensors(tensors, metadata=None):
+    """safetensors bytes with a canonical header (keys sorted, compact JSON, padded to 8 bytes): the library writes
+    its metadata map in hash order, so equal content could otherwise serialise to different bytes. The data
+    section and its offsets are the library's (tensors in a fixed order)."""
+    from safetensors.torch import save
+    blob = save(tensors, metadata=metadata)
+    n = int.from_bytes(blob[:8], "little")
+    header = json.dumps(json.loads(blob[8:8 + n]), sort_keys=True, separators=(",", ":")).encode()
+    header += b" " * (-len(header) % 8)
+    return len(header).to_bytes(8, "little") + header + blob[8 + n:]
 
 
 def meta_of(path):
@@ -86,13 +99,17 @@ class Projector:
                 for i in self.layers}
 
     def save(self, path, meta):
-        from safetensors.torch import save_file
+        """The map file (bytes reproducible: a canonical header)."""
         t = self.tensors()
         check_weights(t, f"Projector.save {path}")
-        save_file(t, str(path), metadata={k: str(v) for k, v in dict(meta, split=self.split).items()})
+        Path(path).write_bytes(stable_safetensors(t, {k: str(v) for k, v in dict(meta, split=self.split).items()}))
 
     @classmethod
     def load(cls, path, device="cpu", dtype=torch.bfloat16, sha256=None):
+        """A map file, or a release directory (ridgefill.json + int8 maps: ridge/release.py)."""
+        if Path(path).is_dir():
+            from . import release
+            return release.load(path, device, dtype)
         from safetensors.torch import load as from_bytes
 
         from ..utils import integrity
