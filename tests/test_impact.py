@@ -5,7 +5,6 @@ import math
 
 import pytest
 import torch
-import torch.nn.functional as F
 
 from ridgefill_data_b200.engine import impact as IM
 from ridgefill_data_b200.engine.prefill import run_lower

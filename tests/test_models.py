@@ -52,7 +52,7 @@ def test_prefill_then_decode_equals_full(fixture, request):
 
 
 def test_gdn_row_segments_invariant(tiny_qwen35, monkeypatch):
-    from ridgefill_data_b200.models import base, hybrid
+    from ridgefill_data_b200.models import hybrid
     path, _ = tiny_qwen35
     m = load(path, dtype=torch.float32)
     ids = torch.randint(0, 300, (200,), generator=torch.Generator().manual_seed(8))
