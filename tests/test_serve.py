@@ -220,3 +220,16 @@ def test_openai_endpoints(text_server):
         with pytest.raises(urllib.error.HTTPError) as e:
             C.post_json(url, "/v1/completions", bad)
         assert e.value.code == 400
+
+
+def test_server_cli_build():
+    """The server CLI's model / maps / arms / tokenizer assembly (no socket)."""
+    import argparse
+    from ridgefill_data_b200.serve.__main__ import build
+    a = argparse.Namespace(model="tiny-llama", checkpoint=None, backend="torch", device="cpu", maps=None,
+                           synthetic_maps=True, split=4, tail=64, tokenizer="char", interleave=4)
+    model, arms, tok, eos, props = build(a)
+    assert set(arms) == {"on", "off"} and arms["on"].split == 4 and arms["on"].tail == 64
+    assert props["vocab"] == model.cfg.vocab and eos == (tok.eos_token_id,)
+    with pytest.raises(SystemExit):
+        build(argparse.Namespace(**dict(vars(a), synthetic_maps=False)))
