@@ -228,7 +228,8 @@ def set_prompts(set_name, cfg, tok, model_name, protocol):
         return TX.niah_prompts(tok, fmt, "mk4"), run_cfg
     if set_name in locked.SETS:
         out, run_cfg["skipped"] = locked.prompts(set_name, tok, cfg, model_name, protocol)
-        for k in ("ruler_max_len", "longbench_max_len", "longppl_max_len", "ruler_max_new", "ruler_variant"):
+        for k in ("ruler_max_len", "longbench_max_len", "longppl_max_len", "ruler_max_new", "ruler_variant", "dataset",
+                  "dataset_manifest_sha256"):
             if cfg.get(k) is not None:
                 run_cfg[k] = cfg.get(k)
         return out, run_cfg
@@ -285,6 +286,8 @@ class Harness:
             raise EvalError(f"multiturn_from {cfg.get('multiturn_from')!r}: one of {MULTITURN_FROM}")
         if cfg.get("drop_bos") and set_name != "grade":
             raise EvalError("drop_bos runs on the grade set only")
+        if cfg.get("dataset") is not None and set_name != "longppl":
+            raise EvalError(f"dataset {cfg['dataset']!r} replaces the locked set for longppl only, not {set_name!r}")
         from . import multiturn as MT
         specs = [s for s in cfg["arms"] if set_name in s.get("sets", SETS)]
         check_reuse(specs)

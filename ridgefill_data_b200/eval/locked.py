@@ -247,8 +247,30 @@ def longppl_docs(tok, man, model, max_len=None, root=None):
     return out, skipped
 
 
+DATASETS = {"fresh-long-20261008": ("longppl",)}        # config 'dataset' -> the sets that frozen set holds
+
+
+def dataset_dir(name):
+    """A frozen set other than the locked one (config 'dataset'): beside the locked set; unknown names refused."""
+    if name not in DATASETS:
+        raise LockedSetError(f"dataset {name!r} is not a known set {sorted(DATASETS)} (absent: the locked set)")
+    return locked_dir().parent / name
+
+
 def prompts(which, tok, cfg, model, protocol, root=None):
-    """(prompts, skipped files) of one locked set for this model."""
+    """(prompts, skipped files) of one locked set for this model; config 'dataset' names another frozen set (its
+    MANIFEST.tsv sha256 pinned by 'dataset_manifest_sha256'), which replaces the locked set for the sets it holds."""
+    name = cfg.get("dataset")
+    if name is not None:
+        droot = Path(root) if root is not None else dataset_dir(name)
+        if name not in DATASETS:
+            raise LockedSetError(f"dataset {name!r} is not a known set {sorted(DATASETS)}")
+        if which not in DATASETS[name]:
+            raise LockedSetError(f"dataset {name!r} holds the {'/'.join(DATASETS[name])} set only, not {which!r}")
+        if not cfg.get("dataset_manifest_sha256"):
+            raise LockedSetError(f"dataset {name!r}: the config pins no dataset_manifest_sha256")
+        man = manifest(droot, cfg["dataset_manifest_sha256"], name)
+        return longppl_docs(tok, man, model, cfg.get("longppl_max_len"), droot)
     man = manifest(root)
     if which == "ruler":
         sel = dict(tasks=cfg.get("ruler_tasks"), lengths=cfg.get("ruler_lengths"), max_new=cfg.get("ruler_max_new"))

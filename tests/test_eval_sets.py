@@ -228,3 +228,20 @@ def test_evaluate_cli_on_locked_sets(tmp_path, locked_root, tiny_llama):
     assert evaluate.main([str(tmp_path / "lp.json"), "ppl"]) == 0
     r = json.loads(next((tmp_path / "lp" / "ppl").glob("*.json")).read_text())
     assert all(r["runs"][a]["nll"] > 0 for a in ("exact", "identity"))
+
+
+def test_alternate_frozen_dataset(locked_root, tmp_path):
+    """Config 'dataset': another frozen set beside the locked one replaces it for longppl only, with its manifest
+    sha256 pinned; unknown names, other sets and an unpinned or wrong pin are refused."""
+    fresh = locked_root.parent / "fresh-long-20261008"
+    _write_set(fresh)
+    pin = hashlib.sha256((fresh / "MANIFEST.tsv").read_bytes()).hexdigest()
+    cfg = dict(dataset="fresh-long-20261008", dataset_manifest_sha256=pin)
+    lp, _ = LK.prompts("longppl", TOK, cfg, "m", {})
+    assert lp and lp[0]["source"].startswith("long-prompts/")
+    for bad in (dict(cfg, dataset="nope"), dict(cfg, dataset_manifest_sha256=None),
+                dict(cfg, dataset_manifest_sha256="0" * 64)):
+        with pytest.raises(SystemExit):
+            LK.prompts("longppl", TOK, bad, "m", {})
+    with pytest.raises(SystemExit):
+        LK.prompts("ruler", TOK, cfg, "m", {})
