@@ -144,6 +144,23 @@ class CostModel:
             c += self.qattn_select(n, split)
         return c + self.H * self.V
 
+    def bypass_arm(self, n, split, tail, kind, rows=None, budget=None, gdn="efficient", pos=0.5, proj_types=None,
+                   rank=None, refresh=None):
+        """A bypass arm of select kind `kind` with `rows` exact rows, or round(budget n) (the qattn rule);
+        tail_match spends them on the exact tail instead."""
+        if rows is None:
+            rows = round(budget * n)
+        if kind == "tail_match":
+            return self.ridgefill(n, split, tail + rows, proj_types=proj_types, rank=rank, refresh=refresh)
+        if kind not in ("digits", "qattn", "random"):
+            raise ValueError(f"bypass kind {kind!r}")
+        return self.bypass(n, split, tail, rows, select=kind, gdn=gdn, pos=pos, proj_types=proj_types, rank=rank,
+                           refresh=refresh)
+
+    def bypass_speedup(self, n, split, tail, kind, rows=None, budget=None, gdn="efficient", pos=0.5, proj_types=None,
+                       rank=None):
+        return self.exact(n) / self.bypass_arm(n, split, tail, kind, rows, budget, gdn, pos, proj_types, rank)
+
     def repair(self, split, rows):
         return sum(self.layer_exact(i, 0, rows) for i in range(split, self.L))
 
@@ -165,8 +182,7 @@ class CostModel:
         if fill == "kvfold":
             return base / self.ridgefill(n, split, tail, kvfold=True)
         if fill == "by_type":
-            types = {"attn" if t == "attention" else t for t, f in fill_by_type.items() if f == "proj"}
-            return base / self.ridgefill(n, split, tail, proj_types=types, rank=rank)
+            return base / self.ridgefill(n, split, tail, proj_types=proj_types_of(fill_by_type), rank=rank)
         return base / self.ridgefill(n, split, tail, projector=fill == "proj", rank=rank, context=context,
                                      refresh=refresh)
 
@@ -174,6 +190,11 @@ class CostModel:
     def seconds(self, macs, tflops=1414.3, eff=0.85):
         """MACs -> seconds at `eff` of the measured sustained bf16 rate (TFLOP/s, 2 FLOPs per MAC)."""
         return 2 * macs / (tflops * 1e12 * eff)
+
+
+def proj_types_of(fill_by_type):
+    """The late layer types ('attn', 'gdn') a fill_by_type runs the ridge map on."""
+    return {"attn" if t == "attention" else t for t, f in fill_by_type.items() if f == "proj"}
 
 
 def diagnostic(fill, fill_by_type=None, exact_part=None, rescale=None):

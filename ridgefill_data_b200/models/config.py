@@ -201,7 +201,7 @@ class ModelConfig:
             c.update(layer_types=["linear_attention" if t == "gdn" else "full_attention" for t in self.layer_types],
                      linear_num_key_heads=self.gdn_nk, linear_num_value_heads=self.gdn_nv,
                      linear_key_head_dim=self.gdn_dk, linear_value_head_dim=self.gdn_dv,
-                     linear_conv_kernel_dim=self.conv_k,
+                     linear_conv_kernel_dim=self.conv_k, attn_output_gate=self.gated_attn,
                      rope_parameters=dict(rope_type="default", rope_theta=self.rope_theta,
                                           partial_rotary_factor=self.partial_rotary))
             if self.arch == "qwen3_5_moe":

@@ -176,3 +176,35 @@ def test_fit_and_evaluate_cli(tmp_path):
         assert out["runs"]["exact"]["kl"] == pytest.approx(0.0, abs=1e-9) and out["runs"]["rf"]["kl"] > 0
     finally:
         del C.PRESETS["cli-tiny"]
+
+
+def test_cost_model_matches_the_reference(tmp_path):
+    """Every MAC rule against the reference's kva/compute.py (installed in baseline/_ref) on the same shapes."""
+    import sys
+    from pathlib import Path
+    ref_root = Path(__file__).resolve().parent.parent / "baseline" / "_ref"
+    if not (ref_root / "kva" / "compute.py").exists():
+        pytest.skip("baseline/_ref not installed")
+    sys.path.insert(0, str(ref_root))
+    from kva import compute as RC
+    for name in ("qwen3.8-27b", "llama-3.1-8b", "qwen3-8b"):
+        cfg = PRESETS[name]
+        d = tmp_path / name
+        d.mkdir()
+        (d / "config.json").write_text(json.dumps(cfg.to_hf()))
+        dm, cm = RC.Dims(d), CostModel(cfg)
+        for n, split, tail in ((16384, cfg.n_layers // 2, 4096), (65536, 3 * cfg.n_layers // 8, 4096), (9000, 8, 512)):
+            assert cm.exact(n) == RC.exact(dm, n)
+            assert cm.ridgefill(n, split, tail) == RC.kva(dm, n, split, tail)
+            assert cm.ridgefill(n, split, tail, projector=False) == RC.kva(dm, n, split, tail, projector=False)
+            assert cm.skip(n, split, tail) == RC.skip(dm, n, split, tail)
+            assert cm.tail_budget(n, split, tail) == RC.tail_budget(dm, n, split, tail)
+            assert cm.swiftkv(n, split) == RC.swiftkv(dm, n, split)
+            assert cm.qattn_select(n, split) == RC.qattn_select(dm, n, split)
+            for kind, kw in (("qattn", dict(budget=0.1)), ("digits", dict(rows=300)), ("tail_match", dict(rows=256))):
+                assert cm.bypass_arm(n, split, tail, kind, **kw) == RC.bypass_arm(dm, n, split, tail, kind, **kw)
+            assert cm.repair(split, 5000) == RC.repair(dm, split, 5000)
+            assert cm.repair_selected(split, 300, n - tail) == RC.repair_selected(dm, split, 300, n - tail)
+            for fill in ("proj", "identity", "kvfold"):
+                assert cm.speedup(n, fill, split=split, tail=tail) == pytest.approx(
+                    RC.speedup(dm, n, fill, split=split, tail=tail), rel=1e-12)
