@@ -203,7 +203,8 @@ def harness_main(cfg, a):
     if a.canary != "off":
         split = min(x.split for x in h.arms if x.split is not None) if any(x.split for x in h.arms) else \
             model.n_layers // 2
-        print(f"canary: {canary.check(model, root, split, 'record' if a.canary in ('accept', 'reset') else 'check')}")
+        tol = cfg.get("canary_tolerance")
+        print(f"canary: {canary.check(model, root, split, a.canary, tol)}")
     try:
         protocol = PR.load()
     except OSError:

@@ -1,8 +1,9 @@
 """Job-start canary (code/kva/canary.py:145-219 role): a fixed synthetic prompt through the exact arm and an
-identity-fill arm; the logits' sha256 (and values) must match the reference stored for this host key (GPU name,
-driver, CUDA and torch versions, model) bitwise, or within `tol` (max abs logit difference) when given. The first
-run on a new host key writes the reference (mode 'record'); a mismatch raises CanaryMismatch before any result
-is produced."""
+identity-fill arm; the logits' sha256 (and values) must match a stored variant for this host key (GPU name, driver,
+CUDA and torch versions, model) bitwise, or within `tol` (max abs logit difference) when given (models with known
+numeric variants). The file keeps a list of accepted variants: the first run on a new host key records the first
+one; mode 'accept' appends the current result as another variant after a reviewed mismatch, 'reset' replaces the
+list. A result that matches no variant raises CanaryMismatch before any result is produced."""
 from __future__ import annotations
 
 import hashlib
@@ -42,22 +43,35 @@ def run(model, split):
     return out
 
 
-def check(model, results_dir, split, mode="check", tol=None):
-    key, facts = host_key(model.cfg.name)
-    path = Path(results_dir) / f"canary-{key}.json"
-    got = run(model, split)
-    if mode == "record" or not path.exists():
-        prov.write_json(path, dict(facts=facts, arms=got))
-        return "recorded"
-    ref = json.loads(path.read_text())["arms"]
-    for arm, r in ref.items():
+def _matches(got, variant, tol):
+    for arm, r in variant.items():
         g = got[arm]
         if g["sha256"] == r["sha256"]:
             continue
-        if tol is not None:
-            diff = max(abs(a - b) for a, b in zip(g["values"], r["values"]))
-            if diff <= tol and g["argmax"] == r["argmax"]:
-                continue
-        raise CanaryMismatch(f"canary {arm}: logits differ from the reference {path} (sha {g['sha256'][:12]} vs "
-                             f"{r['sha256'][:12]})")
-    return "ok"
+        if tol is not None and g["argmax"] == r["argmax"] and \
+                max(abs(a - b) for a, b in zip(g["values"], r["values"])) <= tol:
+            continue
+        return False
+    return True
+
+
+def check(model, results_dir, split, mode="check", tol=None):
+    """'recorded' | 'ok (variant k)' | 'accepted (variant k)' | 'reset'; raises CanaryMismatch in mode check."""
+    if mode not in ("check", "record", "accept", "reset"):
+        raise ValueError(f"canary mode {mode!r}")
+    key, facts = host_key(model.cfg.name)
+    path = Path(results_dir) / f"canary-{key}.json"
+    got = run(model, split)
+    if not path.exists() or mode in ("record", "reset"):
+        prov.write_json(path, dict(facts=facts, variants=[got]))
+        return "reset" if mode == "reset" else "recorded"
+    stored = json.loads(path.read_text())
+    variants = stored.get("variants") or [stored["arms"]]
+    for k, v in enumerate(variants):
+        if _matches(got, v, tol):
+            return f"ok (variant {k})"
+    if mode == "accept":
+        prov.write_json(path, dict(facts=facts, variants=variants + [got]))
+        return f"accepted (variant {len(variants)})"
+    raise CanaryMismatch(f"canary: logits match none of the {len(variants)} stored variant(s) in {path} "
+                         f"(exact sha {got['exact']['sha256'][:12]}); after review, mode 'accept' adds this one")

@@ -144,14 +144,19 @@ def test_canary_record_then_check(tmp_path, tiny_qwen35):
     path, _ = tiny_qwen35
     m = load(path, dtype=torch.float32)
     assert canary.check(m, tmp_path, split=4) == "recorded"
-    assert canary.check(m, tmp_path, split=4) == "ok"
+    assert canary.check(m, tmp_path, split=4) == "ok (variant 0)"
     f = next(tmp_path.glob("canary-*.json"))
     rec = json.loads(f.read_text())
-    rec["arms"]["exact"]["sha256"] = "0" * 64
-    rec["arms"]["exact"]["values"][0] += 1.0
+    rec["variants"][0]["exact"]["sha256"] = "0" * 64
+    rec["variants"][0]["exact"]["values"][0] += 1e-3
     f.write_text(json.dumps(rec))
+    assert canary.check(m, tmp_path, split=4, tol=1e-2) == "ok (variant 0)"        # within the tolerance
     with pytest.raises(canary.CanaryMismatch):
         canary.check(m, tmp_path, split=4)
+    assert canary.check(m, tmp_path, split=4, mode="accept") == "accepted (variant 1)"
+    assert canary.check(m, tmp_path, split=4) == "ok (variant 1)"
+    assert canary.check(m, tmp_path, split=4, mode="reset") == "reset"
+    assert len(json.loads(f.read_text())["variants"]) == 1
 
 
 def test_fit_and_evaluate_cli(tmp_path):
