@@ -101,17 +101,23 @@ def check_tail_from(spec):
 
 
 class Files:
-    """Map files, corrections, predictors and frequency tables, each loaded once; their sha256 recorded."""
+    """Map files, corrections, predictors and frequency tables, each loaded once; their sha256 recorded. A map file
+    is checked against the sha256 that the fit records give for it (the JSON files under `records`, default the map
+    file's own directory, where the fit writes them) when they name it, else against its disk copy."""
 
-    def __init__(self, device):
+    def __init__(self, device, records=None):
         self.device = device
+        self.records = records
         self.maps, self.st, self.pred, self.freq, self.hashes = {}, {}, {}, {}, {}
 
     def projector(self, path, kind="proj"):
         from ..ridge.projector import KVFold, Projector
+        from ..utils.integrity import recorded_sha256
         if path not in self.maps:
             cls = KVFold if kind == "kvfold" else Projector
-            self.maps[path] = cls.load(path, "cpu")
+            recs = self.records or Path(path).parent        # fit records sit beside the maps they describe
+            ref = None if Path(path).is_dir() else recorded_sha256(path, recs)
+            self.maps[path] = cls.load(path, "cpu", sha256=ref)
             self.hashes[path] = self.maps[path].sha256
         return self.maps[path]
 
@@ -266,7 +272,7 @@ class Harness:
             raise EvalError(f"set {set_name!r}: one of {SETS}")
         self.m, self.tok, self.cfg, self.set = model, tok, cfg, set_name
         self.out = Path(out_dir)
-        self.files = files or Files(model.device)
+        self.files = files or Files(model.device, cfg.get("fit_records"))
         self.eos = tuple(eos)
         self.log = log
         self.fmt = cfg.get("niah_format", "raw")

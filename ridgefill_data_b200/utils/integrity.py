@@ -128,6 +128,33 @@ def verify_model(model_dir):
     return bad
 
 
+def recorded_sha256(path, results):
+    """The sha256 that the JSON records under `results` give for a file of this name (a key X holding the path with
+    its X_sha256 beside it, e.g. projector / projector_sha256 in fit records, or path / sha256); None when no
+    record names it, or when records disagree (one of them hashed a bad read, so none is trusted)."""
+    import json
+    name = Path(path).name
+    found = set()
+
+    def walk(o):
+        if isinstance(o, dict):
+            for k, v in o.items():
+                if isinstance(v, str) and Path(v).name == name:
+                    sha = o.get("sha256" if k == "path" else k + "_sha256")
+                    if isinstance(sha, str):
+                        found.add(sha)
+                walk(v)
+        elif isinstance(o, list):
+            for v in o:
+                walk(v)
+    for f in sorted(Path(results).glob("*.json")) if Path(results).is_dir() else []:
+        try:
+            walk(json.loads(f.read_text()))
+        except (ValueError, OSError):
+            continue
+    return found.pop() if len(found) == 1 else None
+
+
 def read_verified(path, ref=None):
     """(bytes, sha256) of the file read normally and checked against ref (None: the disk copy read
     around the cache). On a mismatch the bytes are re-read from the disk; IntegrityError if the disk

@@ -196,3 +196,20 @@ def test_protocol_gate_agrees_with_reference(monkeypatch):
                 verdicts.append(("refused", str(e).count("\n  - ")))
         assert verdicts[0] == verdicts[1], (name, verdicts)
         assert verdicts[0][0] == "refused"
+
+
+def test_map_files_checked_against_fit_records(tmp_path):
+    """A map file named by a fit record (projector / projector_sha256) must hash to the recorded value."""
+    from ridgefill_data_b200.utils.integrity import IntegrityError, recorded_sha256
+    W, B = synthetic_maps(16, 2, 4, "cpu", dtype=torch.float32)
+    path = tmp_path / "m-sweep-s2.safetensors"
+    Projector(2, W, B).save(path, dict(model="m"))
+    import hashlib
+    sha = hashlib.sha256(path.read_bytes()).hexdigest()
+    (tmp_path / "fit-sweep-m-s2.json").write_text(json.dumps(dict(projector=str(path), projector_sha256=sha)))
+    assert recorded_sha256(path, tmp_path) == sha
+    files = H.Files("cpu")
+    assert files.projector(str(path)).sha256 == sha
+    (tmp_path / "fit-sweep-m-s2.json").write_text(json.dumps(dict(projector=str(path), projector_sha256="0" * 64)))
+    with pytest.raises(IntegrityError):
+        H.Files("cpu").projector(str(path))
