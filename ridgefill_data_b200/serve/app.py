@@ -133,7 +133,10 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
         if n_predict < 1:
             raise BadRequest("max_tokens must be at least 1")
         stops = _stops(body)
-        req, q = submit(ids, n_predict, arm)
+        try:
+            req, q = submit(ids, n_predict, arm)
+        except ValueError as e:
+            raise BadRequest(str(e))
         rid = ("chatcmpl-" if kind == "chat" else "cmpl-") + uuid.uuid4().hex[:24]
         created = int(time.time())
         obj = "chat.completion" if kind == "chat" else "text_completion"

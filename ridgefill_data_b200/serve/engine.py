@@ -94,6 +94,13 @@ class Scheduler:
             raise ValueError("n_predict must be at least 1")
         if req.ids.dim() != 1 or req.ids.numel() == 0:
             raise ValueError("the prompt must be a non-empty 1-D id sequence")
+        limit = getattr(self.model, "max_positions", None)
+        if limit and req.ids.numel() + req.n_predict > limit:
+            raise ValueError(f"{req.ids.numel()} prompt ids + {req.n_predict} new tokens exceed the model's "
+                             f"{limit} positions")
+        vocab = getattr(getattr(self.model, "cfg", None), "vocab", None)
+        if vocab and (int(req.ids.min()) < 0 or int(req.ids.max()) >= vocab):
+            raise ValueError(f"prompt ids outside the vocabulary [0, {vocab})")
         req.rid = req.rid or f"req-{next(self._ids)}"
         req.t_submit = time.perf_counter()
         with self._lock:

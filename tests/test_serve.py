@@ -91,6 +91,11 @@ def test_eos_and_bad_requests(setup):
         assert evs[-1]["stop_type"] == "eos" and evs[-1]["tokens_predicted"] == 1
         with pytest.raises(ValueError):
             sched.submit(Request(ids=ids, n_predict=0, arm=arms["off"], emit=print))
+        with pytest.raises(ValueError, match="vocabulary"):
+            sched.submit(Request(ids=torch.tensor([CFG.vocab]), n_predict=1, arm=arms["off"], emit=print))
+        if model.max_positions:
+            with pytest.raises(ValueError, match="positions"):
+                sched.submit(Request(ids=ids, n_predict=model.max_positions, arm=arms["off"], emit=print))
     finally:
         sched.stop()
 
