@@ -66,8 +66,17 @@ def build(cfg, split, tail, device, modules=None, seed=0, std=0.02, map_seed=123
                           "external vLLM fork)")
     tmp = Path(tempfile.mkdtemp(prefix="rf_ref_model_"))
     (tmp / "config.json").write_text(json.dumps(cfg.to_hf()))
+    dev = torch.device(device)
+
+    class DeviceDrawn(RandomSource):
+        """Every tensor drawn on the benchmark device (the main arm's draws, bit for bit), then moved where the
+        reference asks for it (its embedding table stays on the host): no host-side generation of a 2.5 GB table."""
+
+        def get(self, key, device="cpu", dtype=None):
+            return super().get(key, dev, dtype).to(device)
+
     stock = RM.Checkpoint
-    RM.Checkpoint = lambda path: RandomSource(cfg, seed=seed, std=std)
+    RM.Checkpoint = lambda path: DeviceDrawn(cfg, seed=seed, std=std)
     try:
         model = RM.model_class(tmp)(tmp, device=device, dtype=torch.bfloat16)
     finally:
