@@ -14,19 +14,27 @@ class KeyTokenReferenceMissing(ValueError):
     pass
 
 
+def _bos_list(bos):
+    """The BOS ids kept in front of a tail-only context: a list (possibly empty); None means none."""
+    return [] if bos is None else list(bos)
+
+
 def check_tail(n, scored, tail, bos):
-    usable = n - (1 if bos is not None else 0)
+    usable = n - len(_bos_list(bos))
     if not scored + 1 <= tail < usable:
         raise ValueError(f"key-token tail {tail}: needs scored + 1 ({scored + 1}) <= tail < {usable}")
 
 
 @torch.no_grad()
 def exact_tail_only(model, ids, tail, bos, scored):
-    """Exact log-probs of the last `scored` tokens given only [BOS] + the last `tail` prompt tokens."""
-    check_tail(ids.shape[0], scored, tail, bos)
+    """Exact log-probs of the last `scored` tokens given only the prompt's own BOS ids (`bos`, a list, possibly
+    empty) + the last `tail` prompt tokens."""
+    ids = torch.as_tensor(ids, dtype=torch.long)
+    b = _bos_list(bos)
+    check_tail(ids.shape[0], scored, tail, b)
     ctx = ids[-tail:]
-    if bos is not None:
-        ctx = torch.cat((ids[:1], ctx))
+    if b:
+        ctx = torch.cat((torch.tensor(b, dtype=torch.long), ctx))
     logits, _ = model.forward_exact(ctx.to(model.device),
                                     keep=torch.arange(ctx.shape[0] - scored - 1, ctx.shape[0], device=model.device))
     return score_tokens(logits, ctx, scored)
@@ -46,11 +54,15 @@ def nll_delta(lp_arm, lp_exact, mask=None):
 
 
 def readout(rec, threshold=THRESHOLD):
-    """Per arm: NLL delta vs exact over all scored tokens, the novel tokens and the key tokens."""
+    """Per arm: NLL delta vs exact over all scored tokens, the novel tokens and the key tokens. Reads evaluation
+    records ({"runs": {arm: {"logprobs"}}, "tail_only": {"logprobs"}}) or {"lp": {arm: [...]}, "tail_only": [...]}."""
     if "tail_only" not in rec:
         raise KeyTokenReferenceMissing("record lacks the exact tail-only log-probs")
+    if "lp" not in rec:
+        rec = dict(rec, lp={a: r["logprobs"] for a, r in rec["runs"].items() if "logprobs" in r})
+    tail = rec["tail_only"]["logprobs"] if isinstance(rec["tail_only"], dict) else rec["tail_only"]
     exact = torch.as_tensor(rec["lp"]["exact"])
-    keys = key_mask(exact, torch.as_tensor(rec["tail_only"]), threshold)
+    keys = key_mask(exact, torch.as_tensor(tail), threshold)
     novel = torch.as_tensor(rec["novel"], dtype=torch.bool) if "novel" in rec else None
     out = {}
     for arm, lp in rec["lp"].items():

@@ -24,9 +24,37 @@ def load_records(directory):
     return [json.loads(p.read_text()) for p in sorted(Path(directory).glob("*.json"))]
 
 
-def _value(run, metric):
+DERIVED = ("nll", "nll_novel", "nll_key", "correct", "turn2_correct", "turn1_correct")
+
+
+def metric_value(rec, arm, metric, threshold=2.0):
+    """One arm's value of `metric` on one record: a scalar field of the run, or a metric derived from the
+    evaluation record's fields: nll (mean -logprob over the scored tokens), nll_novel (the novel-token mask of a
+    graded prompt), nll_key (key tokens: exact log-prob above the tail-only one by more than `threshold` nats),
+    correct / turn1_correct / turn2_correct (0 / 1). None when the record does not hold it."""
+    run = rec.get("runs", {}).get(arm)
+    if run is None:
+        return None
     v = run.get(metric)
-    return float(v) if isinstance(v, (int, float)) and math.isfinite(float(v)) else None
+    if isinstance(v, bool):
+        return float(v)
+    if isinstance(v, (int, float)):
+        return float(v) if math.isfinite(float(v)) else None
+    lp = run.get("logprobs")
+    if metric == "nll" and lp:
+        return -sum(lp) / len(lp)
+    if metric == "nll_novel" and lp and "novel" in rec:
+        xs = [-x for x, m in zip(lp, rec["novel"]) if m]
+        return sum(xs) / len(xs) if xs else None
+    if metric == "nll_key" and lp and "tail_only" in rec and "exact" in rec["runs"]:
+        tail = rec["tail_only"]["logprobs"] if isinstance(rec["tail_only"], dict) else rec["tail_only"]
+        ex = rec["runs"]["exact"]["logprobs"]
+        xs = [-x for x, e, t in zip(lp, ex, tail) if e - t > threshold]
+        return sum(xs) / len(xs) if xs else None
+    if metric in ("turn1_correct", "turn2_correct") and "turns" in run:
+        k = int(metric[4]) - 1
+        return float(run["turns"][k]["correct"]) if len(run["turns"]) > k else None
+    return None
 
 
 def paired_table(records, metric, ref, arms=None, n_resamples=ST.N_RESAMPLES, upper=None, lower=None):
@@ -35,8 +63,7 @@ def paired_table(records, metric, ref, arms=None, n_resamples=ST.N_RESAMPLES, up
     arms = arms or sorted({a for r in records for a in r.get("runs", {})} - {ref})
     rows, units = [], []
     for r in records:
-        runs = r.get("runs", {})
-        vals = {a: _value(runs.get(a, {}), metric) for a in arms + [ref]}
+        vals = {a: metric_value(r, a, metric) for a in arms + [ref]}
         if all(v is not None for v in vals.values()):
             units.append((r.get("name"), vals))
     if len(units) < 2:

@@ -25,7 +25,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import sys
 from pathlib import Path
 
@@ -58,9 +57,9 @@ def load_spec(path):
 def _values(records, metric, arm):
     out = {}
     for r in records:
-        v = r.get("runs", {}).get(arm, {}).get(metric)
-        if isinstance(v, (int, float)) and math.isfinite(float(v)):
-            out[r.get("name")] = float(v)
+        v = TB.metric_value(r, arm, metric)
+        if v is not None:
+            out[r.get("name")] = v
     return out
 
 

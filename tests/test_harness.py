@@ -213,3 +213,22 @@ def test_map_files_checked_against_fit_records(tmp_path):
     (tmp_path / "fit-sweep-m-s2.json").write_text(json.dumps(dict(projector=str(path), projector_sha256="0" * 64)))
     with pytest.raises(IntegrityError):
         H.Files("cpu").projector(str(path))
+
+
+def test_tables_read_harness_records(env):
+    """The grade records the harness writes feed the paired tables and the key-token readout directly (derived
+    metrics nll / nll_novel / nll_key from the per-token log-probs)."""
+    from ridgefill_data_b200.eval import keytok, tables as TB
+    tmp, model, maps = env
+    cfg = dict(name="t", keytoken_tail=600, arms=[dict(name="rf", split=4, tail=600, fill="proj", projector=maps),
+                                                  dict(name="id", split=4, tail=600, fill="identity")])
+    out = tmp / "grade-tables"
+    H.Harness(model, TOK, cfg, "grade", out, log=lambda *_: None).run(_grade_prompts())
+    recs = TB.load_records(out)
+    rows = TB.paired_table(recs, "nll_novel", "exact", n_resamples=200)
+    assert {r["arm"] for r in rows} == {"rf", "id"} and all(r["n"] == 2 for r in rows)
+    r0 = recs[0]
+    assert TB.metric_value(r0, "exact", "nll") == pytest.approx(-sum(r0["runs"]["exact"]["logprobs"]) / TX.SCORED)
+    ro = keytok.readout(r0)
+    assert set(ro) == {"exact", "rf", "id"} and ro["exact"]["all"][0] == 0.0
+    assert len(r0["tail_only"]["logprobs"]) == TX.SCORED
