@@ -148,3 +148,30 @@ def test_causal_attention_is_context_dependent():
     k2[:, 0] += 1.0                                   # change an earlier row only
     out2 = O.attend(q, k2, v, 8 ** -0.5)
     assert float((out2[5] - out[5]).abs().max()) > 1e-6     # a later row's output moves: no exact per-row fill
+
+
+def test_random_control_is_count_matched_and_uniform():
+    """Lemma 11 (count-matched random control): the random arm picks exactly k of P rows, uniformly, so its expected
+    gain is k / P of the total; checked on engine.select.random_rows over many prompt names."""
+    from ridgefill_data_b200.engine import select as SEL
+    P, k, draws = 20, 5, 4000
+    freq = torch.zeros(P)
+    for j in range(draws):
+        rows = SEL.random_rows(f"prompt-{j}", P, k)
+        assert len(rows) == k and len(set(rows)) == k and all(0 <= r < P for r in rows)
+        freq[rows] += 1
+    share = freq / draws
+    assert float((share - k / P).abs().max()) < 0.035          # ~5 standard errors at 4000 draws
+
+
+@FAST
+@given(st.integers(0, 2 ** 31 - 1))
+def test_rms_norm_is_not_affine(seed):
+    """Lemma 12: an affine fill keeps midpoints; RMSNorm does not (off a ray through the origin), so no affine map of
+    the boundary state reproduces a normalised late input on every row."""
+    g = torch.Generator().manual_seed(seed)
+    x, y = torch.randn(2, 16, generator=g, dtype=torch.float64)
+    w = torch.ones(16, dtype=torch.float64)
+    f = lambda t: O.rms_norm(t, w, 0.0)  # noqa: E731
+    gap = f((x + y) / 2) - (f(x) + f(y)) / 2
+    assert float(gap.norm()) > 1e-4
