@@ -12,6 +12,8 @@ checks of the statements, not proofs.
                                         exactly that row's attention weight times the change; later rows none
   9  QK-norm invariance                 ops.oracle.rms_norm (eps 0) ignores a positive scale of its input
   10 speedup with exact rows            CostModel.bypass: every exact row costs, the speedup falls with the rows
+  11 count-matched random control       engine.select.random_rows: exactly k distinct rows, uniform over many prompts
+  12 RMSNorm is not affine              ops.oracle.rms_norm does not keep midpoints
   13 context dependence                 causal attention output of a row depends on earlier rows (no per-row fill)
 """
 import math
