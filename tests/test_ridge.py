@@ -143,3 +143,46 @@ def test_unitrms_and_kvfold_fits(tmp_path):
     cos = torch.nn.functional.cosine_similarity(k.float(), true[:, 0].float(), dim=-1).mean()
     assert cos > 0.3 and r["kvfold"]["mean_kv_cos"][str(r["kvfold"]["lambda_star"])] > 0.3
     assert r["unitrms"]["lambda_star"] in (1e-3, 1e-1)
+
+
+def test_ridge_matches_the_reference():
+    """Sufficient statistics (plain and row-weighted), eigen fits for a lambda grid and the reduced-rank fits with
+    their energy shares against the reference's kva/ridge.py on the same rows (baseline/_ref)."""
+    import sys
+    from pathlib import Path
+    ref_root = Path(__file__).resolve().parent.parent / "baseline" / "_ref"
+    if not (ref_root / "kva" / "ridge.py").exists():
+        pytest.skip("baseline/_ref not installed")
+    sys.path.insert(0, str(ref_root))
+    from kva import ridge as RR
+    from ridgefill_data_b200.ridge.fit import EigenFit
+    from ridgefill_data_b200.ridge.stats import RidgeStats
+    g = torch.Generator().manual_seed(9)
+    d = 24
+    docs = [torch.randn(n, d, generator=g) for n in (90, 130, 61)]
+    maps = {1: torch.randn(d, d, generator=g), 2: torch.randn(d, d, generator=g)}
+    for weighted in (False, True):
+        ours, ref = RidgeStats(0, [1, 2], d), RR.RidgeStats(0, [1, 2], d, "cpu")
+        for x in docs:
+            ys = {i: x @ m + 0.1 * torch.randn(x.shape[0], d, generator=g) for i, m in maps.items()}
+            w = torch.rand(x.shape[0], generator=g) + 0.5 if weighted else None
+            ours.add(x, ys, block=64, w=w)
+            ref.add(x, ys, block=64, w=w)
+        a, b = ours.state(), ref.state()
+        assert a["n"] == pytest.approx(b["n"])
+        for k in ("cx", "sx", "sxx"):
+            torch.testing.assert_close(a[k], b[k], rtol=1e-9, atol=1e-7)
+        for k in ("cy", "sy", "sxy"):
+            for i in (1, 2):
+                torch.testing.assert_close(a[k][i], b[k][i], rtol=1e-9, atol=1e-7)
+        lams = [1e-4, 1e-2, 1.0]
+        fo, fr = EigenFit(a), RR.RidgeFit(b)
+        for i in (1, 2):
+            wo, wr = fo.layer(i, lams), fr.layer(i, lams)
+            for lam in lams:
+                torch.testing.assert_close(wo[lam][0], wr[lam][0], rtol=1e-5, atol=1e-6)
+                torch.testing.assert_close(wo[lam][1], wr[lam][1], rtol=1e-5, atol=1e-6)
+            (ro, eo), (rr, er) = fo.reduced_rank(i, 1e-2, [4, 12]), fr.reduced_rank(i, 1e-2, [4, 12])
+            torch.testing.assert_close(eo, er, rtol=1e-9, atol=1e-12)
+            for r in (4, 12):
+                torch.testing.assert_close(ro[r][0], rr[r][0], rtol=1e-5, atol=1e-6)
