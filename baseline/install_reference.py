@@ -63,6 +63,10 @@ def main(argv):
                     to = dst_fin / ("cells" if f.parent.name == "cells" else "") / f.name
                     shutil.copyfile(f, to)
                     record.setdefault("files_data", {})["finals/" + to.relative_to(dst_fin).as_posix()] = sha256(f)
+            for extra in ("stats.py",):              # its statistics, run as an oracle by the tests
+                if (fin / extra).is_file():
+                    shutil.copyfile(fin / extra, dst_fin / extra)
+                    record["files"]["../finals/" + extra] = sha256(fin / extra)
             (dst_fin / "lib").mkdir()                # its cell-to-config code, run as an oracle by the tests
             for f in sorted((fin / "lib").glob("*.py")):
                 shutil.copyfile(f, dst_fin / "lib" / f.name)

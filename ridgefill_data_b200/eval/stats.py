@@ -295,3 +295,9 @@ def noninferiority(data, *, lower=None, upper=None, alpha=ALPHA, unit_range=None
 
 
 tost = noninferiority
+
+
+def tost(data, *, lower=None, upper=None, alpha=ALPHA, **kw):
+    """noninferiority() under the name the battery's earlier statistics used (equivalence when both margins are
+    declared); the same rule, including the refusal of a degenerate interval."""
+    return noninferiority(data, lower=lower, upper=upper, alpha=alpha, **kw)

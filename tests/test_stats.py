@@ -92,3 +92,38 @@ def test_paired_tables(tmp_path):
     assert md.count("\n") == 3 and "ridgefill" in md
     tex = TB.latex(rows, "nll", "exact")
     assert tex.startswith("\\begin{tabular}") and "\\checkmark" in tex
+
+
+def test_statistics_match_the_reference():
+    """BCa intervals (plain, ratio, stratified), p-values, Holm, MDE and non-inferiority against the reference's
+    finals/stats.py (installed in baseline/_ref): the same declared seed and resample count give the same numbers."""
+    import importlib.util
+    from pathlib import Path
+    path = Path(__file__).resolve().parent.parent / "baseline" / "_ref" / "finals" / "stats.py"
+    if not path.exists():
+        pytest.skip("baseline/_ref not installed")
+    spec = importlib.util.spec_from_file_location("ref_finals_stats", path)
+    RS = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(RS)
+    assert (RS.SEED, RS.N_RESAMPLES) == (ST.SEED, ST.N_RESAMPLES)
+    rng = np.random.default_rng(5)
+    x = rng.normal(0.2, 1.0, 70)
+    pairs = np.stack([rng.normal(1.0, 0.2, 50), rng.normal(2.0, 0.2, 50)], 1)
+    strata = ["a"] * 30 + ["b"] * 40
+    cases = [(x, {}), (pairs, dict(stat=lambda m: m[..., 0] / m[..., 1])),
+             (x, dict(strata=strata, weighting="stratum")), (x, dict(strata=strata))]
+    for data, kw in cases:
+        a, b = ST.bca(data, n_resamples=2000, **kw), RS.bca(data, n_resamples=2000, **kw)
+        assert (a.estimate, a.lo, a.hi) == pytest.approx((b.estimate, b.lo, b.hi), rel=1e-12, abs=1e-12)
+        assert ST.pvalue(a) == pytest.approx(RS.pvalue(b), abs=1e-12)
+    p = {"a": 0.01, "b": 0.04, "c": 0.03, "d": 0.2}
+    assert ST.holm(p) == pytest.approx(RS.holm(p))
+    assert ST.mde(1.3, 64) == pytest.approx(RS.mde(1.3, 64))
+    for kw in (dict(upper=0.5), dict(lower=-0.5), dict(lower=-5.0, unit_range=(-100, 100))):
+        a, b = ST.noninferiority(x, n_resamples=2000, **kw), RS.noninferiority(x, n_resamples=2000, **kw)
+        assert a.passed == b.passed and (a.lo, a.hi) == pytest.approx((b.lo, b.hi), rel=1e-12, abs=1e-12)
+    z = np.zeros(96)
+    a, b = ST.noninferiority(z, lower=-5.0, unit_range=(-100, 100)), RS.noninferiority(z, lower=-5.0,
+                                                                                       unit_range=(-100, 100))
+    assert (a.passed, a.method) == (b.passed, b.method) and a.lo == pytest.approx(b.lo)
+    assert ST.tost(x, upper=0.5, n_resamples=500).passed == RS.tost(x, upper=0.5, n_resamples=500).passed
