@@ -54,19 +54,27 @@ def nll_delta(lp_arm, lp_exact, mask=None):
 
 
 def readout(rec, threshold=THRESHOLD):
-    """Per arm: NLL delta vs exact over all scored tokens, the novel tokens and the key tokens. Reads evaluation
-    records ({"runs": {arm: {"logprobs"}}, "tail_only": {"logprobs"}}) or {"lp": {arm: [...]}, "tail_only": [...]}."""
-    if "tail_only" not in rec:
-        raise KeyTokenReferenceMissing("record lacks the exact tail-only log-probs")
-    if "lp" not in rec:
-        rec = dict(rec, lp={a: r["logprobs"] for a, r in rec["runs"].items() if "logprobs" in r})
+    """{arm: {all | novel | key: {delta, n}}} for every non-exact arm of a grade or longppl evaluation record:
+    the mean NLL change against exact over all scored tokens, the novel tokens and the key tokens (exact log-prob
+    above the tail-only one by more than `threshold` nats). Reads {"runs": {arm: {"logprobs"}}, "tail_only":
+    {"logprobs"}} records (also the flat {"lp": {arm: [...]}, "tail_only": [...]} form)."""
+    if rec.get("tail_only") is None:
+        raise KeyTokenReferenceMissing(f"{rec.get('name')}: no tail_only log-probs (run with keytoken_tail)")
+    lp = rec["lp"] if "lp" in rec else {a: r["logprobs"] for a, r in rec["runs"].items() if "logprobs" in r}
     tail = rec["tail_only"]["logprobs"] if isinstance(rec["tail_only"], dict) else rec["tail_only"]
-    exact = torch.as_tensor(rec["lp"]["exact"])
-    keys = key_mask(exact, torch.as_tensor(tail), threshold)
-    novel = torch.as_tensor(rec["novel"], dtype=torch.bool) if "novel" in rec else None
+    f64 = dict(dtype=torch.float64)
+    exact = torch.as_tensor(lp["exact"], **f64)
+    masks = dict(all=None, novel=torch.as_tensor(rec["novel"], dtype=torch.bool) if "novel" in rec else None,
+                 key=key_mask(exact, torch.as_tensor(tail, **f64), threshold))
     out = {}
-    for arm, lp in rec["lp"].items():
-        lp = torch.as_tensor(lp)
-        out[arm] = dict(all=nll_delta(lp, exact), novel=nll_delta(lp, exact, novel) if novel is not None else None,
-                        key=nll_delta(lp, exact, keys))
+    for arm, values in lp.items():
+        if arm == "exact":
+            continue
+        v = torch.as_tensor(values, **f64)
+        out[arm] = {}
+        for k, m in masks.items():
+            if k == "novel" and m is None:
+                continue
+            d, n = nll_delta(v, exact, m)
+            out[arm][k] = dict(delta=d, n=n)
     return out

@@ -123,7 +123,7 @@ def test_keytok_readout():
     rec = dict(lp=dict(exact=[-1.0, -2.0, -0.5], arm=[-1.5, -2.0, -3.0]), tail_only=[-4.0, -2.1, -0.6],
                novel=[True, False, True])
     out = keytok.readout(rec)
-    assert out["arm"]["key"] == (0.5, 1) and out["arm"]["all"][1] == 3
+    assert out["arm"]["key"] == dict(delta=0.5, n=1) and out["arm"]["all"]["n"] == 3 and "exact" not in out
 
 
 def test_spec_validation():

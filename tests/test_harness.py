@@ -230,5 +230,5 @@ def test_tables_read_harness_records(env):
     r0 = recs[0]
     assert TB.metric_value(r0, "exact", "nll") == pytest.approx(-sum(r0["runs"]["exact"]["logprobs"]) / TX.SCORED)
     ro = keytok.readout(r0)
-    assert set(ro) == {"exact", "rf", "id"} and ro["exact"]["all"][0] == 0.0
+    assert set(ro) == {"rf", "id"} and ro["rf"]["all"]["n"] == TX.SCORED
     assert len(r0["tail_only"]["logprobs"]) == TX.SCORED
