@@ -33,7 +33,7 @@ def run(model, n, cache, first_logits, steps, arm, feed=None, logprobs=False):
         check_finite(logits, f"{arm.name} decode step {t}")
         tops.append(int(logits.argmax()))
         if logprobs:
-            lps.append(torch.log_softmax(logits.double(), -1).float().cpu())
+            lps.append(torch.log_softmax(logits.float(), -1).cpu())
         if t == steps - 1:
             break
         nxt = tops[t] if feed is None else int(feed[t])
@@ -42,9 +42,11 @@ def run(model, n, cache, first_logits, steps, arm, feed=None, logprobs=False):
 
 
 def kl_steps(lp_exact, lp_arm):
-    """KL(exact || arm) per step [steps] from log-probs [steps, V]: sum_v p_exact (log p_exact - log p_arm), fp64."""
-    pe, pa = lp_exact.double(), lp_arm.double()
-    return (pe.exp() * (pe - pa)).sum(-1)
+    """KL(exact || arm) per step [steps] from fp32 log-probs [steps, V]: sum_v p_exact (log p_exact - log p_arm)
+    (the decode set's recorded arithmetic: fp32 log-softmax, torch's KL reduction, so records compare across
+    harnesses)."""
+    import torch.nn.functional as F
+    return F.kl_div(lp_arm, lp_exact, reduction="none", log_target=True).sum(-1)
 
 
 def agreement(exact_tokens, arm_tokens):

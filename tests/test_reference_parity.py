@@ -151,3 +151,69 @@ def test_arm_options_match_reference(name, case):
             from ridgefill_data_b200.engine.decode import greedy
             our_toks, _ = greedy(ours, ids, ocache, got, 4, our_arm)
             assert our_toks == ref_toks
+
+
+def test_multiturn_harness_matches_reference():
+    """The multi-turn set on mk4 prompts (turn plans, follow-up turns, repair by position and by question): the same
+    generated tokens every turn and the same repair rows and costs as the reference's kva/multiturn.py."""
+    import random as _random
+    from kva import multiturn as RMT
+    from ridgefill_data_b200.eval import multiturn as MT
+    from ridgefill_data_b200.eval import text as TX
+    tok = TX.CharTokenizer()
+    words = ["alpha", "beta", "gamma", "delta", "omega", "river", "stone", "cloud", "north", "amber"]
+    r = _random.Random(9)
+    corpus = {"prose": " ".join(r.choice(words) for _ in range(4000))}
+    p = TX.niah_prompts(tok, "raw", variant="mk4", text_of=corpus, lengths=(700,), sources=("prose",))[0]
+    cfg = CONFIGS["qwen3.5-9b"]
+    ref_model, _, _ = R.build(cfg, 4, 200, "cpu", MODS)
+    ours = from_config(cfg, seed=0, device="cpu", dtype=torch.bfloat16)
+    assert MT.plan(tok, p, 3) == RMT.plan(tok, p, 3)
+    specs = [dict(name="id", split=4, tail=200, fill="identity"),
+             dict(name="id-rep", split=4, tail=200, fill="identity", repair=1.0),
+             dict(name="id-repq", split=4, tail=200, fill="identity", repair=0.5, repair_by="question")]
+    RK = MODS[2]
+    orec, rrec = dict(runs={}), dict(runs={})
+    with torch.no_grad():
+        MT.run_prompt(ours, tok, p, [Arm(s["name"], split=4, tail=200, fill="identity", meta=dict(s)) for s in specs],
+                      orec, "raw", (2,), 4, None, 3)
+        RMT.run_prompt(ref_model, tok, p, [RK.Arm(s["name"], split=4, tail=200, fill="identity", meta=dict(s))
+                                           for s in specs], rrec, "raw", (2,), 4, None, 3)
+    assert orec["turns"] == rrec["turns"] and orec["runs"].keys() == rrec["runs"].keys()
+    for arm, o in orec["runs"].items():
+        rr = rrec["runs"][arm]
+        assert [t["gen"] for t in o["turns"]] == [t["gen"] for t in rr["turns"]], arm
+        assert [t["correct"] for t in o["turns"]] == [t["correct"] for t in rr["turns"]], arm
+        if "repair" in o:
+            for k in ("rows", "macs", "layers", "row_layers", "hs_bytes"):
+                assert o["repair"][k] == rr["repair"][k], (arm, k)
+
+
+def test_decode_agreement_matches_reference():
+    """The decode set's forced and free passes (engine/agree.py) against the reference's kva/agree.py."""
+    from kva import agree as RA
+    from ridgefill_data_b200.engine import agree as AG
+    from ridgefill_data_b200.engine.decode import fork_cache
+    from ridgefill_data_b200.engine.prefill import prefill
+    cfg = CONFIGS["qwen3.5-9b"]
+    RK = MODS[2]
+    ref_model, _, ref_step = R.build(cfg, 4, 16, "cpu", MODS)
+    ours = from_config(cfg, seed=0, device="cpu", dtype=torch.bfloat16)
+    ids = uniform_prompt(64, cfg.vocab, seed=3)
+    W, B = synthetic_maps(cfg.hidden, 4, cfg.n_layers, "cpu")
+    with torch.no_grad():
+        oex, ocache_ex, _ = prefill(ours, ids, Arm("exact"), keep=1)
+        arm = Arm("rf", split=4, tail=16, fill="proj", projector=Projector(4, W, B))
+        oarm_l, oarm_c, _ = prefill(ours, ids, arm, keep=1)
+        fields, (y, lp) = AG.exact_record(ours, 64, fork_cache(ocache_ex), oex, 6, Arm("exact"))
+        ours_cmp = AG.compare(ours, 64, oarm_c, oarm_l, 6, arm, y, lp)
+        rex, rcache_ex = ref_model.forward_exact(ids, keep=torch.tensor([63]))
+        ry, rlp = RA.decode(ref_model, 64, [dict(c) for c in rcache_ex], rex, 6, RK.Arm("exact"), logprobs=True)
+        rarm = RK.Arm("rf", split=4, tail=16, fill="proj", projector=RK.Projector(4, W, B))
+        hs, lower = RK.run_lower(ref_model, ids, [4])
+        rl, rc, _ = RK.finish(ref_model, ids, hs[4], lower, rarm, 1)
+        ref_cmp = RA.compare(ref_model, 64, rc, rl, 6, rarm, ry, rlp)
+    assert y == ry and fields["gen"] == ry
+    for k in ("gen", "first_divergence", "frac_identical", "forced_top1_agree"):
+        assert ours_cmp[k] == ref_cmp[k], k
+    assert ours_cmp["kl"] == ref_cmp["kl"] and ours_cmp["kl_mean"] == ref_cmp["kl_mean"]
