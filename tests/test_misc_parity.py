@@ -123,3 +123,47 @@ def test_derived_sets(tmp_path, monkeypatch, which):
     for x, y in zip(a, b):
         for key in ("ids", "refs", "needles", "max_new", "turn_plan", "asks"):
             assert x.get(key) == y.get(key), key
+
+
+def test_first_order_impact_matches_reference():
+    """Per-row first-order fill impact (exact late layers, filled caches, backward through the tail) against the
+    reference's kva/impact.py on the same tiny hybrid model and identity fill."""
+    sys.path.insert(0, str(REF.parent))
+    import reference_arm as RA
+    from ridgefill_data_b200.eval.data import uniform_prompt
+    from ridgefill_data_b200.models.base import from_config
+    from ridgefill_data_b200.models.tiny import tiny_configs
+    from ridgefill_data_b200.engine.prefill import run_lower
+    mods = RA.import_reference()
+    RK = mods[2]
+    cfg = tiny_configs(8, 64)["qwen3.5-9b"]
+    ours = from_config(cfg, seed=0, device="cpu", dtype=torch.float32)
+    ids = uniform_prompt(96, cfg.vocab, seed=5)
+    split, P, scored = 4, 64, 16
+    rows = torch.arange(96 - scored - 1, 96 - 1)
+    tgt = ids[96 - scored:]
+    oh, _ = run_lower(ours, ids, [split])
+    ot, _ = IM.exact_late(ours, oh[split], split, P, rows, tgt)
+    okv, ogdn = IM.fill_late(ours, split, P, lambda i: oh[split][:P])
+    ores, oloss = IM.impact(ours, split, oh[split][P:], P, okv, ot, ogdn, rows - P, tgt)
+    # the reference's model in fp32 on the same seeded weights
+    rm = mods[1]
+    import json as _json
+    import tempfile
+    from pathlib import Path as _P
+    from ridgefill_data_b200.models.checkpoint import RandomSource
+    tmp = _P(tempfile.mkdtemp())
+    (tmp / "config.json").write_text(_json.dumps(cfg.to_hf()))
+    stock = rm.Checkpoint
+    rm.Checkpoint = lambda path: RandomSource(cfg, seed=0, std=0.02)
+    try:
+        rmod = rm.model_class(tmp)(tmp, device="cpu", dtype=torch.float32)
+    finally:
+        rm.Checkpoint = stock
+    rh, _ = RK.run_lower(rmod, ids, [split])
+    rt, _ = RI.exact_late(rmod, rh[split], split, P, rows, tgt)
+    rkv, rgdn = RI.fill_late(rmod, split, P, lambda i: rh[split][:P])
+    rres, rloss = RI.impact(rmod, split, rh[split][P:], P, rkv, rt, rgdn, rows - P, tgt)
+    assert oloss == pytest.approx(rloss, rel=1e-6)
+    for k in ("impact", "err", "grad_norm"):
+        torch.testing.assert_close(ores[k], rres[k], rtol=1e-4, atol=1e-7)
