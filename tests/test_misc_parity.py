@@ -167,3 +167,38 @@ def test_first_order_impact_matches_reference():
     assert oloss == pytest.approx(rloss, rel=1e-6)
     for k in ("impact", "err", "grad_norm"):
         torch.testing.assert_close(ores[k], rres[k], rtol=1e-4, atol=1e-7)
+
+
+def test_grade_and_niah_builders_match_reference(tmp_path, monkeypatch):
+    """The graded prompts (plan file, novel-token masks, short references, raw / chat, BOS dropped) and the K20
+    NIAH prompts (raw, chat, mk4 distractors; the generator's seeded draws) against the reference's kva/data.py on
+    the same plan, corpus and character tokenizer."""
+    import json
+    sys.path.insert(0, str(HERE))
+    from test_eval_sets import TOK
+    from kva import data as RD
+    from ridgefill_data_b200.eval import text as TX
+    r = random.Random(4)
+    words = ["alpha", "beta", "Gamma", "delta", "7", "omega", "river", "stone", "cloud", "north", ".", ","]
+    body = lambda n: " ".join(r.choice(words) for _ in range(n))  # noqa: E731
+    plan = [dict(name=f"g{j}", kind="prose", text=body(400), short_start=500) for j in range(3)]
+    helps = dict(rows=[dict(name=p["name"], helps=j % 2 == 0) for j, p in enumerate(plan)])
+    (tmp_path / "plan-grade.json").write_text(json.dumps(plan))
+    (tmp_path / "swap_summary.json").write_text(json.dumps(helps))
+    monkeypatch.setattr(RD, "INPUTS", tmp_path)
+    for fmt, drop in (("raw", False), ("chat", False), ("raw", True)):
+        ours = TX.grade_prompts(TOK, fmt, drop_bos=drop, plan=plan, helps={x["name"]: x["helps"] for x in helps["rows"]})
+        ref = RD.grade_prompts(TOK, fmt, drop_bos=drop)
+        assert len(ours) == len(ref)
+        for a, b in zip(ours, ref):
+            for k in ("name", "ids", "short_ids", "novel", "short_tail_match", "truncated", "helps16"):
+                assert a[k] == b[k], (fmt, k)
+    corpus = {s: body(40000) for s in TX.NIAH_SOURCES}
+    monkeypatch.setattr(RD, "corpus", lambda: corpus)
+    for fmt, variant in (("raw", None), ("chat", None), ("raw", "mk4")):
+        ours = TX.niah_prompts(TOK, fmt, variant=variant, text_of=corpus)
+        ref = RD.niah_prompts(TOK, fmt, variant)
+        assert len(ours) == len(ref) == 60
+        for a, b in zip(ours, ref):
+            for k in ("name", "ids", "key", "value", "needle_start", "needle_end", "depth", "distractors"):
+                assert a.get(k) == b.get(k), (fmt, variant, k)
