@@ -1,110 +1,139 @@
-"""Multi-turn use of a carried cache and deferred repair (code/kva/multiturn.py:148-255 semantics).
+"""Carried-cache turns and deferred repair (the semantics of code/kva/multiturn.py:148-255).
 
-A pasted document is prefilled once (possibly approximately) and cached; later turns extend the cache exactly
-(extend), decode greedily (decode), and may pay the skipped late-layer work back:
-  repair            layers >= split recomputed exactly over rows [0, R) from their exact layer-split inputs, on a
-                    scratch cache, as chunked prefill of those rows would (R = round(r P), every cached row at r = 1)
-  repair_selected   chosen prefix rows recomputed through layers >= split by finish(exact_rows=...)'s computation
-                    over the other rows as filled; their K/V replace the cached ones (GDN states stay)
-Both replace cache list entries only, never a tensor in place, so forks of the cache stay intact.
+A document is prefilled once, possibly with RidgeFill, and its cache is kept for later turns:
+
+* `extend` runs new rows exactly on top of the cache and `decode` generates greedily from it;
+* `repair` pays the skipped late-layer work back for the first R cached rows: layers >= split run exactly over
+  those rows from their exact split-layer inputs, on a scratch cache, the way a chunked prefill of the rows would;
+  attention layers keep the cached K/V of rows >= R, and a GDN layer's state is replaced only when R covers every
+  row it has absorbed;
+* `repair_selected` recomputes chosen prefix rows through layers >= split with every other row read as filled
+  (the computation of finish(exact_rows=...)), and writes those rows' K/V into the cache; GDN states stay.
+
+Repairs swap whole per-layer cache entries and never write into a cached tensor, so forks that share the
+cache's storage are left as they were.
 """
 from __future__ import annotations
 
 import torch
 
 
+def _positions(model, start, count):
+    return torch.arange(start, start + count, device=model.device)
+
+
 def extend(model, cache, ids, start, split=None, before=None):
-    """Exact forward of new rows at positions start, ... on top of cache. before(low): called once the rows
-    have passed layers < split with their inputs there. Returns (last-row logits, the rows' split inputs)."""
+    """Run rows `ids` exactly at positions start, start + 1, ... on top of `cache`.
+
+    before(low), if given, is called as the rows reach layer `split`, with low = {layer < split: that layer's input
+    rows}. Returns (logits of the last row, the rows' layer-`split` inputs or None)."""
     ids = torch.as_tensor(ids, device=model.device)
-    pos = torch.arange(start, start + ids.shape[0], device=model.device)
-    h, hb, low = model.embed(ids), None, {}
+    pos = _positions(model, start, ids.shape[0])
+    h = model.embed(ids)
+    inputs = {}
+    at_split = None
     for i in range(model.n_layers):
         if i == split:
-            hb = h
+            at_split = h
             if before is not None:
-                before(low)
-        if before is not None and split is not None and i < split:
-            low[i] = h
+                before(inputs)
+        elif split is not None and before is not None and i < split:
+            inputs[i] = h
         h = model.layer(i, h, pos, cache)
-    return model.logits(h[-1:]), hb
+    return model.logits(h[-1:]), at_split
 
 
 def decode(model, cache, logits, start, steps, eos=(), split=None):
-    """Greedy decode feeding rows from start. Returns (ids, 'stop' | 'length', fed rows' split inputs)."""
-    out, hb = [], []
-    tok = int(logits[-1].argmax())
-    reason = "length"
+    """Greedy generation of at most `steps` tokens; each generated token except the last is fed back at positions
+    start, start + 1, .... Returns (ids, "stop" on an eos id or "length", the fed rows' layer-`split` inputs
+    stacked, or None)."""
+    eos = set(eos)
+    ids, fed = [], []
+    nxt = int(logits[-1].argmax())
+    finish = "length"
     for t in range(steps):
-        out.append(tok)
-        if tok in eos:
-            reason = "stop"
+        ids.append(nxt)
+        if nxt in eos:
+            finish = "stop"
             break
-        if t == steps - 1:
+        if len(ids) == steps:
             break
-        lg, b = extend(model, cache, [tok], start + t, split)
-        hb.append(b)
-        tok = int(lg[-1].argmax())
-    return out, reason, (torch.cat(hb) if hb and split is not None else None)
+        lg, hb = extend(model, cache, [nxt], start + t, split)
+        if hb is not None:
+            fed.append(hb)
+        nxt = int(lg[-1].argmax())
+    return ids, finish, (torch.cat(fed) if fed else None)
 
 
 def cached_rows(cache, layer):
-    c = cache[layer]
-    return c.get("n", c.get("len", 0))
+    """Rows held by one layer's cache entry (attention: 'n'; GDN: 'len')."""
+    entry = cache[layer]
+    return entry["n"] if "n" in entry else entry.get("len", 0)
 
 
 def repair_rows(r, P, H):
-    return H if P > 0 and r >= 1 else round(r * P)
+    """Rows a deferred repair of share r covers: every cached row (H) at r >= 1, else round(r * P)."""
+    if r >= 1 and P > 0:
+        return H
+    return round(r * P)
 
 
-def _put_kv(model, cache, i, k, v):
-    new = {}
-    model._append_kv(new, k, v)
-    cache[i] = new
+def _fresh_kv(model, k, v):
+    entry = {}
+    model._append_kv(entry, k, v)
+    return entry
 
 
 def repair(model, cache, hb, split, rows):
-    H = cached_rows(cache, split)
-    if not 0 <= rows <= H or hb.shape[0] < rows:
-        raise ValueError(f"repair of {rows} rows: {H} cached, {hb.shape[0]} inputs")
-    if rows == 0:
+    """Exact recomputation of layers >= split over cached rows [0, rows) from their layer-split inputs hb."""
+    held = cached_rows(cache, split)
+    if rows < 0 or rows > held or rows > hb.shape[0]:
+        raise ValueError(f"cannot repair {rows} rows: the cache holds {held}, {hb.shape[0]} split inputs given")
+    if not rows:
         return
-    pos = torch.arange(rows, device=model.device)
-    tmp = model.new_cache()
+    scratch = model.new_cache()
+    pos = _positions(model, 0, rows)
     h = hb[:rows].to(model.device)
     for i in range(split, model.n_layers):
-        h = model.layer(i, h, pos, tmp)
-        c, t = cache[i], tmp[i]
+        h = model.layer(i, h, pos, scratch)
+        new, old = scratch[i], cache[i]
         if model.layer_types[i] == "attn":
-            _put_kv(model, cache, i, torch.cat((t["k"], c["k"][:, rows:]), 1), torch.cat((t["v"], c["v"][:, rows:]), 1))
-        elif rows == c["len"]:
-            cache[i] = dict(conv=t["conv"], rec=t["rec"], len=rows)
-        tmp[i] = {}
+            k = torch.cat([new["k"], old["k"][:, rows:]], dim=1)
+            v = torch.cat([new["v"], old["v"][:, rows:]], dim=1)
+            cache[i] = _fresh_kv(model, k, v)
+        elif old["len"] == rows:
+            cache[i] = {"conv": new["conv"], "rec": new["rec"], "len": rows}
+        scratch[i] = {}
 
 
 def fill_inputs(model, arm, i, b):
-    f = arm.fill_of(model.layer_types[i])
-    if f == "proj":
-        return arm.projector(i, b)
-    if f == "identity":
+    """Layer i's filled inputs of rows whose layer-split inputs are b, under the arm's fill."""
+    kind = arm.fill_of(model.layer_types[i])
+    if kind == "identity":
         return b
-    raise ValueError(f"no fill inputs for fill {f!r}")
+    if kind == "proj":
+        return arm.projector(i, b)
+    raise ValueError(f"fill {kind!r} has no per-layer inputs to recompute from")
 
 
 def repair_selected(model, cache, arm, b, rows):
-    if len(rows) == 0:
+    """Recompute prefix rows `rows` through layers >= arm.split over the filled prefix (b: every prefix row's
+    layer-split input) and write their K/V into the cache."""
+    if not len(rows):
         return
-    P = b.shape[0]
-    r = torch.as_tensor(rows, dtype=torch.long, device=model.device)
-    pos = torch.arange(P, device=model.device)
+    sel = torch.as_tensor(rows, dtype=torch.long, device=model.device)
     b = b.to(model.device)
-    hr = b[r]
-    tmp = model.new_cache()
+    pos = _positions(model, 0, b.shape[0])
+    scratch = model.new_cache()
+    cur = b.index_select(0, sel)
     for i in range(arm.split, model.n_layers):
-        x = fill_inputs(model, arm, i, b)
-        hr_next = model.layer_rows(i, x.index_copy(0, r, hr.to(x.dtype)), pos, r, tmp)
+        base = fill_inputs(model, arm, i, b)
+        x = base.index_copy(0, sel, cur.to(base.dtype))
+        nxt = model.layer_rows(i, x, pos, sel, scratch)
         if model.layer_types[i] == "attn":
-            c, t = cache[i], tmp[i]
-            _put_kv(model, cache, i, c["k"].index_copy(1, r, t["k"][:, r]), c["v"].index_copy(1, r, t["v"][:, r]))
-        tmp[i] = {}
-        hr = hr_next
+            got, old = scratch[i], cache[i]
+            k = old["k"].index_copy(1, sel, got["k"].index_select(1, sel))
+            v = old["v"].index_copy(1, sel, got["v"].index_select(1, sel))
+            cache[i] = _fresh_kv(model, k, v)
+        scratch[i] = {}
+        cur = nxt
