@@ -1,19 +1,19 @@
-"""Statistics of paired arm-vs-reference results (code/finals/stats.py): BCa bootstrap intervals, p-values by
-interval inversion, Holm's step-down adjustment, minimum detectable effects and one-sided non-inferiority tests.
+"""Statistics of paired arm-vs-reference results (the rules of code/finals/stats.py): BCa bootstrap intervals,
+p-values by inverting the interval, Holm's step-down adjustment, minimum detectable effects and one-sided
+non-inferiority (two one-sided tests when both margins are given).
 
-Declared constants (kept as the reference declares them so intervals reproduce): 5000 resamples of units with seed
-20261004, 95% two-sided level, alpha 0.05, power 0.80. A unit is one prompt / document / row holding every arm
-(the pairing unit); strata (e.g. a task) resample within themselves.
+Declared constants, kept equal to the reference's so that the same data give the same intervals: B = 5000
+resamples drawn from numpy's default_rng(20261004), a 95% two-sided level, alpha 0.05 and power 0.80. The
+resampling unit is the pairing unit (a prompt, a document, a row); with strata every stratum is resampled within
+itself, strata in sorted label order, one integer draw of shape (B, stratum size) each.
 
-BCa (Efron 1987, "Better bootstrap confidence intervals"): with theta_b the resampled statistics and theta_(i) the
-leave-one-unit-out statistics,
-    z0 = Phi^-1( (#{theta_b < theta} + #{theta_b <= theta}) / (2 B) )            (ties count one half)
-    a  = sum d^3 / (6 (sum d^2)^1.5),  d = mean(theta_(.)) - theta_(i)            (jackknife acceleration)
-    endpoint(z) = quantile of theta_b at Phi(z0 + (z0 + z) / (1 - a (z0 + z))),  z = -/+ Phi^-1(1 - level / 2 ... )
-with linearly interpolated quantiles. Estimands are "unit" weighted (every unit once) or "stratum" weighted (the
-mean of the stratum means). Identical paired differences give a degenerate zero-width interval (flagged), which a
-non-inferiority test never accepts as evidence unless the bounded-data binomial floor decides.
-Pure numpy + statistics.NormalDist; scipy serves as the oracle in the tests.
+BCa (Efron 1987): from the resampled statistics t_b and the leave-one-unit-out statistics t_(i),
+    z0 = Phi^-1(share of t_b below the estimate, ties counted one half)
+    a  = sum(d^3) / (6 (sum d^2)^(3/2)),   d_i = mean(t_(.)) - t_(i)
+and the interval ends are the linearly interpolated quantiles of t_b at Phi(z0 + (z0 + z) / (1 - a (z0 + z))) for
+z = Phi^-1((1 - level) / 2) and its negation. An estimand weighs every unit once ("unit") or averages the stratum
+means ("stratum"). Data without any variation give a zero-width interval flagged degenerate, which a
+non-inferiority test never takes as evidence (except through the bounded-data binomial floor).
 """
 from __future__ import annotations
 
@@ -28,78 +28,90 @@ N_RESAMPLES = 5000
 LEVEL = 0.95
 ALPHA = 0.05
 POWER = 0.80
-_N = NormalDist()
+_PHI = NormalDist()
 
-ESTIMANDS = {
-    "nll": "unit",          # document-weighted mean of per-document arm-minus-exact NLL
-    "accuracy": "unit",     # row-weighted (pooled over tasks and lengths)
-    "longbench": "stratum", # mean of the task means
-    "agreement": "unit",    # prompt-weighted share of agreeing decode steps
-    "kl": "unit",           # prompt-weighted mean per-step KL
-}
+# how each reported estimand weighs its units
+ESTIMANDS = dict(nll="unit", accuracy="unit", longbench="stratum", agreement="unit", kl="unit")
 
 
 class StatsError(ValueError):
-    """The statistic cannot be computed from these inputs as declared."""
+    """The declared statistic is not defined for these inputs."""
 
 
 class IntervalUndefined(StatsError):
-    """The statistic is not finite on some resample or leave-one-out set; carries the point estimate."""
+    """The statistic is infinite or NaN on some resample or leave-one-out set (the point estimate is kept)."""
 
     def __init__(self, estimate, n_bad, n_resamples):
-        super().__init__(f"the statistic is not finite on {n_bad} of {n_resamples} resamples")
-        self.estimate, self.n_bad, self.n_resamples = estimate, n_bad, n_resamples
+        self.estimate = estimate
+        self.n_bad = n_bad
+        self.n_resamples = n_resamples
+        super().__init__(f"{n_bad}/{n_resamples} bootstrap resamples give a non-finite statistic")
 
 
 def weighting_of(estimand):
-    if estimand not in ESTIMANDS:
-        raise StatsError(f"undeclared estimand {estimand!r}: declared are {sorted(ESTIMANDS)}")
-    return ESTIMANDS[estimand]
+    try:
+        return ESTIMANDS[estimand]
+    except KeyError:
+        raise StatsError(f"estimand {estimand!r} is not declared (one of {sorted(ESTIMANDS)})") from None
 
 
 def paired(a, b, *, what, subset=False):
-    """(sorted units, xa, xb) of two {unit: value} maps that must hold the same units (b may hold more when
-    subset)."""
-    ka, kb = set(a), set(b)
-    if not ka:
-        raise StatsError(f"{what}: no units on the first side")
-    only_a, only_b = sorted(ka - kb), sorted(kb - ka)
-    if only_a or (only_b and not subset):
-        raise StatsError(f"{what}: unpaired units (first only {only_a[:5]}, second only {only_b[:5]})")
-    units = sorted(ka)
-    xa = np.array([a[u] for u in units], dtype=float)
-    xb = np.array([b[u] for u in units], dtype=float)
-    if not (np.isfinite(xa).all() and np.isfinite(xb).all()):
-        raise StatsError(f"{what}: non-finite value in a paired unit")
-    return units, xa, xb
+    """Align two {unit: value} maps: (sorted units, values of a, values of b). Both must hold the same units, except
+    that b may hold extra ones when subset is set."""
+    if not a:
+        raise StatsError(f"{what}: the first map is empty")
+    missing_b = sorted(set(a) - set(b))
+    extra_b = sorted(set(b) - set(a))
+    if missing_b or (extra_b and not subset):
+        raise StatsError(f"{what}: units do not pair up ({missing_b[:5]} lack a partner, {extra_b[:5]} are extra)")
+    units = sorted(a)
+    va = np.fromiter((a[u] for u in units), dtype=float, count=len(units))
+    vb = np.fromiter((b[u] for u in units), dtype=float, count=len(units))
+    if not np.isfinite(np.concatenate([va, vb])).all():
+        raise StatsError(f"{what}: a paired value is NaN or infinite")
+    return units, va, vb
 
 
-def _strata(n, strata):
-    if strata is None:
-        return [np.arange(n)]
-    labels = np.asarray([str(s) for s in strata])
-    if labels.shape != (n,):
-        raise StatsError(f"strata has {labels.shape[0]} labels for {n} units")
-    return [np.flatnonzero(labels == lab) for lab in sorted(set(labels.tolist()))]
+class _Design:
+    """Units, strata and weighting of one estimand; computes it on the data, on resamples and leaving each unit
+    out."""
 
+    def __init__(self, x, strata, weighting):
+        self.x = x
+        n = x.shape[0]
+        if strata is None:
+            self.groups = [np.arange(n)]
+        else:
+            labels = np.array([str(s) for s in strata])
+            if labels.shape != (n,):
+                raise StatsError(f"{labels.shape[0]} stratum labels for {n} units")
+            self.groups = [np.flatnonzero(labels == lab) for lab in sorted(set(labels.tolist()))]
+        self.by_unit = weighting == "unit"
+        if not self.by_unit and any(len(g) < 2 for g in self.groups):
+            raise StatsError("stratum weighting needs two or more units in every stratum")
 
-def _means(x, groups, weighting):
-    if weighting == "unit":
-        return x.mean(axis=0)
-    return np.mean([x[g].mean(axis=0) for g in groups], axis=0)
+    def point(self):
+        if self.by_unit:
+            return self.x.mean(axis=0)
+        return np.mean([self.x[g].mean(axis=0) for g in self.groups], axis=0)
 
+    def resampled(self, rng, B):
+        draws = [g[rng.integers(0, len(g), (B, len(g)))] for g in self.groups]
+        if self.by_unit:
+            return self.x[np.concatenate(draws, axis=1)].mean(axis=1)
+        return np.mean([self.x[d].mean(axis=1) for d in draws], axis=0)
 
-def _loo_means(x, groups, weighting):
-    """Leave-one-unit-out estimand means [n, k] in closed form."""
-    n = x.shape[0]
-    if weighting == "unit":
-        return (x.sum(axis=0)[None, :] - x) / (n - 1)
-    gm = np.stack([x[g].mean(axis=0) for g in groups])
-    out = np.empty_like(x)
-    for gi, g in enumerate(groups):
-        others = gm.sum(axis=0) - gm[gi]
-        out[g] = (others[None, :] + (x[g].sum(axis=0)[None, :] - x[g]) / (len(g) - 1)) / len(groups)
-    return out
+    def leave_one_out(self):
+        x = self.x
+        if self.by_unit:
+            return (x.sum(axis=0)[None, :] - x) / (x.shape[0] - 1)
+        means = np.stack([x[g].mean(axis=0) for g in self.groups])
+        total = means.sum(axis=0)
+        out = np.empty_like(x)
+        for j, g in enumerate(self.groups):
+            without = (x[g].sum(axis=0)[None, :] - x[g]) / (len(g) - 1)
+            out[g] = ((total - means[j])[None, :] + without) / len(self.groups)
+        return out
 
 
 @dataclass
@@ -118,99 +130,103 @@ class BCa:
     theta_b: np.ndarray = field(repr=False)
 
     def excludes(self, null=0.0):
-        return self.lo > null or self.hi < null
+        return not self.lo <= null <= self.hi
+
+
+def _below(values, at):
+    """Share of values below `at`, a value equal to it counting one half."""
+    return (np.count_nonzero(values < at) + np.count_nonzero(values <= at)) / (2 * values.size)
 
 
 def bca(data, *, stat=None, strata=None, weighting="unit", n_resamples=N_RESAMPLES, seed=SEED, level=LEVEL):
-    """BCa interval of stat(estimand means) over units. data [n] or [n, k] (a unit's columns resample together);
-    stat maps [..., k] means to [...] (default: column 0)."""
+    """BCa interval of stat(means) over units; data is [n] or [n, k] (the k columns of a unit move together) and
+    stat maps [..., k] means to [...] (default: the first column)."""
     x = np.asarray(data, dtype=float)
-    x = x[:, None] if x.ndim == 1 else x
+    if x.ndim == 1:
+        x = x.reshape(-1, 1)
     if x.ndim != 2:
-        raise StatsError(f"data must be (n,) or (n, k), got {x.shape}")
-    n, k = x.shape
+        raise StatsError(f"expected data of shape (n,) or (n, k), not {x.shape}")
+    n = x.shape[0]
     if n < 2:
-        raise StatsError(f"BCa needs at least 2 units, got {n}")
+        raise StatsError(f"{n} unit(s): a bootstrap interval needs two or more")
     if not np.isfinite(x).all():
-        raise StatsError("non-finite value in the data")
+        raise StatsError("the data hold NaN or infinite values")
     if weighting not in ("unit", "stratum"):
-        raise StatsError(f"unknown weighting {weighting!r}")
-    if not 0.0 < level < 1.0 or n_resamples < 100:
-        raise StatsError(f"level {level} / n_resamples {n_resamples} out of range")
-    stat = stat or (lambda m: m[..., 0])
-    groups = _strata(n, strata)
-    if weighting == "stratum" and min(len(g) for g in groups) < 2:
-        raise StatsError("stratum weighting needs at least 2 units per stratum")
-    rng = np.random.default_rng(seed)
-    picks = [g[rng.integers(0, len(g), (n_resamples, len(g)))] for g in groups]
-    if weighting == "unit":
-        idx = np.concatenate(picks, axis=1)
-        means_b = x[idx].mean(axis=1)                                  # [B, k]
-    else:
-        means_b = np.mean([x[p].mean(axis=1) for p in picks], axis=0)
+        raise StatsError(f"weighting must be 'unit' or 'stratum', not {weighting!r}")
+    if not (0.0 < level < 1.0) or n_resamples < 100:
+        raise StatsError(f"need 0 < level < 1 and at least 100 resamples (level {level}, {n_resamples} resamples)")
+    if stat is None:
+        stat = lambda m: m[..., 0]                                   # noqa: E731
+    design = _Design(x, strata, weighting)
+    boot_means = design.resampled(np.random.default_rng(seed), n_resamples)
     with np.errstate(divide="ignore", invalid="ignore"):
-        theta_b = np.asarray(stat(means_b), dtype=float)
-        theta = float(stat(_means(x, groups, weighting)))
-        theta_j = np.asarray(stat(_loo_means(x, groups, weighting)), dtype=float)
-    if not (np.isfinite(theta_b).all() and np.isfinite(theta_j).all() and math.isfinite(theta)):
-        raise IntervalUndefined(theta, int(np.count_nonzero(~np.isfinite(theta_b))), n_resamples)
-    se = float(theta_b.std(ddof=1))
-    d = theta_j.mean() - theta_j
+        t_b = np.asarray(stat(boot_means), dtype=float)
+        est = float(stat(design.point()))
+        t_j = np.asarray(stat(design.leave_one_out()), dtype=float)
+    if not (math.isfinite(est) and np.isfinite(t_b).all() and np.isfinite(t_j).all()):
+        raise IntervalUndefined(est, int((~np.isfinite(t_b)).sum()), n_resamples)
+    se = float(t_b.std(ddof=1))
+    d = t_j.mean() - t_j
+    common = dict(n=n, level=level, n_resamples=n_resamples, seed=seed, theta_b=t_b)
     if se == 0.0 and not d.any():
-        return BCa(theta, theta, theta, n, 0.0, 0.0, 0.0, level, n_resamples, seed, True, theta_b)
-    share = (np.count_nonzero(theta_b < theta) + np.count_nonzero(theta_b <= theta)) / (2 * n_resamples)
-    if not 0.0 < share < 1.0:
-        raise StatsError(f"BCa undefined: the estimate {theta:.6g} lies outside every bootstrap resample")
-    z0 = _N.inv_cdf(share)
-    ss = float((d * d).sum())
-    a = float((d ** 3).sum() / (6.0 * ss ** 1.5)) if ss > 0 else 0.0
-    z = _N.inv_cdf((1.0 - level) / 2.0)
-    levels = [_N.cdf(z0 + (z0 + zz) / (1.0 - a * (z0 + zz))) for zz in (z, -z)]
-    lo, hi = np.quantile(theta_b, levels)
-    return BCa(theta, float(lo), float(hi), n, se, z0, a, level, n_resamples, seed, False, theta_b)
+        return BCa(est, est, est, se=0.0, z0=0.0, a=0.0, degenerate=True, **common)
+    frac = _below(t_b, est)
+    if frac <= 0.0 or frac >= 1.0:
+        raise StatsError(f"no BCa interval: every resample lies on one side of the estimate {est:.6g}")
+    z0 = _PHI.inv_cdf(frac)
+    d2 = float((d * d).sum())
+    accel = float((d ** 3).sum() / (6.0 * d2 ** 1.5)) if d2 > 0 else 0.0
+    z = _PHI.inv_cdf((1.0 - level) / 2.0)
+
+    def adjusted(zq):
+        return _PHI.cdf(z0 + (z0 + zq) / (1.0 - accel * (z0 + zq)))
+
+    lo, hi = np.quantile(t_b, [adjusted(z), adjusted(-z)])
+    return BCa(est, float(lo), float(hi), se=se, z0=z0, a=accel, degenerate=False, **common)
 
 
 def pvalue(res, null=0.0):
-    """Two-sided p-value of theta = null: the level at which a BCa endpoint reaches null (floor 1 / B)."""
-    floor = 1.0 / res.n_resamples
+    """Two-sided p-value of the hypothesis theta = null: twice the BCa tail level at which an interval end reaches
+    null, at least 1 / B."""
+    B = res.n_resamples
+    floor = 1.0 / B
     if res.degenerate:
         return 1.0 if res.estimate == null else floor
-    B = res.n_resamples
-    g = (np.count_nonzero(res.theta_b < null) + np.count_nonzero(res.theta_b <= null)) / (2 * B)
-    g = min(max(g, 1.0 / (2 * B)), 1.0 - 1.0 / (2 * B))
-    v = _N.inv_cdf(g) - res.z0
-    if 1.0 + res.a * v <= 0.0:
+    g = float(np.clip(_below(res.theta_b, null), 0.5 / B, 1.0 - 0.5 / B))
+    v = _PHI.inv_cdf(g) - res.z0
+    den = 1.0 + res.a * v
+    if den <= 0.0:
         return floor
-    tail = _N.cdf(v / (1.0 + res.a * v) - res.z0)
-    return float(min(1.0, max(floor, 2.0 * min(tail, 1.0 - tail))))
+    tail = _PHI.cdf(v / den - res.z0)
+    return float(np.clip(2.0 * min(tail, 1.0 - tail), floor, 1.0))
 
 
 def holm(pvals):
-    """Holm step-down adjusted p-values of one family {name: p} (monotone, capped at 1)."""
-    order = sorted(pvals, key=lambda name: (pvals[name], name))
-    out, running = {}, 0.0
-    for i, name in enumerate(order):
-        p = pvals[name]
-        if not 0.0 <= p <= 1.0:
-            raise StatsError(f"Holm: p-value of {name!r} is {p}")
-        running = max(running, min(1.0, (len(order) - i) * p))
-        out[name] = running
-    return out
+    """Holm step-down adjusted p-values of one family {name: p}: monotone in the raw order, capped at 1."""
+    bad = {k: p for k, p in pvals.items() if not 0.0 <= p <= 1.0}
+    if bad:
+        raise StatsError(f"Holm adjustment of p-values outside [0, 1]: {bad}")
+    ranked = sorted(pvals.items(), key=lambda kv: (kv[1], kv[0]))
+    m = len(ranked)
+    steps = np.minimum(1.0, np.array([(m - i) * p for i, (_, p) in enumerate(ranked)]))
+    adj = np.maximum.accumulate(steps) if m else steps
+    return {name: float(v) for (name, _), v in zip(ranked, adj)}
 
 
 def mde(sd, n, alpha=ALPHA, power=POWER):
-    """(z(1 - alpha / 2) + z(power)) sd / sqrt(n)."""
-    if n < 2 or not math.isfinite(sd) or sd < 0:
-        raise StatsError(f"MDE needs n >= 2 and a finite sd >= 0 (n {n}, sd {sd})")
-    return (_N.inv_cdf(1.0 - alpha / 2.0) + _N.inv_cdf(power)) * sd / math.sqrt(n)
+    """Minimum detectable effect of a two-sided test: (z(1 - alpha / 2) + z(power)) * sd / sqrt(n)."""
+    if n < 2 or not (math.isfinite(sd) and sd >= 0):
+        raise StatsError(f"an MDE needs n >= 2 units and a finite, non-negative sd (got n={n}, sd={sd})")
+    return (_PHI.inv_cdf(1.0 - alpha / 2.0) + _PHI.inv_cdf(power)) * sd / math.sqrt(n)
 
 
 def mde_paired(deltas, alpha=ALPHA, power=POWER):
+    """(sd, n, MDE) of one-dimensional paired differences."""
     d = np.asarray(deltas, dtype=float)
-    if d.ndim != 1 or d.size < 2 or not np.isfinite(d).all():
-        raise StatsError("MDE needs at least 2 finite paired deltas")
+    if d.ndim != 1 or len(d) < 2 or not np.isfinite(d).all():
+        raise StatsError("an MDE of paired differences needs a 1-D array of two or more finite values")
     sd = float(d.std(ddof=1))
-    return sd, int(d.size), mde(sd, d.size, alpha, power)
+    return sd, len(d), mde(sd, len(d), alpha, power)
 
 
 @dataclass
@@ -227,77 +243,80 @@ class NonInferiority:
     reason: str
 
 
-DEGENERATE = "degenerate: zero observed variation is not a finite-sample guarantee"
+DEGENERATE = "degenerate: data without variation give no finite-sample guarantee"
 
 
 def binomial_floor(n, alpha=ALPHA):
-    """One-sided (1 - alpha) upper bound on the share of worse units when none of n is: 1 - alpha^(1/n)."""
+    """One-sided (1 - alpha) upper bound on the share of worse units when none of n is worse: 1 - alpha^(1/n)."""
     return 1.0 - alpha ** (1.0 / n)
 
 
+def _check_range(x, unit_range, kw):
+    a, b = float(unit_range[0]), float(unit_range[1])
+    if x.ndim != 1:
+        raise StatsError("a unit_range bound applies to one-dimensional paired differences")
+    if kw.get("weighting", "unit") != "unit":
+        raise StatsError("the binomial floor is defined for unit-weighted means")
+    if not (a < 0.0 < b):
+        raise StatsError(f"unit_range {unit_range} must contain 0 in its interior")
+    if x.min() < a or x.max() > b:
+        raise StatsError(f"paired differences fall outside unit_range {unit_range}")
+    return a, b
+
+
 def noninferiority(data, *, lower=None, upper=None, alpha=ALPHA, unit_range=None, **kw):
-    """Paired differences against one-sided margins (both: two one-sided tests). Passes when the one-sided
-    (1 - alpha) bounds (the ends of the (1 - 2 alpha) BCa interval) sit on the right side of the margins.
-    unit_range (a < 0 < b): bounded per-unit differences; where no unit is worse in a margin's direction that bound
-    is the exact binomial floor share x (a or b), and it replaces a less conservative BCa bound otherwise."""
+    """Test paired differences against one-sided margins. A side passes when its one-sided (1 - alpha) bound (an
+    end of the (1 - 2 alpha) BCa interval) lies inside the margin. With unit_range = (a, b), a < 0 < b, the
+    differences are bounded: on a side where no unit is worse, the bound is the exact binomial floor share times
+    a or b, and on the other sides the floor replaces the BCa bound where it is the stricter one."""
     if lower is None and upper is None:
-        raise StatsError("non-inferiority needs at least one declared margin")
-    if lower is not None and upper is not None and not lower < upper:
-        raise StatsError(f"margins out of order: {lower} >= {upper}")
+        raise StatsError("declare a lower or an upper margin")
+    if lower is not None and upper is not None and lower >= upper:
+        raise StatsError(f"the lower margin {lower} must lie below the upper margin {upper}")
     if not 0.0 < alpha < 0.5:
-        raise StatsError(f"alpha {alpha} out of range")
-    r = bca(data, level=1.0 - 2.0 * alpha, **kw)
+        raise StatsError(f"alpha must lie in (0, 0.5), not {alpha}")
+    res = bca(data, level=1.0 - 2.0 * alpha, **kw)
     x = np.asarray(data, dtype=float)
-    degenerate = r.degenerate or bool((x == x[:1]).all())
-    lo, hi = r.lo, r.hi
-    methods, reasons = set(), []
+    flat = res.degenerate or bool(np.all(x == x[:1]))
+    pct = f"{100 * (1 - alpha):g}%"
+
+    def refused():
+        return NonInferiority(res.estimate, res.lo, res.hi, lower, upper, False, res.n, alpha, "bca", DEGENERATE)
+
+    bounds = {"lower": res.lo, "upper": res.hi}
+    methods, notes = set(), []
     if unit_range is None:
-        if degenerate:
-            return NonInferiority(r.estimate, lo, hi, lower, upper, False, r.n, alpha, "bca", DEGENERATE)
+        if flat:
+            return refused()
         methods.add("bca")
-        reasons.append(f"one-sided {100 * (1 - alpha):g}% BCa bound")
+        notes.append(f"one-sided {pct} BCa bound")
     else:
-        a, b = (float(v) for v in unit_range)
-        if x.ndim != 1:
-            raise StatsError("unit_range applies to (n,) paired differences only")
-        if kw.get("weighting", "unit") != "unit":
-            raise StatsError("the binomial floor holds for unit-weighted means only")
-        if not a < 0.0 < b:
-            raise StatsError(f"unit_range {unit_range} must hold 0 strictly inside")
-        if x.min() < a or x.max() > b:
-            raise StatsError(f"a paired difference lies outside unit_range {unit_range}")
-        share = binomial_floor(r.n, alpha)
+        a, b = _check_range(x, unit_range, kw)
+        share = binomial_floor(res.n, alpha)
         for side, margin in (("lower", lower), ("upper", upper)):
             if margin is None:
                 continue
             floor = share * (a if side == "lower" else b)
-            none_worse = bool((x >= 0).all() if side == "lower" else (x <= 0).all())
-            if none_worse:
-                bound, m = floor, "exact-binomial-floor"
-                reasons.append(f"no unit worse: exact binomial floor ({100 * share:.2f}% worse units at most)")
-            elif degenerate:
-                return NonInferiority(r.estimate, lo, hi, lower, upper, False, r.n, alpha, "bca", DEGENERATE)
-            else:
-                bca_bound = r.lo if side == "lower" else r.hi
-                stricter = floor < bca_bound if side == "lower" else floor > bca_bound
-                bound, m = (floor, "exact-binomial-floor") if stricter else (bca_bound, "bca")
-                reasons.append(f"one-sided {100 * (1 - alpha):g}% BCa bound" +
-                               (", replaced by the stricter binomial floor" if stricter else ""))
-            if side == "lower":
-                lo = bound
-            else:
-                hi = bound
-            methods.add(m)
-    ok = (lower is None or lo >= lower) and (upper is None or hi <= upper)
-    method = methods.pop() if len(methods) == 1 else "+".join(sorted(methods))
-    return NonInferiority(r.estimate, float(lo), float(hi), lower, upper, bool(ok), r.n, alpha, method,
-                          "; ".join(reasons))
-
-
-tost = noninferiority
+            if (x >= 0).all() if side == "lower" else (x <= 0).all():
+                bounds[side] = floor
+                methods.add("exact-binomial-floor")
+                notes.append(f"no unit worse: exact binomial floor ({100 * share:.2f}% worse units at most)")
+                continue
+            if flat:
+                return refused()
+            stricter = floor < bounds[side] if side == "lower" else floor > bounds[side]
+            if stricter:
+                bounds[side] = floor
+            methods.add("exact-binomial-floor" if stricter else "bca")
+            notes.append(f"one-sided {pct} BCa bound" + (", replaced by the stricter binomial floor" if stricter
+                                                          else ""))
+    lo, hi = bounds["lower"], bounds["upper"]
+    passed = (lower is None or lo >= lower) and (upper is None or hi <= upper)
+    method = "+".join(sorted(methods))
+    return NonInferiority(res.estimate, float(lo), float(hi), lower, upper, bool(passed), res.n, alpha, method,
+                          "; ".join(notes))
 
 
 def tost(data, *, lower=None, upper=None, alpha=ALPHA, **kw):
-    """noninferiority() under the name the battery's earlier statistics used (equivalence when both margins are
-    declared); the same rule, including the refusal of a degenerate interval."""
+    """The same test as noninferiority(), under its older name (an equivalence test when both margins are given)."""
     return noninferiority(data, lower=lower, upper=upper, alpha=alpha, **kw)
