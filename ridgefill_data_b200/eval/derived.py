@@ -1,16 +1,17 @@
-"""Prompt sets derived from locked RULER rows (code/kva/derived.py): a second question on a cached prefix
-(twokey) and the question placed before the document (qfirst). Manifests hold ids, row numbers, needle ordinals
-and sha256 hashes only; prompts are rebuilt from the locked rows at run time and every sample is checked against
-its manifest entry first.
+"""Prompt sets derived from the locked RULER rows (the sets of code/kva/derived.py):
 
-twokey  every row of ruler/niah_multikey_1_<L>.jsonl (4 keyed needles, one asked). Turn 1 is the row as RULER runs
-        it; turn 2 asks one of the other three keys, random.Random(f"{SEED}:{sample id}").choice over them in
-        document order, in RULER's one-key wording. Rows without exactly 4 distinct keys and 4 distinct 7-digit
-        values, one of them the answer, and RULER's question / prefix for it, are refused by name.
-qfirst  every row of the 4 RULER NIAH tasks: instruction \\n question \\n context, and the answer prefix without
-        " for <query>", so the keys appear only before the document.
-Sample ids: ruler2k-<L>-<row:02d> and rulerqf-<task>-<L>-<row:02d>. The wording regexes follow RULER's templates
-(they have to match RULER's text).
+twokey  each row of ruler/niah_multikey_1_<L>.jsonl holds four keyed needles and asks one. Turn 1 is the row as
+        RULER runs it; turn 2, asked on the carried cache, names one of the three other keys in RULER's one-key
+        wording, chosen by random.Random(f"{SEED}:{sample id}").choice over them in document order. A row that
+        does not hold four distinct keys with four distinct 7-digit values, one of them the answer, under RULER's
+        question and answer prefix for it, is refused by name.
+qfirst  each row of the four RULER NIAH tasks, reordered to instruction, question, document, with " for <query>"
+        cut from the answer prefix so the keys appear only ahead of the document.
+
+Only ids, row numbers, needle ordinals and sha256 pins are committed (the manifest); the prompts are rebuilt from
+the locked rows at run time and each one is compared with its manifest entry before use. Sample ids are
+ruler2k-<L>-<row:02d> and rulerqf-<task>-<L>-<row:02d>. The patterns below quote RULER's templates, which the
+rows have to match, so they read as RULER writes them.
 """
 from __future__ import annotations
 
@@ -25,135 +26,153 @@ from . import locked as LK
 from . import text as TX
 
 SEED = 20261004
+NIAH_STEPS = 128
+SETS = ("twokey", "qfirst")
+TWOKEY_TASK = "niah_multikey_1"
+QFIRST_TASKS = ("niah_single_1", "niah_multikey_1", "niah_multivalue", "niah_multiquery")
+
+# RULER's wording
 NEEDLE = re.compile(r"One of the special magic numbers for ([^\n.:]+?) is: (\d+)\.")
 QUESTION = "What is the special magic number for {key} mentioned in the provided text?"
 PREFIX = " The special magic number for {key} mentioned in the provided text is"
 QUERY = re.compile(r"What (?:is|are all) the special magic numbers? for (.+) mentioned in the provided text\?")
 INSTRUCTION = re.compile(r"(Some|A) special magic numbers? (are|is) hidden within the following text\. Make sure to "
                          r"memorize it\. I will quiz you about the numbers? afterwards\.")
-TWOKEY_TASK = "niah_multikey_1"
-QFIRST_TASKS = ("niah_single_1", "niah_multikey_1", "niah_multivalue", "niah_multiquery")
-NIAH_STEPS = 128
-SETS = ("twokey", "qfirst")
+_SEVEN_DIGITS = re.compile(r"[0-9]{7}")
+_PINNED = ("source", "source_sha256", "row_sha256", "text_sha256", "turn1_needle", "turn2_needle")
 
 
 class DerivedRowError(ValueError):
-    """A locked row lacks the structure a derived set needs."""
+    """A locked row does not have the structure its derived set is built from."""
 
 
 class DerivedSetMismatch(SystemExit):
-    """The rebuilt prompts do not match the committed manifest."""
+    """What the locked rows give differs from the committed manifest."""
 
 
 def derived_dir():
-    env = os.environ.get("RF_DERIVED_DIR")
-    return Path(env) if env else TX.data_root() / "derived"
+    return Path(os.environ["RF_DERIVED_DIR"]) if os.environ.get("RF_DERIVED_DIR") else TX.data_root() / "derived"
 
 
 def manifest_path(which):
     return derived_dir() / f"ruler-{which}.json"
 
 
-def _sha(obj):
-    return hashlib.sha256(json.dumps(obj, ensure_ascii=False).encode()).hexdigest()
+def _digest(data: bytes):
+    return hashlib.sha256(data).hexdigest()
 
 
 def sources(which):
-    tasks = (TWOKEY_TASK,) if which == "twokey" else QFIRST_TASKS
-    return [f"ruler/{t}_{L}.jsonl" for t in tasks for L in LK.RULER_LENGTHS]
+    names = [TWOKEY_TASK] if which == "twokey" else list(QFIRST_TASKS)
+    return [f"ruler/{name}_{L}.jsonl" for name in names for L in LK.RULER_LENGTHS]
 
 
 def _task_len(rel):
-    task, L = rel[len("ruler/"):-len(".jsonl")].rsplit("_", 1)
+    stem = rel.removeprefix("ruler/").removesuffix(".jsonl")
+    task, _, L = stem.rpartition("_")
     return task, int(L)
 
 
 def sample_id(which, rel, row):
     task, L = _task_len(rel)
-    return f"ruler2k-{L}-{row:02d}" if which == "twokey" else f"rulerqf-{task}-{L}-{row:02d}"
+    if which == "twokey":
+        return f"ruler2k-{L}-{row:02d}"
+    return f"rulerqf-{task}-{L}-{row:02d}"
 
 
 def needles(text):
-    """[(key, value, char start, char end)] of RULER's numeric needles, in document order."""
-    return [(m.group(1), m.group(2), m.start(), m.end()) for m in NEEDLE.finditer(text)]
+    """(key, value, first char, end char) of each numeric needle of a RULER document, in order."""
+    return [(m[1], m[2], *m.span()) for m in NEEDLE.finditer(text)]
 
 
 def twokey(row, sid):
-    ns = needles(row["input"])
-    keys, values = [n[0] for n in ns], [n[1] for n in ns]
-    if len(ns) != 4 or len(set(keys)) != 4 or len(set(values)) != 4 or not all(re.fullmatch(r"\d{7}", v) for v in values):
-        raise DerivedRowError(f"{sid}: needs 4 needles with distinct keys and distinct 7-digit values "
-                              f"({len(ns)} needles, {len(set(keys))} keys, {len(set(values))} values)")
-    asked = [j for j, v in enumerate(values) if [v] == row["outputs"]]
-    if len(asked) != 1:
-        raise DerivedRowError(f"{sid}: outputs is not exactly one needle's value ({len(asked)} matches)")
-    t = asked[0]
-    if row["input"].rsplit("\n", 1)[-1] != QUESTION.format(key=keys[t]) or row["answer_prefix"] != PREFIX.format(key=keys[t]):
-        raise DerivedRowError(f"{sid}: question line or answer prefix is not RULER's one-key wording for the asked key")
-    u = random.Random(f"{SEED}:{sid}").choice([j for j in range(4) if j != t])
-    turns = [dict(key=keys[j], value=values[j], chars=(ns[j][2], ns[j][3])) for j in (t, u)]
-    return dict(user=row["input"], reply=row["answer_prefix"], turns=turns, turn1_needle=t, turn2_needle=u,
-                ask=dict(question=QUESTION.format(key=keys[u]), reply=PREFIX.format(key=keys[u])))
+    found = needles(row["input"])
+    keys = [f[0] for f in found]
+    vals = [f[1] for f in found]
+    shape_ok = (len(found) == 4 and len(set(keys)) == 4 and len(set(vals)) == 4
+                and all(_SEVEN_DIGITS.fullmatch(v) for v in vals))
+    if not shape_ok:
+        raise DerivedRowError(f"{sid}: expected 4 needles with 4 distinct keys and 4 distinct 7-digit values, found "
+                              f"{len(found)} needles, {len(set(keys))} keys, {len(set(vals))} values")
+    answer = [j for j, v in enumerate(vals) if row["outputs"] == [v]]
+    if len(answer) != 1:
+        raise DerivedRowError(f"{sid}: the outputs field matches {len(answer)} needle values, not exactly one")
+    first = answer[0]
+    last_line = row["input"].split("\n")[-1]
+    if last_line != QUESTION.format(key=keys[first]) or row["answer_prefix"] != PREFIX.format(key=keys[first]):
+        raise DerivedRowError(f"{sid}: the question or answer prefix is not RULER's one-key template for the answer")
+    others = [j for j in range(4) if j != first]
+    second = random.Random(f"{SEED}:{sid}").choice(others)
+    turns = [{"key": keys[j], "value": vals[j], "chars": (found[j][2], found[j][3])} for j in (first, second)]
+    follow = {"question": QUESTION.format(key=keys[second]), "reply": PREFIX.format(key=keys[second])}
+    return {"user": row["input"], "reply": row["answer_prefix"], "turns": turns, "turn1_needle": first,
+            "turn2_needle": second, "ask": follow}
 
 
 def question_first(row, sid):
-    head, _, rest = row["input"].partition("\n")
-    context, _, question = rest.rpartition("\n")
-    if not INSTRUCTION.fullmatch(head):
-        raise DerivedRowError(f"{sid}: the first line is not RULER's NIAH instruction")
+    lines = row["input"].split("\n")
+    head, question = lines[0], lines[-1]
+    context = "\n".join(lines[1:-1])
+    if len(lines) < 2 or INSTRUCTION.fullmatch(head) is None:
+        raise DerivedRowError(f"{sid}: the row does not open with RULER's NIAH instruction")
     q = QUERY.fullmatch(question)
     if q is None or not context:
-        raise DerivedRowError(f"{sid}: the last line is not RULER's NIAH question after a document")
-    tag = f" for {q.group(1)}"
-    reply = row["answer_prefix"].replace(tag, "")
-    if row["answer_prefix"].count(tag) != 1 or q.group(1) in reply:
-        raise DerivedRowError(f"{sid}: the answer prefix does not carry the question's keys exactly once")
-    return dict(user=f"{head}\n{question}\n{context}", reply=reply)
+        raise DerivedRowError(f"{sid}: the row does not close with RULER's NIAH question after the document")
+    cut = f" for {q[1]}"
+    prefix = row["answer_prefix"]
+    reply = prefix.replace(cut, "")
+    if prefix.count(cut) != 1 or q[1] in reply:
+        raise DerivedRowError(f"{sid}: the query's keys occur {prefix.count(cut)} times in the answer prefix")
+    return {"user": "\n".join((head, question, context)), "reply": reply}
 
 
 def build_one(which, row, sid):
-    return twokey(row, sid) if which == "twokey" else question_first(row, sid)
+    return (twokey if which == "twokey" else question_first)(row, sid)
 
 
 def text_sha256(which, built):
-    parts = [built["user"], built["reply"]]
+    """Pin of the text a derived sample feeds the model: sha256 of the JSON list of its pieces."""
+    pieces = [built["user"], built["reply"]]
     if which == "twokey":
-        parts += [built["ask"]["question"], built["ask"]["reply"]]
-    return _sha(parts)
+        pieces.extend((built["ask"]["question"], built["ask"]["reply"]))
+    return _digest(json.dumps(pieces, ensure_ascii=False).encode())
 
 
-def _lines(rel, root):
-    return [line for line in (root / rel).read_text().splitlines() if line.strip()]
+def _rows(root, rel):
+    """(row number, raw line, parsed row) of a locked JSONL file, blank lines skipped."""
+    lines = [ln for ln in (Path(root) / rel).read_text().splitlines() if ln.strip()]
+    return [(i, ln, json.loads(ln)) for i, ln in enumerate(lines)]
 
 
 def _frozen_sha(root):
-    return json.loads((root / "FROZEN.json").read_text())["manifest_sha256"]
+    return json.loads((Path(root) / "FROZEN.json").read_text())["manifest_sha256"]
 
 
 def _record(which, rel, sha, i, line, row, built, sid):
-    s = dict(id=sid, source=rel, source_sha256=sha, row=i, index=row.get("index"), length=_task_len(rel)[1],
-             row_sha256=hashlib.sha256(line.encode()).hexdigest(), text_sha256=text_sha256(which, built))
+    entry = {"id": sid, "source": rel, "source_sha256": sha, "row": i, "index": row.get("index"),
+             "length": _task_len(rel)[1], "row_sha256": _digest(line.encode()),
+             "text_sha256": text_sha256(which, built)}
     if which == "twokey":
-        s.update(turn1_needle=built["turn1_needle"], turn2_needle=built["turn2_needle"])
-    return s
+        entry["turn1_needle"] = built["turn1_needle"]
+        entry["turn2_needle"] = built["turn2_needle"]
+    return entry
 
 
 def build_manifest(which, root=None):
-    """The manifest of a derived set from the locked rows (no text inside)."""
+    """The committed manifest of a derived set, from the locked rows (pins only, no text)."""
     if which not in SETS:
-        raise ValueError(f"unknown derived set {which!r}: one of {SETS}")
-    root = Path(root) if root is not None else LK.locked_dir()
-    man = LK.manifest(root)
+        raise ValueError(f"derived set {which!r} is not one of {SETS}")
+    root = LK.locked_dir() if root is None else Path(root)
+    locked = LK.manifest(root)
     samples = []
-    for rel in sources(which):
-        if rel not in man:
-            continue
-        sha = LK.source(rel, man, root)
-        for i, line in enumerate(_lines(rel, root)):
-            row, sid = json.loads(line), sample_id(which, rel, i)
+    for rel in (r for r in sources(which) if r in locked):
+        sha = LK.source(rel, locked, root)
+        for i, line, row in _rows(root, rel):
+            sid = sample_id(which, rel, i)
             samples.append(_record(which, rel, sha, i, line, row, build_one(which, row, sid), sid))
-    return dict(set=f"ruler-{which}", version=1, seed=SEED, builder="ridgefill_data_b200.eval.derived",
-                locked_manifest_sha256=_frozen_sha(root), sources=sources(which), count=len(samples), samples=samples)
+    return {"set": f"ruler-{which}", "version": 1, "seed": SEED, "builder": "ridgefill_data_b200.eval.derived",
+            "locked_manifest_sha256": _frozen_sha(root), "sources": sources(which), "count": len(samples),
+            "samples": samples}
 
 
 def dumps(manifest):
@@ -161,98 +180,113 @@ def dumps(manifest):
 
 
 def token_spans(tok, text, chars, ids, base):
-    """[first, last + 1) of the tokens of `text` (encoded alone, placed at ids[base:]) overlapping each character
-    span of `chars`; refuses when that encoding is not the one in ids."""
+    """Token range [first, last + 1) covering each character span of `text`, where text encoded on its own sits
+    at ids[base:]; refused when ids do not hold that encoding there."""
     enc = tok(text, add_special_tokens=False, return_offsets_mapping=True)
-    got = list(enc["input_ids"])
-    if ids[base:base + len(got)] != got:
-        raise DerivedSetMismatch("the prompt's token ids are not the text's encoding (tokenizer offsets)")
-    out = []
-    for start, end in chars:
-        hit = [i for i, (s, e) in enumerate(enc["offset_mapping"]) if s < end and e > start]
-        if not hit:
-            raise DerivedSetMismatch("a needle maps to no token")
-        out.append((base + hit[0], base + hit[-1] + 1))
-    return out
+    own = list(enc["input_ids"])
+    if ids[base:base + len(own)] != own:
+        raise DerivedSetMismatch("the prompt does not hold the text's own encoding where the needle offsets point")
+    offsets = enc["offset_mapping"]
+    spans = []
+    for lo, hi in chars:
+        touching = [t for t, (a, b) in enumerate(offsets) if a < hi and b > lo]
+        if not touching:
+            raise DerivedSetMismatch(f"no token covers characters [{lo}, {hi})")
+        spans.append((base + touching[0], base + touching[-1] + 1))
+    return spans
 
 
 def token_span(tok, text, start, end, ids, base):
-    return token_spans(tok, text, [(start, end)], ids, base)[0]
+    (span,) = token_spans(tok, text, [(start, end)], ids, base)
+    return span
+
+
+def _load_manifest(which, root):
+    path = manifest_path(which)
+    if not path.is_file():
+        raise DerivedSetMismatch(f"missing {path}: write it with build_manifest / dumps")
+    m = json.loads(path.read_text())
+    expected = (_frozen_sha(root), SEED, sources(which))
+    if (m.get("locked_manifest_sha256"), m.get("seed"), m.get("sources")) != expected:
+        raise DerivedSetMismatch(f"{path} pins a different locked set, seed or source list")
+    return path, m
+
+
+def _twokey_fields(tok, fmt, built, ids):
+    if fmt == "chat":
+        base, body = len(TX.chat_pieces(tok)[0]), built["user"]
+    else:
+        base, body = len(TX.bos_ids(tok)), built["user"] + built["reply"]
+    plan = []
+    for t in built["turns"]:
+        lo, hi = token_span(tok, body, *t["chars"], ids, base)
+        plan.append({"key": t["key"], "value": t["value"], "needle_start": lo, "needle_end": hi})
+    head = plan[0]
+    return dict(set="multiturn", turn_plan=plan, asks=[built["ask"]], key=head["key"], value=head["value"],
+                needle_start=head["needle_start"], needle_end=head["needle_end"])
 
 
 def prompts(which, tok, fmt, man, max_len=None, tasks=None, lengths=None, max_new=None, root=None):
-    """(prompts, skipped files) of a derived set, every sample checked against its manifest."""
-    root = Path(root) if root is not None else LK.locked_dir()
-    path = manifest_path(which)
-    if not path.is_file():
-        raise DerivedSetMismatch(f"{path} does not exist (build_manifest writes it)")
-    m = json.loads(path.read_text())
-    if m.get("locked_manifest_sha256") != _frozen_sha(root) or m.get("seed") != SEED or m.get("sources") != sources(which):
-        raise DerivedSetMismatch(f"{path} was built from another locked set, seed or source list")
-    by_id = {s["id"]: s for s in m["samples"]}
+    """(prompts, skipped source files) of a derived set; every prompt is checked against the manifest first."""
+    root = LK.locked_dir() if root is None else Path(root)
+    path, m = _load_manifest(which, root)
+    pinned = {s["id"]: s for s in m["samples"]}
     tasks, lengths = LK.ruler_selection(tasks, lengths)
     caps = LK.check_max_new(max_new)
     chosen = [rel for rel in sources(which) if _task_len(rel)[0] in tasks and _task_len(rel)[1] in lengths]
-    out, skipped, seen = [], [], set()
+    out, skipped, built_ids = [], [], set()
     for rel in chosen:
         task, L = _task_len(rel)
         if max_len and L > max_len:
             skipped.append(rel)
             continue
         sha = LK.source(rel, man, root)
-        for i, line in enumerate(_lines(rel, root)):
-            row, sid = json.loads(line), sample_id(which, rel, i)
+        for i, line, row in _rows(root, rel):
+            sid = sample_id(which, rel, i)
             try:
                 built = build_one(which, row, sid)
             except DerivedRowError as e:
-                raise DerivedSetMismatch(str(e))
-            want = by_id.get(sid)
-            got = _record(which, rel, sha, i, line, row, built, sid)
+                raise DerivedSetMismatch(str(e)) from None
+            want = pinned.get(sid)
             if want is None:
-                raise DerivedSetMismatch(f"{sid} ({rel}) is not in {path}")
-            bad = [k for k in ("source", "source_sha256", "row_sha256", "text_sha256", "turn1_needle", "turn2_needle")
-                   if want.get(k) != got.get(k)]
-            if bad:
-                raise DerivedSetMismatch(f"{sid}: {', '.join(bad)} differ from {path}")
-            seen.add(sid)
+                raise DerivedSetMismatch(f"{sid} from {rel} has no entry in {path}")
+            have = _record(which, rel, sha, i, line, row, built, sid)
+            differ = [k for k in _PINNED if want.get(k) != have.get(k)]
+            if differ:
+                raise DerivedSetMismatch(f"{sid}: {', '.join(differ)} do not match {path}")
+            built_ids.add(sid)
             ids = LK.wrap(tok, fmt, built["user"], built["reply"])
             q = dict(name=sid, task=task, ruler_task="niah", length=L, source=rel, source_sha256=sha, row=i,
-                     index=row.get("index"), max_new=caps.get(task, NIAH_STEPS), format=fmt, derived=f"ruler-{which}",
-                     derived_sha256=want["text_sha256"], ids=ids)
+                     index=row.get("index"), max_new=caps.get(task, NIAH_STEPS), format=fmt,
+                     derived=f"ruler-{which}", derived_sha256=want["text_sha256"], ids=ids)
             if which == "qfirst":
                 q.update(set="ruler", metric="string_match_all", refs=row["outputs"], variant="qfirst",
                          needles=LK.needle_spans(tok, fmt, built["user"], built["reply"], ids, row["outputs"], sid))
             else:
-                if fmt == "chat":
-                    base, body = len(TX.chat_pieces(tok)[0]), built["user"]
-                else:
-                    base, body = len(TX.bos_ids(tok)), built["user"] + built["reply"]
-                plan = []
-                for t in built["turns"]:
-                    s, e = token_span(tok, body, *t["chars"], ids, base)
-                    plan.append(dict(key=t["key"], value=t["value"], needle_start=s, needle_end=e))
-                q.update(set="multiturn", turn_plan=plan, asks=[built["ask"]], key=plan[0]["key"],
-                         value=plan[0]["value"], needle_start=plan[0]["needle_start"], needle_end=plan[0]["needle_end"])
+                q.update(_twokey_fields(tok, fmt, built, ids))
             out.append(q)
-    extra = sorted(s["id"] for s in m["samples"] if s["source"] in chosen and s["source"] not in skipped
-                   and s["id"] not in seen)
-    if extra:
-        raise DerivedSetMismatch(f"{path} lists samples the locked rows do not have: {extra[:5]}")
+    live = set(chosen) - set(skipped)
+    orphans = sorted(s["id"] for s in m["samples"] if s["source"] in live and s["id"] not in built_ids)
+    if orphans:
+        raise DerivedSetMismatch(f"{path} pins samples that the locked rows no longer give: {orphans[:5]}")
     return out, skipped
 
 
 def pick_decode_docs(paths, n=20, max_len=32768, seed=SEED):
-    """Long-prompt documents for the decode study: the manifest's long-prompt files up to max_len, shuffled by
-    random.Random(seed), taken round-robin over the length bins (ascending) until n. Returns lp-<stem> names."""
-    docs = [p for p in paths if p.startswith("long-prompts/") and p.endswith(".txt")]
-    docs = [p for p in docs if LK.doc_length(p) <= max_len]
+    """n long-prompt documents for the decode study: the manifest's long-prompts/*.txt files of at most max_len
+    tokens, shuffled by random.Random(seed), then dealt round-robin from the length bins in ascending order.
+    Returns lp-<file stem> names."""
+    docs = [p for p in paths if p.startswith("long-prompts/") and p.endswith(".txt") and LK.doc_length(p) <= max_len]
     random.Random(seed).shuffle(docs)
-    bins = {L: [p for p in docs if LK.doc_length(p) == L] for L in sorted({LK.doc_length(p) for p in docs})}
+    bins = {}
+    for p in docs:
+        bins.setdefault(LK.doc_length(p), []).append(p)
+    queues = [bins[L] for L in sorted(bins)]
     picked = []
-    while len(picked) < n and any(bins.values()):
-        for L in bins:
-            if bins[L] and len(picked) < n:
-                picked.append(bins[L].pop(0))
+    while len(picked) < n and any(queues):
+        for q in queues:
+            if q and len(picked) < n:
+                picked.append(q.pop(0))
     if len(picked) < n:
-        raise ValueError(f"only {len(picked)} long-prompt documents <= {max_len} tokens, {n} wanted")
-    return ["lp-" + p.rsplit("/", 1)[-1][:-len(".txt")] for p in picked]
+        raise ValueError(f"{n} long-prompt documents of at most {max_len} tokens wanted, {len(picked)} available")
+    return ["lp-" + Path(p).stem for p in picked]
