@@ -1,12 +1,14 @@
-"""Layer-major RidgeFill prefill (code/kva/kva.py:282-460 semantics).
+"""Layer-major RidgeFill prefill (the computation of code/kva/kva.py:282-460, reordered by causality).
 
-  1. run_lower: layers < split run exactly on all N prompt rows (shared by every arm at that split);
-  2. finish: for each late layer i >= split, the prefix rows [0, P) only fill layer i's cache (from a
-     predicted input, SwiftKV's K/V, the K/V fold, ...), then the exact tail rows [P, N) run the full layer
-     over that cache (attention over all N cached rows; the GDN recurrence continues from the filled state).
-This is the engine's chunk-major computation reordered by causality. With the B200 model the fills of all
-late layers are independent of each other (each reads only h_S), so finish() batches the ridge maps of
-every late layer into one fused fill (models/b200.py: fill_batch) before the tail walks the layers.
+run_lower runs layers < split exactly over all N prompt rows; every arm at that split shares the result. finish
+then walks the late layers i >= split. At each one the prefix rows [0, P) only write layer i's cache: K/V of an
+attention layer, conv window and delta-rule state of a GDN layer, computed from a stand-in for the layer's input
+(the ridge-predicted x_i, the split input itself, SwiftKV's K/V, the K/V fold, ...). The exact tail rows [P, N)
+then run the whole layer against that cache.
+
+When every late layer's prefix fill is a plain projector or identity fill, the fills depend on h_S alone and not
+on each other. The B200 model then writes all of them in one batched, fused fill (fill_batch) before the tail
+walks the layers.
 """
 from __future__ import annotations
 
@@ -14,256 +16,350 @@ import torch
 
 from .arm import ORACLE_RESCALE, TAIL_RESCALE
 
+_EPS = 1e-30
+
 
 def context_input(b, mix, split, k):
-    """The context projector's input rows [b, c_{split-1}, .., c_{split-k}]."""
-    return torch.cat([b] + [mix[split - j].to(b.device, b.dtype) for j in range(1, k + 1)], -1)
+    """Context projector input: the split rows b followed by the mixer outputs of layers split-1, ..., split-k."""
+    cols = [b]
+    cols += [mix[split - j].to(b.device, b.dtype) for j in range(1, k + 1)]
+    return torch.cat(cols, dim=-1)
+
+
+def _keep_split(model, h, device):
+    if device is not None:
+        return h.to(device)
+    return model.stable(h) if hasattr(model, "stable") else h
 
 
 def run_lower(model, ids, splits, hs_device=None, hook=None, mix=None, tick=None, reserve=64):
-    """Exact forward up to max(splits). Returns ({split: h_split [N, H]}, cache with layers < max(splits)
-    filled). hook(i, h): every layer input; mix(i, a): every mixer output; tick(i): called before layer i with no
-    tensor (a scheduler's point to run other work between layers); reserve: cache rows kept free past the prompt
-    (decode steps append there without copying)."""
-    if isinstance(splits, int):
-        splits = [splits]
+    """Exact forward through layers < max(splits).
+
+    Returns ({split: layer-split input rows [N, H]}, a cache whose layers < max(splits) are filled). hook(i, h) sees
+    every layer input, mix(i, a) every mixer output; tick(i) runs before layer i (a scheduler's slot for other
+    work between layers); `reserve` cache rows past the prompt are preallocated so decode appends in place."""
+    wanted = {splits} if isinstance(splits, int) else set(splits)
     ids = ids.to(model.device)
-    pos = torch.arange(ids.shape[0], device=model.device)
+    n = ids.shape[0]
     if hasattr(model, "reserve"):
-        model.reserve(ids.shape[0] + reserve)
+        model.reserve(n + reserve)
+    pos = torch.arange(n, device=model.device)
     cache = model.new_cache()
+    kept = {}
     h = model.embed(ids)
-    hs = {}
-    top = max(splits)
-    stable = getattr(model, "stable", lambda t: t)
-    for i in range(top):
-        if i in splits:
-            hs[i] = stable(h) if hs_device is None else h.to(hs_device)
+    last = max(wanted)
+    for i in range(last):
+        if i in wanted:
+            kept[i] = _keep_split(model, h, hs_device)
         if hook is not None:
-            hook(i, stable(h))
+            hook(i, _keep_split(model, h, None))
         if tick is not None:
             tick(i)
         h = model.layer(i, h, pos, cache, mix=mix)
-    hs[top] = stable(h) if hs_device is None else h.to(hs_device)
-    return hs, cache
+    kept[last] = _keep_split(model, h, hs_device)
+    return kept, cache
 
 
 def late_inputs_row0(model, ids, split):
-    """Exact late-layer inputs of position 0 (it depends on itself only)."""
+    """True late-layer inputs of position 0, which attends to itself only."""
+    return oracle_layers(model, ids[:1], split)
+
+
+def oracle_layers(model, ids, first):
     got = {}
-    model.forward_exact(ids[:1], hook=lambda i, h: got.__setitem__(i, h) if i != "final" and i >= split else None)
+
+    def grab(i, h):
+        if i != "final" and i >= first:
+            got[i] = h
+    model.forward_exact(ids, hook=grab)
     return got
 
 
 def oracle_tap(store, first, rows, device="cpu"):
-    """hook(i, h) keeping rows [0, rows) of every layer input i >= first (the true late inputs)."""
-    def hook(i, h):
-        if i != "final" and i >= first:
-            store[i] = h[:rows].to(device)
-    return hook
+    """A forward hook storing rows [0, rows) of every layer input from layer `first` on (the true late inputs)."""
+    def tap(i, h):
+        if i == "final" or i < first:
+            return
+        store[i] = h[:rows].to(device)
+    return tap
 
 
 def kv_target(model, i, h):
-    """Pre-RoPE [k | v] [tokens, 2 * kv_heads * head_dim] of layer inputs h (the K/V fold's target)."""
-    r = model.reads(i, h)
-    return torch.cat((r["k"].flatten(1), r["v"].flatten(1)), 1)
+    """[k | v] before RoPE, [tokens, 2 * kv_heads * head_dim], of layer i for inputs h (the K/V fold's target)."""
+    reads = model.reads(i, h)
+    return torch.cat([reads["k"].flatten(1), reads["v"].flatten(1)], dim=1)
 
 
 def splice_kv(model, i, x, xo, part):
-    """Pre-RoPE (k, v): `part` from the true inputs xo, the other half from the filled inputs x."""
-    f, e = model.reads(i, x), model.reads(i, xo)
-    return (e["k"], f["v"]) if part == "k" else (f["k"], e["v"])
+    """(k, v) before RoPE with `part` ('k' or 'v') read from the true inputs xo and the other from the fill x."""
+    filled, true = model.reads(i, x), model.reads(i, xo)
+    out = {"k": filled["k"], "v": filled["v"]}
+    out[part] = true[part]
+    return out["k"], out["v"]
 
 
 def rescale_kv(model, i, x, mode, xo=None, scale=None):
-    """Pre-RoPE (k, v) filled from x with one half rescaled per row and KV head: knorm / vnorm to the norm of
-    the true inputs xo, kdir xo's direction at the filled norm, ktail / vtail times scale [kv_heads, 1]."""
-    f = model.reads(i, x)
-    part = mode[0]
-    a = f[part].float()
-    if scale is None:
-        t = model.reads(i, xo)[part].float()
-        na, nt = a.norm(dim=-1, keepdim=True), t.norm(dim=-1, keepdim=True)
-        a = t * (na / nt.clamp_min(1e-30)) if mode == "kdir" else a * (nt / na.clamp_min(1e-30))
+    """(k, v) before RoPE filled from x, with the half named by mode[0] rescaled per row and KV head:
+    knorm / vnorm take the norm of the true inputs' half, kdir takes the true direction at the filled norm,
+    ktail / vtail multiply by `scale` [kv_heads, 1]."""
+    filled = model.reads(i, x)
+    half = mode[0]
+    got = filled[half].float()
+    if scale is not None:
+        got = got * scale
     else:
-        a = a * scale
-    a = a.to(f[part].dtype)
-    return (a, f["v"]) if part == "k" else (f["k"], a)
+        true = model.reads(i, xo)[half].float()
+        n_fill = got.norm(dim=-1, keepdim=True)
+        n_true = true.norm(dim=-1, keepdim=True)
+        if mode == "kdir":
+            got = true * (n_fill / n_true.clamp_min(_EPS))
+        else:
+            got = got * (n_true / n_fill.clamp_min(_EPS))
+    out = {"k": filled["k"], "v": filled["v"]}
+    out[half] = got.to(filled[half].dtype)
+    return out["k"], out["v"]
 
 
 def tail_scale(model, i, h_true, x_fill, part):
-    """[kv_heads, 1]: mean over tail rows of ||true|| / ||filled|| of layer i's K or V."""
-    t = model.reads(i, h_true)[part].float().norm(dim=-1)
-    f = model.reads(i, x_fill)[part].float().norm(dim=-1)
-    return (t / f.clamp_min(1e-30)).mean(0)[:, None]
+    """[kv_heads, 1]: the tail rows' mean ratio of the true to the filled norm of layer i's K or V."""
+    true = model.reads(i, h_true)[part].float().norm(dim=-1)
+    fill = model.reads(i, x_fill)[part].float().norm(dim=-1)
+    return (true / fill.clamp_min(_EPS)).mean(0).unsqueeze(1)
 
 
-def _validate(arm, model, n, P, oracle, rows, fill_reuse, mix):
-    split, R, part, tb, rs = arm.split, arm.refresh, arm.exact_part, arm.tail_bias_from, arm.rescale
+def _problems(arm, model, n, P, oracle, rows, fill_reuse, mix):
+    """Yield a message for every option combination finish() does not define."""
+    tail = n - P
+    R, part, tb, rs = arm.refresh, arm.exact_part, arm.tail_bias_from, arm.rescale
     if arm.context and (mix is None or not arm.uses("proj") or arm.uses("swiftkv") or arm.uses("kvfold")):
-        raise ValueError("context arms fill from a projector and need the lower mixer outputs (mix)")
-    if rows is not None and (fill_reuse is not None or arm.fill == "swiftkv" or arm.uses("kvfold")
-                             or int(rows[-1]) >= P or bool((rows.diff() <= 0).any())):
-        raise ValueError("exact rows: sorted unique rows < P, no fill reuse, not swiftkv or kvfold")
-    if R is not None and (not split <= R < model.n_layers - 1 or arm.fill != "proj" or arm.fill_by_type
-                          or fill_reuse is not None or arm.f1 or arm.st
-                          or getattr(arm.refresh_projector, "split", None) != R + 1):
-        raise ValueError("refresh R: split <= R < L - 1, fill 'proj', a refresh_projector of split R + 1; no fill "
-                         "reuse, f1 or st")
+        yield "a context arm fills from a projector and needs the lower layers' mixer outputs (mix)"
+    if rows is not None:
+        ordered = bool((rows.diff() > 0).all())
+        if fill_reuse is not None or arm.fill == "swiftkv" or arm.uses("kvfold") or int(rows[-1]) >= P \
+                or not ordered:
+            yield "exact rows must be increasing prefix rows, without fill reuse, swiftkv or kvfold"
+    if R is not None:
+        ok = arm.split <= R < model.n_layers - 1 and arm.fill == "proj" and not arm.fill_by_type \
+            and fill_reuse is None and not arm.f1 and not arm.st \
+            and getattr(arm.refresh_projector, "split", None) == R + 1
+        if not ok:
+            yield (f"refresh at layer {R} needs split <= R < n_layers - 1, fill 'proj', a refresh_projector fitted "
+                   "at R + 1, and no fill reuse, f1 or st")
     if part is not None and (part not in ("k", "v") or oracle is None or rows is not None or R is not None
                              or fill_reuse is not None):
-        raise ValueError("exact_part 'k' | 'v' reads the true late inputs (oracle); no exact rows, refresh or reuse")
+        yield "exact_part ('k' or 'v') reads the true late inputs (oracle) and excludes exact rows, refresh, reuse"
     if tb is not None and (arm.context or R is not None or fill_reuse is not None):
-        raise ValueError("tail_bias_from: no context, refresh or fill reuse")
+        yield "tail_bias_from excludes context, refresh and fill reuse"
     skip = arm.tail_bias_skip_last
-    if (tb is None and skip) or (tb is not None and not 0 <= skip < n - P):
-        raise ValueError(f"tail_bias_skip_last {skip}: needs tail_bias_from and 0 <= it < the tail ({n - P})")
-    if rs is not None and (rs not in ORACLE_RESCALE + TAIL_RESCALE or arm.fill != "proj" or arm.f1
-                           or part is not None or rows is not None or R is not None or fill_reuse is not None
-                           or (rs in ORACLE_RESCALE and oracle is None) or (rs in TAIL_RESCALE and arm.context)):
-        raise ValueError("rescale knorm | kdir | vnorm (oracle) | ktail | vtail (no context): fill 'proj'; no f1, "
-                         "exact_part, exact rows, refresh or fill reuse")
+    if (skip and tb is None) or (tb is not None and not 0 <= skip < tail):
+        yield f"tail_bias_skip_last={skip} needs tail_bias_from and must lie in [0, {tail})"
+    if rs is not None:
+        allowed = rs in ORACLE_RESCALE + TAIL_RESCALE and arm.fill == "proj" and not arm.f1 and part is None \
+            and rows is None and R is None and fill_reuse is None
+        if not allowed or (rs in ORACLE_RESCALE and oracle is None) or (rs in TAIL_RESCALE and arm.context):
+            yield (f"rescale {rs!r}: one of {ORACLE_RESCALE + TAIL_RESCALE} on a 'proj' fill (the first three read "
+                   "the oracle, the tail ones take no context), without f1, exact_part, exact rows, refresh, reuse")
     rskip = arm.rescale_skip_last
-    if (rs not in TAIL_RESCALE and rskip) or (rs in TAIL_RESCALE and not 0 <= rskip < n - P):
-        raise ValueError(f"rescale_skip_last {rskip}: needs rescale ktail | vtail and 0 <= it < the tail ({n - P})")
+    if (rskip and rs not in TAIL_RESCALE) or (rs in TAIL_RESCALE and not 0 <= rskip < tail):
+        yield f"rescale_skip_last={rskip} needs a tail rescale and must lie in [0, {tail})"
 
 
 def _plain_batchable(arm, model, P, rows, fill_reuse, row0, fill_store):
-    """True when every late layer's prefix fill is a plain projector or identity fill (no per-layer
-    dependence on the tail): the B200 model then runs all fills as one batch."""
-    return (P > 0 and hasattr(model, "fill_batch") and arm.fill in ("proj", "identity") and arm.fill_by_type is None
-            and rows is None and fill_reuse is None and row0 is None and not arm.context and arm.refresh is None
-            and arm.tail_bias_from is None and arm.exact_part is None and arm.rescale is None)
+    """Every late prefix fill is a plain projector / identity fill that reads h_S only, so a model with
+    fill_batch can write them all at once."""
+    if P <= 0 or not hasattr(model, "fill_batch") or arm.fill not in ("proj", "identity"):
+        return False
+    extras = (arm.fill_by_type, rows, fill_reuse, row0, arm.refresh, arm.tail_bias_from, arm.exact_part,
+              arm.rescale)
+    return all(e is None for e in extras) and not arm.context
+
+
+class _LateLayers:
+    """finish()'s state for one arm while it walks the late layers."""
+
+    def __init__(self, model, ids, h_split, arm, oracle, rows, row_inputs, mix):
+        self.model, self.arm, self.oracle, self.row_inputs = model, arm, oracle, row_inputs
+        n = ids.shape[0]
+        self.n = n
+        self.P = P = arm.prefix_len(n)
+        self.pos = torch.arange(n, device=model.device)
+        self.h_split = h_split
+        self.b = h_split[:P]                    # prefix rows' layer-split inputs
+        self.h = h_split[P:]                    # the exact tail, advanced layer by layer
+        self.rows = rows
+        self.hr = h_split[rows] if rows is not None else None      # exact rows, advanced layer by layer
+        self.src = self.b                       # what the projector reads (context columns / refreshed rows)
+        if arm.context:
+            lower_mix = {j: mix[j][:P] for j in range(arm.split - arm.context, arm.split)}
+            self.src = context_input(self.b, lower_mix, arm.split, arm.context)
+        self.row0 = late_inputs_row0(model, ids, arm.split) if (arm.f1 and P > 0) else None
+        self.n_bias = n - P - arm.tail_bias_skip_last
+        self.n_scale = n - P - arm.rescale_skip_last
+
+    # -- stand-in inputs of one late layer
+    def projected(self, i):
+        a = self.arm
+        refreshed = a.refresh is not None and i > a.refresh
+        x = (a.refresh_projector if refreshed else a.projector)(i, self.src)
+        if a.tail_bias_from is None or i < a.tail_bias_from:
+            return x, None
+        # self.h holds the tail's layer-i inputs: the mean tail residual of the map is added to every prefix row
+        predicted = a.projector(i, self.h_split[self.P:self.n - a.tail_bias_skip_last]).float()
+        bias = (self.h[:self.n_bias].float() - predicted).mean(0).to(x.dtype)
+        return x + bias, bias
+
+    def stand_in(self, i, fill):
+        if fill == "proj":
+            return self.projected(i)
+        if fill == "identity":
+            return self.b, None
+        if fill == "oracle":
+            return self.oracle[i][:self.P].to(self.b.device), None
+        raise ValueError(f"unknown fill {fill!r}")
+
+    # -- writing layer i's prefix cache
+    def write(self, i, cache):
+        fill = self.arm.fill_of(self.model.layer_types[i])
+        handler = {"swiftkv": self._swift, "kvfold": self._kvfold, "none": self._none}.get(fill, self._computed)
+        handler(i, fill, cache)
+
+    def _swift(self, i, fill, cache):
+        self.model.swift_fill(i, self.b, self.pos[:self.P], cache)
+
+    def _kvfold(self, i, fill, cache):
+        if self.model.layer_types[i] != "attn" or self.row0 is not None:
+            raise ValueError("the K/V fold writes attention layers only (GDN layers via fill_by_type), without f1")
+        k, v = self.arm.kvfold.kv(i, self.b)
+        self.model.fill_kv(i, k, v, self.pos[:self.P], cache)
+
+    def _none(self, i, fill, cache):
+        if self.row0 is not None:
+            raise ValueError("fill 'none' cannot take f1")
+        if self.rows is None:
+            return
+        if self.row_inputs is not None:         # only the exact rows reach this layer
+            self.row_inputs[i] = self.hr
+        self.hr = self.model.layer(i, self.hr, self.pos[self.rows], cache)
+
+    def _computed(self, i, fill, cache):
+        m, a, P = self.model, self.arm, self.P
+        ppos = self.pos[:P]
+        x, bias = self.stand_in(i, fill)
+        if self.row0 is not None:
+            x = torch.cat((self.row0[i], x[1:]), 0)
+        if self.rows is not None:
+            if self.row_inputs is not None:
+                self.row_inputs[i] = self.hr
+            x = x.index_copy(0, self.rows, self.hr.to(x.dtype))
+        attn = m.layer_types[i] == "attn"
+        if i == a.refresh:
+            self.src = m.layer(i, x, ppos, cache)
+            if self.rows is not None:
+                self.hr = self.src[self.rows]
+        elif self.rows is not None:
+            self.hr = m.layer_rows(i, x, ppos, self.rows, cache)
+        elif a.exact_part is not None and attn:
+            m.fill_kv(i, *splice_kv(m, i, x, self.oracle[i][:P].to(x.device), a.exact_part), ppos, cache)
+        elif a.rescale is not None and attn:
+            m.fill_kv(i, *self._rescaled(i, x, bias), ppos, cache)
+        else:
+            m.fill(i, x, ppos, cache)
+
+    def _rescaled(self, i, x, bias):
+        a, m = self.arm, self.model
+        if a.rescale not in TAIL_RESCALE:
+            return rescale_kv(m, i, x, a.rescale, xo=self.oracle[i][:self.P].to(x.device))
+        tail_fill = a.projector(i, self.h_split[self.P:self.n - a.rescale_skip_last])
+        if bias is not None:
+            tail_fill = tail_fill + bias
+        factor = tail_scale(m, i, self.h[:self.n_scale], tail_fill, a.rescale[0])
+        return rescale_kv(m, i, x, a.rescale, scale=factor)
+
+
+def _swiftkv_native(model, h_split, arm, keep, keep_cache, cache, n):
+    if arm.split != model.swift_layers:
+        raise ValueError(f"native SwiftKV runs only at its own split ({model.swift_layers})")
+    pos = torch.arange(n, device=model.device)
+    first = n - keep
+    h = h_split[first:]
+    for i in range(arm.split, model.n_layers):
+        model.swift_fill(i, h_split, pos, cache)
+        h = model.swift_layer(i, h, pos[first:], cache)
+        if not keep_cache:
+            cache[i] = {}
+    return model.logits(h), cache, arm.prefix_len(n)
 
 
 def finish(model, ids, h_split, lower_cache, arm, keep, oracle=None, keep_cache=True, fill_store=None,
            fill_reuse=None, exact_rows=None, row_inputs=None, hook=None, mix=None, timer=None, tick=None):
-    """Layers >= arm.split for one arm. keep: number of final rows whose logits to return. Returns
-    (logits [keep, V] fp32, cache, P). tick(i): called before late layer i's tail rows run. See the module doc and
-    engine/arm.py for the options."""
+    """Layers >= arm.split for one arm; returns (logits of the last `keep` rows [keep, V] fp32, cache, P).
+
+    oracle: true late inputs (oracle fills, exact_part, oracle rescales); fill_store / fill_reuse: save or reuse
+    the prefix fills per layer; exact_rows: prefix rows recomputed exactly through the late layers over the others
+    as filled (row_inputs receives their per-layer inputs); hook(i, h): the tail's layer inputs; tick(i): runs
+    before the tail enters late layer i; timer: a stage timer around the batched fill. The arm's own options are
+    documented in engine/arm.py."""
     n = ids.shape[0]
     split = arm.split
-    P = arm.prefix_len(n)
-    pos = torch.arange(n, device=model.device)
     if hasattr(model, "reserve"):
         model.reserve(n + 64)
     h_split = h_split.to(model.device)
-    cache = [dict(c) for c in lower_cache[:split]] + [dict() for _ in range(model.n_layers - split)]
+    cache = [dict(c) for c in lower_cache[:split]]
+    cache += [{} for _ in range(split, model.n_layers)]
     if arm.fill == "swiftkv_native":
-        if split != model.swift_layers:
-            raise ValueError(f"SwiftKV native runs at its own split {model.swift_layers}")
-        q0 = n - keep
-        h = h_split[q0:]
-        for i in range(split, model.n_layers):
-            model.swift_fill(i, h_split, pos, cache)
-            h = model.swift_layer(i, h, pos[q0:], cache)
-            if not keep_cache:
-                cache[i] = {}
-        return model.logits(h), cache, P
+        return _swiftkv_native(model, h_split, arm, keep, keep_cache, cache, n)
+    P = arm.prefix_len(n)
     if keep > n - P:
-        raise ValueError(f"keep {keep} rows > exact tail {n - P}")
+        raise ValueError(f"{keep} logit rows asked from an exact tail of {n - P}")
     rows = None
-    if exact_rows is not None and len(exact_rows) > 0:
+    if exact_rows is not None and len(exact_rows):
         rows = torch.as_tensor(exact_rows, dtype=torch.long, device=model.device)
-    _validate(arm, model, n, P, oracle, rows, fill_reuse, mix)
-    b = h_split[:P]
-    h = h_split[P:]
-    bx = b
-    if arm.context:
-        bx = context_input(b, {j: mix[j][:P] for j in range(split - arm.context, split)}, split, arm.context)
-    row0 = late_inputs_row0(model, ids, split) if (arm.f1 and P > 0) else None
-    hr = h_split[rows] if rows is not None else None
-    R, part, tb, rs = arm.refresh, arm.exact_part, arm.tail_bias_from, arm.rescale
-    t_mean = n - P - arm.tail_bias_skip_last
-    t_scale = n - P - arm.rescale_skip_last
+    for problem in _problems(arm, model, n, P, oracle, rows, fill_reuse, mix):
+        raise ValueError(problem)
+    run = _LateLayers(model, ids, h_split, arm, oracle, rows, row_inputs, mix)
+    tail_pos = run.pos[P:]
 
-    batched = _plain_batchable(arm, model, P, rows, fill_reuse, row0, fill_store)
+    batched = _plain_batchable(arm, model, P, rows, fill_reuse, run.row0, fill_store)
     if batched:
         late = list(range(split, model.n_layers))
-        if timer is not None:
-            with timer.stage("fill"):
-                model.fill_batch(late, b, pos[:P], cache, arm.projector if arm.fill == "proj" else None)
+        proj = arm.projector if arm.fill == "proj" else None
+        if timer is None:
+            model.fill_batch(late, run.b, run.pos[:P], cache, proj)
         else:
-            model.fill_batch(late, b, pos[:P], cache, arm.projector if arm.fill == "proj" else None)
+            with timer.stage("fill"):
+                model.fill_batch(late, run.b, run.pos[:P], cache, proj)
 
+    stable = getattr(model, "stable", None)
     for i in range(split, model.n_layers):
-        if P > 0 and fill_reuse is not None:
-            if fill_reuse[i].get("n", P) != P:
-                raise ValueError(f"reused fill of layer {i} has {fill_reuse[i]['n']} rows, P = {P}")
-            cache[i] = dict(fill_reuse[i])
-        elif P > 0 and not batched:
-            fill = arm.fill_of(model.layer_types[i])
-            if fill == "swiftkv":
-                model.swift_fill(i, b, pos[:P], cache)
-            elif fill == "kvfold":
-                if model.layer_types[i] != "attn" or row0 is not None:
-                    raise ValueError("kvfold fills attention layers only (fill_by_type for GDN layers), without f1")
-                model.fill_kv(i, *arm.kvfold.kv(i, b), pos[:P], cache)
-            elif fill == "none":
-                if row0 is not None:
-                    raise ValueError("fill 'none' takes no f1")
-                if rows is not None:                     # only the exact rows reach layer i
-                    if row_inputs is not None:
-                        row_inputs[i] = hr
-                    hr = model.layer(i, hr, pos[rows], cache)
-            else:
-                bias = None
-                if fill == "proj":
-                    x = arm.projector(i, bx) if R is None or i <= R else arm.refresh_projector(i, bx)
-                    if tb is not None and i >= tb:       # h is the tail's layer-i input before layer i runs
-                        r = h[:t_mean].float() - arm.projector(i, h_split[P:n - arm.tail_bias_skip_last]).float()
-                        bias = r.mean(0).to(x.dtype)
-                        x = x + bias
-                elif fill == "identity":
-                    x = b
-                elif fill == "oracle":
-                    x = oracle[i][:P].to(b.device)
-                else:
-                    raise ValueError(fill)
-                if row0 is not None:
-                    x = torch.cat((row0[i], x[1:]), 0)
-                if rows is not None:
-                    if row_inputs is not None:
-                        row_inputs[i] = hr
-                    x = x.index_copy(0, rows, hr.to(x.dtype))
-                if i == R:
-                    bx = model.layer(i, x, pos[:P], cache)
-                    if rows is not None:
-                        hr = bx[rows]
-                elif rows is not None:
-                    hr = model.layer_rows(i, x, pos[:P], rows, cache)
-                elif part is not None and model.layer_types[i] == "attn":
-                    model.fill_kv(i, *splice_kv(model, i, x, oracle[i][:P].to(x.device), part), pos[:P], cache)
-                elif rs is not None and model.layer_types[i] == "attn":
-                    if rs in TAIL_RESCALE:
-                        xt = arm.projector(i, h_split[P:n - arm.rescale_skip_last])
-                        kv = rescale_kv(model, i, x, rs, scale=tail_scale(
-                            model, i, h[:t_scale], xt if bias is None else xt + bias, rs[0]))
-                    else:
-                        kv = rescale_kv(model, i, x, rs, xo=oracle[i][:P].to(x.device))
-                    model.fill_kv(i, *kv, pos[:P], cache)
-                else:
-                    model.fill(i, x, pos[:P], cache)
-        if P > 0 and fill_store is not None:
-            fill_store[i] = dict(cache[i])
-        st = arm.st.get(i) if (arm.st and P > 0) else None
-        if st is not None:
-            cache[i]["rec"] = cache[i]["rec"] + st.to(cache[i]["rec"])
+        if P > 0:
+            if fill_reuse is not None:
+                have = fill_reuse[i].get("n", P)
+                if have != P:
+                    raise ValueError(f"the reused fill of layer {i} holds {have} rows; this arm fills {P}")
+                cache[i] = dict(fill_reuse[i])
+            elif not batched:
+                run.write(i, cache)
+            if fill_store is not None:
+                fill_store[i] = dict(cache[i])
+            st = arm.st.get(i) if arm.st else None
+            if st is not None:
+                cache[i]["rec"] = cache[i]["rec"] + st.to(cache[i]["rec"])
         if hook is not None:
-            hook(i, model.stable(h) if hasattr(model, "stable") else h)
+            hook(i, stable(run.h) if stable is not None else run.h)
         if tick is not None:
             tick(i)
-        h = model.layer(i, h, pos[P:], cache)
+        run.h = model.layer(i, run.h, tail_pos, cache)
         if not keep_cache:
             cache[i] = {}
-    return model.logits(h[-keep:]), cache, P
+    return model.logits(run.h[-keep:]), cache, P
 
 
 def prefill(model, ids, arm, keep=1, **kw):
-    """run_lower + finish for one arm: (logits [keep, V], cache, P)."""
-    if arm.fill == "exact" or arm.split is None:
-        pos_keep = torch.arange(ids.shape[0] - keep, ids.shape[0], device=model.device)
-        logits, cache = model.forward_exact(ids.to(model.device), keep=pos_keep)
+    """Full prefill of one arm (run_lower, then finish): (logits [keep, V], cache, P)."""
+    if arm.split is None or arm.fill == "exact":
+        n = ids.shape[0]
+        logits, cache = model.forward_exact(ids.to(model.device),
+                                            keep=torch.arange(n - keep, n, device=model.device))
         return logits, cache, 0
     hs, lower = run_lower(model, ids, [arm.split])
     return finish(model, ids, hs[arm.split], lower, arm, keep, **kw)
