@@ -63,16 +63,25 @@ class Arm:
             return n
         return max(0, n - self.tail)
 
+    def fills(self):
+        """Every fill this arm applies to some late layer."""
+        return tuple(self.fill_by_type.values()) if self.fill_by_type else (self.fill,)
+
     def fill_of(self, layer_type):
+        """The fill of a late layer of this type ('attn' or 'gdn'; by_type specs name attention 'attention')."""
         if self.fill_by_type is None:
             return self.fill
-        return self.fill_by_type["attention" if layer_type == "attn" else layer_type]
+        key = "attention" if layer_type == "attn" else layer_type
+        if key not in self.fill_by_type:
+            raise ValueError(f"arm {self.name}: fill_by_type gives no fill for {key} layers")
+        return self.fill_by_type[key]
 
     def uses(self, fill):
-        return fill in (self.fill_by_type.values() if self.fill_by_type else (self.fill,))
+        return fill in self.fills()
 
     def uses_oracle(self):
-        return self.uses("oracle") or self.exact_part is not None or self.rescale in ORACLE_RESCALE
+        """The arm reads the true late-layer inputs (an oracle fill, exact_part or an oracle rescale)."""
+        return self.exact_part is not None or self.rescale in ORACLE_RESCALE or "oracle" in self.fills()
 
 
 def pop_split(n_layers):
@@ -82,15 +91,15 @@ def pop_split(n_layers):
 
 def rounded_tail(n, base, block):
     """Tail length when the prefix boundary is rounded down to a block multiple (tail >= base)."""
-    return n - max(0, (n - base) // block * block)
+    prefix = (n - base) // block * block if n > base else 0
+    return n - prefix
 
 
 def exclude_scored(arm, scored):
     """The arm with its tail statistics (ktail / vtail scale, tail bias) kept off the last `scored` rows."""
-    if scored <= 0:
-        return arm
-    if arm.rescale in TAIL_RESCALE and arm.rescale_skip_last < scored:
-        arm = dataclasses.replace(arm, rescale_skip_last=scored)
-    if arm.tail_bias_from is not None and arm.tail_bias_skip_last < scored:
-        arm = dataclasses.replace(arm, tail_bias_skip_last=scored)
-    return arm
+    changes = {}
+    if scored > 0 and arm.rescale in TAIL_RESCALE:
+        changes["rescale_skip_last"] = max(arm.rescale_skip_last, scored)
+    if scored > 0 and arm.tail_bias_from is not None:
+        changes["tail_bias_skip_last"] = max(arm.tail_bias_skip_last, scored)
+    return dataclasses.replace(arm, **changes) if changes else arm

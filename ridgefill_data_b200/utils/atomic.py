@@ -23,17 +23,18 @@ class AtomicWriteError(RuntimeError):
 
 
 def sha256_file(path, bufsize=1 << 20):
-    h = hashlib.sha256()
+    digest = hashlib.sha256()
     with open(path, "rb") as f:
-        while chunk := f.read(bufsize):
-            h.update(chunk)
-    return h.hexdigest()
+        for block in iter(lambda: f.read(bufsize), b""):
+            digest.update(block)
+    return digest.hexdigest()
 
 
 def write_bytes(path, data):
     path = Path(path)
-    path.parent.mkdir(parents=True, exist_ok=True)
-    fd, tmp = tempfile.mkstemp(dir=path.parent, prefix=f".{path.name}.")
+    folder = path.parent
+    folder.mkdir(parents=True, exist_ok=True)
+    fd, tmp = tempfile.mkstemp(prefix="." + path.name + ".", dir=folder)
     try:
         with os.fdopen(fd, "wb") as f:
             f.write(data)
@@ -60,7 +61,7 @@ def sidecar_line(path, digest):
 
 def write_result(path, obj):
     """JSON + sidecar, atomically; returns the sha256."""
-    data = json.dumps(obj, indent=1, sort_keys=True).encode() + b"\n"
+    data = (json.dumps(obj, sort_keys=True, indent=1) + "\n").encode()
     write_bytes(path, data)
     digest = hashlib.sha256(data).hexdigest()
     write_bytes(f"{path}.sha256", sidecar_line(path, digest).encode())
@@ -92,16 +93,17 @@ def refresh_sidecar(path):
 
 def treehash(root):
     root = Path(root)
-    h = hashlib.sha256()
+    lines = []
     for p in sorted(root.rglob("*")):
-        if p.is_file() and not p.name.startswith(".") and not p.name.endswith(".sha256"):
-            h.update(f"{p.relative_to(root).as_posix()} {sha256_file(p)}\n".encode())
-    return h.hexdigest()
+        hidden_or_sidecar = p.name.startswith(".") or p.name.endswith(".sha256")
+        if p.is_file() and not hidden_or_sidecar:
+            lines.append(f"{p.relative_to(root).as_posix()} {sha256_file(p)}\n")
+    return hashlib.sha256("".join(lines).encode()).hexdigest()
 
 
 def main(argv=None):
-    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    sub = ap.add_subparsers(dest="cmd", required=True)
+    ap = argparse.ArgumentParser(prog="ridgefill_data_b200.utils.atomic", description="atomic result files")
+    sub = ap.add_subparsers(required=True, dest="cmd")
     for name in ("treehash", "sidecar"):
         sub.add_parser(name).add_argument("path")
     sub.add_parser("check").add_argument("paths", nargs="+")
