@@ -52,32 +52,36 @@ class CharTokenizer:
     """Dry-run tokenizer without files: one id per character (code point + 10, ids below 10 reserved: 1 BOS,
     2 EOS), offsets, decode and a minimal chat template. For tiny random models only."""
     bos_token_id, eos_token_id = 1, 2
+    OFFSET = 10
 
     def __call__(self, text, add_special_tokens=True, return_offsets_mapping=False):
-        enc = _Encoding(input_ids=([1] if add_special_tokens else []) + [ord(c) + 10 for c in text])
+        ids = [self.bos_token_id] if add_special_tokens else []
+        ids.extend(ord(ch) + self.OFFSET for ch in text)
+        enc = _Encoding(input_ids=ids)
         if return_offsets_mapping:
-            enc["offset_mapping"] = [(i, i + 1) for i in range(len(text))]
+            enc["offset_mapping"] = list(zip(range(len(text)), range(1, len(text) + 1)))
         return enc
 
     def decode(self, ids, skip_special_tokens=False):
-        return "".join(chr(int(i) - 10) for i in ids if int(i) >= 10)
+        return "".join(chr(t - self.OFFSET) for t in map(int, ids) if t >= self.OFFSET)
 
     def apply_chat_template(self, msgs, tokenize=False, add_generation_prompt=True, **_):
-        return "<u>" + msgs[0]["content"] + "</u><a>"
+        return f"<u>{msgs[0]['content']}</u><a>"
 
 
 def tokenizer(model_path):
     """The model's tokenizer (transformers, local files); "char" gives the dry-run CharTokenizer."""
     if str(model_path) == "char":
         return CharTokenizer()
-    from transformers import AutoTokenizer
-    return AutoTokenizer.from_pretrained(str(model_path))
+    import transformers
+    return transformers.AutoTokenizer.from_pretrained(str(model_path))
 
 
 def bos_ids(tok):
     """[BOS] when the tokenizer's default encoding starts with one (Llama), else [] (Qwen)."""
-    ids = tok("a").input_ids
-    return ids[:1] if tok.bos_token_id is not None and ids and ids[0] == tok.bos_token_id else []
+    bos = tok.bos_token_id
+    first = tok("a").input_ids[:1]
+    return first if bos is not None and first == [bos] else []
 
 
 def encode(tok, text):
@@ -107,29 +111,38 @@ def copy_mask(ids, span=COPY_SPAN):
 
 def novel_mask(ids, scored, span=COPY_SPAN):
     """Novel-token mask of the last `scored` ids: a token is novel unless copy_mask marks it (a token-id rule)."""
-    return [not m for m in copy_mask(ids, span)[-scored:]]
+    copied = copy_mask(ids, span)[-scored:]
+    return [not c for c in copied]
 
 
 def chat_pieces(tok):
     """(user-turn open ids, assistant-turn open ids) of the model's chat template around one user message, with
     thinking off where the template has the switch."""
-    mark = "\x00DOC\x00"
-    rendered = tok.apply_chat_template([{"role": "user", "content": mark}], tokenize=False,
-                                       add_generation_prompt=True, enable_thinking=False)
-    pre, post = rendered.split(mark)
-    return encode(tok, pre), encode(tok, post)
+    return _around(tok, "\x00DOC\x00", enable_thinking=False)
+
+
+def _around(tok, mark, **options):
+    """Token ids of the chat template before and after one user message (with the assistant header)."""
+    convo = [dict(role="user", content=mark)]
+    before, after = tok.apply_chat_template(convo, tokenize=False, add_generation_prompt=True, **options).split(mark)
+    return encode(tok, before), encode(tok, after)
 
 
 def eos_ids(model_path, tok):
     """The tokenizer's EOS plus every eos_token_id of generation_config.json / config.json (text_config too)."""
-    out = {tok.eos_token_id} if tok.eos_token_id is not None else set()
-    for name in ("generation_config.json", "config.json"):
-        f = Path(model_path) / name
-        if f.exists():
-            c = json.loads(f.read_text())
-            e = c.get("eos_token_id", c.get("text_config", {}).get("eos_token_id"))
-            out |= set(e) if isinstance(e, list) else ({e} if e is not None else set())
-    return out
+    found = set()
+    if tok.eos_token_id is not None:
+        found.add(tok.eos_token_id)
+    for f in (Path(model_path) / "generation_config.json", Path(model_path) / "config.json"):
+        if not f.exists():
+            continue
+        conf = json.loads(f.read_text())
+        value = conf["eos_token_id"] if "eos_token_id" in conf else conf.get("text_config", {}).get("eos_token_id")
+        if isinstance(value, list):
+            found.update(value)
+        elif value is not None:
+            found.add(value)
+    return found
 
 
 # ----------------------------------------------------------------------------------------- graded set
@@ -222,12 +235,26 @@ def niah_needle(key, value):
 
 def _frame(tok, fmt):
     """(head ids, tail ids) around a NIAH body: raw BOS / nothing; chat the template's user and assistant opens."""
-    if fmt == "chat":
-        mark = "\x00NIAH\x00"
-        pre, post = tok.apply_chat_template([{"role": "user", "content": mark}], tokenize=False,
-                                            add_generation_prompt=True).split(mark)
-        return encode(tok, pre), encode(tok, post)
-    return bos_ids(tok), []
+    if fmt != "chat":
+        return bos_ids(tok), []
+    return _around(tok, "\x00NIAH\x00")
+
+
+def _splice(head, body, sentences):
+    """head + body with each needle sentence inserted at int(depth * len(body)) (sentences in depth order);
+    returns (ids, [start, end) of the target sentence)."""
+    ids = list(head)
+    span = (None, None)
+    cut = 0
+    for depth, sentence, target in sentences:
+        at = int(depth * len(body))
+        ids.extend(body[cut:at])
+        if target:
+            span = (len(ids), len(ids) + len(sentence))
+        ids.extend(sentence)
+        cut = at
+    ids.extend(body[cut:])
+    return ids, span
 
 
 def niah_prompts(tok, fmt="raw", variant=None, text_of=None, lengths=NIAH_LENGTHS, sources=NIAH_SOURCES):
@@ -253,20 +280,12 @@ def niah_prompts(tok, fmt="raw", variant=None, text_of=None, lengths=NIAH_LENGTH
                 placed += [(dd, kk, str(r2.randrange(1_000_000, 10_000_000)), False) for dd, kk in zip(depths, keys)]
             elif variant is not None:
                 raise ValueError(f"unknown NIAH variant {variant!r}")
-            coded = sorted(((dd, encode(tok, niah_needle(kk, vv)), tgt) for dd, kk, vv, tgt in placed),
-                           key=lambda x: x[0])
+            sentences = sorted(((dd, encode(tok, niah_needle(kk, vv)), tgt) for dd, kk, vv, tgt in placed),
+                               key=lambda x: x[0])
             q = encode(tok, niah_question(fmt, key))
-            body = hay[:L - sum(len(n) for _, n, _ in coded) - len(q)]
-            ids, prev = list(head), 0
-            start = end = None
-            for dd, n, tgt in coded:
-                at = int(dd * len(body))
-                ids += body[prev:at]
-                if tgt:
-                    start, end = len(ids), len(ids) + len(n)
-                ids += n
-                prev = at
-            ids += body[prev:] + q + tail
+            body = hay[:L - sum(len(n) for _, n, _ in sentences) - len(q)]
+            ids, (start, end) = _splice(head, body, sentences)
+            ids += q + tail
             rec = dict(name=name, length=L, source=src, depth=d, key=key, value=value, format=fmt,
                        char_start=c["char_start"], char_end=c["char_end"], needle_start=start, needle_end=end, ids=ids)
             if variant:
@@ -276,11 +295,15 @@ def niah_prompts(tok, fmt="raw", variant=None, text_of=None, lengths=NIAH_LENGTH
     return out
 
 
+_THINK = re.compile(r"<think>.*?(</think>|$)", re.S)
+_SEVEN = re.compile(r"(?<!\d)\d{7}(?!\d)")
+
+
 def niah_correct(text, value):
     """The first standalone 7-digit number, after dropping any think block, equals the value."""
-    text = re.sub(r"<think>.*?(</think>|$)", "", text, flags=re.S)
-    m = re.search(r"(?<!\d)\d{7}(?!\d)", text)
-    return bool(m and m.group(0) == value)
+    visible = _THINK.sub("", text)
+    found = _SEVEN.search(visible)
+    return found is not None and found.group(0) == value
 
 
 # ---------------------------------------------------------------------------------- calibration sets
@@ -289,7 +312,7 @@ HELD_EXCLUDE_SHA256 = {"84f57b5fa277a7ed4af11992762af87605d6b02b1d71b0589743ac4a
 
 
 def name_sha256(name):
-    return hashlib.sha256(name.encode()).hexdigest()
+    return hashlib.sha256(name.encode("utf-8")).hexdigest()
 
 
 def calib_exclude(which, path=None):
@@ -317,8 +340,10 @@ def calib_docs(which):
 
 def calib_ids(tok, which, limit=None):
     bos = bos_ids(tok)
-    docs = calib_docs(which)[:limit] if limit else calib_docs(which)
-    return [dict(name=d["name"], ids=cap(bos + encode(tok, d["text"]), bos)) for d in docs]
+    docs = calib_docs(which)
+    if limit:
+        docs = docs[:limit]
+    return [{"name": d["name"], "ids": cap(bos + encode(tok, d["text"]), bos)} for d in docs]
 
 
 GRAM = 50
@@ -339,10 +364,10 @@ def adapt_docs(tok, slices, eval_prompts):
     docs, dropped = [], []
     for src, spans in slices.items():
         for s, e in spans:
-            ids = bos + encode(tok, text_of[src][s:e])
             name = f"adapt-{src}-{s}"
-            if grams(ids) & taken:
-                dropped.append(name)
+            doc_ids = bos + encode(tok, text_of[src][s:e])
+            if taken.isdisjoint(grams(doc_ids)):
+                docs.append({"name": name, "source": f"corpus/{src}.txt[{s}:{e}]", "ids": doc_ids})
             else:
-                docs.append(dict(name=name, source=f"corpus/{src}.txt[{s}:{e}]", ids=ids))
+                dropped.append(name)
     return docs, dropped
