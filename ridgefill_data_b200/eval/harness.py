@@ -266,6 +266,96 @@ def gen_budget(set_name, q, steps_dec, turns):
 
 
 # ---------------------------------------------------------------------------------------------- runner
+class _Signals:
+    """One prompt's exact lower layers, shared by every arm, and the selection signals read from them (each
+    computed once, on first use): window attention mass, predicted surprisal, key diversity, fill deviation and
+    the attention a row receives from later prefix rows."""
+
+    def __init__(self, h, ids, todo, refs, known):
+        self.m, self.files = h.m, h.files
+        m = h.m
+        n = ids.shape[0]
+        self.ids = ids
+        every = todo + refs
+        selects = [b.meta["select"] for b in every if b.meta.get("select")]
+        self.oracle, self.tap = None, None
+        readers = [a for a in todo if a.uses_oracle()]
+        if readers:
+            self.oracle = {}
+            self.tap = oracle_tap(self.oracle, min(a.split for a in readers), max(a.prefix_len(n) for a in readers))
+        ends = {known} | {b.prefix_len(n) for b in every if b.meta.get("select")
+                          and "qattn" in SEL.signals(b.meta["select"]) and b.meta["select"].get("window") == "prefix"}
+        self.windows = {e: {} for e in ends}
+        self.want_windows = any("qattn" in SEL.signals(s) for s in selects)
+        self.recv_P = sorted({b.prefix_len(n) for b in every if b.meta.get("select")
+                              and "qfp" in SEL.signals(b.meta["select"])})
+        self.recv = {}
+        self.qfp_stride = int(h.cfg.get("qfp_stride", 1))
+        self.pos = torch.arange(n, device=m.device)
+        self.mixes = {}
+        mix_layers = {a.split - k for a in todo for k in range(1, a.context + 1)}
+
+        def keep_mix(i, x):
+            if i in mix_layers:
+                self.mixes[i] = x
+        splits = {a.split for a in every if a.split is not None} or {h.exact_split}
+        hooked = self.tap is not None or self.want_windows or bool(self.recv_P)
+        self.hs, self.lower = run_lower(m, ids, splits, hook=self._lower_hook if hooked else None,
+                                        mix=keep_mix if mix_layers else None)
+        self.cached = {}
+        self.emb = None
+
+    def _lower_hook(self, i, h):
+        m = self.m
+        if self.tap is not None:
+            self.tap(i, h)
+        if self.want_windows:
+            for end, rows in self.windows.items():
+                rows[i] = h[max(0, end - SEL.WINDOW):end].clone()
+        if self.recv_P and isinstance(i, int) and m.layer_types[i] == "attn":
+            from ..engine import impact as IM
+            x = m.in_norm(h, m.W[i]["ln1"])
+            q, k = m.queries(i, x, self.pos), IM.attn_kv(m, i, x, self.pos)[0]
+            for P_ in self.recv_P:
+                self.recv[P_, i] = IM.received_mass(q, k, m.scale, rows_below=P_, stride=self.qfp_stride)[1]
+
+    def _once(self, key, make):
+        if key not in self.cached:
+            self.cached[key] = make()
+        return self.cached[key]
+
+    def mass(self, split, layers, end):
+        used = tuple(SEL.qattn_layers(self.m, split, layers))
+        return self._once(("mass", used, end),
+                          lambda: SEL.window_mass(self.m, self.windows[end], self.lower, used, end))
+
+    def pred(self, split, path, P):
+        from ..engine.pred import prefix_scores
+        if self.emb is None:
+            self.emb = self.m.embed(self.ids.to(self.m.device))
+        return self._once(("pred", split, path, P),
+                          lambda: prefix_scores(self.files.predictor(path), self.hs[split], self.emb, P))
+
+    def keydiff(self, split, layers, P):
+        used = tuple(SEL.qattn_layers(self.m, split, layers))
+        return self._once(("keydiff", used, P), lambda: SEL.key_diff(self.lower, used, P))
+
+    def deviation(self, a, P):
+        path = a.meta["select"].get("projector")
+        proj = self.files.projector(path) if path else a.projector
+        return self._once(("deviation", id(proj), a.split, P),
+                          lambda: SEL.fill_deviation(self.m, proj, self.hs[a.split], a.split, P))
+
+    def received(self, split, P_):
+        below = sum(v for (pp, i), v in self.recv.items() if pp == P_ and i < split)
+        return SEL.per_later_token(below, P_)
+
+    def release_below(self, top):
+        """Drop the lower-layer caches from layer `top` up once no remaining arm reads them."""
+        for i in range(top, len(self.lower)):
+            self.lower[i] = {}
+
+
 class Harness:
     def __init__(self, model, tok, cfg, set_name, out_dir, files=None, eos=(), log=print):
         if set_name not in SETS:
@@ -371,143 +461,89 @@ class Harness:
         write_json(path, rec)
 
     @torch.no_grad()
+    def _plan(self, p, rec, n, keep, scored):
+        """The arms still to run on this prompt (exact first where others need it) and the matched arms their
+        controls read."""
+        exact = Arm("exact", split=self.exact_split)
+        todo = [exact] + sorted(self.arms, key=lambda x: -(x.split or 0))
+        todo = [a for a in todo if not (a.name in rec["runs"] and _complete(rec["runs"][a.name], self.set))]
+        todo = [exclude_scored(dataclasses.replace(a, tail=keep) if a.tail_from else a, scored) for a in todo]
+        needs_exact = self.set == "decode" or any(a.uses_oracle() for a in todo)
+        if todo and needs_exact and todo[0].name != "exact":
+            todo.insert(0, exact)
+        refs = [self.by_name[a.meta["select"]["match"]] for a in todo if "match" in a.meta.get("select", {})]
+        return todo, refs
+
     def run_prompt(self, p, rec):
-        m, tok = self.m, self.tok
+        m = self.m
         if self.set == "multiturn":
             from . import multiturn as MT
-            return MT.run_prompt(m, tok, p, self.arms, rec, self.fmt, self.eos, p.get("max_new", NIAH_STEPS),
+            return MT.run_prompt(m, self.tok, p, self.arms, rec, self.fmt, self.eos, p.get("max_new", NIAH_STEPS),
                                  self.digit_set, self.turns)
         ids = torch.tensor(list(p["ids"]))
         n = ids.shape[0]
-        keep = KEEP if self.set == "grade" else p["cont_len"] + 1 if self.set == "longppl" else 1
+        if self.set == "grade":
+            keep = KEEP
+        elif self.set == "longppl":
+            keep = p["cont_len"] + 1
+        else:
+            keep = 1
         scored = keep - 1 if self.set in ("grade", "longppl") else 0
-        known = n - scored
-        todo = [Arm("exact", split=self.exact_split)] + sorted(self.arms, key=lambda x: -(x.split or 0))
-        todo = [a for a in todo if not (a.name in rec["runs"] and _complete(rec["runs"][a.name], self.set))]
-        todo = [dataclasses.replace(a, tail=keep) if a.tail_from else a for a in todo]
-        todo = [exclude_scored(a, scored) for a in todo]
-        if self.set == "decode" and todo and todo[0].name != "exact":
-            todo.insert(0, Arm("exact", split=self.exact_split))
-        refs = [self.by_name[a.meta["select"]["match"]] for a in todo if "match" in a.meta.get("select", {})]
-        oracle, tap = None, None
-        if any(a.uses_oracle() for a in todo):
-            if todo[0].name != "exact":
-                todo.insert(0, Arm("exact", split=self.exact_split))
-            oracle = {}
-            tap = oracle_tap(oracle, min(a.split for a in todo if a.uses_oracle()),
-                             max(a.prefix_len(n) for a in todo if a.uses_oracle()))
-        need = sorted({a.split for a in todo + refs if a.split is not None})
-        ends = {known}
-        for b in todo + refs:
-            sel = b.meta.get("select", {})
-            if sel and "qattn" in SEL.signals(sel) and sel.get("window") == "prefix":
-                ends.add(b.prefix_len(n))
-        wins = {e: {} for e in ends}
-        want_win = any("qattn" in SEL.signals(b.meta["select"]) for b in todo + refs if b.meta.get("select"))
-        recv_P = sorted({b.prefix_len(n) for b in todo + refs if b.meta.get("select")
-                         and "qfp" in SEL.signals(b.meta["select"])})
-        recv = {}
-        pos_all = torch.arange(n, device=m.device)
-
-        def lower_hook(i, h):
-            if tap is not None:
-                tap(i, h)
-            if want_win:
-                for end, win in wins.items():
-                    win[i] = h[max(0, end - SEL.WINDOW):end].clone()
-            if recv_P and isinstance(i, int) and m.layer_types[i] == "attn":
-                from ..engine import impact as IM
-                x = m.in_norm(h, m.W[i]["ln1"])
-                q, k = m.queries(i, x, pos_all), IM.attn_kv(m, i, x, pos_all)[0]
-                for P_ in recv_P:
-                    recv[(P_, i)] = IM.received_mass(q, k, m.scale, rows_below=P_,
-                                                     stride=int(self.cfg.get("qfp_stride", 1)))[1]
-        mixes = {}
-        mix_layers = {a.split - k for a in todo for k in range(1, a.context + 1)}
-        hs, lower = run_lower(m, ids, set(need) if need else {self.exact_split},
-                              hook=lower_hook if (tap is not None or want_win or recv_P) else None,
-                              mix=(lambda i, x: mixes.__setitem__(i, x) if i in mix_layers else None)
-                              if mix_layers else None)
-        masses, scores, emb = {}, {}, []
-
-        def mass_of(split, layers, end):
-            key = (tuple(SEL.qattn_layers(m, split, layers)), end)
-            if key not in masses:
-                masses[key] = SEL.window_mass(m, wins[end], lower, key[0], end)
-            return masses[key]
-
-        def pred_of(split, path, P):
-            from ..engine.pred import prefix_scores
-            if not emb:
-                emb.append(m.embed(ids.to(m.device)))
-            if (split, path, P) not in scores:
-                scores[split, path, P] = prefix_scores(self.files.predictor(path), hs[split], emb[0], P)
-            return scores[split, path, P]
-
-        def keys_of(split, layers, P):
-            key = ("keydiff", tuple(SEL.qattn_layers(m, split, layers)), P)
-            if key not in scores:
-                scores[key] = SEL.key_diff(lower, key[1], P)
-            return scores[key]
-
-        def dev_of(a, P):
-            q = a.meta["select"].get("projector")
-            proj = self.files.projector(q) if q else a.projector
-            key = ("deviation", id(proj), a.split, P)
-            if key not in scores:
-                scores[key] = SEL.fill_deviation(m, proj, hs[a.split], a.split, P)
-            return scores[key]
-
-        def recv_of(split, P_):
-            low = sum(v for (pp, i), v in recv.items() if pp == P_ and i < split)
-            return SEL.per_later_token(low, P_)
-        picks = SEL.choose(todo + refs, n, list(p["ids"]), p["name"], self.digit_set, mass_of, pred_of, keys_of,
-                           dev_of, self.files.freq.get, self.breaks, recv_of, self.tbytes, known=known)
-        fills, ref_dec = {}, None
+        todo, refs = self._plan(p, rec, n, keep, scored)
+        sig = _Signals(self, ids, todo, refs, known=n - scored)
+        picks = SEL.choose(todo + refs, n, list(p["ids"]), p["name"], self.digit_set, sig.mass, sig.pred,
+                           sig.keydiff, sig.deviation, self.files.freq.get, self.breaks, sig.received, self.tbytes,
+                           known=n - scored)
+        saved_fills, ref_dec = {}, None
         for j, a in enumerate(todo):
-            t1 = time.time()
-            if m.device.type == "cuda":
+            later = todo[j + 1:]
+            started = time.time()
+            on_gpu = m.device.type == "cuda"
+            if on_gpu:
                 torch.cuda.reset_peak_memory_stats()
-            store = {} if any(b.meta.get("reuse_fill") == a.name for b in todo[j + 1:]) else None
-            reuse = fills.pop(a.meta.get("reuse_fill"), None)
             pick = picks.get(a.name)
-            run_arm = dataclasses.replace(a, tail=a.tail + pick["extra_tail"]) if pick else a
-            if a.meta.get("tail_round"):
-                tr = a.meta["tail_round"]
-                run_arm = dataclasses.replace(run_arm, tail=rounded_tail(n, tr["base"], tr["block"]))
-            logits, cache, P = finish(m, ids, hs[a.split], lower, run_arm, keep, keep_cache=keep == 1,
-                                      fill_store=store, fill_reuse=reuse, oracle=oracle,
-                                      exact_rows=pick["rows"] if pick else None,
-                                      hook=tap if a.name == "exact" else None, mix=mixes or None)
+            arm = a if not pick else dataclasses.replace(a, tail=a.tail + pick["extra_tail"])
+            rounding = a.meta.get("tail_round")
+            if rounding:
+                arm = dataclasses.replace(arm, tail=rounded_tail(n, rounding["base"], rounding["block"]))
+            store = {} if any(b.meta.get("reuse_fill") == a.name for b in later) else None
+            logits, cache, P = finish(m, ids, sig.hs[a.split], sig.lower, arm, keep, keep_cache=keep == 1,
+                                      fill_store=store, fill_reuse=saved_fills.pop(a.meta.get("reuse_fill"), None),
+                                      oracle=sig.oracle, exact_rows=pick["rows"] if pick else None,
+                                      hook=sig.tap if a.name == "exact" else None, mix=sig.mixes or None)
             check_finite(logits, f"{p['name']} {a.name}")
             if store is not None:
-                fills[a.name] = store
+                saved_fills[a.name] = store
             run = self._run_fields(a, P, n, pick, p)
             self._score(run, a, p, ids, n, keep, logits, cache, P, rec, ref_dec)
             if self.set == "decode" and a.name == "exact":
                 ref_dec = run.pop("_ref")
-            run["wall_s"] = round(time.time() - t1, 3)
-            if m.device.type == "cuda":
-                run["mem_gib"] = dict(alloc_peak=round(torch.cuda.max_memory_allocated() / 2**30, 2),
-                                      reserved_peak=round(torch.cuda.max_memory_reserved() / 2**30, 2))
+            run["wall_s"] = round(time.time() - started, 3)
+            if on_gpu:
+                gib = 2 ** 30
+                run["mem_gib"] = {"alloc_peak": round(torch.cuda.max_memory_allocated() / gib, 2),
+                                  "reserved_peak": round(torch.cuda.max_memory_reserved() / gib, 2)}
             rec["runs"][a.name] = run
             del logits, cache
-            rest = {b.split for b in todo[j + 1:]}
-            top = max(rest) if rest else 0
-            for i in range(top, len(lower)):
-                lower[i] = {}
+            sig.release_below(max((b.split for b in later), default=0))
+        self._extra_references(p, rec)
+        return self._summary(rec)
+
+    def _extra_references(self, p, rec):
+        """The tail-only key-token reference and the graded set's short-context reference, once per record."""
+        m = self.m
         if self.key_tail is not None and rec.get("tail_only", {}).get("T") != self.key_tail:
             from .keytok import exact_tail_only
-            sc = KEEP - 1 if self.set == "grade" else p["cont_len"]
+            n_scored = KEEP - 1 if self.set == "grade" else p["cont_len"]
             bos = self._bos_of(p["ids"])
-            rec["tail_only"] = dict(T=self.key_tail, bos=bos, logprobs=[
-                round(float(x), 6) for x in exact_tail_only(m, list(p["ids"]), self.key_tail, bos, sc)])
+            lps = exact_tail_only(m, list(p["ids"]), self.key_tail, bos, n_scored)
+            rec["tail_only"] = {"T": self.key_tail, "bos": bos, "logprobs": [round(float(x), 6) for x in lps]}
         if self.set == "grade" and "short" not in rec and "short_ids" in p:
-            s = torch.tensor(p["short_ids"])
-            lg, _ = m.forward_exact(s.to(m.device), keep=torch.arange(s.shape[0] - KEEP, s.shape[0], device=m.device))
-            rec["short"] = dict(n=s.shape[0], tail_match=p.get("short_tail_match"),
-                                logprobs=[round(float(x), 6) for x in score_tokens(lg, s, KEEP - 1)])
-        return self._summary(rec)
+            short = torch.tensor(p["short_ids"])
+            rows = torch.arange(short.shape[0] - KEEP, short.shape[0], device=m.device)
+            logits, _ = m.forward_exact(short.to(m.device), keep=rows)
+            rec["short"] = {"n": short.shape[0], "tail_match": p.get("short_tail_match"),
+                            "logprobs": [round(float(x), 6) for x in score_tokens(logits, short, KEEP - 1)]}
 
     def _run_fields(self, a, P, n, pick, p):
         run = dict(P=P, split=a.split, tail=n - P, fill=a.fill, st=bool(a.st), f1=a.f1)
