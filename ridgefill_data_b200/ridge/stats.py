@@ -96,43 +96,56 @@ class RidgeStats:
             self.add_layer(i, ys[i])
 
     def state(self):
-        cpu = lambda t: t.detach().cpu()  # noqa: E731
-        return dict(split=self.split, layers=self.layers, dim=self.dim, n=self.n, cx=cpu(self.cx).double(),
-                    cy={i: cpu(v).double() for i, v in self.cy.items()}, sx=cpu(self.sx), sxx=cpu(self.sxx),
-                    sy={i: cpu(v) for i, v in self.sy.items()}, sxy={i: cpu(v) for i, v in self.sxy.items()})
+        """The accumulators as a host dict (shifts in fp64): split, layers, dim, n, cx, cy, sx, sxx, sy, sxy."""
+        def host(t):
+            return t.detach().cpu()
+
+        out = {"split": self.split, "layers": self.layers, "dim": self.dim, "n": self.n,
+               "cx": host(self.cx).double(), "sx": host(self.sx), "sxx": host(self.sxx)}
+        out["cy"] = {i: host(v).double() for i, v in self.cy.items()}
+        out["sy"] = {i: host(self.sy[i]) for i in self.sy}
+        out["sxy"] = {i: host(self.sxy[i]) for i in self.sxy}
+        return out
 
 
 def residual(state):
-    """Statistics of the target y - x (ridge towards the identity map): shifts cy - cx, sums sy - sx,
+    """Statistics of the target y - x (a ridge towards the identity map): shifts cy - cx, sums sy - sx and
     sxy - sxx (code/kva/ridge.py:134-139)."""
-    sx, sxx = state["sx"].double(), state["sxx"].double()
-    return dict(state, sx=sx, sxx=sxx, cy={i: state["cy"][i] - state["cx"] for i in state["layers"]},
-                sy={i: state["sy"][i].double() - sx for i in state["layers"]},
-                sxy={i: state["sxy"][i].double() - sxx for i in state["layers"]})
+    sx = state["sx"].double()
+    sxx = state["sxx"].double()
+    res = dict(state, sx=sx, sxx=sxx)
+    res["cy"] = {i: state["cy"][i] - state["cx"] for i in state["layers"]}
+    res["sy"] = {i: state["sy"][i].double() - sx for i in state["layers"]}
+    res["sxy"] = {i: state["sxy"][i].double() - sxx for i in state["layers"]}
+    return res
+
+
+def _moved(s, s2, n, d_row, d_col, s_col=None):
+    """A cross sum about shifted centres: the sum of (x + d_row)(y + d_col)^T given s2 = sum x y^T, s = sum x,
+    s_col = sum y (defaults to s) and the row count n."""
+    s_col = s if s_col is None else s_col
+    return s2 + torch.outer(s, d_col) + torch.outer(d_row, s_col) + n * torch.outer(d_row, d_col)
 
 
 def combine(a, b, w=1.0):
-    """Statistics of a's rows plus w times b's rows, b re-expressed about a's shifts
-    (code/kva/ridge.py:142-156). Both are state() dicts over the same split and layers."""
-    d = b["cx"] - a["cx"]
-    out = dict(a, n=a["n"] + w * b["n"])
-    sxb = b["sx"] + b["n"] * d
-    out["sx"] = a["sx"] + w * sxb
-    out["sxx"] = a["sxx"] + w * (b["sxx"] + torch.outer(b["sx"], d) + torch.outer(d, b["sx"])
-                                 + b["n"] * torch.outer(d, d))
+    """Statistics of a's rows plus w times b's rows, with b moved onto a's shifts (Chan et al.'s pairwise update;
+    code/kva/ridge.py:142-156). Both are state() dicts over the same split and layers."""
+    nb = b["n"]
+    dx = b["cx"] - a["cx"]
+    out = dict(a, n=a["n"] + w * nb)
+    out["sx"] = a["sx"] + w * (b["sx"] + nb * dx)
+    out["sxx"] = a["sxx"] + w * _moved(b["sx"], b["sxx"], nb, dx, dx)
     out["sy"], out["sxy"] = {}, {}
     for i in a["layers"]:
-        e = b["cy"][i] - a["cy"][i]
-        out["sy"][i] = a["sy"][i] + w * (b["sy"][i] + b["n"] * e)
-        out["sxy"][i] = a["sxy"][i] + w * (b["sxy"][i] + torch.outer(b["sx"], e) + torch.outer(d, b["sy"][i])
-                                           + b["n"] * torch.outer(d, e))
+        dy = b["cy"][i] - a["cy"][i]
+        out["sy"][i] = a["sy"][i] + w * (b["sy"][i] + nb * dy)
+        out["sxy"][i] = a["sxy"][i] + w * _moved(b["sx"], b["sxy"][i], nb, dx, dy, s_col=b["sy"][i])
     return out
 
 
 def raw_moments(state, i):
-    """Uncentred sum(x x^T) and sum(x y_i^T) (fp64) reconstructed from the shifted sums."""
+    """Uncentred sum(x x^T) and sum(x y_i^T) (fp64) rebuilt from the shifted sums."""
     n, cx, sx = state["n"], state["cx"].double(), state["sx"].double()
-    cy, sy = state["cy"][i].double(), state["sy"][i].double()
-    xx = state["sxx"].double() + torch.outer(sx, cx) + torch.outer(cx, sx) + n * torch.outer(cx, cx)
-    xy = state["sxy"][i].double() + torch.outer(sx, cy) + torch.outer(cx, sy) + n * torch.outer(cx, cy)
+    xx = _moved(sx, state["sxx"].double(), n, cx, cx)
+    xy = _moved(sx, state["sxy"][i].double(), n, cx, state["cy"][i].double(), s_col=state["sy"][i].double())
     return xx, xy
