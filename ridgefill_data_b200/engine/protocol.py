@@ -324,7 +324,7 @@ def validate(cfg, p=None, ledger_path=None, archive=None, env=os.environ, set_na
         known = registered(ledger_path or protocol_file().parent / cur["ledger"])
         unknown = sorted(set(regs) - known)
         if unknown:
-            errors.append(f"registrations missing from the ledger: {unknown}")
+            errors.append(f"registrations not in the ledger: {unknown}")
     else:
         errors.append("no 'registration' given: list the ledger hypotheses this run serves")
     errors += frozen_gate(regs, cur)
@@ -338,7 +338,7 @@ def validate(cfg, p=None, ledger_path=None, archive=None, env=os.environ, set_na
            if cfg.get("drop_bos") or model not in p["models"] or not _row_in_config(a, by_name, model, p)]
     reason = str(cfg.get("exploratory", "")).strip()
     if off and not reason:
-        errors.append(f"arms {off} are not protocol rows: fix them or give an 'exploratory' reason")
+        errors.append(f"arms {off} lie outside the protocol: fix them or give an 'exploratory' reason")
     if errors:
         raise ProtocolError("protocol check failed:\n  - " + "\n  - ".join(errors))
     return {"version": p["version"], "sha256": p["sha256"], "registration": list(regs),
