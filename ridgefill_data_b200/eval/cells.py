@@ -25,41 +25,58 @@ class SchemaError(RuntimeError):
     """The schema uses a keyword this validator does not implement."""
 
 
+def _type_ok(t, value, where):
+    if t not in PY_TYPES:
+        raise SchemaError(f"unknown type {t!r} at {where}")
+    numeric_bool = t in ("integer", "number") and isinstance(value, bool)
+    return isinstance(value, PY_TYPES[t]) and not numeric_bool
+
+
+def _object_errors(schema, value, where):
+    props = schema.get("properties", {})
+    out = [f"{where}: missing required field {k!r}" for k in schema.get("required", []) if k not in value]
+    unknown = [k for k in value if k not in props]
+    if unknown and schema.get("additionalProperties") is False:
+        out.append(f"{where}: unknown field(s) {unknown}")
+    for k, v in value.items():
+        if k in props:
+            out.extend(validate(props[k], v, f"{where}.{k}"))
+    return out
+
+
+def _array_errors(schema, value, where):
+    out = []
+    least = schema.get("minItems", 0)
+    if len(value) < least:
+        out.append(f"{where}: needs >= {least} items, has {len(value)}")
+    if schema.get("uniqueItems"):
+        canon = [json.dumps(v, sort_keys=True) for v in value]
+        if len(set(canon)) != len(canon):
+            out.append(f"{where}: duplicate items")
+    if "items" in schema:
+        for j, v in enumerate(value):
+            out.extend(validate(schema["items"], v, f"{where}[{j}]"))
+    return out
+
+
 def validate(schema, value, where="$"):
-    """Every problem of value against schema (empty list: valid)."""
-    unknown = [k for k in schema if k not in META and k not in KEYWORDS]
-    if unknown:
-        raise SchemaError(f"schema keyword(s) {unknown} at {where} are not implemented")
+    """Every problem of value against schema (an empty list: valid)."""
+    unsupported = [k for k in schema if k not in META | KEYWORDS]
+    if unsupported:
+        raise SchemaError(f"schema keyword(s) {unsupported} at {where} are not implemented")
+    if "type" in schema and not _type_ok(schema["type"], value, where):
+        return [f"{where}: expected {schema['type']}, got {type(value).__name__}"]
     errs = []
-    t = schema.get("type")
-    if t is not None:
-        if t not in PY_TYPES:
-            raise SchemaError(f"unknown type {t!r} at {where}")
-        if not isinstance(value, PY_TYPES[t]) or (t in ("integer", "number") and isinstance(value, bool)):
-            return [f"{where}: expected {t}, got {type(value).__name__}"]
     if "enum" in schema and value not in schema["enum"]:
         errs.append(f"{where}: {value!r} not in {schema['enum']}")
     if "const" in schema and value != schema["const"]:
         errs.append(f"{where}: must be {schema['const']!r}, got {value!r}")
-    if isinstance(value, str) and "pattern" in schema and not re.match(schema["pattern"], value):
+    if "pattern" in schema and isinstance(value, str) and re.match(schema["pattern"], value) is None:
         errs.append(f"{where}: {value!r} does not match {schema['pattern']!r}")
     if isinstance(value, dict):
-        props = schema.get("properties", {})
-        errs += [f"{where}: missing required field {k!r}" for k in schema.get("required", []) if k not in value]
-        extra = [k for k in value if k not in props]
-        if schema.get("additionalProperties") is False and extra:
-            errs.append(f"{where}: unknown field(s) {extra}")
-        for k, v in value.items():
-            if k in props:
-                errs += validate(props[k], v, f"{where}.{k}")
+        errs += _object_errors(schema, value, where)
     if isinstance(value, list):
-        if len(value) < schema.get("minItems", 0):
-            errs.append(f"{where}: needs >= {schema['minItems']} items, has {len(value)}")
-        if schema.get("uniqueItems") and len({json.dumps(v, sort_keys=True) for v in value}) != len(value):
-            errs.append(f"{where}: duplicate items")
-        if "items" in schema:
-            for j, v in enumerate(value):
-                errs += validate(schema["items"], v, f"{where}[{j}]")
+        errs += _array_errors(schema, value, where)
     return errs
 
 
@@ -74,73 +91,111 @@ SET_BLOCKS = {"longppl": ("keytoken",), "decode": ("decode",), "multiturn": ("se
 
 
 def _uses_maps(arm):
-    return arm.startswith("ridgefill") or arm == "kvexact"
+    return arm == "kvexact" or arm.startswith("ridgefill")
+
+
+def _flashnext(cell):
+    missing = [k for k in ENGINE_ONLY if k not in cell]
+    missing += [k for k in ("ttft_min_speedup", "ttft_length") if k not in cell.get("margins", {})]
+    if missing or "runs" in cell or cell.get("split") != "-":
+        return [f"flashnext_cell: needs {missing or 'split -'} and no runs (it runs on the engine's own driver)"]
+    return []
+
+
+# per-run rules, applied to every run in this order: each returns its messages
+def _exact_listed(cell, run, rid, arms):
+    return [] if "exact" in arms else [f"exact_in_every_run: run {rid} does not list 'exact'"]
+
+
+def _swiftkv(cell, run, rid, arms):
+    swift = [a for a in arms if a in SWIFTKV_ARMS]
+    if run.get("model") != "swiftkv":
+        return [f"swiftkv_runs: run {rid} lists {swift} off the SwiftKV model"] if swift else []
+    out = []
+    if not swift or set(arms) - {"exact", *SWIFTKV_ARMS}:
+        out.append(f"swiftkv_runs: run {rid} on the SwiftKV model lists {arms}")
+    llama = str(cell.get("model", {}).get("name", "")).startswith("llama")
+    if "swiftkv_model" not in cell or not llama:
+        out.append(f"swiftkv_runs: run {rid} needs 'swiftkv_model' and a llama model")
+    return out
+
+
+def _controls(cell, run, rid, arms):
+    return [f"controls_need_their_rows_arm: run {rid}: {c} needs {rows} in the same run"
+            for c, rows in CONTROLS.items() if c in arms and rows not in arms]
+
+
+def _qblind(cell, run, rid, arms):
+    if run.get("split") != "3/8" and any(a in QBLIND_ARMS for a in arms):
+        return [f"qblind_at_the_blind_split: run {rid} has a qblind arm at {run.get('split')}"]
+    return []
+
+
+def _tailbudget(cell, run, rid, arms):
+    if "nofill+tailbudget" in arms and "tailbudget" not in cell:
+        return [f"tailbudget_declared: run {rid} has nofill+tailbudget without the cell's 'tailbudget'"]
+    return []
+
+
+def _projector(cell, run, rid, arms):
+    if "projector" not in cell and any(map(_uses_maps, arms)):
+        return [f"ridgefill_requires_projector: run {rid} needs the cell's 'projector'"]
+    return []
+
+
+def _set_blocks(cell, run, rid, arms):
+    s, derived = run.get("set"), cell.get("derived", {})
+    out = [f"set_blocks: run {rid} (set {s}) needs the cell's '{k}'" for k in SET_BLOCKS.get(s, ()) if k not in cell]
+    if s == "multiturn" and "ruler-twokey" not in derived:
+        out.append(f"set_blocks: run {rid} (set multiturn) needs derived 'ruler-twokey'")
+    if run.get("variant") == "qfirst" and not (s == "ruler" and "ruler-qfirst" in derived):
+        out.append(f"set_blocks: run {rid} (variant qfirst) runs on ruler with derived 'ruler-qfirst'")
+    return out
+
+
+def _row_selection(cell, run, rid, arms):
+    s = run.get("set")
+    out = []
+    if ("tasks" in run and s != "ruler") or ("lengths" in run and s not in ("ruler", "multiturn")):
+        out.append(f"row_selection: run {rid}: tasks on ruler runs only, lengths on ruler and multiturn runs")
+    cap = cell.get("max_len")
+    if cap and any(L > cap for L in run.get("lengths", [])):
+        out.append(f"row_selection: run {rid} selects lengths over max_len {cap}")
+    return out
+
+
+RUN_RULES = (_exact_listed, _swiftkv, _controls, _qblind, _tailbudget, _projector, _set_blocks, _row_selection)
 
 
 def semantic(cell):
-    """(errors, warnings) of the cross-field rules."""
-    errs, warns = [], []
+    """(errors, warnings) of the cross-field rules, each message led by its rule's name."""
     if cell.get("kind") == "flashnext":
-        need = [k for k in ENGINE_ONLY if k not in cell] + [k for k in ("ttft_min_speedup", "ttft_length")
-                                                            if k not in cell.get("margins", {})]
-        if need or "runs" in cell or cell.get("split") != "-":
-            errs.append(f"flashnext_cell: needs {need or 'split -'} and no runs (it runs on the engine's own driver)")
-        return errs, warns
+        return _flashnext(cell), []
+    errs, warns = [], []
     if "runs" not in cell:
         errs.append("primary_run: a reference cell needs 'runs'")
     want = PRIMARY_SPLIT.get(cell.get("kind"), "3/8")
-    if cell.get("split") != want or cell.get("tail") != 4096:
+    if (cell.get("split"), cell.get("tail")) != (want, 4096):
         errs.append(f"primary_run: a {cell.get('kind')} cell declares split {want} and tail 4096, not "
                     f"{cell.get('split')} / {cell.get('tail')}")
-    present = [k for k in ENGINE_ONLY if k in cell]
-    if present:
-        errs.append(f"flashnext_cell: {present} belong to the engine-tier cell")
-    for f in cell.get("projector", {}).get("files", []):
-        if "sha256" not in f:
-            warns.append(f"projector_unpinned: {f['file']} declares no sha256: the cell can not be registered or run")
+    engine_keys = [k for k in ENGINE_ONLY if k in cell]
+    if engine_keys:
+        errs.append(f"flashnext_cell: {engine_keys} belong to the engine-tier cell")
+    warns += [f"projector_unpinned: {f['file']} declares no sha256: the cell can not be registered or run"
+              for f in cell.get("projector", {}).get("files", []) if "sha256" not in f]
     runs = cell.get("runs", [])
     ids = [r.get("id") for r in runs]
-    dup = sorted({i for i in ids if ids.count(i) > 1})
-    if dup:
-        errs.append(f"run_ids_unique: duplicate run ids {dup}")
+    repeated = sorted({i for i in ids if ids.count(i) > 1})
+    if repeated:
+        errs.append(f"run_ids_unique: duplicate run ids {repeated}")
     if runs and not any(r.get("role") == "primary" and r.get("split") == cell.get("split") for r in runs):
         errs.append(f"primary_run: no run with role 'primary' at the primary split {cell.get('split')}")
-    derived = cell.get("derived", {})
-    for r in runs:
-        arms, rid, s = r.get("arms", []), r.get("id"), r.get("set")
-        if "exact" not in arms:
-            errs.append(f"exact_in_every_run: run {rid} does not list 'exact'")
-        swift = [a for a in arms if a in SWIFTKV_ARMS]
-        if r.get("model") == "swiftkv":
-            if set(arms) - {"exact", *SWIFTKV_ARMS} or not swift:
-                errs.append(f"swiftkv_runs: run {rid} on the SwiftKV model lists {arms}")
-            if "swiftkv_model" not in cell or not str(cell.get("model", {}).get("name", "")).startswith("llama"):
-                errs.append(f"swiftkv_runs: run {rid} needs 'swiftkv_model' and a llama model")
-        elif swift:
-            errs.append(f"swiftkv_runs: run {rid} lists {swift} off the SwiftKV model")
-        for c, rows in CONTROLS.items():
-            if c in arms and rows not in arms:
-                errs.append(f"controls_need_their_rows_arm: run {rid}: {c} needs {rows} in the same run")
-        if any(a in QBLIND_ARMS for a in arms) and r.get("split") != "3/8":
-            errs.append(f"qblind_at_the_blind_split: run {rid} has a qblind arm at {r.get('split')}")
-        if "nofill+tailbudget" in arms and "tailbudget" not in cell:
-            errs.append(f"tailbudget_declared: run {rid} has nofill+tailbudget without the cell's 'tailbudget'")
-        if any(_uses_maps(a) for a in arms) and "projector" not in cell:
-            errs.append(f"ridgefill_requires_projector: run {rid} needs the cell's 'projector'")
-        for k in SET_BLOCKS.get(s, ()):
-            if k not in cell:
-                errs.append(f"set_blocks: run {rid} (set {s}) needs the cell's '{k}'")
-        if s == "multiturn" and "ruler-twokey" not in derived:
-            errs.append(f"set_blocks: run {rid} (set multiturn) needs derived 'ruler-twokey'")
-        if r.get("variant") == "qfirst" and (s != "ruler" or "ruler-qfirst" not in derived):
-            errs.append(f"set_blocks: run {rid} (variant qfirst) runs on ruler with derived 'ruler-qfirst'")
-        if ("tasks" in r and s != "ruler") or ("lengths" in r and s not in ("ruler", "multiturn")):
-            errs.append(f"row_selection: run {rid}: tasks on ruler runs only, lengths on ruler and multiturn runs")
-        cap = cell.get("max_len")
-        if cap and any(L > cap for L in r.get("lengths", [])):
-            errs.append(f"row_selection: run {rid} selects lengths over max_len {cap}")
-    if "dataset" in cell and (cell.get("kind") not in ("nll", "nll-causal", "nll-fresh")
-                              or any(r.get("set") != "longppl" for r in runs)):
+    for run in runs:
+        for rule in RUN_RULES:
+            errs += rule(cell, run, run.get("id"), run.get("arms", []))
+    longppl_only = cell.get("kind") in ("nll", "nll-causal", "nll-fresh") and all(r.get("set") == "longppl"
+                                                                                   for r in runs)
+    if "dataset" in cell and not longppl_only:
         errs.append(f"dataset_longppl_only: dataset {cell['dataset']!r} serves nll cells whose runs are all longppl")
     if cell.get("registration") == "FINAL-TBD":
         warns.append("final_tbd_flagged: registration 'FINAL-TBD': the cell does not run until it is registered")
