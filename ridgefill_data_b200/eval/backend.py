@@ -49,82 +49,95 @@ class StaleProjector(RuntimeError):
 
 
 def layer_of(model_entry, frac):
-    num, den = (int(x) for x in frac.split("/"))
-    return num * model_entry["layers"] // den
+    """The layer a split fraction 'a/b' names: floor(a * layers / b)."""
+    num, _, den = frac.partition("/")
+    return int(num) * model_entry["layers"] // int(den)
 
 
 def _model_of(cell, run):
-    return cell["swiftkv_model"]["name"] if run.get("model") == "swiftkv" else cell["model"]["name"]
+    source = cell["swiftkv_model"] if run.get("model") == "swiftkv" else cell["model"]
+    return source["name"]
+
+
+def _declared_maps(cell):
+    return {f["layer"]: f["file"] for f in cell.get("projector", {}).get("files", [])}
 
 
 def arm_spec(p, cell, run, paper, layer):
+    """The harness arm spec of a paper arm name at a layer (the protocol template, renamed <paper>-s<layer>, with
+    the map under $RF_PROJ_DIR and a control's match pointing at its rows arm)."""
     from ..engine import protocol as PR
-    kind = PAPER.get(paper)
-    if kind is None:
+    if paper not in PAPER:
         raise HarnessGap(f"unknown arm {paper!r}")
+    kind = PAPER[paper]
     model = _model_of(cell, run)
-    m = p["models"][model]
-    split = m["pop_split"] if kind == "pop-native" else layer
-    tail = None if kind in PR.TAILLESS else cell["tail"]
-    spec = PR.template(kind, model, split, tail, p)
+    split = p["models"][model]["pop_split"] if kind == "pop-native" else layer
+    spec = PR.template(kind, model, split, None if kind in PR.TAILLESS else cell["tail"], p)
     spec["name"] = f"{paper}-s{split}"
     if "projector" in spec:
-        declared = {f["layer"]: f["file"] for f in cell.get("projector", {}).get("files", [])}
-        if declared.get(split) != spec["projector"]:
-            raise HarnessGap(f"cell {cell['name']}: arm {paper} at layer {split} reads {spec['projector']}, which the "
-                             f"cell's projector.files does not declare ({declared.get(split)})")
-        spec["projector"] = f"$RF_PROJ_DIR/{spec['projector']}"
-    sel = spec.get("select", {})
-    if "match" in sel:
-        sel["match"] = f"{ROWS_OF[kind.split('+')[0]]}-s{split}"
+        declared = _declared_maps(cell).get(split)
+        if declared != spec["projector"]:
+            raise HarnessGap(f"cell {cell['name']}: arm {paper} at layer {split} reads {spec['projector']}, which "
+                             f"the cell's projector.files does not declare ({declared})")
+        spec["projector"] = "$RF_PROJ_DIR/" + spec["projector"]
+    select = spec.get("select", {})
+    if "match" in select:
+        select["match"] = f"{ROWS_OF[kind.partition('+')[0]]}-s{split}"
     if kind == "skip+tailbudget":
-        sel["budget"] = cell["tailbudget"]["b"]
+        select["budget"] = cell["tailbudget"]["b"]
     return spec
 
 
 def _group_key(run):
-    return (run["set"], run.get("variant"), run.get("model"), tuple(run.get("tasks", ())),
-            tuple(run.get("lengths", ())))
+    selection = (tuple(run.get("tasks", ())), tuple(run.get("lengths", ())))
+    return (run["set"], run.get("variant"), run.get("model")) + selection
+
+
+def _set_fields(cell, run):
+    """Config keys a run's set (and its row selection) adds."""
+    kind = run["set"]
+    out = {}
+    if kind == "longppl":
+        out["keytoken_tail"] = cell["keytoken"]["tail"]
+    elif kind == "decode":
+        dec = cell["decode"]
+        out.update(decode_from=dec["from"], decode_steps=dec["steps"], only=",".join(dec["only"]))
+    elif kind == "multiturn":
+        out.update(multiturn_from=cell["secondq"]["from"], multiturn_turns=cell["secondq"]["turns"])
+    elif kind == "ttft":
+        out["ttft_lengths"] = list(cell.get("ttft_lengths", TTFT_LENGTHS))
+    if "dataset" in cell:
+        out.update(dataset=cell["dataset"], dataset_manifest_sha256=cell["dataset_manifest_sha256"])
+    for key, field in (("variant", "ruler_variant"), ("tasks", "ruler_tasks"), ("lengths", "ruler_lengths")):
+        if run.get(key):
+            out[field] = run[key] if key == "variant" else list(run[key])
+    return out
 
 
 def harness_config(cell, runs, p):
-    """(config, set) of runs sharing a set, variant, model and row selection."""
-    run = runs[0]
-    model = _model_of(cell, run)
-    m = p["models"][model]
-    arms, parts = [], []
+    """(config, set) of the runs that share a set, variant, model and row selection."""
+    first = runs[0]
+    model = _model_of(cell, first)
+    entry = p["models"][model]
+    arms, described = [], []
     for r in runs:
-        layer = 16 if r.get("model") == "swiftkv" else layer_of(m, r["split"])
-        if layer not in m["splits"]:
-            raise HarnessGap(f"split {r['split']} of {model} is layer {layer}, not one of the protocol's {m['splits']}")
-        arms += [arm_spec(p, cell, r, a, layer) for a in r["arms"] if a != "exact"]
-        parts.append(f"{r['id']} ({r['role']}, split {r['split']} = layer {layer})")
-    cfg = {"name": f"{cell['model']['name']}-{run['id']}", "protocol": cell["code_tag"].removeprefix("protocol-v"),
-           "registration": [cell["registration"]], "model": f"$RF_MODEL_DIR/{model}",
-           "tokenizer": f"$RF_MODEL_DIR/{cell['model']['name']}", "niah_format": m.get("niah_format"),
-           "note": f"cell {cell['name']}, set {run['set']}, runs {', '.join(parts)}; generated from the cell",
-           "arms": arms, **cell.get("caps", {})}
-    if run["set"] == "longppl":
-        cfg["keytoken_tail"] = cell["keytoken"]["tail"]
-    if "dataset" in cell:
-        cfg.update(dataset=cell["dataset"], dataset_manifest_sha256=cell["dataset_manifest_sha256"])
-    if run["set"] == "decode":
-        cfg.update(decode_from=cell["decode"]["from"], decode_steps=cell["decode"]["steps"],
-                   only=",".join(cell["decode"]["only"]))
-    if run["set"] == "multiturn":
-        cfg.update(multiturn_from=cell["secondq"]["from"], multiturn_turns=cell["secondq"]["turns"])
-    if run["set"] == "ttft":
-        cfg["ttft_lengths"] = list(cell.get("ttft_lengths", TTFT_LENGTHS))
-    if run.get("variant"):
-        cfg["ruler_variant"] = run["variant"]
-    if run.get("tasks"):
-        cfg["ruler_tasks"] = list(run["tasks"])
-    if run.get("lengths"):
-        cfg["ruler_lengths"] = list(run["lengths"])
+        layer = 16 if r.get("model") == "swiftkv" else layer_of(entry, r["split"])
+        if layer not in entry["splits"]:
+            raise HarnessGap(f"split {r['split']} of {model} is layer {layer}, not one of the protocol's "
+                             f"{entry['splits']}")
+        arms.extend(arm_spec(p, cell, r, a, layer) for a in r["arms"] if a != "exact")
+        described.append(f"{r['id']} ({r['role']}, split {r['split']} = layer {layer})")
     names = [a["name"] for a in arms]
-    if len(set(names)) != len(names):
+    cfg = dict(cell.get("caps", {}))
+    cfg.update(name=f"{cell['model']['name']}-{first['id']}", protocol=cell["code_tag"].removeprefix("protocol-v"),
+               registration=[cell["registration"]], model=f"$RF_MODEL_DIR/{model}",
+               tokenizer=f"$RF_MODEL_DIR/{cell['model']['name']}", niah_format=entry.get("niah_format"),
+               note=f"cell {cell['name']}, set {first['set']}, runs {', '.join(described)}; generated from the cell",
+               arms=arms)
+    cfg.update(_set_fields(cell, first))
+    if len(names) != len(set(names)):
         raise HarnessGap(f"cell {cell['name']}: an arm appears twice in {cfg['name']}: {names}")
-    return cfg, run["set"]
+    return cfg, first["set"]
 
 
 def harness_configs(cell, p):
@@ -133,7 +146,7 @@ def harness_configs(cell, p):
     groups = {}
     for r in cell["runs"]:
         groups.setdefault(_group_key(r), []).append(r)
-    return [harness_config(cell, runs, p) for runs in groups.values()]
+    return [harness_config(cell, members, p) for members in groups.values()]
 
 
 def config_bytes(cfg):
