@@ -56,7 +56,8 @@ def locked_dir():
 
 
 def _sha256(path):
-    return hashlib.sha256(Path(path).read_bytes()).hexdigest()
+    with open(path, "rb") as f:
+        return hashlib.file_digest(f, "sha256").hexdigest()
 
 
 def manifest(root=None, pin=None, name="the locked set"):
@@ -115,18 +116,22 @@ def check_max_new(max_new):
     """{task: tokens} that only LOWERS RULER's tokens_to_generate for named RULER tasks."""
     if max_new is None:
         return {}
-    bad = {t: v for t, v in dict(max_new).items()
-           if t not in RULER_TASKS or type(v) is not int or not 0 < v <= RULER_TASKS[t][1]}
+    caps = dict(max_new)
+
+    def allowed(task, v):
+        return task in RULER_TASKS and type(v) is int and 0 < v <= RULER_TASKS[task][1]
+    bad = {t: v for t, v in caps.items() if not allowed(t, v)}
     if bad:
         raise LockedSetError(f"ruler_max_new {bad}: each cap names a RULER task and lowers its tokens_to_generate")
-    return dict(max_new)
+    return caps
 
 
 def ruler_selection(tasks=None, lengths=None):
-    tasks = list(RULER_TASKS) if tasks is None else list(tasks)
-    lengths = list(RULER_LENGTHS) if lengths is None else list(lengths)
-    bad = [t for t in tasks if t not in RULER_TASKS] + [L for L in lengths if L not in RULER_LENGTHS]
-    if bad or not tasks or not lengths:
+    tasks = list(RULER_TASKS if tasks is None else tasks)
+    lengths = list(RULER_LENGTHS if lengths is None else lengths)
+    bad = [t for t in tasks if t not in RULER_TASKS]
+    bad += [L for L in lengths if L not in RULER_LENGTHS]
+    if bad or not (tasks and lengths):
         raise LockedSetError(f"ruler_tasks / ruler_lengths: {bad or 'empty'} not RULER's")
     return tasks, lengths
 
@@ -138,15 +143,16 @@ class NeedleSpanError(ValueError):
 def needle_spans(tok, fmt, user, reply, ids, refs, name):
     """Token spans [start, end) of the numeric needles whose value a NIAH row scores, in document order."""
     from . import derived
-    hits = [(v, s, e) for _, v, s, e in derived.needles(user) if v in refs]
-    if sorted(v for v, _, _ in hits) != sorted(refs):
+    hits = [(value, lo, hi) for _, value, lo, hi in derived.needles(user) if value in refs]
+    if sorted(h[0] for h in hits) != sorted(refs):
         raise NeedleSpanError(f"{name}: its {len(refs)} scored values are not each found exactly once among its "
                               f"needles ({len(hits)} carry one)")
     if fmt == "chat":
         text, base = user, len(TX.chat_pieces(tok)[0])
     else:
         text, base = user + reply, len(TX.bos_ids(tok))
-    return [list(s) for s in derived.token_spans(tok, text, [(s, e) for _, s, e in hits], ids, base)]
+    spans = derived.token_spans(tok, text, [(lo, hi) for _, lo, hi in hits], ids, base)
+    return [[a, b] for a, b in spans]
 
 
 def ruler_prompts(tok, fmt, man, max_len=None, tasks=None, lengths=None, max_new=None, root=None):
@@ -163,12 +169,13 @@ def ruler_prompts(tok, fmt, man, max_len=None, tasks=None, lengths=None, max_new
             sha = source(rel, man, root)
             for i, r in enumerate(rows(rel, root)):
                 name = f"ruler-{task}-{L}-{i:02d}"
-                ids = wrap(tok, fmt, r["input"], r["answer_prefix"])
-                q = dict(name=name, set="ruler", task=task, ruler_task=kind, length=L, source=rel, source_sha256=sha,
-                         row=i, index=r.get("index"), max_new=caps.get(task, steps), metric=metric, refs=r["outputs"],
-                         format=fmt, ids=ids)
+                user, reply = r["input"], r["answer_prefix"]
+                ids = wrap(tok, fmt, user, reply)
+                q = {"name": name, "set": "ruler", "task": task, "ruler_task": kind, "length": L, "source": rel,
+                     "source_sha256": sha, "row": i, "index": r.get("index"), "max_new": caps.get(task, steps),
+                     "metric": metric, "refs": r["outputs"], "format": fmt, "ids": ids}
                 if kind == "niah":
-                    q["needles"] = needle_spans(tok, fmt, r["input"], r["answer_prefix"], ids, r["outputs"], name)
+                    q["needles"] = needle_spans(tok, fmt, user, reply, ids, r["outputs"], name)
                 out.append(q)
     return out, skipped
 
@@ -179,8 +186,10 @@ def middle_truncate(tok, prompt, max_len):
     ids = tok(prompt).input_ids
     if len(ids) <= max_len:
         return prompt, False
-    half = int(max_len / 2)
-    return tok.decode(ids[:half], skip_special_tokens=True) + tok.decode(ids[-half:], skip_special_tokens=True), True
+    keep = int(max_len / 2)
+    head = tok.decode(ids[:keep], skip_special_tokens=True)
+    tail = tok.decode(ids[len(ids) - keep:], skip_special_tokens=True)
+    return head + tail, True
 
 
 def longbench_prompts(tok, fmt, man, max_len, root=None):
@@ -200,24 +209,28 @@ def longbench_prompts(tok, fmt, man, max_len, root=None):
             if r["dataset"] != task:
                 raise LockedSetError(f"{rel} row {i} is from {r['dataset']!r}")
             prompt, cut = middle_truncate(tok, templates[task].format(**r), max_len)
-            f = "raw" if task in LONGBENCH_NO_CHAT else fmt
-            out.append(dict(name=f"lb-{task}-{i:02d}", set="longbench", task=task, length=r.get("length"), source=rel,
-                            source_sha256=sha, row=i, id=r.get("_id"), max_new=budgets[task],
-                            metric=MT.LONGBENCH_METRIC[task].__name__, refs=r["answers"],
-                            all_classes=r.get("all_classes"), truncated=cut, format=f, ids=wrap(tok, f, prompt)))
+            row_fmt = fmt if task not in LONGBENCH_NO_CHAT else "raw"
+            q = {"name": f"lb-{task}-{i:02d}", "set": "longbench", "task": task, "length": r.get("length"),
+                 "source": rel, "source_sha256": sha, "row": i, "id": r.get("_id"), "max_new": budgets[task],
+                 "metric": MT.LONGBENCH_METRIC[task].__name__, "refs": r["answers"],
+                 "all_classes": r.get("all_classes"), "truncated": cut, "format": row_fmt}
+            q["ids"] = wrap(tok, row_fmt, prompt)
+            out.append(q)
     return out, []
 
 
 def splits_column(model, columns):
     """The SPLITS.tsv token-count column whose tokenizer name prefixes the model's, or None."""
-    keys = [c[len("prompt_tokens_"):] for c in columns if c.startswith("prompt_tokens_")]
-    hits = [k for k in keys if model.startswith(k)]
-    return max(hits, key=len) if hits else None
+    prefix = "prompt_tokens_"
+    names = [c.removeprefix(prefix) for c in columns if c.startswith(prefix)]
+    matching = sorted((k for k in names if model.startswith(k)), key=len)
+    return matching[-1] if matching else None
 
 
 def doc_length(rel):
     """Nominal length of a long-prompt file <name>_<L>_<k>.txt."""
-    return int(rel.rsplit("/", 1)[-1][:-len(".txt")].rsplit("_", 2)[-2])
+    stem = Path(rel).name.removesuffix(".txt")
+    return int(stem.split("_")[-2])
 
 
 def longppl_docs(tok, man, model, max_len=None, root=None):
@@ -237,13 +250,14 @@ def longppl_docs(tok, man, model, max_len=None, root=None):
         body = (root / rel).read_text()
         s = int(r["split_char"])
         head, cont = TX.encode(tok, body[:s]), TX.encode(tok, body[s:])
-        if col and (len(head), len(cont)) != (int(r[f"prompt_tokens_{col}"]), int(r[f"continuation_tokens_{col}"])):
-            raise LockedSetError(f"{rel}: {len(head)} + {len(cont)} tokens, SPLITS.tsv counts differ for {col}")
+        if col:
+            counted = (int(r[f"prompt_tokens_{col}"]), int(r[f"continuation_tokens_{col}"]))
+            if counted != (len(head), len(cont)):
+                raise LockedSetError(f"{rel}: {len(head)} + {len(cont)} tokens, SPLITS.tsv counts differ for {col}")
         ids = bos + head + cont
-        stem = rel.rsplit("/", 1)[-1][:-len(".txt")]
-        out.append(dict(name=f"lp-{stem}", set="longppl", task=man[rel]["domain"], length=L, source=rel,
-                        source_sha256=sha, split_char=s, cont_len=len(cont), novel=TX.novel_mask(ids, len(cont)),
-                        format="raw", ids=ids))
+        out.append({"name": "lp-" + Path(rel).name.removesuffix(".txt"), "set": "longppl",
+                    "task": man[rel]["domain"], "length": L, "source": rel, "source_sha256": sha, "split_char": s,
+                    "cont_len": len(cont), "novel": TX.novel_mask(ids, len(cont)), "format": "raw", "ids": ids})
     return out, skipped
 
 
@@ -299,12 +313,13 @@ def check_tails(prompts_, tails):
 
 def score(q, text):
     """Per generation-set row: the prediction as scored, its 0-1 score and the metric's name."""
-    if q["set"] == "ruler":
-        pred = MT.postprocess_pred(text)
-        return dict(pred=pred, metric=q["metric"], score=MT.ruler_row(q["metric"], pred, q["refs"]))
-    return dict(pred=text, metric=q["metric"], score=MT.longbench_row(q["task"], text, q["refs"], q["all_classes"]))
+    if q["set"] != "ruler":
+        value = MT.longbench_row(q["task"], text, q["refs"], q["all_classes"])
+        return {"pred": text, "metric": q["metric"], "score": value}
+    pred = MT.postprocess_pred(text)
+    return {"pred": pred, "metric": q["metric"], "score": MT.ruler_row(q["metric"], pred, q["refs"])}
 
 
 def nll(logprobs, mask=None):
-    xs = [-x for i, x in enumerate(logprobs) if mask is None or mask[i]]
-    return sum(xs) / len(xs)
+    picked = list(logprobs) if mask is None else [x for x, keep in zip(logprobs, mask) if keep]
+    return -sum(picked) / len(picked)
