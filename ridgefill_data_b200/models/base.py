@@ -85,7 +85,8 @@ class Model:
 
     # ---- common ops
     def new_cache(self):
-        return [dict() for _ in range(self.n_layers)]
+        """One empty per-layer cache entry per layer."""
+        return [{} for _ in range(self.n_layers)]
 
     def embed(self, ids):
         return F.embedding(ids.to(self.embed_w.device), self.embed_w).to(self.device)
@@ -101,7 +102,8 @@ class Model:
 
         def run(x):
             x = self.post_norm(x, w["ln2"])
-            return F.linear(F.silu(F.linear(x, w["gate"])) * F.linear(x, w["up"]), w["down"])
+            act = F.silu(F.linear(x, w["gate"])) * F.linear(x, w["up"])
+            return F.linear(act, w["down"])
 
         return h + _rows(run, h)
 
@@ -109,12 +111,12 @@ class Model:
         return max(1, ROW_BYTES // (self.hidden * self.dtype.itemsize))
 
     def mlp_rows(self, i, h):
-        n = h.shape[0]
-        if n <= self.row_block():
+        limit = self.row_block()
+        if h.shape[0] <= limit:
             return self.mlp(i, h)
-        step = max(MLP_ROWS, self.row_block() // MLP_ROWS * MLP_ROWS)
-        for a in range(0, n, step):
-            h[a:a + step] = self.mlp(i, h[a:a + step])
+        step = max(MLP_ROWS, (limit // MLP_ROWS) * MLP_ROWS)     # whole MLP blocks per run, in place
+        for lo in range(0, h.shape[0], step):
+            h[lo:lo + step] = self.mlp(i, h[lo:lo + step])
         return h
 
     def _append_kv(self, cache, k, v):
@@ -122,29 +124,30 @@ class Model:
         in place; cache['k'] / cache['v'] are views of the first cache['n'] rows. Shallow copies of a
         cache (per-arm forks) share the buffer; rows below every copy's length are never rewritten
         (code/kva/model.py:139-159)."""
-        n = cache.get("n", 0)
-        m = k.shape[1]
-        kb = cache.get("kbuf")
-        if kb is None or n + m > kb.shape[1]:
-            cap = n + m + KV_RESERVE
-            nkb = k.new_empty(k.shape[0], cap, k.shape[2])
-            nvb = v.new_empty(v.shape[0], cap, v.shape[2])
-            if n:
-                nkb[:, :n] = cache["kbuf"][:, :n]
-                nvb[:, :n] = cache["vbuf"][:, :n]
-            cache["kbuf"], cache["vbuf"] = nkb, nvb
-        cache["kbuf"][:, n:n + m] = k
-        cache["vbuf"][:, n:n + m] = v
-        cache["n"] = n + m
-        cache["k"], cache["v"] = cache["kbuf"][:, :n + m], cache["vbuf"][:, :n + m]
+        have = cache.get("n", 0)
+        total = have + k.shape[1]
+        if "kbuf" not in cache or total > cache["kbuf"].shape[1]:
+            grown = {}
+            for name, rows in (("kbuf", k), ("vbuf", v)):
+                buf = rows.new_empty(rows.shape[0], total + KV_RESERVE, rows.shape[2])
+                if have:
+                    buf[:, :have] = cache[name][:, :have]
+                grown[name] = buf
+            cache.update(grown)
+        cache["kbuf"][:, have:total] = k
+        cache["vbuf"][:, have:total] = v
+        cache["n"] = total
+        cache["k"] = cache["kbuf"][:, :total]
+        cache["v"] = cache["vbuf"][:, :total]
 
     def _heads(self, x, n_heads):
         return x.view(x.shape[0], n_heads, self.head_dim).transpose(0, 1)
 
     def fill_kv(self, i, k, v, pos, cache):
         """Attention cache fill from pre-RoPE K and V [tokens, kv_heads, head_dim]."""
+        k_heads, v_heads = k.transpose(0, 1), v.transpose(0, 1)
         cos, sin = ops.rope_cos_sin(self.inv_freq, pos, k.dtype)
-        self._append_kv(cache[i], ops.apply_rope(k.transpose(0, 1), cos, sin), v.transpose(0, 1))
+        self._append_kv(cache[i], ops.apply_rope(k_heads, cos, sin), v_heads)
 
     def stable(self, h):
         """h itself, or a copy when h lives in a buffer that later layers reuse (tensor-parallel outputs)."""
@@ -167,17 +170,17 @@ class Model:
     def forward_exact(self, ids, hook=None, cache=None, keep=None, gdn_checkpoint_every=None, mix=None):
         """Exact forward over all rows. hook(i, h) sees each layer's input and hook('final', h) the
         final-norm input; mix(i, a) each layer's mixer output. keep: row indices whose logits to return."""
-        pos = torch.arange(ids.shape[0], device=self.device)
-        cache = self.new_cache() if cache is None else cache
+        if cache is None:
+            cache = self.new_cache()
+        positions = torch.arange(ids.shape[0], device=self.device)
         h = self.embed(ids)
         for i in range(self.n_layers):
             if hook is not None:
                 hook(i, self.stable(h))
-            h = self.layer(i, h, pos, cache, gdn_checkpoint_every=gdn_checkpoint_every, mix=mix)
+            h = self.layer(i, h, positions, cache, gdn_checkpoint_every=gdn_checkpoint_every, mix=mix)
         if hook is not None:
             hook("final", self.stable(h))
-        out = self.logits(h[keep]) if keep is not None else None
-        return out, cache
+        return (None if keep is None else self.logits(h[keep])), cache
 
 
 def model_class(cfg: ModelConfig, backend="torch"):
