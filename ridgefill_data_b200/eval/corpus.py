@@ -60,37 +60,45 @@ def strings_of(obj):
             yield from strings_of(v)
 
 
-def file_grams(path):
-    """Unique fingerprints of a file: .txt as text, .json / .jsonl per decoded string value."""
+def _pieces(path):
+    """The texts of a file: a .txt whole, a .json / .jsonl file as its decoded string values."""
     path = Path(path)
     raw = path.read_text(encoding="utf-8", errors="ignore")
     if path.suffix == ".json":
-        parts = list(strings_of(json.loads(raw)))
-    elif path.suffix == ".jsonl":
-        parts = [s for line in raw.splitlines() if line.strip() for s in strings_of(json.loads(line))]
-    else:
-        parts = [raw]
-    g = [grams(s) for s in parts]
-    return np.unique(np.concatenate(g)) if g else np.zeros(0, np.uint64)
+        return list(strings_of(json.loads(raw)))
+    if path.suffix == ".jsonl":
+        return [piece for line in raw.splitlines() if line.strip() for piece in strings_of(json.loads(line))]
+    return [raw]
+
+
+def _union(arrays):
+    arrays = list(arrays)
+    return np.unique(np.concatenate(arrays)) if arrays else np.zeros(0, np.uint64)
+
+
+def file_grams(path):
+    """Distinct fingerprints of a file (each of its texts fingerprinted on its own)."""
+    return _union(grams(piece) for piece in _pieces(path))
 
 
 def reference(paths, texts=()):
-    parts = [file_grams(p) for p in paths] + [grams(t) for t in texts]
-    return np.unique(np.concatenate(parts)) if parts else np.zeros(0, np.uint64)
+    """Sorted distinct fingerprints of reference files and texts."""
+    return _union([file_grams(p) for p in paths] + [grams(t) for t in texts])
 
 
 def shared(g, ref):
     """How many distinct fingerprints of g occur in the sorted array ref."""
-    u = np.unique(g)
-    if not len(u) or not len(ref):
+    distinct = np.unique(g)
+    if distinct.size == 0 or ref.size == 0:
         return 0
-    i = np.minimum(np.searchsorted(ref, u), len(ref) - 1)
-    return int((ref[i] == u).sum())
+    return int(np.isin(distinct, ref, assume_unique=True).sum())
 
 
 def self_repeat(g):
     """Share of a document's gram positions that repeat an earlier gram of the same document (boilerplate)."""
-    return 1.0 - len(np.unique(g)) / len(g) if len(g) else 0.0
+    if len(g) == 0:
+        return 0.0
+    return 1.0 - np.unique(g).size / len(g)
 
 
 class Seen:
@@ -120,24 +128,26 @@ class Seen:
 def cut_points(n, fracs=FRACS, min_cut=MIN_CUT, gap=GAP):
     """Window ends of a document of n tokens: each fraction of n raised to min_cut, kept when at least `gap` away
     from every end already kept (longest first, so the document's own end is always one). Ascending."""
-    cuts = []
-    for f in sorted(fracs, reverse=True):
-        c = max(min_cut, round(f * n))
-        if c <= n and all(abs(c - k) >= gap for k in cuts):
-            cuts.append(c)
-    return sorted(cuts)
+    kept = []
+    for frac in sorted(fracs, reverse=True):
+        end = max(min_cut, round(frac * n))
+        far_enough = min((abs(end - k) for k in kept), default=gap) >= gap
+        if end <= n and far_enough:
+            kept.append(end)
+    return sorted(kept)
 
 
 def read_tsv(path):
     with open(path, newline="") as f:
-        return list(csv.DictReader(f, delimiter="\t"))
+        return [dict(row) for row in csv.DictReader(f, dialect="excel-tab")]
 
 
 def write_tsv(path, rows, fields=None):
+    columns = list(fields) if fields else list(rows[0])
     with open(path, "w", newline="") as f:
-        w = csv.DictWriter(f, fieldnames=fields or list(rows[0]), delimiter="\t", extrasaction="ignore")
-        w.writeheader()
-        w.writerows(rows)
+        out = csv.DictWriter(f, columns, extrasaction="ignore", dialect="excel-tab")
+        out.writeheader()
+        out.writerows(rows)
 
 
 def overlap_report(calib, evaluation, n=GRAM):
@@ -156,17 +166,10 @@ def overlap_report(calib, evaluation, n=GRAM):
 
 def _texts(paths):
     out = {}
-    for p in paths:
-        p = Path(p)
-        files = sorted(p.rglob("*")) if p.is_dir() else [p]
-        for f in files:
+    for p in map(Path, paths):
+        for f in (sorted(p.rglob("*")) if p.is_dir() else [p]):
             if f.is_file() and f.suffix in (".txt", ".json", ".jsonl"):
-                raw = f.read_text(encoding="utf-8", errors="ignore")
-                if f.suffix == ".json":
-                    raw = "\n".join(strings_of(json.loads(raw)))
-                elif f.suffix == ".jsonl":
-                    raw = "\n".join(s for line in raw.splitlines() if line.strip() for s in strings_of(json.loads(line)))
-                out[str(f)] = raw
+                out[str(f)] = "\n".join(_pieces(f))
     return out
 
 
