@@ -24,13 +24,22 @@ I8_GROUP = 128
 
 
 def check_weights(tensors, where):
-    for k, t in tensors.items():
-        t = t.float()
-        bad = ~torch.isfinite(t) | (t.abs() > MAX_ABS_WEIGHT)
-        if bad.any():
-            r, c = bad.nonzero()[0].tolist()
-            raise ValueError(f"{where}: {k} has {int(bad.sum())} non-finite or |w| > {MAX_ABS_WEIGHT:g} weights "
-                             f"(first at row {r}, col {c}: {t[r, c].item():.4g}); refusing")
+    """Refuse any map holding a NaN / inf or a weight beyond MAX_ABS_WEIGHT in magnitude."""
+    for name, t in tensors.items():
+        vals = t.float()
+        ok = torch.isfinite(vals) & (vals.abs() <= MAX_ABS_WEIGHT)
+        if bool(ok.all()):
+            continue
+        where_bad = (~ok).nonzero()
+        r, c = where_bad[0].tolist()
+        raise ValueError(f"{where}: refusing {name}: {where_bad.shape[0]} weights are NaN, infinite or above "
+                         f"{MAX_ABS_WEIGHT:g} in magnitude (first at row {r}, col {c}: {vals[r, c].item():.4g})")
+
+
+def _header_meta(data):
+    """The __metadata__ map of safetensors bytes (empty when absent)."""
+    size = int.from_bytes(data[:8], "little")
+    return json.loads(data[8:8 + size]).get("__metadata__") or {}
 
 
 def stable_safetensors(tensors, metadata=None):
@@ -114,13 +123,14 @@ class Projector:
 
         from ..utils import integrity
         data, sha = integrity.read_verified(path, sha256)
-        meta = json.loads(data[8:8 + int.from_bytes(data[:8], "little")]).get("__metadata__") or {}
+        meta = _header_meta(data)
         W, B = {}, {}
-        for k, t in from_bytes(data).items():
-            i = int(k.split(".")[1])
-            check_weights({k: t}, f"Projector.load {path}")
-            W[i] = t[:, :-1].to(device, dtype).contiguous()
-            B[i] = t[:, -1].to(device, dtype).contiguous()
+        for name, packed in from_bytes(data).items():
+            check_weights({name: packed}, f"Projector.load {path}")
+            layer = int(name.split(".")[1])
+            weight, bias = packed.split([packed.shape[1] - 1, 1], dim=1)
+            W[layer] = weight.to(device, dtype).contiguous()
+            B[layer] = bias.squeeze(1).to(device, dtype).contiguous()
         p = cls(int(meta["split"]), W, B, meta)
         p.sha256 = sha
         return p
