@@ -11,46 +11,42 @@ from .scoring import check_finite
 def step(model, tok, position, cache, arm):
     """One exact decode step: token `tok` at `position` through every layer over `cache` (appended in place).
     Returns the next-token logits [1, V] fp32."""
-    native = arm is not None and arm.fill == "swiftkv_native"
-    pos = torch.tensor([position], device=model.device)
-    h = model.embed(torch.tensor([tok], device=model.device))
-    b = None
-    for i in range(model.n_layers):
-        if native and i >= arm.split:
-            if i == arm.split:
-                b = h
-            model.swift_fill(i, b, pos, cache)
-            h = model.swift_layer(i, h, pos, cache)
-        else:
-            h = model.layer(i, h, pos, cache)
+    dev = model.device
+    pos = torch.tensor([position], device=dev)
+    h = model.embed(torch.tensor([tok], device=dev))
+    swift_from = arm.split if arm is not None and arm.fill == "swiftkv_native" else model.n_layers
+    for i in range(swift_from):
+        h = model.layer(i, h, pos, cache)
+    boundary = h
+    for i in range(swift_from, model.n_layers):      # SwiftKV's own late layers read the boundary state
+        model.swift_fill(i, boundary, pos, cache)
+        h = model.swift_layer(i, h, pos, cache)
     return model.logits(h)
 
 
 @torch.no_grad()
 def greedy(model, ids, cache, first_logits, steps, arm, eos=()):
     """Greedy continuation of up to `steps` tokens, stopping after an EOS. Returns (tokens, 'stop' | 'length')."""
-    out = []
-    tok = int(check_finite(first_logits[-1], f"{arm.name} first token").argmax())
-    n = ids.shape[0]
-    for t in range(steps):
-        out.append(tok)
-        if tok in eos:
-            return out, "stop"
-        if t == steps - 1:
+    made = []
+    start = ids.shape[0]
+    nxt = int(check_finite(first_logits[-1], f"{arm.name} first token").argmax())
+    while len(made) < steps:
+        made.append(nxt)
+        if nxt in eos:
+            return made, "stop"
+        if len(made) == steps:
             break
-        logits = step(model, tok, n + t, cache, arm)
-        tok = int(check_finite(logits[-1], f"{arm.name} decode step {t + 1}").argmax())
-    return out, "length"
+        logits = step(model, nxt, start + len(made) - 1, cache, arm)
+        nxt = int(check_finite(logits[-1], f"{arm.name} decode step {len(made)}").argmax())
+    return made, "length"
 
 
 def fork_cache(cache):
     """A per-arm fork of a cache: per-layer dict copies sharing K/V buffers (rows below every fork's length
     are never rewritten) and cloned recurrent states."""
-    out = []
-    for c in cache:
-        d = dict(c)
-        for k in ("rec", "conv"):
-            if k in d and d[k] is not None:
-                d[k] = d[k].clone()
-        out.append(d)
-    return out
+    forks = []
+    for entry in cache:
+        fork = dict(entry)
+        fork.update({k: fork[k].clone() for k in ("rec", "conv") if fork.get(k) is not None})
+        forks.append(fork)
+    return forks

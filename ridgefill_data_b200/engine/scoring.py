@@ -10,9 +10,10 @@ class NonFiniteLogits(RuntimeError):
 
 
 def check_finite(logits, where):
-    if not bool(torch.isfinite(logits).all()):
-        raise NonFiniteLogits(f"non-finite logits ({where})")
-    return logits
+    """logits, after checking that every value is finite."""
+    if torch.isfinite(logits).all().item():
+        return logits
+    raise NonFiniteLogits(f"{where}: the logits hold NaN or inf")
 
 
 def _device_scorer(*tensors):
@@ -26,8 +27,8 @@ def score_tokens(logits, ids, keep_targets):
     if _device_scorer(logits):
         from ..ops.kernels import score_rows
         return score_rows(logits[:-1], targets=tgt)["logprob"].cpu()
-    lp = torch.log_softmax(logits[:-1].double(), -1)
-    return lp.gather(1, tgt[:, None])[:, 0].cpu()
+    logp = logits[:-1].double().log_softmax(-1)
+    return logp[torch.arange(tgt.shape[0], device=logp.device), tgt].cpu()
 
 
 def mean_nll(logits, ids, keep_targets):
