@@ -27,37 +27,64 @@ def plan_path():
     return TX.data_root() / "niah-general-dev" / "plan.json"
 
 
+class _Haystacks:
+    """Token ids of each K20 cell's haystack for one tokenizer, encoded on first use."""
+
+    def __init__(self, tok, text_of, lengths):
+        self.tok, self.text_of = tok, text_of
+        self.cells = {(c["length"], c["source"]): c for c in TX.k20_cells(text_of, lengths=lengths)}
+        self.ids = {}
+
+    def __call__(self, L, src):
+        key = (L, src)
+        if key not in self.ids:
+            c = self.cells[key]
+            hay = TX.encode(self.tok, self.text_of[src][c["char_start"]:c["char_end"]])
+            if len(hay) < L:
+                raise RuntimeError(f"niahg haystack {L}-{src}: {len(hay)} tokens < {L}")
+            self.ids[key] = hay
+        return self.ids[key]
+
+
+def _needle(tok, needle_text, value):
+    """(needle ids, [first, last] token of the value inside them, the lead-in text before the value)."""
+    at = needle_text.index(value)
+    enc = tok(needle_text, add_special_tokens=False, return_offsets_mapping=True)
+    stop = at + len(value)
+    inside = [t for t, (a, b) in enumerate(enc["offset_mapping"]) if a < stop and b > at]
+    return list(enc["input_ids"]), (inside[0], inside[-1]), needle_text[:at].strip()
+
+
+def _question(p, fmt, lead):
+    if fmt == "chat":
+        return p["question"]
+    first = p["question"].split("?")[0]
+    return f"{first}? {lead}"
+
+
 def prompts(tok, fmt="raw", types=TYPES, plan=None, text_of=None, lengths=TX.NIAH_LENGTHS):
-    """lengths: the K20 generator's length grid (its draws depend on the whole grid)."""
-    plan = json.loads(Path(plan_path()).read_text()) if plan is None else plan
-    plan = [p for p in plan if p["type"] in types]
+    """The plan's prompts for this tokenizer. lengths: the K20 generator's length grid (its draws depend on the
+    whole grid)."""
+    if plan is None:
+        plan = json.loads(Path(plan_path()).read_text())
     text_of = TX.corpus() if text_of is None else text_of
-    cells = {(c["length"], c["source"]): c for c in TX.k20_cells(text_of, lengths=lengths)}
+    hay = _Haystacks(tok, text_of, lengths)
     head, tail = TX._frame(tok, fmt)
-    hay = {}
     out = []
-    for p in plan:
-        L, src, value, needle_text = p["length"], p["source"], p["value"], p["needle_text"]
-        c = cells[(L, src)]
-        if (L, src) not in hay:
-            hay[(L, src)] = TX.encode(tok, text_of[src][c["char_start"]:c["char_end"]])
-            if len(hay[(L, src)]) < L:
-                raise RuntimeError(f"niahg haystack {L}-{src}: {len(hay[(L, src)])} tokens < {L}")
-        v0 = needle_text.index(value)
-        lead = needle_text[:v0].strip()
-        q_text = p["question"] if fmt == "chat" else p["question"].split("?")[0] + "? " + lead
-        enc = tok(needle_text, add_special_tokens=False, return_offsets_mapping=True)
-        needle = list(enc["input_ids"])
-        vt = [i for i, (s, e) in enumerate(enc["offset_mapping"]) if s < v0 + len(value) and e > v0]
-        q = TX.encode(tok, q_text)
-        body = hay[(L, src)][:L - len(needle) - len(q)]
-        at = int(p["depth"] * len(body))
-        ids = head + body[:at] + needle + body[at:] + q + tail
-        ns = len(head) + at
-        out.append(dict(name=p["name"], type=p["type"], subtype=p.get("subtype"), length=L, source=src,
-                        depth=p["depth"], key=p["key"], value=value, format=fmt, char_start=c["char_start"],
-                        char_end=c["char_end"], needle_start=ns, needle_end=ns + len(needle),
-                        value_start=ns + vt[0], value_end=ns + vt[-1] + 1, ids=ids))
+    for p in (row for row in plan if row["type"] in types):
+        L, src = p["length"], p["source"]
+        needle, (v_first, v_last), lead = _needle(tok, p["needle_text"], p["value"])
+        q = TX.encode(tok, _question(p, fmt, lead))
+        body = hay(L, src)[:L - len(needle) - len(q)]
+        cut = int(p["depth"] * len(body))
+        start = len(head) + cut
+        c = hay.cells[L, src]
+        rec = {"name": p["name"], "type": p["type"], "subtype": p.get("subtype"), "length": L, "source": src,
+               "depth": p["depth"], "key": p["key"], "value": p["value"], "format": fmt,
+               "char_start": c["char_start"], "char_end": c["char_end"], "needle_start": start,
+               "needle_end": start + len(needle), "value_start": start + v_first, "value_end": start + v_last + 1}
+        rec["ids"] = head + body[:cut] + needle + body[cut:] + q + tail
+        out.append(rec)
     return out
 
 
@@ -74,63 +101,68 @@ _WORD = re.compile(r"[\w'-]")
 
 
 def reply_text(text):
-    for end in _END:
-        text = text.split(end)[0]
-    return _SPECIAL.sub(" ", _THINK.sub(" ", text))
+    """The reply up to its first end-of-turn token, with think blocks and special tokens blanked."""
+    cut = min((text.find(e) for e in _END if e in text), default=len(text))
+    return _SPECIAL.sub(" ", _THINK.sub(" ", text[:cut]))
+
+
+def _unquote(t):
+    return t.strip().strip(_QUOTES).strip()
 
 
 def extract(text):
-    lines = [ln.strip() for ln in reply_text(text).splitlines() if ln.strip()]
-    if not lines:
+    """The answer: the reply's first non-empty line, unquoted, with a restated lead-in dropped."""
+    first = next((ln.strip() for ln in reply_text(text).splitlines() if ln.strip()), "")
+    if not first:
         return ""
-    a = lines[0].lstrip("-•> ").strip().strip(_QUOTES).strip()
-    return _LEAD.sub("", a).strip().strip(_QUOTES).strip()
+    return _unquote(_LEAD.sub("", _unquote(first.lstrip("-•> "))))
+
+
+def _tail_clean(t):
+    return t.rstrip(".,;:!?").strip(_QUOTES)
 
 
 def normalize(s, typ):
+    """Comparable form of an answer or a value of one needle type."""
     s = unicodedata.normalize("NFKC", s).translate(_DASHES)
     if typ == "ident":
-        s = re.sub(r"\(\)$", "", s.strip().strip(_QUOTES).strip())
-        return s.rstrip(".,;:!?").strip(_QUOTES)
+        return _tail_clean(re.sub(r"\(\)$", "", _unquote(s)))
     if typ == "hexid":
-        s = re.sub(r"\s+", "", s.casefold().strip().strip(_QUOTES))
-        return s.rstrip(".,;:!?").strip(_QUOTES)
-    s = "".join(c if c.isalnum() or c in " -'" or c.isspace() else " " for c in s.casefold())
-    s = re.sub(r"(?<![a-z0-9])['-]|['-](?![a-z0-9])", " ", s)     # only inner hyphens / apostrophes survive
-    return re.sub(r"\s+", " ", s).strip()
+        return _tail_clean(re.sub(r"\s+", "", s.casefold().strip().strip(_QUOTES)))
+    kept = "".join(ch if (ch.isalnum() or ch.isspace() or ch in "-'") else " " for ch in s.casefold())
+    kept = re.sub(r"(?<![a-z0-9])['-]|['-](?![a-z0-9])", " ", kept)     # only inner hyphens / apostrophes stay
+    return " ".join(kept.split())
 
 
 def edit_distance(a, b, cap=3):
-    """Levenshtein distance, or cap + 1 once the lengths alone differ by more than cap."""
+    """Levenshtein distance; cap + 1 as soon as the lengths alone differ by more than cap."""
     if abs(len(a) - len(b)) > cap:
         return cap + 1
-    row = list(range(len(b) + 1))
-    for i, ca in enumerate(a, 1):
-        nxt = [i]
-        for j, cb in enumerate(b, 1):
-            nxt.append(min(row[j] + 1, nxt[j - 1] + 1, row[j - 1] + (ca != cb)))
-        row = nxt
-    return row[-1]
+    prev = list(range(len(b) + 1))
+    for i in range(1, len(a) + 1):
+        cur = [i] + [0] * len(b)
+        for j in range(1, len(b) + 1):
+            cur[j] = min(prev[j] + 1, cur[j - 1] + 1, prev[j - 1] + (a[i - 1] != b[j - 1]))
+        prev = cur
+    return prev[len(b)]
+
+
+def _miss_form(got, want):
+    if not got:
+        return "none"
+    if want.startswith(got):
+        return "truncated"
+    return "near" if edit_distance(got, want) <= 2 else "wrong"
 
 
 def score(text, value, typ, fmt):
-    """dict(correct, form, answer); form: ok / none / truncated / near / wrong."""
-    ans = extract(text)
-    cut = re.split(r"\s", ans, maxsplit=1)[0] if (fmt != "chat" and typ == "hexid") else ans
-    na, nv = normalize(cut, typ), normalize(value, typ)
+    """{"correct", "form", "answer"}; form is ok, none, truncated, near or wrong."""
+    answer = extract(text)
+    compared = answer.split(None, 1)[0] if (answer and fmt != "chat" and typ == "hexid") else answer
+    got, want = normalize(compared, typ), normalize(value, typ)
     if fmt == "chat":
-        ok = na == nv
-    else:
-        ok = na.startswith(nv) and not _WORD.match(na[len(nv):len(nv) + 1])
-        na = na[:len(nv)]
-    if ok:
-        form = "ok"
-    elif not na:
-        form = "none"
-    elif nv.startswith(na):
-        form = "truncated"
-    elif edit_distance(na, nv) <= 2:
-        form = "near"
-    else:
-        form = "wrong"
-    return dict(correct=ok, form=form, answer=ans)
+        ok = got == want
+    else:                                    # a completion runs on: the value must end at a word boundary
+        ok = got.startswith(want) and _WORD.match(got[len(want):len(want) + 1]) is None
+        got = got[:len(want)]
+    return {"correct": ok, "form": "ok" if ok else _miss_form(got, want), "answer": answer}
