@@ -1,9 +1,11 @@
-"""Atomic result files with sha256 sidecars and a results-tree hash (code/finals/lib/atomic.py).
+"""Result files that are either complete or absent, each with a sha256 sidecar, and a hash over a results tree
+(the file discipline of code/finals/lib/atomic.py).
 
-write_result(path, obj): JSON to a temporary file beside the target, fsync, read back (the bytes must match what
-was written), rename, fsync the directory; then the same for '<path>.sha256' in `sha256sum -c` format. A file is
-finished only when it and a matching sidecar exist. treehash(root): sha256 over the sorted '<relpath> <sha256>'
-lines of every regular file (hidden files and sidecars excluded), for receipts naming exactly which bytes moved.
+write_result(path, obj) writes the JSON through write_bytes: a temporary file in the target's folder, synced, read
+back and compared byte for byte, renamed over the target, then the folder synced. '<path>.sha256' (sha256sum
+format) is written the same way afterwards, so a file counts as finished only when both exist and agree.
+treehash(root) hashes the sorted '<relative path> <sha256>' lines of every regular file under root (hidden files
+and sidecars left out), so that a receipt can name exactly which bytes moved.
 
     python -m ridgefill_data_b200.utils.atomic treehash DIR | sidecar FILE | check FILE...
 """
@@ -17,9 +19,11 @@ import sys
 import tempfile
 from pathlib import Path
 
+_HEX = frozenset("0123456789abcdef")
+
 
 class AtomicWriteError(RuntimeError):
-    """The bytes did not read back as written."""
+    """What was written did not read back identically."""
 
 
 def sha256_file(path, bufsize=1 << 20):
@@ -30,65 +34,80 @@ def sha256_file(path, bufsize=1 << 20):
     return digest.hexdigest()
 
 
+def _fsync_folder(folder):
+    handle = os.open(folder, os.O_RDONLY)
+    try:
+        os.fsync(handle)
+    finally:
+        os.close(handle)
+
+
+def _write_checked(tmp, data, target):
+    with open(tmp, "wb") as out:
+        out.write(data)
+        out.flush()
+        os.fsync(out.fileno())
+    if Path(tmp).read_bytes() != data:
+        raise AtomicWriteError(f"{target}: the temporary file did not read back as written")
+
+
 def write_bytes(path, data):
+    """Replace `path` with `data` so that readers see the old file or the new one, never a mix."""
     path = Path(path)
     folder = path.parent
     folder.mkdir(parents=True, exist_ok=True)
     fd, tmp = tempfile.mkstemp(prefix="." + path.name + ".", dir=folder)
+    os.close(fd)
     try:
-        with os.fdopen(fd, "wb") as f:
-            f.write(data)
-            f.flush()
-            os.fsync(f.fileno())
-        with open(tmp, "rb") as f:
-            if f.read() != data:
-                raise AtomicWriteError(f"{path}: read-back differs from the written bytes")
+        _write_checked(tmp, data, path)
         os.replace(tmp, path)
     except BaseException:
-        if os.path.exists(tmp):
-            os.unlink(tmp)
+        Path(tmp).unlink(missing_ok=True)
         raise
-    dfd = os.open(path.parent, os.O_RDONLY)
-    try:
-        os.fsync(dfd)
-    finally:
-        os.close(dfd)
+    _fsync_folder(folder)
 
 
 def sidecar_line(path, digest):
     return f"{digest}  {Path(path).name}\n"
 
 
+def _sidecar(path):
+    return Path(f"{path}.sha256")
+
+
 def write_result(path, obj):
-    """JSON + sidecar, atomically; returns the sha256."""
+    """The JSON of obj and its sidecar, each written atomically; returns the sha256."""
     data = (json.dumps(obj, sort_keys=True, indent=1) + "\n").encode()
     write_bytes(path, data)
     digest = hashlib.sha256(data).hexdigest()
-    write_bytes(f"{path}.sha256", sidecar_line(path, digest).encode())
+    write_bytes(_sidecar(path), sidecar_line(path, digest).encode())
     return digest
 
 
 def read_sidecar(path):
-    """The sha256 a sidecar records for path, or None (missing or malformed)."""
-    sc = Path(f"{path}.sha256")
-    if not sc.exists():
+    """The sha256 that the sidecar of `path` records, or None when it is missing or malformed."""
+    side = _sidecar(path)
+    if not side.exists():
         return None
-    try:
-        digest, name = sc.read_text().splitlines()[0].split("  ", 1)
-    except (ValueError, IndexError):
+    lines = side.read_text().splitlines()
+    if not lines or "  " not in lines[0]:
         return None
-    if name != Path(path).name or len(digest) != 64 or set(digest) - set("0123456789abcdef"):
-        return None
-    return digest
+    digest, _, name = lines[0].partition("  ")
+    well_formed = len(digest) == 64 and set(digest) <= _HEX and name == Path(path).name
+    return digest if well_formed else None
 
 
 def finished(path):
-    p = Path(path)
-    return p.exists() and read_sidecar(p) is not None and read_sidecar(p) == sha256_file(p)
+    """The file exists and its sidecar records its current sha256."""
+    path = Path(path)
+    if not path.exists():
+        return False
+    recorded = read_sidecar(path)
+    return recorded is not None and recorded == sha256_file(path)
 
 
 def refresh_sidecar(path):
-    write_bytes(f"{path}.sha256", sidecar_line(path, sha256_file(path)).encode())
+    write_bytes(_sidecar(path), sidecar_line(path, sha256_file(path)).encode())
 
 
 def treehash(root):
@@ -104,20 +123,20 @@ def treehash(root):
 def main(argv=None):
     ap = argparse.ArgumentParser(prog="ridgefill_data_b200.utils.atomic", description="atomic result files")
     sub = ap.add_subparsers(required=True, dest="cmd")
-    for name in ("treehash", "sidecar"):
-        sub.add_parser(name).add_argument("path")
+    sub.add_parser("treehash").add_argument("path")
+    sub.add_parser("sidecar").add_argument("path")
     sub.add_parser("check").add_argument("paths", nargs="+")
     a = ap.parse_args(argv)
     if a.cmd == "treehash":
         print(treehash(a.path))
-    elif a.cmd == "sidecar":
+        return 0
+    if a.cmd == "sidecar":
         refresh_sidecar(a.path)
-    else:
-        bad = [p for p in a.paths if not finished(p)]
-        for p in bad:
-            print(f"MISMATCH {p}: no sidecar or it does not match", file=sys.stderr)
-        return 2 if bad else 0
-    return 0
+        return 0
+    unfinished = [p for p in a.paths if not finished(p)]
+    for p in unfinished:
+        print(f"MISMATCH {p}: no sidecar or it does not match", file=sys.stderr)
+    return 2 if unfinished else 0
 
 
 if __name__ == "__main__":
