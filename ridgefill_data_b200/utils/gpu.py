@@ -44,20 +44,29 @@ def setup(env=None, torch=None):
     torch.backends.cudnn.allow_tf32 = False
     if deterministic:
         torch.use_deterministic_algorithms(True, warn_only=True)
-    cap = float(env.get("RF_VRAM_CAP_GIB", 0)) * 2**30 or p.total_memory
+    gib = 2 ** 30
+    total = p.total_memory
+    cap = float(env.get("RF_VRAM_CAP_GIB", 0)) * gib or total
     torch.cuda.set_device(dev_index)
-    torch.cuda.set_per_process_memory_fraction(min(1.0, cap / p.total_memory), dev_index)
-    return torch.device(f"cuda:{dev_index}"), dict(
-        deterministic=deterministic, vendor="nvidia", name=p.name, arch=f"sm_{p.major}{p.minor}",
-        sms=p.multi_processor_count, total_gib=round(p.total_memory / 2**30, 2), cap_gib=cap / 2**30,
-        runtime=f"cuda {torch.version.cuda}", local_rank=local, world=world)
+    torch.cuda.set_per_process_memory_fraction(min(1.0, cap / total), dev_index)
+    info = {"deterministic": deterministic, "vendor": "nvidia", "name": p.name,
+            "arch": f"sm_{p.major}{p.minor}", "sms": p.multi_processor_count}
+    info.update(total_gib=round(total / gib, 2), cap_gib=cap / gib, runtime="cuda " + str(torch.version.cuda),
+                local_rank=local, world=world)
+    return torch.device("cuda", dev_index), info
+
+
+def _gib(device, counter):
+    if device.type != "cuda":
+        return 0.0
+    return counter(device) / 2 ** 30
 
 
 def peak_gib(device):
     import torch
-    return torch.cuda.max_memory_allocated(device) / 2**30 if device.type == "cuda" else 0.0
+    return _gib(device, torch.cuda.max_memory_allocated)
 
 
 def used_gib(device):
     import torch
-    return torch.cuda.memory_allocated(device) / 2**30 if device.type == "cuda" else 0.0
+    return _gib(device, torch.cuda.memory_allocated)
