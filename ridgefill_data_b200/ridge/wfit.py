@@ -28,49 +28,63 @@ RANK_FLOOR = 0.1
 def rank_fraction(x):
     """Mean rank of each value among x (0-based, ties share their mean rank) divided by len(x)."""
     _, inverse, counts = torch.unique(x, return_inverse=True, return_counts=True)
-    mean_rank = counts.cumsum(0) - (counts + 1) / 2
-    return mean_rank.double()[inverse] / x.numel()
+    first_rank = counts.cumsum(0) - counts                 # 0-based rank of each distinct value's first copy
+    shared = first_rank + (counts - 1) / 2
+    return shared.double()[inverse] / x.numel()
+
+
+_SHAPE_FNS = {
+    "qfp": lambda q: q,
+    "sqrt": lambda q: q.clamp_min(0).sqrt(),
+    "rank": lambda q: (1 - rank_fraction(q)).clamp_min(RANK_FLOOR).reciprocal(),
+}
 
 
 def row_weights(qfp, shape):
-    """Fit weights [n] fp64 of one document's rows from their qfp [n]."""
+    """Fit weights [n] fp64 of one document's rows from their qfp [n]: the shape of rows 1.. scaled to mean 1,
+    and weight 1 for row 0."""
+    if shape not in _SHAPE_FNS:
+        raise ValueError(f"unknown weight shape {shape!r} (one of {SHAPES})")
     q = qfp.double().cpu()
-    if shape == "qfp":
-        s = q[1:]
-    elif shape == "sqrt":
-        s = q[1:].clamp_min(0).sqrt()
-    elif shape == "rank":
-        s = 1 / (1 - rank_fraction(q[1:])).clamp_min(RANK_FLOOR)
-    else:
-        raise ValueError(f"weight shape {shape!r} not in {SHAPES}")
-    w = torch.ones_like(q)
-    if s.numel() and s.mean() > 0:
-        w[1:] = s / s.mean()
-    return w
+    shaped = _SHAPE_FNS[shape](q[1:])
+    weights = torch.ones_like(q)
+    if shaped.numel() > 0:
+        mean = shaped.mean()
+        if mean > 0:
+            weights[1:] = shaped / mean
+    return weights
+
+
+class _QfpTap:
+    """A forward hook that sums, over the attention layers below the split, the mass each row receives from
+    later rows; from the split on it hands each late layer's input rows to `late` with the finished qfp."""
+
+    def __init__(self, model, n, split, stride, late):
+        self.model, self.n, self.split, self.stride, self.late = model, n, split, stride, late
+        self.pos = torch.arange(n, device=model.device)
+        self.received = torch.zeros(n, dtype=torch.float64)
+        self.qfp = None
+
+    def __call__(self, i, h):
+        if i == "final":
+            return
+        m = self.model
+        if i < self.split:
+            if m.layer_types[i] == "attn":
+                x = m.in_norm(h, m.W[i]["ln1"])
+                keys, _ = IM.attn_kv(m, i, x, self.pos)
+                self.received.add_(IM.received_mass(m.queries(i, x, self.pos), keys, m.scale, stride=self.stride))
+            return
+        if self.qfp is None:
+            self.qfp = per_later_token(self.received, self.n)
+        self.late(i, h, self.qfp)
 
 
 @torch.no_grad()
 def doc_pass(model, ids, split, stride, late):
-    """One exact forward of a document. By layer `split` its qfp [n] (fp64 CPU) is complete; late(i, h, qfp)
-    then sees every late layer's input rows h (i >= split)."""
-    n = ids.shape[0]
-    pos = torch.arange(n, device=model.device)
-    recv = torch.zeros(n, dtype=torch.float64)
-    qfp = []
-
-    def hook(i, h):
-        if i == "final":
-            return
-        if i < split and model.layer_types[i] == "attn":
-            x = model.in_norm(h, model.W[i]["ln1"])
-            q = model.queries(i, x, pos)
-            k, _ = IM.attn_kv(model, i, x, pos)
-            recv.add_(IM.received_mass(q, k, model.scale, stride=stride))
-        if i >= split:
-            if not qfp:
-                qfp.append(per_later_token(recv, n))
-            late(i, h, qfp[0])
-    model.forward_exact(ids.to(model.device), hook=hook)
+    """One exact forward of a document. By layer `split` its qfp [n] (host fp64) is complete; late(i, h, qfp)
+    then sees the input rows h of every late layer i >= split."""
+    model.forward_exact(ids.to(model.device), hook=_QfpTap(model, ids.shape[0], split, stride, late))
 
 
 def capture_weighted(model, docs, split, shape="rank", stride=1, device=None, log=print):
