@@ -136,16 +136,15 @@ def attend(q, k, v, scale):
 def causal_conv(x, state, weight):
     """Depthwise causal conv (kernel K) + SiLU continuing from `state` [K-1, C] (None: zeros).
     x [n, C]; weight [C, K]. Returns (out [n, C] in x.dtype, new state [K-1, C])."""
-    kk = weight.shape[1]
-    if state is None:
-        state = x.new_zeros(kk - 1, x.shape[1])
-    xx = torch.cat((state.to(x.dtype), x), 0)
-    n = x.shape[0]
-    acc = torch.zeros(n, x.shape[1], dtype=torch.float32, device=x.device)
-    wf = weight.float()
-    for j in range(kk):
-        acc += xx[j:j + n].float() * wf[:, j]
-    return F.silu(acc).to(x.dtype), xx[n:].clone() if n >= kk - 1 else xx[-(kk - 1):].clone()
+    n, channels = x.shape
+    width = weight.shape[1]
+    history = x.new_zeros(width - 1, channels) if state is None else state.to(x.dtype)
+    window = torch.cat([history, x], 0)                          # [width - 1 + n, C]
+    taps = weight.float()
+    acc = torch.zeros(n, channels, dtype=torch.float32, device=x.device)
+    for j in range(width):                                       # oldest tap first (the accumulation order)
+        acc += window[j:j + n].float() * taps[:, j]
+    return F.silu(acc).to(x.dtype), window[window.shape[0] - (width - 1):].clone()
 
 
 def unit_lower_inverse(a):
@@ -162,6 +161,12 @@ def unit_lower_inverse(a):
     return t
 
 
+def _initial_state(state, h, dk, dv, device):
+    if state is None:
+        return torch.zeros(h, dk, dv, dtype=torch.float32, device=device)
+    return state.float().clone()
+
+
 def delta_rule(q, k, v, g, beta, state=None, chunk=64, checkpoint_every=None, offset=0, need_out=True):
     """Chunked gated delta rule in fp32, continuing from `state`.
 
@@ -174,26 +179,26 @@ def delta_rule(q, k, v, g, beta, state=None, chunk=64, checkpoint_every=None, of
     multiples of it. Returns (out [H, n, dv] fp32 or None, state [H, dk, dv], checkpoints)."""
     h, n, dk = k.shape
     dv = v.shape[-1]
-    S = torch.zeros(h, dk, dv, dtype=torch.float32, device=k.device) if state is None else state.float().clone()
+    if checkpoint_every and checkpoint_every % chunk:
+        raise ValueError(f"checkpoint_every={checkpoint_every} must be a multiple of the chunk ({chunk})")
+    S = _initial_state(state, h, dk, dv, k.device)
     out = torch.empty(h, n, dv, dtype=torch.float32, device=k.device) if need_out else None
     cks = {}
-    if checkpoint_every:
-        assert checkpoint_every % chunk == 0
     tri = torch.ones(chunk, chunk, dtype=torch.bool, device=k.device).tril()
     for c0 in range(0, n, chunk):
         c1 = min(n, c0 + chunk)
         m = c1 - c0
-        pad = chunk - m
 
         def take(x):
-            x = x[:, c0:c1].float()
-            if pad:
-                x = F.pad(x, (0, 0, 0, pad) if x.dim() == 3 else (0, pad))
-            return x
+            part = x[:, c0:c1].float()
+            if m == chunk:
+                return part
+            return F.pad(part, (0, chunk - m) if part.dim() == 2 else (0, 0, 0, chunk - m))
 
-        qc, kc, vc, gc, bc = take(q), take(k), take(v), take(g), take(beta)
+        qc, kc, vc, gc, bc = (take(x) for x in (q, k, v, g, beta))
         gam = gc.cumsum(-1)
-        decay = torch.where(tri, gam[:, :, None] - gam[:, None, :], torch.full_like(gam[:, :, None].expand(-1, -1, chunk), -math.inf)).exp()
+        rel = gam[:, :, None] - gam[:, None, :]
+        decay = torch.where(tri, rel, torch.full_like(rel, -math.inf)).exp()
         a = (bc[:, :, None] * (kc @ kc.transpose(-1, -2)) * decay).tril(-1)
         t = unit_lower_inverse(a)
         u = t @ (bc[:, :, None] * vc)
@@ -214,14 +219,14 @@ def delta_rule_recurrent(q, k, v, g, beta, state=None):
     """Token-by-token gated delta rule (the definition; decode and tests)."""
     h, n, dk = k.shape
     dv = v.shape[-1]
-    S = torch.zeros(h, dk, dv, dtype=torch.float32, device=k.device) if state is None else state.float().clone()
+    S = _initial_state(state, h, dk, dv, k.device)
     out = torch.empty(h, n, dv, dtype=torch.float32, device=k.device)
     for t in range(n):
-        S = S * g[:, t].float().exp()[:, None, None]
-        kt, vt = k[:, t].float(), v[:, t].float()
-        err = (vt - torch.einsum("hkv,hk->hv", S, kt)) * beta[:, t].float()[:, None]
-        S = S + kt[:, :, None] * err[:, None, :]
-        out[:, t] = torch.einsum("hkv,hk->hv", S, q[:, t].float())
+        S = S * g[:, t].float().exp()[:, None, None]                     # decay
+        key, val = k[:, t].float(), v[:, t].float()
+        correction = (val - torch.einsum("hkv,hk->hv", S, key)) * beta[:, t].float()[:, None]
+        S = S + key[:, :, None] * correction[:, None, :]                 # delta-rule write
+        out[:, t] = torch.einsum("hkv,hk->hv", S, q[:, t].float())       # read
     return out, S
 
 
