@@ -52,43 +52,57 @@ class RidgeStats:
     """Accumulators for one split over its late layers (fp64, on `device`)."""
 
     def __init__(self, split, layers, dim, device="cpu", out_dim=None):
-        self.split, self.layers, self.dim, self.device = split, list(layers), dim, torch.device(device)
-        out_dim = dim if out_dim is None else out_dim
-        f64 = dict(dtype=torch.float64, device=self.device)
+        self.split = split
+        self.layers = list(layers)
+        self.dim = dim
+        self.device = torch.device(device)
+        width = dim if out_dim is None else out_dim
+
+        def zeros(*shape):
+            return torch.zeros(*shape, dtype=torch.float64, device=self.device)
+
         self.n = 0.0
-        self.cx = None
-        self.cy = {}
-        self.sx = torch.zeros(dim, **f64)
-        self.sxx = torch.zeros(dim, dim, **f64)
-        self.sy = {i: torch.zeros(out_dim, **f64) for i in self.layers}
-        self.sxy = {i: torch.zeros(dim, out_dim, **f64) for i in self.layers}
-        self._x = None
+        self.cx, self.cy = None, {}
+        self.sx, self.sxx = zeros(dim), zeros(dim, dim)
+        self.sy = {i: zeros(width) for i in self.layers}
+        self.sxy = {i: zeros(dim, width) for i in self.layers}
+        self._x = self._w = None
+        self._block = BLOCK
+
+    def _weighted(self, centred, start):
+        """Centred rows times their row weights (unchanged when unweighted)."""
+        if self._w is None:
+            return centred
+        return centred * self._w[start:start + centred.shape[0]]
+
+    def _centred_x(self, start, device):
+        return self._x[start:start + self._block].float() - self.cx.to(device)
 
     @torch.no_grad()
     def begin(self, x, block=BLOCK, w=None):
-        """Boundary rows x [n, d] of one document; follow with add_layer for every layer."""
+        """Split-layer rows x [n, d] of one document; add_layer then takes each late layer's rows."""
         if self.cx is None:
-            self.cx = x[:block].float().mean(0)
+            self.cx = x[:block].float().mean(0)          # the shift: the first block's mean
         self._x, self._block = x, block
-        self._w = None if w is None else w.to(x.device, torch.float32)[:, None]
-        self.n += x.shape[0] if w is None else float(w.double().sum())
-        for r in range(0, x.shape[0], block):
-            xc = x[r:r + block].float() - self.cx.to(x.device)
-            xw = xc if self._w is None else xc * self._w[r:r + xc.shape[0]]
+        self._w = None if w is None else w.to(x.device, torch.float32).unsqueeze(1)
+        self.n += float(w.double().sum()) if w is not None else x.shape[0]
+        for start in range(0, x.shape[0], block):
+            xc = self._centred_x(start, x.device)
+            xw = self._weighted(xc, start)
             self.sx += xw.sum(0).double().to(self.device)
             cross_acc(self.sxx, xw, xc, block)
 
     @torch.no_grad()
     def add_layer(self, i, y):
+        """Layer i's true input rows y [n, d_out] for the rows given to begin()."""
+        block = self._block
         if i not in self.cy:
-            self.cy[i] = y[:self._block].float().mean(0)
-        for r in range(0, y.shape[0], self._block):
-            xc = self._x[r:r + self._block].float() - self.cx.to(y.device)
-            xw = xc if self._w is None else xc * self._w[r:r + xc.shape[0]]
-            yc = y[r:r + self._block].float() - self.cy[i].to(y.device)
-            yw = yc if self._w is None else yc * self._w[r:r + yc.shape[0]]
-            self.sy[i] += yw.sum(0).double().to(self.device)
-            cross_acc(self.sxy[i], xw, yc, self._block)
+            self.cy[i] = y[:block].float().mean(0)
+        for start in range(0, y.shape[0], block):
+            xw = self._weighted(self._centred_x(start, y.device), start)
+            yc = y[start:start + block].float() - self.cy[i].to(y.device)
+            self.sy[i] += self._weighted(yc, start).sum(0).double().to(self.device)
+            cross_acc(self.sxy[i], xw, yc, block)
 
     def add(self, x, ys, block=BLOCK, w=None):
         self.begin(x, block, w)
