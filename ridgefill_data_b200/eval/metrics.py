@@ -16,12 +16,12 @@ def postprocess_pred(text):
 
 def ruler_row(metric, pred, ref):
     """One row's term (0-1) of string_match_all (share of references found) or string_match_part (any found)."""
-    hits = [1.0 if r.lower() in pred.lower() else 0.0 for r in ref]
-    if metric == "string_match_all":
-        return sum(hits) / len(ref)
-    if metric == "string_match_part":
-        return max(hits)
-    raise ValueError(f"unknown RULER metric {metric!r}")
+    text = pred.lower()
+    found = [float(r.lower() in text) for r in ref]
+    combine = {"string_match_all": lambda: sum(found) / len(ref), "string_match_part": lambda: max(found)}
+    if metric not in combine:
+        raise ValueError(f"unknown RULER metric {metric!r}")
+    return combine[metric]()
 
 
 def ruler_score(rows):
@@ -88,22 +88,33 @@ def _sentences(text):
     return [" ".join(p.split()) for p in text.split(".") if len(p) > 0]
 
 
+def _lcs_table(x, y):
+    """lengths[i][j] = LCS length of x[:i] and y[:j]."""
+    lengths = [[0] * (len(y) + 1)]
+    for xi in x:
+        prev, row = lengths[-1], [0]
+        for j, yj in enumerate(y, 1):
+            row.append(prev[j - 1] + 1 if xi == yj else max(prev[j], row[j - 1]))
+        lengths.append(row)
+    return lengths
+
+
 def _lcs_words(x, y):
-    n, m = len(x), len(y)
-    tab = [[0] * (m + 1) for _ in range(n + 1)]
-    for i in range(1, n + 1):
-        for j in range(1, m + 1):
-            tab[i][j] = tab[i - 1][j - 1] + 1 if x[i - 1] == y[j - 1] else max(tab[i - 1][j], tab[i][j - 1])
-    out, i, j = [], n, m
-    while i > 0 and j > 0:
+    """One longest common subsequence of word lists x and y, read back from the end (on a tie the step drops a
+    word of y, as the official ROUGE-L scorer does)."""
+    lengths = _lcs_table(x, y)
+    words = []
+    i, j = len(x), len(y)
+    while i and j:
         if x[i - 1] == y[j - 1]:
-            out.append(x[i - 1])
-            i, j = i - 1, j - 1
-        elif tab[i - 1][j] > tab[i][j - 1]:
+            words.append(x[i - 1])
+            i -= 1
+            j -= 1
+        elif lengths[i - 1][j] > lengths[i][j - 1]:
             i -= 1
         else:
             j -= 1
-    return out
+    return words
 
 
 def rouge_l(hyp, ref):
