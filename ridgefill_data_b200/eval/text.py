@@ -149,42 +149,52 @@ def eos_ids(model_path, tok):
 CHAT_ASK = "\n\nContinue the text above from exactly where it stops."
 
 
+def _grade_builder(tok, fmt):
+    """(head ids kept when capping, text -> prompt ids) of one graded-prompt format."""
+    bos = bos_ids(tok)
+    if fmt == "raw":
+        return bos, lambda text: bos + encode(tok, text)
+    if fmt != "chat":
+        raise ValueError(f"unknown grade format {fmt!r}")
+    user_open, reply_open = chat_pieces(tok)
+    ask = encode(tok, CHAT_ASK)
+
+    def chat(text):
+        doc = encode(tok, text)
+        cut = len(doc) - SCORED
+        return user_open + doc[:cut] + ask + reply_open + doc[cut:]
+    return user_open, chat
+
+
+def _helps_table():
+    f = inputs_dir() / "swap_summary.json"
+    if not f.exists():
+        return {}
+    return {row["name"]: row["helps"] for row in json.loads(f.read_text())["rows"]}
+
+
 def grade_prompts(tok, fmt="raw", drop_bos=False, plan=None, helps=None):
     """The graded prompts: scored on the last SCORED tokens, novel tokens primary.
     raw: BOS + the text. chat: the text minus its last SCORED tokens plus CHAT_ASK as the user turn, then the
     assistant header, then those SCORED tokens as the reply (joined as ids, so the scored ids equal raw's).
     Capping drops from the left after the head. drop_bos: the same prompts without their (required) BOS.
     plan / helps default to inputs/plan-grade.json and inputs/swap_summary.json."""
-    if plan is None:
-        plan = json.loads(_need(inputs_dir() / "plan-grade.json").read_text())
-    if helps is None:
-        f = inputs_dir() / "swap_summary.json"
-        helps = {r["name"]: r["helps"] for r in json.loads(f.read_text())["rows"]} if f.exists() else {}
+    plan = json.loads(_need(inputs_dir() / "plan-grade.json").read_text()) if plan is None else plan
+    helps = _helps_table() if helps is None else helps
+    head, build = _grade_builder(tok, fmt)
     bos = bos_ids(tok)
-    if fmt == "raw":
-        head = bos
-
-        def build(text):
-            return bos + encode(tok, text)
-    elif fmt == "chat":
-        head, reply_open = chat_pieces(tok)
-        ask = encode(tok, CHAT_ASK)
-
-        def build(text):
-            doc = encode(tok, text)
-            return head + doc[:-SCORED] + ask + reply_open + doc[-SCORED:]
-    else:
-        raise ValueError(f"unknown grade format {fmt!r}")
     out = []
     for p in plan:
         full = build(p["text"])
         ids = cap(full, head)
         short = build(p["text"][p["short_start"]:])
-        rec = dict(name=p["name"], kind=p["kind"], ids=ids, full_len=len(full), truncated=len(full) > len(ids),
-                   short_ids=short, short_tail_match=short[-SCORED:] == ids[-SCORED:],
-                   novel=novel_mask(ids[1:], SCORED), helps16=helps.get(p["name"]), format=fmt)
+        rec = {"name": p["name"], "kind": p["kind"], "ids": ids, "full_len": len(full),
+               "truncated": len(ids) < len(full), "short_ids": short,
+               "short_tail_match": ids[-SCORED:] == short[-SCORED:], "novel": novel_mask(ids[1:], SCORED),
+               "helps16": helps.get(p["name"]), "format": fmt}
         if drop_bos:
-            if not bos or ids[0] != bos[0] or short[0] != bos[0]:
+            starts_with_bos = bool(bos) and ids[0] == bos[0] and short[0] == bos[0]
+            if not starts_with_bos:
                 raise ValueError(f"drop_bos: prompt {p['name']} does not start with a BOS")
             rec.update(ids=ids[1:], short_ids=short[1:], bos_dropped=True)
         out.append(rec)
@@ -207,17 +217,27 @@ def corpus(root=None):
     return {p.stem: p.read_text() for p in sorted(root.glob("*.txt"))}
 
 
+def _draw_value(rng):
+    return str(rng.randrange(1_000_000, 10_000_000))
+
+
 def k20_cells(text_of, lengths=NIAH_LENGTHS, sources=NIAH_SOURCES):
-    """Per (length, source) cell: the haystack's character range and, per depth, (depth, key, value): one seeded
-    stream of draws, in the generator's order."""
+    """Per (length, source) cell: the haystack's character range and, per depth, (depth, key, value). One seeded
+    stream serves every cell in (length, source) order; per cell it draws the haystack offset, then a key and a
+    value for each depth."""
     rng = random.Random(NIAH_SEED)
     cells = []
     for L in lengths:
+        span = L * CHARS_PER_TOKEN
         for si, src in enumerate(sources):
-            span = L * CHARS_PER_TOKEN
-            start = max(0, len(text_of[src]) - span - si * 1000 - rng.randrange(20000))
-            needles = [(d, rng.choice(NIAH_KEYS), str(rng.randrange(1_000_000, 10_000_000))) for d in NIAH_DEPTHS]
-            cells.append(dict(length=L, source=src, char_start=start, char_end=start + span, needles=needles))
+            back = si * 1000 + rng.randrange(20000)
+            start = max(0, len(text_of[src]) - span - back)
+            needles = []
+            for depth in NIAH_DEPTHS:
+                key = rng.choice(NIAH_KEYS)
+                needles.append((depth, key, _draw_value(rng)))
+            cells.append({"length": L, "source": src, "char_start": start, "char_end": start + span,
+                          "needles": needles})
     return cells
 
 
@@ -257,11 +277,21 @@ def _splice(head, body, sentences):
     return ids, span
 
 
+def _distractors(name, key, depth):
+    """mk4: three other keys at three other depths with fresh values, from the prompt's own seeded stream."""
+    r = random.Random(f"{name}-mk4")
+    keys = r.sample([k for k in NIAH_KEYS if k != key], 3)
+    depths = r.sample([x for x in NIAH_DEPTHS if x != depth], 3)
+    return [(dd, kk, _draw_value(r)) for dd, kk in zip(depths, keys)]
+
+
 def niah_prompts(tok, fmt="raw", variant=None, text_of=None, lengths=NIAH_LENGTHS, sources=NIAH_SOURCES):
     """K20 prompts: haystack tokens, the needle sentence (encoded alone) spliced at int(depth * len(body)), the
     question at the end (raw: ending in 'The special magic number for KEY is'; chat: the user turn with an
     answer-format instruction, then the assistant header). variant 'mk4': plus 3 distractor needles (other keys
     and values) at 3 of the other depths, drawn from a per-prompt RNG so the target is unchanged."""
+    if variant not in (None, "mk4"):
+        raise ValueError(f"unknown NIAH variant {variant!r}")
     text_of = corpus() if text_of is None else text_of
     head, tail = _frame(tok, fmt)
     out = []
@@ -272,25 +302,19 @@ def niah_prompts(tok, fmt="raw", variant=None, text_of=None, lengths=NIAH_LENGTH
             raise RuntimeError(f"NIAH haystack {src}: {len(hay)} tokens < {L}")
         for d, key, value in c["needles"]:
             name = f"niah-{L}-{src}-{int(d * 100)}"
-            placed = [(d, key, value, True)]
-            if variant == "mk4":
-                r2 = random.Random(f"{name}-mk4")
-                keys = r2.sample([k for k in NIAH_KEYS if k != key], 3)
-                depths = r2.sample([x for x in NIAH_DEPTHS if x != d], 3)
-                placed += [(dd, kk, str(r2.randrange(1_000_000, 10_000_000)), False) for dd, kk in zip(depths, keys)]
-            elif variant is not None:
-                raise ValueError(f"unknown NIAH variant {variant!r}")
-            sentences = sorted(((dd, encode(tok, niah_needle(kk, vv)), tgt) for dd, kk, vv, tgt in placed),
+            extra = _distractors(name, key, d) if variant == "mk4" else []
+            placed = [(d, key, value, True)] + [(dd, kk, vv, False) for dd, kk, vv in extra]
+            sentences = sorted(((dd, encode(tok, niah_needle(kk, vv)), target) for dd, kk, vv, target in placed),
                                key=lambda x: x[0])
             q = encode(tok, niah_question(fmt, key))
             body = hay[:L - sum(len(n) for _, n, _ in sentences) - len(q)]
             ids, (start, end) = _splice(head, body, sentences)
-            ids += q + tail
-            rec = dict(name=name, length=L, source=src, depth=d, key=key, value=value, format=fmt,
-                       char_start=c["char_start"], char_end=c["char_end"], needle_start=start, needle_end=end, ids=ids)
+            rec = {"name": name, "length": L, "source": src, "depth": d, "key": key, "value": value, "format": fmt,
+                   "char_start": c["char_start"], "char_end": c["char_end"], "needle_start": start,
+                   "needle_end": end, "ids": ids + q + tail}
             if variant:
-                rec.update(variant=variant, distractors=[dict(depth=dd, key=kk, value=vv)
-                                                         for dd, kk, vv, tgt in placed if not tgt])
+                rec["variant"] = variant
+                rec["distractors"] = [{"depth": dd, "key": kk, "value": vv} for dd, kk, vv in extra]
             out.append(rec)
     return out
 
