@@ -30,38 +30,40 @@ ENGINE_MIN_TAIL = 512   # a block-granular engine never runs a shorter exact tai
 
 @dataclass
 class Arm:
+    """One prefill configuration. Every field past `name` is keyword-only in practice; the JSON arm specs use the
+    same names."""
     name: str
+    # where the approximation starts and how many exact rows end the prompt
     split: int | None = None
     tail: int = 0
+    tail_from: str | None = None                 # "continuation": the tail is the scored continuation
+    # how late layers see the prefix rows
     fill: str = "exact"
-    projector: object = None
-    st: dict | None = None
-    f1: bool = False
-    fill_by_type: dict | None = None
-    kvfold: object = None
-    context: int = 0
-    refresh: int | None = None
-    refresh_projector: object = None
-    tail_bias_from: int | None = None
+    fill_by_type: dict | None = None             # {"attention": fill, "gdn": fill}
+    projector: object = None                     # ridge maps (fill "proj")
+    kvfold: object = None                        # K/V fold maps (fill "kvfold")
+    context: int = 0                             # mixer outputs of this many lower layers join the map input
+    refresh: int | None = None                   # a late layer run in full on the filled rows ...
+    refresh_projector: object = None             # ... feeding the maps fitted at refresh + 1
+    # corrections
+    st: dict | None = None                       # GDN terminal-state corrections {layer: dS}
+    f1: bool = False                             # row 0 reads its exact late inputs
+    tail_bias_from: int | None = None            # add the tail's mean map residual from this layer on
     tail_bias_skip_last: int = 0
-    exact_part: str | None = None
-    rescale: str | None = None
+    rescale: str | None = None                   # K or V norm rescale (see ORACLE_RESCALE / TAIL_RESCALE)
     rescale_skip_last: int = 0
-    tail_from: str | None = None
-    meta: dict = field(default_factory=dict)
+    exact_part: str | None = None                # "k" | "v": that half from the true inputs (a diagnostic)
+    meta: dict = field(default_factory=dict)     # the spec's remaining keys (select, sets, repair, ...)
 
     def __post_init__(self):
         if self.fill not in FILLS:
-            raise ValueError(f"fill {self.fill!r} (one of {FILLS})")
+            raise ValueError(f"arm {self.name}: fill {self.fill!r} is not one of {FILLS}")
         if self.fill_by_type is not None:
             self.fill = "by_type"
 
     def prefix_len(self, n):
-        if self.fill == "exact":
-            return 0
-        if self.fill == "swiftkv_native":
-            return n
-        return max(0, n - self.tail)
+        """Rows [0, P) that are filled rather than run exactly."""
+        return {"exact": 0, "swiftkv_native": n}.get(self.fill, max(0, n - self.tail))
 
     def fills(self):
         """Every fill this arm applies to some late layer."""
