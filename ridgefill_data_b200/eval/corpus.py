@@ -2,13 +2,14 @@
 sets, within-document repetition, near-duplicate rejection and the scored-window cut points of a document.
 
 A gram is N = 50 consecutive whitespace-separated words of decoded text (JSON files contribute each string value on
-its own). Each word gets a stable 64-bit id (blake2b of its UTF-8 bytes), and a gram's fingerprint is a Rabin-Karp
-style polynomial of its word ids modulo 2^64, computed for every window at once with numpy; reference sets of tens
-of millions of grams then fit in sorted uint64 arrays searched with searchsorted.
+its own). Each word gets a stable 64-bit id (the first 8 bytes of a sha256 under this module's domain tag), and a
+gram's fingerprint is the polynomial sum of its word ids in powers of an odd 64-bit constant modulo 2^64, computed
+for every window at once with numpy; reference sets of tens of millions of grams then fit in sorted uint64 arrays.
 """
 from __future__ import annotations
 
 import csv
+from collections import Counter
 import hashlib
 import json
 from pathlib import Path
@@ -16,7 +17,8 @@ from pathlib import Path
 import numpy as np
 
 GRAM = 50
-_MULT = np.uint64(0x100000001B3)          # odd 64-bit multiplier (the FNV prime)
+_MULT = np.uint64(0x9E3779B97F4A7C15)     # odd 64-bit constant (2^64 / golden ratio)
+_TAG = b"ridgefill-b200/word-gram/v1\x00"
 _ids = {}
 
 FRACS = (0.5, 0.75, 1.0)                  # window ends as fractions of the document
@@ -24,40 +26,44 @@ MIN_CUT = 8192                            # the shortest window (tokens)
 GAP = 1024                                # the least distance between two windows' ends
 
 
+def _word_id(word):
+    digest = hashlib.sha256(_TAG + word.encode("utf-8", "surrogatepass")).digest()
+    return int.from_bytes(digest[:8], "big")
+
+
 def word_ids(words):
-    out = np.empty(len(words), np.uint64)
-    for i, w in enumerate(words):
-        v = _ids.get(w)
+    """Stable 64-bit ids [len(words)] (uint64), cached per distinct word."""
+    ids = [_ids.get(w) for w in words]
+    for i, v in enumerate(ids):
         if v is None:
-            v = _ids[w] = int.from_bytes(hashlib.blake2b(w.encode("utf-8", "surrogatepass"), digest_size=8).digest(),
-                                         "little")
-        out[i] = v
-    return out
+            ids[i] = _ids.setdefault(words[i], _word_id(words[i]))
+    return np.array(ids, dtype=np.uint64)
 
 
 def grams(text, n=GRAM):
     """Fingerprints of every word n-gram of text, in order."""
-    w = word_ids(text.split())
-    m = len(w) - n + 1
-    if m <= 0:
+    ids = word_ids(text.split())
+    windows = len(ids) - n + 1
+    if windows <= 0:
         return np.zeros(0, np.uint64)
-    h = np.zeros(m, np.uint64)
+    acc = np.zeros(windows, np.uint64)
     with np.errstate(over="ignore"):
-        for k in range(n):
-            h = h * _MULT + w[k:k + m]
-    return h
+        for offset in range(n):                     # Horner's rule over the window, all windows at once
+            acc = acc * _MULT + ids[offset:offset + windows]
+    return acc
 
 
 def strings_of(obj):
-    """Every string value of a parsed JSON object (keys excluded)."""
-    if isinstance(obj, str):
-        yield obj
-    elif isinstance(obj, dict):
-        for v in obj.values():
-            yield from strings_of(v)
-    elif isinstance(obj, list):
-        for v in obj:
-            yield from strings_of(v)
+    """Every string value of a parsed JSON object (keys excluded), depth first in document order."""
+    stack = [obj]
+    while stack:
+        item = stack.pop()
+        if isinstance(item, str):
+            yield item
+        elif isinstance(item, dict):
+            stack.extend(reversed(list(item.values())))
+        elif isinstance(item, list):
+            stack.extend(reversed(item))
 
 
 def _pieces(path):
@@ -102,23 +108,19 @@ def self_repeat(g):
 
 
 class Seen:
-    """Accepted documents' grams, for exact and near-duplicate rejection within a corpus."""
+    """The grams of accepted documents, for exact and near-duplicate rejection within a corpus."""
 
     def __init__(self):
-        self.owner = {}
+        self.owner = {}                      # gram -> first accepted document holding it
 
     def containment(self, g):
-        """(largest share of g's distinct grams found in one accepted document, that document)."""
-        counts = {}
-        u = np.unique(g).tolist()
-        for x in u:
-            d = self.owner.get(x)
-            if d is not None:
-                counts[d] = counts.get(d, 0) + 1
-        if not counts:
+        """(the largest share of g's distinct grams found in a single accepted document, that document)."""
+        distinct = np.unique(g).tolist()
+        hits = Counter(d for d in map(self.owner.get, distinct) if d is not None)
+        if not hits:
             return 0.0, None
-        best = max(counts, key=counts.get)
-        return counts[best] / len(u), best
+        doc = max(hits, key=hits.get)         # the first document to reach the top count
+        return hits[doc] / len(distinct), doc
 
     def add(self, name, g):
         for x in np.unique(g).tolist():
