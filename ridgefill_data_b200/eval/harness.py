@@ -50,52 +50,64 @@ class EvalError(ValueError):
 
 
 # ---------------------------------------------------------------------------------------------- arm checks
+# keys whose equality makes two arms' prefix fills (and P) identical
+_FILL_KEYS = ("split", "tail", "tail_round", "tail_from", "fill", "fill_by_type", "projector", "kvfold", "select",
+              "context", "refresh", "refresh_projector", "tail_bias_from", "tail_bias_skip_last", "exact_part",
+              "rescale", "rescale_skip_last")
+_PER_PROMPT_KEYS = ("select", "tail_bias_from", "rescale")       # set at all, they make the fill prompt-specific
+
+
 def check_reuse(specs):
-    """reuse_fill: the named arm must come earlier, with the same split, tail, fill, maps and selection."""
-    by_name = {}
-    for s in specs:
-        src = by_name.get(s.get("reuse_fill"))
-        if "reuse_fill" in s and src is None:
-            raise EvalError(f"arm {s['name']}: reuse_fill {s['reuse_fill']!r} is not an earlier arm")
-        if src is not None:
-            diff = [k for k in ("split", "tail", "tail_round", "tail_from", "fill", "fill_by_type", "projector",
-                                "kvfold", "select", "context", "refresh", "refresh_projector", "tail_bias_from",
-                                "tail_bias_skip_last", "exact_part", "rescale", "rescale_skip_last")
-                    if s.get(k) != src.get(k) or (k == "select" and s.get(k))
-                    or (k in ("tail_bias_from", "rescale") and s.get(k) is not None)]
-            if diff:
-                raise EvalError(f"arm {s['name']} reuses the fill of {src['name']} but its P or fill can differ "
-                                f"({', '.join(diff)})")
-        by_name[s["name"]] = s
+    """reuse_fill names an earlier arm whose fill this arm may take over: same P, same maps, same fill, and
+    nothing that computes the fill from the prompt's tail or selection."""
+    earlier = {}
+    for spec in specs:
+        name = spec.get("reuse_fill")
+        if "reuse_fill" in spec and name not in earlier:
+            raise EvalError(f"arm {spec['name']}: reuse_fill {name!r} is not an earlier arm")
+        if name in earlier:
+            src = earlier[name]
+            differs = [k for k in _FILL_KEYS if spec.get(k) != src.get(k)
+                       or (k in _PER_PROMPT_KEYS and (spec.get(k) if k == "select" else spec.get(k) is not None))]
+            if differs:
+                raise EvalError(f"arm {spec['name']} reuses the fill of {src['name']} but its P or fill can differ "
+                                f"({', '.join(differs)})")
+        earlier[spec["name"]] = spec
+
+
+def _tail_round_problems(spec, tr):
+    if not isinstance(tr, dict) or set(tr) != {"base", "block"} or type(tr["base"]) is not int \
+            or type(tr["block"]) is not int:
+        yield f"{tr!r} is not {{'base': int, 'block': int}}"
+    else:
+        if tr["base"] != spec.get("tail") or tr["base"] < ENGINE_MIN_TAIL:
+            yield (f"base {tr['base']} must equal the arm's tail ({spec.get('tail')}) and be at least "
+                   f"{ENGINE_MIN_TAIL}")
+        if tr["block"] < 1:
+            yield f"block {tr['block']} must be positive"
+    if spec.get("select"):
+        yield "with a select the rows would be picked against the unrounded boundary"
+    if spec.get("tail_from") is not None:
+        yield "tail_from sets the tail per prompt"
 
 
 def check_tail_round(specs):
-    for s in specs:
-        tr = s.get("tail_round")
-        if tr is None:
+    """tail_round {base, block}: the tail grows so the prefix ends on a block multiple (as a block engine runs)."""
+    for spec in specs:
+        if spec.get("tail_round") is None:
             continue
-        bad = []
-        if not (isinstance(tr, dict) and set(tr) == {"base", "block"} and type(tr["base"]) is int
-                and type(tr["block"]) is int):
-            bad.append(f"{tr!r} is not {{'base': int, 'block': int}}")
-        else:
-            if tr["base"] != s.get("tail") or tr["base"] < ENGINE_MIN_TAIL:
-                bad.append(f"base {tr['base']} must equal the arm's tail ({s.get('tail')}) and be at least "
-                           f"{ENGINE_MIN_TAIL}")
-            if tr["block"] < 1:
-                bad.append(f"block {tr['block']} must be positive")
-        if s.get("select"):
-            bad.append("with a select the rows would be picked against the unrounded boundary")
-        if s.get("tail_from") is not None:
-            bad.append("tail_from sets the tail per prompt")
-        if bad:
-            raise EvalError(f"arm {s['name']}: tail_round refused: " + "; ".join(bad))
+        problems = list(_tail_round_problems(spec, spec["tail_round"]))
+        if problems:
+            raise EvalError(f"arm {spec['name']}: tail_round refused: " + "; ".join(problems))
 
 
 def check_tail_from(spec):
+    """tail_from 'continuation' makes every prompt's tail its scored continuation: nothing else may set it."""
     tf = spec.get("tail_from")
-    if tf is not None and (tf != "continuation" or "tail" in spec or spec.get("select") or spec.get("tail_round")
-                           or spec.get("reuse_fill")):
+    if tf is None:
+        return
+    clashes = "tail" in spec or any(spec.get(k) for k in ("select", "tail_round", "reuse_fill"))
+    if tf != "continuation" or clashes:
         raise EvalError(f"arm {spec['name']}: tail_from 'continuation' sets the tail per prompt: no 'tail', select, "
                         "tail_round or reuse_fill")
 
@@ -146,52 +158,65 @@ class Files:
         return self.freq[path]
 
 
+_ARM_FIELDS = {"split": None, "tail": 0, "fill": "exact", "tail_from": None, "f1": False, "fill_by_type": None,
+               "tail_bias_from": None, "tail_bias_skip_last": 0, "exact_part": None, "rescale": None,
+               "rescale_skip_last": 0}
+
+
+def _same_split(arm, maps, path):
+    if maps.split != arm.split:
+        raise EvalError(f"arm {arm.name}: {path} is for split {maps.split}, not {arm.split}")
+
+
 def build_arm(spec, files):
+    """An Arm from a JSON arm spec, its map files loaded (once) through `files` and checked against the arm."""
     check_tail_from(spec)
-    a = Arm(spec["name"], split=spec.get("split"), tail=spec.get("tail", 0), fill=spec.get("fill", "exact"),
-            tail_from=spec.get("tail_from"), f1=spec.get("f1", False), fill_by_type=spec.get("fill_by_type"),
-            tail_bias_from=spec.get("tail_bias_from"), tail_bias_skip_last=spec.get("tail_bias_skip_last", 0),
-            exact_part=spec.get("exact_part"), rescale=spec.get("rescale"),
-            rescale_skip_last=spec.get("rescale_skip_last", 0), meta=dict(spec))
+    a = Arm(spec["name"], meta=dict(spec), **{k: spec.get(k, default) for k, default in _ARM_FIELDS.items()})
     if spec.get("projector"):
         a.projector = files.projector(spec["projector"])
-        if a.projector.split != a.split:
-            raise EvalError(f"arm {a.name}: {spec['projector']} is for split {a.projector.split}, not {a.split}")
+        _same_split(a, a.projector, spec["projector"])
         a.context = spec.get("context", 0)
-        if int(a.projector.meta.get("context", 0)) != a.context:
-            raise EvalError(f"arm {a.name}: context {a.context}, but {spec['projector']} reads context "
-                            f"{a.projector.meta.get('context', 0)}")
+        fitted = int(a.projector.meta.get("context", 0))
+        if fitted != a.context:
+            raise EvalError(f"arm {a.name}: context {a.context}, but {spec['projector']} reads context {fitted}")
     if spec.get("refresh") is not None:
-        a.refresh, a.refresh_projector = spec["refresh"], files.projector(spec["refresh_projector"])
-        if a.refresh_projector.split != a.refresh + 1 or int(a.refresh_projector.meta.get("context", 0)):
+        a.refresh = spec["refresh"]
+        a.refresh_projector = files.projector(spec["refresh_projector"])
+        plain = int(a.refresh_projector.meta.get("context", 0)) == 0
+        if a.refresh_projector.split != a.refresh + 1 or not plain:
             raise EvalError(f"arm {a.name}: refresh {a.refresh} needs a plain projector of split {a.refresh + 1}")
     if spec.get("kvfold"):
         a.kvfold = files.projector(spec["kvfold"], "kvfold")
-        if a.kvfold.split != a.split:
-            raise EvalError(f"arm {a.name}: {spec['kvfold']} is for split {a.kvfold.split}, not {a.split}")
+        _same_split(a, a.kvfold, spec["kvfold"])
     if spec.get("st"):
         a.st = files.correction(spec["st"])
     return a
 
 
+def _select_ok(sel, sig, by_name):
+    matched = sel["kind"] in ("random", "tail_match")
+    return (sel["kind"] in SEL.KINDS
+            and (sel.get("match") in by_name) == matched
+            and bool(sel.get("predictor")) == ("pred" in sig)
+            and bool(sel.get("table")) == bool(sig & {"freq", "frag"}))
+
+
 def check_selects(arms, files):
+    """Every select spec is well formed and its predictor, table or deviation maps exist for the arm's split."""
     by_name = {a.name: a for a in arms}
-    for a in arms:
-        sel = a.meta.get("select")
-        if not sel:
-            continue
+    for a in (x for x in arms if x.meta.get("select")):
+        sel = a.meta["select"]
         sig = SEL.signals(sel)
-        if (sel["kind"] not in SEL.KINDS or (sel.get("match") in by_name) != (sel["kind"] in ("random", "tail_match"))
-                or bool(sel.get("predictor")) != ("pred" in sig) or bool(sel.get("table")) != bool(sig & {"freq", "frag"})):
+        if not _select_ok(sel, sig, by_name):
             raise EvalError(f"arm {a.name}: bad select spec {sel}")
         if sel.get("table"):
             files.table(sel["table"])
         if sel.get("predictor") and files.predictor(sel["predictor"]).split != a.split:
             raise EvalError(f"arm {a.name}: predictor {sel['predictor']} is not for split {a.split}")
         if "deviation" in sig:
-            q = sel.get("projector")
-            proj = files.projector(q) if q else a.projector
-            if proj is None or proj.split != a.split:
+            path = sel.get("projector")
+            maps = files.projector(path) if path else a.projector
+            if maps is None or maps.split != a.split:
                 raise EvalError(f"arm {a.name}: deviation needs a projector of split {a.split}")
 
 
