@@ -134,6 +134,10 @@ def main():
     ap.add_argument("--tp-comm", default="nvls", choices=("nccl", "fused", "nvls"),
                     help="tensor-parallel collectives: nvls (fused GEMM + NVSwitch multicast kernels; falls back to "
                          "nccl where the GPUs offer no multicast), nccl (baseline), fused (peer stores)")
+    ap.add_argument("--tp-fill", default="columns", choices=("columns", "rows"),
+                    help="tensor-parallel map fill: columns (each rank a column slice of every map, then a gather; "
+                         "the default) or rows (each rank a block of prefix rows through the whole map, then an "
+                         "all-to-all of the heads' projections: parallel/rowfill.py)")
     args = ap.parse_args()
     dsplit, dtail = DEFAULT_SPLIT_TAIL.get(args.model, (32, 4096))
     args.split = dsplit if args.split is None else args.split
@@ -164,13 +168,13 @@ def main():
     if tp_mode:
         from ridgefill_data_b200.parallel.tp import TensorParallel, shard
         try:
-            tp = TensorParallel(mode=args.tp_comm)
+            tp = TensorParallel(mode=args.tp_comm, fill=args.tp_fill)
         except Exception as e:                       # no NVSwitch multicast here: the NCCL baseline
             if args.tp_comm != "nvls":
                 raise
             print(f"nvls unavailable ({e}); using nccl", file=sys.stderr)
             args.tp_comm = "nccl"
-            tp = TensorParallel(mode="nccl")
+            tp = TensorParallel(mode="nccl", fill=args.tp_fill)
         shard(model, tp)
     ids_host = uniform_prompt(args.seq, cfg.vocab, seed=2 + (0 if tp_mode else rank)).pin_memory()
     ids_dev = ids_host.to(device)
@@ -267,7 +271,8 @@ def main():
                     data="synthetic (seeded uniform prompt; random-init weights and ridge maps of the named shapes)",
                     config=dict(model=args.model, global_batch=1 if tp_mode else world, seq_len=args.seq,
                                 split=args.split, tail=args.tail,
-                                parallelism=(f"tp{world}" + ("" if args.tp_comm == "nccl" else f"-{args.tp_comm}")) if tp_mode
+                                parallelism=(f"tp{world}" + ("" if args.tp_comm == "nccl" else f"-{args.tp_comm}")
+                                             + ("-rowfill" if args.tp_fill == "rows" else "")) if tp_mode
                                 else f"dp{world}",
                                 l2="inputs larger than L2 (the weights, tens of GB, are streamed every step)"),
                     clocks=clocks, gpu_launches=int(launches),

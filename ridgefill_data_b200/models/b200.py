@@ -240,6 +240,9 @@ class _B200:
             else:
                 w = W[i] if W[i].dtype == self.dtype else W[i].to(self.dtype)
                 c = B[i] if B[i].dtype == self.dtype else B[i].to(self.dtype)
+                if getattr(self.tp, "row_fill", None) is not None:
+                    self.tp.row_fill.fill_layer(self, i, b, pos, cache, w, c)
+                    continue
                 x = self.tp.map_fill(b, w, c) if self.tp is not None else G.linear(b, w, bias=c)
             self.fill(i, x, pos, cache)
 

@@ -20,6 +20,8 @@ map fill's column gather in late layers):
   nvls        parallel/nvls.py: NVSwitch multicast: partials reduced in the switch (multimem.ld_reduce) and the sums
               multicast to every rank (multimem.st) by one kernel with its own cross-rank barriers; map slices
               multicast into every rank's x_l
+With fill="rows" the map fill is row-parallel instead (parallel/rowfill.py): each rank maps a block of prefix rows
+through the whole map and the unsharded fill projection, and an all-to-all delivers each rank its heads' columns.
 """
 from __future__ import annotations
 
@@ -30,13 +32,19 @@ from ..ops import gemm as G
 
 
 class TensorParallel:
-    def __init__(self, group=None, mode="nccl"):
+    def __init__(self, group=None, mode="nccl", fill="columns"):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.mode = mode
         self.fused = None
         self.fused_fill = None
+        if fill not in ("columns", "rows"):
+            raise ValueError(f"TP map-fill layout {fill!r} (columns | rows)")
+        self.row_fill = None
+        if fill == "rows" and self.world > 1:           # parallel/rowfill.py: row blocks and an all-to-all
+            from .rowfill import RowParallelFill
+            self.row_fill = RowParallelFill(group)
         if mode == "fused" and self.world > 1:
             from .fused import FusedMapFill, FusedRowParallel
             self.fused = FusedRowParallel(group)
@@ -146,6 +154,8 @@ def shard(model, tp: TensorParallel):
     if world == 1:
         model.tp = tp
         return model
+    if getattr(tp, "row_fill", None) is not None:
+        tp.row_fill.prepare(model)           # the unsharded fill projections, before the slicing below
     local = {}
     for i, w in enumerate(model.W):
         if model.layer_types[i] == "attn":
