@@ -1,5 +1,6 @@
 """Tensor parallelism on 2 GPUs (spawned NCCL ranks): the sharded B200 model reproduces the unsharded one's
-logits for exact forward and RidgeFill prefill. Skipped with fewer than 2 visible GPUs."""
+logits for exact forward and RidgeFill prefill (map fill by column slices, or by row blocks and an
+all-to-all). Skipped with fewer than 2 visible GPUs."""
 import os
 import socket
 
@@ -18,7 +19,7 @@ def _free_port():
     return port
 
 
-def _worker(rank, world, port, mode, q):
+def _worker(rank, world, port, mode, q, fill="columns"):
     import torch.distributed as dist
     from datetime import timedelta
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -53,7 +54,7 @@ def _worker(rank, world, port, mode, q):
                 ref, _ = m.forward_exact(ids, keep=keep)
                 hs, lower = run_lower(m, ids, [split])
                 ref_rf, _, _ = finish(m, ids, hs[split], lower, arm, 4)
-                tp = TensorParallel(mode=mode)
+                tp = TensorParallel(mode=mode, fill=fill)
                 shard(m, tp)
                 got, _ = m.forward_exact(ids, keep=keep)
                 hs, lower = run_lower(m, ids, [split])
@@ -71,14 +72,15 @@ def _worker(rank, world, port, mode, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["nccl", "fused", "nvls"])
-def test_tp2_matches_single_gpu(mode):
+@pytest.mark.parametrize("mode,fill", [("nccl", "columns"), ("fused", "columns"), ("nvls", "columns"),
+                                       ("nccl", "rows")])
+def test_tp2_matches_single_gpu(mode, fill):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q, fill)) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=600) for _ in procs)
