@@ -93,10 +93,11 @@ def era(version, current, archive):
 
 
 def phase(p):
-    ph = p.get("phase", "development")
-    if ph not in PHASES:
-        raise ProtocolError(f"protocol {p.get('version')}: phase {ph!r} is neither of {PHASES}")
-    return ph
+    """'development' (the default) or 'frozen'."""
+    declared = p.get("phase", PHASES[0])
+    if declared in PHASES:
+        return declared
+    raise ProtocolError(f"protocol {p.get('version')}: phase {declared!r} is neither of {PHASES}")
 
 
 def _has_final(regs):
@@ -245,18 +246,27 @@ def protocol_row(spec, model, p):
 
 
 def battery_row(spec, model, p):
-    return protocol_row(spec, model, p) and arm_kind(spec, p) not in p.get("outside_battery", ())
+    """A protocol row that the battery tables include (kinds listed under outside_battery are rows, not battery)."""
+    if not protocol_row(spec, model, p):
+        return False
+    return arm_kind(spec, p) not in set(p.get("outside_battery", ()))
 
 
 def battery_cells(model, p):
-    """(split, tail, kind) of every battery row of a model, in table order."""
-    m = p["models"][model]
-    kinds = [k for k in p["arms"] if k != "exact"]
-    cells = [(s, t, k) for s in m["splits"] for t in p["tails"] for k in kinds if k not in TAILLESS]
-    cells.append((m.get("pop_split"), None, "pop-native"))
-    cells += [(s, None, "swiftkv-native") for s in m["splits"]]
-    return [(s, t, k) for s, t, k in cells
-            if s is not None and k in p["arms"] and battery_row(template(k, model, s, t, p), model, p)]
+    """(split, tail, kind) of every battery row of a model, in table order: the split x tail grid of the tailed
+    kinds, then the model's pop-native cell, then swiftkv-native at each split."""
+    entry = p["models"][model]
+    listed = [k for k in p["arms"] if k != "exact"]
+    candidates = [(s, t, k) for s in entry["splits"] for t in p["tails"] for k in listed if k not in TAILLESS]
+    candidates.append((entry.get("pop_split"), None, "pop-native"))
+    candidates.extend((s, None, "swiftkv-native") for s in entry["splits"])
+    keep = []
+    for s, t, k in candidates:
+        if s is None or k not in p["arms"]:
+            continue
+        if battery_row(template(k, model, s, t, p), model, p):
+            keep.append((s, t, k))
+    return keep
 
 
 def _row_in_config(spec, by_name, model, p):
