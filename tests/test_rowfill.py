@@ -109,3 +109,32 @@ def test_fill_layout_is_refused_when_unknown():
         assert TP.TensorParallel(mode="nccl", fill="rows").row_fill is None      # one rank: nothing to exchange
     finally:
         dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_prepare_on_packed_b200_weights(monkeypatch, world):
+    """prepare() keeps the unsharded fill projections of a packed B200 hybrid; after tp.shard, each rank's plan
+    columns of them are exactly the rows its sharded attention k|v and GDN conv / b / a projections hold. (The
+    model is built on the CPU with the device set-up skipped: only its packed weights are read here.)"""
+    from ridgefill_data_b200.models import b200
+    from ridgefill_data_b200.models.checkpoint import RandomSource
+    from ridgefill_data_b200.models.tiny import tiny_configs
+    from ridgefill_data_b200.parallel import tp as TP
+    monkeypatch.setattr(b200._B200, "_kernel_setup", lambda self: setattr(self, "_rope_tables", None))
+    cfg = tiny_configs(8, 64)["qwen3.5-9b"].replace(intermediate=512)      # 4 FFN blocks of 128 rows
+    if cfg.n_heads % world or cfg.gdn_nk % world or cfg.gdn_nv % world:
+        pytest.skip("head counts do not split over this many ranks")
+    for rank in range(world):
+        model = b200.B200Hybrid(cfg, RandomSource(cfg, seed=0), device="cpu", dtype=torch.bfloat16)
+        fill = RF.RowParallelFill.__new__(RF.RowParallelFill)
+        fill.group, fill.rank, fill.world, fill.proj, fill.cols = None, rank, world, {}, {}
+        fill.prepare(model)
+        fake = SimpleNamespace(rank=rank, world=world, row_fill=None, group=None)
+        TP.shard(model, fake)
+        for i, w in enumerate(model.W):
+            mine = fill.proj[i].index_select(0, fill.cols[i][rank])
+            if model.layer_types[i] == "attn":
+                q_rows = model.n_heads * cfg.head_dim * (2 if cfg.gated_attn else 1)
+                assert torch.equal(mine, w["qkv_p"][q_rows:]), (rank, i)
+            else:
+                assert torch.equal(mine, w["in_p"][:model.conv_dim + 2 * model.nv]), (rank, i)
