@@ -33,8 +33,8 @@ def verify_install(root=REF):
     """The installed kva package, checked file by file against the hashes recorded at install time."""
     rec_path = root / "INSTALL.json"
     if not rec_path.is_file():
-        raise Unavailable("baseline/_ref is not installed (run baseline/install_reference.py on the reference "
-                          "checkout)")
+        raise Unavailable(f"the reference is not installed: no {rec_path} (run baseline/install_reference.py on "
+                          "the reference checkout)")
     rec = json.loads(rec_path.read_text())
     if not rec.get("files"):
         raise Unavailable("baseline/_ref holds no copied kva package")
@@ -154,15 +154,17 @@ def run(args, metric, baseline_tok_s, clock_sampler):
         time.sleep(0.3)
         barrier()
         torch.cuda.synchronize()
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record()
-        for _ in range(args.steps):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        ev[0].record()
+        for s in range(args.steps):
             step(ids_dev)
-        t1.record()
+            ev[s + 1].record()
         torch.cuda.synchronize()
         barrier()
         clocks = sampler.stop()
-        ms = t0.elapsed_time(t1) / args.steps
+        ms = ev[0].elapsed_time(ev[args.steps]) / args.steps
+        per = sorted(ev[s].elapsed_time(ev[s + 1]) for s in range(args.steps))
+        p50 = (per[(args.steps - 1) // 2] + per[args.steps // 2]) / 2
         barrier()
         torch.cuda.synchronize()
         w0 = time.perf_counter()
@@ -172,11 +174,11 @@ def run(args, metric, baseline_tok_s, clock_sampler):
             tok_host.copy_(logits[-1].argmax().view(1), non_blocking=True)
             torch.cuda.current_stream().synchronize()
         e2e_ms = (time.perf_counter() - w0) * 1e3 / args.steps
-    stats = torch.tensor([ms, e2e_ms], dtype=torch.float64)
+    stats = torch.tensor([ms, e2e_ms, p50], dtype=torch.float64)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
         dist.destroy_process_group()
-    ms_max, e2e_max = stats.tolist()
+    ms_max, e2e_max, p50_max = stats.tolist()
     tokens = args.seq * world
     value = tokens / (ms_max / 1e3)
     base = baseline_tok_s.get(args.model, {}).get(args.seq)
@@ -184,7 +186,7 @@ def run(args, metric, baseline_tok_s, clock_sampler):
         print(json.dumps(dict(
             impl="reference", metric=metric, value=round(value, 1), unit="tokens/s", n_gpus=world, steps=args.steps,
             warmup=args.warmup, ms_per_step=round(ms_max, 3), higher_is_better=True, scaling="weak",
-            vs_baseline=round(value / base, 3) if base else None, dtype="bf16",
+            vs_baseline=None, vs_published_other_hw=round(value / base, 3) if base else None, dtype="bf16",
             data="synthetic (seeded uniform prompt; the same random-init weights and ridge maps as the main arm)",
             config=dict(model=args.model, global_batch=world, seq_len=args.seq, split=args.split, tail=args.tail,
                         parallelism=f"dp{world}", deterministic=info.get("deterministic"),
@@ -193,7 +195,7 @@ def run(args, metric, baseline_tok_s, clock_sampler):
             e2e=dict(value=round(tokens / (e2e_max / 1e3), 1), unit="tokens/s", ms_per_step=round(e2e_max, 3),
                      h2d_bytes_per_step=int(ids_host.numel() * ids_host.element_size()),
                      d2h_bytes_per_step=int(tok_host.numel() * tok_host.element_size())),
-            ttft_ms=round(ms_max, 3),
+            ttft_ms=round(ms_max, 3), ttft_p50_ms=round(p50_max, 3),
             path="kva.gpu.setup + kva.model.model_class + kva.kva.run_lower/finish (unmodified, baseline/_ref)")),
             flush=True)
     return None

@@ -32,8 +32,10 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-# Published RidgeFill prompt time of the 27B hybrid at 16K tokens (llama.cpp fork, resident maps, split 16,
-# tail 4096, one A100 40 GB): 10.380 s -> tokens / s.
+# Published RidgeFill prompt times (other hardware and engines: the 27B hybrid on a llama.cpp fork, resident maps,
+# split 16, tail 4096, one A100 40 GB; Flash-Next on a vLLM fork, TP2 on AMD R9700) -> tokens / s. BASELINE.json
+# publishes no number for this metric on a B200, so the JSON line's vs_baseline stays null and the ratio to these
+# published A100 / R9700 figures is reported under its own name (vs_published_other_hw).
 BASELINE_TOK_S = {"qwen3.8-27b": {16384: 16384 / 10.380, 32768: 32768 / 21.112, 65536: 65536 / 46.284,
                                    122880: 122880 / 100.014},
                   # Flash-Next RidgeFill TTFT medians (vLLM fork, TP2 on 2x AMD R9700): 9K / 16K / 32K
@@ -103,6 +105,30 @@ def reference_arm(args):
                  ClockSampler)
 
 
+def measured_peaks():
+    """Roofline denominators measured on this pool (MEASURED_PEAKS.json beside this file), else the stated fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return dict(bf16_tflops_sustained=float(d["bf16_tflops_sustained"]), bf16_tflops=float(d["bf16_tflops"]),
+                    hbm_gbs=float(d["hbm_gbs"]), source="measured")
+    except (OSError, KeyError, ValueError):
+        return dict(bf16_tflops_sustained=1400.0, bf16_tflops=1590.0, hbm_gbs=6650.0, source="fallback")
+
+
+def timed(fn, steps):
+    """Run fn() `steps` times back to back with one CUDA event between steps: (mean ms, p50 ms, per-step ms)."""
+    import torch
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    ev[0].record()
+    for s in range(steps):
+        fn()
+        ev[s + 1].record()
+    torch.cuda.synchronize()
+    per = [ev[s].elapsed_time(ev[s + 1]) for s in range(steps)]
+    return ev[0].elapsed_time(ev[steps]) / steps, statistics.median(per), per
+
+
 def build_engine(args, device):
     from ridgefill_data_b200.engine.arm import Arm
     from ridgefill_data_b200.models.base import from_config
@@ -126,7 +152,13 @@ def main():
     ap.add_argument("--seq", type=int, default=16384)
     ap.add_argument("--tail", type=int)
     ap.add_argument("--split", type=int)
-    ap.add_argument("--exact", action="store_true", help="also time full (exact) prefill for the speedup")
+    ap.add_argument("--exact", dest="exact", action="store_true", default=True,
+                    help="also time full (exact) prefill at every length for the speedup (the default)")
+    ap.add_argument("--no-exact", dest="exact", action="store_false")
+    ap.add_argument("--sweep", default="auto",
+                    help="extra prompt lengths (comma-separated, or 'none') timed after the headline length: p50 "
+                         "TTFT of RidgeFill and of full prefill at each; 'auto' = 32K, 64K and 128K for the 27B hybrid")
+    ap.add_argument("--sweep-steps", type=int, default=5, help="timed steps per sweep length (p50 over them)")
     ap.add_argument("--parallel", default="tp", choices=("tp", "dp"))
     ap.add_argument("--stages", action="store_true",
                     help="after the timed steps, one extra step with per-stage device times (lower layers, fill, "
@@ -202,17 +234,10 @@ def main():
         barrier()
         torch.cuda.synchronize()
         launches0 = ext().launch_count()
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record()
-        for _ in range(args.steps):
-            step(ids_dev)
-        t1.record()
-        torch.cuda.synchronize()
+        ms, p50_ms, _ = timed(lambda: step(ids_dev), args.steps)
         barrier()
         launches = ext().launch_count() - launches0
         clocks = sampler.stop()
-        ms = t0.elapsed_time(t1) / args.steps
 
         if args.stages:                          # diagnostics outside the timed region
             from ridgefill_data_b200.utils.trace import StageTimer
@@ -238,36 +263,61 @@ def main():
         e2e_ms = (time.perf_counter() - w0) * 1e3 / args.steps
         barrier()
 
-        exact_ms = None
-        if args.exact:
-            from ridgefill_data_b200.engine.arm import Arm
-            from ridgefill_data_b200.engine.prefill import prefill
-            ex = Arm("exact")
-            keep = torch.arange(args.seq - 1, args.seq, device=device)
-            prefill(model, ids_dev, ex)
+        def exact_p50(ids, steps):
+            keep = torch.arange(ids.shape[0] - 1, ids.shape[0], device=device)
+            model.forward_exact(ids, keep=keep)                     # warm-up at this length
             torch.cuda.synchronize()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for _ in range(max(1, args.steps // 2)):
-                model.forward_exact(ids_dev, keep=keep)
-            e1.record()
+            barrier()
+            return timed(lambda: model.forward_exact(ids, keep=keep), steps)[1]
+
+        exact_ms = exact_p50(ids_dev, max(3, min(10, args.steps // 2))) if args.exact else None
+
+        # ---- the other prompt lengths of the metric (outside the headline timed region): p50 TTFT of RidgeFill
+        # and of full prefill at each
+        sweep = []
+        lengths = [] if args.sweep == "none" else (
+            [32768, 65536, 131072] if args.sweep == "auto" and args.model == "qwen3.8-27b" else
+            [] if args.sweep == "auto" else [int(x) for x in args.sweep.split(",") if x.strip()])
+        for L in [x for x in lengths if x != args.seq and x > args.tail]:
+            ids_l = uniform_prompt(L, cfg.vocab, seed=2 + (0 if tp_mode else rank)).to(device)
+            step(ids_l)                                               # warm-up at this length
             torch.cuda.synchronize()
-            exact_ms = e0.elapsed_time(e1) / max(1, args.steps // 2)
+            barrier()
+            _, rf50, _ = timed(lambda: step(ids_l), args.sweep_steps)
+            ex50 = exact_p50(ids_l, max(2, args.sweep_steps // 2 + 1)) if args.exact else 0.0
+            sweep.append((L, rf50, ex50))
+            del ids_l
+            torch.cuda.empty_cache()
         check_errors(device)
 
-    stats = torch.tensor([ms, e2e_ms, exact_ms or 0.0], dtype=torch.float64, device=device)
+    flat = [ms, e2e_ms, exact_ms or 0.0, p50_ms] + [v for s in sweep for v in s[1:]]
+    stats = torch.tensor(flat, dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    ms_max, e2e_max, exact_max = stats.tolist()
+    vals = stats.tolist()
+    ms_max, e2e_max, exact_max, p50_max = vals[:4]
     tokens = args.seq * (1 if tp_mode else world)
     value = tokens / (ms_max / 1e3)
     e2e_value = tokens / (e2e_max / 1e3)
     base = BASELINE_TOK_S.get(args.model, {}).get(args.seq)
+    from ridgefill_data_b200.eval.cost import CostModel
+    cost = CostModel(cfg)
+    flops = 2 * cost.ridgefill(args.seq, args.split, args.tail) * (1 if tp_mode else world)
+    peaks = measured_peaks()
+    tflops = flops / (ms_max / 1e3) / 1e12
+    by_len = {str(args.seq): dict(ttft_p50_ms=round(p50_max, 3),
+                                  exact_p50_ms=round(exact_max, 3) if exact_ms else None,
+                                  speedup_vs_exact=round(exact_max / p50_max, 3) if exact_ms else None)}
+    for j, (L, _, _) in enumerate(sweep):
+        rf50, ex50 = vals[4 + 2 * j], vals[5 + 2 * j]
+        by_len[str(L)] = dict(ttft_p50_ms=round(rf50, 3), exact_p50_ms=round(ex50, 3) if args.exact else None,
+                              speedup_vs_exact=round(ex50 / rf50, 3) if args.exact else None,
+                              tok_s=round(L * (1 if tp_mode else world) / (rf50 / 1e3), 1))
     if rank == 0:
         line = dict(metric=METRIC.get(args.model, f"prefill tok/s (RidgeFill TTFT), {args.model}"), value=round(value, 1), unit="tokens/s", n_gpus=world, steps=args.steps,
                     warmup=args.warmup, ms_per_step=round(ms_max, 3), higher_is_better=True,
-                    scaling="strong" if tp_mode else "weak", vs_baseline=round(value / base, 3) if base else None, dtype="bf16",
+                    scaling="strong" if tp_mode else "weak", vs_baseline=None,
+                    vs_published_other_hw=round(value / base, 3) if base else None, dtype="bf16",
                     data="synthetic (seeded uniform prompt; random-init weights and ridge maps of the named shapes)",
                     config=dict(model=args.model, global_batch=1 if tp_mode else world, seq_len=args.seq,
                                 split=args.split, tail=args.tail,
@@ -279,9 +329,12 @@ def main():
                     e2e=dict(value=round(e2e_value, 1), unit="tokens/s", ms_per_step=round(e2e_max, 3),
                              h2d_bytes_per_step=int(ids_host.numel() * ids_host.element_size()),
                              d2h_bytes_per_step=int(tok_host.numel() * tok_host.element_size())),
-                    ttft_ms=round(ms_max, 3))
+                    ttft_ms=round(ms_max, 3), ttft_p50_ms=round(p50_max, 3),
+                    flops_per_step=round(flops), tflops=round(tflops, 1),
+                    frac_of_sustained_bf16=round(tflops / (peaks["bf16_tflops_sustained"] * world), 3),
+                    peaks_source=peaks["source"], ttft_by_len=by_len)
         if exact_ms:
-            line.update(exact_prefill_ms=round(exact_max, 3), speedup_vs_exact=round(exact_max / ms_max, 3))
+            line.update(exact_prefill_ms=round(exact_max, 3), speedup_vs_exact=round(exact_max / p50_max, 3))
         print(json.dumps(line), flush=True)
     if tp is not None:
         torch.cuda.synchronize()

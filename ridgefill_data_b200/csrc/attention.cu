@@ -231,11 +231,8 @@ __global__ void __launch_bounds__(FA_THREADS) flash_attn_kernel(AttnArgs a) {
 template <int HD>
 static void launch_fa(const AttnArgs& a, cudaStream_t stream) {
   constexpr int SMEM = FaSmem<HD>::BYTES;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(flash_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    set = true;
-  }
+  static PerDeviceOnce once;
+  once([] { cudaFuncSetAttribute(flash_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM); });
   dim3 grid((a.nq + FA_BM - 1) / FA_BM, a.hq);
   flash_attn_kernel<HD><<<grid, FA_THREADS, SMEM, stream>>>(a); count_launch();
 }

@@ -367,11 +367,8 @@ static CUtensorMap tmap3(const void* base, int hd, int rows, int heads, long hea
 template <int HD, int BN>
 static void launch_tc(const AttnArgs& x, cudaStream_t stream) {
   using Cfg = TcFaCfg<HD, BN>;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(tc_flash_kernel<HD, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-    set = true;
-  }
+  static PerDeviceOnce once;
+  once([] { cudaFuncSetAttribute(tc_flash_kernel<HD, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM); });
   CUtensorMap tq = tmap3(x.q, HD, x.nq, x.hq, x.q_head_stride, 128);
   CUtensorMap tk = tmap3(x.k, HD, x.nk, x.hkv, x.kv_head_stride, BN);
   CUtensorMap tv = tmap3(x.v, HD, x.nk, x.hkv, x.kv_head_stride, BN);

@@ -290,8 +290,9 @@ void comm_signal_b(std::vector<int64_t> flag_ptrs, int64_t slot, int64_t value) 
   rf::comm_signal(flags_of(flag_ptrs), (int)slot, (int)value, cur());
 }
 
-void comm_wait_b(int64_t flags, int64_t first, int64_t n, int64_t value, Tensor err) {
-  rf::comm_wait(reinterpret_cast<const int*>(flags), (int)first, (int)n, (int)value, err.data_ptr<int>(), cur());
+void comm_wait_b(int64_t flags, int64_t first, int64_t n, int64_t value, Tensor err, int64_t limit_ns) {
+  rf::comm_wait(reinterpret_cast<const int*>(flags), (int)first, (int)n, (int)value, err.data_ptr<int>(), cur(),
+                (uint64_t)std::max<int64_t>(0, limit_ns));
 }
 
 void comm_reduce_rows_b(int64_t recv, int64_t slot_stride, c10::optional<Tensor> residual, int64_t red, int64_t rows,
@@ -691,7 +692,8 @@ void register_comm(pybind11::module_& m) {
   m.def("ipc_close", &ipc_close_b);
   m.def("tensor_at", &tensor_at);
   m.def("comm_signal", &comm_signal_b);
-  m.def("comm_wait", &comm_wait_b);
+  m.def("comm_wait", &comm_wait_b, pybind11::arg("flags"), pybind11::arg("first"), pybind11::arg("n"),
+        pybind11::arg("value"), pybind11::arg("err"), pybind11::arg("limit_ns") = 0);
   m.def("comm_reduce_rows", &comm_reduce_rows_b);
   m.def("comm_gather_rows", &comm_gather_rows_b);
   m.def("gemm_peer", &gemm_peer_b);

@@ -32,13 +32,14 @@ void comm_signal(const PeerFlags& f, int slot, int value, cudaStream_t stream) {
   count_launch();
 }
 
-__global__ void wait_flags_kernel(const int* flags, int first, int n, int value, int* err) {
-  if (threadIdx.x < n) wait_value(flags + first + threadIdx.x, value, err);
+__global__ void wait_flags_kernel(const int* flags, int first, int n, int value, int* err, uint64_t limit_ns) {
+  if (threadIdx.x < n) wait_value(flags + first + threadIdx.x, value, err, limit_ns);
   __syncthreads();
 }
 
-void comm_wait(const int* flags, int first, int n, int value, int* err, cudaStream_t stream) {
-  wait_flags_kernel<<<1, 32, 0, stream>>>(flags, first, n, value, err);
+void comm_wait(const int* flags, int first, int n, int value, int* err, cudaStream_t stream, uint64_t limit_ns) {
+  if (n > 32) throw std::runtime_error("comm_wait: at most 32 flags per call");
+  wait_flags_kernel<<<1, 32, 0, stream>>>(flags, first, n, value, err, limit_ns ? limit_ns : kCommWaitNs);
   count_launch();
 }
 

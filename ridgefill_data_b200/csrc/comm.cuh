@@ -15,16 +15,16 @@ __device__ __forceinline__ void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Spin (bounded by kCommWaitNs of wall time) until *flag == value; records kErrTimeoutPeer and returns false on
-// expiry.
-__device__ __forceinline__ bool wait_value(const int* flag, int value, int* err) {
+// Spin (bounded by limit_ns of wall time, kCommWaitNs by default) until *flag == value; records kErrTimeoutPeer
+// and returns false on expiry.
+__device__ __forceinline__ bool wait_value(const int* flag, int value, int* err, uint64_t limit_ns = kCommWaitNs) {
   if (ld_acquire_sys(flag) == value) return true;
   const uint64_t t0 = global_timer_ns();
   uint32_t spins = 0;
   while (true) {
     if (ld_acquire_sys(flag) == value) return true;
     if ((++spins & 63u) == 0u) {
-      if (global_timer_ns() - t0 > kCommWaitNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         record_error(err, kErrTimeoutPeer);
         return false;
       }

@@ -850,21 +850,20 @@ __global__ void __launch_bounds__(128) gdn_output_kernel(GdnScanArgs a, int n_pa
 void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream) {
   if (a.n <= 0) return;
   if (a.dk != DK || a.dv % SVS != 0 || a.dv > 128 || a.nv % a.nk != 0 || (a.q != nullptr && (a.s_buf == nullptr || a.vt_buf == nullptr))) {
-    if (a.err) cudaMemsetAsync(a.err, kErrBadShape, 1, stream);
+    record_error_async(a.err, kErrBadShape, stream);
     return;
   }
   const int n_chunks = (a.n + GC - 1) / GC;
   const int n_pad = n_chunks * GC;
-  static bool set = false;
-  if (!set) {
+  static PerDeviceOnce once;
+  once([] {
     cudaFuncSetAttribute(gdn_wy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(WySmem));
     cudaFuncSetAttribute(gdn_state_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(StateSmem));
     cudaFuncSetAttribute(gdn_state_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(StateSmem));
     cudaFuncSetAttribute(gdn_state_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(StateSmem));
     cudaFuncSetAttribute(gdn_group_prop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PropSmem));
     cudaFuncSetAttribute(gdn_output_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(OutSmem));
-    set = true;
-  }
+  });
   gdn_wy_kernel<<<dim3(n_chunks, a.nv), 128, sizeof(WySmem), stream>>>(a, n_pad);
   count_launch();
   const bool two_level = a.groups > 1 && a.dv == DK && a.grp_buf != nullptr &&

@@ -22,14 +22,16 @@
 //
 // All calls share the one array and it keeps the previous call's contents. Every scratch element the
 // kernels read is written earlier in the same call, and the error word is cleared at the start of each
-// call. Calls that overlap on the GPU (concurrent streams, or several host threads) race on the array:
-// issue them one after another.
+// call; rf_gdn_noalloc_last_error reads it back after the call (gdn_noalloc.h declares the interface).
+// Calls that overlap on the GPU (concurrent streams, or several host threads) race on the array: issue
+// them one after another.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
 #include <mutex>
 
+#include "gdn_noalloc.h"
 #include "kernels.h"
 
 namespace {
@@ -54,13 +56,6 @@ size_t align256(size_t b) { return (b + 255) / 256 * 256; }
 
 extern "C" {
 
-enum RfNoAllocStatus {
-  RF_NOALLOC_OK = 0,
-  RF_NOALLOC_BAD_ARGS = 1,
-  RF_NOALLOC_TOO_LARGE = 2,
-  RF_NOALLOC_CUDA_ERROR = 3,
-};
-
 // Bytes of scratch a call of this shape needs (0 for a shape the kernels do not support).
 size_t rf_gdn_noalloc_scratch_bytes(int n, int nk, int nv, int dk, int dv, int output_mode) {
   if (n <= 0 || nk <= 0 || nv <= 0 || dk != 128 || (dv != 64 && dv != 128) || nv % nk != 0) return 0;
@@ -83,6 +78,8 @@ const char* rf_gdn_noalloc_strerror(int status) {
       return "the call needs more scratch than the fixed 16 MiB device array holds (see "
              "rf_gdn_noalloc_scratch_bytes); split the sequence into shorter calls";
     case RF_NOALLOC_CUDA_ERROR: return "a CUDA runtime call failed (cudaGetLastError has the cause)";
+    case RF_NOALLOC_KERNEL_ERROR:
+      return "a kernel of the last call recorded an error code (a timed-out bounded wait, a bad shape or index)";
     default: return "unknown status";
   }
 }
@@ -150,6 +147,23 @@ int rf_gdn_chunk_scan_noalloc(const void* q, const void* k, const void* v, const
   a.err = slot.err;
   rf::gdn_chunk_scan(a, stream);
   return cudaPeekAtLastError() == cudaSuccess ? RF_NOALLOC_OK : RF_NOALLOC_CUDA_ERROR;
+}
+
+int rf_gdn_noalloc_last_error(int* code, cudaStream_t stream) {
+  if (code == nullptr) return RF_NOALLOC_BAD_ARGS;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return RF_NOALLOC_CUDA_ERROR;
+  int* err = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_slots_mu);
+    err = g_slots[dev].err;
+  }
+  if (err == nullptr) return RF_NOALLOC_BAD_ARGS;
+  // a pageable host destination: the copy is staged by the driver, nothing is allocated here
+  if (cudaMemcpyAsync(code, err, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return RF_NOALLOC_CUDA_ERROR;
+  return *code == 0 ? RF_NOALLOC_OK : RF_NOALLOC_KERNEL_ERROR;
 }
 
 }  // extern "C"

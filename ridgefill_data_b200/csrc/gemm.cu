@@ -622,13 +622,10 @@ template <int BN, int EPI, bool A_MN, bool B_MN>
 static void launch_gemm(const GemmOperands& op, GemmArgs args, int max_ctas, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   auto kernel = gemm_kernel<BN, EPI, A_MN, B_MN>;
-  static bool attr_set[64] = {false};
+  static PerDeviceOnce once;
+  once([kernel] { cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes<BN, EPI>()); });
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes<BN, EPI>());
-    attr_set[dev & 63] = true;
-  }
   CUtensorMap ta = A_MN ? make_tmap_bf16_2d(op.A, args.M, args.K, op.lda, 64, 64)
                         : make_tmap_bf16_2d(op.A, args.K, args.M, op.lda, 64, BM);
   CUtensorMap tb = B_MN ? make_tmap_bf16_2d(op.B, args.N, args.K, op.ldb, 64, 64)

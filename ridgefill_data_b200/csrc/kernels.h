@@ -5,9 +5,31 @@
 #include <cstdint>
 
 #include <atomic>
+#include <mutex>
 #include <string>
+#include <utility>
 
 namespace rf {
+
+// Runs a set-up step once per CUDA device (the current one) for one call site, safely from several host threads.
+// Function attributes such as the dynamic shared-memory limit belong to a device, so every device a process
+// launches on needs its own cudaFuncSetAttribute.
+struct PerDeviceOnce {
+  static constexpr int kMaxDevices = 64;
+  std::once_flag flag[kMaxDevices];
+  template <class F>
+  void operator()(F&& f) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+      f();
+      return;
+    }
+    std::call_once(flag[dev], std::forward<F>(f));
+  }
+};
+
+// Writes `code` into a device error word the way the kernels do (first error wins), in the stream's order.
+void record_error_async(int* err, int code, cudaStream_t stream);
 
 // Host-side count of kernel launches issued by this library (bench.py reports it per timed region).
 inline std::atomic<long>& launch_counter() {
@@ -229,7 +251,8 @@ struct GatherRowsArgs {
 };
 
 void comm_signal(const PeerFlags& f, int slot, int value, cudaStream_t stream);
-void comm_wait(const int* flags, int first, int n, int value, int* err, cudaStream_t stream);
+// limit_ns: the wait's wall-time limit (0: the default, 10 s); on expiry kErrTimeoutPeer is recorded in err.
+void comm_wait(const int* flags, int first, int n, int value, int* err, cudaStream_t stream, uint64_t limit_ns = 0);
 void comm_reduce_rows(const ReduceRowsArgs& a, cudaStream_t stream);
 void comm_gather_rows(const GatherRowsArgs& a, cudaStream_t stream);
 void* ipc_malloc(size_t bytes);

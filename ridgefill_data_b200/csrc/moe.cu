@@ -480,11 +480,8 @@ void grouped_gemm(const __nv_bfloat16* xp, long rows_cap, const __nv_bfloat16* w
                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("grouped_gemm: tensor map encode failed " + std::to_string((int)r));
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM);
-    set = true;
-  }
+  static PerDeviceOnce once;
+  once([] { cudaFuncSetAttribute(grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G_SMEM); });
   GroupedArgs a{N, K, E, seg_start, tile_start, out, ldo, swiglu, err};
   int dev = 0;
   cudaGetDevice(&dev);

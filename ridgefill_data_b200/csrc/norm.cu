@@ -217,4 +217,13 @@ void embed_gather(const __nv_bfloat16* table, const int64_t* ids, __nv_bfloat16*
   count_launch();
 }
 
+// ------------------------------------------------------------------------------------ host-side error records
+__global__ void record_error_kernel(int* err, int code) { record_error(err, code); }
+
+void record_error_async(int* err, int code, cudaStream_t stream) {
+  if (err == nullptr) return;
+  record_error_kernel<<<1, 1, 0, stream>>>(err, code);
+  count_launch();
+}
+
 }  // namespace rf

@@ -14,6 +14,7 @@
 // copy and polled locally with ld.acquire.sys; every wait is bounded (kCommWaitNs) and a timeout records
 // kErrTimeoutPeer and skips the data movement. The grid never exceeds one CTA per SM, so all CTAs are resident
 // while they wait.
+#include "gemm.h"
 #include "kernels.h"
 #include "comm.cuh"
 
@@ -132,10 +133,8 @@ __global__ void nvls_barrier_kernel(NvlsFlags f, int slot, int epoch, int* err) 
 }
 
 static int grid_for(long units, int device) {
-  static int sms[16] = {0};
-  if (sms[device] == 0) cudaDeviceGetAttribute(&sms[device], cudaDevAttrMultiProcessorCount, device);
   const long want = (units + kNvlsThreads - 1) / kNvlsThreads;
-  return (int)std::max(1L, std::min<long>(want, sms[device]));
+  return (int)std::max(1L, std::min<long>(want, num_sms(device)));
 }
 
 void nvls_allreduce(const NvlsAllReduceArgs& a, cudaStream_t stream) {

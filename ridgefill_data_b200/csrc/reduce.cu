@@ -201,12 +201,11 @@ __global__ void window_mass_combine_kernel(WindowMassArgs a, int nq_total, int n
 
 void window_mass(const WindowMassArgs& a, cudaStream_t stream) {
   if (a.n <= 0 || a.w <= 0) return;
-  static bool set = false;
-  if (!set) {
+  static PerDeviceOnce once;
+  once([] {
     cudaFuncSetAttribute(window_mass_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(WmSmem));
     cudaFuncSetAttribute(window_mass_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(WmSmem));
-    set = true;
-  }
+  });
   const int nblk = (a.n + WM_KEYS - 1) / WM_KEYS;
   const dim3 grid(nblk, a.hkv);
   window_mass_kernel<1><<<grid, 128, sizeof(WmSmem), stream>>>(a);

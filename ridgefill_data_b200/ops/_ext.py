@@ -86,9 +86,11 @@ def check_errors(device=None):
     """Raise if any kernel recorded an error (a bounded wait that timed out, a bad shape or index) in the device
     error word; clears it."""
     import torch
-    dev = torch.cuda.current_device() if device is None else torch.device(device).index or 0
+    dev = torch.device(device).index if device is not None else None
+    if dev is None:                      # None or a bare "cuda": the current device
+        dev = torch.cuda.current_device()
     w = ext().error_word(dev)
     code = int(w.item())
     if code:
         w.zero_()
-        raise RuntimeError(f"sm_100a kernel reported error code {code}: {ERROR_CODES.get(code, 'unknown')}")
+        raise KernelError("check_errors", code)

@@ -63,8 +63,8 @@ def test_zero_repair_is_a_no_op(model):
     before = {i: {k: v.clone() for k, v in c.items() if torch.is_tensor(v)} for i, c in enumerate(cache)}
     MT.repair(model, cache, hb, arm.split, 0)
     for i, c in enumerate(cache):
-        for k, v in before[i].items():
-            assert torch.equal(c[k], v)
+        for k, v in before[i].items():   # reserve rows past the filled length are uninitialised (may hold NaN)
+            torch.testing.assert_close(c[k], v, rtol=0, atol=0, equal_nan=True)
 
 
 def test_partial_repair_touches_rows_below_r_only(model):
