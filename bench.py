@@ -159,6 +159,10 @@ def main():
                     help="extra prompt lengths (comma-separated, or 'none') timed after the headline length: p50 "
                          "TTFT of RidgeFill and of full prefill at each; 'auto' = 32K, 64K and 128K for the 27B hybrid")
     ap.add_argument("--sweep-steps", type=int, default=5, help="timed steps per sweep length (p50 over them)")
+    ap.add_argument("--arm", default="ridgefill", choices=("ridgefill", "quality"),
+                    help="ridgefill (plain fill of every late prefix row) or quality (plus exact prefix rows chosen by "
+                         "the lower layers' window attention mass, --qattn-share of the prompt)")
+    ap.add_argument("--qattn-share", type=float, default=0.2)
     ap.add_argument("--parallel", default="tp", choices=("tp", "dp"))
     ap.add_argument("--stages", action="store_true",
                     help="after the timed steps, one extra step with per-stage device times (lower layers, fill, "
@@ -213,9 +217,20 @@ def main():
     tok_host = torch.empty(1, dtype=torch.long).pin_memory()
 
     def step(ids):
+        if args.arm == "quality":
+            return quality_step(ids)
         hs, lower = run_lower(model, ids, [arm.split])
         logits, _, _ = finish(model, ids, hs[arm.split], lower, arm, keep=1, keep_cache=False)
         return logits
+
+    from ridgefill_data_b200.engine.quality import QualityMode, prefill_quality
+    qmode = QualityMode(qattn_share=args.qattn_share)
+
+    def quality_step(ids):
+        """The quality mode (engine/quality.py): exact prefix rows (rule tokens, repeated spans of the prompt's end,
+        and the rows the last 64 prompt rows attend to most in the exact lower layers) recomputed exactly through
+        every late layer over the filled rows. Synthetic token ids have no digit or special tokens."""
+        return prefill_quality(model, ids, arm, qmode, keep=1, keep_cache=False)[0]
 
     def barrier():
         if world > 1:
@@ -302,7 +317,9 @@ def main():
     base = BASELINE_TOK_S.get(args.model, {}).get(args.seq)
     from ridgefill_data_b200.eval.cost import CostModel
     cost = CostModel(cfg)
-    flops = 2 * cost.ridgefill(args.seq, args.split, args.tail) * (1 if tp_mode else world)
+    macs = (cost.bypass(args.seq, args.split, args.tail, round(args.qattn_share * args.seq), select="qattn")
+            if args.arm == "quality" else cost.ridgefill(args.seq, args.split, args.tail))
+    flops = 2 * macs * (1 if tp_mode else world)
     peaks = measured_peaks()
     tflops = flops / (ms_max / 1e3) / 1e12
     by_len = {str(args.seq): dict(ttft_p50_ms=round(p50_max, 3),
@@ -320,7 +337,9 @@ def main():
                     vs_published_other_hw=round(value / base, 3) if base else None, dtype="bf16",
                     data="synthetic (seeded uniform prompt; random-init weights and ridge maps of the named shapes)",
                     config=dict(model=args.model, global_batch=1 if tp_mode else world, seq_len=args.seq,
-                                split=args.split, tail=args.tail,
+                                split=args.split, tail=args.tail, arm=args.arm,
+                                **({"qattn_share": args.qattn_share, "qattn_window": 64} if args.arm == "quality"
+                                   else {}),
                                 parallelism=(f"tp{world}" + ("" if args.tp_comm == "nccl" else f"-{args.tp_comm}")
                                              + ("-rowfill" if args.tp_fill == "rows" else "")) if tp_mode
                                 else f"dp{world}",

@@ -1,5 +1,6 @@
 // Flash prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM), for queries at contiguous
-// positions q_start .. q_start + nq - 1 over keys 0 .. nk - 1 (query at position p sees keys j <= p).
+// positions q_start .. q_start + nq - 1, or at the ascending positions qpos[0 .. nq) (the exact rows of a bypass
+// arm), over keys 0 .. nk - 1 (query at position p sees keys j <= p).
 //
 // CTA = 128 query rows of one query head (GQA: K/V of head / (hq / hkv)); 192 threads:
 //   warp 0      TMA: Q once, K and V tiles of BN keys into a 2-stage ring (3-D tensor maps [heads][rows][hd], so
@@ -34,6 +35,7 @@ struct TcFaCfg {
 
 struct TcFaArgs {
   int hq, hkv, nq, nk, q_start;
+  const int* qpos;   // ascending query positions, or nullptr: q_start + row
   float scale_log2;
   const __nv_bfloat16* gate;
   long gate_row, gate_head;
@@ -86,7 +88,9 @@ __global__ void __launch_bounds__(192, 1)
   const int kvh = head / (a.hq / a.hkv);
   const int q0 = qt * 128;
   const int rows_valid = min(128, a.nq - q0);
-  const int n_keys = min(a.nk, a.q_start + q0 + rows_valid);
+  // keys this tile reads: up to the last (largest) query position of the tile
+  const int last_pos = a.qpos != nullptr ? a.qpos[q0 + rows_valid - 1] : a.q_start + q0 + rows_valid - 1;
+  const int n_keys = max(0, min(a.nk, last_pos + 1));
   const int ntiles = (n_keys + BN - 1) / BN;
 
   if (threadIdx.x == 0) {
@@ -199,7 +203,8 @@ __global__ void __launch_bounds__(192, 1)
     // ---------------------------------------------------------------- softmax + epilogue
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int pos = a.q_start + q0 + r;
+    // rows past nq see no key (their outputs are not stored)
+    const int pos = a.qpos == nullptr ? a.q_start + q0 + r : (r < rows_valid ? a.qpos[q0 + r] : -1);
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
@@ -372,7 +377,7 @@ static void launch_tc(const AttnArgs& x, cudaStream_t stream) {
   CUtensorMap tq = tmap3(x.q, HD, x.nq, x.hq, x.q_head_stride, 128);
   CUtensorMap tk = tmap3(x.k, HD, x.nk, x.hkv, x.kv_head_stride, BN);
   CUtensorMap tv = tmap3(x.v, HD, x.nk, x.hkv, x.kv_head_stride, BN);
-  TcFaArgs a{x.hq, x.hkv, x.nq, x.nk, x.q_start, x.scale * 1.4426950408889634f, x.gate, x.gate_row, x.gate_head,
+  TcFaArgs a{x.hq, x.hkv, x.nq, x.nk, x.q_start, x.qpos, x.scale * 1.4426950408889634f, x.gate, x.gate_row, x.gate_head,
              x.out, x.out_row, x.err};
   dim3 grid((x.nq + 127) / 128, x.hq);
   tc_flash_kernel<HD, BN><<<grid, 192, Cfg::SMEM, stream>>>(tq, tk, tv, a);
@@ -380,7 +385,7 @@ static void launch_tc(const AttnArgs& x, cudaStream_t stream) {
 }
 
 bool flash_attention_tc(const AttnArgs& x, cudaStream_t stream) {
-  if (x.qpos != nullptr || x.nq <= 0) return false;
+  if (x.nq <= 0) return false;
   if (reinterpret_cast<uintptr_t>(x.q) % 16 || reinterpret_cast<uintptr_t>(x.k) % 16 ||
       reinterpret_cast<uintptr_t>(x.v) % 16)
     return false;

@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import torch
 
+from ..ridge.projector import Projector
 from .arm import ORACLE_RESCALE, TAIL_RESCALE
 
 _EPS = 1e-30
@@ -200,7 +201,10 @@ class _LateLayers:
     def projected(self, i):
         a = self.arm
         refreshed = a.refresh is not None and i > a.refresh
-        x = (a.refresh_projector if refreshed else a.projector)(i, self.src)
+        proj = a.refresh_projector if refreshed else a.projector
+        on_device = getattr(self.model, "project_map", None)      # the B200 model's own GEMM
+        x = on_device(proj, i, self.src) if on_device is not None and isinstance(proj, Projector) \
+            else proj(i, self.src)
         if a.tail_bias_from is None or i < a.tail_bias_from:
             return x, None
         # self.h holds the tail's layer-i inputs: the mean tail residual of the map is added to every prefix row

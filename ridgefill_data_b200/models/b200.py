@@ -214,6 +214,52 @@ class _B200:
             h2 = G.linear(y, wo, residual=h)
         return self.mlp(i, h2)
 
+    def layer_rows(self, i, h, pos, rows, cache):
+        """Exact rows on the kernels: cache[i] is written from every row's input h (the filled prefix with the exact
+        rows' true inputs in place) and the exact layer output of rows h[rows] is returned, as the torch models'
+        layer_rows (models/llama.py, models/hybrid.py; the bypass of code/kva/kva.py:392-459).
+        Attention: K/V of every row, queries of the selected rows only, tcgen05 attention at their positions. GDN:
+        the delta rule runs over every row (a row's output needs the state at its own position); the output norm,
+        out_proj and the MLP run on the selected rows."""
+        w = self.W[i]
+        x = self._norm(h, w["ln1"])
+        hr = h[rows]
+        if self.layer_types[i] == "attn":
+            hd, hq = self.head_dim, self.n_heads
+            gated = self.cfg.gated_attn
+            qw = hq * hd * (2 if gated else 1)
+            c = cache[i]
+            self._write_kv(i, G.linear(x, w["qkv_p"][qw:]), pos, c)
+            p0, parr = self._span(pos)
+            tables = self.rope(p0 + pos.numel() if parr is None else int(pos.max()) + 1)
+            rpos = pos[rows].to(torch.int32).contiguous()
+            qg = G.linear(x[rows], w["qkv_p"][:qw])
+            nr = qg.shape[0]
+            q = torch.empty(hq, nr, hd, dtype=self.dtype, device=self.device)
+            K.head_norm_rope(qg, hq, hd, 2 * hd if gated else hd, q, nr * hd, hd, norm_w=w.get("q_norm"),
+                             norm_mode=self._qk_mode(), eps=self.eps, tables=tables, rot=self.cfg.rot_dim, pos=rpos)
+            y = torch.empty(nr, hq * hd, dtype=self.dtype, device=self.device)
+            K.attention(q, c["kbuf"], c["vbuf"], c["n"], self.scale, y, qpos=rpos,
+                        gate=qg[:, hd:] if gated else None, gate_head=2 * hd)
+            wo = w["o"]
+        else:
+            proj = G.linear(x, w["in_p"])
+            out = self._gdn_core_dev(i, proj, cache, True)
+            z = proj[:, self.conv_dim + 2 * self.nv:]
+            y = K.gated_rmsnorm(out[rows], z[rows], w["norm"], self.nv, self.cfg.gdn_dv, self.eps)
+            wo = w["out"]
+        h2 = self.tp.row_parallel(y, wo, hr) if self.tp is not None else G.linear(y, wo, residual=hr)
+        return self.mlp(i, h2)
+
+    def project_map(self, projector, i, src):
+        """x_i = src W_i^T + c_i on the tcgen05 GEMM (bias epilogue); column-sharded under tensor parallelism."""
+        W, B = projector.device_maps(self.device)
+        w = W[i] if W[i].dtype == self.dtype else W[i].to(self.dtype)
+        c = B[i] if B[i].dtype == self.dtype else B[i].to(self.dtype)
+        if self.tp is not None:
+            return self.tp.map_fill(src, w, c)
+        return G.linear(src, w, bias=c)
+
     def fill(self, i, x, pos, cache, st=None, checkpoint_every=None, **_):
         if checkpoint_every:
             return super().fill(i, x, pos, cache, st=st, checkpoint_every=checkpoint_every)

@@ -3,8 +3,10 @@
     python -m ridgefill_data_b200.serve --model qwen3.8-27b --synthetic-maps --port 8080          # random-init shape
     python -m ridgefill_data_b200.serve --checkpoint DIR --maps maps.safetensors --tokenizer DIR   # a real model
 
-Modes per request (`ridgefill_mode`): "on" = RidgeFill (split / tail of the maps or the flags), "off" = exact
-prefill. Decoding is always exact and greedy.
+Modes per request (`ridgefill_mode`): "on" = RidgeFill (split / tail of the maps or the flags), "quality" = RidgeFill
+with exact prefix rows (engine/quality.py: digit / special tokens, repeated spans of the prompt's end, the rows the
+prompt's end attends to most; exact prefill below --min-prompt), "off" = exact prefill. Decoding is always exact and
+greedy.
 """
 from __future__ import annotations
 
@@ -35,12 +37,22 @@ def build(args):
         proj = Projector(split, W, B)
     else:
         raise SystemExit("give --maps FILE (a fitted map file) or --synthetic-maps (benchmark shapes only)")
-    arms = {"off": Arm("exact"), "on": Arm("ridgefill", split=split, tail=args.tail, fill="proj", projector=proj)}
     tok, eos = None, ()
     if args.tokenizer:
         from ..eval.text import eos_ids, tokenizer
         tok = tokenizer(args.tokenizer)
         eos = eos_ids(args.tokenizer, tok) if args.tokenizer != "char" else (tok.eos_token_id,)
+    from ..engine.quality import QualityMode, digit_ids_of, special_ids_of
+    q = QualityMode()
+    qmode = QualityMode(min_prompt=getattr(args, "min_prompt", q.min_prompt),
+                        share=getattr(args, "quality_share", q.share),
+                        qattn_share=getattr(args, "qattn_share", q.qattn_share),
+                        qattn_window=getattr(args, "qattn_window", q.qattn_window),
+                        lexical=bool(getattr(args, "lexical", q.lexical)),
+                        digit_ids=digit_ids_of(tok), special_ids=special_ids_of(tok))
+    arms = {"off": Arm("exact"), "on": Arm("ridgefill", split=split, tail=args.tail, fill="proj", projector=proj),
+            "quality": Arm("quality", split=split, tail=args.tail, fill="proj", projector=proj,
+                           meta={"quality": qmode})}
     vocab = model.cfg.vocab
     props = dict(model=str(name), n_layers=model.n_layers, vocab=vocab, split=split, tail=args.tail,
                  backend=args.backend, interleave=args.interleave)
@@ -58,6 +70,11 @@ def main(argv=None):
     ap.add_argument("--split", type=int, default=32)
     ap.add_argument("--tail", type=int, default=4096)
     ap.add_argument("--tokenizer")
+    ap.add_argument("--min-prompt", type=int, default=8192, help="quality mode: shorter prompts run exact")
+    ap.add_argument("--quality-share", type=float, default=0.5, help="quality mode: cap on exact prefix rows")
+    ap.add_argument("--qattn-share", type=float, default=0.2, help="quality mode: rows picked by window attention")
+    ap.add_argument("--qattn-window", type=int, default=64)
+    ap.add_argument("--lexical", type=int, default=1, help="quality mode: repeated-span rows (1 on, 0 off)")
     ap.add_argument("--interleave", type=int, default=4, help="decode round every this many prefill layers (0: off)")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8080)

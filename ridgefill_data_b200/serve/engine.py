@@ -157,7 +157,13 @@ class Scheduler:
         tick = self._tick_for(req)
         try:
             ids = req.ids.to(model.device)
-            if arm.fill == "exact" or arm.split is None:
+            quality = arm.meta.get("quality")
+            if quality is not None:
+                from ..engine.quality import prefill_quality
+                logits, cache, P, rows = prefill_quality(model, ids, arm, quality, keep=1,
+                                                         reserve=req.n_predict + 64, tick=tick)
+                req.filled, hs = int(P) - len(rows), None
+            elif arm.fill == "exact" or arm.split is None:
                 hs, cache = run_lower(model, ids, [model.n_layers], tick=tick, reserve=req.n_predict + 64)
                 logits = model.logits(hs[model.n_layers][-1:])
                 req.filled = 0

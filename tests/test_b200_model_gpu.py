@@ -116,3 +116,54 @@ def test_moe_forward_matches_torch():
     ld, _ = dut.forward_exact(ids, keep=keep)
     l32, _ = _fp32(MOE).forward_exact(ids, keep=keep)
     assert _rel(ld, l32) < 1.5 * _rel(lr, l32) + 5e-3, (_rel(ld, l32), _rel(lr, l32))
+
+
+@pytest.mark.parametrize("cfg", [HYB, LLAMA, QWEN3], ids=lambda c: c.name)
+def test_exact_rows_layer_rows_matches_fp32(cfg):
+    """layer_rows on the kernels (K/V of every row, queries of the exact rows at their positions on the tcgen05
+    attention, GDN over every row) against the fp32 oracle's layer_rows, one late layer at a time."""
+    dut, f32 = from_config(cfg, seed=0, device="cuda", std=0.05, backend="b200"), _fp32(cfg)
+    n = 300
+    g = torch.Generator(device="cuda").manual_seed(7)
+    h = torch.randn(n, cfg.hidden, device="cuda", generator=g)
+    pos = torch.arange(n, device="cuda")
+    rows = torch.tensor(sorted({3, 17, 64, 65, 130, 200, 257, 299}), device="cuda")
+    for i in range(cfg.n_layers):
+        cd, cf = dut.new_cache(), f32.new_cache()
+        yd = dut.layer_rows(i, h.bfloat16(), pos, rows, cd)
+        yf = f32.layer_rows(i, h, pos, rows, cf)
+        assert yd.shape == yf.shape == (rows.numel(), cfg.hidden)
+        assert _rel(yd, yf) < 3e-2, (i, _rel(yd, yf))
+        if cfg.layer_types[i] == "attn":
+            assert _rel(cd[i]["k"], cf[i]["k"]) < 3e-2 and _rel(cd[i]["v"], cf[i]["v"]) < 3e-2
+        else:
+            assert _rel(cd[i]["rec"], cf[i]["rec"]) < 5e-2
+        # the selected rows' outputs equal the whole layer's outputs at those rows
+        cl = dut.new_cache()
+        full = dut.layer(i, h.bfloat16(), pos, cl)[rows]
+        assert _rel(yd, full) < 2e-2, (i, _rel(yd, full))
+
+
+@pytest.mark.parametrize("cfg", [HYB, LLAMA], ids=lambda c: c.name)
+def test_exact_rows_finish_matches_fp32(cfg):
+    """A bypass arm (ridge fill plus exact prefix rows) through finish() on the kernels against fp32."""
+    split = cfg.n_layers // 2
+    g = torch.Generator(device="cuda").manual_seed(3)
+    d = cfg.hidden
+    W = {i: (torch.eye(d, device="cuda") + 0.01 * torch.randn(d, d, device="cuda", generator=g)).bfloat16()
+         for i in range(split, cfg.n_layers)}
+    B = {i: (0.01 * torch.randn(d, device="cuda", generator=g)).bfloat16() for i in range(split, cfg.n_layers)}
+    arm = Arm("bypass", split=split, tail=100, fill="proj", projector=Projector(split, W, B))
+    ids = torch.randint(0, cfg.vocab, (400,), generator=torch.Generator().manual_seed(2)).cuda()
+    rows = [5, 6, 40, 128, 129, 250, 299]
+    ref, dut = _pair(cfg)
+    out = {}
+    for name, m in (("ref", ref), ("dut", dut), ("f32", _fp32(cfg))):
+        hs, lower = run_lower(m, ids, [split])
+        out[name] = finish(m, ids, hs[split], lower, arm, 4, exact_rows=rows)
+    e_dut, e_ref = _rel(out["dut"][0], out["f32"][0]), _rel(out["ref"][0], out["f32"][0])
+    assert e_dut < 1.5 * e_ref + 5e-3, (e_dut, e_ref)
+    # the exact rows change the answer: without them the logits differ
+    hs, lower = run_lower(dut, ids, [split])
+    plain = finish(dut, ids, hs[split], lower, arm, 4)[0]
+    assert _rel(plain, out["dut"][0]) > 0

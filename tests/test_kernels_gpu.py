@@ -71,18 +71,28 @@ def test_flash_attention(hd, hq, hkv, nq, nk, gated, impl):
     check_errors()
 
 
-def test_flash_attention_qpos():
+@pytest.mark.parametrize("impl,hd,nk,nsel,gated", [("mma", 128, 400, 90, False), ("tcgen05", 128, 400, 90, False),
+                                                  ("tcgen05", 256, 1000, 300, True), ("tcgen05", 128, 2100, 700, False)])
+def test_flash_attention_qpos(impl, hd, nk, nsel, gated):
+    """Queries at arbitrary ascending positions (the exact rows of a bypass arm) against the fp32 oracle."""
     torch.manual_seed(3)
-    hq, hkv, hd, nk = 4, 2, 128, 400
-    qpos = torch.tensor(sorted(set(torch.randint(0, nk, (90,)).tolist())), device=dev)
+    hq, hkv = 4, 2
+    qpos = torch.tensor(sorted(set(torch.randint(0, nk, (nsel,)).tolist())), device=dev)
     nq = qpos.numel()
     q = torch.randn(hq, nq, hd, device=dev).bfloat16()
     k = torch.randn(hkv, nk, hd, device=dev).bfloat16()
     v = torch.randn(hkv, nk, hd, device=dev).bfloat16()
+    gate = torch.randn(nq, hq * 2 * hd, device=dev).bfloat16() if gated else None
     out = torch.empty(nq, hq * hd, device=dev, dtype=torch.bfloat16)
-    K.attention(q, k, v, nk, hd ** -0.5, out, qpos=qpos.int())
+    K.attention(q, k, v, nk, hd ** -0.5, out, qpos=qpos.int(), gate=gate[:, hd:] if gated else None,
+                gate_head=2 * hd, impl=impl)
     ref = O.attend_at(q, k, v, hd ** -0.5, qpos)
+    if gated:
+        ref = ref * torch.sigmoid(gate.view(nq, hq, 2 * hd)[..., hd:].reshape(nq, -1).float())
     assert _rel(out, ref) < 2e-2
+    from ridgefill_data_b200.ops._ext import check_errors
+    torch.cuda.synchronize()
+    check_errors()
 
 
 @pytest.mark.parametrize("n,need_out,with_state", [(200, True, False), (64, True, True), (333, False, True),

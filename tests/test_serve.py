@@ -234,7 +234,8 @@ def test_server_cli_build():
     a = argparse.Namespace(model="tiny-llama", checkpoint=None, backend="torch", device="cpu", maps=None,
                            synthetic_maps=True, split=4, tail=64, tokenizer="char", interleave=4)
     model, arms, tok, eos, props = build(a)
-    assert set(arms) == {"on", "off"} and arms["on"].split == 4 and arms["on"].tail == 64
+    assert set(arms) == {"on", "off", "quality"} and arms["on"].split == 4 and arms["on"].tail == 64
+    assert arms["quality"].meta["quality"].min_prompt == 8192 and arms["quality"].split == 4
     assert props["vocab"] == model.cfg.vocab and eos == (tok.eos_token_id,)
     with pytest.raises(SystemExit):
         build(argparse.Namespace(**dict(vars(a), synthetic_maps=False)))
