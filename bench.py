@@ -116,13 +116,18 @@ def measured_peaks():
         return dict(bf16_tflops_sustained=1400.0, bf16_tflops=1590.0, hbm_gbs=6650.0, source="fallback")
 
 
-def timed(fn, steps):
-    """Run fn() `steps` times back to back with one CUDA event between steps: (mean ms, p50 ms, per-step ms)."""
+def timed(fn, steps, nvtx=False):
+    """Run fn() `steps` times back to back with one CUDA event between steps: (mean ms, p50 ms, per-step ms).
+    nvtx: each step inside an NVTX range named "step" (for a profiler's range filter)."""
     import torch
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     ev[0].record()
     for s in range(steps):
+        if nvtx:
+            torch.cuda.nvtx.range_push("step")
         fn()
+        if nvtx:
+            torch.cuda.nvtx.range_pop()
         ev[s + 1].record()
     torch.cuda.synchronize()
     per = [ev[s].elapsed_time(ev[s + 1]) for s in range(steps)]
@@ -249,7 +254,7 @@ def main():
         barrier()
         torch.cuda.synchronize()
         launches0 = ext().launch_count()
-        ms, p50_ms, _ = timed(lambda: step(ids_dev), args.steps)
+        ms, p50_ms, _ = timed(lambda: step(ids_dev), args.steps, nvtx=os.environ.get("RF_NVTX") == "1")
         barrier()
         launches = ext().launch_count() - launches0
         clocks = sampler.stop()
