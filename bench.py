@@ -143,7 +143,13 @@ def build_engine(args, device):
     cfg = PRESETS[args.model]
     model = from_config(cfg, seed=0, device=device, backend="b200", std=0.02)
     W, B = synthetic_maps(cfg.hidden, args.split, cfg.n_layers, device)   # ridge maps near the identity
-    arm = Arm("ridgefill", split=args.split, tail=args.tail, fill="proj", projector=Projector(args.split, W, B))
+    if args.maps == "streamed":                 # pinned host maps streamed through a ring of device slots
+        from ridgefill_data_b200.ridge.projector import StreamedProjector
+        proj = StreamedProjector(args.split, W, B, slots=args.map_slots)
+        del W, B
+    else:
+        proj = Projector(args.split, W, B)
+    arm = Arm("ridgefill", split=args.split, tail=args.tail, fill="proj", projector=proj)
     return cfg, model, arm
 
 
@@ -168,6 +174,10 @@ def main():
                     help="ridgefill (plain fill of every late prefix row) or quality (plus exact prefix rows chosen by "
                          "the lower layers' window attention mass, --qattn-share of the prompt)")
     ap.add_argument("--qattn-share", type=float, default=0.2)
+    ap.add_argument("--maps", default="resident", choices=("resident", "streamed"),
+                    help="ridge maps resident in HBM, or in pinned host memory streamed per prompt through "
+                         "--map-slots device buffers (copies overlap the lower layers)")
+    ap.add_argument("--map-slots", type=int, default=8)
     ap.add_argument("--parallel", default="tp", choices=("tp", "dp"))
     ap.add_argument("--stages", action="store_true",
                     help="after the timed steps, one extra step with per-stage device times (lower layers, fill, "
@@ -224,7 +234,7 @@ def main():
     def step(ids):
         if args.arm == "quality":
             return quality_step(ids)
-        hs, lower = run_lower(model, ids, [arm.split])
+        hs, lower = run_lower(model, ids, [arm.split], maps=arm.projector)
         logits, _, _ = finish(model, ids, hs[arm.split], lower, arm, keep=1, keep_cache=False)
         return logits
 
@@ -342,7 +352,8 @@ def main():
                     vs_published_other_hw=round(value / base, 3) if base else None, dtype="bf16",
                     data="synthetic (seeded uniform prompt; random-init weights and ridge maps of the named shapes)",
                     config=dict(model=args.model, global_batch=1 if tp_mode else world, seq_len=args.seq,
-                                split=args.split, tail=args.tail, arm=args.arm,
+                                split=args.split, tail=args.tail, arm=args.arm, maps=args.maps,
+                                **({"map_slots": args.map_slots} if args.maps == "streamed" else {}),
                                 **({"qattn_share": args.qattn_share, "qattn_window": 64} if args.arm == "quality"
                                    else {}),
                                 parallelism=(f"tp{world}" + ("" if args.tp_comm == "nccl" else f"-{args.tp_comm}")
@@ -356,7 +367,8 @@ def main():
                     ttft_ms=round(ms_max, 3), ttft_p50_ms=round(p50_max, 3),
                     flops_per_step=round(flops), tflops=round(tflops, 1),
                     frac_of_sustained_bf16=round(tflops / (peaks["bf16_tflops_sustained"] * world), 3),
-                    peaks_source=peaks["source"], ttft_by_len=by_len)
+                    peaks_source=peaks["source"], ttft_by_len=by_len,
+                    hbm_peak_gib=round(torch.cuda.max_memory_allocated(device) / 2 ** 30, 2))
         if exact_ms:
             line.update(exact_prefill_ms=round(exact_max, 3), speedup_vs_exact=round(exact_max / p50_max, 3))
         print(json.dumps(line), flush=True)

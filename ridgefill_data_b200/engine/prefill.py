@@ -33,13 +33,16 @@ def _keep_split(model, h, device):
     return model.stable(h) if hasattr(model, "stable") else h
 
 
-def run_lower(model, ids, splits, hs_device=None, hook=None, mix=None, tick=None, reserve=64):
+def run_lower(model, ids, splits, hs_device=None, hook=None, mix=None, tick=None, reserve=64, maps=None):
     """Exact forward through layers < max(splits).
 
     Returns ({split: layer-split input rows [N, H]}, a cache whose layers < max(splits) are filled). hook(i, h) sees
     every layer input, mix(i, a) every mixer output; tick(i) runs before layer i (a scheduler's slot for other
-    work between layers); `reserve` cache rows past the prompt are preallocated so decode appends in place."""
+    work between layers); `reserve` cache rows past the prompt are preallocated so decode appends in place; maps: the
+    arm's projector, told that a prompt starts (streamed maps begin their copies, overlapping these layers)."""
     wanted = {splits} if isinstance(splits, int) else set(splits)
+    if maps is not None and hasattr(maps, "begin") and model.device.type == "cuda":
+        maps.begin(model.device)
     ids = ids.to(model.device)
     n = ids.shape[0]
     if hasattr(model, "reserve"):
@@ -365,5 +368,5 @@ def prefill(model, ids, arm, keep=1, **kw):
         logits, cache = model.forward_exact(ids.to(model.device),
                                             keep=torch.arange(n - keep, n, device=model.device))
         return logits, cache, 0
-    hs, lower = run_lower(model, ids, [arm.split])
+    hs, lower = run_lower(model, ids, [arm.split], maps=arm.projector)
     return finish(model, ids, hs[arm.split], lower, arm, keep, **kw)

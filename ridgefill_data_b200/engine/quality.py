@@ -121,7 +121,8 @@ def prefill_quality(model, ids, arm, mode, keep=1, keep_cache=True, reserve=64, 
     def grab(i, h):
         if i in layers:
             win[i] = h[n - w:n].clone()
-    hs, lower = run_lower(model, ids, [arm.split], hook=grab if layers else None, reserve=reserve, tick=tick)
+    hs, lower = run_lower(model, ids, [arm.split], hook=grab if layers else None, reserve=reserve, tick=tick,
+                          maps=arm.projector)
     P = arm.prefix_len(n)
     mass = S.window_mass(model, win, lower, layers, end=n) if layers else None
     rows = pick_rows(ids.cpu(), P, mode, mass)

@@ -253,12 +253,12 @@ class _B200:
 
     def project_map(self, projector, i, src):
         """x_i = src W_i^T + c_i on the tcgen05 GEMM (bias epilogue); column-sharded under tensor parallelism."""
-        W, B = projector.device_maps(self.device)
-        w = W[i] if W[i].dtype == self.dtype else W[i].to(self.dtype)
-        c = B[i] if B[i].dtype == self.dtype else B[i].to(self.dtype)
-        if self.tp is not None:
-            return self.tp.map_fill(src, w, c)
-        return G.linear(src, w, bias=c)
+        w, c = projector.device_map(i, self.device)
+        w = w if w.dtype == self.dtype else w.to(self.dtype)
+        c = c if c.dtype == self.dtype else c.to(self.dtype)
+        x = self.tp.map_fill(src, w, c) if self.tp is not None else G.linear(src, w, bias=c)
+        projector.done_with(i)
+        return x
 
     def fill(self, i, x, pos, cache, st=None, checkpoint_every=None, **_):
         if checkpoint_every:
@@ -278,18 +278,19 @@ class _B200:
     def fill_batch(self, layers, b, pos, cache, projector=None):
         """Cache-only fills of every late layer from the same boundary rows b: x_i = b W_i^T + c_i (tcgen05
         GEMM with the bias epilogue; identity fill when projector is None), then the layer's fill."""
-        if projector is not None:
-            W, B = projector.device_maps(self.device)
         for i in layers:
             if projector is None:
                 x = b
             else:
-                w = W[i] if W[i].dtype == self.dtype else W[i].to(self.dtype)
-                c = B[i] if B[i].dtype == self.dtype else B[i].to(self.dtype)
+                w, c = projector.device_map(i, self.device)
+                w = w if w.dtype == self.dtype else w.to(self.dtype)
+                c = c if c.dtype == self.dtype else c.to(self.dtype)
                 if getattr(self.tp, "row_fill", None) is not None:
                     self.tp.row_fill.fill_layer(self, i, b, pos, cache, w, c)
+                    projector.done_with(i)
                     continue
                 x = self.tp.map_fill(b, w, c) if self.tp is not None else G.linear(b, w, bias=c)
+                projector.done_with(i)
             self.fill(i, x, pos, cache)
 
 

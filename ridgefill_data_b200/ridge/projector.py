@@ -100,8 +100,112 @@ class Projector:
         W, B = self.device_maps(b.device)
         return F.linear(b, W[i].to(b.dtype), B[i].to(b.dtype))
 
+    def device_map(self, i, device):
+        """(W_i, c_i) on `device` for a consumer that calls done_with(i) once its kernels reading them are queued."""
+        W, B = self.device_maps(device)
+        return W[i], B[i]
+
+    def done_with(self, i):
+        """The consumer of layer i's map has queued every kernel that reads it (resident maps: nothing to do)."""
+
+    def begin(self, device):
+        """A prompt's prefill starts (resident maps: nothing to do)."""
+
     def release(self):
         self._dev = None
+
+
+class StreamedProjector(Projector):
+    """Maps kept in pinned host memory and streamed to the GPU per prompt, for HBM budgets that cannot hold every late
+    layer's map (the E3 engine's --ridgefill-stream-projector option, code/qwen38-27b-kit/common.py:27).
+
+    A ring of `slots` device buffers holds the maps in flight. begin() (called as the prompt's lower layers start)
+    queues the host-to-device copies of the first `slots` maps on a copy stream, so they overlap the lower layers;
+    device_map(i) makes the compute stream wait for layer i's copy; done_with(i) records when the compute stream is
+    finished with the slot and queues the copy of map i + slots into it. HBM held: slots x (d_out x (d_in + 1)) bf16
+    instead of every late layer's map. Maps are consumed in layer order."""
+
+    def __init__(self, split, weights, biases, meta=None, slots=4):
+        host_w = {i: w.detach().to("cpu").contiguous().pin_memory() for i, w in weights.items()}
+        host_b = {i: c.detach().to("cpu").contiguous().pin_memory() for i, c in biases.items()}
+        super().__init__(split, host_w, host_b, meta)
+        self.slots = max(1, int(slots))
+        self._ring = None
+        self._order = []
+        self._ready = {}
+
+    def _setup(self, device):
+        device = torch.device(device)
+        if self._ring is not None and self._ring["device"] == device:
+            return self._ring
+        first = self.layers[0]
+        W0, B0 = self.W[first], self.b[first]
+        k = min(self.slots, len(self.layers))
+        self._ring = dict(device=device, stream=torch.cuda.Stream(device=device),
+                          w=[torch.empty_like(W0, device=device) for _ in range(k)],
+                          b=[torch.empty_like(B0, device=device) for _ in range(k)],
+                          free=[None] * k, slot_of={})
+        return self._ring
+
+    def _issue(self, pos):
+        r = self._ring
+        layer = self._order[pos]
+        slot = pos % len(r["w"])
+        with torch.cuda.stream(r["stream"]):
+            if r["free"][slot] is not None:
+                r["stream"].wait_event(r["free"][slot])     # the kernels that read this slot last have finished
+            r["w"][slot].copy_(self.W[layer], non_blocking=True)
+            r["b"][slot].copy_(self.b[layer], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(r["stream"])
+        self._ready[layer] = (slot, ev, pos)
+
+    def begin(self, device):
+        r = self._setup(device)
+        self._order = list(self.layers)
+        self._ready = {}
+        for pos in range(min(len(r["w"]), len(self._order))):
+            self._issue(pos)
+
+    def device_map(self, i, device):
+        if self._ring is None or self._ring["device"] != torch.device(device) or i not in self._ready:
+            self.begin(device)                                  # a consumer that did not call begin()
+            while self._ready and i not in self._ready:
+                self.done_with(next(iter(self._ready)))
+        slot, ev, _ = self._ready[i]
+        torch.cuda.current_stream(self._ring["device"]).wait_event(ev)
+        return self._ring["w"][slot], self._ring["b"][slot]
+
+    def done_with(self, i):
+        if i not in self._ready:
+            return
+        slot, _, pos = self._ready.pop(i)
+        r = self._ring
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(r["device"]))
+        r["free"][slot] = ev
+        nxt = pos + len(r["w"])
+        if nxt < len(self._order):
+            self._issue(nxt)
+
+    def device_maps(self, device):
+        raise RuntimeError("streamed maps are read one layer at a time (device_map / done_with)")
+
+    def __call__(self, i, b):
+        if b.device.type != "cuda":
+            return F.linear(b, self.W[i].to(b.device, b.dtype), self.b[i].to(b.device, b.dtype))
+        w, c = self.device_map(i, b.device)
+        out = F.linear(b, w.to(b.dtype), c.to(b.dtype))
+        self.done_with(i)
+        return out
+
+    def resident_bytes(self):
+        r = self._ring
+        return 0 if r is None else sum(t.numel() * t.element_size() for t in r["w"] + r["b"])
+
+    def release(self):
+        torch.cuda.synchronize() if self._ring is not None else None
+        self._ring, self._ready = None, {}
 
     def tensors(self):
         return {f"layer.{i}": torch.cat((self.W[i], self.b[i][:, None]), 1).to(torch.bfloat16).cpu().contiguous()

@@ -168,7 +168,8 @@ class Scheduler:
                 logits = model.logits(hs[model.n_layers][-1:])
                 req.filled = 0
             else:
-                hs, lower = run_lower(model, ids, [arm.split], tick=tick, reserve=req.n_predict + 64)
+                hs, lower = run_lower(model, ids, [arm.split], tick=tick, reserve=req.n_predict + 64,
+                                      maps=arm.projector)
                 logits, cache, P = finish(model, ids, hs[arm.split], lower, arm, keep=1, tick=tick)
                 req.filled = int(P)
             del hs

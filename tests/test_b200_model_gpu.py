@@ -167,3 +167,29 @@ def test_exact_rows_finish_matches_fp32(cfg):
     hs, lower = run_lower(dut, ids, [split])
     plain = finish(dut, ids, hs[split], lower, arm, 4)[0]
     assert _rel(plain, out["dut"][0]) > 0
+
+
+@pytest.mark.parametrize("slots", [1, 3])
+def test_streamed_maps_equal_resident_maps(slots):
+    """Maps streamed from pinned host memory through a ring of device slots (copies on a side stream, ordered by
+    events) give bitwise the fill of resident maps, through the batched fill and the per-layer path."""
+    from ridgefill_data_b200.ridge.projector import StreamedProjector
+    cfg = HYB
+    dut = from_config(cfg, seed=0, device="cuda", std=0.05, backend="b200")
+    split = cfg.n_layers // 2
+    g = torch.Generator(device="cuda").manual_seed(3)
+    d = cfg.hidden
+    W = {i: (torch.eye(d, device="cuda") + 0.01 * torch.randn(d, d, device="cuda", generator=g)).bfloat16()
+         for i in range(split, cfg.n_layers)}
+    B = {i: (0.01 * torch.randn(d, device="cuda", generator=g)).bfloat16() for i in range(split, cfg.n_layers)}
+    ids = torch.randint(0, cfg.vocab, (400,), generator=torch.Generator().manual_seed(2)).cuda()
+    res = Arm("ridgefill", split=split, tail=100, fill="proj", projector=Projector(split, W, B))
+    sp = StreamedProjector(split, W, B, slots=slots)
+    stream = Arm("ridgefill", split=split, tail=100, fill="proj", projector=sp)
+    for rows in (None, [3, 50, 200]):            # batched fill; per-layer path with exact rows
+        out = {}
+        for name, arm in (("res", res), ("str", stream)):
+            hs, lower = run_lower(dut, ids, [split], maps=arm.projector)
+            out[name] = finish(dut, ids, hs[split], lower, arm, 4, exact_rows=rows)[0]
+        assert torch.equal(out["res"], out["str"]), rows
+    assert sp.resident_bytes() == min(slots, cfg.n_layers - split) * (d * d + d) * 2
