@@ -193,15 +193,13 @@ class _B200:
         return self.logits(h)
 
     # ---- per-layer API
-    def _mixer_out(self, i, h, pos, cache, need_out=True):
+    def _mixer_out(self, i, h, pos, cache, need_out=True, checkpoint_every=None):
         if self.layer_types[i] == "attn":
             return self._attn_mix(i, h, pos, cache), self.W[i]["o"]
-        return self._gdn_mix(i, h, cache), self.W[i]["out"]
+        return self._gdn_mix(i, h, cache, checkpoint_every), self.W[i]["out"]
 
     def layer(self, i, h, pos, cache, mix=None, gdn_checkpoint_every=None, **_):
-        if gdn_checkpoint_every and self.layer_types[i] == "gdn":
-            return super().layer(i, h, pos, cache, gdn_checkpoint_every=gdn_checkpoint_every, mix=mix)
-        y, wo = self._mixer_out(i, h, pos, cache)
+        y, wo = self._mixer_out(i, h, pos, cache, checkpoint_every=gdn_checkpoint_every)
         if self.tp is not None:
             h2 = self.tp.row_parallel(y, wo, h)
             if mix is not None:
@@ -261,8 +259,6 @@ class _B200:
         return x
 
     def fill(self, i, x, pos, cache, st=None, checkpoint_every=None, **_):
-        if checkpoint_every:
-            return super().fill(i, x, pos, cache, st=st, checkpoint_every=checkpoint_every)
         w = self.W[i]
         xn = self._norm(x, w["ln1"])
         if self.layer_types[i] == "attn":
@@ -270,10 +266,10 @@ class _B200:
             kv = G.linear(xn, w["qkv_p"][qw:])
             self._write_kv(i, kv, pos, cache[i])
             return {}
-        self._gdn_fill(i, xn, cache)
+        ck = self._gdn_fill(i, xn, cache, checkpoint_every)
         if st is not None:
             cache[i]["rec"] = cache[i]["rec"] + st.to(cache[i]["rec"])
-        return {}
+        return ck
 
     def fill_batch(self, layers, b, pos, cache, projector=None):
         """Cache-only fills of every late layer from the same boundary rows b: x_i = b W_i^T + c_i (tcgen05
@@ -382,18 +378,47 @@ class B200Hybrid(_B200, Hybrid):
         c["len"] = c.get("len", 0) + proj.shape[0]
         return out
 
-    def _gdn_mix(self, i, h, cache):
+    def _gdn_core_ckpt(self, i, proj, cache, need_out, every):
+        """_gdn_core_dev in pieces of `every` rows (within GDN_ROWS segments, the oracle's grouping), keeping the
+        fp32 recurrent state after every full piece: ({absolute position: state [nv, dk, dv]}, outputs or None).
+        The states are the ones the oracle's delta_rule(checkpoint_every=...) returns (ops/oracle.py)."""
+        from .base import GDN_ROWS
+        if every % 64:
+            raise ValueError(f"checkpoint_every={every} must be a multiple of the chunk (64)")
+        n = proj.shape[0]
+        offset = cache[i].get("len", 0)
+        outs, cks = [], {}
+        for lo in range(0, n, GDN_ROWS):
+            hi = min(n, lo + GDN_ROWS)
+            for s in range(lo, hi, every):
+                e = min(hi, s + every)
+                o = self._gdn_core_dev(i, proj[s:e], cache, need_out)
+                if need_out:
+                    outs.append(o)
+                if e - s == every:
+                    cks[offset + e] = cache[i]["rec"].clone()
+        return cks, (torch.cat(outs) if need_out else None)
+
+    def _gdn_mix(self, i, h, cache, checkpoint_every=None):
         w = self.W[i]
         x = self._norm(h, w["ln1"])
         proj = G.linear(x, w["in_p"])
-        o = self._gdn_core_dev(i, proj, cache, True)
+        if checkpoint_every:
+            ck, o = self._gdn_core_ckpt(i, proj, cache, True, checkpoint_every)
+            if ck:
+                cache[i].setdefault("checkpoints", {}).update(ck)
+        else:
+            o = self._gdn_core_dev(i, proj, cache, True)
         z = proj[:, self.conv_dim + 2 * self.nv:]
         return K.gated_rmsnorm(o, z, w["norm"], self.nv, self.cfg.gdn_dv, self.eps)
 
-    def _gdn_fill(self, i, xn, cache):
+    def _gdn_fill(self, i, xn, cache, checkpoint_every=None):
         w = self.W[i]
         proj = G.linear(xn, w["in_p"][:self.conv_dim + 2 * self.nv])
+        if checkpoint_every:
+            return self._gdn_core_ckpt(i, proj, cache, False, checkpoint_every)[0]
         self._gdn_core_dev(i, proj, cache, False)
+        return {}
 
     def mlp(self, i, h):
         if self.cfg.moe:

@@ -193,3 +193,30 @@ def test_streamed_maps_equal_resident_maps(slots):
             out[name] = finish(dut, ids, hs[split], lower, arm, 4, exact_rows=rows)[0]
         assert torch.equal(out["res"], out["str"]), rows
     assert sp.resident_bytes() == min(slots, cfg.n_layers - split) * (d * d + d) * 2
+
+
+def test_gdn_state_checkpoints_match_fp32():
+    """GDN recurrent-state checkpoints on the kernels (exact layers and cache-only fills) against the fp32 oracle:
+    the same absolute positions, the same states within bf16 tolerance."""
+    dut, f32 = from_config(HYB, seed=0, device="cuda", std=0.05, backend="b200"), _fp32(HYB)
+    ids = torch.randint(0, HYB.vocab, (333,), generator=torch.Generator().manual_seed(5)).cuda()
+    _, cd = dut.forward_exact(ids, gdn_checkpoint_every=128)
+    _, cf = f32.forward_exact(ids, gdn_checkpoint_every=128)
+    for i, t in enumerate(HYB.layer_types):
+        if t != "gdn":
+            continue
+        kd, kf = cd[i]["checkpoints"], cf[i]["checkpoints"]
+        assert sorted(kd) == sorted(kf) == [128, 256]
+        for p in kf:
+            assert _rel(kd[p], kf[p]) < 5e-2, (i, p, _rel(kd[p], kf[p]))
+        assert _rel(cd[i]["rec"], cf[i]["rec"]) < 5e-2
+    # a fill with checkpoints
+    g = torch.Generator(device="cuda").manual_seed(9)
+    x = torch.randn(300, HYB.hidden, device="cuda", generator=g)
+    pos = torch.arange(300, device="cuda")
+    i = HYB.layer_types.index("gdn")
+    c1, c2 = dut.new_cache(), f32.new_cache()
+    k1 = dut.fill(i, x.bfloat16(), pos, c1, checkpoint_every=64)
+    k2 = f32.fill(i, x, pos, c2, checkpoint_every=64)
+    assert sorted(k1) == sorted(k2) == [64, 128, 192, 256]
+    assert all(_rel(k1[p], k2[p]) < 5e-2 for p in k2)
