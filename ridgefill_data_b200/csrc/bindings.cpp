@@ -77,6 +77,13 @@ void gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, c10::optional<tor
 int64_t sm_count(int64_t dev) { return rf::num_sms((int)dev); }
 int64_t launch_count() { return rf::launch_counter().load(); }
 
+// Whether 256-column store / SwiGLU products run on the two-SM kernel (gemm2sm.cu); returns the previous setting.
+bool set_gemm_2sm(bool on) {
+  const bool was = rf::gemm_2sm_enabled;
+  rf::gemm_2sm_enabled = on;
+  return was;
+}
+
 }  // namespace
 
 void register_ops(pybind11::module_& m);   // bind_ops.cpp
@@ -86,6 +93,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("error_word", &error_word);
   m.def("sm_count", &sm_count);
   m.def("launch_count", &launch_count);
+  m.def("set_gemm_2sm", &set_gemm_2sm);
   m.def("gemm", &gemm, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("bias") = py::none(),
         py::arg("residual") = py::none(), py::arg("epi") = 0, py::arg("bn") = 256, py::arg("a_mn") = false,
         py::arg("b_mn") = false, py::arg("k_splits") = 1, py::arg("k_chunk") = 0, py::arg("max_ctas") = 0);

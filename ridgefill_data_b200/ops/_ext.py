@@ -66,6 +66,8 @@ def ext():
             "the sm_100a extension ridgefill_data_b200._C is not built; run `python setup.py build_ext --inplace`"
         ) from e
     _mod = Checked(mod) if os.environ.get("RF_CHECK_EACH") == "1" else mod
+    if os.environ.get("RF_GEMM_2SM") == "0":     # A/B switch: every product on the one-SM GEMM kernel
+        mod.set_gemm_2sm(False)
     return _mod
 
 

@@ -79,3 +79,37 @@ def test_no_error_recorded():
     from ridgefill_data_b200.ops._ext import check_errors
     torch.cuda.synchronize()
     check_errors()
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 64), (300, 1000, 200), (1024, 5120, 5120), (4100, 2304, 1024)])
+def test_two_sm_gemm_matches_one_sm_and_fp32(m, n, k):
+    """The cta_group::2 kernel (256 x 256 tiles over an SM pair) against the fp32 reference and the one-SM kernel,
+    with bias and residual, and the SwiGLU epilogue."""
+    from ridgefill_data_b200.ops import gemm
+    from ridgefill_data_b200.ops._ext import check_errors, ext
+    torch.manual_seed(5)
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05
+    b = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+    h = torch.randn(m, n, device="cuda", dtype=torch.bfloat16)
+    ref = _ref(x, w) + b.float() + h.float()
+    outs = {}
+    for two in (True, False):
+        was = ext().set_gemm_2sm(two)
+        try:
+            outs[two] = gemm.linear(x, w, bias=b, residual=h, bn=256).float()
+        finally:
+            ext().set_gemm_2sm(was)
+    for two, got in outs.items():
+        err = (got - ref).abs().max().item() / ref.abs().max().item()
+        assert err < 1e-2, (two, err)
+    assert (outs[True] - outs[False]).abs().max().item() <= 1e-2 * ref.abs().max().item()
+    if n % 256 == 0:
+        g = torch.randn(n // 2, k, device="cuda", dtype=torch.bfloat16) * 0.05
+        u = torch.randn(n // 2, k, device="cuda", dtype=torch.bfloat16) * 0.05
+        act = gemm.swiglu_linear(x, gemm.pack_gate_up(g, u)).float()
+        rg, ru = _ref(x, g), _ref(x, u)
+        want = torch.nn.functional.silu(rg) * ru
+        assert (act - want).abs().max().item() / want.abs().max().item() < 2e-2
+    torch.cuda.synchronize()
+    check_errors()
