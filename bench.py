@@ -134,6 +134,59 @@ def timed(fn, steps, nvtx=False):
     return ev[0].elapsed_time(ev[steps]) / steps, statistics.median(per), per
 
 
+def fit_bench(args):
+    """bench.py --fit: the ridge fit at a model's full shape, timed by stage (capture with the fp64 Gram sums, the
+    Cholesky solves over the lambda grid, the held-out lambda choice), against the reference's recorded 27B fit
+    (capture 610 s, 90-137 s of eigen-fit per split, 26 min in all for 839,652 rows and splits 16 / 24 / 32 on one
+    RTX 5090). Calibration rows are seeded Zipf(1.1) documents; data parallel over the ranks under torchrun."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=1800), device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    from ridgefill_data_b200.eval.data import zipf_docs
+    from ridgefill_data_b200.models.base import from_config
+    from ridgefill_data_b200.models.config import PRESETS
+    from ridgefill_data_b200.ridge import sweep
+    cfg = PRESETS[args.model]
+    model = from_config(cfg, seed=0, device=device, backend="b200", std=0.02)
+    splits = [int(s) for s in args.fit_splits.split(",")]
+    n_docs = -(-args.fit_rows // args.fit_doc)
+    docs = zipf_docs(n_docs, args.fit_doc, cfg.vocab, seed=1)
+    held = zipf_docs(args.fit_held, args.fit_doc, cfg.vocab, seed=3)
+    timings = {}
+    t0 = time.perf_counter()
+    res = sweep.fit(model, docs, splits, held=held, solver="cholesky", log=None, timings=timings,
+                    group=dist.group.WORLD if world > 1 else None)
+    torch.cuda.synchronize()
+    total = time.perf_counter() - t0
+    stats = torch.tensor([total] + [timings[k] for k in sorted(timings)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    vals = stats.tolist()
+    if rank == 0:
+        print(json.dumps(dict(
+            metric="ridge fit wall time (capture + fp64 Gram sums + Cholesky solves + lambda choice)",
+            value=round(vals[0], 2), unit="s", higher_is_better=False, n_gpus=world, dtype="bf16 activations, fp64 sums",
+            data="synthetic (seeded Zipf(1.1) calibration documents, random-init weights of the named shape)",
+            config=dict(model=args.model, rows=n_docs * args.fit_doc, docs=n_docs, doc_len=args.fit_doc,
+                        splits=splits, held_docs=args.fit_held, lambdas=len(sweep.LAMBDAS),
+                        parallelism=f"dp{world}"),
+            stages_s={k: round(v, 2) for k, v in zip(sorted(timings), vals[1:])},
+            lambda_star={str(S): r["lambda_star"] for S, r in res.items()},
+            hbm_peak_gib=round(torch.cuda.max_memory_allocated(device) / 2 ** 30, 2),
+            reference_recorded=dict(capture_s=610, fit_s_per_split="90-137", total_min=26, rows=839652,
+                                    hardware="1x RTX 5090, PyTorch fit_sweep.py --stream"))), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def build_engine(args, device):
     from ridgefill_data_b200.engine.arm import Arm
     from ridgefill_data_b200.models.base import from_config
@@ -178,6 +231,11 @@ def main():
                     help="ridge maps resident in HBM, or in pinned host memory streamed per prompt through "
                          "--map-slots device buffers (copies overlap the lower layers)")
     ap.add_argument("--map-slots", type=int, default=8)
+    ap.add_argument("--fit", action="store_true", help="time the ridge fit instead of the prefill (see fit_bench)")
+    ap.add_argument("--fit-rows", type=int, default=839652)
+    ap.add_argument("--fit-doc", type=int, default=8192, help="calibration document length (tokens)")
+    ap.add_argument("--fit-splits", default="16,24,32")
+    ap.add_argument("--fit-held", type=int, default=2)
     ap.add_argument("--parallel", default="tp", choices=("tp", "dp"))
     ap.add_argument("--stages", action="store_true",
                     help="after the timed steps, one extra step with per-stage device times (lower layers, fill, "
@@ -196,6 +254,8 @@ def main():
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         return reference_arm(args)
+    if args.fit:
+        return fit_bench(args)
 
     import torch
     import torch.distributed as dist

@@ -205,13 +205,22 @@ def select_lambda_kv(model, held, S, fold_maps, lams):
     return max(lams, key=lambda lam: mean[str(lam)]), mean, per_layer
 
 
+def _now(model):
+    """Wall seconds after the device has finished its queued work (stage boundaries of the fit's timings)."""
+    if model.device.type == "cuda":
+        torch.cuda.synchronize(model.device)
+    return time.perf_counter()
+
+
 def fit(model, docs, splits, lambdas=LAMBDAS, held=None, out_dir=None, name=None, solver=None, center=True,
-        save_stats=False, log=print, meta_extra=None, group=None, unitrms=False, kvfold=False):
+        save_stats=False, log=print, meta_extra=None, group=None, unitrms=False, kvfold=False, timings=None):
     """Fit maps for every split. Returns {S: dict(projector, lambda_star, mean_read_cos, per_layer_read_cos,
     record)}; writes files when out_dir is given. unitrms: also the unit-RMS-target maps of the same capture,
     saved as <name>-sweep-s<S>-unitrms with the raw fit as its control <name>-sweep-s<S>-rawctl
     (results[S]["unitrms"]); kvfold: also the K/V fold (pre-RoPE [k | v] of every late attention layer straight
-    from the unit-RMS boundary state), saved as <name>-kvfold-s<S> (results[S]["kvfold"])."""
+    from the unit-RMS boundary state), saved as <name>-kvfold-s<S> (results[S]["kvfold"]). timings: a dict that
+    receives the stage seconds (capture_s with the Gram sums and their reduction; per split fit_s<S> for the solves
+    over the lambda grid and select_s<S> for the held-out lambda choice)."""
     splits = sorted(int(s) for s in splits)
     name = name or model.cfg.name or "model"
     L = model.n_layers
@@ -226,7 +235,10 @@ def fit(model, docs, splits, lambdas=LAMBDAS, held=None, out_dir=None, name=None
         if stale:
             raise StaleProjector("fitted on another calibration list: " + ", ".join(f"{p} ({r})" for p, r in stale))
     solver = solver or ("cholesky" if model.device.type == "cuda" else "eigen")
+    t_cap = _now(model)
     stats = capture(model, docs, splits, log=log, group=group, unitrms=unitrms, kvfold=kvfold)
+    if timings is not None:
+        timings["capture_s"] = _now(model) - t_cap
     extra = {k: stats.pop(k) for k in ("unitrms", "kvfold") if k in stats}
     results = {}
     for S in sorted(splits, reverse=True):
@@ -242,11 +254,16 @@ def fit(model, docs, splits, lambdas=LAMBDAS, held=None, out_dir=None, name=None
                                                                       extra["kvfold"][S].sq.items()})
             torch.save(dict(state, dtype="float64", docs=[d["name"] for d in docs], model=name, **more),
                        out_dir / f"{name}-s{S}.pt")
+        t_fit = _now(model)
         maps = fit_split(state, S, L, lambdas, solver, center, model.device)
+        t_sel = _now(model)
         if held:
             best, mean, per_layer = select_lambda(model, held, S, maps, lambdas)
         else:
             best, mean, per_layer = lambdas[len(lambdas) // 2], {}, {}
+        if timings is not None:
+            timings[f"fit_s{S}"] = t_sel - t_fit
+            timings[f"select_s{S}"] = _now(model) - t_sel
         W = {i: maps[best][i][0].to(torch.bfloat16).cpu() for i in range(S, L)}
         B = {i: maps[best][i][1].to(torch.bfloat16).cpu() for i in range(S, L)}
         meta = dict(model=name, model_commit="", lam=best, rows=rows, taps=S, sweep=True, note="",
