@@ -28,8 +28,9 @@ struct TcFaCfg {
   static constexpr int K_BYTES = BN * HD * 2;
   static constexpr int V_BYTES = BN * HD * 2;
   static constexpr int P_BYTES = 128 * BN * 2;
-  static constexpr int BAR_BYTES = 8 * 16 + 16;
-  static constexpr int SMEM = 1024 + Q_BYTES + 2 * (K_BYTES + V_BYTES) + P_BYTES + BAR_BYTES;
+  static constexpr int BAR_BYTES = 8 * 18 + 16;
+  // two P buffers: the softmax of block j + 1 writes its P while the tensor cores still read block j's
+  static constexpr int SMEM = 1024 + Q_BYTES + 2 * (K_BYTES + V_BYTES) + 2 * P_BYTES + BAR_BYTES;
   static constexpr int O_COL = 2 * BN;
 };
 
@@ -68,7 +69,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sK = sQ + Cfg::Q_BYTES;
   uint8_t* sV = sK + 2 * Cfg::K_BYTES;
   uint8_t* sP = sV + 2 * Cfg::V_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + Cfg::P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::P_BYTES);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;    // [2]
   uint64_t* v_full = bars + 3;    // [2]
@@ -76,10 +77,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* v_empty = bars + 7;   // [2]
   uint64_t* s_full = bars + 9;    // [2]
   uint64_t* s_free = bars + 11;   // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* p_free = bars + 14;
-  uint64_t* o_final = bars + 15;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* p_full = bars + 13;    // [2]
+  uint64_t* p_free = bars + 15;    // [2]
+  uint64_t* o_final = bars + 17;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = warp_id(), lane = lane_id();
@@ -103,8 +104,10 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(p_free, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&p_full[s], 128);
+      mbar_init(&p_free[s], 1);
+    }
     mbar_init(o_final, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -149,19 +152,19 @@ __global__ void __launch_bounds__(192, 1)
     tc_fence_after();
     const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
     auto issue_pv = [&](int jj) -> bool {
-      const int st = jj & 1;
-      if (!mbar_wait(p_full, jj & 1, a.err, kErrTimeoutMma)) return false;
+      const int st = jj & 1;       // K/V stage and P buffer of block jj
+      if (!mbar_wait(&p_full[st], (jj >> 1) & 1, a.err, kErrTimeoutMma)) return false;
       if (!mbar_wait(&v_full[st], (jj >> 1) & 1, a.err, kErrTimeoutMma)) return false;
       tc_fence_after();
       if (lane == 0) {
         const uint32_t v_addr = smem_u32(sV + st * Cfg::V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(p_addr + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t ad = sdesc_sw128(p_addr + st * Cfg::P_BYTES + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, BN * 128, 1024);
           umma_f16(tmem + Cfg::O_COL, ad, bd, IDESC_O, (jj > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(p_free);
+        umma_commit(&p_free[st]);
         umma_commit(&v_empty[st]);
       }
       __syncwarp();
@@ -257,13 +260,15 @@ __global__ void __launch_bounds__(192, 1)
         sum += x[e];
       }
       l = l * factor + sum;
-      if (j >= 1) {
-        if (!mbar_wait(p_free, (j - 1) & 1, a.err, kErrTimeoutEpilogue)) {
+      const int pb = j & 1;
+      if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
+        // O is rescaled in TMEM: every P V product so far (the last one is block j - 1's) must have landed
+        if (!mbar_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err, kErrTimeoutEpilogue)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
+        {
 #pragma unroll 1
           for (int c = 0; c < HD; c += 32) {
             uint32_t v[32];
@@ -281,6 +286,11 @@ __global__ void __launch_bounds__(192, 1)
           tmem_wait_st();
         }
       }
+      // P buffer pb was last read by block j - 2's P V product
+      if (j >= 2 && !mbar_wait(&p_free[pb], ((j - 2) >> 1) & 1, a.err, kErrTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
       // P row -> shared memory, 128-byte swizzle, K-major (keys along K), 64-key column blocks
 #pragma unroll
       for (int c = 0; c < BN; c += 8) {
@@ -290,12 +300,12 @@ __global__ void __launch_bounds__(192, 1)
         pk.z = pack_bf16x2(x[c + 4], x[c + 5]);
         pk.w = pack_bf16x2(x[c + 6], x[c + 7]);
         const int blk = c >> 6, chunk = (c & 63) >> 3;
-        uint8_t* dst = sP + blk * 128 * 128 + r * 128 + ((chunk ^ (r & 7)) << 4);
+        uint8_t* dst = sP + pb * Cfg::P_BYTES + blk * 128 * 128 + r * 128 + ((chunk ^ (r & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = pk;
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[pb]);
     }
     // epilogue
     if (ok && mbar_wait(o_final, 0, a.err, kErrTimeoutEpilogue)) {
