@@ -115,6 +115,53 @@ class Projector:
         self._dev = None
 
 
+    def tensors(self):
+        return {f"layer.{i}": torch.cat((self.W[i], self.b[i][:, None]), 1).to(torch.bfloat16).cpu().contiguous()
+                for i in self.layers}
+
+    def save(self, path, meta):
+        """The map file (bytes reproducible: a canonical header)."""
+        t = self.tensors()
+        check_weights(t, f"Projector.save {path}")
+        Path(path).write_bytes(stable_safetensors(t, {k: str(v) for k, v in dict(meta, split=self.split).items()}))
+
+    @classmethod
+    def load(cls, path, device="cpu", dtype=torch.bfloat16, sha256=None):
+        """A map file, or a release directory (ridgefill.json + int8 maps: ridge/release.py)."""
+        if Path(path).is_dir():
+            from . import release
+            return release.load(path, device, dtype)
+        from safetensors.torch import load as from_bytes
+
+        from ..utils import integrity
+        data, sha = integrity.read_verified(path, sha256)
+        meta = _header_meta(data)
+        W, B = {}, {}
+        for name, packed in from_bytes(data).items():
+            check_weights({name: packed}, f"Projector.load {path}")
+            layer = int(name.split(".")[1])
+            weight, bias = packed.split([packed.shape[1] - 1, 1], dim=1)
+            W[layer] = weight.to(device, dtype).contiguous()
+            B[layer] = bias.squeeze(1).to(device, dtype).contiguous()
+        p = cls(int(meta["split"]), W, B, meta)
+        p.sha256 = sha
+        return p
+
+    @classmethod
+    def load_i8(cls, files, split, device="cpu", dtype=torch.bfloat16):
+        """The int8 release layout: files {layer: path of a safetensors file holding proj.L.codes / scale /
+        bias}. Dequantised exactly in fp32 (8-bit code x bf16 scale fits fp32), then one cast to dtype."""
+        from safetensors.torch import load_file
+        W, B = {}, {}
+        for L, path in files.items():
+            t = load_file(str(path))
+            w, b = dequant_i8(t[f"proj.{L}.codes"], t[f"proj.{L}.scale"], t[f"proj.{L}.bias"])
+            check_weights({f"layer.{L}": torch.cat((w, b[:, None]), 1)}, f"Projector.load_i8 {path}")
+            W[int(L)] = w.to(device, dtype).contiguous()
+            B[int(L)] = b.to(device, dtype).contiguous()
+        return cls(split, W, B, dict(layout="i8_row128"))
+
+
 class StreamedProjector(Projector):
     """Maps kept in pinned host memory and streamed to the GPU per prompt, for HBM budgets that cannot hold every late
     layer's map (the E3 engine's --ridgefill-stream-projector option, code/qwen38-27b-kit/common.py:27).
@@ -206,52 +253,6 @@ class StreamedProjector(Projector):
     def release(self):
         torch.cuda.synchronize() if self._ring is not None else None
         self._ring, self._ready = None, {}
-
-    def tensors(self):
-        return {f"layer.{i}": torch.cat((self.W[i], self.b[i][:, None]), 1).to(torch.bfloat16).cpu().contiguous()
-                for i in self.layers}
-
-    def save(self, path, meta):
-        """The map file (bytes reproducible: a canonical header)."""
-        t = self.tensors()
-        check_weights(t, f"Projector.save {path}")
-        Path(path).write_bytes(stable_safetensors(t, {k: str(v) for k, v in dict(meta, split=self.split).items()}))
-
-    @classmethod
-    def load(cls, path, device="cpu", dtype=torch.bfloat16, sha256=None):
-        """A map file, or a release directory (ridgefill.json + int8 maps: ridge/release.py)."""
-        if Path(path).is_dir():
-            from . import release
-            return release.load(path, device, dtype)
-        from safetensors.torch import load as from_bytes
-
-        from ..utils import integrity
-        data, sha = integrity.read_verified(path, sha256)
-        meta = _header_meta(data)
-        W, B = {}, {}
-        for name, packed in from_bytes(data).items():
-            check_weights({name: packed}, f"Projector.load {path}")
-            layer = int(name.split(".")[1])
-            weight, bias = packed.split([packed.shape[1] - 1, 1], dim=1)
-            W[layer] = weight.to(device, dtype).contiguous()
-            B[layer] = bias.squeeze(1).to(device, dtype).contiguous()
-        p = cls(int(meta["split"]), W, B, meta)
-        p.sha256 = sha
-        return p
-
-    @classmethod
-    def load_i8(cls, files, split, device="cpu", dtype=torch.bfloat16):
-        """The int8 release layout: files {layer: path of a safetensors file holding proj.L.codes / scale /
-        bias}. Dequantised exactly in fp32 (8-bit code x bf16 scale fits fp32), then one cast to dtype."""
-        from safetensors.torch import load_file
-        W, B = {}, {}
-        for L, path in files.items():
-            t = load_file(str(path))
-            w, b = dequant_i8(t[f"proj.{L}.codes"], t[f"proj.{L}.scale"], t[f"proj.{L}.bias"])
-            check_weights({f"layer.{L}": torch.cat((w, b[:, None]), 1)}, f"Projector.load_i8 {path}")
-            W[int(L)] = w.to(device, dtype).contiguous()
-            B[int(L)] = b.to(device, dtype).contiguous()
-        return cls(split, W, B, dict(layout="i8_row128"))
 
 
 def dequant_i8(codes, scale, bias):
