@@ -198,18 +198,22 @@ def test_streamed_maps_equal_resident_maps(slots):
 def test_gdn_state_checkpoints_match_fp32():
     """GDN recurrent-state checkpoints on the kernels (exact layers and cache-only fills) against the fp32 oracle:
     the same absolute positions, the same states within bf16 tolerance."""
-    dut, f32 = from_config(HYB, seed=0, device="cuda", std=0.05, backend="b200"), _fp32(HYB)
+    ref, dut = _pair(HYB)
+    f32 = _fp32(HYB)
     ids = torch.randint(0, HYB.vocab, (333,), generator=torch.Generator().manual_seed(5)).cuda()
     _, cd = dut.forward_exact(ids, gdn_checkpoint_every=128)
+    _, cr = ref.forward_exact(ids, gdn_checkpoint_every=128)
     _, cf = f32.forward_exact(ids, gdn_checkpoint_every=128)
     for i, t in enumerate(HYB.layer_types):
         if t != "gdn":
             continue
         kd, kf = cd[i]["checkpoints"], cf[i]["checkpoints"]
-        assert sorted(kd) == sorted(kf) == [128, 256]
-        for p in kf:
-            assert _rel(kd[p], kf[p]) < 5e-2, (i, p, _rel(kd[p], kf[p]))
-        assert _rel(cd[i]["rec"], cf[i]["rec"]) < 5e-2
+        assert sorted(kd) == sorted(kf) == sorted(cr[i]["checkpoints"]) == [128, 256]
+        for p in kf:   # no further from fp32 than the torch bf16 path (errors grow with depth for both)
+            e_dut, e_ref = _rel(kd[p], kf[p]), _rel(cr[i]["checkpoints"][p], kf[p])
+            assert e_dut < 1.5 * e_ref + 2e-2, (i, p, e_dut, e_ref)
+        e_dut, e_ref = _rel(cd[i]["rec"], cf[i]["rec"]), _rel(cr[i]["rec"], cf[i]["rec"])
+        assert e_dut < 1.5 * e_ref + 2e-2, (i, e_dut, e_ref)
     # a fill with checkpoints
     g = torch.Generator(device="cuda").manual_seed(9)
     x = torch.randn(300, HYB.hidden, device="cuda", generator=g)
