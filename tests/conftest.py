@@ -8,6 +8,10 @@ import torch
 for _k in ("HF_HUB_OFFLINE", "HF_HUB_DISABLE_IMPLICIT_TOKEN"):
     os.environ.setdefault(_k, "1")
 
+# under pytest-xdist, share the cores among the workers instead of every worker starting one thread per core
+if os.environ.get("PYTEST_XDIST_WORKER_COUNT"):
+    torch.set_num_threads(max(1, (os.cpu_count() or 1) // int(os.environ["PYTEST_XDIST_WORKER_COUNT"])))
+
 VOCAB = 300          # ids drawn by the tests stay below this
 
 
