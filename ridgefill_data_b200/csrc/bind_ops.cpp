@@ -587,6 +587,22 @@ void nvls_allreduce_b(int64_t mc_in, int64_t mc_out, int64_t out_local, c10::opt
   rf::nvls_allreduce(a, cur());
 }
 
+void nvls_allreduce_f64_b(int64_t mc_in, int64_t mc_out, int64_t n, int64_t flags_local,
+                          std::vector<int64_t> flag_peers, int64_t rank, int64_t slot_in, int64_t slot_out,
+                          int64_t epoch, int64_t counter, Tensor err) {
+  rf::NvlsAllReduceF64Args a{};
+  a.mc_in = reinterpret_cast<const void*>(mc_in);
+  a.mc_out = reinterpret_cast<void*>(mc_out);
+  a.n = n;
+  a.f = nvls_flags_of(flags_local, flag_peers, rank);
+  a.slot_in = (int)slot_in;
+  a.slot_out = (int)slot_out;
+  a.epoch = (int)epoch;
+  a.counter = reinterpret_cast<int*>(counter);
+  a.err = err.data_ptr<int>();
+  rf::nvls_allreduce_f64(a, cur());
+}
+
 void nvls_allgather_b(Tensor src, int64_t mc_out, int64_t d, int64_t col_off, int64_t flags_local,
                       std::vector<int64_t> flag_peers, int64_t rank, int64_t slot, int64_t epoch, int64_t counter,
                       Tensor err) {
@@ -680,6 +696,7 @@ void register_comm(pybind11::module_& m) {
   m.def("window_mass", &window_mass_b);
   m.def("nvls_allreduce", &nvls_allreduce_b);
   m.def("nvls_allgather", &nvls_allgather_b);
+  m.def("nvls_allreduce_f64", &nvls_allreduce_f64_b);
   m.def("nvls_barrier", &nvls_barrier_b);
   m.def("router_topk", &router_topk_b);
   m.def("moe_align", &moe_align_b);

@@ -211,7 +211,17 @@ struct NvlsAllGatherArgs {
   int* counter;
   int* err;
 };
+struct NvlsAllReduceF64Args {
+  const void* mc_in;                // multicast address of every rank's fp64 vector [n]
+  void* mc_out;                     // multicast address of the output vectors
+  long n;
+  NvlsFlags f;
+  int slot_in, slot_out, epoch;
+  int* counter;
+  int* err;
+};
 void nvls_allreduce(const NvlsAllReduceArgs& a, cudaStream_t stream);
+void nvls_allreduce_f64(const NvlsAllReduceF64Args& a, cudaStream_t stream);
 void nvls_allgather(const NvlsAllGatherArgs& a, cudaStream_t stream);
 void nvls_barrier(const NvlsFlags& f, int slot, int epoch, int* err, cudaStream_t stream);
 

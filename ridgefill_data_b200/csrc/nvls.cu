@@ -8,6 +8,9 @@
 //                     tensor's bytes) against 2 (N - 1) / N S each way for a ring. A cross-rank barrier before (every
 //                     rank's partial written) and after (every rank's sums landed), then every CTA copies the
 //                     gathered rows into the caller's fresh output tensor.
+//  nvls_allreduce_f64 one-shot all-reduce of an fp64 vector (the ridge fit's sufficient statistics): rank r reads
+//                     elements [r n / N, (r + 1) n / N) summed in the switch (multimem.ld_reduce .f64, exact
+//                     fp64 adds) and multicasts the sums; barriers as above.
 //  nvls_allgather     each rank's column slice [rows, cols] of a [rows, d] tensor written into every rank's copy at
 //                     column offset rank * cols by one multimem.st per 16 bytes, then a cross-rank barrier.
 // Barriers are epoch-stamped flag words in a symmetric int32 array, written with st.release.sys to every peer's
@@ -126,6 +129,35 @@ __global__ void __launch_bounds__(kNvlsThreads) nvls_allgather_kernel(NvlsAllGat
   if (blockIdx.x == 0) wait_all(a.f, a.slot, a.epoch, a.err, &s_ok);
 }
 
+__global__ void __launch_bounds__(kNvlsThreads) nvls_allreduce_f64_kernel(NvlsAllReduceF64Args a) {
+  __shared__ int s_ok;
+  if (blockIdx.x == 0 && threadIdx.x == 0) arrive(a.f, a.slot_in, a.epoch);
+  const bool ok = wait_all(a.f, a.slot_in, a.epoch, a.err, &s_ok);
+  if (ok) {
+    const long per = (a.n + a.f.world - 1) / a.f.world;
+    const long i0 = (long)a.f.rank * per, i1 = min(a.n, i0 + per);
+    const long stride = (long)gridDim.x * blockDim.x;
+    const double* in = reinterpret_cast<const double*>(a.mc_in);
+    double* out = reinterpret_cast<double*>(a.mc_out);
+    for (long u0 = i0 + (long)blockIdx.x * blockDim.x + threadIdx.x; u0 < i1; u0 += stride * kNvlsUnroll) {
+      double v[kNvlsUnroll];
+#pragma unroll
+      for (int k = 0; k < kNvlsUnroll; ++k) {
+        const long u = u0 + k * stride;
+        if (u < i1)
+          asm volatile("multimem.ld_reduce.relaxed.sys.global.add.f64 %0, [%1];" : "=d"(v[k]) : "l"(in + u) : "memory");
+      }
+#pragma unroll
+      for (int k = 0; k < kNvlsUnroll; ++k) {
+        const long u = u0 + k * stride;
+        if (u < i1) asm volatile("multimem.st.relaxed.sys.global.f64 [%0], %1;" ::"l"(out + u), "d"(v[k]) : "memory");
+      }
+    }
+  }
+  last_cta_arrive(a.f, a.slot_out, a.epoch, a.counter);
+  if (ok) wait_all(a.f, a.slot_out, a.epoch, a.err, &s_ok);
+}
+
 __global__ void nvls_barrier_kernel(NvlsFlags f, int slot, int epoch, int* err) {
   __shared__ int s_ok;
   if (threadIdx.x == 0) arrive(f, slot, epoch);
@@ -147,6 +179,14 @@ void nvls_allreduce(const NvlsAllReduceArgs& a, cudaStream_t stream) {
     nvls_allreduce_kernel<true><<<grid, kNvlsThreads, 0, stream>>>(a);
   else
     nvls_allreduce_kernel<false><<<grid, kNvlsThreads, 0, stream>>>(a);
+  count_launch();
+}
+
+void nvls_allreduce_f64(const NvlsAllReduceF64Args& a, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long mine = (a.n + a.f.world - 1) / a.f.world;
+  nvls_allreduce_f64_kernel<<<grid_for(mine / kNvlsUnroll + 1, dev), kNvlsThreads, 0, stream>>>(a);
   count_launch();
 }
 

@@ -186,6 +186,40 @@ class NvlsMapFill(_NvlsBase):
         return self.buf.t[off:off + P * d].view(P, d)
 
 
+class NvlsF64Reducer(_NvlsBase):
+    """In-place sum over ranks of fp64 tensors (the ridge fit's sufficient statistics) through NVSwitch multicast:
+    each tensor is staged in chunks of `chunk` elements into a symmetric buffer, every rank reduces its share of the
+    chunk in the switch (exact fp64 adds, multimem.ld_reduce) and multicasts the sums, and the chunk is copied
+    back. Replaces the NCCL all-reduce at the end of a data-parallel capture."""
+
+    COUNTER = 58
+
+    def __init__(self, group=None, chunk=1 << 25):
+        super().__init__(group)
+        self.chunk = int(chunk)
+        self.buf_in = _Symm(self.chunk, torch.float64, group)
+        self.buf_out = _Symm(self.chunk, torch.float64, group)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+
+    def allreduce_(self, tensors):
+        for t in tensors:
+            flat = t.view(-1)
+            for s in range(0, flat.numel(), self.chunk):
+                m = min(self.chunk, flat.numel() - s)
+                self.buf_in.t[:m].copy_(flat[s:s + m])
+                self.epoch += 1
+                ext().nvls_allreduce_f64(self.buf_in.mc, self.buf_out.mc, m, self.flag_local, self.flags.ptrs,
+                                         self.rank, SLOT_AR_IN, SLOT_AR_OUT, self.epoch, self.counter(self.COUNTER),
+                                         self.err)
+                flat[s:s + m].copy_(self.buf_out.t[:m])
+        return tensors
+
+    def close(self):
+        super().close()
+        self.buf_in = self.buf_out = None
+
+
 def nccl_allreduce_reference(x, group=None):
     y = x.clone()
     dist.all_reduce(y, group=group)

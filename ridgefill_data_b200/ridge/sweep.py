@@ -116,18 +116,43 @@ def capture(model, docs, splits, device=None, log=print, group=None, unitrms=Fal
             if log and (j % 10 == 0 or j == len(docs) - 1):
                 log(f"capture {j + 1}/{len(docs)} rows {int(stats[splits[0]].n)} ({time.time() - t0:.0f}s)")
     if group is not None:
-        import torch.distributed as dist
-        for st in stats.values():
-            n = torch.tensor([st.n], dtype=torch.float64, device=st.sx.device)
-            dist.all_reduce(n, group=group)
-            st.n = float(n.item())
-            for t in [st.sx, st.sxx] + list(st.sy.values()) + list(st.sxy.values()):
-                dist.all_reduce(t, group=group)
+        _reduce_sums(stats, group, log)
     if kvfold:
         for S, st in extra["kvfold"].items():
             st.sq = sq[S]
     stats.update(extra)
     return stats
+
+
+def _reduce_sums(stats, group, log=None):
+    """Sum every rank's fp64 statistics: through NVSwitch multicast (parallel/nvls.py NvlsF64Reducer, this package's
+    kernel) when the GPUs offer it, else one NCCL all-reduce per tensor."""
+    import torch.distributed as dist
+    tensors = []
+    for st in stats.values():
+        n = torch.tensor([st.n], dtype=torch.float64, device=st.sx.device)
+        dist.all_reduce(n, group=group)
+        st.n = float(n.item())
+        tensors += [st.sx, st.sxx] + list(st.sy.values()) + list(st.sxy.values())
+    reducer = None
+    if tensors and tensors[0].is_cuda and dist.get_backend(group) == "nccl":
+        try:
+            from ..parallel.nvls import NvlsF64Reducer, NvlsUnavailable
+            reducer = NvlsF64Reducer(group)
+        except (NvlsUnavailable, RuntimeError) as e:       # no multicast objects on these GPUs
+            if log:
+                log(f"fp64 sums through NCCL ({e})")
+    if reducer is not None:
+        try:
+            reducer.allreduce_(tensors)
+            from ..ops._ext import check_errors
+            torch.cuda.synchronize()
+            check_errors()
+        finally:
+            reducer.close()
+        return
+    for t in tensors:
+        dist.all_reduce(t, group=group)
 
 
 def read_cos(model, i, pred, true):

@@ -136,3 +136,55 @@ def test_data_parallel_fit_matches_single_gpu():
         p.join(timeout=60)
     for r, err in res.items():
         assert isinstance(err, float) and err < 1e-3, (r, err)
+
+
+def _f64_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from ridgefill_data_b200.parallel.nvls import NvlsF64Reducer, NvlsUnavailable
+        try:
+            red = NvlsF64Reducer(chunk=1000)          # small chunks: several per tensor, a ragged last one
+        except NvlsUnavailable as e:
+            q.put((rank, f"skip: {e}"))
+            return
+        dev = torch.device("cuda", rank)
+        mine = [torch.randn(2500, generator=torch.Generator().manual_seed(10 * rank + j), dtype=torch.float64)
+                .to(dev).view(50, 50) for j in range(2)] + [torch.full((3,), float(rank + 1), dtype=torch.float64,
+                                                                       device=dev)]
+        want = [sum(torch.randn(2500, generator=torch.Generator().manual_seed(10 * r + j), dtype=torch.float64)
+                    for r in range(world)).view(50, 50) for j in range(2)]
+        want.append(torch.full((3,), float(sum(range(1, world + 1))), dtype=torch.float64))
+        red.allreduce_(mine)
+        torch.cuda.synchronize()
+        from ridgefill_data_b200.ops._ext import check_errors
+        check_errors(dev)
+        red.close()
+        q.put((rank, all(torch.equal(a.cpu(), b) for a, b in zip(mine, want))))
+    except Exception as e:  # pragma: no cover
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nvls_fp64_allreduce_is_exact():
+    """The fit's fp64 sums reduced in the NVSwitch (two ranks: one exact fp64 add per element) equal the host sum
+    bitwise, across chunk boundaries."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_f64_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    if any(isinstance(v, str) and v.startswith("skip") for v in res.values()):
+        pytest.skip(str(res))
+    assert all(v is True for v in res.values()), res
