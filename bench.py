@@ -163,7 +163,7 @@ def fit_bench(args):
     timings = {}
     t0 = time.perf_counter()
     res = sweep.fit(model, docs, splits, held=held, solver="cholesky", log=None, timings=timings,
-                    group=dist.group.WORLD if world > 1 else None)
+                    group=dist.group.WORLD if world > 1 else None, lean=True)
     torch.cuda.synchronize()
     total = time.perf_counter() - t0
     stats = torch.tensor([total] + [timings[k] for k in sorted(timings)], dtype=torch.float64, device=device)

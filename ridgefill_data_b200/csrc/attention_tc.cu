@@ -22,15 +22,15 @@
 
 namespace rf {
 
-template <int HD, int BN>
+template <int HD, int BN, int PB>
 struct TcFaCfg {
   static constexpr int Q_BYTES = 128 * HD * 2;
   static constexpr int K_BYTES = BN * HD * 2;
   static constexpr int V_BYTES = BN * HD * 2;
   static constexpr int P_BYTES = 128 * BN * 2;
   static constexpr int BAR_BYTES = 8 * 18 + 16;
-  // two P buffers: the softmax of block j + 1 writes its P while the tensor cores still read block j's
-  static constexpr int SMEM = 1024 + Q_BYTES + 2 * (K_BYTES + V_BYTES) + 2 * P_BYTES + BAR_BYTES;
+  // PB P buffers (2: the softmax of block j + 1 writes its P while the tensor cores still read block j's)
+  static constexpr int SMEM = 1024 + Q_BYTES + 2 * (K_BYTES + V_BYTES) + PB * P_BYTES + BAR_BYTES;
   static constexpr int O_COL = 2 * BN;
 };
 
@@ -56,11 +56,11 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-template <int HD, int BN>
+template <int HD, int BN, int PB>
 __global__ void __launch_bounds__(192, 1)
     tc_flash_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, TcFaArgs a) {
-  using Cfg = TcFaCfg<HD, BN>;
+  using Cfg = TcFaCfg<HD, BN, PB>;
   constexpr uint32_t IDESC_S = idesc_bf16_f32(128, BN, false, false);
   constexpr uint32_t IDESC_O = idesc_bf16_f32(128, HD, false, true);
   extern __shared__ uint8_t smem_raw[];
@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sK = sQ + Cfg::Q_BYTES;
   uint8_t* sV = sK + 2 * Cfg::K_BYTES;
   uint8_t* sP = sV + 2 * Cfg::V_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * Cfg::P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + PB * Cfg::P_BYTES);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;    // [2]
   uint64_t* v_full = bars + 3;    // [2]
@@ -152,19 +152,20 @@ __global__ void __launch_bounds__(192, 1)
     tc_fence_after();
     const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
     auto issue_pv = [&](int jj) -> bool {
-      const int st = jj & 1;       // K/V stage and P buffer of block jj
-      if (!mbar_wait(&p_full[st], (jj >> 1) & 1, a.err, kErrTimeoutMma)) return false;
+      const int st = jj & 1;       // K/V stage of block jj
+      const int pq = jj % PB;      // its P buffer
+      if (!mbar_wait(&p_full[pq], (jj / PB) & 1, a.err, kErrTimeoutMma)) return false;
       if (!mbar_wait(&v_full[st], (jj >> 1) & 1, a.err, kErrTimeoutMma)) return false;
       tc_fence_after();
       if (lane == 0) {
         const uint32_t v_addr = smem_u32(sV + st * Cfg::V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(p_addr + st * Cfg::P_BYTES + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t ad = sdesc_sw128(p_addr + pq * Cfg::P_BYTES + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(v_addr + kk * 2048, BN * 128, 1024);
           umma_f16(tmem + Cfg::O_COL, ad, bd, IDESC_O, (jj > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&p_free[st]);
+        umma_commit(&p_free[pq]);
         umma_commit(&v_empty[st]);
       }
       __syncwarp();
@@ -260,10 +261,10 @@ __global__ void __launch_bounds__(192, 1)
         sum += x[e];
       }
       l = l * factor + sum;
-      const int pb = j & 1;
+      const int pb = j % PB;
       if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
         // O is rescaled in TMEM: every P V product so far (the last one is block j - 1's) must have landed
-        if (!mbar_wait(&p_free[(j - 1) & 1], ((j - 1) >> 1) & 1, a.err, kErrTimeoutEpilogue)) {
+        if (!mbar_wait(&p_free[(j - 1) % PB], ((j - 1) / PB) & 1, a.err, kErrTimeoutEpilogue)) {
           ok = false;
           break;
         }
@@ -286,8 +287,8 @@ __global__ void __launch_bounds__(192, 1)
           tmem_wait_st();
         }
       }
-      // P buffer pb was last read by block j - 2's P V product
-      if (j >= 2 && !mbar_wait(&p_free[pb], ((j - 2) >> 1) & 1, a.err, kErrTimeoutEpilogue)) {
+      // P buffer pb was last read by block j - PB's P V product
+      if (j >= PB && !mbar_wait(&p_free[pb], ((j - PB) / PB) & 1, a.err, kErrTimeoutEpilogue)) {
         ok = false;
         break;
       }
@@ -379,20 +380,22 @@ static CUtensorMap tmap3(const void* base, int hd, int rows, int heads, long hea
   return tm;
 }
 
-template <int HD, int BN>
+template <int HD, int BN, int PB>
 static void launch_tc(const AttnArgs& x, cudaStream_t stream) {
-  using Cfg = TcFaCfg<HD, BN>;
+  using Cfg = TcFaCfg<HD, BN, PB>;
   static PerDeviceOnce once;
-  once([] { cudaFuncSetAttribute(tc_flash_kernel<HD, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM); });
+  once([] { cudaFuncSetAttribute(tc_flash_kernel<HD, BN, PB>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM); });
   CUtensorMap tq = tmap3(x.q, HD, x.nq, x.hq, x.q_head_stride, 128);
   CUtensorMap tk = tmap3(x.k, HD, x.nk, x.hkv, x.kv_head_stride, BN);
   CUtensorMap tv = tmap3(x.v, HD, x.nk, x.hkv, x.kv_head_stride, BN);
   TcFaArgs a{x.hq, x.hkv, x.nq, x.nk, x.q_start, x.qpos, x.scale * 1.4426950408889634f, x.gate, x.gate_row, x.gate_head,
              x.out, x.out_row, x.err};
   dim3 grid((x.nq + 127) / 128, x.hq);
-  tc_flash_kernel<HD, BN><<<grid, 192, Cfg::SMEM, stream>>>(tq, tk, tv, a);
+  tc_flash_kernel<HD, BN, PB><<<grid, 192, Cfg::SMEM, stream>>>(tq, tk, tv, a);
   count_launch();
 }
+
+int attn_p_buffers = 2;
 
 bool flash_attention_tc(const AttnArgs& x, cudaStream_t stream) {
   if (x.nq <= 0) return false;
@@ -403,8 +406,14 @@ bool flash_attention_tc(const AttnArgs& x, cudaStream_t stream) {
     return false;
   if (x.out_row % 8) return false;
   switch (x.hd) {
-    case 128: launch_tc<128, 128>(x, stream); return true;
-    case 256: launch_tc<256, 64>(x, stream); return true;
+    case 128:
+      if (attn_p_buffers == 1) launch_tc<128, 128, 1>(x, stream);
+      else launch_tc<128, 128, 2>(x, stream);
+      return true;
+    case 256:
+      if (attn_p_buffers == 1) launch_tc<256, 64, 1>(x, stream);
+      else launch_tc<256, 64, 2>(x, stream);
+      return true;
     default: return false;
   }
 }

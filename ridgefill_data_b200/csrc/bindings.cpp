@@ -94,6 +94,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sm_count", &sm_count);
   m.def("launch_count", &launch_count);
   m.def("set_gemm_2sm", &set_gemm_2sm);
+  m.def("set_attn_p_buffers", [](int64_t n) {
+    const int was = rf::attn_p_buffers;
+    rf::attn_p_buffers = n == 1 ? 1 : 2;
+    return was;
+  });
   m.def("gemm", &gemm, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("bias") = py::none(),
         py::arg("residual") = py::none(), py::arg("epi") = 0, py::arg("bn") = 256, py::arg("a_mn") = false,
         py::arg("b_mn") = false, py::arg("k_splits") = 1, py::arg("k_chunk") = 0, py::arg("max_ctas") = 0);

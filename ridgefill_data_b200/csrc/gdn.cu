@@ -129,8 +129,115 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(GdnPrepArgs a) {
   }
 }
 
+// Register form of gdn_prep for head dims 64 / 128 (NCH = 2 / 4 channels per lane, one 4- or 8-byte load per lane
+// per token) and 4 conv taps: each warp walks PREP_RUN consecutive tokens of one head and keeps the conv window (the
+// previous K - 1 pre-conv rows of its channels) and the conv taps in registers, so a token costs one global load and one store
+// per lane; SiLU on the fast reciprocal. Same arithmetic order as gdn_prep_kernel (taps oldest first, fp32 sum,
+// bf16 rounding of the conv output before the l2 norm).
+constexpr int PREP_RUN = 16;      // tokens per warp
+constexpr int PREP_WARPS = 8;     // warps per CTA (tokens per CTA = 128)
+
+template <int NCH, int K>
+__global__ void __launch_bounds__(32 * PREP_WARPS) gdn_prep_fast_kernel(GdnPrepArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int task = blockIdx.y;
+  const int C = 2 * a.nk * a.dk + a.nv * a.dv;
+  const bool is_qk = task < 2 * a.nk;
+  const bool is_q = task < a.nk;
+  const int c0 = is_qk ? task * a.dk : 2 * a.nk * a.dk + (task - 2 * a.nk) * a.dv;
+  const int ch = c0 + lane * NCH;                       // this lane's first channel
+  const int t_begin = (blockIdx.x * PREP_WARPS + warp) * PREP_RUN;
+  if (t_begin < a.n) {
+    float w[NCH][K];
+#pragma unroll
+    for (int j = 0; j < NCH; ++j)
+#pragma unroll
+      for (int tap = 0; tap < K; ++tap) w[j][tap] = __bfloat162float(a.conv_w[(long)(ch + j) * K + tap]);
+    auto load_row = [&](int tkn, float (&x)[NCH]) {
+      const __nv_bfloat16* src = nullptr;
+      if (tkn >= 0) src = a.proj + (long)tkn * a.proj_row + ch;
+      else if (a.conv_state != nullptr) src = a.conv_state + (long)(K - 1 + tkn) * C + ch;
+      if (src == nullptr) {
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) x[j] = 0.f;
+      } else if constexpr (NCH == 4) {
+        const uint2 v = *reinterpret_cast<const uint2*>(src);
+        x[0] = bf16_lo(v.x); x[1] = bf16_hi(v.x); x[2] = bf16_lo(v.y); x[3] = bf16_hi(v.y);
+      } else {
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(src);
+        x[0] = bf16_lo(v); x[1] = bf16_hi(v);
+      }
+    };
+    // window[s] holds the row s + 1 - K relative to the current token (oldest first); window[K - 1] = current
+    float win[K][NCH];
+#pragma unroll
+    for (int s = 0; s < K - 1; ++s) load_row(t_begin - (K - 1) + s, win[s]);
+    const float qscale = rsqrtf((float)a.dk);
+    const int t_end = min(a.n, t_begin + PREP_RUN);
+    const int hh = is_qk ? (is_q ? task : task - a.nk) : task - 2 * a.nk;
+    __nv_bfloat16* dst_base = is_qk ? (is_q ? a.q : a.k) + (long)hh * a.n * a.dk
+                                    : a.v + (long)hh * a.n * a.dv;
+    const int dh = is_qk ? a.dk : a.dv;
+    for (int tkn = t_begin; tkn < t_end; ++tkn) {
+      load_row(tkn, win[K - 1]);
+      float y[NCH];
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) {
+        float acc = 0.f;
+#pragma unroll
+        for (int tap = 0; tap < K; ++tap) acc += win[tap][j] * w[j][tap];
+        y[j] = bf16r(__fdividef(acc, 1.f + __expf(-acc)));
+        ss += y[j] * y[j];
+      }
+      float scale = 1.f;
+      if (is_qk) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        scale = rsqrtf(ss + 1e-6f) * (is_q ? qscale : 1.f);
+      }
+      __nv_bfloat16* dst = dst_base + (long)tkn * dh + lane * NCH;
+      if constexpr (NCH == 4) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(y[0] * scale, y[1] * scale),
+                                                   pack_bf16x2(y[2] * scale, y[3] * scale));
+      } else {
+        *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(y[0] * scale, y[1] * scale);
+      }
+#pragma unroll
+      for (int s = 0; s < K - 1; ++s)
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) win[s][j] = win[s + 1][j];
+    }
+  }
+  if (task == 0) {   // gates of this CTA's tokens
+    const int t0 = blockIdx.x * PREP_WARPS * PREP_RUN;
+    for (int v = threadIdx.x; v < PREP_WARPS * PREP_RUN * a.nv; v += 32 * PREP_WARPS) {
+      const int tt = v / a.nv, h = v % a.nv;
+      const int tkn = t0 + tt;
+      if (tkn >= a.n) continue;
+      const __nv_bfloat16* prow = a.proj + (long)tkn * a.proj_row;
+      const float b = __bfloat162float(prow[a.b_off + h]);
+      const float av = __bfloat162float(prow[a.a_off + h]);
+      a.beta[(long)h * a.n + tkn] = bf16r(1.f / (1.f + expf(-b)));
+      a.g[(long)h * a.n + tkn] = -expf(a.A_log[h]) * softplus_f(av + a.dt_bias[h]);
+    }
+  }
+}
+
 void gdn_prep(const GdnPrepArgs& a, cudaStream_t stream) {
   if (a.n <= 0) return;
+  const int C = 2 * a.nk * a.dk + a.nv * a.dv;
+  const bool fast = a.dk == a.dv && (a.dk == 128 || a.dk == 64) && a.K == 4 && a.proj_row % 4 == 0 && C % 4 == 0 &&
+                    reinterpret_cast<uintptr_t>(a.proj) % 8 == 0 &&
+                    (a.conv_state == nullptr || reinterpret_cast<uintptr_t>(a.conv_state) % 8 == 0);
+  if (fast) {
+    const int per_cta = PREP_WARPS * PREP_RUN;
+    dim3 grid((a.n + per_cta - 1) / per_cta, 2 * a.nk + a.nv);
+    if (a.dk == 128) gdn_prep_fast_kernel<4, 4><<<grid, 32 * PREP_WARPS, 0, stream>>>(a);
+    else gdn_prep_fast_kernel<2, 4><<<grid, 32 * PREP_WARPS, 0, stream>>>(a);
+    count_launch();
+    return;
+  }
   dim3 grid((a.n + PREP_T - 1) / PREP_T, 2 * a.nk + a.nv);
   gdn_prep_kernel<<<grid, 128, 0, stream>>>(a);
   count_launch();
@@ -159,12 +266,13 @@ constexpr int DK = 128;           // key head dim supported by the chunk kernels
 constexpr int PK = DK + 8;        // smem pitch of [64][dk] tiles
 constexpr int PA = GC + 1;        // fp32 [64][64] pitch
 
+constexpr int PT = GC + 8;        // bf16 pitch of the ta / tb tiles
 struct WySmem {
   __nv_bfloat16 k[GC * PK];
   __nv_bfloat16 v[GC * PK];       // dv <= 128
-  __nv_bfloat16 ta[GC * (GC + 8)];  // T diag(beta e^gam)
-  __nv_bfloat16 tb[GC * (GC + 8)];  // T diag(beta)
-  float A[GC * PA];               // strictly lower A, then scratch
+  // strictly lower A, then scratch of the blocked inverse; once T is complete the same bytes hold
+  // ta = T diag(beta e^gam) and tb = T diag(beta) (bf16 [64][PT] each), which keeps the block at 3 CTAs per SM
+  float A[(2 * GC * PT * 2 + 3) / 4 > GC * PA ? (2 * GC * PT * 2 + 3) / 4 : GC * PA];
   float T[GC * PA];               // (I + A)^-1
   float gam[GC];
   float beta[GC];
@@ -295,14 +403,15 @@ __global__ void __launch_bounds__(128) gdn_wy_kernel(GdnScanArgs a, int n_pad) {
     }
     __syncthreads();
   }
-  // ta = T diag(beta e^gam), tb = T diag(beta) (bf16, lower triangle incl. diagonal)
+  // ta = T diag(beta e^gam), tb = T diag(beta) (bf16, lower triangle incl. diagonal), over A's bytes
+  __nv_bfloat16* s_ta = reinterpret_cast<__nv_bfloat16*>(s.A);
+  __nv_bfloat16* s_tb = s_ta + GC * PT;
   for (int v = tid; v < GC * (GC / 2); v += 128) {
     const int r = v / (GC / 2), c = (v % (GC / 2)) * 2;
     const float t0 = r >= c ? s.T[r * PA + c] : 0.f;
     const float t1 = r >= c + 1 ? s.T[r * PA + c + 1] : 0.f;
-    *reinterpret_cast<uint32_t*>(&s.ta[r * (GC + 8) + c]) =
-        pack2(t0 * s.beta[c] * s.eg[c], t1 * s.beta[c + 1] * s.eg[c + 1]);
-    *reinterpret_cast<uint32_t*>(&s.tb[r * (GC + 8) + c]) = pack2(t0 * s.beta[c], t1 * s.beta[c + 1]);
+    *reinterpret_cast<uint32_t*>(&s_ta[r * PT + c]) = pack2(t0 * s.beta[c] * s.eg[c], t1 * s.beta[c + 1] * s.eg[c + 1]);
+    *reinterpret_cast<uint32_t*>(&s_tb[r * PT + c]) = pack2(t0 * s.beta[c], t1 * s.beta[c + 1]);
   }
   __syncthreads();
   // W = ta k [64 x dk] -> w_buf rows; U^T = v^T tb^T [dv x 64] -> u_buf as per-chunk [dv][64] tiles
@@ -310,7 +419,7 @@ __global__ void __launch_bounds__(128) gdn_wy_kernel(GdnScanArgs a, int n_pad) {
     __nv_bfloat16* wdst = a.w_buf + ((long)h * n_pad + r0) * DK;
     uint32_t af[4][4];
 #pragma unroll
-    for (int ks = 0; ks < GC / 16; ++ks) lda_row(af[ks], s.ta, GC + 8, warp * 16, ks * 16, lane);
+    for (int ks = 0; ks < GC / 16; ++ks) lda_row(af[ks], s_ta, PT, warp * 16, ks * 16, lane);
     for (int nb = 0; nb < DK; nb += 64) {
       float acc[8][4];
 #pragma unroll
@@ -347,7 +456,7 @@ __global__ void __launch_bounds__(128) gdn_wy_kernel(GdnScanArgs a, int n_pad) {
 #pragma unroll
         for (int j2 = 0; j2 < 4; ++j2) {
           uint32_t bf[4];
-          ldb_nk(bf, s.tb, GC + 8, j2 * 16, ks * 16, lane);  // B[k][n] = tb[n][k]
+          ldb_nk(bf, s_tb, PT, j2 * 16, ks * 16, lane);  // B[k][n] = tb[n][k]
           mma_bf16(acc[2 * j2], af, bf[0], bf[1]);
           mma_bf16(acc[2 * j2 + 1], af, bf[2], bf[3]);
         }

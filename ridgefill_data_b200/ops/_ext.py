@@ -68,6 +68,8 @@ def ext():
     _mod = Checked(mod) if os.environ.get("RF_CHECK_EACH") == "1" else mod
     if os.environ.get("RF_GEMM_2SM") == "0":     # A/B switch: every product on the one-SM GEMM kernel
         mod.set_gemm_2sm(False)
+    if os.environ.get("RF_ATTN_PBUF") == "1":    # A/B switch: one P buffer in the tcgen05 attention
+        mod.set_attn_p_buffers(1)
     return _mod
 
 

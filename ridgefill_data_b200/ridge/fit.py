@@ -113,6 +113,9 @@ class CholeskyFit:
         self.cxx = cxx.to(self.device)
 
     def _rhs(self, layers):
+        key = tuple(layers)
+        if getattr(self, "_rhs_key", None) == key:          # built once per layer set (one solve per lambda)
+            return self._rhs_val
         cols, means = [], []
         for i in layers:
             if self.center:
@@ -122,7 +125,8 @@ class CholeskyFit:
                 mean_y = None
             cols.append(cxy.to(self.device))
             means.append(mean_y)
-        return torch.cat(cols, 1), means
+        self._rhs_key, self._rhs_val = key, (torch.cat(cols, 1), means)
+        return self._rhs_val
 
     def layers(self, layers, lams):
         """{lam: {i: (weight, bias)}} for every layer in `layers`."""

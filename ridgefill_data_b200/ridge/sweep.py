@@ -190,6 +190,46 @@ def select_lambda(model, held, S, maps, lams):
     return best, mean, per_layer
 
 
+def fit_select_lean(model, stats_state, S, lams, held, solver="cholesky", center=True):
+    """The per-split solve and held-out lambda choice without holding every lambda's maps: the held documents'
+    true late inputs are captured once, each lambda's maps are solved, scored (mean read cosine, as
+    select_lambda) and dropped, and only the best lambda's maps are kept (on the host). Returns (best, mean,
+    per_layer, {best: {i: (weight, bias)}}). For full-size models, where every lambda's maps of every late layer
+    would not fit next to the model and the statistics."""
+    L = model.n_layers
+    late = list(range(S, L))
+    held_in = []
+    with torch.no_grad():
+        for d in held:
+            got = {}
+            model.forward_exact(torch.as_tensor(d["ids"]).to(model.device),
+                                hook=lambda i, h: got.__setitem__(i, h) if i != "final" and i >= S else None)
+            held_in.append(got)
+        per_layer = {"identity": {i: sum(read_cos(model, i, g[S], g[i]) for g in held_in) / len(held_in)
+                                  for i in late}}
+        fit_ = CholeskyFit(stats_state, center=center, device=model.device) if solver == "cholesky" \
+            else EigenFit(stats_state, center=center)
+        best, best_maps = None, None
+        for lam in lams:
+            maps = fit_.layers(late, [lam])[lam] if solver == "cholesky" else \
+                {i: fit_.layer(i, [lam])[lam] for i in late}
+            scores = {}
+            for i in late:
+                w, b = maps[i]
+                tot = 0.0
+                for g in held_in:
+                    x = F.linear(g[S], w.to(g[S].device, g[S].dtype), b.to(g[S].device, g[S].dtype))
+                    tot += read_cos(model, i, x, g[i])
+                scores[i] = tot / len(held_in)
+            per_layer[str(lam)] = scores
+            if best is None or sum(scores.values()) > sum(per_layer[str(best)].values()):
+                best = lam
+                best_maps = {i: (w.cpu(), b.cpu()) for i, (w, b) in maps.items()}
+            del maps
+    mean = {c: sum(v.values()) / len(v) for c, v in per_layer.items()}
+    return best, mean, per_layer, {best: best_maps}
+
+
 def fit_split(stats_state, S, L, lams, solver="eigen", center=True, device=None):
     """{lam: {i: (weight, bias)}} fp32 maps of split S."""
     late = list(range(S, L))
@@ -238,14 +278,17 @@ def _now(model):
 
 
 def fit(model, docs, splits, lambdas=LAMBDAS, held=None, out_dir=None, name=None, solver=None, center=True,
-        save_stats=False, log=print, meta_extra=None, group=None, unitrms=False, kvfold=False, timings=None):
+        save_stats=False, log=print, meta_extra=None, group=None, unitrms=False, kvfold=False, timings=None,
+        lean=False):
     """Fit maps for every split. Returns {S: dict(projector, lambda_star, mean_read_cos, per_layer_read_cos,
     record)}; writes files when out_dir is given. unitrms: also the unit-RMS-target maps of the same capture,
     saved as <name>-sweep-s<S>-unitrms with the raw fit as its control <name>-sweep-s<S>-rawctl
     (results[S]["unitrms"]); kvfold: also the K/V fold (pre-RoPE [k | v] of every late attention layer straight
     from the unit-RMS boundary state), saved as <name>-kvfold-s<S> (results[S]["kvfold"]). timings: a dict that
     receives the stage seconds (capture_s with the Gram sums and their reduction; per split fit_s<S> for the solves
-    over the lambda grid and select_s<S> for the held-out lambda choice)."""
+    over the lambda grid and select_s<S> for the held-out lambda choice). lean: solve, score and drop one lambda at a
+    time (fit_select_lean; results[S]["maps"] then holds only the chosen lambda), for full-size models; with lean
+    the solves and the scoring are timed together as fit_s<S>."""
     splits = sorted(int(s) for s in splits)
     name = name or model.cfg.name or "model"
     L = model.n_layers
@@ -280,15 +323,23 @@ def fit(model, docs, splits, lambdas=LAMBDAS, held=None, out_dir=None, name=None
             torch.save(dict(state, dtype="float64", docs=[d["name"] for d in docs], model=name, **more),
                        out_dir / f"{name}-s{S}.pt")
         t_fit = _now(model)
-        maps = fit_split(state, S, L, lambdas, solver, center, model.device)
-        t_sel = _now(model)
-        if held:
-            best, mean, per_layer = select_lambda(model, held, S, maps, lambdas)
+        if lean and held:
+            del stats[S]                                  # the device sums are no longer needed (state is on host)
+            best, mean, per_layer, maps = fit_select_lean(model, state, S, lambdas, held, solver, center)
+            t_sel = _now(model)
         else:
-            best, mean, per_layer = lambdas[len(lambdas) // 2], {}, {}
+            maps = fit_split(state, S, L, lambdas, solver, center, model.device)
+            t_sel = _now(model)
+            if held:
+                best, mean, per_layer = select_lambda(model, held, S, maps, lambdas)
+            else:
+                best, mean, per_layer = lambdas[len(lambdas) // 2], {}, {}
         if timings is not None:
             timings[f"fit_s{S}"] = t_sel - t_fit
-            timings[f"select_s{S}"] = _now(model) - t_sel
+            if not (lean and held):
+                timings[f"select_s{S}"] = _now(model) - t_sel
+        if model.device.type == "cuda":
+            torch.cuda.empty_cache()
         W = {i: maps[best][i][0].to(torch.bfloat16).cpu() for i in range(S, L)}
         B = {i: maps[best][i][1].to(torch.bfloat16).cpu() for i in range(S, L)}
         meta = dict(model=name, model_commit="", lam=best, rows=rows, taps=S, sweep=True, note="",

@@ -186,3 +186,25 @@ def test_ridge_matches_the_reference():
             torch.testing.assert_close(eo, er, rtol=1e-9, atol=1e-12)
             for r in (4, 12):
                 torch.testing.assert_close(ro[r][0], rr[r][0], rtol=1e-5, atol=1e-6)
+
+
+def test_lean_fit_selects_the_same_lambda_and_maps(tiny_llama):
+    """fit(lean=True) solves, scores and drops one lambda at a time; it must pick the lambda the full path picks and
+    return the same maps for it."""
+    from ridgefill_data_b200.eval.data import zipf_docs
+    from ridgefill_data_b200.models.base import load
+    from ridgefill_data_b200.ridge import sweep
+    path, _ = tiny_llama
+    m = load(path, dtype=torch.float32)
+    docs = zipf_docs(4, 96, 300, seed=1)
+    held = zipf_docs(2, 96, 300, seed=3)
+    lams = (1e-3, 0.03, 1.0)
+    full = sweep.fit(m, docs, [2], lambdas=lams, held=held, log=None)[2]
+    lean = sweep.fit(m, docs, [2], lambdas=lams, held=held, log=None, lean=True)[2]
+    assert lean["lambda_star"] == full["lambda_star"]
+    for c in [str(x) for x in lams] + ["identity"]:
+        assert abs(lean["mean_read_cos"][c] - full["mean_read_cos"][c]) < 1e-9
+    best = full["lambda_star"]
+    for i, (w, b) in full["maps"][best].items():
+        wl, bl = lean["maps"][best][i]
+        assert torch.allclose(w, wl) and torch.allclose(b, bl)
