@@ -135,13 +135,13 @@ void flash_attention(Tensor q, int64_t q_head_stride, Tensor k, Tensor v, int64_
 }
 
 void gdn_prep(Tensor proj, int64_t b_off, int64_t a_off, Tensor conv_w, OptT conv_state, Tensor A_log,
-              Tensor dt_bias, int64_t n, int64_t nk, int64_t nv, int64_t dk, int64_t dv, int64_t K, Tensor q, Tensor k,
+              Tensor dt_bias, int64_t n, int64_t nk, int64_t nv, int64_t dk, int64_t dv, int64_t K, OptT q, Tensor k,
               Tensor v, Tensor beta, Tensor g) {
   need(proj, at::kBFloat16, "proj");
   need(conv_w, at::kBFloat16, "conv_w");
   need(A_log, at::kFloat, "A_log");
   need(dt_bias, at::kFloat, "dt_bias");
-  need(q, at::kBFloat16, "q");
+  if (q.has_value()) need(*q, at::kBFloat16, "q");
   need(k, at::kBFloat16, "k");
   need(v, at::kBFloat16, "v");
   need(beta, at::kFloat, "beta");
@@ -167,7 +167,7 @@ void gdn_prep(Tensor proj, int64_t b_off, int64_t a_off, Tensor conv_w, OptT con
   a.dk = (int)dk;
   a.dv = (int)dv;
   a.K = (int)K;
-  a.q = bf(q);
+  a.q = q.has_value() ? bf(*q) : nullptr;
   a.k = bf(k);
   a.v = bf(v);
   a.beta = beta.data_ptr<float>();

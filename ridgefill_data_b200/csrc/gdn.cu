@@ -35,7 +35,7 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(GdnPrepArgs a) {
   __shared__ __align__(16) __nv_bfloat16 rows[(PREP_T + 7) * 128];
   __shared__ float wsh[128 * 8];
   const int t0 = blockIdx.x * PREP_T;
-  const int task = blockIdx.y;
+  const int task = blockIdx.y + (a.q == nullptr ? a.nk : 0);   // no q heads in fill mode
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int C = 2 * a.nk * a.dk + a.nv * a.dv;
   int c0, dh;
@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(128) gdn_prep_kernel(GdnPrepArgs a) {
     for (int j = 0; j < 4; ++j)
       if (j < per) dst[j * 32 + lane] = __float2bfloat16(val[j] * scale);
   }
-  if (task == 0) {   // gates of this token block
+  if (blockIdx.y == 0) {   // gates of this token block
     for (int v = threadIdx.x; v < PREP_T * a.nv; v += 128) {
       const int tt = v / a.nv, h = v % a.nv;
       const int tkn = t0 + tt;
@@ -140,7 +140,7 @@ constexpr int PREP_WARPS = 8;     // warps per CTA (tokens per CTA = 128)
 template <int NCH, int K>
 __global__ void __launch_bounds__(32 * PREP_WARPS) gdn_prep_fast_kernel(GdnPrepArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int task = blockIdx.y;
+  const int task = blockIdx.y + (a.q == nullptr ? a.nk : 0);   // no q heads in fill mode
   const int C = 2 * a.nk * a.dk + a.nv * a.dv;
   const bool is_qk = task < 2 * a.nk;
   const bool is_q = task < a.nk;
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(32 * PREP_WARPS) gdn_prep_fast_kernel(GdnPrepA
         for (int j = 0; j < NCH; ++j) win[s][j] = win[s + 1][j];
     }
   }
-  if (task == 0) {   // gates of this CTA's tokens
+  if (blockIdx.y == 0) {   // gates of this CTA's tokens
     const int t0 = blockIdx.x * PREP_WARPS * PREP_RUN;
     for (int v = threadIdx.x; v < PREP_WARPS * PREP_RUN * a.nv; v += 32 * PREP_WARPS) {
       const int tt = v / a.nv, h = v % a.nv;
@@ -232,13 +232,13 @@ void gdn_prep(const GdnPrepArgs& a, cudaStream_t stream) {
                     (a.conv_state == nullptr || reinterpret_cast<uintptr_t>(a.conv_state) % 8 == 0);
   if (fast) {
     const int per_cta = PREP_WARPS * PREP_RUN;
-    dim3 grid((a.n + per_cta - 1) / per_cta, 2 * a.nk + a.nv);
+    dim3 grid((a.n + per_cta - 1) / per_cta, (a.q == nullptr ? 1 : 2) * a.nk + a.nv);
     if (a.dk == 128) gdn_prep_fast_kernel<4, 4><<<grid, 32 * PREP_WARPS, 0, stream>>>(a);
     else gdn_prep_fast_kernel<2, 4><<<grid, 32 * PREP_WARPS, 0, stream>>>(a);
     count_launch();
     return;
   }
-  dim3 grid((a.n + PREP_T - 1) / PREP_T, 2 * a.nk + a.nv);
+  dim3 grid((a.n + PREP_T - 1) / PREP_T, (a.q == nullptr ? 1 : 2) * a.nk + a.nv);
   gdn_prep_kernel<<<grid, 128, 0, stream>>>(a);
   count_launch();
 }

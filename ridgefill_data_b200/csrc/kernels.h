@@ -100,7 +100,7 @@ struct GdnPrepArgs {
   const float* A_log;           // [nv]
   const float* dt_bias;         // [nv]
   int n, nk, nv, dk, dv, K;
-  __nv_bfloat16* q;             // [nk, n, dk] l2-normed, scaled by dk^-0.5
+  __nv_bfloat16* q;             // [nk, n, dk] l2-normed, scaled by dk^-0.5 (nullptr: fill mode, q heads skipped)
   __nv_bfloat16* k;             // [nk, n, dk] l2-normed
   __nv_bfloat16* v;             // [nv, n, dv]
   float* beta;                  // [nv, n]

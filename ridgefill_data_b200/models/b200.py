@@ -363,7 +363,7 @@ class B200Hybrid(_B200, Hybrid):
         c = cache[i]
         conv_state = c.get("conv")
         q, k, v, beta, g = K.gdn_prep(proj, C, C + nv, w["conv"], conv_state, w["A_log"], w["dt_bias"],
-                                      self.nk, nv, cfg.gdn_dk, cfg.gdn_dv)
+                                      self.nk, nv, cfg.gdn_dk, cfg.gdn_dv, need_q=need_out)
         new_conv = (conv_state.clone() if conv_state is not None
                     else torch.zeros(cfg.conv_k - 1, C, dtype=self.dtype, device=self.device))
         K.gdn_conv_state_update(proj, new_conv, C)
@@ -413,8 +413,17 @@ class B200Hybrid(_B200, Hybrid):
         return K.gated_rmsnorm(o, z, w["norm"], self.nv, self.cfg.gdn_dv, self.eps)
 
     def _gdn_fill(self, i, xn, cache, checkpoint_every=None):
+        """State-only fill: the q projection is needed only for the last conv_k - 1 rows (the conv window the next
+        rows continue from), so the in-projection GEMM skips the q rows of every other row."""
         w = self.W[i]
-        proj = G.linear(xn, w["in_p"][:self.conv_dim + 2 * self.nv])
+        C, nv = self.conv_dim, self.nv
+        qd = self.nk * self.cfg.gdn_dk
+        rows = xn.shape[0]
+        proj = torch.empty(rows, C + 2 * nv, dtype=self.dtype, device=self.device)
+        G.linear(xn, w["in_p"][qd:C + 2 * nv], out=proj[:, qd:])
+        last = min(rows, self.cfg.conv_k - 1)
+        if last:
+            G.linear(xn[rows - last:], w["in_p"][:qd], out=proj[rows - last:, :qd])
         if checkpoint_every:
             return self._gdn_core_ckpt(i, proj, cache, False, checkpoint_every)[0]
         self._gdn_core_dev(i, proj, cache, False)

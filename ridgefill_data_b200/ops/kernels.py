@@ -67,12 +67,13 @@ def attention(q, k_cache, v_cache, nk, scale, out, q_start=0, qpos=None, gate=No
     return out
 
 
-def gdn_prep(proj, b_off, a_off, conv_w, conv_state, A_log, dt_bias, nk, nv, dk, dv):
+def gdn_prep(proj, b_off, a_off, conv_w, conv_state, A_log, dt_bias, nk, nv, dk, dv, need_q=True):
     """Conv + SiLU + l2norm + gates for the rows of proj [n, *]: returns q, k [nk, n, dk], v [nv, n, dv]
-    (bf16) and beta, g [nv, n] (fp32)."""
+    (bf16) and beta, g [nv, n] (fp32). need_q False (a state-only fill): q is None and its columns of proj are
+    not read."""
     n = proj.shape[0]
     dev = proj.device
-    q = torch.empty(nk, n, dk, dtype=BF16, device=dev)
+    q = torch.empty(nk, n, dk, dtype=BF16, device=dev) if need_q else None
     k = torch.empty(nk, n, dk, dtype=BF16, device=dev)
     v = torch.empty(nv, n, dv, dtype=BF16, device=dev)
     beta = torch.empty(nv, n, dtype=torch.float32, device=dev)
