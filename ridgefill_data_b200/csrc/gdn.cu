@@ -297,6 +297,55 @@ __device__ __forceinline__ void blk_mm(float* out, const float* X, const float* 
   o[1] = accumulate ? o[1] + sign * a1 : sign * a1;
 }
 
+// One distance D of the blocked inverse: for every pair (i, j = i - D) at once, X_ij = sum_{k=j}^{i-1} A_ik T_kj
+// into A's upper block (j, i), then T_ij = -T_ii X_ij. Thread = (row r, columns c, c + 1) of every pair's block; the
+// pairs' and columns' sums are independent chains (accumulated in registers, the k order as blk_mm's).
+template <int D>
+__device__ __forceinline__ void wy_offdiag(float* A, float* T, int tid) {
+  constexpr int NP = 4 - D;
+  const int r = tid >> 3, c = (tid & 7) * 2;
+  float acc[NP][2];
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    acc[p][0] = acc[p][1] = 0.f;
+#pragma unroll
+    for (int k = p; k < p + D; ++k) {
+      const float* xr = A + ((p + D) * 16 + r) * PA + k * 16;
+      const float* yc = T + (k * 16) * PA + p * 16 + c;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float x = xr[e];
+        acc[p][0] += x * yc[e * PA];
+        acc[p][1] += x * yc[e * PA + 1];
+      }
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    float* o = A + (p * 16 + r) * PA + (p + D) * 16 + c;
+    o[0] = acc[p][0];
+    o[1] = acc[p][1];
+  }
+  __syncthreads();
+#pragma unroll
+  for (int p = 0; p < NP; ++p) {
+    const int i = p + D;
+    const float* xr = T + (i * 16 + r) * PA + i * 16;
+    const float* yc = A + (p * 16) * PA + i * 16 + c;
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float x = xr[e];
+      a0 += x * yc[e * PA];
+      a1 += x * yc[e * PA + 1];
+    }
+    float* o = T + (i * 16 + r) * PA + p * 16 + c;
+    o[0] = -a0;
+    o[1] = -a1;
+  }
+  __syncthreads();
+}
+
 __global__ void __launch_bounds__(128) gdn_wy_kernel(GdnScanArgs a, int n_pad) {
   extern __shared__ __align__(16) uint8_t wy_raw[];
   WySmem& s = *reinterpret_cast<WySmem*>(wy_raw);
@@ -378,31 +427,27 @@ __global__ void __launch_bounds__(128) gdn_wy_kernel(GdnScanArgs a, int n_pad) {
   }
   __syncthreads();
   // (I + A)^-1, blocked 4 x 4 in 16 x 16 blocks. Diagonal blocks by forward substitution: warp w inverts
-  // block w, lane c < 16 owning column c.
+  // block w, lane c < 16 owning column c, kept in registers (entries above the diagonal are zero, so the sum over
+  // j < c adds nothing and the order of the nonzero terms is j = c .. r - 1, as before).
   if (lane < 16) {
     const int b0 = warp * 16;
     const int c = lane;
+    float tc[16];
+#pragma unroll
     for (int r = 0; r < 16; ++r) {
       float v = (r == c) ? 1.f : 0.f;
-      for (int j = c; j < r; ++j) v -= s.A[(b0 + r) * PA + b0 + j] * s.T[(b0 + j) * PA + b0 + c];
-      s.T[(b0 + r) * PA + b0 + c] = (r >= c) ? v : 0.f;
+#pragma unroll
+      for (int j = 0; j < r; ++j) v -= s.A[(b0 + r) * PA + b0 + j] * tc[j];
+      tc[r] = (r >= c) ? v : 0.f;
+      s.T[(b0 + r) * PA + b0 + c] = tc[r];
     }
   }
   __syncthreads();
   // Off-diagonal blocks by distance: T_ij = -T_ii * sum_{k=j}^{i-1} A_ik T_kj (scratch X_ij in the zero
-  // upper triangle of A: block (j, i)).
-  for (int d = 1; d < 4; ++d) {
-    for (int j = 0; j + d < 4; ++j) {
-      const int i = j + d;
-      for (int k = j; k < i; ++k) blk_mm(s.A, s.A, s.T, i, k, k, j, j, i, k > j, 1.f, tid);
-    }
-    __syncthreads();
-    for (int j = 0; j + d < 4; ++j) {
-      const int i = j + d;
-      blk_mm(s.T, s.T, s.A, i, i, j, i, i, j, false, -1.f, tid);
-    }
-    __syncthreads();
-  }
+  // upper triangle of A: block (j, i)); every pair of one distance in flight at once.
+  wy_offdiag<1>(s.A, s.T, tid);
+  wy_offdiag<2>(s.A, s.T, tid);
+  wy_offdiag<3>(s.A, s.T, tid);
   // ta = T diag(beta e^gam), tb = T diag(beta) (bf16, lower triangle incl. diagonal), over A's bytes
   __nv_bfloat16* s_ta = reinterpret_cast<__nv_bfloat16*>(s.A);
   __nv_bfloat16* s_tb = s_ta + GC * PT;
