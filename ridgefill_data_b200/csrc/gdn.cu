@@ -279,24 +279,6 @@ struct WySmem {
   float eg[GC];
 };
 
-// 16x16 fp32 block product: out (+)= sign * X_blk Y_blk; thread owns two adjacent outputs of one row.
-__device__ __forceinline__ void blk_mm(float* out, const float* X, const float* Y, int xb_r, int xb_c, int yb_r,
-                                       int yb_c, int ob_r, int ob_c, bool accumulate, float sign, int tid) {
-  const int r = tid >> 3, c = (tid & 7) * 2;
-  const float* xr = X + (xb_r * 16 + r) * PA + xb_c * 16;
-  const float* yc = Y + (yb_r * 16) * PA + yb_c * 16 + c;
-  float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const float x = xr[k];
-    a0 += x * yc[k * PA];
-    a1 += x * yc[k * PA + 1];
-  }
-  float* o = out + (ob_r * 16 + r) * PA + ob_c * 16 + c;
-  o[0] = accumulate ? o[0] + sign * a0 : sign * a0;
-  o[1] = accumulate ? o[1] + sign * a1 : sign * a1;
-}
-
 // One distance D of the blocked inverse: for every pair (i, j = i - D) at once, X_ij = sum_{k=j}^{i-1} A_ik T_kj
 // into A's upper block (j, i), then T_ij = -T_ii X_ij. Thread = (row r, columns c, c + 1) of every pair's block; the
 // pairs' and columns' sums are independent chains (accumulated in registers, the k order as blk_mm's).
