@@ -240,9 +240,14 @@ __global__ void __launch_bounds__(192, 1)
           if (key > pos || key >= n_keys) x[e] = -INFINITY;
         }
       }
-      float mt = -INFINITY;
+      // row max and row sum as 8 independent chains (one softmax warp per scheduler: nothing else hides the
+      // latency of a 64-long dependent chain)
+      float mp[8];
 #pragma unroll
-      for (int e = 0; e < BN; ++e) mt = fmaxf(mt, x[e]);
+      for (int u = 0; u < 8; ++u) mp[u] = x[u];
+#pragma unroll
+      for (int e = 8; e < BN; ++e) mp[e & 7] = fmaxf(mp[e & 7], x[e]);
+      const float mt = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       const float m_new = fmaxf(m_used, mt * a.scale_log2);   // scale > 0: max commutes with it
       bool rescale = false;
       float factor = 1.f;
@@ -254,12 +259,13 @@ __global__ void __launch_bounds__(192, 1)
         m_used = m_new;
       }
       const float base = m_used == -INFINITY ? 0.f : m_used;
-      float sum = 0.f;
+      float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int e = 0; e < BN; ++e) {
         x[e] = ex2(fmaf(x[e], a.scale_log2, -base));
-        sum += x[e];
+        sp[e & 7] += x[e];
       }
+      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       l = l * factor + sum;
       const int pb = j % PB;
       if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
