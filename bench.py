@@ -324,7 +324,7 @@ def main():
         barrier()
         torch.cuda.synchronize()
         launches0 = ext().launch_count()
-        ms, p50_ms, _ = timed(lambda: step(ids_dev), args.steps, nvtx=os.environ.get("RF_NVTX") == "1")
+        ms, p50_ms, step_ms = timed(lambda: step(ids_dev), args.steps, nvtx=os.environ.get("RF_NVTX") == "1")
         barrier()
         launches = ext().launch_count() - launches0
         clocks = sampler.stop()
@@ -428,7 +428,8 @@ def main():
                     flops_per_step=round(flops), tflops=round(tflops, 1),
                     frac_of_sustained_bf16=round(tflops / (peaks["bf16_tflops_sustained"] * world), 3),
                     peaks_source=peaks["source"], ttft_by_len=by_len,
-                    hbm_peak_gib=round(torch.cuda.max_memory_allocated(device) / 2 ** 30, 2))
+                    hbm_peak_gib=round(torch.cuda.max_memory_allocated(device) / 2 ** 30, 2),
+                    steps_ms_rank0=[round(x, 2) for x in step_ms])
         if exact_ms:
             line.update(exact_prefill_ms=round(exact_max, 3), speedup_vs_exact=round(exact_max / p50_max, 3))
         print(json.dumps(line), flush=True)
