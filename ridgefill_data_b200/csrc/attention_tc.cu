@@ -56,11 +56,25 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-template <int HD, int BN, int PB>
+// 2^x for x <= 0 on the FMA and integer pipes instead of the special-function unit. Range reduction by the
+// round-to-nearest of an fp32 add with 1.5 * 2^23: x = n + f, n integer, f in [-1/2, 1/2]; 2^f by a cubic whose
+// coefficients come from a Lawson (iteratively reweighted least-squares) minimax fit of 2^f on [-1/2, 1/2] for
+// relative error (7.5e-5 in exact arithmetic, 1.5e-4 evaluated in fp32: far below the bf16 rounding of P); 2^n
+// by adding n to the exponent field. Inputs below -126 (masked scores included) give exactly 0.
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float t = __fadd_rn(x, 12582912.f);
+  const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
+  const float p = fmaf(fmaf(fmaf(0.05517144f, f, 0.24261071f), f, 0.69326097f), f, 0.99992812f);
+  const int n = __float_as_int(t) - 0x4B400000;
+  return x < -126.f ? 0.f : __int_as_float(__float_as_int(p) + (n << 23));
+}
+
+template <int HD, int BN, int PB, int POLY>
 __global__ void __launch_bounds__(192, 1)
     tc_flash_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, TcFaArgs a) {
   using Cfg = TcFaCfg<HD, BN, PB>;
+  static_assert(POLY >= 0 && POLY <= 8, "POLY: columns of every 8 whose exponential runs on the FMA pipe");
   constexpr uint32_t IDESC_S = idesc_bf16_f32(128, BN, false, false);
   constexpr uint32_t IDESC_O = idesc_bf16_f32(128, HD, false, true);
   extern __shared__ uint8_t smem_raw[];
@@ -262,7 +276,8 @@ __global__ void __launch_bounds__(192, 1)
       float sp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int e = 0; e < BN; ++e) {
-        x[e] = ex2(fmaf(x[e], a.scale_log2, -base));
+        const float z = fmaf(x[e], a.scale_log2, -base);
+        x[e] = (e & 7) < POLY ? exp2_fma(z) : ex2(z);   // POLY of every 8 columns off the SFU
         sp[e & 7] += x[e];
       }
       const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
@@ -386,22 +401,25 @@ static CUtensorMap tmap3(const void* base, int hd, int rows, int heads, long hea
   return tm;
 }
 
-template <int HD, int BN, int PB>
+template <int HD, int BN, int PB, int POLY>
 static void launch_tc(const AttnArgs& x, cudaStream_t stream) {
   using Cfg = TcFaCfg<HD, BN, PB>;
   static PerDeviceOnce once;
-  once([] { cudaFuncSetAttribute(tc_flash_kernel<HD, BN, PB>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM); });
+  once([] {
+    cudaFuncSetAttribute(tc_flash_kernel<HD, BN, PB, POLY>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+  });
   CUtensorMap tq = tmap3(x.q, HD, x.nq, x.hq, x.q_head_stride, 128);
   CUtensorMap tk = tmap3(x.k, HD, x.nk, x.hkv, x.kv_head_stride, BN);
   CUtensorMap tv = tmap3(x.v, HD, x.nk, x.hkv, x.kv_head_stride, BN);
   TcFaArgs a{x.hq, x.hkv, x.nq, x.nk, x.q_start, x.qpos, x.scale * 1.4426950408889634f, x.gate, x.gate_row, x.gate_head,
              x.out, x.out_row, x.err};
   dim3 grid((x.nq + 127) / 128, x.hq);
-  tc_flash_kernel<HD, BN, PB><<<grid, 192, Cfg::SMEM, stream>>>(tq, tk, tv, a);
+  tc_flash_kernel<HD, BN, PB, POLY><<<grid, 192, Cfg::SMEM, stream>>>(tq, tk, tv, a);
   count_launch();
 }
 
 int attn_p_buffers = 2;
+int attn_poly = 0;
 
 bool flash_attention_tc(const AttnArgs& x, cudaStream_t stream) {
   if (x.nq <= 0) return false;
@@ -413,12 +431,16 @@ bool flash_attention_tc(const AttnArgs& x, cudaStream_t stream) {
   if (x.out_row % 8) return false;
   switch (x.hd) {
     case 128:
-      if (attn_p_buffers == 1) launch_tc<128, 128, 1>(x, stream);
-      else launch_tc<128, 128, 2>(x, stream);
+      if (attn_p_buffers == 1) launch_tc<128, 128, 1, 0>(x, stream);
+      else if (attn_poly == 2) launch_tc<128, 128, 2, 2>(x, stream);
+      else if (attn_poly == 4) launch_tc<128, 128, 2, 4>(x, stream);
+      else launch_tc<128, 128, 2, 0>(x, stream);
       return true;
     case 256:
-      if (attn_p_buffers == 1) launch_tc<256, 64, 1>(x, stream);
-      else launch_tc<256, 64, 2>(x, stream);
+      if (attn_p_buffers == 1) launch_tc<256, 64, 1, 0>(x, stream);
+      else if (attn_poly == 2) launch_tc<256, 64, 2, 2>(x, stream);
+      else if (attn_poly == 4) launch_tc<256, 64, 2, 4>(x, stream);
+      else launch_tc<256, 64, 2, 0>(x, stream);
       return true;
     default: return false;
   }

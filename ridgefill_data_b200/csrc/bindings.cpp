@@ -94,6 +94,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sm_count", &sm_count);
   m.def("launch_count", &launch_count);
   m.def("set_gemm_2sm", &set_gemm_2sm);
+  m.def("set_attn_poly", [](int64_t n) {
+    const int was = rf::attn_poly;
+    rf::attn_poly = (n == 2 || n == 4) ? (int)n : 0;
+    return was;
+  });
   m.def("set_attn_p_buffers", [](int64_t n) {
     const int was = rf::attn_p_buffers;
     rf::attn_p_buffers = n == 1 ? 1 : 2;

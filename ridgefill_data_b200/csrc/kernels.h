@@ -89,6 +89,7 @@ struct AttnArgs {
 void flash_attention(const AttnArgs& a, cudaStream_t stream);
 bool flash_attention_tc(const AttnArgs& a, cudaStream_t stream);
 extern int attn_p_buffers;   // 1 or 2 shared-memory P buffers in the tcgen05 attention (2 by default)
+extern int attn_poly;        // 0, 2 or 4 of every 8 softmax exponentials on the FMA pipe (exp2_fma)
 
 // ---- gdn.cu
 struct GdnPrepArgs {

@@ -70,6 +70,8 @@ def ext():
         mod.set_gemm_2sm(False)
     if os.environ.get("RF_ATTN_PBUF") == "1":    # A/B switch: one P buffer in the tcgen05 attention
         mod.set_attn_p_buffers(1)
+    if os.environ.get("RF_ATTN_POLY") in ("2", "4"):   # A/B switch: softmax exponentials partly on the FMA pipe
+        mod.set_attn_poly(int(os.environ["RF_ATTN_POLY"]))
     return _mod
 
 

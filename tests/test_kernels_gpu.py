@@ -171,3 +171,28 @@ def test_gdn_two_level_scan_matches_sequential_and_oracle(groups, need_out):
     assert _rel(states[groups], rs) < 3e-2
     if need_out:
         assert _rel(outs[groups].view(n, nv, dv).transpose(0, 1), ro) < 3e-2
+
+
+@pytest.mark.parametrize("poly", [2, 4])
+@pytest.mark.parametrize("hd", [128, 256])
+def test_flash_attention_with_fma_exponentials(poly, hd):
+    """Part of every row's exponentials on the FMA pipe (range-reduced cubic, csrc/attention_tc.cu exp2_fma): the
+    result stays within the same tolerance of the fp32 oracle as the special-function path, and close to it."""
+    from ridgefill_data_b200.ops._ext import ext
+    torch.manual_seed(9)
+    hq, hkv, nq = 4, 2, 300
+    q = torch.randn(hq, nq, hd, device=dev).bfloat16()
+    k = torch.randn(hkv, nq, hd, device=dev).bfloat16()
+    v = torch.randn(hkv, nq, hd, device=dev).bfloat16()
+    ref = O.attend(q, k, v, hd ** -0.5)
+    outs = {}
+    for mode in (0, poly):
+        was = ext().set_attn_poly(mode)
+        try:
+            out = torch.empty(nq, hq * hd, device=dev, dtype=torch.bfloat16)
+            K.attention(q, k, v, nq, hd ** -0.5, out, impl="tcgen05")
+            outs[mode] = out
+        finally:
+            ext().set_attn_poly(was)
+    assert _rel(outs[poly], ref) < 2e-2
+    assert _rel(outs[poly], outs[0]) < 5e-3
