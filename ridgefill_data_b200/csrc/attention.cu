@@ -239,7 +239,10 @@ static void launch_fa(const AttnArgs& a, cudaStream_t stream) {
 
 void flash_attention(const AttnArgs& a, cudaStream_t stream) {
   if (a.nq <= 0) return;
+  if (a.kv_pages != nullptr && a.impl == 1)
+    throw std::runtime_error("flash_attention: paged K/V runs on the tcgen05 kernel only");
   if (a.impl != 1 && flash_attention_tc(a, stream)) return;
+  if (a.kv_pages != nullptr) throw std::runtime_error("flash_attention: paged K/V not supported for this call");
   if (a.impl == 2) throw std::runtime_error("flash_attention: the tcgen05 path does not cover this call");
   switch (a.hd) {
     case 64: launch_fa<64>(a, stream); break;

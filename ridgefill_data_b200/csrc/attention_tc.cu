@@ -37,6 +37,8 @@ struct TcFaCfg {
 struct TcFaArgs {
   int hq, hkv, nq, nk, q_start;
   const int* qpos;   // ascending query positions, or nullptr: q_start + row
+  const int* kv_pages;   // paged K/V: page of every page_size key rows (nullptr: contiguous [hkv][rows][hd])
+  int page_size;
   float scale_log2;
   const __nv_bfloat16* gate;
   long gate_row, gate_head;
@@ -148,17 +150,28 @@ __global__ void __launch_bounds__(192, 1)
           break;
         }
         mbar_expect_tx(&k_full[st], Cfg::K_BYTES);
+        // paged K/V: the key tile lies inside one page (page_size is a multiple of BN)
+        const int page = a.kv_pages != nullptr ? a.kv_pages[(j * BN) / a.page_size] : 0;
+        const int prow = a.kv_pages != nullptr ? (j * BN) % a.page_size : j * BN;
 #pragma unroll
-        for (int b = 0; b < HD / 64; ++b)
-          tma_load_3d(sK + st * Cfg::K_BYTES + b * BN * 128, &tmK, &k_full[st], b * 64, j * BN, kvh);
+        for (int b = 0; b < HD / 64; ++b) {
+          if (a.kv_pages != nullptr)
+            tma_load_4d(sK + st * Cfg::K_BYTES + b * BN * 128, &tmK, &k_full[st], b * 64, prow, kvh, page);
+          else
+            tma_load_3d(sK + st * Cfg::K_BYTES + b * BN * 128, &tmK, &k_full[st], b * 64, j * BN, kvh);
+        }
         if (!mbar_wait(&v_empty[st], par, a.err, kErrTimeoutProducer)) {
           *abort_flag = 1;
           break;
         }
         mbar_expect_tx(&v_full[st], Cfg::V_BYTES);
 #pragma unroll
-        for (int b = 0; b < HD / 64; ++b)
-          tma_load_3d(sV + st * Cfg::V_BYTES + b * BN * 128, &tmV, &v_full[st], b * 64, j * BN, kvh);
+        for (int b = 0; b < HD / 64; ++b) {
+          if (a.kv_pages != nullptr)
+            tma_load_4d(sV + st * Cfg::V_BYTES + b * BN * 128, &tmV, &v_full[st], b * 64, prow, kvh, page);
+          else
+            tma_load_3d(sV + st * Cfg::V_BYTES + b * BN * 128, &tmV, &v_full[st], b * 64, j * BN, kvh);
+        }
       }
     }
   } else if (warp == 1) {
@@ -401,6 +414,20 @@ static CUtensorMap tmap3(const void* base, int hd, int rows, int heads, long hea
   return tm;
 }
 
+// 4-D map over a page pool [pages][heads][page_size][hd], box {64, box_rows, 1, 1}
+static CUtensorMap tmap4_pages(const void* base, int hd, int page_size, int heads, int pages, int box_rows) {
+  CUtensorMap tm;
+  cuuint64_t dims[4] = {(cuuint64_t)hd, (cuuint64_t)page_size, (cuuint64_t)heads, (cuuint64_t)pages};
+  cuuint64_t strides[3] = {(cuuint64_t)hd * 2, (cuuint64_t)page_size * hd * 2, (cuuint64_t)heads * page_size * hd * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode_fa()(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("tc_flash: paged tensor map encode failed " + std::to_string((int)r));
+  return tm;
+}
+
 template <int HD, int BN, int PB, int POLY>
 static void launch_tc(const AttnArgs& x, cudaStream_t stream) {
   using Cfg = TcFaCfg<HD, BN, PB>;
@@ -409,10 +436,16 @@ static void launch_tc(const AttnArgs& x, cudaStream_t stream) {
     cudaFuncSetAttribute(tc_flash_kernel<HD, BN, PB, POLY>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
   });
   CUtensorMap tq = tmap3(x.q, HD, x.nq, x.hq, x.q_head_stride, 128);
-  CUtensorMap tk = tmap3(x.k, HD, x.nk, x.hkv, x.kv_head_stride, BN);
-  CUtensorMap tv = tmap3(x.v, HD, x.nk, x.hkv, x.kv_head_stride, BN);
-  TcFaArgs a{x.hq, x.hkv, x.nq, x.nk, x.q_start, x.qpos, x.scale * 1.4426950408889634f, x.gate, x.gate_row, x.gate_head,
-             x.out, x.out_row, x.err};
+  CUtensorMap tk, tv;
+  if (x.kv_pages != nullptr) {
+    tk = tmap4_pages(x.k, HD, x.page_size, x.hkv, x.num_pages, BN);
+    tv = tmap4_pages(x.v, HD, x.page_size, x.hkv, x.num_pages, BN);
+  } else {
+    tk = tmap3(x.k, HD, x.nk, x.hkv, x.kv_head_stride, BN);
+    tv = tmap3(x.v, HD, x.nk, x.hkv, x.kv_head_stride, BN);
+  }
+  TcFaArgs a{x.hq, x.hkv, x.nq, x.nk, x.q_start, x.qpos, x.kv_pages, x.page_size, x.scale * 1.4426950408889634f,
+             x.gate, x.gate_row, x.gate_head, x.out, x.out_row, x.err};
   dim3 grid((x.nq + 127) / 128, x.hq);
   tc_flash_kernel<HD, BN, PB, POLY><<<grid, 192, Cfg::SMEM, stream>>>(tq, tk, tv, a);
   count_launch();
@@ -423,6 +456,11 @@ int attn_poly = 0;
 
 bool flash_attention_tc(const AttnArgs& x, cudaStream_t stream) {
   if (x.nq <= 0) return false;
+  if (x.kv_pages != nullptr) {
+    const int bn = x.hd == 256 ? 64 : 128;
+    if ((x.hd != 128 && x.hd != 256) || x.page_size <= 0 || x.page_size % bn != 0 || x.num_pages <= 0)
+      throw std::runtime_error("flash_attention: paged K/V needs head_dim 128 / 256 and a page size multiple of 128");
+  }
   if (reinterpret_cast<uintptr_t>(x.q) % 16 || reinterpret_cast<uintptr_t>(x.k) % 16 ||
       reinterpret_cast<uintptr_t>(x.v) % 16)
     return false;

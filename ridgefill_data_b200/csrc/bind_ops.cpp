@@ -37,7 +37,8 @@ void rmsnorm(Tensor x, Tensor w, Tensor out, double eps, bool zero_centred) {
 
 void head_norm_rope(Tensor src, int64_t src_row_stride, int64_t src_head_stride, int64_t n_heads, int64_t head_dim,
                     int64_t n_rows, OptT norm_w, int64_t norm_mode, double eps, OptT cos, OptT sin, int64_t rot,
-                    OptT pos, int64_t pos_offset, Tensor dst, int64_t dst_head_stride, int64_t dst_row_stride) {
+                    OptT pos, int64_t pos_offset, Tensor dst, int64_t dst_head_stride, int64_t dst_row_stride,
+                    OptT dst_pages, int64_t page_size, int64_t dst_page_stride, int64_t dst_row0) {
   need(src, at::kBFloat16, "src");
   need(dst, at::kBFloat16, "dst");
   TORCH_CHECK(head_dim % 32 == 0 && head_dim <= 256, "head_norm_rope: head_dim % 32 == 0, <= 256");
@@ -65,6 +66,14 @@ void head_norm_rope(Tensor src, int64_t src_row_stride, int64_t src_head_stride,
     a.pos = pos->data_ptr<int>();
   }
   a.pos_offset = (int)pos_offset;
+  if (dst_pages.has_value()) {
+    need(*dst_pages, at::kInt, "dst_pages");
+    TORCH_CHECK(page_size > 0, "head_norm_rope: page_size");
+    a.dst_pages = dst_pages->data_ptr<int>();
+    a.page_size = (int)page_size;
+    a.dst_page_stride = dst_page_stride;
+    a.dst_row0 = (int)dst_row0;
+  }
   a.dst = bf(dst);
   a.dst_head_stride = dst_head_stride;
   a.dst_row_stride = dst_row_stride;
@@ -95,7 +104,8 @@ void embed_gather(Tensor table, Tensor ids, Tensor out) {
 
 void flash_attention(Tensor q, int64_t q_head_stride, Tensor k, Tensor v, int64_t kv_head_stride, Tensor out,
                      int64_t hq, int64_t hkv, int64_t hd, int64_t nq, int64_t nk, OptT qpos, int64_t q_start,
-                     double scale, OptT gate, int64_t gate_row, int64_t gate_head, int64_t impl, Tensor err) {
+                     double scale, OptT gate, int64_t gate_row, int64_t gate_head, int64_t impl, Tensor err,
+                     OptT kv_pages, int64_t page_size, int64_t num_pages) {
   need(q, at::kBFloat16, "q");
   need(k, at::kBFloat16, "k");
   need(v, at::kBFloat16, "v");
@@ -131,6 +141,13 @@ void flash_attention(Tensor q, int64_t q_head_stride, Tensor k, Tensor v, int64_
   a.out_row = out.stride(0);
   a.err = err.data_ptr<int>();
   a.impl = (int)impl;
+  if (kv_pages.has_value()) {
+    need(*kv_pages, at::kInt, "kv_pages");
+    a.kv_pages = kv_pages->data_ptr<int>();
+    a.page_size = (int)page_size;
+    a.num_pages = (int)num_pages;
+    TORCH_CHECK(kv_pages->numel() * page_size >= nk, "flash_attention: the page table covers fewer than nk rows");
+  }
   rf::flash_attention(a, cur());
 }
 
@@ -248,10 +265,18 @@ void gdn_chunk_scan(OptT q, Tensor k, Tensor v, Tensor beta, Tensor g, Tensor st
 void register_ops(pybind11::module_& m) {
   namespace py = pybind11;
   m.def("rmsnorm", &rmsnorm);
-  m.def("head_norm_rope", &head_norm_rope);
+  m.def("head_norm_rope", &head_norm_rope, py::arg("src"), py::arg("src_row_stride"), py::arg("src_head_stride"),
+        py::arg("n_heads"), py::arg("head_dim"), py::arg("n_rows"), py::arg("norm_w"), py::arg("norm_mode"),
+        py::arg("eps"), py::arg("cos"), py::arg("sin"), py::arg("rot"), py::arg("pos"), py::arg("pos_offset"),
+        py::arg("dst"), py::arg("dst_head_stride"), py::arg("dst_row_stride"), py::arg("dst_pages") = py::none(),
+        py::arg("page_size") = 0, py::arg("dst_page_stride") = 0, py::arg("dst_row0") = 0);
   m.def("gated_rmsnorm", &gated_rmsnorm);
   m.def("embed_gather", &embed_gather);
-  m.def("flash_attention", &flash_attention);
+  m.def("flash_attention", &flash_attention, py::arg("q"), py::arg("q_head_stride"), py::arg("k"), py::arg("v"),
+        py::arg("kv_head_stride"), py::arg("out"), py::arg("hq"), py::arg("hkv"), py::arg("hd"), py::arg("nq"),
+        py::arg("nk"), py::arg("qpos"), py::arg("q_start"), py::arg("scale"), py::arg("gate"), py::arg("gate_row"),
+        py::arg("gate_head"), py::arg("impl"), py::arg("err"), py::arg("kv_pages") = py::none(),
+        py::arg("page_size") = 0, py::arg("num_pages") = 0);
   m.def("gdn_prep", &gdn_prep);
   m.def("gdn_conv_state_update", &gdn_conv_state_update);
   m.def("gdn_chunk_scan", &gdn_chunk_scan);

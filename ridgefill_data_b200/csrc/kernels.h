@@ -58,6 +58,12 @@ struct HeadNormRopeArgs {
   __nv_bfloat16* dst;           // head h of row t at dst + h * dst_head_stride + t * dst_row_stride
   long dst_head_stride;
   long dst_row_stride;
+  // paged destination (dst_pages != nullptr): row t goes to cache row r = dst_row0 + t, stored in page
+  // dst_pages[r / page_size] at dst + page * dst_page_stride + h * dst_head_stride + (r % page_size) * dst_row_stride
+  const int* dst_pages = nullptr;
+  int page_size = 0;
+  long dst_page_stride = 0;
+  int dst_row0 = 0;
 };
 void head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t stream);
 
@@ -85,6 +91,11 @@ struct AttnArgs {
   long out_row;
   int* err;                    // bounded-wait error word (tcgen05 path)
   int impl;                    // 0 auto (tcgen05 when possible), 1 mma.sync kernel, 2 tcgen05 only
+  // paged K/V (kv_pages != nullptr, tcgen05 path only): k / v point at pools [num_pages][hkv][page_size][hd]; key row
+  // j lives in page kv_pages[j / page_size] at row j % page_size; page_size a multiple of the key tile (128)
+  const int* kv_pages = nullptr;
+  int page_size = 0;
+  int num_pages = 0;
 };
 void flash_attention(const AttnArgs& a, cudaStream_t stream);
 bool flash_attention_tc(const AttnArgs& a, cudaStream_t stream);

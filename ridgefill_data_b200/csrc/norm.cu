@@ -142,7 +142,14 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(HeadNormRopeArgs a)
     }
     for (int j = 0; j < per; ++j) v[j] = out[j];
   }
-  __nv_bfloat16* dst = a.dst + (long)head * a.dst_head_stride + (long)row * a.dst_row_stride;
+  __nv_bfloat16* dst;
+  if (a.dst_pages != nullptr) {
+    const int r = a.dst_row0 + row;
+    dst = a.dst + (long)a.dst_pages[r / a.page_size] * a.dst_page_stride + (long)head * a.dst_head_stride +
+          (long)(r % a.page_size) * a.dst_row_stride;
+  } else {
+    dst = a.dst + (long)head * a.dst_head_stride + (long)row * a.dst_row_stride;
+  }
   for (int j = 0; j < per; ++j) dst[lane * per + j] = __float2bfloat16(v[j]);
 }
 

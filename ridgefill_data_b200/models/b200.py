@@ -29,6 +29,7 @@ class _B200:
 
     zero_centred = False
     capacity_hint = 0
+    kv_pool = None     # models.kvpool.KVPool: attention caches in shared pages (multi-sequence serving)
     tp = None          # parallel.tp.TensorParallel when the weights are sharded over ranks
     ep = None          # parallel.ep.ExpertParallel when the experts are spread over ranks
 
@@ -97,8 +98,11 @@ class _B200:
             del w["gate"], w["up"]
 
     # ---- attention
-    def _kv_reserve(self, c, m):
+    def _kv_reserve(self, c, m, i=None):
         n = c.get("n", 0)
+        if self.kv_pool is not None:
+            self.kv_pool.grow(i, c, n + m, self.device)
+            return n
         kb = c.get("kbuf")
         if kb is None or n + m > kb.shape[1]:
             cap = max(n + m + KV_RESERVE, self.capacity_hint)
@@ -113,7 +117,17 @@ class _B200:
 
     def _commit_kv(self, c, n_new):
         c["n"] = n_new
+        if self.kv_pool is not None:          # paged: no single K/V tensor of the layer
+            c["k"] = c["v"] = None
+            return
         c["k"], c["v"] = c["kbuf"][:, :n_new], c["vbuf"][:, :n_new]
+
+    def _attend(self, i, q, c, nk, out, **kw):
+        """tcgen05 attention over cache entry c of layer i (contiguous buffers, or the pool's pages)."""
+        if self.kv_pool is not None:
+            pool = self.kv_pool
+            return K.attention(q, pool.k[i], pool.v[i], nk, self.scale, out, pages=c["pages_dev"], **kw)
+        return K.attention(q, c["kbuf"], c["vbuf"], nk, self.scale, out, **kw)
 
     def _qk_mode(self):
         if not self.cfg.qk_norm:
@@ -126,10 +140,19 @@ class _B200:
         m = kv_src.shape[0]
         hd, hkv = self.head_dim, self.n_kv
         p0, parr = self._span(pos)
-        n0 = self._kv_reserve(c, m)
+        n0 = self._kv_reserve(c, m, i)
+        tables = self.rope(p0 + m if parr is None else int(pos.max()) + 1)
+        if self.kv_pool is not None:
+            pool = self.kv_pool
+            paged = dict(pages=c["pages_dev"], page_size=pool.page_size, page_stride=pool.page_stride, row0=n0)
+            K.head_norm_rope(kv_src, hkv, hd, hd, pool.k[i], pool.page_size * hd, hd, norm_w=w.get("k_norm"),
+                             norm_mode=self._qk_mode(), eps=self.eps, tables=tables, rot=self.cfg.rot_dim,
+                             pos=parr, pos_offset=p0, **paged)
+            K.head_norm_rope(kv_src[:, hkv * hd:], hkv, hd, hd, pool.v[i], pool.page_size * hd, hd, **paged)
+            self._commit_kv(c, n0 + m)
+            return n0
         kb, vb = c["kbuf"], c["vbuf"]
         cap = kb.shape[1]
-        tables = self.rope(p0 + m if parr is None else int(pos.max()) + 1)
         K.head_norm_rope(kv_src, hkv, hd, hd, kb[:, n0:], cap * hd, hd, norm_w=w.get("k_norm"),
                          norm_mode=self._qk_mode(), eps=self.eps, tables=tables, rot=self.cfg.rot_dim,
                          pos=parr, pos_offset=p0)
@@ -160,8 +183,7 @@ class _B200:
         K.head_norm_rope(qkv, hq, hd, 2 * hd if gated else hd, q, n * hd, hd, norm_w=w.get("q_norm"),
                          norm_mode=self._qk_mode(), eps=self.eps, tables=tables, rot=self.cfg.rot_dim, pos=parr,
                          pos_offset=p0)
-        K.attention(q, c["kbuf"], c["vbuf"], n0 + n, self.scale, o, q_start=n0,
-                    gate=qkv[:, hd:] if gated else None, gate_head=2 * hd)
+        self._attend(i, q, c, n0 + n, o, q_start=n0, gate=qkv[:, hd:] if gated else None, gate_head=2 * hd)
         return o
 
     def decode_batch(self, toks, positions, caches):
@@ -237,8 +259,7 @@ class _B200:
             K.head_norm_rope(qg, hq, hd, 2 * hd if gated else hd, q, nr * hd, hd, norm_w=w.get("q_norm"),
                              norm_mode=self._qk_mode(), eps=self.eps, tables=tables, rot=self.cfg.rot_dim, pos=rpos)
             y = torch.empty(nr, hq * hd, dtype=self.dtype, device=self.device)
-            K.attention(q, c["kbuf"], c["vbuf"], c["n"], self.scale, y, qpos=rpos,
-                        gate=qg[:, hd:] if gated else None, gate_head=2 * hd)
+            self._attend(i, q, c, c["n"], y, qpos=rpos, gate=qg[:, hd:] if gated else None, gate_head=2 * hd)
             wo = w["o"]
         else:
             proj = G.linear(x, w["in_p"])

@@ -29,13 +29,16 @@ def rope_tables(inv_freq, max_pos, device, dtype=BF16):
 
 
 def head_norm_rope(src, n_heads, head_dim, head_stride, dst, dst_head_stride, dst_row_stride, norm_w=None,
-                   norm_mode=-1, eps=1e-6, tables=None, rot=0, pos=None, pos_offset=0):
+                   norm_mode=-1, eps=1e-6, tables=None, rot=0, pos=None, pos_offset=0, pages=None, page_size=0,
+                   page_stride=0, row0=0):
     """Per (row, head) of src [n, *] (head h at column h * head_stride): optional head RMSNorm, RoPE on the
     first rot dims at positions pos (int32 [n]) or pos_offset + row; written to dst + h * dst_head_stride +
-    row * dst_row_stride (element strides)."""
+    row * dst_row_stride (element strides). With pages (int32 page ids): row t is cache row row0 + t, stored in
+    page pages[(row0 + t) // page_size] of the pool dst (page_stride elements apart) at row (row0 + t) % page_size."""
     cos, sin = tables if tables is not None else (None, None)
     ext().head_norm_rope(src, src.stride(0), head_stride, n_heads, head_dim, src.shape[0], norm_w, norm_mode,
-                         float(eps), cos, sin, rot, pos, pos_offset, dst, dst_head_stride, dst_row_stride)
+                         float(eps), cos, sin, rot, pos, pos_offset, dst, dst_head_stride, dst_row_stride,
+                         pages, page_size, page_stride, row0)
 
 
 def gated_rmsnorm(o, z, w, heads, dv, eps, out=None):
@@ -55,15 +58,25 @@ def embed(table, ids):
 ATTN_IMPL = {"auto": 0, "mma": 1, "tcgen05": 2}
 
 
-def attention(q, k_cache, v_cache, nk, scale, out, q_start=0, qpos=None, gate=None, gate_head=0, impl="auto"):
+def attention(q, k_cache, v_cache, nk, scale, out, q_start=0, qpos=None, gate=None, gate_head=0, impl="auto",
+              pages=None):
     """Causal GQA attention. q [hq, nq, hd] (any head pitch, row pitch hd); k_cache/v_cache [hkv, cap, hd]
     (the first nk rows valid); queries at positions q_start + row (or qpos int32 [nq]); out [nq, hq * hd];
-    gate: a [nq, *] view whose head h starts at column h * gate_head (o * sigmoid(gate))."""
+    gate: a [nq, *] view whose head h starts at column h * gate_head (o * sigmoid(gate)).
+    pages (int32 page ids, tcgen05 kernel only): k_cache / v_cache are page pools [num_pages, hkv, page_size, hd]
+    and key row j lives in page pages[j // page_size]."""
     hq, nq, hd = q.shape
-    hkv = k_cache.shape[0]
-    ext().flash_attention(q, q.stride(0), k_cache, v_cache, k_cache.stride(0), out, hq, hkv, hd, nq, nk, qpos,
-                          q_start, float(scale), gate, gate.stride(0) if gate is not None else 0, gate_head,
-                          ATTN_IMPL[impl], ext().error_word(q.device.index or 0))
+    if pages is None:
+        hkv = k_cache.shape[0]
+        ext().flash_attention(q, q.stride(0), k_cache, v_cache, k_cache.stride(0), out, hq, hkv, hd, nq, nk, qpos,
+                              q_start, float(scale), gate, gate.stride(0) if gate is not None else 0, gate_head,
+                              ATTN_IMPL[impl], ext().error_word(q.device.index or 0))
+        return out
+    n_pages, hkv, page_size, _ = k_cache.shape
+    ext().flash_attention(q, q.stride(0), k_cache, v_cache, page_size * hd, out, hq, hkv, hd, nq, nk, qpos, q_start,
+                          float(scale), gate, gate.stride(0) if gate is not None else 0, gate_head, ATTN_IMPL[impl],
+                          ext().error_word(q.device.index or 0), kv_pages=pages, page_size=page_size,
+                          num_pages=n_pages)
     return out
 
 

@@ -53,6 +53,9 @@ def build(args):
     arms = {"off": Arm("exact"), "on": Arm("ridgefill", split=split, tail=args.tail, fill="proj", projector=proj),
             "quality": Arm("quality", split=split, tail=args.tail, fill="proj", projector=proj,
                            meta={"quality": qmode})}
+    if getattr(args, "kv_pages", 0):
+        from ..models.kvpool import KVPool
+        model.kv_pool = KVPool(model, args.kv_pages, getattr(args, "page_size", 128))
     vocab = model.cfg.vocab
     props = dict(model=str(name), n_layers=model.n_layers, vocab=vocab, split=split, tail=args.tail,
                  backend=args.backend, interleave=args.interleave)
@@ -75,6 +78,10 @@ def main(argv=None):
     ap.add_argument("--qattn-share", type=float, default=0.2, help="quality mode: rows picked by window attention")
     ap.add_argument("--qattn-window", type=int, default=64)
     ap.add_argument("--lexical", type=int, default=1, help="quality mode: repeated-span rows (1 on, 0 off)")
+    ap.add_argument("--kv-pages", type=int, default=0,
+                    help="serve every request from one paged K/V pool of this many pages per attention layer "
+                         "(0: a contiguous cache per request)")
+    ap.add_argument("--page-size", type=int, default=128, help="rows per K/V page (a multiple of 128)")
     ap.add_argument("--interleave", type=int, default=4, help="decode round every this many prefill layers (0: off)")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8080)

@@ -155,6 +155,9 @@ class Scheduler:
         n = int(req.ids.numel())
         req.t_prefill0 = time.perf_counter()
         tick = self._tick_for(req)
+        pool = getattr(model, "kv_pool", None)
+        if pool is not None:
+            pool.owner = req.rid                       # pages taken during this prefill belong to the request
         try:
             ids = req.ids.to(model.device)
             quality = arm.meta.get("quality")
@@ -176,6 +179,8 @@ class Scheduler:
             tok = int(D.check_finite(logits[-1], f"{req.rid} first token").argmax())
         except Exception as e:                         # report, drop the request, keep serving
             self.stats["errors"] += 1
+            if pool is not None:
+                pool.release_owner(req.rid)
             self._emit(req, {"error": f"{type(e).__name__}: {e}", "stop": True})
             return
         now = time.perf_counter()
@@ -206,6 +211,17 @@ class Scheduler:
         """One token for every active request: the plain ones together through model.decode_batch (one pass over
         the weights for all of them, up to max_batch rows at a time), SwiftKV-native ones alone (their late layers
         run a different path)."""
+        pool = getattr(self.model, "kv_pool", None)
+        saved = pool.owner if pool is not None else None
+        if pool is not None:       # pages a decode step takes are released with the cache that holds them
+            pool.owner = "decode"
+        try:
+            self._decode_round_inner()
+        finally:
+            if pool is not None:
+                pool.owner = saved
+
+    def _decode_round_inner(self):
         reqs = list(self.active)
         plain = [r for r in reqs if r.arm.fill != "swiftkv_native"]
         toks = {}
@@ -236,7 +252,7 @@ class Scheduler:
             except Exception as e:
                 self.stats["errors"] += 1
                 self._emit(req, {"error": f"{type(e).__name__}: {e}", "stop": True})
-                req.cache = None
+                self._release(req)
                 continue
             req.position += 1
             req.t_last = time.perf_counter()
@@ -246,6 +262,14 @@ class Scheduler:
             else:
                 keep.append(req)
         self.active = keep
+
+    def _release(self, req):
+        """Drop the request's cache; with a paged KV pool its pages go back to the pool."""
+        pool = getattr(self.model, "kv_pool", None)
+        if pool is not None and req.cache is not None:
+            pool.release(req.cache)
+            pool.release_owner(req.rid)
+        req.cache = None
 
     def _final(self, req):
         n = int(req.ids.numel())
@@ -264,7 +288,7 @@ class Scheduler:
         if req.filled:
             timings["ridgefill"] = dict(n_filled=req.filled, split=arm.split, tail=arm.tail, fill=arm.fill,
                                         n_cached_exact_prefix=0)
-        req.cache = None
+        self._release(req)
         with self._lock:
             self.stats["completed"] += 1
         self._emit(req, {"tokens": [], "content": "", "stop": True, "stop_type": stop_type,
