@@ -243,10 +243,11 @@ def main():
     ap.add_argument("--tp-comm", default="nvls", choices=("nccl", "fused", "nvls"),
                     help="tensor-parallel collectives: nvls (fused GEMM + NVSwitch multicast kernels; falls back to "
                          "nccl where the GPUs offer no multicast), nccl (baseline), fused (peer stores)")
-    ap.add_argument("--tp-fill", default="columns", choices=("columns", "rows"),
-                    help="tensor-parallel map fill: columns (each rank a column slice of every map, then a gather; "
-                         "the default) or rows (each rank a block of prefix rows through the whole map, then an "
-                         "all-to-all of the heads' projections: parallel/rowfill.py)")
+    ap.add_argument("--tp-fill", default="auto", choices=("auto", "columns", "rows"),
+                    help="tensor-parallel map fill: columns (each rank a column slice of every map, then the fused "
+                         "NVLS gather), rows (each rank a block of prefix rows through the whole map, then an "
+                         "all-to-all of the heads' projections: parallel/rowfill.py), or auto: rows from 8 ranks on "
+                         "(measured 144.4 vs 150.1 ms at TP 8, 16K), columns below (349.1 vs 366.0 ms at TP 2)")
     args = ap.parse_args()
     dsplit, dtail = DEFAULT_SPLIT_TAIL.get(args.model, (32, 4096))
     args.split = dsplit if args.split is None else args.split
@@ -276,6 +277,8 @@ def main():
     cfg, model, arm = build_engine(args, device)
     tp_mode = world > 1 and args.parallel == "tp"
     tp = None
+    if tp_mode and args.tp_fill == "auto":
+        args.tp_fill = "rows" if world >= 8 else "columns"
     if tp_mode:
         from ridgefill_data_b200.parallel.tp import TensorParallel, shard
         try:
