@@ -99,6 +99,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     rf::attn_poly = (n == 2 || n == 4) ? (int)n : 0;
     return was;
   });
+  m.def("set_attn_softmax_groups", [](int64_t n) {
+    const int was = rf::attn_softmax_groups;
+    rf::attn_softmax_groups = n == 2 ? 2 : 1;
+    return was;
+  });
+  m.def("set_attn_rotate", [](int64_t n) {
+    const int was = rf::attn_rotate;
+    rf::attn_rotate = n ? 1 : 0;
+    return was;
+  });
+  m.def("set_attn_s_buffers", [](int64_t n) {
+    const int was = rf::attn_s_buffers;
+    rf::attn_s_buffers = (n == 2 || n == 3) ? (int)n : 0;
+    return was;
+  });
   m.def("set_attn_p_buffers", [](int64_t n) {
     const int was = rf::attn_p_buffers;
     rf::attn_p_buffers = n == 1 ? 1 : 2;

@@ -68,6 +68,12 @@ def ext():
     _mod = Checked(mod) if os.environ.get("RF_CHECK_EACH") == "1" else mod
     if os.environ.get("RF_GEMM_2SM") == "0":     # A/B switch: every product on the one-SM GEMM kernel
         mod.set_gemm_2sm(False)
+    if os.environ.get("RF_ATTN_SWG") == "2":     # A/B switch: two softmax warpgroups in the tcgen05 attention
+        mod.set_attn_softmax_groups(2)
+    if os.environ.get("RF_ATTN_ROT") == "1":     # A/B switch: per-CTA rotation of the key-tile order
+        mod.set_attn_rotate(1)
+    if os.environ.get("RF_ATTN_SBUF") in ("2", "3"):   # A/B switch: TMEM S buffers (default per head dim)
+        mod.set_attn_s_buffers(int(os.environ["RF_ATTN_SBUF"]))
     if os.environ.get("RF_ATTN_PBUF") == "1":    # A/B switch: one P buffer in the tcgen05 attention
         mod.set_attn_p_buffers(1)
     if os.environ.get("RF_ATTN_POLY") in ("2", "4"):   # A/B switch: softmax exponentials partly on the FMA pipe

@@ -173,6 +173,36 @@ def test_gdn_two_level_scan_matches_sequential_and_oracle(groups, need_out):
         assert _rel(outs[groups].view(n, nv, dv).transpose(0, 1), ro) < 3e-2
 
 
+@pytest.mark.parametrize("variant", [("set_attn_softmax_groups", 2), ("set_attn_s_buffers", 2),
+                                     ("set_attn_s_buffers", 3), ("set_attn_p_buffers", 1), ("set_attn_rotate", 1)])
+@pytest.mark.parametrize("hd", [128, 256])
+def test_flash_attention_pipeline_variants(variant, hd):
+    """The tcgen05 attention's pipeline variants (two softmax warpgroups swapping the row max per tile, two or
+    three TMEM S buffers, one P buffer, key tiles in a per-CTA rotated order) against the fp32 oracle and the default build, causal over 300 rows with
+    keys past the last query tile."""
+    from ridgefill_data_b200.ops._ext import check_errors, ext
+    setter, value = variant
+    torch.manual_seed(13)
+    hq, hkv, nq = 4, 2, 300
+    q = torch.randn(hq, nq, hd, device=dev).bfloat16()
+    k = torch.randn(hkv, nq, hd, device=dev).bfloat16()
+    v = torch.randn(hkv, nq, hd, device=dev).bfloat16()
+    ref = O.attend(q, k, v, hd ** -0.5)
+    outs = {}
+    for mode in ("default", "variant"):
+        was = getattr(ext(), setter)(value) if mode == "variant" else None
+        try:
+            out = torch.empty(nq, hq * hd, device=dev, dtype=torch.bfloat16)
+            K.attention(q, k, v, nq, hd ** -0.5, out, impl="tcgen05")
+            outs[mode] = out
+        finally:
+            if was is not None:
+                getattr(ext(), setter)(was)
+    check_errors(dev)
+    assert _rel(outs["variant"], ref) < 2e-2
+    assert _rel(outs["variant"], outs["default"]) < 5e-3
+
+
 @pytest.mark.parametrize("poly", [2, 4])
 @pytest.mark.parametrize("hd", [128, 256])
 def test_flash_attention_with_fma_exponentials(poly, hd):
