@@ -219,14 +219,18 @@ void gdn_chunk_scan(OptT q, Tensor k, Tensor v, Tensor beta, Tensor g, Tensor st
   if (q.has_value()) {
     need(*q, at::kBFloat16, "q");
     a.q = cbf(*q);
-    TORCH_CHECK(out.has_value() && s_buf.has_value() && vt_buf.has_value(),
-                "gdn_chunk_scan: output mode needs out, s_buf and vt_buf");
-    need(*s_buf, at::kBFloat16, "s_buf");
-    need(*vt_buf, at::kBFloat16, "vt_buf");
-    TORCH_CHECK(s_buf->numel() >= nv * (n_pad / 64) * dk * dv, "gdn_chunk_scan: s_buf size");
-    TORCH_CHECK(vt_buf->numel() >= nv * n_pad * dv, "gdn_chunk_scan: vt_buf size");
-    a.s_buf = bf(*s_buf);
-    a.vt_buf = bf(*vt_buf);
+    TORCH_CHECK(out.has_value(), "gdn_chunk_scan: output mode needs out");
+    // s_buf / vt_buf: only the split output path (gdn_fused_output = 0) reads them
+    TORCH_CHECK(rf::gdn_fused_output || (s_buf.has_value() && vt_buf.has_value()),
+                "gdn_chunk_scan: the split output path needs s_buf and vt_buf");
+    if (s_buf.has_value() && vt_buf.has_value()) {
+      need(*s_buf, at::kBFloat16, "s_buf");
+      need(*vt_buf, at::kBFloat16, "vt_buf");
+      TORCH_CHECK(s_buf->numel() >= nv * (n_pad / 64) * dk * dv, "gdn_chunk_scan: s_buf size");
+      TORCH_CHECK(vt_buf->numel() >= nv * n_pad * dv, "gdn_chunk_scan: vt_buf size");
+      a.s_buf = bf(*s_buf);
+      a.vt_buf = bf(*vt_buf);
+    }
   }
   a.k = cbf(k);
   a.v = cbf(v);

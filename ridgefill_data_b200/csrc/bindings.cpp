@@ -99,6 +99,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     rf::attn_poly = (n == 2 || n == 4) ? (int)n : 0;
     return was;
   });
+  m.def("set_gdn_fused_output", [](int64_t n) {
+    const int was = rf::gdn_fused_output;
+    rf::gdn_fused_output = n ? 1 : 0;
+    return was;
+  });
+  m.def("gdn_fused_output", []() { return rf::gdn_fused_output; });
   m.def("set_attn_softmax_groups", [](int64_t n) {
     const int was = rf::attn_softmax_groups;
     rf::attn_softmax_groups = n == 2 ? 2 : 1;

@@ -10,8 +10,10 @@
 //   scan kernel      (parallel over value head x 64-column slice of the state, sequential over chunks)
 //                    V' = U - W S;  O = (q e^gamma) S + (q k^T * decay) V'  (output mode);
 //                    S <- e^(gamma_C) S + (k e^(gamma_C - gamma))^T V'.
-//                    The fp32 state lives in mma accumulators for the whole sequence; its bf16 copy in shared
-//                    memory feeds the products. Fill mode (q == nullptr) skips the output.
+//                    The fp32 state lives in mma accumulators for the whole sequence. Output mode computes O
+//                    in the same pass (gdn_state_out_kernel); the older split form (the state pass stores the
+//                    chunk-start states and V', a parallel pass reads them back) stays behind
+//                    gdn_fused_output = 0. Fill mode (q == nullptr) skips the output.
 // Matches the reference's chunk arithmetic (code/kva/ops.py:199-262) with bf16 tensor-core products and
 // fp32 accumulation/state.
 #include "kernels.h"
@@ -842,6 +844,278 @@ __global__ void __launch_bounds__(128, 1) gdn_group_prop_kernel(GdnScanArgs a, i
   }
 }
 
+// -------------------------------------------------------------------------- fused state + output pass
+// Output mode without the chunk-state round trip: the sequential state pass itself produces every chunk's output
+// rows for its 64 value dims, so the chunk-start states (bf16 [dv][dk] per chunk) and V' never go to memory and
+// the separate output pass disappears. Per chunk, warp w (value dims m0 + 16w .. + 16):
+//   P      = rows 16w.. of the chunk's (q k^T) * e^(gam_r - gam_c) (r >= c), bf16 -> shared memory (all warps)
+//   O^T    = S^T q^T, column r scaled by e^(gam_r)               (A = S^T from the accumulators, B = q rows)
+//   V'^T   = U^T - S^T W^T                                        (as in the state pass)
+//   O^T   += V'^T P^T                                             (A = V'^T from the accumulators, B = P rows)
+//   S^T   <- e^(gl) S^T + (V'^T diag(e^(gl - gam))) k             (as in the state pass)
+// O^T is staged transposed in shared memory and stored as whole 128-byte row segments. The recurrence's chain is
+// unchanged; the output products are independent of it and fill its latency.
+// MODE 0: sequential over every chunk from a.state (updated in place); MODE 2: one chunk group of the two-level
+// scan from start_buf (its end state is known from pass 2).
+constexpr int PQ = GC + 8;        // pitch of the P tile and of the output staging tile
+
+struct StateOutSmem {
+  __nv_bfloat16 w[SST][GC * PK];
+  __nv_bfloat16 k[SST][GC * PK];
+  __nv_bfloat16 q[SST][GC * PK];
+  __nv_bfloat16 ut[SST][SVS * PU];
+  float g[SST][GC];
+  __nv_bfloat16 p[GC * PQ];       // masked, decayed q k^T of the chunk
+  __nv_bfloat16 o[GC * PQ];       // output rows x this CTA's 64 value dims
+};
+
+__device__ __forceinline__ void state_out_issue_loads(StateOutSmem& s, const GdnScanArgs& a, int stage, int chunk,
+                                                      int h, int kh, int m0, int n_pad, int tid) {
+  const int r0 = chunk * GC;
+  const int rows = min(GC, a.n - r0);
+  const __nv_bfloat16* wp = a.w_buf + ((long)h * n_pad + r0) * DK;
+  const __nv_bfloat16* up = a.u_buf + ((long)h * n_pad + r0) * a.dv + (long)m0 * GC;
+  const __nv_bfloat16* kp = a.k + ((long)kh * a.n + r0) * DK;
+  const __nv_bfloat16* qp = a.q + ((long)kh * a.n + r0) * DK;
+  for (int v = tid; v < GC * (DK / 8); v += 128) {
+    const int r = v / (DK / 8), c = (v % (DK / 8)) * 8;
+    cp_async16(&s.w[stage][r * PK + c], wp + (long)r * DK + c, true);   // padded rows hold zeros
+    const bool ok = r < rows;
+    cp_async16(&s.k[stage][r * PK + c], ok ? kp + (long)r * DK + c : kp, ok);
+    cp_async16(&s.q[stage][r * PK + c], ok ? qp + (long)r * DK + c : qp, ok);
+  }
+  for (int v = tid; v < SVS * (GC / 8); v += 128) {
+    const int r = v / (GC / 8), c = (v % (GC / 8)) * 8;
+    cp_async16(&s.ut[stage][r * PU + c], up + (long)r * GC + c, true);
+  }
+  if (tid < GC) {
+    const float* gp = a.g + (long)h * a.n + r0;
+    cp_async4(&s.g[stage][tid], tid < rows ? gp + tid : gp, tid < rows);
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(128, 1) gdn_state_out_kernel(GdnScanArgs a, int n_pad) {
+  static_assert(MODE == 0 || MODE == 2, "sequential scan or the two-level scan's output pass");
+  extern __shared__ __align__(16) uint8_t so_raw[];
+  StateOutSmem& s = *reinterpret_cast<StateOutSmem*>(so_raw);
+  const int h = blockIdx.x;
+  const int m0 = (int)blockIdx.y * SVS;
+  const int kh = h / (a.nv / a.nk);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int mrow = warp * 16;
+  const int n_chunks_all = (a.n + GC - 1) / GC;
+  const int per_group = MODE == 0 ? n_chunks_all : (n_chunks_all + a.groups - 1) / a.groups;
+  const int c_begin = MODE == 0 ? 0 : (int)blockIdx.z * per_group;
+  const int c_end = MODE == 0 ? n_chunks_all : min(n_chunks_all, c_begin + per_group);
+  float* state = a.state + (long)h * DK * a.dv;
+  const long grp_idx = ((long)h * a.groups + blockIdx.z) * ((long)a.dv * DK);
+
+  float S[16][4];
+#pragma unroll
+  for (int nt = 0; nt < 16; ++nt) {
+    const int m = m0 + mrow + g;
+    const int c = nt * 8 + 2 * t;
+    if constexpr (MODE == 0) {
+      S[nt][0] = state[(long)c * a.dv + m];
+      S[nt][1] = state[(long)(c + 1) * a.dv + m];
+      S[nt][2] = state[(long)c * a.dv + m + 8];
+      S[nt][3] = state[(long)(c + 1) * a.dv + m + 8];
+    } else {
+      const float* sp = a.start_buf + grp_idx;
+      S[nt][0] = sp[(long)m * DK + c];
+      S[nt][1] = sp[(long)m * DK + c + 1];
+      S[nt][2] = sp[(long)(m + 8) * DK + c];
+      S[nt][3] = sp[(long)(m + 8) * DK + c + 1];
+    }
+  }
+  for (int p = 0; p < SST - 1; ++p) {
+    if (c_begin + p < c_end) state_out_issue_loads(s, a, p, c_begin + p, h, kh, m0, n_pad, tid);
+    cp_async_commit();
+  }
+  for (int ch = c_begin; ch < c_end; ++ch) {
+    const int stage = (ch - c_begin) % SST;
+    const int r0 = ch * GC;
+    const int rows = min(GC, a.n - r0);
+    if (ch + SST - 1 < c_end)
+      state_out_issue_loads(s, a, (ch - c_begin + SST - 1) % SST, ch + SST - 1, h, kh, m0, n_pad, tid);
+    cp_async_commit();
+    cp_async_wait<SST - 1>();
+    __syncthreads();
+    // gates: every warp scans the chunk's log decays (lane l holds gam[2l] = ge, gam[2l + 1] = go)
+    const float x0 = s.g[stage][2 * lane], x1 = s.g[stage][2 * lane + 1];
+    const float pair = x0 + x1;
+    float incl = pair;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const float ge = incl - x1, go = incl;
+    const float gl = __shfl_sync(0xffffffffu, incl, 31);
+    const float f_even = __expf(gl - ge), f_odd = __expf(gl - go);
+    const float e_even = __expf(ge), e_odd = __expf(go);
+    // P rows mrow.. (all 64 columns): q k^T over dk, causal mask and decay, bf16 into s.p
+    {
+      float pa[8][4];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pa[j][0] = pa[j][1] = pa[j][2] = pa[j][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < DK / 16; ++ks) {
+        uint32_t af[4];
+        lda_row(af, s.q[stage], PK, mrow, ks * 16, lane);
+#pragma unroll
+        for (int j2 = 0; j2 < 4; ++j2) {
+          uint32_t bf[4];
+          ldb_nk(bf, s.k[stage], PK, j2 * 16, ks * 16, lane);
+          mma_bf16(pa[2 * j2], af, bf[0], bf[1]);
+          mma_bf16(pa[2 * j2 + 1], af, bf[2], bf[3]);
+        }
+      }
+      const int ra = mrow + g, rb = ra + 8;
+      const float gae = __shfl_sync(0xffffffffu, ge, ra >> 1), gao = __shfl_sync(0xffffffffu, go, ra >> 1);
+      const float gbe = __shfl_sync(0xffffffffu, ge, rb >> 1), gbo = __shfl_sync(0xffffffffu, go, rb >> 1);
+      const float gra = (ra & 1) ? gao : gae, grb = (rb & 1) ? gbo : gbe;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = (e >= 2) ? rb : ra;
+          const int c = j * 8 + 2 * t + (e & 1);
+          const float gc = __shfl_sync(0xffffffffu, (e & 1) ? go : ge, c >> 1);
+          pa[j][e] = (r >= c) ? pa[j][e] * __expf(((e >= 2) ? grb : gra) - gc) : 0.f;
+        }
+        *reinterpret_cast<uint32_t*>(&s.p[ra * PQ + j * 8 + 2 * t]) = pack2(pa[j][0], pa[j][1]);
+        *reinterpret_cast<uint32_t*>(&s.p[rb * PQ + j * 8 + 2 * t]) = pack2(pa[j][2], pa[j][3]);
+      }
+    }
+    // S^T as bf16 A fragments (k = dk in steps of 16: n-tiles 2ks, 2ks + 1)
+    uint32_t sa[8][4];
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      sa[ks][0] = pack2(S[2 * ks][0], S[2 * ks][1]);
+      sa[ks][1] = pack2(S[2 * ks][2], S[2 * ks][3]);
+      sa[ks][2] = pack2(S[2 * ks + 1][0], S[2 * ks + 1][1]);
+      sa[ks][3] = pack2(S[2 * ks + 1][2], S[2 * ks + 1][3]);
+    }
+    // O^T = S^T q^T [16 x 64 chunk rows], then column r times e^(gam_r)
+    float o[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+      for (int j2 = 0; j2 < 4; ++j2) {
+        uint32_t bf[4];
+        ldb_nk(bf, s.q[stage], PK, j2 * 16, ks * 16, lane);   // B[k = dk][n = row] = q[row][dk]
+        mma_bf16(o[2 * j2], sa[ks], bf[0], bf[1]);
+        mma_bf16(o[2 * j2 + 1], sa[ks], bf[2], bf[3]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = j * 8 + 2 * t;                      // chunk rows c, c + 1 (= lane (c >> 1)'s pair)
+      const float s0 = __shfl_sync(0xffffffffu, e_even, c >> 1);
+      const float s1 = __shfl_sync(0xffffffffu, e_odd, c >> 1);
+      o[j][0] *= s0;
+      o[j][1] *= s1;
+      o[j][2] *= s0;
+      o[j][3] *= s1;
+    }
+    // V'^T = U^T - S^T W^T: [16 x 64], n-tiles over chunk rows
+    float vt[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) vt[j][0] = vt[j][1] = vt[j][2] = vt[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+      for (int j2 = 0; j2 < 4; ++j2) {
+        uint32_t bf[4];
+        ldb_nk(bf, s.w[stage], PK, j2 * 16, ks * 16, lane);   // B[k = dk][n = row] = W[row][dk]
+        mma_bf16(vt[2 * j2], sa[ks], bf[0], bf[1]);
+        mma_bf16(vt[2 * j2 + 1], sa[ks], bf[2], bf[3]);
+      }
+    }
+    const __nv_bfloat16* ut = s.ut[stage];
+    uint32_t va[4][4], vu[4][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = j * 8 + 2 * t;
+      const float2 u0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ut[(mrow + g) * PU + c]));
+      const float2 u1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ut[(mrow + g + 8) * PU + c]));
+      const float v0 = u0.x - vt[j][0], v1 = u0.y - vt[j][1], v2 = u1.x - vt[j][2], v3 = u1.y - vt[j][3];
+      vu[j >> 1][(j & 1) ? 2 : 0] = pack2(v0, v1);
+      vu[j >> 1][(j & 1) ? 3 : 1] = pack2(v2, v3);
+      const float fc0 = __shfl_sync(0xffffffffu, f_even, c >> 1);
+      const float fc1 = __shfl_sync(0xffffffffu, f_odd, c >> 1);
+      va[j >> 1][(j & 1) ? 2 : 0] = pack2(v0 * fc0, v1 * fc1);
+      va[j >> 1][(j & 1) ? 3 : 1] = pack2(v2 * fc0, v3 * fc1);
+    }
+    __syncthreads();   // every warp's P rows are in s.p
+    // O^T += V'^T P^T (B[k = row'][n = row] = P[row][row'])
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+      for (int j2 = 0; j2 < 4; ++j2) {
+        uint32_t bf[4];
+        ldb_nk(bf, s.p, PQ, j2 * 16, kk * 16, lane);
+        mma_bf16(o[2 * j2], vu[kk], bf[0], bf[1]);
+        mma_bf16(o[2 * j2 + 1], vu[kk], bf[2], bf[3]);
+      }
+    }
+    // O^T -> s.o[row][value dim]
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = j * 8 + 2 * t;
+      const int m = mrow + g;
+      s.o[c * PQ + m] = __float2bfloat16(o[j][0]);
+      s.o[(c + 1) * PQ + m] = __float2bfloat16(o[j][1]);
+      s.o[c * PQ + m + 8] = __float2bfloat16(o[j][2]);
+      s.o[(c + 1) * PQ + m + 8] = __float2bfloat16(o[j][3]);
+    }
+    // S^T <- e^gl S^T + Vs^T k
+    const float cd = __expf(gl);
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      S[nt][0] *= cd;
+      S[nt][1] *= cd;
+      S[nt][2] *= cd;
+      S[nt][3] *= cd;
+    }
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+      for (int j2 = 0; j2 < 8; ++j2) {
+        uint32_t bf[4];
+        ldb_kn(bf, s.k[stage], PK, j2 * 16, ks * 16, lane);   // B[k = row][n = dk] = k[row][dk]
+        mma_bf16(S[2 * j2], va[ks], bf[0], bf[1]);
+        mma_bf16(S[2 * j2 + 1], va[ks], bf[2], bf[3]);
+      }
+    }
+    __syncthreads();   // s.o is complete; this stage and s.p are free again
+    // output rows of the chunk, this CTA's 64 value dims: 8 x 16-byte segments per row
+    for (int v = tid; v < GC * (SVS / 8); v += 128) {
+      const int r = v / (SVS / 8), c = (v % (SVS / 8)) * 8;
+      if (r < rows)
+        *reinterpret_cast<uint4*>(a.out + (long)(r0 + r) * a.out_row + (long)h * a.dv + m0 + c) =
+            *reinterpret_cast<const uint4*>(&s.o[r * PQ + c]);
+    }
+  }
+  cp_async_wait<0>();
+  if constexpr (MODE == 0) {
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) {
+      const int m = m0 + mrow + g;
+      const int c = nt * 8 + 2 * t;
+      state[(long)c * a.dv + m] = S[nt][0];
+      state[(long)(c + 1) * a.dv + m] = S[nt][1];
+      state[(long)c * a.dv + m + 8] = S[nt][2];
+      state[(long)(c + 1) * a.dv + m + 8] = S[nt][3];
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------- output pass
 // Parallel over (chunk, value head): O = (q e^gam) S_c + (q k^T * decay) V' for the chunk's rows, with
 // S_c^T [dv][dk] and V'^T [dv][64] from the state pass read as [N][K] B operands.
@@ -983,9 +1257,15 @@ __global__ void __launch_bounds__(128) gdn_output_kernel(GdnScanArgs a, int n_pa
   }
 }
 
+int gdn_fused_output = 1;
+
 void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream) {
   if (a.n <= 0) return;
-  if (a.dk != DK || a.dv % SVS != 0 || a.dv > 128 || a.nv % a.nk != 0 || (a.q != nullptr && (a.s_buf == nullptr || a.vt_buf == nullptr))) {
+  // output mode on the fused state + output pass unless switched off or the output rows are not 16-byte aligned
+  const bool fused = a.q != nullptr && gdn_fused_output && a.out != nullptr &&
+                     reinterpret_cast<uintptr_t>(a.out) % 16 == 0 && a.out_row % 8 == 0;
+  if (a.dk != DK || a.dv % SVS != 0 || a.dv > 128 || a.nv % a.nk != 0 ||
+      (a.q != nullptr && !fused && (a.s_buf == nullptr || a.vt_buf == nullptr))) {
     record_error_async(a.err, kErrBadShape, stream);
     return;
   }
@@ -999,14 +1279,21 @@ void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream) {
     cudaFuncSetAttribute(gdn_state_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(StateSmem));
     cudaFuncSetAttribute(gdn_group_prop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PropSmem));
     cudaFuncSetAttribute(gdn_output_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(OutSmem));
+    cudaFuncSetAttribute(gdn_state_out_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sizeof(StateOutSmem));
+    cudaFuncSetAttribute(gdn_state_out_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sizeof(StateOutSmem));
   });
   gdn_wy_kernel<<<dim3(n_chunks, a.nv), 128, sizeof(WySmem), stream>>>(a, n_pad);
   count_launch();
   const bool two_level = a.groups > 1 && a.dv == DK && a.grp_buf != nullptr &&
                          (a.q == nullptr || a.start_buf != nullptr) && n_chunks >= 2 * a.groups;
   if (!two_level) {
-    gdn_state_kernel<0><<<dim3(a.nv, a.dv / SVS), 128, sizeof(StateSmem), stream>>>(a, n_pad, a.q ? a.s_buf : nullptr,
-                                                                                  a.q ? a.vt_buf : nullptr);
+    if (fused)
+      gdn_state_out_kernel<0><<<dim3(a.nv, a.dv / SVS), 128, sizeof(StateOutSmem), stream>>>(a, n_pad);
+    else
+      gdn_state_kernel<0><<<dim3(a.nv, a.dv / SVS), 128, sizeof(StateSmem), stream>>>(a, n_pad, a.q ? a.s_buf : nullptr,
+                                                                                    a.q ? a.vt_buf : nullptr);
     count_launch();
   } else {
     gdn_state_kernel<1><<<dim3(a.nv, 2 * a.dv / SVS, a.groups), 128, sizeof(StateSmem), stream>>>(a, n_pad, nullptr,
@@ -1014,12 +1301,15 @@ void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream) {
     gdn_group_prop_kernel<<<dim3(a.nv, a.dv / SVS), 128, sizeof(PropSmem), stream>>>(a, a.q != nullptr ? 1 : 0);
     count_launch(2);
     if (a.q != nullptr) {
-      gdn_state_kernel<2><<<dim3(a.nv, a.dv / SVS, a.groups), 128, sizeof(StateSmem), stream>>>(a, n_pad, a.s_buf,
-                                                                                              a.vt_buf);
+      if (fused)
+        gdn_state_out_kernel<2><<<dim3(a.nv, a.dv / SVS, a.groups), 128, sizeof(StateOutSmem), stream>>>(a, n_pad);
+      else
+        gdn_state_kernel<2><<<dim3(a.nv, a.dv / SVS, a.groups), 128, sizeof(StateSmem), stream>>>(a, n_pad, a.s_buf,
+                                                                                                a.vt_buf);
       count_launch();
     }
   }
-  if (a.q != nullptr) {
+  if (a.q != nullptr && !fused) {
     gdn_output_kernel<<<dim3(n_chunks, a.nv), 128, sizeof(OutSmem), stream>>>(a, n_pad, a.s_buf, a.vt_buf);
     count_launch();
   }

@@ -146,6 +146,7 @@ struct GdnScanArgs {
   float* start_buf;         // scratch [nv][groups][dv][dk]: group-start S^T (output mode)
 };
 void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream);
+extern int gdn_fused_output;   // 1 (default): output mode in the state pass; 0: state pass + separate output pass
 
 // ---- moe.cu
 void router_topk(const float* logits, long ld, int n, int E, int k, int* idx, float* wts, int norm,

@@ -119,8 +119,10 @@ def gdn_scan(q, k, v, beta, g, state, out=None, groups=None):
     n_pad = (n + 63) // 64 * 64
     w_buf = torch.empty(nv, n_pad, dk, dtype=BF16, device=k.device)
     u_buf = torch.empty(nv, n_pad, dv, dtype=BF16, device=k.device)
-    s_buf = torch.empty(nv, n_pad // 64, dv, dk, dtype=BF16, device=k.device) if q is not None else None
-    vt_buf = torch.empty(nv, n_pad, dv, dtype=BF16, device=k.device) if q is not None else None
+    # chunk-start states and V' in memory only for the split output path (the fused state pass writes O itself)
+    split = q is not None and (not ext().gdn_fused_output() or out.data_ptr() % 16 != 0 or out.stride(0) % 8 != 0)
+    s_buf = torch.empty(nv, n_pad // 64, dv, dk, dtype=BF16, device=k.device) if split else None
+    vt_buf = torch.empty(nv, n_pad, dv, dtype=BF16, device=k.device) if split else None
     if groups is None:
         groups = scan_groups(nv, dv, n) if dv == dk else 1
     grp_buf = start_buf = None
