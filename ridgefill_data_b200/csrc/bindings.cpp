@@ -105,6 +105,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return was;
   });
   m.def("gdn_fused_output", []() { return rf::gdn_fused_output; });
+  // phase trace of the tcgen05 GDN state pass: an int64 CUDA tensor of >= 128 * 16 stamps, or None
+  m.def("set_gdn_tc_trace", [](c10::optional<at::Tensor> t) {
+    rf::gdn_tc_trace = t.has_value() ? reinterpret_cast<unsigned long long*>(t->data_ptr<int64_t>()) : nullptr;
+  });
+  m.def("set_gdn_state_tc", [](int64_t n) {
+    const int was = rf::gdn_state_tc;
+    rf::gdn_state_tc = n ? 1 : 0;
+    return was;
+  });
   m.def("set_attn_softmax_groups", [](int64_t n) {
     const int was = rf::attn_softmax_groups;
     rf::attn_softmax_groups = n == 2 ? 2 : 1;

@@ -1289,9 +1289,10 @@ void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream) {
   const bool two_level = a.groups > 1 && a.dv == DK && a.grp_buf != nullptr &&
                          (a.q == nullptr || a.start_buf != nullptr) && n_chunks >= 2 * a.groups;
   if (!two_level) {
-    if (fused)
-      gdn_state_out_kernel<0><<<dim3(a.nv, a.dv / SVS), 128, sizeof(StateOutSmem), stream>>>(a, n_pad);
-    else
+    if (fused) {
+      if (!gdn_state_out_tc(a, n_pad, 0, stream))
+        gdn_state_out_kernel<0><<<dim3(a.nv, a.dv / SVS), 128, sizeof(StateOutSmem), stream>>>(a, n_pad);
+    } else
       gdn_state_kernel<0><<<dim3(a.nv, a.dv / SVS), 128, sizeof(StateSmem), stream>>>(a, n_pad, a.q ? a.s_buf : nullptr,
                                                                                     a.q ? a.vt_buf : nullptr);
     count_launch();
@@ -1301,9 +1302,10 @@ void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream) {
     gdn_group_prop_kernel<<<dim3(a.nv, a.dv / SVS), 128, sizeof(PropSmem), stream>>>(a, a.q != nullptr ? 1 : 0);
     count_launch(2);
     if (a.q != nullptr) {
-      if (fused)
-        gdn_state_out_kernel<2><<<dim3(a.nv, a.dv / SVS, a.groups), 128, sizeof(StateOutSmem), stream>>>(a, n_pad);
-      else
+      if (fused) {
+        if (!gdn_state_out_tc(a, n_pad, 2, stream))
+          gdn_state_out_kernel<2><<<dim3(a.nv, a.dv / SVS, a.groups), 128, sizeof(StateOutSmem), stream>>>(a, n_pad);
+      } else
         gdn_state_kernel<2><<<dim3(a.nv, a.dv / SVS, a.groups), 128, sizeof(StateSmem), stream>>>(a, n_pad, a.s_buf,
                                                                                                 a.vt_buf);
       count_launch();

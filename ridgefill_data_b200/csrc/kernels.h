@@ -147,6 +147,12 @@ struct GdnScanArgs {
 };
 void gdn_chunk_scan(const GdnScanArgs& a, cudaStream_t stream);
 extern int gdn_fused_output;   // 1 (default): output mode in the state pass; 0: state pass + separate output pass
+// gdn_tc.cu: the output-mode state pass (sequential, mode 0, or the two-level scan's pass 3, mode 2) on tcgen05 with
+// the state in TMEM; false when the shapes do not fit it (dk = dv = 128) or it is switched off (gdn_state_tc = 0,
+// the default: measured slower than the mma.sync pass)
+bool gdn_state_out_tc(const GdnScanArgs& a, int n_pad, int mode, cudaStream_t stream);
+extern int gdn_state_tc;
+extern unsigned long long* gdn_tc_trace;   // [chunks][16] ns phase stamps of the first CTA, or nullptr
 
 // ---- moe.cu
 void router_topk(const float* logits, long ld, int n, int E, int k, int* idx, float* wts, int norm,

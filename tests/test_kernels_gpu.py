@@ -136,9 +136,9 @@ def test_gdn_prep_and_scan(n, need_out, with_state):
 
 @pytest.mark.parametrize("n,dv,groups", [(1000, 128, 1), (1000, 128, 4), (333, 64, 1), (64, 128, 1)])
 def test_gdn_fused_output_pass_matches_split_and_oracle(n, dv, groups):
-    """Output mode computed inside the state pass (no chunk-start states in memory) against the split form (state
-    pass storing chunk states and V', then the parallel output pass) and the fp32 oracle: sequential and two-level
-    scans, a partial last chunk and dv 64. Also checks that the fused launches allocate no chunk-state scratch."""
+    """Output mode computed inside the state pass (no chunk-start states in memory), on tcgen05 with the state in
+    TMEM and on mma.sync, against the split form (state pass storing chunk states and V', then the parallel output
+    pass) and the fp32 oracle: sequential and two-level scans, a partial last chunk and dv 64 (mma.sync only)."""
     from ridgefill_data_b200.ops._ext import check_errors, ext
     torch.manual_seed(17)
     nk, nv, dk = 1, 3, 128
@@ -150,19 +150,24 @@ def test_gdn_fused_output_pass_matches_split_and_oracle(n, dv, groups):
     state = torch.randn(nv, dk, dv, device=dev) * 0.1
     q, k, v, beta, g = K.gdn_prep(proj, C, C + nv, conv_w, None, A_log, dt, nk, nv, dk, dv)
     outs, states = {}, {}
-    for fused in (1, 0):
-        was = ext().set_gdn_fused_output(fused)
+    # 2: fused on tcgen05 (state in TMEM, where dk = dv = 128), 1: fused on mma.sync, 0: split passes
+    for mode in (2, 1, 0):
+        was_f = ext().set_gdn_fused_output(1 if mode else 0)
+        was_t = ext().set_gdn_state_tc(1 if mode == 2 else 0)
         try:
             out = torch.empty(n, nv * dv, device=dev, dtype=torch.bfloat16)
             st = state.clone()
             K.gdn_scan(q, k, v, beta, g, st, out, groups=groups)
-            outs[fused], states[fused] = out, st
+            outs[mode], states[mode] = out, st
         finally:
-            ext().set_gdn_fused_output(was)
-    torch.cuda.synchronize()
-    check_errors()
+            ext().set_gdn_fused_output(was_f)
+            ext().set_gdn_state_tc(was_t)
+        torch.cuda.synchronize()
+        check_errors()
     assert _rel(states[1], states[0]) < 1e-4    # same recurrence, fp32 contraction order may differ
     assert _rel(outs[1].float(), outs[0].float()) < 1e-2
+    assert _rel(states[2], states[0]) < 1e-2    # tcgen05: bf16 state operand rounded at other points
+    assert _rel(outs[2].float(), outs[0].float()) < 1e-2
     co, _ = O.causal_conv(proj[:, :C], None, conv_w)
     qo, ko, vo = co.split([nk * dk, nk * dk, nv * dv], -1)
     qo = O.l2norm(qo.reshape(n, nk, dk).float()).transpose(0, 1) * dk ** -0.5
@@ -171,8 +176,9 @@ def test_gdn_fused_output_pass_matches_split_and_oracle(n, dv, groups):
     bo = torch.sigmoid(proj[:, C:C + nv]).float().T
     go = (-A_log.exp() * F.softplus(proj[:, C + nv:].float() + dt)).T
     ro, rs, _ = O.delta_rule(qo.repeat_interleave(nv, 0), ko.repeat_interleave(nv, 0), vo, go, bo, state)
-    assert _rel(outs[1].view(n, nv, dv).transpose(0, 1), ro) < 3e-2
-    assert _rel(states[1], rs) < 3e-2
+    for mode in (2, 1):
+        assert _rel(outs[mode].view(n, nv, dv).transpose(0, 1), ro) < 3e-2
+        assert _rel(states[mode], rs) < 3e-2
 
 
 @pytest.mark.parametrize("groups", [3, 8])
