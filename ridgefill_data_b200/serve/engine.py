@@ -303,6 +303,14 @@ class Scheduler:
             name = f"ridgefill_{k}" + ("_total" if k not in ("waiting", "active") else "")
             kind = "gauge" if k in ("waiting", "active") else "counter"
             lines += [f"# TYPE {name} {kind}", f"{name} {v}"]
+        dev = getattr(self.model, "device", None)
+        if dev is not None and getattr(dev, "type", "") == "cuda":
+            import torch
+            lines += ["# TYPE ridgefill_hbm_peak_gib gauge",
+                      f"ridgefill_hbm_peak_gib {torch.cuda.max_memory_allocated(dev) / 2 ** 30:.3f}"]
+        pool = getattr(self.model, "kv_pool", None)
+        if pool is not None:
+            lines += ["# TYPE ridgefill_kv_pages_free gauge", f"ridgefill_kv_pages_free {pool.free_pages()}"]
         for name, xs in (("ridgefill_ttft_ms", self.ttft_ms), ("ridgefill_prompt_ms", self.prompt_ms)):
             xs = sorted(xs)
             lines.append(f"# TYPE {name} summary")
