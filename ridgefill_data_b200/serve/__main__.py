@@ -82,14 +82,19 @@ def main(argv=None):
                     help="serve every request from one paged K/V pool of this many pages per attention layer "
                          "(0: a contiguous cache per request)")
     ap.add_argument("--page-size", type=int, default=128, help="rows per K/V page (a multiple of 128)")
-    ap.add_argument("--interleave", type=int, default=4, help="decode round every this many prefill layers (0: off)")
+    ap.add_argument("--interleave", type=int, default=4,
+                    help="decode round every this many prefill layers (0: off; the period until --decode-gap-ms has "
+                         "a measured prefill cost to work from)")
+    ap.add_argument("--decode-gap-ms", type=float, default=100.0,
+                    help="target gap between a running stream's tokens while a prompt is prefilled: each prefill's "
+                         "decode-round period follows its size (0: every --interleave layers)")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8080)
     a = ap.parse_args(argv)
     from .app import Server, create_app
     from .engine import Scheduler
     model, arms, tok, eos, props = build(a)
-    sched = Scheduler(model, eos=eos, interleave=a.interleave).start()
+    sched = Scheduler(model, eos=eos, interleave=a.interleave, gap_ms=a.decode_gap_ms).start()
     try:
         Server(create_app(sched, arms, tok, props), a.host, a.port, log_level="info").run()
     finally:

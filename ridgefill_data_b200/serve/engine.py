@@ -5,9 +5,11 @@ keeps every started request in the decode set until it has produced its tokens. 
 active request by one greedy token (an exact full-model step over its own cache); the requests of a round go
 through the model together (`decode_batch`: one pass over the weights, per-sequence attention and recurrent
 state), which is what makes concurrent streams cheap on a weight-bandwidth-bound decode. A long prefill does not stall
-the running streams: the engine's layer loop calls `tick(i)` before every layer, and every `interleave` layers the
-worker runs one decode round for the other requests, so their inter-token gap during a prefill is bounded by
-`interleave` layers of that prefill instead of all of it (the quantity the fixed-arrival mix measures). Under
+the running streams: the engine's layer loop calls `tick(i)` before every layer, and every k layers the worker
+runs one decode round for the other requests, so their inter-token gap during a prefill is bounded by k layers of
+that prefill instead of all of it (the quantity the fixed-arrival mix measures). k is `interleave`, or with
+`gap_ms` it is sized to the prefill: gap_ms / (rows x the per-row, per-layer cost learned from large prefills that
+ran alone), so a short prompt runs uninterrupted and a long one yields about every gap_ms. Under
 tensor parallelism the layer outputs live in rotating collective buffers, so interleaving is off there.
 
 Events are plain dicts handed to the request's `emit` callback from the worker thread, in the field layout of the
@@ -56,10 +58,18 @@ class Request:
 
 
 class Scheduler:
-    def __init__(self, model, eos=(), interleave=4, max_active=64, max_batch=32, sync=None):
+    def __init__(self, model, eos=(), interleave=4, max_active=64, max_batch=32, sync=None, gap_ms=0.0,
+                 sample_rows=4096):
         self.model = model
         self.eos = frozenset(int(e) for e in eos)
         self.interleave = int(interleave)
+        # gap_ms > 0: the decode-round period of a prefill follows its size, so that the running streams wait about
+        # gap_ms between tokens: period = gap_ms / (rows x the measured ms per row and layer of prefills of at least
+        # sample_rows rows that ran with no decode round inside; shorter ones are dominated by fixed costs). Until
+        # one such prefill is measured, `interleave` layers.
+        self.gap_ms = float(gap_ms)
+        self.sample_rows = int(sample_rows)
+        self._row_layer_ms = None
         self.max_active = int(max_active)
         self.max_batch = int(max_batch)
         self.waiting = queue.Queue()
@@ -131,14 +141,21 @@ class Scheduler:
                 self._wake.wait(0.05)
                 self._wake.clear()
 
+    def period_for(self, rows):
+        """Prefill layers between decode rounds for a prompt of `rows` tokens."""
+        if self.gap_ms > 0 and self._row_layer_ms:
+            return max(1, int(self.gap_ms / max(1e-9, rows * self._row_layer_ms)))
+        return self.interleave
+
     def _tick_for(self, owner):
-        """tick(i) for the prefill of `owner`: a decode round of the running streams every `interleave` layers."""
+        """tick(i) for the prefill of `owner`: a decode round of the running streams every period_for(rows) layers."""
         if self.interleave <= 0 or getattr(self.model, "tp", None) is not None:
             return None
         count = itertools.count(1)
+        period = self.period_for(int(owner.ids.numel()))
 
         def tick(i):                      # the owner joins the decode set only after its prefill
-            if next(count) % self.interleave == 0 and self.active:
+            if next(count) % period == 0 and self.active:
                 self.stats["interleaved_rounds"] += 1
                 self._decode_round()
         return tick
@@ -154,6 +171,7 @@ class Scheduler:
         model, arm = self.model, req.arm
         n = int(req.ids.numel())
         req.t_prefill0 = time.perf_counter()
+        rounds0 = self.stats["interleaved_rounds"]
         tick = self._tick_for(req)
         pool = getattr(model, "kv_pool", None)
         if pool is not None:
@@ -186,6 +204,9 @@ class Scheduler:
         now = time.perf_counter()
         req.cache, req.position, req.t_first, req.t_last = cache, n, now, now
         self.prompt_ms.append(1e3 * (now - req.t_prefill0))
+        if self.stats["interleaved_rounds"] == rounds0 and n >= self.sample_rows:   # a clean per-row cost sample
+            x = self.prompt_ms[-1] / (n * max(1, getattr(model, "n_layers", 1)))
+            self._row_layer_ms = x if self._row_layer_ms is None else 0.7 * self._row_layer_ms + 0.3 * x
         self.ttft_ms.append(1e3 * (now - req.t_submit))
         self.stats["prompt_tokens"] += n
         self.stats["filled_tokens"] += req.filled

@@ -53,6 +53,34 @@ def _collect(sched, ids, n, arm):
     return evs, done
 
 
+def test_decode_gap_sets_the_interleave_period_from_measured_prefill_cost(setup):
+    """With gap_ms, a prefill's decode-round period follows its size: the first prefill (nothing decoding) is a
+    clean cost sample; afterwards period_for(rows) ~ gap / (rows x ms per row-layer), at least 1."""
+    model, arms = setup
+    sched = Scheduler(model, interleave=3, gap_ms=50.0, sample_rows=1)
+    assert sched.period_for(100) == 3                       # no measurement yet: the fixed period
+    ev, done = _collect(sched, uniform_prompt(64, CFG.vocab, seed=8), 2, arms["off"])
+    sched.start()
+    try:
+        assert done.wait(60)
+    finally:
+        sched.stop()
+    assert sched._row_layer_ms is not None and sched._row_layer_ms > 0
+    sched._row_layer_ms = 0.01                              # 0.01 ms per row and layer
+    assert sched.period_for(1000) == 5
+    assert sched.period_for(10) == 500
+    assert sched.period_for(10 ** 6) == 1
+    assert Scheduler(model, interleave=3).period_for(1000) == 3   # gap_ms 0: always the fixed period
+    big = Scheduler(model, interleave=3, gap_ms=50.0)             # default: only prefills of 4096+ rows are samples
+    ev, done = _collect(big, uniform_prompt(64, CFG.vocab, seed=9), 2, arms["off"])
+    big.start()
+    try:
+        assert done.wait(60)
+    finally:
+        big.stop()
+    assert big._row_layer_ms is None and big.period_for(1000) == 3
+
+
 def test_scheduler_matches_greedy_and_interleaves(setup):
     model, arms = setup
     sched = Scheduler(model, interleave=1)
