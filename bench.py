@@ -248,6 +248,9 @@ def main():
                          "NVLS gather), rows (each rank a block of prefix rows through the whole map, then an "
                          "all-to-all of the heads' projections: parallel/rowfill.py), or auto: rows from 8 ranks on "
                          "(measured 144.4 vs 150.1 ms at TP 8, 16K), columns below (349.1 vs 366.0 ms at TP 2)")
+    ap.add_argument("--tp-overlap", type=int, default=1,
+                    help="nvls row-parallel products in this many row chunks, each chunk's GEMM beside the previous "
+                         "chunk's all-reduce on a second stream (1: the fused GEMM + all-reduce kernel)")
     args = ap.parse_args()
     dsplit, dtail = DEFAULT_SPLIT_TAIL.get(args.model, (32, 4096))
     args.split = dsplit if args.split is None else args.split
@@ -282,7 +285,7 @@ def main():
     if tp_mode:
         from ridgefill_data_b200.parallel.tp import TensorParallel, shard
         try:
-            tp = TensorParallel(mode=args.tp_comm, fill=args.tp_fill)
+            tp = TensorParallel(mode=args.tp_comm, fill=args.tp_fill, overlap=args.tp_overlap)
         except Exception as e:                       # no NVSwitch multicast here: the NCCL baseline
             if args.tp_comm != "nvls":
                 raise
@@ -420,7 +423,9 @@ def main():
                                 **({"qattn_share": args.qattn_share, "qattn_window": 64} if args.arm == "quality"
                                    else {}),
                                 parallelism=(f"tp{world}" + ("" if args.tp_comm == "nccl" else f"-{args.tp_comm}")
-                                             + ("-rowfill" if args.tp_fill == "rows" else "")) if tp_mode
+                                             + ("-rowfill" if args.tp_fill == "rows" else "")
+                                             + (f"-overlap{args.tp_overlap}" if args.tp_overlap > 1
+                                                and args.tp_comm == "nvls" else "")) if tp_mode
                                 else f"dp{world}",
                                 l2="inputs larger than L2 (the weights, tens of GB, are streamed every step)"),
                     clocks=clocks, gpu_launches=int(launches),

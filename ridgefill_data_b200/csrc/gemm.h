@@ -76,7 +76,8 @@ struct GemmArgs {
 void gemm_bf16(const GemmOperands& op, GemmArgs args, int epi, int bn, int max_ctas, cudaStream_t stream);
 // gemm2sm.cu: the two-SM (cta_group::2, 256 x 256 tile) kernel for K-major store / SwiGLU products with M >= 256;
 // returns false (nothing launched) for any other call. gemm_bf16 tries it first for 256-column tiles.
-bool gemm_bf16_2sm(const GemmOperands& op, const GemmArgs& args, int epi, cudaStream_t stream);
+// max_ctas >= 2: at most max_ctas / 2 clusters (the rest of the SMs stay free for a kernel on another stream)
+bool gemm_bf16_2sm(const GemmOperands& op, const GemmArgs& args, int epi, int max_ctas, cudaStream_t stream);
 extern bool gemm_2sm_enabled;
 CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t pitch_elems,
                               uint32_t box_inner, uint32_t box_outer);

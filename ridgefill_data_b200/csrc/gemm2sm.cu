@@ -408,7 +408,7 @@ CUtensorMap tmap_rows128(const void* base, uint64_t k, uint64_t rows, uint64_t p
 }
 
 template <int EPI>
-void launch2sm(const GemmOperands& op, const GemmArgs& args, cudaStream_t stream) {
+void launch2sm(const GemmOperands& op, const GemmArgs& args, int max_ctas, cudaStream_t stream) {
   auto kernel = gemm2sm_kernel<EPI>;
   static PerDeviceOnce once;
   static int max_clusters[PerDeviceOnce::kMaxDevices] = {0};
@@ -438,6 +438,7 @@ void launch2sm(const GemmOperands& op, const GemmArgs& args, cudaStream_t stream
                                                                                           : num_sms(dev) / 2;
   const int tiles = ((args.M + kTileM - 1) / kTileM) * ((args.N + kTileN - 1) / kTileN);
   if (tiles < clusters) clusters = tiles;
+  if (max_ctas >= 2 && max_ctas / 2 < clusters) clusters = max_ctas / 2;   // leave SMs to a concurrent kernel
   const CUtensorMap ta = tmap_rows128(op.A, args.K, args.M, op.lda);
   const CUtensorMap tb = tmap_rows128(op.B, args.K, args.N, op.ldb);
   kernel<<<2 * clusters, kThreads, kSmemBytes, stream>>>(ta, tb, args);
@@ -448,13 +449,14 @@ void launch2sm(const GemmOperands& op, const GemmArgs& args, cudaStream_t stream
 
 bool gemm_2sm_enabled = true;
 
-bool gemm_bf16_2sm(const GemmOperands& op, const GemmArgs& args, int epi, cudaStream_t stream) {
+bool gemm_bf16_2sm(const GemmOperands& op, const GemmArgs& args, int epi, int max_ctas, cudaStream_t stream) {
   if (!gemm_2sm_enabled || op.a_mn || op.b_mn || args.k_splits != 1) return false;
   if (epi != kEpiStore && epi != kEpiSwiGLU) return false;
   if (epi == kEpiSwiGLU && args.N % kTileN != 0) return false;
   if (args.M < kTileM || args.K % 8 != 0) return false;   // small M: the one-SM tiles waste less
-  if (epi == kEpiStore) launch2sm<kEpiStore>(op, args, stream);
-  else launch2sm<kEpiSwiGLU>(op, args, stream);
+  if (max_ctas == 1) return false;
+  if (epi == kEpiStore) launch2sm<kEpiStore>(op, args, max_ctas, stream);
+  else launch2sm<kEpiSwiGLU>(op, args, max_ctas, stream);
   return true;
 }
 

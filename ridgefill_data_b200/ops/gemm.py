@@ -16,12 +16,13 @@ def _bn(n):
     return 256 if n >= 2048 or n % 256 == 0 else 128
 
 
-def linear(x, w, bias=None, residual=None, out=None, bn=None):
-    """x [M, K] bf16, w [N, K] bf16 -> [M, N] bf16 = x w^T + bias (+ residual, which may be `out`)."""
+def linear(x, w, bias=None, residual=None, out=None, bn=None, max_ctas=0):
+    """x [M, K] bf16, w [N, K] bf16 -> [M, N] bf16 = x w^T + bias (+ residual, which may be `out`). max_ctas > 0: the
+    GEMM keeps to that many SMs (the others stay free for a kernel running beside it on another stream)."""
     m, n = x.shape[0], w.shape[0]
     if out is None:
         out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
-    ext().gemm(x, w, out, bias, residual, EPI_STORE, bn or _bn(n), False, False, 1, 0, 0)
+    ext().gemm(x, w, out, bias, residual, EPI_STORE, bn or _bn(n), False, False, 1, 0, int(max_ctas))
     return out
 
 

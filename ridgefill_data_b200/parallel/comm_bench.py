@@ -132,13 +132,23 @@ def main(argv=None):
             check_errors()
             assert torch.equal(rp(y, w, h).float(), want), "dedicated comm CTAs changed the result"
         rp.comm_ctas = 0
+        overlapped = {}
+        rp.fused_gemm = False
+        for k in (2, 4, 8):
+            rp.overlap, rp.overlap_min_rows = k, 1024
+            overlapped[k] = round(_time(lambda: rp(y, w, h)), 4)
+            torch.cuda.synchronize()
+            check_errors()
+            assert torch.equal(rp(y, w, h).float(), got_split), "the overlapped chunks changed the result"
+        rp.overlap, rp.overlap_min_rows = 1, NvlsRowParallel.overlap_min_rows
+        rp.fused_gemm = True
         t_gemm_symm = _time(lambda: G.linear(y, w, out=part))
         t_gemm = _time(lambda: G.linear(y, w))
         flops = 2 * rows * d * a.k
         roof2 = max(flops / (GEMM_TFLOPS * 1e12), S / (LINK_GBS * 1e9)) * 1e3
         out.append(dict(case="gemm+allreduce", rows=rows, d=d, k=a.k, world=world, gemm_ms=round(t_gemm, 4),
                         gemm_into_symmetric_ms=round(t_gemm_symm, 4), fused_comm_off_ms=round(t2_gemm_part, 4),
-                        fused_dedicated_comm_ctas_ms=dedicated,
+                        fused_dedicated_comm_ctas_ms=dedicated, overlapped_chunks_ms=overlapped,
                         nccl_ms=round(t1, 4), nvls_two_kernels_ms=round(t2s, 4), nvls_fused_ms=round(t2, 4),
                         fused_vs_two_kernel_max_rel_diff=ferr, roofline_ms=round(roof2, 4),
                         nvls_fused_frac_of_roofline=round(roof2 / t2, 3)))

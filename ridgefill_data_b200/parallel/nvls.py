@@ -87,6 +87,11 @@ class NvlsRowParallel(_NvlsBase):
     fused_gemm = True      # one kernel: GEMM tiles + per-row-block reduction by the comm warps (kEpiNvlsAR)
     comm_off = False       # diagnostics only: the fused kernel moves no data (times its GEMM part)
     comm_ctas = 0          # > 0: CTAs dedicated to the reduction (the rest compute tiles); 0: every CTA does both
+    # overlap > 1: the rows go in up to `overlap` chunks; chunk j's GEMM (on all but max_ctas SMs) runs while chunk
+    # j - 1's all-reduce (max_ctas CTAs) runs beside it on a second stream. Neither kernel waits on the other, so
+    # they need not be co-resident; the reduction kernels of different ranks wait on each other as before.
+    overlap = 1
+    overlap_min_rows = 2048
 
     def __init__(self, group=None):
         super().__init__(group)
@@ -135,8 +140,49 @@ class NvlsRowParallel(_NvlsBase):
         self._ensure(rows, d)
         return self.part.t[:rows * d].view(rows, d)
 
+    def _chunks(self, rows):
+        k = min(self.overlap, rows // self.overlap_min_rows) if self.overlap > 1 else 1
+        if k <= 1:
+            return [(0, rows)]
+        step = -(-rows // k)
+        step = -(-step // 128) * 128                   # whole 128-row blocks per chunk
+        return [(a, min(rows, a + step)) for a in range(0, rows, step)]
+
+    def _overlapped(self, y, w, h, chunks):
+        rows, d = y.shape[0], w.shape[0]
+        part = self.partial_view(rows, d)
+        out = self.outs[self.turn]
+        self.turn = (self.turn + 1) % len(self.outs)
+        main = torch.cuda.current_stream()
+        if getattr(self, "comm_stream", None) is None:
+            self.comm_stream = torch.cuda.Stream()
+        comm = self.comm_stream
+        sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        gemm_ctas = max(2, sms - self.max_ctas)
+        for a, b in chunks:
+            G.linear(y[a:b], w, residual=h[a:b] if self.rank == 0 else None, out=part[a:b], max_ctas=gemm_ctas)
+            ev = torch.cuda.Event()
+            ev.record(main)
+            comm.wait_event(ev)
+            m = b - a
+            share = -(-m // self.world)
+            r0, r1 = min(m, self.rank * share), min(m, (self.rank + 1) * share)
+            off = 2 * a * d
+            self.epoch += 1
+            with torch.cuda.stream(comm):
+                ext().nvls_allreduce(self.part.mc + off, out.mc + off, out.ptrs[self.rank] + off, None, m, d, r0, r1,
+                                     self.flag_local, self.flags.ptrs, self.rank, SLOT_AR_IN, SLOT_AR_OUT, self.epoch,
+                                     self.counter(COUNTER_AR), self.err, self.max_ctas, self.acc32)
+        done = torch.cuda.Event()
+        done.record(comm)
+        main.wait_event(done)
+        return out.t[:rows * d].view(rows, d)
+
     def __call__(self, y, w, h):
         rows, d = y.shape[0], w.shape[0]
+        chunks = self._chunks(rows)
+        if len(chunks) > 1:
+            return self._overlapped(y, w, h, chunks)
         part = self.partial_view(rows, d)
         if not self.fused_gemm:
             G.linear(y, w, residual=h if self.rank == 0 else None, out=part)

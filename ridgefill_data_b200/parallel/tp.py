@@ -19,7 +19,8 @@ map fill's column gather in late layers):
               owner's receive slot; map columns into every rank's x_l), the owner reduces, every rank gathers
   nvls        parallel/nvls.py: NVSwitch multicast: partials reduced in the switch (multimem.ld_reduce) and the sums
               multicast to every rank (multimem.st) by one kernel with its own cross-rank barriers; map slices
-              multicast into every rank's x_l
+              multicast into every rank's x_l. With overlap > 1 the row-parallel product goes in row chunks: each
+              chunk's GEMM runs on most SMs while the previous chunk's all-reduce runs on 32 CTAs on a second stream
 With fill="rows" the map fill is row-parallel instead (parallel/rowfill.py): each rank maps a block of prefix rows
 through the whole map and the unsharded fill projection, and an all-to-all delivers each rank its heads' columns.
 """
@@ -32,7 +33,7 @@ from ..ops import gemm as G
 
 
 class TensorParallel:
-    def __init__(self, group=None, mode="nccl", fill="columns"):
+    def __init__(self, group=None, mode="nccl", fill="columns", overlap=1, overlap_min_rows=None):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -53,6 +54,9 @@ class TensorParallel:
             from .nvls import NvlsMapFill, NvlsRowParallel
             self.fused = NvlsRowParallel(group)
             self.fused_fill = NvlsMapFill(group)
+            self.fused.overlap = int(overlap)            # row chunks: GEMM of one beside the all-reduce of another
+            if overlap_min_rows is not None:
+                self.fused.overlap_min_rows = int(overlap_min_rows)
         elif mode not in ("nccl", "fused", "nvls"):
             raise ValueError(f"TP communication mode {mode!r} (nccl | fused | nvls)")
 

@@ -54,7 +54,10 @@ def _worker(rank, world, port, mode, q, fill="columns"):
                 ref, _ = m.forward_exact(ids, keep=keep)
                 hs, lower = run_lower(m, ids, [split])
                 ref_rf, _, _ = finish(m, ids, hs[split], lower, arm, 4)
-                tp = TensorParallel(mode=mode, fill=fill)
+                if mode == "nvls+overlap":     # row chunks of 128: GEMM of one beside the all-reduce of another
+                    tp = TensorParallel(mode="nvls", fill=fill, overlap=4, overlap_min_rows=64)
+                else:
+                    tp = TensorParallel(mode=mode, fill=fill)
                 shard(m, tp)
                 got, _ = m.forward_exact(ids, keep=keep)
                 hs, lower = run_lower(m, ids, [split])
@@ -73,7 +76,7 @@ def _worker(rank, world, port, mode, q, fill="columns"):
 
 
 @pytest.mark.parametrize("mode,fill", [("nccl", "columns"), ("fused", "columns"), ("nvls", "columns"),
-                                       ("nccl", "rows")])
+                                       ("nvls+overlap", "columns"), ("nccl", "rows")])
 def test_tp2_matches_single_gpu(mode, fill):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
