@@ -30,19 +30,20 @@
 
 namespace rf {
 
-template <int HD, int BN, int PB, int SWG, int NS>
+template <int HD, int BN, int PB, int SWG, int NS, int QT>
 struct TcFaCfg {
   static constexpr int Q_BYTES = 128 * HD * 2;
   static constexpr int K_BYTES = BN * HD * 2;
   static constexpr int V_BYTES = BN * HD * 2;
   static constexpr int P_BYTES = 128 * BN * 2;
-  static constexpr int BAR_BYTES = 8 * 24;
+  static constexpr int BAR_BYTES = 8 * 26;
   static constexpr int RED_BYTES = SWG == 2 ? 2 * 128 * 4 : 0;   // partial row max of each warpgroup
   // PB P buffers (2: the softmax of block j + 1 writes its P while the tensor cores still read block j's)
   static constexpr int SMEM = 1024 + Q_BYTES + 2 * (K_BYTES + V_BYTES) + PB * P_BYTES + BAR_BYTES + RED_BYTES;
   static constexpr int O_COL = NS * BN;
+  static constexpr int Q_COL = O_COL + HD;     // QT: Q rows as the A operand in TMEM (2 bf16 per column)
   static constexpr int THREADS = 96 + 128 * SWG;
-  static_assert(O_COL + HD <= 512, "S buffers and O in the 512 TMEM columns");
+  static_assert(O_COL + HD + (QT ? HD / 2 : 0) <= 512, "S buffers, O (and Q) in the 512 TMEM columns");
   static_assert(SMEM <= 232448, "shared memory of one CTA");
 };
 
@@ -84,11 +85,11 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return x < -126.f ? 0.f : __int_as_float(__float_as_int(p) + (n << 23));
 }
 
-template <int HD, int BN, int PB, int POLY, int SWG, int NS>
+template <int HD, int BN, int PB, int POLY, int SWG, int NS, int QT>
 __global__ void __launch_bounds__(96 + 128 * SWG, 1)
     tc_flash_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, TcFaArgs a) {
-  using Cfg = TcFaCfg<HD, BN, PB, SWG, NS>;
+  using Cfg = TcFaCfg<HD, BN, PB, SWG, NS, QT>;
   static_assert(NS == 2 || NS == 3, "two or three S buffers");
   static_assert(SWG == 1 || SWG == 2, "one or two softmax warpgroups");
   static_assert(BN % (32 * SWG) == 0, "every warpgroup's part of an S tile is whole 32-column TMEM loads");
@@ -114,9 +115,10 @@ __global__ void __launch_bounds__(96 + 128 * SWG, 1)
   uint64_t* o_final = bars + 19;
   uint64_t* x_full = bars + 20;    // both warpgroups wrote their partial row max
   uint64_t* x_read = bars + 21;    // both warpgroups read the other's
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 22);
+  uint64_t* q_tmem = bars + 22;    // QT: the Q rows are in TMEM
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 23);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* red = reinterpret_cast<float*>(bars + 24);   // [SWG][128]
+  float* red = reinterpret_cast<float*>(bars + 25);   // [SWG][128]
 
   const int warp = warp_id(), lane = lane_id();
   const int qt = gridDim.x - 1 - blockIdx.x;   // late (heavy) query tiles first
@@ -152,6 +154,7 @@ __global__ void __launch_bounds__(96 + 128 * SWG, 1)
     mbar_init(o_final, 1);
     mbar_init(x_full, 128 * SWG);
     mbar_init(x_read, 128 * SWG);
+    mbar_init(q_tmem, 128);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -214,6 +217,7 @@ __global__ void __launch_bounds__(96 + 128 * SWG, 1)
     }
   } else if (warp == 1) {
     bool ok = mbar_wait(q_full, 0, a.err, kErrTimeoutMma);
+    if constexpr (QT) ok = ok && mbar_wait(q_tmem, 0, a.err, kErrTimeoutMma);
     tc_fence_after();
     const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
     auto issue_pv = [&](int jj) -> bool {
@@ -247,9 +251,13 @@ __global__ void __launch_bounds__(96 + 128 * SWG, 1)
         const uint32_t k_addr = smem_u32(sK + st * Cfg::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128(q_addr + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sdesc_sw128(k_addr + (kk >> 2) * BN * 128 + (kk & 3) * 32, 16, 1024);
-          umma_f16(tmem + sb * BN, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
+          if constexpr (QT) {   // A from TMEM: K step kk is columns 8 kk .. 8 kk + 7 of the Q rows
+            umma_f16_ts(tmem + sb * BN, tmem + Cfg::Q_COL + 8 * kk, bd, IDESC_S, kk > 0 ? 1u : 0u);
+          } else {
+            const uint64_t ad = sdesc_sw128(q_addr + (kk >> 2) * 128 * 128 + (kk & 3) * 32, 16, 1024);
+            umma_f16(tmem + sb * BN, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
+          }
         }
         umma_commit(&s_full[sb]);
         umma_commit(&k_empty[st]);
@@ -285,6 +293,32 @@ __global__ void __launch_bounds__(96 + 128 * SWG, 1)
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     int xph = 0;
+    if constexpr (QT) {
+      // the first warpgroup copies its Q row from the swizzled shared tile into TMEM (the S product's A operand)
+      if (wg == 0) {
+        ok = mbar_wait(q_full, 0, a.err, kErrTimeoutEpilogue);
+        if (ok) {
+#pragma unroll 1
+          for (int b = 0; b < HD / 64; ++b) {
+            uint32_t w16a[16], w16b[16];
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+              const uint4 v = *reinterpret_cast<const uint4*>(sQ + b * 128 * 128 + r * 128 + ((ch ^ (r & 7)) << 4));
+              uint32_t* dst = ch < 4 ? w16a + 4 * ch : w16b + 4 * (ch - 4);
+              dst[0] = v.x;
+              dst[1] = v.y;
+              dst[2] = v.z;
+              dst[3] = v.w;
+            }
+            tmem_st16(tmem + lane_off + Cfg::Q_COL + b * 32, w16a);
+            tmem_st16(tmem + lane_off + Cfg::Q_COL + b * 32 + 16, w16b);
+          }
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        mbar_arrive(q_tmem);
+      }
+    }
     // one value per row to the other warpgroup and back (SWG == 2); NaN marks a warpgroup that stopped, so both
     // stop at the same tile. The write of phase p waits until the other side has read phase p - 1.
     auto exchange = [&](float v, float& other) -> bool {
@@ -505,13 +539,13 @@ static CUtensorMap tmap4_pages(const void* base, int hd, int page_size, int head
   return tm;
 }
 
-template <int HD, int BN, int PB, int POLY, int SWG, int NS>
+template <int HD, int BN, int PB, int POLY, int SWG, int NS, int QT = 0>
 static void launch_tc(const AttnArgs& x, cudaStream_t stream) {
-  using Cfg = TcFaCfg<HD, BN, PB, SWG, NS>;
+  using Cfg = TcFaCfg<HD, BN, PB, SWG, NS, QT>;
   static PerDeviceOnce once;
   once([] {
-    cudaFuncSetAttribute(tc_flash_kernel<HD, BN, PB, POLY, SWG, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         Cfg::SMEM);
+    cudaFuncSetAttribute(tc_flash_kernel<HD, BN, PB, POLY, SWG, NS, QT>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
   });
   CUtensorMap tq = tmap3(x.q, HD, x.nq, x.hq, x.q_head_stride, 128);
   CUtensorMap tk, tv;
@@ -526,7 +560,7 @@ static void launch_tc(const AttnArgs& x, cudaStream_t stream) {
              x.scale * 1.4426950408889634f,
              x.gate, x.gate_row, x.gate_head, x.out, x.out_row, x.err};
   dim3 grid((x.nq + 127) / 128, x.hq);
-  tc_flash_kernel<HD, BN, PB, POLY, SWG, NS><<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(tq, tk, tv, a);
+  tc_flash_kernel<HD, BN, PB, POLY, SWG, NS, QT><<<grid, Cfg::THREADS, Cfg::SMEM, stream>>>(tq, tk, tv, a);
   count_launch();
 }
 
@@ -535,13 +569,15 @@ int attn_poly = 0;
 int attn_softmax_groups = 1;
 int attn_s_buffers = 0;
 int attn_rotate = 0;
+int attn_q_tmem = 0;
 
 // NS0: the S-buffer count measured faster for this head dim (head_dim 256: 2, 128: 3); attn_s_buffers overrides it
 template <int HD, int BN, int NS0>
 static void launch_variant(const AttnArgs& x, cudaStream_t stream) {
   constexpr int NS1 = NS0 == 2 ? 3 : 2;
   const bool other = attn_s_buffers != 0 && attn_s_buffers != NS0;
-  if (other) launch_tc<HD, BN, 2, 0, 1, NS1>(x, stream);
+  if (attn_q_tmem) launch_tc<HD, BN, 2, 0, 1, 2, 1>(x, stream);   // Q in TMEM leaves room for two S buffers
+  else if (other) launch_tc<HD, BN, 2, 0, 1, NS1>(x, stream);
   else if (attn_softmax_groups == 2) launch_tc<HD, BN, 2, 0, 2, NS0>(x, stream);
   else if (attn_p_buffers == 1) launch_tc<HD, BN, 1, 0, 1, NS0>(x, stream);
   else if (attn_poly == 2) launch_tc<HD, BN, 2, 2, 1, NS0>(x, stream);

@@ -119,6 +119,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     rf::attn_softmax_groups = n == 2 ? 2 : 1;
     return was;
   });
+  m.def("set_attn_q_tmem", [](int64_t n) {
+    const int was = rf::attn_q_tmem;
+    rf::attn_q_tmem = n ? 1 : 0;
+    return was;
+  });
   m.def("set_attn_rotate", [](int64_t n) {
     const int was = rf::attn_rotate;
     rf::attn_rotate = n ? 1 : 0;

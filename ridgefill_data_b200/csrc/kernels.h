@@ -103,6 +103,7 @@ extern int attn_p_buffers;   // 1 or 2 shared-memory P buffers in the tcgen05 at
 extern int attn_poly;         // 0, 2 or 4 of every 8 softmax exponentials on the FMA pipe (exp2_fma)
 extern int attn_softmax_groups;   // softmax warpgroups of the tcgen05 attention (1 or 2; 1 by default)
 extern int attn_s_buffers;        // TMEM S buffers of the tcgen05 attention (2 or 3; 0: per head dim)
+extern int attn_q_tmem;           // 1: the tcgen05 attention's S product reads Q from TMEM (A operand)
 extern int attn_rotate;           // 1: every CTA of the tcgen05 attention walks the key tiles from its own start
 
 // ---- gdn.cu

@@ -74,6 +74,8 @@ def ext():
         mod.set_gdn_fused_output(0)
     if os.environ.get("RF_ATTN_SWG") == "2":     # A/B switch: two softmax warpgroups in the tcgen05 attention
         mod.set_attn_softmax_groups(2)
+    if os.environ.get("RF_ATTN_QT") == "1":      # A/B switch: Q read from TMEM by the S product
+        mod.set_attn_q_tmem(1)
     if os.environ.get("RF_ATTN_ROT") == "1":     # A/B switch: per-CTA rotation of the key-tile order
         mod.set_attn_rotate(1)
     if os.environ.get("RF_ATTN_SBUF") in ("2", "3"):   # A/B switch: TMEM S buffers (default per head dim)

@@ -221,11 +221,12 @@ def test_gdn_two_level_scan_matches_sequential_and_oracle(groups, need_out):
 
 
 @pytest.mark.parametrize("variant", [("set_attn_softmax_groups", 2), ("set_attn_s_buffers", 2),
-                                     ("set_attn_s_buffers", 3), ("set_attn_p_buffers", 1), ("set_attn_rotate", 1)])
+                                     ("set_attn_s_buffers", 3), ("set_attn_p_buffers", 1), ("set_attn_rotate", 1),
+                                     ("set_attn_q_tmem", 1)])
 @pytest.mark.parametrize("hd", [128, 256])
 def test_flash_attention_pipeline_variants(variant, hd):
     """The tcgen05 attention's pipeline variants (two softmax warpgroups swapping the row max per tile, two or
-    three TMEM S buffers, one P buffer, key tiles in a per-CTA rotated order) against the fp32 oracle and the default build, causal over 300 rows with
+    three TMEM S buffers, one P buffer, key tiles in a per-CTA rotated order, Q read from TMEM by the S product) against the fp32 oracle and the default build, causal over 300 rows with
     keys past the last query tile."""
     from ridgefill_data_b200.ops._ext import check_errors, ext
     setter, value = variant
