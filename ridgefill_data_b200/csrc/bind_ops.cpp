@@ -38,7 +38,8 @@ void rmsnorm(Tensor x, Tensor w, Tensor out, double eps, bool zero_centred) {
 void head_norm_rope(Tensor src, int64_t src_row_stride, int64_t src_head_stride, int64_t n_heads, int64_t head_dim,
                     int64_t n_rows, OptT norm_w, int64_t norm_mode, double eps, OptT cos, OptT sin, int64_t rot,
                     OptT pos, int64_t pos_offset, Tensor dst, int64_t dst_head_stride, int64_t dst_row_stride,
-                    OptT dst_pages, int64_t page_size, int64_t dst_page_stride, int64_t dst_row0) {
+                    OptT dst_pages, int64_t page_size, int64_t dst_page_stride, int64_t dst_row0,
+                    bool dst_row_from_pos, int64_t dst_rows) {
   need(src, at::kBFloat16, "src");
   need(dst, at::kBFloat16, "dst");
   TORCH_CHECK(head_dim % 32 == 0 && head_dim <= 256, "head_norm_rope: head_dim % 32 == 0, <= 256");
@@ -73,6 +74,11 @@ void head_norm_rope(Tensor src, int64_t src_row_stride, int64_t src_head_stride,
     a.page_size = (int)page_size;
     a.dst_page_stride = dst_page_stride;
     a.dst_row0 = (int)dst_row0;
+  }
+  if (dst_row_from_pos) {
+    TORCH_CHECK(pos.has_value() && dst_rows > 0, "head_norm_rope: rows from positions need pos and the capacity");
+    a.dst_row_from_pos = 1;
+    a.dst_rows = (int)dst_rows;
   }
   a.dst = bf(dst);
   a.dst_head_stride = dst_head_stride;
@@ -273,7 +279,8 @@ void register_ops(pybind11::module_& m) {
         py::arg("n_heads"), py::arg("head_dim"), py::arg("n_rows"), py::arg("norm_w"), py::arg("norm_mode"),
         py::arg("eps"), py::arg("cos"), py::arg("sin"), py::arg("rot"), py::arg("pos"), py::arg("pos_offset"),
         py::arg("dst"), py::arg("dst_head_stride"), py::arg("dst_row_stride"), py::arg("dst_pages") = py::none(),
-        py::arg("page_size") = 0, py::arg("dst_page_stride") = 0, py::arg("dst_row0") = 0);
+        py::arg("page_size") = 0, py::arg("dst_page_stride") = 0, py::arg("dst_row0") = 0,
+        py::arg("dst_row_from_pos") = false, py::arg("dst_rows") = 0);
   m.def("gated_rmsnorm", &gated_rmsnorm);
   m.def("embed_gather", &embed_gather);
   m.def("flash_attention", &flash_attention, py::arg("q"), py::arg("q_head_stride"), py::arg("k"), py::arg("v"),

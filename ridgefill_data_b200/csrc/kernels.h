@@ -64,6 +64,10 @@ struct HeadNormRopeArgs {
   int page_size = 0;
   long dst_page_stride = 0;
   int dst_row0 = 0;
+  // dst_row_from_pos: source row t goes to cache row pos[t] (positions read on the device: a decode step captured in
+  // a CUDA graph writes at the position held in device memory); rows >= dst_rows (the capacity) are not written
+  int dst_row_from_pos = 0;
+  int dst_rows = 0;
 };
 void head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t stream);
 

@@ -143,7 +143,14 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(HeadNormRopeArgs a)
     for (int j = 0; j < per; ++j) v[j] = out[j];
   }
   __nv_bfloat16* dst;
-  if (a.dst_pages != nullptr) {
+  if (a.dst_row_from_pos) {
+    const int r = a.pos[row];
+    if (r < 0 || r >= a.dst_rows) return;   // outside the cache's capacity: nothing written
+    dst = a.dst_pages != nullptr
+              ? a.dst + (long)a.dst_pages[r / a.page_size] * a.dst_page_stride + (long)head * a.dst_head_stride +
+                    (long)(r % a.page_size) * a.dst_row_stride
+              : a.dst + (long)head * a.dst_head_stride + (long)r * a.dst_row_stride;
+  } else if (a.dst_pages != nullptr) {
     const int r = a.dst_row0 + row;
     dst = a.dst + (long)a.dst_pages[r / a.page_size] * a.dst_page_stride + (long)head * a.dst_head_stride +
           (long)(r % a.page_size) * a.dst_row_stride;

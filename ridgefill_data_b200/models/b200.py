@@ -214,6 +214,78 @@ class _B200:
             h = self.mlp(i, G.linear(y, wo, residual=h))
         return self.logits(h)
 
+    # ---- decode on device-resident positions (one CUDA graph serves every step: engine/decode_graph.py)
+    def decode_step_dev(self, tok_dev, pos_dev, caches):
+        """Next-token logits [R, V] fp32 of R sequences advanced by one token each, with the tokens (int64 [R]) and
+        their positions (int32 [R]: each sequence's length before the token) in device memory. K/V rows are written
+        at the positions read on the device, attention bounds its keys by them (query positions), and the GDN conv
+        and recurrent states are updated in place, so nothing reads a position on the host and a CUDA graph of this
+        call replays for every step. The attention caches must already have room for the positions and the RoPE
+        tables must reach past them; the host keeps the lengths (engine/decode_graph.py). Same kernels and
+        arithmetic as decode_batch."""
+        if self.tp is not None or getattr(self.cfg, "moe", False):
+            raise NotImplementedError("device-position decode runs dense single-GPU models")
+        R = tok_dev.shape[0]
+        h = self.embed(tok_dev)
+        for i in range(self.n_layers):
+            w = self.W[i]
+            x = self._norm(h, w["ln1"])
+            if self.layer_types[i] == "attn":
+                qkv = G.linear(x, w["qkv_p"])
+                y = torch.empty(R, self.n_heads * self.head_dim, dtype=self.dtype, device=self.device)
+                for r in range(R):
+                    self._attn_step_dev(i, qkv[r:r + 1], pos_dev[r:r + 1], caches[r][i], y[r:r + 1])
+                wo = w["o"]
+            else:
+                proj = G.linear(x, w["in_p"])
+                o = torch.cat([self._gdn_step_dev(i, proj[r:r + 1], caches[r]) for r in range(R)])
+                z = proj[:, self.conv_dim + 2 * self.nv:]
+                y = K.gated_rmsnorm(o, z, w["norm"], self.nv, self.cfg.gdn_dv, self.eps)
+                wo = w["out"]
+            h = self.mlp(i, G.linear(y, wo, residual=h))
+        return self.logits(h)
+
+    def _attn_step_dev(self, i, qkv, p_dev, c, o):
+        """One decode row of attention layer i: K/V written at cache row p_dev[0], the query at that position over
+        keys 0 .. p_dev[0] (both read on the device)."""
+        w = self.W[i]
+        hd, hq, hkv = self.head_dim, self.n_heads, self.n_kv
+        gated = self.cfg.gated_attn
+        qw = hq * hd * (2 if gated else 1)
+        tables = self._rope_tables
+        if self.kv_pool is not None:
+            pool = self.kv_pool
+            kd, vd = pool.k[i], pool.v[i]
+            rows, stride = len(c["pages"]) * pool.page_size, pool.page_size * hd
+            paged = dict(pages=c["pages_dev"], page_size=pool.page_size, page_stride=pool.page_stride)
+        else:
+            kd, vd = c["kbuf"], c["vbuf"]
+            rows, stride, paged = kd.shape[1], kd.shape[1] * hd, {}
+        K.head_norm_rope(qkv[:, qw:], hkv, hd, hd, kd, stride, hd, norm_w=w.get("k_norm"), norm_mode=self._qk_mode(),
+                         eps=self.eps, tables=tables, rot=self.cfg.rot_dim, pos=p_dev, row_from_pos=True,
+                         dst_rows=rows, **paged)
+        K.head_norm_rope(qkv[:, qw + hkv * hd:], hkv, hd, hd, vd, stride, hd, pos=p_dev, row_from_pos=True,
+                         dst_rows=rows, **paged)
+        q = torch.empty(hq, 1, hd, dtype=self.dtype, device=self.device)
+        K.head_norm_rope(qkv, hq, hd, 2 * hd if gated else hd, q, hd, hd, norm_w=w.get("q_norm"),
+                         norm_mode=self._qk_mode(), eps=self.eps, tables=tables, rot=self.cfg.rot_dim, pos=p_dev)
+        K.attention(q, kd, vd, rows, self.scale, o, qpos=p_dev, gate=qkv[:, hd:] if gated else None,
+                    gate_head=2 * hd, pages=c["pages_dev"] if self.kv_pool is not None else None)
+
+    def _gdn_step_dev(self, i, proj, cache):
+        """One decode row of GDN layer i, its conv and recurrent states updated in place."""
+        w = self.W[i]
+        cfg = self.cfg
+        C, nv = self.conv_dim, self.nv
+        c = cache[i]
+        conv_state, rec = c["conv"], c["rec"]
+        q, k, v, beta, g = K.gdn_prep(proj, C, C + nv, w["conv"], conv_state, w["A_log"], w["dt_bias"], self.nk, nv,
+                                      cfg.gdn_dk, cfg.gdn_dv)
+        K.gdn_conv_state_update(proj, conv_state, C)
+        out = torch.empty(1, self.vd, dtype=self.dtype, device=self.device)
+        K.gdn_scan(q, k, v, beta, g, rec, out, groups=1)
+        return out
+
     # ---- per-layer API
     def _mixer_out(self, i, h, pos, cache, need_out=True, checkpoint_every=None):
         if self.layer_types[i] == "attn":

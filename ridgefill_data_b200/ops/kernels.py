@@ -30,15 +30,16 @@ def rope_tables(inv_freq, max_pos, device, dtype=BF16):
 
 def head_norm_rope(src, n_heads, head_dim, head_stride, dst, dst_head_stride, dst_row_stride, norm_w=None,
                    norm_mode=-1, eps=1e-6, tables=None, rot=0, pos=None, pos_offset=0, pages=None, page_size=0,
-                   page_stride=0, row0=0):
+                   page_stride=0, row0=0, row_from_pos=False, dst_rows=0):
     """Per (row, head) of src [n, *] (head h at column h * head_stride): optional head RMSNorm, RoPE on the
     first rot dims at positions pos (int32 [n]) or pos_offset + row; written to dst + h * dst_head_stride +
     row * dst_row_stride (element strides). With pages (int32 page ids): row t is cache row row0 + t, stored in
-    page pages[(row0 + t) // page_size] of the pool dst (page_stride elements apart) at row (row0 + t) % page_size."""
+    page pages[(row0 + t) // page_size] of the pool dst (page_stride elements apart) at row (row0 + t) % page_size.
+    row_from_pos: row t goes to cache row pos[t] instead (read on the device), rows >= dst_rows not written."""
     cos, sin = tables if tables is not None else (None, None)
     ext().head_norm_rope(src, src.stride(0), head_stride, n_heads, head_dim, src.shape[0], norm_w, norm_mode,
                          float(eps), cos, sin, rot, pos, pos_offset, dst, dst_head_stride, dst_row_stride,
-                         pages, page_size, page_stride, row0)
+                         pages, page_size, page_stride, row0, bool(row_from_pos), int(dst_rows))
 
 
 def gated_rmsnorm(o, z, w, heads, dv, eps, out=None):
