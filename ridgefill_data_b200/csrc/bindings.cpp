@@ -1,5 +1,6 @@
 // Python bindings of the sm_100a kernels (torch tensors -> raw pointers + the current stream).
 #include <torch/extension.h>
+#include <algorithm>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -93,6 +94,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("error_word", &error_word);
   m.def("sm_count", &sm_count);
   m.def("launch_count", &launch_count);
+  m.def("set_gemv", [](bool on) {
+    const bool was = rf::gemv_enabled;
+    rf::gemv_enabled = on;
+    return was;
+  });
+  m.def("set_gemv_max_rows", [](int64_t n) {
+    const int was = rf::gemv_max_rows;
+    rf::gemv_max_rows = (int)std::max<int64_t>(0, std::min<int64_t>(8, n));
+    return was;
+  });
   m.def("set_gemm_2sm", &set_gemm_2sm);
   m.def("set_attn_poly", [](int64_t n) {
     const int was = rf::attn_poly;

@@ -26,7 +26,7 @@ def _length(model, cache):
 
 
 class DecodeGraph:
-    def __init__(self, model, caches, headroom):
+    def __init__(self, model, caches, headroom, pool=None):
         if not hasattr(model, "decode_step_dev"):
             raise NotImplementedError("the model has no device-position decode step")
         self.model = model
@@ -48,7 +48,9 @@ class DecodeGraph:
         self._pos_host = torch.zeros(R, dtype=torch.int32).pin_memory()
         self._copied = None          # the previous step's host -> device copies (the pinned buffers are reused)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.no_grad(), torch.cuda.graph(self.graph):
+        # pool: a memory pool shared with earlier graphs (torch.cuda.graph_pool_handle()), so a new capture reuses
+        # their blocks instead of allocating device memory; only one of them may be replayed at a time
+        with torch.no_grad(), torch.cuda.graph(self.graph, pool=pool):
             self.logits = model.decode_step_dev(self.tok, self.pos, self.caches)
 
     def room(self):

@@ -112,6 +112,10 @@ class _B200:
             if n:
                 nkb[:, :n] = c["kbuf"][:, :n]
                 nvb[:, :n] = c["vbuf"][:, :n]
+            # rows past the ones about to be written stay zero: attention bounded by query positions (the decode
+            # graph) reads whole key tiles, and a masked key's weight 0 times a NaN left in V would still be NaN
+            nkb[:, n + m:].zero_()
+            nvb[:, n + m:].zero_()
             c["kbuf"], c["vbuf"] = nkb, nvb
         return n
 
@@ -189,8 +193,11 @@ class _B200:
     def decode_batch(self, toks, positions, caches):
         """R sequences advanced by one token each in one pass over the weights: the embedding, every projection,
         MLP (or MoE) and the logits run on the R stacked rows; only the per-sequence parts (K/V append and
-        attention over that sequence's cache, the GDN conv and recurrent step on its state) run per row. Every
-        GEMM computes its rows independently, so each row equals the single-sequence step bitwise."""
+        attention over that sequence's cache, the GDN conv and recurrent step on its state) run per row. The tile
+        GEMMs sum every row the same way whatever the row count, so each row equals the single-sequence step bitwise
+        when they run every product; products of 1-2 rows take the GEMV by default (csrc/gemv.cu: faster, another
+        summation order), which makes a single step differ from a batched row by bf16 rounding (set_gemv(False)
+        restores the bitwise property)."""
         if self.tp is not None or len(toks) == 1:
             return super().decode_batch(toks, positions, caches)
         R = len(toks)

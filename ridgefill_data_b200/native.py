@@ -1,7 +1,7 @@
 """Standalone native programs (no Python or torch inside): built in-tree with nvcc for sm_100a.
 
-  identity_check   csrc/native/identity_check.cu + csrc/gemm.cu + csrc/gemm2sm.cu: the fill GEMM (one-SM and two-SM
-                   kernels) with an identity map must copy
+  identity_check   csrc/native/identity_check.cu + csrc/gemm.cu + csrc/gemm2sm.cu + csrc/gemv.cu: the fill GEMM
+                   (one-SM and two-SM kernels) with an identity map must copy
                    its input bit for bit (both N-tile widths, with and without the bias epilogue)
 
 build_native() compiles every program into ridgefill_data_b200/bin/ (the driver's build step calls it);
@@ -17,7 +17,8 @@ CSRC = PKG / "csrc"
 BIN = PKG / "bin"
 NVCC = ["nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-lineinfo",
         "--expt-relaxed-constexpr", f"-I{CSRC}"]
-PROGRAMS = {"identity_check": ([CSRC / "native" / "identity_check.cu", CSRC / "gemm.cu", CSRC / "gemm2sm.cu"],
+PROGRAMS = {"identity_check": ([CSRC / "native" / "identity_check.cu", CSRC / "gemm.cu", CSRC / "gemm2sm.cu",
+                                 CSRC / "gemv.cu"],
                                ["-lcuda"])}
 
 

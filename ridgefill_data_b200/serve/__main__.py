@@ -85,6 +85,8 @@ def main(argv=None):
     ap.add_argument("--interleave", type=int, default=4,
                     help="decode round every this many prefill layers (0: off; the period until --decode-gap-ms has "
                          "a measured prefill cost to work from)")
+    ap.add_argument("--decode-graphs", type=int, default=1,
+                    help="decode rounds as CUDA-graph replays while the running requests stay the same (1 on, 0 off)")
     ap.add_argument("--decode-gap-ms", type=float, default=100.0,
                     help="target gap between a running stream's tokens while a prompt is prefilled: each prefill's "
                          "decode-round period follows its size (0: every --interleave layers)")
@@ -94,7 +96,8 @@ def main(argv=None):
     from .app import Server, create_app
     from .engine import Scheduler
     model, arms, tok, eos, props = build(a)
-    sched = Scheduler(model, eos=eos, interleave=a.interleave, gap_ms=a.decode_gap_ms).start()
+    sched = Scheduler(model, eos=eos, interleave=a.interleave, gap_ms=a.decode_gap_ms,
+                      graphs=bool(a.decode_graphs)).start()
     try:
         Server(create_app(sched, arms, tok, props), a.host, a.port, log_level="info").run()
     finally:

@@ -59,7 +59,7 @@ class Request:
 
 class Scheduler:
     def __init__(self, model, eos=(), interleave=4, max_active=64, max_batch=32, sync=None, gap_ms=0.0,
-                 sample_rows=4096):
+                 sample_rows=4096, graphs=True, graph_min_tokens=8):
         self.model = model
         self.eos = frozenset(int(e) for e in eos)
         self.interleave = int(interleave)
@@ -70,6 +70,14 @@ class Scheduler:
         self.gap_ms = float(gap_ms)
         self.sample_rows = int(sample_rows)
         self._row_layer_ms = None
+        # decode rounds as CUDA-graph replays (engine/decode_graph.py) while the set of running requests stays the
+        # same; a new graph is captured when it changes and every request has graph_min_tokens or more to go
+        self.graphs = bool(graphs) and model.device.type == "cuda"
+        self.graph_min_tokens = int(graph_min_tokens)
+        self._graph = None
+        self._graph_key = None
+        self._graph_pool = None
+        self._seen_key = None        # the previous round's set: a graph is captured once a set repeats
         self.max_active = int(max_active)
         self.max_batch = int(max_batch)
         self.waiting = queue.Queue()
@@ -81,7 +89,7 @@ class Scheduler:
         self.sync = sync if sync is not None else (torch.cuda.synchronize if model.device.type == "cuda"
                                                   else (lambda: None))
         self.stats = dict(requests=0, completed=0, errors=0, prompt_tokens=0, predicted_tokens=0,
-                          filled_tokens=0, interleaved_rounds=0, decode_batches=0)
+                          filled_tokens=0, interleaved_rounds=0, decode_batches=0, graph_captures=0, graph_steps=0)
         self.ttft_ms, self.prompt_ms = [], []
         self._lock = threading.Lock()
 
@@ -242,6 +250,32 @@ class Scheduler:
             if pool is not None:
                 pool.owner = saved
 
+    def _graph_for(self, grp):
+        """The decode graph of this group of requests (reused, or captured now), or None for an eager round."""
+        if not self.graphs or len(grp) > self.max_batch:
+            return None
+        key = tuple(id(r) for r in grp)
+        g = self._graph
+        if g is not None and self._graph_key == key and g.room() > 0 and g.lengths == [r.position for r in grp]:
+            return g
+        self._graph = self._graph_key = None
+        seen, self._seen_key = self._seen_key, key
+        left = min(r.n_predict - len(r.produced) for r in grp)
+        if left < self.graph_min_tokens or seen != key:   # capture only for a set that held for a round
+            return None
+        from ..engine.decode_graph import DecodeGraph
+        if self._graph_pool is None:
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        try:
+            g = DecodeGraph(self.model, [r.cache for r in grp],
+                            headroom=max(r.n_predict - len(r.produced) for r in grp), pool=self._graph_pool)
+        except NotImplementedError:        # no device-position decode for this model: eager rounds from now on
+            self.graphs = False
+            return None
+        self._graph, self._graph_key = g, key
+        self.stats["graph_captures"] += 1
+        return g
+
     def _decode_round_inner(self):
         reqs = list(self.active)
         plain = [r for r in reqs if r.arm.fill != "swiftkv_native"]
@@ -249,8 +283,13 @@ class Scheduler:
         for j in range(0, len(plain), self.max_batch):
             grp = plain[j:j + self.max_batch]
             try:
-                logits = self.model.decode_batch([r.tok for r in grp], [r.position for r in grp],
-                                                 [r.cache for r in grp])
+                g = self._graph_for(grp) if len(plain) <= self.max_batch else None
+                if g is not None:
+                    logits = g.step([r.tok for r in grp])
+                    self.stats["graph_steps"] += 1
+                else:
+                    logits = self.model.decode_batch([r.tok for r in grp], [r.position for r in grp],
+                                                     [r.cache for r in grp])
                 self.stats["decode_batches"] += 1
                 for r, row in zip(grp, logits):
                     toks[id(r)] = row

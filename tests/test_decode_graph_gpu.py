@@ -82,3 +82,36 @@ def test_graph_decode_refuses_past_its_room():
         dg.step(toks)
         with pytest.raises(RuntimeError, match="room"):
             dg.step(toks)
+
+
+def test_scheduler_graph_rounds_match_eager_rounds():
+    """The server's decode rounds as graph replays produce the same tokens as eager rounds (two requests decoding
+    together, one joining after the other's prefill)."""
+    import threading
+    from ridgefill_data_b200.engine.arm import Arm
+    from ridgefill_data_b200.serve.engine import Request, Scheduler
+    results = {}
+    for graphs in (False, True):
+        m = from_config(HYB, seed=0, device="cuda", std=0.05, backend="b200")
+        sched = Scheduler(m, interleave=2, graphs=graphs, graph_min_tokens=4)
+        evs, done = {}, {}
+        for name, n, seed in (("a", 90, 1), ("b", 200, 2)):
+            ids = torch.randint(0, HYB.vocab, (n,), generator=torch.Generator().manual_seed(seed))
+            evs[name], done[name] = [], threading.Event()
+
+            def emit(ev, name=name):
+                evs[name].append(ev)
+                if ev.get("stop"):
+                    done[name].set()
+            sched.submit(Request(ids=ids, n_predict=14, arm=Arm("exact"), emit=emit, ignore_eos=True))
+        sched.start()
+        try:
+            assert all(d.wait(120) for d in done.values())
+        finally:
+            sched.stop()
+        results[graphs] = {k: [t for e in v if not e.get("stop") for t in e["tokens"]] for k, v in evs.items()}
+        if graphs:
+            assert sched.stats["graph_steps"] > 0, sched.stats
+        del m, sched
+        torch.cuda.empty_cache()
+    assert results[True] == results[False]

@@ -113,3 +113,40 @@ def test_two_sm_gemm_matches_one_sm_and_fp32(m, n, k):
         assert (act - want).abs().max().item() / want.abs().max().item() < 2e-2
     torch.cuda.synchronize()
     check_errors()
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
+def test_small_m_gemv_epilogues_match_fp32_and_tile_gemm(m):
+    """1-8 row products (a decode step) take the GEMV kernel (csrc/gemv.cu): store with bias + residual written in
+    place, fp32, and the packed SwiGLU, against the fp32 reference and the tile GEMM (gemv switched off)."""
+    from ridgefill_data_b200.ops import gemm
+    from ridgefill_data_b200.ops._ext import check_errors, ext
+    torch.manual_seed(11 + m)
+    k, n, f = 1024, 1000, 256                              # n not a multiple of the tile, odd column count per warp
+    x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05
+    b = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+    h = torch.randn(m, n, device="cuda", dtype=torch.bfloat16)
+    g = torch.randn(f, k, device="cuda", dtype=torch.bfloat16) * 0.1
+    u = torch.randn(f, k, device="cuda", dtype=torch.bfloat16) * 0.1
+    gu = gemm.pack_gate_up(g, u)
+    outs = {}
+    rows_was = ext().set_gemv_max_rows(8)                  # every row count of the test on the GEMV
+    for on in (True, False):
+        was = ext().set_gemv(on)
+        try:
+            hh = h.clone()
+            gemm.linear(x, w, bias=b, residual=hh, out=hh)
+            outs[on] = (hh.float(), gemm.linear_f32(x, w), gemm.swiglu_linear(x, gu).float())
+        finally:
+            ext().set_gemv(was)
+    ext().set_gemv_max_rows(rows_was)
+    torch.cuda.synchronize()
+    check_errors()
+    ref_store = _ref(x, w) + b.float() + h.float()
+    ref_f32 = _ref(x, w)
+    ref_sw = torch.nn.functional.silu(_ref(x, g)) * _ref(x, u)
+    for got, ref in zip(outs[True], (ref_store, ref_f32, ref_sw)):
+        assert (got - ref).abs().max().item() / ref.abs().max().item() < 1e-2
+    for a, b2 in zip(outs[True], outs[False]):
+        assert (a - b2).abs().max().item() / b2.abs().max().item() < 1e-2

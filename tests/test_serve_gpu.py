@@ -59,8 +59,12 @@ def test_scheduler_b200_interleaved_streams_match_engine():
 
 @pytest.mark.parametrize("gated", [True, False])
 def test_decode_batch_b200_matches_single_steps(gated):
-    """decode_batch on the sm_100a model: every row bitwise equal to that sequence's single decode step."""
+    """decode_batch on the sm_100a model: every row bitwise equal to that sequence's single decode step when every
+    product runs on the tile GEMMs (they sum each row the same way whatever the row count). With the GEMV taking
+    1-2 row products (the default: faster single-stream decode) a single step sums in another order, so there the
+    rows agree within bf16 rounding."""
     from ridgefill_data_b200.engine.decode import fork_cache, step
+    from ridgefill_data_b200.ops._ext import ext
     cfg = HYB if gated else ModelConfig(arch="llama", n_layers=4, hidden=512, vocab=1024, n_heads=8, n_kv=2,
                                         head_dim=64, intermediate=1536, eps=1e-5, rope_theta=5e5,
                                         name="tiny-llama-gpu")
@@ -72,8 +76,19 @@ def test_decode_batch_b200_matches_single_steps(gated):
             ids = torch.randint(0, cfg.vocab, (n,), generator=g).cuda()
             logits, cache, _ = prefill(model, ids, Arm("exact"), keep=1)
             seqs.append((int(logits[-1].argmax()), n, cache))
-        single = [step(model, t, p, fork_cache(c), None)[-1] for t, p, c in seqs]
-        batched = model.decode_batch([t for t, _, _ in seqs], [p for _, p, _ in seqs],
-                                     [fork_cache(c) for _, _, c in seqs])
+        runs = {}
+        for gemv in (False, True):
+            was = ext().set_gemv(gemv)
+            try:
+                single = [step(model, t, p, fork_cache(c), None)[-1] for t, p, c in seqs]
+                batched = model.decode_batch([t for t, _, _ in seqs], [p for _, p, _ in seqs],
+                                             [fork_cache(c) for _, _, c in seqs])
+            finally:
+                ext().set_gemv(was)
+            runs[gemv] = (single, batched)
+    single, batched = runs[False]
     for r in range(3):
         assert torch.equal(batched[r], single[r]), (batched[r] - single[r]).abs().max()
+    single, batched = runs[True]
+    for r in range(3):
+        assert (batched[r] - single[r]).abs().max() / single[r].abs().max() < 3e-2
