@@ -50,7 +50,8 @@ class DecodeGraph:
         self.graph = torch.cuda.CUDAGraph()
         # pool: a memory pool shared with earlier graphs (torch.cuda.graph_pool_handle()), so a new capture reuses
         # their blocks instead of allocating device memory; only one of them may be replayed at a time
-        with torch.no_grad(), torch.cuda.graph(self.graph, pool=pool):
+        # thread-local capture: other threads of the process (a server's request threads) may use CUDA meanwhile
+        with torch.no_grad(), torch.cuda.graph(self.graph, pool=pool, capture_error_mode="thread_local"):
             self.logits = model.decode_step_dev(self.tok, self.pos, self.caches)
 
     def room(self):

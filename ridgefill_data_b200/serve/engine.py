@@ -272,6 +272,11 @@ class Scheduler:
         except NotImplementedError:        # no device-position decode for this model: eager rounds from now on
             self.graphs = False
             return None
+        except Exception as e:             # a capture that failed: report once, decode eagerly from now on
+            self.graphs = False
+            import sys
+            print(f"decode graphs off: capture failed ({type(e).__name__}: {e})", file=sys.stderr)
+            return None
         self._graph, self._graph_key = g, key
         self.stats["graph_captures"] += 1
         return g
