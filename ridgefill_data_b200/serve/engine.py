@@ -327,6 +327,8 @@ class Scheduler:
             else:
                 keep.append(req)
         self.active = keep
+        if self._graph is not None and len(keep) != len(reqs):   # a request of the graph ended: its caches go
+            self._graph = self._graph_key = None
 
     def _release(self, req):
         """Drop the request's cache; with a paged KV pool its pages go back to the pool."""
