@@ -115,3 +115,25 @@ def test_scheduler_graph_rounds_match_eager_rounds():
         del m, sched
         torch.cuda.empty_cache()
     assert results[True] == results[False]
+
+
+def test_greedy_graph_decode_matches_eager_steps(monkeypatch):
+    """engine.decode.greedy: a long run replays one decode graph; its tokens equal the eager steps' (RF_DECODE_GRAPH=0)
+    and the caller's recurrent-state tensors are left as they were."""
+    from ridgefill_data_b200.engine.arm import Arm
+    from ridgefill_data_b200.engine.decode import fork_cache, greedy
+    from ridgefill_data_b200.engine.prefill import prefill
+    m = from_config(HYB, seed=0, device="cuda", std=0.05, backend="b200")
+    ids = torch.randint(0, HYB.vocab, (300,), generator=torch.Generator().manual_seed(21)).cuda()
+    arm = Arm("exact")
+    with torch.no_grad():
+        logits, cache, _ = prefill(m, ids, arm, keep=1)
+    gdn = [i for i, t in enumerate(m.layer_types) if t != "attn"]
+    before = cache[gdn[0]]["rec"].clone()
+    toks = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("RF_DECODE_GRAPH", mode)
+        c = fork_cache(cache)
+        toks[mode], _ = greedy(m, ids, c, logits, 24, arm)
+    assert toks["1"] == toks["0"]
+    assert torch.equal(cache[gdn[0]]["rec"], before)
