@@ -20,6 +20,52 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __forceinline__ float bfr(float x) { return __bfloat162float(__float2bfloat16(x)); }
 
+// per (4 or 8) consecutive bf16 of a lane as one 8- or 16-byte access when the address allows it, else one by one.
+// per is a compile-time constant at every call, so the loops unroll and the arrays stay in registers.
+__device__ __forceinline__ void load_bf16(const __nv_bfloat16* p, int per, float (&v)[8]) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  if (per == 8 && (a & 15) == 0) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else if (per == 4 && (a & 7) == 0) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    for (int j = 0; j < per; ++j) v[j] = __bfloat162float(p[j]);
+  }
+}
+
+__device__ __forceinline__ void store_bf16(__nv_bfloat16* p, int per, const float (&v)[8]) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  if (per == 8 && (a & 15) == 0) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+  } else if (per == 4 && (a & 7) == 0) {
+    uint2 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint2*>(p) = u;
+  } else {
+    for (int j = 0; j < per; ++j) p[j] = __float2bfloat16(v[j]);
+  }
+}
+
 // ------------------------------------------------------------------------------------- rmsnorm
 // One CTA (256 threads) per row; the row (d <= 8192) is held in registers between the two passes.
 template <int MODE>
@@ -90,7 +136,9 @@ void rmsnorm(const __nv_bfloat16* x, long ldx, const __nv_bfloat16* w, __nv_bflo
 }
 
 // ----------------------------------------------------------------------------- head_norm_rope
-// One warp per (row, head); head_dim <= 256 (8 elements per lane).
+// One warp per (row, head); head_dim <= 256 (PER = head_dim / 32 elements per lane, a template parameter so that the
+// lane's elements live in registers).
+template <int PER>
 __global__ void __launch_bounds__(256) head_norm_rope_kernel(HeadNormRopeArgs a) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -98,30 +146,42 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(HeadNormRopeArgs a)
   const int head = warp % a.n_heads;
   if (row >= a.n_rows) return;
   const int hd = a.head_dim;
-  const int per = hd / 32;  // elements per lane (hd multiple of 32)
+  constexpr int per = PER;  // elements per lane (hd multiple of 32)
   const __nv_bfloat16* src = a.src + (long)row * a.src_row_stride + (long)head * a.src_head_stride;
-  float v[8];
+  // every independent load first (the row, the norm weights, the position and this lane's cos / sin entries), so
+  // one memory latency covers them all
+  float v[8], wv[8], cv[8], sv[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) v[j] = 0.f;
+  for (int j = 0; j < 8; ++j) v[j] = wv[j] = cv[j] = sv[j] = 0.f;
   // lane owns elements lane*per .. lane*per+per-1
-  for (int j = 0; j < per; ++j) v[j] = __bfloat162float(src[lane * per + j]);
+  load_bf16(src + lane * per, per, v);
+  if (a.norm_mode >= 0) load_bf16(a.norm_w + lane * per, per, wv);
+  const int h = a.rot / 2;
+  if (a.rot > 0 && lane * per < a.rot) {
+    const int p = a.pos != nullptr ? __ldg(a.pos + row) : row + a.pos_offset;
+    const __nv_bfloat16* cs = a.cos + (long)p * h;
+    const __nv_bfloat16* sn = a.sin + (long)p * h;
+    for (int j = 0; j < per; ++j) {
+      const int i = lane * per + j;
+      const int t = i < h ? i : i - h;   // rotate-half pairs i and i +- h share the angle of min(i, i - h)
+      if (i < a.rot) {
+        cv[j] = __bfloat162float(cs[t]);
+        sv[j] = __bfloat162float(sn[t]);
+      }
+    }
+  }
   if (a.norm_mode >= 0) {
     float ss = 0.f;
     for (int j = 0; j < per; ++j) ss += v[j] * v[j];
     ss = warp_sum(ss);
     const float inv = rsqrtf(ss / (float)hd + a.eps);
     for (int j = 0; j < per; ++j) {
-      const float wj = __bfloat162float(a.norm_w[lane * per + j]);
       const float f = v[j] * inv;
-      v[j] = (a.norm_mode == 0) ? bfr(bfr(f) * wj) : bfr(f * (1.0f + wj));
+      v[j] = (a.norm_mode == 0) ? bfr(bfr(f) * wv[j]) : bfr(f * (1.0f + wv[j]));
     }
   }
   if (a.rot > 0) {
     // rotate-half over [0, rot): out[i] = x[i] cos[i] - x[i + h] sin[i] (i < h), out[i] = x[i] cos[i - h] + x[i - h] sin
-    const int h = a.rot / 2;
-    const int p = a.pos != nullptr ? a.pos[row] : row + a.pos_offset;
-    const __nv_bfloat16* cs = a.cos + (long)p * h;
-    const __nv_bfloat16* sn = a.sin + (long)p * h;
     float out[8];
     for (int j = 0; j < per; ++j) out[j] = v[j];
     // partner exchange: element i pairs with i +- h; h is a multiple of per when rot % (2*per) == 0
@@ -130,15 +190,7 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(HeadNormRopeArgs a)
       const int i = lane * per + j;
       const float up = __shfl_down_sync(0xffffffffu, v[j], loff);  // value at i + h
       const float dn = __shfl_up_sync(0xffffffffu, v[j], loff);    // value at i - h
-      if (i < a.rot) {
-        if (i < h) {
-          const float c = __bfloat162float(cs[i]), s = __bfloat162float(sn[i]);
-          out[j] = bfr(bfr(v[j] * c) + bfr(-up * s));
-        } else {
-          const float c = __bfloat162float(cs[i - h]), s = __bfloat162float(sn[i - h]);
-          out[j] = bfr(bfr(v[j] * c) + bfr(dn * s));
-        }
-      }
+      if (i < a.rot) out[j] = i < h ? bfr(bfr(v[j] * cv[j]) + bfr(-up * sv[j])) : bfr(bfr(v[j] * cv[j]) + bfr(dn * sv[j]));
     }
     for (int j = 0; j < per; ++j) v[j] = out[j];
   }
@@ -157,18 +209,30 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(HeadNormRopeArgs a)
   } else {
     dst = a.dst + (long)head * a.dst_head_stride + (long)row * a.dst_row_stride;
   }
-  for (int j = 0; j < per; ++j) dst[lane * per + j] = __float2bfloat16(v[j]);
+  store_bf16(dst + lane * per, per, v);
 }
 
 void head_norm_rope(const HeadNormRopeArgs& a, cudaStream_t stream) {
   if (a.n_rows <= 0 || a.n_heads <= 0) return;
   const long warps = (long)a.n_rows * a.n_heads;
   const int blocks = (int)((warps * 32 + 255) / 256);
-  head_norm_rope_kernel<<<blocks, 256, 0, stream>>>(a); count_launch();
+  switch (a.head_dim / 32) {
+    case 1: head_norm_rope_kernel<1><<<blocks, 256, 0, stream>>>(a); break;
+    case 2: head_norm_rope_kernel<2><<<blocks, 256, 0, stream>>>(a); break;
+    case 3: head_norm_rope_kernel<3><<<blocks, 256, 0, stream>>>(a); break;
+    case 4: head_norm_rope_kernel<4><<<blocks, 256, 0, stream>>>(a); break;
+    case 5: head_norm_rope_kernel<5><<<blocks, 256, 0, stream>>>(a); break;
+    case 6: head_norm_rope_kernel<6><<<blocks, 256, 0, stream>>>(a); break;
+    case 7: head_norm_rope_kernel<7><<<blocks, 256, 0, stream>>>(a); break;
+    default: head_norm_rope_kernel<8><<<blocks, 256, 0, stream>>>(a); break;
+  }
+  count_launch();
 }
 
 // ------------------------------------------------------------------------------ gated_rmsnorm
-// y[row, head, :] = bf16( bf16(w * bf16(norm(o))) * silu(z) ); one warp per (row, head), dv <= 256.
+// y[row, head, :] = bf16( bf16(w * bf16(norm(o))) * silu(z) ); one warp per (row, head), dv <= 256. silu(z) on the
+// special-function exponential and a fast divide (relative error near 1e-6, far below the bf16 rounding of y).
+template <int PER>
 __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const __nv_bfloat16* __restrict__ o, long ldo,
                                                             const __nv_bfloat16* __restrict__ z, long ldz,
                                                             const __nv_bfloat16* __restrict__ w,
@@ -179,33 +243,49 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const __nv_bfloat16*
   const int row = warp / heads;
   const int head = warp % heads;
   if (row >= rows) return;
-  const int per = dv / 32;
+  constexpr int per = PER;
   const __nv_bfloat16* orow = o + (long)row * ldo + head * dv;
   const __nv_bfloat16* zrow = z + (long)row * ldz + head * dv;
-  float v[8];
+  float v[8], zv[8], wv[8];
+  load_bf16(orow + lane * per, per, v);
+  load_bf16(zrow + lane * per, per, zv);
+  load_bf16(w + lane * per, per, wv);
   float ss = 0.f;
-  for (int j = 0; j < per; ++j) {
-    v[j] = __bfloat162float(orow[lane * per + j]);
-    ss += v[j] * v[j];
-  }
+  for (int j = 0; j < per; ++j) ss += v[j] * v[j];
   ss = warp_sum(ss);
   const float inv = rsqrtf(ss / (float)dv + eps);
   __nv_bfloat16* yrow = y + (long)row * ldy + head * dv;
+  float out[8];
   for (int j = 0; j < per; ++j) {
-    const int i = lane * per + j;
-    const float t = bfr(__bfloat162float(w[i]) * bfr(v[j] * inv));
-    const float zz = __bfloat162float(zrow[i]);
-    const float sz = zz / (1.0f + expf(-zz));
-    yrow[i] = __float2bfloat16(t * sz);
+    const float t = bfr(wv[j] * bfr(v[j] * inv));
+    const float zz = zv[j];
+    out[j] = t * __fdividef(zz, 1.0f + __expf(-zz));   // silu on the fast exponential, as the GEMM epilogues'
   }
+  store_bf16(yrow + lane * per, per, out);
 }
 
 void gated_rmsnorm(const __nv_bfloat16* o, long ldo, const __nv_bfloat16* z, long ldz, const __nv_bfloat16* w,
                    __nv_bfloat16* y, long ldy, int rows, int heads, int dv, float eps, cudaStream_t stream) {
   if (rows <= 0) return;
   const long warps = (long)rows * heads;
-  gated_rmsnorm_kernel<<<(int)((warps * 32 + 255) / 256), 256, 0, stream>>>(o, ldo, z, ldz, w, y, ldy, rows, heads,
-                                                                            dv, eps); count_launch();
+  switch (dv / 32) {
+#define RF_GATED_CASE(P)                                                                                         \
+    case P:                                                                                                      \
+      gated_rmsnorm_kernel<P><<<(int)((warps * 32 + 255) / 256), 256, 0, stream>>>(o, ldo, z, ldz, w, y, ldy, rows, \
+                                                                                  heads, dv, eps);               \
+      break;
+    RF_GATED_CASE(1)
+    RF_GATED_CASE(2)
+    RF_GATED_CASE(3)
+    RF_GATED_CASE(4)
+    RF_GATED_CASE(5)
+    RF_GATED_CASE(6)
+    RF_GATED_CASE(7)
+    default:
+      RF_GATED_CASE(8)
+#undef RF_GATED_CASE
+  }
+  count_launch();
 }
 
 // ------------------------------------------------------------------------------- embed_gather
