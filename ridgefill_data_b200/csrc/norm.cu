@@ -161,12 +161,19 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(HeadNormRopeArgs a)
     const int p = a.pos != nullptr ? __ldg(a.pos + row) : row + a.pos_offset;
     const __nv_bfloat16* cs = a.cos + (long)p * h;
     const __nv_bfloat16* sn = a.sin + (long)p * h;
-    for (int j = 0; j < per; ++j) {
-      const int i = lane * per + j;
-      const int t = i < h ? i : i - h;   // rotate-half pairs i and i +- h share the angle of min(i, i - h)
-      if (i < a.rot) {
-        cv[j] = __bfloat162float(cs[t]);
-        sv[j] = __bfloat162float(sn[t]);
+    // rotate-half pairs i and i +- h share the angle of min(i, i - h); a lane's per elements lie on one side of h
+    // (per divides h), so its angles are per consecutive table entries: one vector load each for cos and sin
+    const int i0 = lane * per;
+    const int t0 = i0 < h ? i0 : i0 - h;
+    if (i0 + per <= a.rot) {
+      load_bf16(cs + t0, per, cv);
+      load_bf16(sn + t0, per, sv);
+    } else {
+      for (int j = 0; j < per; ++j) {
+        if (i0 + j < a.rot) {
+          cv[j] = __bfloat162float(cs[t0 + j]);
+          sv[j] = __bfloat162float(sn[t0 + j]);
+        }
       }
     }
   }
