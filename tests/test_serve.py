@@ -267,3 +267,62 @@ def test_server_cli_build():
     assert props["vocab"] == model.cfg.vocab and eos == (tok.eos_token_id,)
     with pytest.raises(SystemExit):
         build(argparse.Namespace(**dict(vars(a), synthetic_maps=False)))
+
+
+def test_scheduler_graph_policy_with_a_stand_in_graph(setup, monkeypatch):
+    """The decode-graph policy of the scheduler, with a stand-in graph (CUDA graphs need a GPU): a set of running
+    requests is captured only after it repeats for a round, the capture is reused while the set holds, dropped when
+    one of its requests ends, and the tokens equal eager rounds; a capture that raises turns graphs off for good."""
+    from ridgefill_data_b200.engine import decode_graph as DGM
+    model, arms = setup
+    made = []
+
+    class StandIn:
+        def __init__(self, model, caches, headroom, pool=None):
+            self.model, self.caches = model, list(caches)
+            att = next(i for i, t in enumerate(model.layer_types) if t == "attn")
+            self.lengths = [int(c[att]["n"]) for c in caches]
+            self.limit = [n + headroom for n in self.lengths]
+            self.steps = 0
+            made.append(self)
+
+        def room(self):
+            return min(lim - n for lim, n in zip(self.limit, self.lengths))
+
+        def step(self, toks):
+            out = self.model.decode_batch(list(toks), list(self.lengths), self.caches)
+            self.lengths = [n + 1 for n in self.lengths]
+            self.steps += 1
+            return out
+
+    monkeypatch.setattr(DGM, "DecodeGraph", StandIn)
+
+    def run(graphs):
+        sched = Scheduler(model, interleave=0, graphs=False, graph_min_tokens=3)
+        sched.graphs = graphs                    # the CPU model: switch the policy on by hand
+        evs = {}
+        for name, n, seed, pred in (("a", 24, 31, 9), ("b", 30, 32, 6)):
+            evs[name] = _collect(sched, uniform_prompt(n, CFG.vocab, seed=seed), pred, arms["off"])
+        sched.start()
+        try:
+            assert all(done.wait(60) for _, done in evs.values())
+        finally:
+            sched.stop()
+        toks = {k: [t for e in ev if not e.get("stop") for t in e["tokens"]] for k, (ev, _) in evs.items()}
+        return sched, toks
+
+    sched_e, toks_e = run(False)
+    sched_g, toks_g = run(True)
+    assert toks_g == toks_e
+    assert sched_g.stats["graph_captures"] == len(made) >= 1
+    assert sched_g.stats["graph_steps"] == sum(g.steps for g in made) > 0
+    assert sched_g.stats["graph_steps"] < sched_g.stats["decode_batches"]   # the first round of a set runs eager
+    assert sched_g._graph is None                                             # dropped when its requests ended
+
+    class Broken(StandIn):
+        def __init__(self, *a, **k):
+            raise RuntimeError("capture failed")
+
+    monkeypatch.setattr(DGM, "DecodeGraph", Broken)
+    sched_b, toks_b = run(True)
+    assert toks_b == toks_e and sched_b.graphs is False and sched_b.stats["graph_captures"] == 0
