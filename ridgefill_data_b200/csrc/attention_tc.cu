@@ -18,8 +18,11 @@
 //               O is rescaled in TMEM only when the row max grows by more than 2^8 (otherwise the stale max stays
 //               exact for both O and l); P rounded to bf16 into shared memory in the 128-byte-swizzled K-major
 //               layout; finally O / l (times sigmoid(gate)) to global memory, each warpgroup its HD / SWG columns.
-//               Two warpgroups put two softmax warps on every scheduler, which hides the latency of the per-tile
-//               chain (TMEM load, max, exponentials, P store) that one warp per scheduler leaves exposed.
+// The default is one softmax warpgroup (SWG = 1), two P buffers and exponentials on the special-function unit. The
+// other template choices are measured A/B variants, none faster by more than 2 %: two softmax warpgroups (SWG = 2),
+// one P buffer (PB = 1), part of the exponentials on the FMA pipe (POLY), Q read from TMEM by the S product as the
+// A operand (QT = 1: the first warpgroup copies its Q rows from the swizzled tile into TMEM), and each CTA walking
+// the key tiles from its own start (a.rotate).
 // Every mbarrier wait is bounded (ptx.cuh); the kernel records an error code instead of hanging.
 #include "kernels.h"
 #include "ptx.cuh"
