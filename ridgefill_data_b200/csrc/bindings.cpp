@@ -101,7 +101,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("set_gemv_max_rows", [](int64_t n) {
     const int was = rf::gemv_max_rows;
-    rf::gemv_max_rows = (int)std::max<int64_t>(0, std::min<int64_t>(8, n));
+    rf::gemv_max_rows = (int)std::max<int64_t>(0, std::min<int64_t>(16, n));
+    return was;
+  });
+  m.def("set_gemv_mma", [](bool on) {
+    const bool was = rf::gemv_mma;
+    rf::gemv_mma = on;
     return was;
   });
   m.def("set_gemm_2sm", &set_gemm_2sm);

@@ -650,7 +650,7 @@ void gemm_bf16(const GemmOperands& op, GemmArgs args, int epi, int bn, int max_c
   if (args.k_splits > 1 && args.k_chunk % BK != 0) throw std::runtime_error("split-K chunk must be a multiple of 64");
   if (epi == kEpiSwiGLU && (args.N % bn != 0)) throw std::runtime_error("SwiGLU GEMM needs N % BN == 0");
   if (epi != kEpiF64Acc && args.k_splits != 1) throw std::runtime_error("split-K only with the fp64 epilogue");
-  if (args.M <= 8 && gemm_bf16_gemv(op, args, epi, bn, stream)) return;
+  if (args.M <= 16 && gemm_bf16_gemv(op, args, epi, bn, stream)) return;
   if (bn == 256 && max_ctas != 1 && gemm_bf16_2sm(op, args, epi, max_ctas, stream)) return;
 #define RF_GEMM_CASE(BN_, EPI_, AM_, BMJ_)                                               \
   if (bn == BN_ && epi == EPI_ && op.a_mn == AM_ && op.b_mn == BMJ_) {                   \

@@ -79,11 +79,12 @@ void gemm_bf16(const GemmOperands& op, GemmArgs args, int epi, int bn, int max_c
 // max_ctas >= 2: at most max_ctas / 2 clusters (the rest of the SMs stay free for a kernel on another stream)
 bool gemm_bf16_2sm(const GemmOperands& op, const GemmArgs& args, int epi, int max_ctas, cudaStream_t stream);
 extern bool gemm_2sm_enabled;
-// gemv.cu: products of 1-8 rows (K-major operands, store / SwiGLU / fp32 epilogues) as bandwidth-bound GEMVs; false
-// (nothing launched) for any other call. gemm_bf16 tries it first.
+// gemv.cu: products of 1-16 rows (K-major operands, store / SwiGLU / fp32 epilogues) as bandwidth-bound GEMVs;
+// false (nothing launched) for any other call. gemm_bf16 tries it first.
 bool gemm_bf16_gemv(const GemmOperands& op, const GemmArgs& args, int epi, int bn, cudaStream_t stream);
 extern bool gemv_enabled;
-extern int gemv_max_rows;   // products of up to this many rows (<= 8) take the GEMV
+extern bool gemv_mma;       // true: the tensor-core kernel (1-16 rows); false: the CUDA-core kernel (1-8 rows)
+extern int gemv_max_rows;   // products of up to this many rows take the GEMV
 CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t pitch_elems,
                               uint32_t box_inner, uint32_t box_outer);
 int num_sms(int device);

@@ -68,8 +68,11 @@ def ext():
     _mod = Checked(mod) if os.environ.get("RF_CHECK_EACH") == "1" else mod
     if os.environ.get("RF_GEMM_2SM") == "0":     # A/B switch: every product on the one-SM GEMM kernel
         mod.set_gemm_2sm(False)
-    if os.environ.get("RF_GEMV") == "0":         # A/B switch: 1-8 row products on the tile GEMMs instead of GEMVs
+    if os.environ.get("RF_GEMV") == "0":         # A/B switch: 1-16 row products on the tile GEMMs instead of GEMVs
         mod.set_gemv(False)
+    if os.environ.get("RF_GEMV_MMA") == "0":     # A/B switch: the CUDA-core GEMV for 1-2 rows, tile GEMMs above
+        mod.set_gemv_mma(False)
+        mod.set_gemv_max_rows(2)
     if os.environ.get("RF_GDN_TC") == "1":       # A/B switch: output-mode GDN state pass on tcgen05 (state in TMEM)
         mod.set_gdn_state_tc(1)
     if os.environ.get("RF_GDN_FUSED") == "0":    # A/B switch: GDN output in a separate pass after the state pass

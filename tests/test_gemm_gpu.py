@@ -115,14 +115,18 @@ def test_two_sm_gemm_matches_one_sm_and_fp32(m, n, k):
     check_errors()
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
-def test_small_m_gemv_epilogues_match_fp32_and_tile_gemm(m):
-    """1-8 row products (a decode step) take the GEMV kernel (csrc/gemv.cu): store with bias + residual written in
-    place, fp32, and the packed SwiGLU, against the fp32 reference and the tile GEMM (gemv switched off)."""
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 9, 13, 16])
+@pytest.mark.parametrize("kernel", ["mma", "simt"])
+def test_small_m_gemv_epilogues_match_fp32_and_tile_gemm(m, kernel):
+    """1-16 row products (a decode step) take a GEMV kernel (csrc/gemv.cu; the tensor-core one for 1-16 rows, the
+    CUDA-core one for 1-8): store with bias + residual written in place, fp32, and the packed SwiGLU, against the
+    fp32 reference and the tile GEMM (gemv switched off)."""
     from ridgefill_data_b200.ops import gemm
     from ridgefill_data_b200.ops._ext import check_errors, ext
+    if kernel == "simt" and m > 8:
+        pytest.skip("the CUDA-core GEMV takes at most 8 rows")
     torch.manual_seed(11 + m)
-    k, n, f = 1024, 1000, 256                              # n not a multiple of the tile, odd column count per warp
+    k, n, f = 1000, 1000, 256          # k not a multiple of the 32-wide k block; n not a multiple of 16 columns
     x = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
     w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.05
     b = torch.randn(n, device="cuda", dtype=torch.bfloat16)
@@ -131,18 +135,23 @@ def test_small_m_gemv_epilogues_match_fp32_and_tile_gemm(m):
     u = torch.randn(f, k, device="cuda", dtype=torch.bfloat16) * 0.1
     gu = gemm.pack_gate_up(g, u)
     outs = {}
-    rows_was = ext().set_gemv_max_rows(8)                  # every row count of the test on the GEMV
+    rows_was = ext().set_gemv_max_rows(16)                 # every row count of the test on the GEMV
+    mma_was = ext().set_gemv_mma(kernel == "mma")
     for on in (True, False):
         was = ext().set_gemv(on)
         try:
             hh = h.clone()
+            n0 = ext().launch_count()
             gemm.linear(x, w, bias=b, residual=hh, out=hh)
             outs[on] = (hh.float(), gemm.linear_f32(x, w), gemm.swiglu_linear(x, gu).float())
+            launches = ext().launch_count() - n0
         finally:
             ext().set_gemv(was)
+    ext().set_gemv_mma(mma_was)
     ext().set_gemv_max_rows(rows_was)
     torch.cuda.synchronize()
     check_errors()
+    assert launches == 3
     ref_store = _ref(x, w) + b.float() + h.float()
     ref_f32 = _ref(x, w)
     ref_sw = torch.nn.functional.silu(_ref(x, g)) * _ref(x, u)
@@ -150,3 +159,30 @@ def test_small_m_gemv_epilogues_match_fp32_and_tile_gemm(m):
         assert (got - ref).abs().max().item() / ref.abs().max().item() < 1e-2
     for a, b2 in zip(outs[True], outs[False]):
         assert (a - b2).abs().max().item() / b2.abs().max().item() < 1e-2
+
+
+def test_mma_gemv_rows_do_not_depend_on_the_batch():
+    """The tensor-core GEMV sums every row in one fixed order (its k blocks per warp, the warps in turn), so a row's
+    result is the same bits whether it runs alone or with up to 15 other rows, on every epilogue."""
+    from ridgefill_data_b200.ops import gemm
+    from ridgefill_data_b200.ops._ext import check_errors, ext
+    torch.manual_seed(5)
+    k, n, f = 5120, 1024, 512
+    x = torch.randn(16, k, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(n, k, device="cuda", dtype=torch.bfloat16) * 0.02
+    b = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+    gu = gemm.pack_gate_up(torch.randn(f, k, device="cuda", dtype=torch.bfloat16) * 0.02,
+                           torch.randn(f, k, device="cuda", dtype=torch.bfloat16) * 0.02)
+    rows_was, mma_was, on_was = ext().set_gemv_max_rows(16), ext().set_gemv_mma(True), ext().set_gemv(True)
+    try:
+        full = (gemm.linear(x, w, bias=b), gemm.linear_f32(x, w), gemm.swiglu_linear(x, gu))
+        for m in (1, 2, 3, 7, 8, 9, 15):
+            part = (gemm.linear(x[-m:], w, bias=b), gemm.linear_f32(x[-m:], w), gemm.swiglu_linear(x[-m:], gu))
+            for a, ref in zip(part, full):
+                assert torch.equal(a, ref[-m:]), (m, (a.float() - ref[-m:].float()).abs().max())
+    finally:
+        ext().set_gemv(on_was)
+        ext().set_gemv_mma(mma_was)
+        ext().set_gemv_max_rows(rows_was)
+    torch.cuda.synchronize()
+    check_errors()

@@ -59,10 +59,10 @@ def test_scheduler_b200_interleaved_streams_match_engine():
 
 @pytest.mark.parametrize("gated", [True, False])
 def test_decode_batch_b200_matches_single_steps(gated):
-    """decode_batch on the sm_100a model: every row bitwise equal to that sequence's single decode step when every
-    product runs on the tile GEMMs (they sum each row the same way whatever the row count). With the GEMV taking
-    1-2 row products (the default: faster single-stream decode) a single step sums in another order, so there the
-    rows agree within bf16 rounding."""
+    """decode_batch on the sm_100a model: every row bitwise equal to that sequence's single decode step, both with
+    the default tensor-core GEMV taking the 1-16 row products and with every product on the tile GEMMs (each sums a
+    row the same way whatever the row count). With the CUDA-core GEMV for 1-2 rows (set_gemv_mma(False)) a single
+    step sums in another order than the batched rows' tile GEMMs, so there the rows agree within bf16 rounding."""
     from ridgefill_data_b200.engine.decode import fork_cache, step
     from ridgefill_data_b200.ops._ext import ext
     cfg = HYB if gated else ModelConfig(arch="llama", n_layers=4, hidden=512, vocab=1024, n_heads=8, n_kv=2,
@@ -77,18 +77,22 @@ def test_decode_batch_b200_matches_single_steps(gated):
             logits, cache, _ = prefill(model, ids, Arm("exact"), keep=1)
             seqs.append((int(logits[-1].argmax()), n, cache))
         runs = {}
-        for gemv in (False, True):
-            was = ext().set_gemv(gemv)
+        for kind in ("tile", "mma", "simt"):
+            was = (ext().set_gemv(kind != "tile"), ext().set_gemv_mma(kind == "mma"),
+                   ext().set_gemv_max_rows(2 if kind == "simt" else 16))
             try:
                 single = [step(model, t, p, fork_cache(c), None)[-1] for t, p, c in seqs]
                 batched = model.decode_batch([t for t, _, _ in seqs], [p for _, p, _ in seqs],
                                              [fork_cache(c) for _, _, c in seqs])
             finally:
-                ext().set_gemv(was)
-            runs[gemv] = (single, batched)
-    single, batched = runs[False]
-    for r in range(3):
-        assert torch.equal(batched[r], single[r]), (batched[r] - single[r]).abs().max()
-    single, batched = runs[True]
+                ext().set_gemv(was[0])
+                ext().set_gemv_mma(was[1])
+                ext().set_gemv_max_rows(was[2])
+            runs[kind] = (single, batched)
+    for kind in ("tile", "mma"):
+        single, batched = runs[kind]
+        for r in range(3):
+            assert torch.equal(batched[r], single[r]), (kind, (batched[r] - single[r]).abs().max())
+    single, batched = runs["simt"]
     for r in range(3):
         assert (batched[r] - single[r]).abs().max() / single[r].abs().max() < 3e-2
