@@ -206,6 +206,67 @@ void gdn_conv_state_update(Tensor proj, Tensor state, int64_t n, int64_t C, int6
   rf::gdn_conv_state_update(cbf(proj), proj.stride(0), bf(state), (int)n, (int)C, (int)K, cur());
 }
 
+// One decode row of a GDN layer for R sequences: proj [R, *] (rows of the in-projection), out [R, nv * dv]; the
+// per-sequence conv states [K-1, C] bf16 and recurrent states [nv, dk, dv] fp32 are read from *_src and written to
+// *_dst (the same tensors: in place).
+void gdn_decode_step(Tensor proj, Tensor conv_w, Tensor A_log, Tensor dt_bias, std::vector<Tensor> conv_src,
+                     std::vector<Tensor> conv_dst, std::vector<Tensor> rec_src, std::vector<Tensor> rec_dst, Tensor out,
+                     int64_t b_off, int64_t a_off, int64_t nk, int64_t nv, int64_t dk, int64_t dv, int64_t K) {
+  need(proj, at::kBFloat16, "proj");
+  need(conv_w, at::kBFloat16, "conv_w");
+  need(A_log, at::kFloat, "A_log");
+  need(dt_bias, at::kFloat, "dt_bias");
+  need(out, at::kBFloat16, "out");
+  const int64_t R = proj.size(0);
+  const int64_t C = 2 * nk * dk + nv * dv;
+  TORCH_CHECK(rf::gdn_decode_supported((int)dk, (int)dv, (int)K) && nk > 0 && nv % nk == 0,
+              "gdn_decode_step: dims");
+  TORCH_CHECK(proj.stride(1) == 1 && out.stride(1) == 1 && conv_w.is_contiguous() && out.size(0) == R &&
+                  out.size(1) == nv * dv && proj.size(1) >= a_off + nv && b_off + nv <= a_off && C <= b_off &&
+                  conv_w.size(0) == C && conv_w.size(1) == K && A_log.numel() == nv && dt_bias.numel() == nv,
+              "gdn_decode_step: layouts");
+  TORCH_CHECK((int64_t)conv_src.size() == R && (int64_t)conv_dst.size() == R && (int64_t)rec_src.size() == R &&
+                  (int64_t)rec_dst.size() == R, "gdn_decode_step: one state of each kind per row");
+  for (int64_t r = 0; r < R; ++r) {
+    for (const Tensor* t : {&conv_src[r], &conv_dst[r]}) {
+      need(*t, at::kBFloat16, "conv state");
+      TORCH_CHECK(t->is_contiguous() && t->numel() == (K - 1) * C && t->device() == proj.device(),
+                  "gdn_decode_step: conv state [K-1, C]");
+    }
+    for (const Tensor* t : {&rec_src[r], &rec_dst[r]}) {
+      need(*t, at::kFloat, "recurrent state");
+      TORCH_CHECK(t->is_contiguous() && t->numel() == nv * dk * dv && t->device() == proj.device(),
+                  "gdn_decode_step: recurrent state [nv, dk, dv]");
+    }
+  }
+  c10::cuda::CUDAGuard gd(proj.device());
+  for (int64_t r0 = 0; r0 < R; r0 += rf::kDecodeSeqs) {
+    const int rows = (int)std::min<int64_t>(rf::kDecodeSeqs, R - r0);
+    rf::GdnDecodeArgs a{};
+    a.proj = cbf(proj);
+    a.proj_row = proj.stride(0);
+    a.b_off = (int)b_off;
+    a.a_off = (int)a_off;
+    a.conv_w = cbf(conv_w);
+    a.A_log = A_log.data_ptr<float>();
+    a.dt_bias = dt_bias.data_ptr<float>();
+    a.nk = (int)nk;
+    a.nv = (int)nv;
+    a.dk = (int)dk;
+    a.dv = (int)dv;
+    a.K = (int)K;
+    a.out = bf(out);
+    a.out_row = out.stride(0);
+    for (int s = 0; s < rows; ++s) {
+      a.conv_src[s] = cbf(conv_src[r0 + s]);
+      a.conv_dst[s] = bf(conv_dst[r0 + s]);
+      a.rec_src[s] = rec_src[r0 + s].data_ptr<float>();
+      a.rec_dst[s] = rec_dst[r0 + s].data_ptr<float>();
+    }
+    rf::gdn_decode_step(a, (int)r0, rows, cur());
+  }
+}
+
 void gdn_chunk_scan(OptT q, Tensor k, Tensor v, Tensor beta, Tensor g, Tensor state, OptT out, Tensor w_buf,
                     Tensor u_buf, OptT s_buf, OptT vt_buf, int64_t n, int64_t nk, int64_t nv, int64_t dk, int64_t dv, Tensor err,
                     int64_t groups, OptT grp_buf, OptT start_buf) {
@@ -290,6 +351,7 @@ void register_ops(pybind11::module_& m) {
         py::arg("page_size") = 0, py::arg("num_pages") = 0);
   m.def("gdn_prep", &gdn_prep);
   m.def("gdn_conv_state_update", &gdn_conv_state_update);
+  m.def("gdn_decode_step", &gdn_decode_step);
   m.def("gdn_chunk_scan", &gdn_chunk_scan);
   void register_comm(pybind11::module_ & m);
   register_comm(m);

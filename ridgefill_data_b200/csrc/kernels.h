@@ -127,6 +127,26 @@ struct GdnPrepArgs {
   float* g;                     // [nv, n]
 };
 void gdn_prep(const GdnPrepArgs& a, cudaStream_t stream);
+// gdn_decode.cu: one decode row of a GDN layer for up to kDecodeSeqs sequences (conv, gates, recurrent delta-rule
+// step, conv-state shift); sequence s of the launch reads in-projection row r0 + s and writes output row r0 + s.
+constexpr int kDecodeSeqs = 16;
+struct GdnDecodeArgs {
+  const __nv_bfloat16* proj;     // [R, *] in-projection rows: [q | k | v] conv channels at col 0, b at b_off, a at a_off
+  long proj_row;
+  int b_off, a_off;
+  const __nv_bfloat16* conv_w;   // [C, K]
+  const float* A_log;            // [nv]
+  const float* dt_bias;          // [nv]
+  int nk, nv, dk, dv, K;
+  __nv_bfloat16* out;            // [R, nv * dv]
+  long out_row;
+  const __nv_bfloat16* conv_src[kDecodeSeqs];   // [K-1, C] per sequence
+  __nv_bfloat16* conv_dst[kDecodeSeqs];
+  const float* rec_src[kDecodeSeqs];            // [nv, dk, dv] fp32 per sequence
+  float* rec_dst[kDecodeSeqs];
+};
+bool gdn_decode_supported(int dk, int dv, int K);
+void gdn_decode_step(const GdnDecodeArgs& a, int r0, int rows, cudaStream_t stream);
 void gdn_conv_state_update(const __nv_bfloat16* proj, long proj_row, __nv_bfloat16* state, int n, int C, int K,
                            cudaStream_t stream);
 

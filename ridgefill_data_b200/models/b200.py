@@ -214,7 +214,13 @@ class _B200:
                 wo = w["o"]
             else:
                 proj = G.linear(x, w["in_p"])
-                o = torch.cat([self._gdn_core_dev(i, proj[r:r + 1], caches[r], True) for r in range(R)])
+                entries = [caches[r][i] for r in range(R)]
+                if self._gdn_decode_ok(entries):
+                    o = self._gdn_decode(i, proj, entries, in_place=False)
+                    for c in entries:
+                        c["len"] = c.get("len", 0) + 1
+                else:
+                    o = torch.cat([self._gdn_core_dev(i, proj[r:r + 1], caches[r], True) for r in range(R)])
                 z = proj[:, self.conv_dim + 2 * self.nv:]
                 y = K.gated_rmsnorm(o, z, w["norm"], self.nv, self.cfg.gdn_dv, self.eps)
                 wo = w["out"]
@@ -245,7 +251,11 @@ class _B200:
                 wo = w["o"]
             else:
                 proj = G.linear(x, w["in_p"])
-                o = torch.cat([self._gdn_step_dev(i, proj[r:r + 1], caches[r]) for r in range(R)])
+                entries = [caches[r][i] for r in range(R)]
+                if self._gdn_decode_ok(entries):
+                    o = self._gdn_decode(i, proj, entries, in_place=True)
+                else:
+                    o = torch.cat([self._gdn_step_dev(i, proj[r:r + 1], caches[r]) for r in range(R)])
                 z = proj[:, self.conv_dim + 2 * self.nv:]
                 y = K.gated_rmsnorm(o, z, w["norm"], self.nv, self.cfg.gdn_dv, self.eps)
                 wo = w["out"]
@@ -278,6 +288,42 @@ class _B200:
                          norm_mode=self._qk_mode(), eps=self.eps, tables=tables, rot=self.cfg.rot_dim, pos=p_dev)
         K.attention(q, kd, vd, rows, self.scale, o, qpos=p_dev, gate=qkv[:, hd:] if gated else None,
                     gate_head=2 * hd, pages=c["pages_dev"] if self.kv_pool is not None else None)
+
+    def _gdn_decode_ok(self, entries):
+        """Whether the batched decode step (csrc/gdn_decode.cu) serves these cache entries of one GDN layer: head dims
+        128, fp32 recurrent states and conv windows already there (a prefill made them)."""
+        cfg = self.cfg
+        if not K.gdn_decode_supported(cfg.gdn_dk, cfg.gdn_dv, cfg.conv_k) or self.nv % self.nk:
+            return False
+        if self.conv_dim != 2 * self.nk * cfg.gdn_dk + self.nv * cfg.gdn_dv:
+            return False
+        for c in entries:
+            conv, rec = c.get("conv"), c.get("rec")
+            if conv is None or rec is None or rec.dtype != torch.float32 or not rec.is_contiguous() \
+                    or not conv.is_contiguous():
+                return False
+        return True
+
+    def _gdn_decode(self, i, proj, entries, in_place):
+        """One decode row per sequence of GDN layer i in two launches for all of them (csrc/gdn_decode.cu): proj
+        [R, *] the in-projection rows, entries the R sequences' cache entries of layer i. in_place: the states are
+        updated where they are (the graphed step owns them); otherwise new state tensors replace the entries' ones
+        (the old ones may be shared with a forked cache). Returns the delta rule's outputs [R, nv * dv]."""
+        w = self.W[i]
+        cfg = self.cfg
+        out = torch.empty(proj.shape[0], self.vd, dtype=self.dtype, device=self.device)
+        conv_src = [c["conv"] for c in entries]
+        rec_src = [c["rec"] for c in entries]
+        if in_place:
+            conv_dst, rec_dst = conv_src, rec_src
+        else:
+            conv_dst = [torch.empty_like(t) for t in conv_src]
+            rec_dst = [torch.empty_like(t) for t in rec_src]
+        K.gdn_decode_step(proj, w["conv"], w["A_log"], w["dt_bias"], conv_src, conv_dst, rec_src, rec_dst, out,
+                          self.nk, self.nv, cfg.gdn_dk, cfg.gdn_dv, self.conv_dim, self.conv_dim + self.nv)
+        for c, cd, rd in zip(entries, conv_dst, rec_dst):
+            c["conv"], c["rec"] = cd, rd
+        return out
 
     def _gdn_step_dev(self, i, proj, cache):
         """One decode row of GDN layer i, its conv and recurrent states updated in place."""
@@ -456,11 +502,16 @@ class B200Hybrid(_B200, Hybrid):
         w["sh_gu_p"] = G.pack_gate_up(w["sh_gate"], w["sh_up"]).contiguous()
 
     def _gdn_core_dev(self, i, proj, cache, need_out):
-        """Conv + gates + chunked delta rule over the rows of proj, continuing cache[i]'s states."""
+        """Conv + gates + chunked delta rule over the rows of proj, continuing cache[i]'s states. A single row with
+        output (a decode step) takes the batched decode kernel, the same arithmetic as decode_batch's rows."""
         w = self.W[i]
         cfg = self.cfg
         C, nv = self.conv_dim, self.nv
         c = cache[i]
+        if proj.shape[0] == 1 and need_out and self._gdn_decode_ok([c]):
+            out = self._gdn_decode(i, proj, [c], in_place=False)
+            c["len"] = c.get("len", 0) + 1
+            return out
         conv_state = c.get("conv")
         q, k, v, beta, g = K.gdn_prep(proj, C, C + nv, w["conv"], conv_state, w["A_log"], w["dt_bias"],
                                       self.nk, nv, cfg.gdn_dk, cfg.gdn_dv, need_q=need_out)

@@ -101,6 +101,22 @@ def gdn_conv_state_update(proj, state, channels):
     ext().gdn_conv_state_update(proj, state, proj.shape[0], channels, state.shape[0] + 1)
 
 
+def gdn_decode_supported(dk, dv, conv_k):
+    """Shapes the batched decode step (csrc/gdn_decode.cu) takes: head dims 128, 2-8 conv taps."""
+    return dk == 128 and dv == 128 and 2 <= conv_k <= 8
+
+
+def gdn_decode_step(proj, conv_w, A_log, dt_bias, conv_src, conv_dst, rec_src, rec_dst, out, nk, nv, dk, dv,
+                    b_off, a_off):
+    """One decode row of a GDN layer for R sequences in two launches (csrc/gdn_decode.cu): proj [R, *] in-projection
+    rows ([q | k | v] conv channels, b at b_off, a at a_off), per-sequence conv states [K-1, C] bf16 and recurrent
+    states [nv, dk, dv] fp32 read from *_src and written to *_dst (the same tensors for an update in place), out
+    [R, nv * dv] bf16 (the delta rule's outputs before the gated norm)."""
+    ext().gdn_decode_step(proj, conv_w, A_log, dt_bias, list(conv_src), list(conv_dst), list(rec_src), list(rec_dst),
+                          out, int(b_off), int(a_off), int(nk), int(nv), int(dk), int(dv), int(conv_w.shape[1]))
+    return out
+
+
 def scan_groups(nv, dv, n, sms=148):
     """Chunk groups of the two-level delta-rule scan: enough (value head, 64-row slice, group) CTAs to fill about two
     waves when the heads alone leave the GPU mostly idle (tensor parallelism shrinks the heads per GPU); 1 (the
