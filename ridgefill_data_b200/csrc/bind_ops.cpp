@@ -267,6 +267,92 @@ void gdn_decode_step(Tensor proj, Tensor conv_w, Tensor A_log, Tensor dt_bias, s
   }
 }
 
+// One decode row of an attention layer for R sequences (attention_decode.cu). k / v: per sequence, its contiguous
+// [hkv, rows, hd] buffers or the pool's K / V tensors; pages: empty (contiguous) or one int32 page table per
+// sequence; rows / head_stride per sequence; part_o / part_ml the split workspace.
+void decode_attention(Tensor qkv, Tensor pos, std::vector<Tensor> k, std::vector<Tensor> v, std::vector<Tensor> pages,
+                      std::vector<int64_t> rows, std::vector<int64_t> head_stride, int64_t page_size,
+                      int64_t page_stride, OptT q_norm, OptT k_norm, int64_t norm_mode, double eps, OptT cos, OptT sin,
+                      int64_t rot, double scale, int64_t hq, int64_t hkv, int64_t hd, bool gated, Tensor out,
+                      Tensor part_o, Tensor part_ml, Tensor err) {
+  need(qkv, at::kBFloat16, "qkv");
+  need(pos, at::kInt, "pos");
+  need(out, at::kBFloat16, "out");
+  need(part_o, at::kFloat, "part_o");
+  need(part_ml, at::kFloat, "part_ml");
+  need(err, at::kInt, "err");
+  const int64_t R = qkv.size(0);
+  TORCH_CHECK(rf::decode_attention_supported((int)hd, (int)hq, (int)hkv, (int)rot), "decode_attention: dims");
+  const int64_t G = hq / hkv;
+  const int64_t qw = hq * hd * (gated ? 2 : 1);
+  TORCH_CHECK(qkv.stride(1) == 1 && qkv.size(1) >= qw + 2 * hkv * hd && pos.is_contiguous() && pos.numel() == R &&
+                  out.stride(1) == 1 && out.size(0) == R && out.size(1) == hq * hd,
+              "decode_attention: layouts");
+  const int64_t S = rf::kDecSplits;
+  TORCH_CHECK(part_o.numel() >= R * hkv * S * G * hd && part_ml.numel() >= R * hkv * S * G * 2,
+              "decode_attention: workspace");
+  TORCH_CHECK((int64_t)k.size() == R && (int64_t)v.size() == R && (int64_t)rows.size() == R &&
+                  (int64_t)head_stride.size() == R && (pages.empty() || (int64_t)pages.size() == R),
+              "decode_attention: one cache per row");
+  TORCH_CHECK(rot == 0 || (cos.has_value() && sin.has_value()), "decode_attention: RoPE tables");
+  // rows are read in hd / 32-element vectors (up to 16 bytes): 16-byte aligned bases and row pitches
+  auto aligned = [](const Tensor& t) { return reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0; };
+  TORCH_CHECK(aligned(qkv) && qkv.stride(0) % 8 == 0, "decode_attention: qkv alignment");
+  TORCH_CHECK((!q_norm.has_value() || aligned(*q_norm)) && (!k_norm.has_value() || aligned(*k_norm)),
+              "decode_attention: norm weight alignment");
+  TORCH_CHECK(norm_mode < 0 || (q_norm.has_value() && k_norm.has_value()), "decode_attention: norm weights");
+  for (int64_t r = 0; r < R; ++r) {
+    TORCH_CHECK(rows[r] > 0, "decode_attention: empty cache");
+    for (const Tensor* t : {&k[r], &v[r]}) {
+      need(*t, at::kBFloat16, "cache");
+      TORCH_CHECK(t->is_contiguous() && t->device() == qkv.device() && aligned(*t), "decode_attention: cache layout");
+    }
+    if (pages.empty()) {
+      TORCH_CHECK(head_stride[r] >= rows[r] * hd && k[r].numel() >= hkv * head_stride[r] &&
+                      v[r].numel() >= hkv * head_stride[r], "decode_attention: contiguous cache extent");
+    } else {
+      need(pages[r], at::kInt, "pages");
+      TORCH_CHECK(page_size > 0 && pages[r].numel() * page_size >= rows[r] && head_stride[r] == page_size * hd &&
+                      page_stride >= hkv * page_size * hd, "decode_attention: page table");
+    }
+  }
+  c10::cuda::CUDAGuard gd(qkv.device());
+  for (int64_t r0 = 0; r0 < R; r0 += rf::kDecodeSeqs) {
+    const int n = (int)std::min<int64_t>(rf::kDecodeSeqs, R - r0);
+    rf::DecodeAttnArgs a{};
+    a.qkv = cbf(qkv);
+    a.qkv_row = qkv.stride(0);
+    a.hq = (int)hq;
+    a.hkv = (int)hkv;
+    a.hd = (int)hd;
+    a.gated = gated ? 1 : 0;
+    a.q_norm = q_norm.has_value() ? cbf(*q_norm) : nullptr;
+    a.k_norm = k_norm.has_value() ? cbf(*k_norm) : nullptr;
+    a.norm_mode = (int)norm_mode;
+    a.eps = (float)eps;
+    a.cos = cos.has_value() ? cbf(*cos) : nullptr;
+    a.sin = sin.has_value() ? cbf(*sin) : nullptr;
+    a.rot = (int)rot;
+    a.pos = pos.data_ptr<int>();
+    a.scale_log2 = (float)(scale * 1.4426950408889634);
+    a.out = bf(out);
+    a.out_row = out.stride(0);
+    a.part_o = part_o.data_ptr<float>();
+    a.part_ml = part_ml.data_ptr<float>();
+    a.err = err.data_ptr<int>();
+    a.page_size = (int)page_size;
+    a.page_stride = page_stride;
+    for (int s = 0; s < n; ++s) {
+      a.k[s] = bf(k[r0 + s]);
+      a.v[s] = bf(v[r0 + s]);
+      a.pages[s] = pages.empty() ? nullptr : pages[r0 + s].data_ptr<int>();
+      a.rows[s] = (int)rows[r0 + s];
+      a.head_stride[s] = head_stride[r0 + s];
+    }
+    rf::decode_attention(a, (int)r0, n, cur());
+  }
+}
+
 void gdn_chunk_scan(OptT q, Tensor k, Tensor v, Tensor beta, Tensor g, Tensor state, OptT out, Tensor w_buf,
                     Tensor u_buf, OptT s_buf, OptT vt_buf, int64_t n, int64_t nk, int64_t nv, int64_t dk, int64_t dv, Tensor err,
                     int64_t groups, OptT grp_buf, OptT start_buf) {
@@ -352,6 +438,7 @@ void register_ops(pybind11::module_& m) {
   m.def("gdn_prep", &gdn_prep);
   m.def("gdn_conv_state_update", &gdn_conv_state_update);
   m.def("gdn_decode_step", &gdn_decode_step);
+  m.def("decode_attention", &decode_attention);
   m.def("gdn_chunk_scan", &gdn_chunk_scan);
   void register_comm(pybind11::module_ & m);
   register_comm(m);

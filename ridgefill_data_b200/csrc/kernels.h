@@ -146,6 +146,38 @@ struct GdnDecodeArgs {
   float* rec_dst[kDecodeSeqs];
 };
 bool gdn_decode_supported(int dk, int dv, int K);
+constexpr int kDecSplits = 64;   // key splits per (sequence, KV head) of the decode attention, at most
+// attention_decode.cu: one decode row of an attention layer for up to kDecodeSeqs sequences (K/V append at the
+// row of each sequence's device position, q / k head norm + RoPE, split-key attention, combine); sequence s of the
+// launch reads projected row r0 + s, position pos[r0 + s], and writes output row r0 + s.
+struct DecodeAttnArgs {
+  const __nv_bfloat16* qkv;      // [R, *]: q heads (each [q | gate] when gated) | k heads | v heads
+  long qkv_row;
+  int hq, hkv, hd, gated;
+  const __nv_bfloat16* q_norm;   // [hd] or nullptr
+  const __nv_bfloat16* k_norm;
+  int norm_mode;                 // -1 none, 0 plain RMSNorm, 1 zero-centred
+  float eps;
+  const __nv_bfloat16* cos;      // [max_pos, rot / 2] bf16 tables
+  const __nv_bfloat16* sin;
+  int rot;
+  const int* pos;                // [R] positions; the new K/V row of a sequence is cache row pos
+  float scale_log2;              // softmax scale times log2(e)
+  __nv_bfloat16* out;            // [R, hq * hd]
+  long out_row;
+  float* part_o;                 // [R, hkv, kDecSplits, G, hd] fp32 split partials
+  float* part_ml;                // [R, hkv, kDecSplits, G, 2] (max, sum)
+  int* err;
+  __nv_bfloat16* k[kDecodeSeqs];          // contiguous: [hkv, rows, hd] buffers; paged: the pool's K / V
+  __nv_bfloat16* v[kDecodeSeqs];
+  const int* pages[kDecodeSeqs];          // page table of the sequence, or nullptr (contiguous)
+  int rows[kDecodeSeqs];                  // rows the sequence's cache can hold
+  long head_stride[kDecodeSeqs];          // elements between KV heads (contiguous: rows * hd; paged: page_size * hd)
+  int page_size;
+  long page_stride;
+};
+bool decode_attention_supported(int hd, int hq, int hkv, int rot);
+void decode_attention(const DecodeAttnArgs& a, int r0, int rows, cudaStream_t stream);
 void gdn_decode_step(const GdnDecodeArgs& a, int r0, int rows, cudaStream_t stream);
 void gdn_conv_state_update(const __nv_bfloat16* proj, long proj_row, __nv_bfloat16* state, int n, int C, int K,
                            cudaStream_t stream);

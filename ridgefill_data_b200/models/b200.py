@@ -47,6 +47,9 @@ class _B200:
         """bf16 cos/sin tables covering positions < need (grown on demand)."""
         if self._rope_tables is None or self._rope_tables[0].shape[0] < need:
             n = max(need, 8192, 2 * (self._rope_tables[0].shape[0] if self._rope_tables else 0))
+            if self._rope_tables is not None:
+                # a captured decode graph keeps reading the tables it was captured with: they stay allocated
+                self.__dict__.setdefault("_retired_rope_tables", []).append(self._rope_tables)
             self._rope_tables = K.rope_tables(self.inv_freq, n, self.device)
         return self._rope_tables
 
@@ -181,6 +184,13 @@ class _B200:
         gated = self.cfg.gated_attn
         qw = hq * hd * (2 if gated else 1)
         p0, parr = self._span(pos)
+        if n == 1 and parr is None and c.get("n", 0) == p0 and self._attn_decode_ok():
+            # a decode row (its cache row is its position): the batched decode kernel, as decode_batch's rows
+            self._kv_reserve(c, 1, i)
+            self.rope(p0 + 1)
+            self._attn_decode(i, qkv, torch.tensor([p0], dtype=torch.int32, device=self.device), [c], o)
+            self._commit_kv(c, p0 + 1)
+            return o
         n0 = self._write_kv(i, qkv[:, qw:], pos, c)
         q = torch.empty(hq, n, hd, dtype=self.dtype, device=self.device)
         tables = self.rope(p0 + n if parr is None else int(pos.max()) + 1)
@@ -203,14 +213,24 @@ class _B200:
         R = len(toks)
         h = self.embed(torch.tensor([int(t) for t in toks], device=self.device))
         pos = [torch.tensor([int(p)], device=self.device) for p in positions]
+        pos32 = torch.tensor([int(p) for p in positions], dtype=torch.int32, device=self.device)
         for i in range(self.n_layers):
             w = self.W[i]
             x = self._norm(h, w["ln1"])
             if self.layer_types[i] == "attn":
                 qkv = G.linear(x, w["qkv_p"])
                 y = torch.empty(R, self.n_heads * self.head_dim, dtype=self.dtype, device=self.device)
-                for r in range(R):
-                    self._attn_core(i, qkv[r:r + 1], pos[r], caches[r][i], y[r:r + 1])
+                entries = [caches[r][i] for r in range(R)]
+                if self._attn_decode_ok() and all(c.get("n", 0) == int(p) for c, p in zip(entries, positions)):
+                    for c in entries:
+                        self._kv_reserve(c, 1, i)
+                    self.rope(max(int(p) for p in positions) + 1)
+                    self._attn_decode(i, qkv, pos32, entries, y)
+                    for c, p in zip(entries, positions):
+                        self._commit_kv(c, int(p) + 1)
+                else:
+                    for r in range(R):
+                        self._attn_core(i, qkv[r:r + 1], pos[r], caches[r][i], y[r:r + 1])
                 wo = w["o"]
             else:
                 proj = G.linear(x, w["in_p"])
@@ -246,8 +266,11 @@ class _B200:
             if self.layer_types[i] == "attn":
                 qkv = G.linear(x, w["qkv_p"])
                 y = torch.empty(R, self.n_heads * self.head_dim, dtype=self.dtype, device=self.device)
-                for r in range(R):
-                    self._attn_step_dev(i, qkv[r:r + 1], pos_dev[r:r + 1], caches[r][i], y[r:r + 1])
+                if self._attn_decode_ok():
+                    self._attn_decode(i, qkv, pos_dev, [caches[r][i] for r in range(R)], y)
+                else:
+                    for r in range(R):
+                        self._attn_step_dev(i, qkv[r:r + 1], pos_dev[r:r + 1], caches[r][i], y[r:r + 1])
                 wo = w["o"]
             else:
                 proj = G.linear(x, w["in_p"])
@@ -261,6 +284,33 @@ class _B200:
                 wo = w["out"]
             h = self.mlp(i, G.linear(y, wo, residual=h))
         return self.logits(h)
+
+    def _attn_decode_ok(self):
+        """Whether the batched decode attention (csrc/attention_decode.cu) serves this model's attention layers."""
+        return self.tp is None and K.decode_attention_supported(self.head_dim, self.n_heads, self.n_kv,
+                                                                self.cfg.rot_dim)
+
+    def _attn_decode(self, i, qkv, pos_dev, entries, out):
+        """One decode row per sequence of attention layer i in two launches for all of them: qkv [R, *] the
+        projected rows, pos_dev int32 [R] the positions (a sequence's new K/V row is cache row pos), entries the
+        sequences' cache entries of layer i with room for that row; the RoPE tables must reach past every
+        position. Writes out [R, hq * hd]."""
+        w = self.W[i]
+        hd, R = self.head_dim, len(entries)
+        if self.kv_pool is not None:
+            pool = self.kv_pool
+            k, v = [pool.k[i]] * R, [pool.v[i]] * R
+            pages = [c["pages_dev"] for c in entries]
+            rows = [len(c["pages"]) * pool.page_size for c in entries]
+            strides, ps, pstride = [pool.page_size * hd] * R, pool.page_size, pool.page_stride
+        else:
+            k, v = [c["kbuf"] for c in entries], [c["vbuf"] for c in entries]
+            pages, rows = [], [c["kbuf"].shape[1] for c in entries]
+            strides, ps, pstride = [n * hd for n in rows], 0, 0
+        K.decode_attention(qkv, pos_dev, k, v, pages, rows, strides, ps, pstride, self.n_heads, self.n_kv, hd,
+                           self.cfg.gated_attn, w.get("q_norm"), w.get("k_norm"), self._qk_mode(), self.eps,
+                           self._rope_tables, self.cfg.rot_dim, self.scale, out)
+        return out
 
     def _attn_step_dev(self, i, qkv, p_dev, c, o):
         """One decode row of attention layer i: K/V written at cache row p_dev[0], the query at that position over

@@ -117,6 +117,37 @@ def gdn_decode_step(proj, conv_w, A_log, dt_bias, conv_src, conv_dst, rec_src, r
     return out
 
 
+DEC_SPLITS = 64   # key splits per (sequence, KV head) of the decode attention (kDecSplits)
+
+
+def decode_attention_supported(hd, hq, hkv, rot):
+    """Shapes the batched decode attention (csrc/attention_decode.cu) takes: head_dim 64 / 128 / 256, 1, 2, 4, 6 or 8
+    query heads per KV head, rotary dims a multiple of 2 hd / 32."""
+    if hd not in (64, 128, 256) or hkv <= 0 or hq % hkv or hq // hkv not in (1, 2, 4, 6, 8):
+        return False
+    return rot == 0 or (rot <= hd and rot % (2 * (hd // 32)) == 0)
+
+
+def decode_attention(qkv, pos, k, v, pages, rows, head_stride, page_size, page_stride, hq, hkv, hd, gated, q_norm,
+                     k_norm, norm_mode, eps, tables, rot, scale, out):
+    """One decode row of an attention layer for R sequences in two launches (csrc/attention_decode.cu): qkv [R, *]
+    projected rows (q heads, each [q | gate] when gated, then k and v heads), pos int32 [R] each sequence's position
+    (its new K/V row goes to cache row pos), k / v per sequence its contiguous [hkv, rows, hd] buffers or the pool's
+    tensors, pages [] (contiguous) or one int32 page table per sequence, rows / head_stride per sequence; out
+    [R, hq * hd] bf16."""
+    R = qkv.shape[0]
+    dev = qkv.device
+    G = hq // hkv
+    part_o = torch.empty(R * hkv * DEC_SPLITS * G * hd, dtype=torch.float32, device=dev)
+    part_ml = torch.empty(R * hkv * DEC_SPLITS * G * 2, dtype=torch.float32, device=dev)
+    cos, sin = tables if (tables is not None and rot) else (None, None)
+    ext().decode_attention(qkv, pos, list(k), list(v), list(pages), [int(x) for x in rows],
+                           [int(x) for x in head_stride], int(page_size), int(page_stride), q_norm, k_norm,
+                           int(norm_mode), float(eps), cos, sin, int(rot), float(scale), int(hq), int(hkv), int(hd),
+                           bool(gated), out, part_o, part_ml, ext().error_word(dev.index or 0))
+    return out
+
+
 def scan_groups(nv, dv, n, sms=148):
     """Chunk groups of the two-level delta-rule scan: enough (value head, 64-row slice, group) CTAs to fill about two
     waves when the heads alone leave the GPU mostly idle (tensor parallelism shrinks the heads per GPU); 1 (the
