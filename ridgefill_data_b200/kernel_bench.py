@@ -2,10 +2,12 @@
 
     python -m ridgefill_data_b200.kernel_bench gemm              # two launches, no timing (ncu target)
     python -m ridgefill_data_b200.kernel_bench attn --time 10    # 3 warm-up launches, then 10 timed
+    python -m ridgefill_data_b200.kernel_bench decode_attn --m 8 --n 16384 --time 10   # 8 sequences at 16K
 
 Each workload is sized so its inputs exceed the 126 MB L2 where that is the point (GEMM, MoE) and stays a
 few GB on the device, so an ncu capture of one launch ends in seconds. Timing prints ms per launch and the
-achieved TFLOP/s (or GB/s) with the algorithmic count; the flops formulas are next to each workload.
+achieved TFLOP/s and, for the decode workloads (bound by what they read), GB/s, with the algorithmic counts next
+to each workload.
 """
 from __future__ import annotations
 
@@ -72,15 +74,65 @@ def _moe(dev, a):
     return (lambda: MO.grouped(xp, w, seg, tiles, swiglu=True)), dict(flops=2 * n * k * 2 * F * d, shape=[n, E, k, d, F])
 
 
-WORKLOADS = {"gemm": _gemm, "attn": _attn, "gdn": _gdn, "moe": _moe}
+def _gemv(dev, a):
+    """Decode-size products: m rows (1-16) against an n x k weight (the 27B MLP down projection by default)."""
+    from .ops import gemm as G
+    m, n, k = a.m or 8, a.n or 5120, a.k or 17408
+    x = torch.randn(m, k, device=dev).bfloat16()
+    w = (torch.randn(n, k, device=dev) * 0.02).bfloat16()
+    out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    return (lambda: G.linear(x, w, out=out)), dict(flops=2 * m * n * k, bytes=2 * (n * k + m * k + m * n),
+                                                   shape=[m, n, k])
+
+
+def _decode_attn(dev, a):
+    """One decode row of a 27B attention layer for m sequences at position n (contiguous caches of n + 64 rows)."""
+    from .ops import kernels as K
+    R, n = a.m or 8, a.n or 16384
+    hq, hkv, hd, rot = 24, 4, a.hd or 256, 64
+    rows = n + 64
+    qkv = torch.randn(R, hq * 2 * hd + 2 * hkv * hd, device=dev).bfloat16()
+    kb = [torch.randn(hkv, rows, hd, device=dev).bfloat16() for _ in range(R)]
+    vb = [torch.randn(hkv, rows, hd, device=dev).bfloat16() for _ in range(R)]
+    pos = torch.full((R,), n, dtype=torch.int32, device=dev)
+    qn = (torch.randn(hd, device=dev) * 0.1).bfloat16()
+    kn = (torch.randn(hd, device=dev) * 0.1).bfloat16()
+    inv_freq = 1.0 / (1e7 ** (torch.arange(0, rot, 2, dtype=torch.float32) / rot))
+    tables = K.rope_tables(inv_freq, rows, dev)
+    out = torch.empty(R, hq * hd, device=dev, dtype=torch.bfloat16)
+    run = lambda: K.decode_attention(qkv, pos, kb, vb, [], [rows] * R, [rows * hd] * R, 0, 0, hq, hkv,  # noqa: E731
+                                     hd, True, qn, kn, 1, 1e-6, tables, rot, hd ** -0.5, out)
+    return run, dict(flops=R * 4 * hq * hd * (n + 1), bytes=R * 2 * hkv * (n + 1) * hd * 2, shape=[R, n, hq, hkv, hd])
+
+
+def _gdn_decode(dev, a):
+    """One decode row of a 27B GDN layer (48 value heads of 128 x 128 fp32 state) for m sequences."""
+    from .ops import kernels as K
+    R, nv = a.m or 8, a.nv or 48
+    nk, dk, dv = max(1, nv // 3), 128, 128
+    C = 2 * nk * dk + nv * dv
+    proj = (torch.randn(R, C + 2 * nv, device=dev) * 0.5).bfloat16()
+    conv_w = (torch.randn(C, 4, device=dev) / 2).bfloat16()
+    A_log = torch.rand(nv, device=dev) * 2.7
+    dt = torch.randn(nv, device=dev) * 0.1
+    conv = [torch.randn(3, C, device=dev).bfloat16() for _ in range(R)]
+    rec = [torch.zeros(nv, dk, dv, device=dev) for _ in range(R)]
+    out = torch.empty(R, nv * dv, device=dev, dtype=torch.bfloat16)
+    run = lambda: K.gdn_decode_step(proj, conv_w, A_log, dt, conv, conv, rec, rec, out, nk, nv, dk, dv,  # noqa: E731
+                                    C, C + nv)
+    return run, dict(flops=R * 2 * 4 * nv * dk * dv, bytes=R * nv * dk * dv * 4 * 2, shape=[R, nk, nv, dk, dv])
+
+
+WORKLOADS = {"gemm": _gemm, "attn": _attn, "gdn": _gdn, "moe": _moe, "gemv": _gemv, "decode_attn": _decode_attn,
+             "gdn_decode": _gdn_decode}
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("workload", choices=sorted(WORKLOADS))
     ap.add_argument("--time", type=int, default=0, help="timed launches (0: two untimed launches only)")
-    ap.add_argument("--m", type=int, default=0)
-    ap.add_argument("--n", type=int, default=0)
+    ap.add_argument("--m", type=int, default=0, help="rows (gemm, gemv) or sequences (decode_attn, gdn_decode)")
+    ap.add_argument("--n", type=int, default=0, help="columns (gemm, gemv), tokens, or the decode position")
     ap.add_argument("--k", type=int, default=0)
     ap.add_argument("--hd", type=int, default=0)
     ap.add_argument("--impl", default="auto", help="attention: auto | mma | tcgen05")
@@ -112,9 +164,11 @@ def main(argv=None):
         ms.append(s.elapsed_time(e))
     ms.sort()
     med = ms[len(ms) // 2]
-    print(json.dumps(dict(workload=a.workload, ms_median=round(med, 4), ms_min=round(ms[0], 4),
-                          tflops=round(info["flops"] / med / 1e9, 1), l2="flushed (256 MB write) before each launch",
-                          **info)))
+    rate = dict(tflops=round(info["flops"] / med / 1e9, 1))
+    if "bytes" in info:
+        rate["gbs"] = round(info["bytes"] / med / 1e6, 1)
+    print(json.dumps(dict(workload=a.workload, ms_median=round(med, 4), ms_min=round(ms[0], 4), **rate,
+                          l2="flushed (256 MB write) before each launch", **info)))
 
 
 if __name__ == "__main__":

@@ -202,12 +202,13 @@ class _B200:
 
     def decode_batch(self, toks, positions, caches):
         """R sequences advanced by one token each in one pass over the weights: the embedding, every projection,
-        MLP (or MoE) and the logits run on the R stacked rows; only the per-sequence parts (K/V append and
-        attention over that sequence's cache, the GDN conv and recurrent step on its state) run per row. Products of
-        1-16 rows take the tensor-core GEMV (csrc/gemv.cu) and larger ones the tile GEMMs; each sums every row the
-        same way whatever the row count, so each row equals the single-sequence step bitwise. The CUDA-core GEMV
-        (set_gemv_mma(False), 1-2 rows) sums in another order than the tile GEMMs, so with it a single step differs
-        from a batched row by bf16 rounding."""
+        MLP (or MoE) and the logits run on the R stacked rows, and the per-sequence parts run for all sequences in
+        two launches per layer: K/V append and attention over each sequence's cache (csrc/attention_decode.cu), the
+        GDN conv and recurrent step on each sequence's state (csrc/gdn_decode.cu); shapes those kernels do not take
+        run per sequence. Products of 1-16 rows take the tensor-core GEMV (csrc/gemv.cu) and larger ones the tile
+        GEMMs; every kernel computes a row the same way whatever the batch, so each row equals the single-sequence
+        step bitwise. The CUDA-core GEMV (set_gemv_mma(False), 1-2 rows) sums in another order than the tile GEMMs,
+        so with it a single step differs from a batched row by bf16 rounding."""
         if self.tp is not None or len(toks) == 1:
             return super().decode_batch(toks, positions, caches)
         R = len(toks)
