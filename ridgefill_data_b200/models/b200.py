@@ -341,9 +341,12 @@ class _B200:
                     gate_head=2 * hd, pages=c["pages_dev"] if self.kv_pool is not None else None)
 
     def _gdn_decode_ok(self, entries):
-        """Whether the batched decode step (csrc/gdn_decode.cu) serves these cache entries of one GDN layer: head dims
-        128, fp32 recurrent states and conv windows already there (a prefill made them)."""
+        """Whether the batched decode step (csrc/gdn_decode.cu) serves these cache entries of one GDN layer: one GPU
+        (tensor-parallel ranks keep the per-sequence path), head dims 128, fp32 recurrent states and conv windows
+        already there (a prefill made them)."""
         cfg = self.cfg
+        if self.tp is not None:
+            return False
         if not K.gdn_decode_supported(cfg.gdn_dk, cfg.gdn_dv, cfg.conv_k) or self.nv % self.nk:
             return False
         if self.conv_dim != 2 * self.nk * cfg.gdn_dk + self.nv * cfg.gdn_dv:
