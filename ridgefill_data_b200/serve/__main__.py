@@ -2,15 +2,21 @@
 
     python -m ridgefill_data_b200.serve --model qwen3.8-27b --synthetic-maps --port 8080          # random-init shape
     python -m ridgefill_data_b200.serve --checkpoint DIR --maps maps.safetensors --tokenizer DIR   # a real model
+    python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 -m ridgefill_data_b200.serve ...
+                                                 # tensor parallel over 2 GPUs: rank 0 serves HTTP, all ranks compute
 
 Modes per request (`ridgefill_mode`): "on" = RidgeFill (split / tail of the maps or the flags), "quality" = RidgeFill
 with exact prefix rows (engine/quality.py: digit / special tokens, repeated spans of the prompt's end, the rows the
 prompt's end attends to most; exact prefill below --min-prompt), "off" = exact prefill. Decoding is always exact and
 greedy.
+
+Under torchrun with several ranks the model is sharded over them (parallel/tp.py) and served in lockstep
+(serve/lockstep.py): rank 0 runs the HTTP server and the scheduler, the other ranks run every model call with it.
 """
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 
 
@@ -90,9 +96,13 @@ def main(argv=None):
     ap.add_argument("--decode-gap-ms", type=float, default=100.0,
                     help="target gap between a running stream's tokens while a prompt is prefilled: each prefill's "
                          "decode-round period follows its size (0: every --interleave layers)")
+    ap.add_argument("--tp-comm", default="nvls", choices=("nccl", "fused", "nvls"),
+                    help="tensor parallel (under torchrun with several ranks): the all-reduce / all-gather kernels")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8080)
     a = ap.parse_args(argv)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        return main_tp(a)
     from .app import Server, create_app
     from .engine import Scheduler
     model, arms, tok, eos, props = build(a)
@@ -102,6 +112,50 @@ def main(argv=None):
         Server(create_app(sched, arms, tok, props), a.host, a.port, log_level="info").run()
     finally:
         sched.stop()
+    return 0
+
+
+def main_tp(a):
+    """One rank of a tensor-parallel server (torchrun): the model sharded over the ranks, rank 0 serving HTTP."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from ..parallel.tp import TensorParallel, shard
+    from .app import Server, create_app
+    from .engine import Scheduler
+    from .lockstep import Lockstep, serve_worker
+    if a.kv_pages:
+        raise SystemExit("--kv-pages serves one GPU; a tensor-parallel server keeps a K/V cache per request")
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    control = dist.new_group(backend="gloo")          # the lockstep commands: small host objects
+    a.device = f"cuda:{local}"
+    model, arms, tok, eos, props = build(a)
+    try:
+        tp = TensorParallel(mode=a.tp_comm, fill="rows" if world >= 8 else "columns")
+    except Exception as e:                            # no NVSwitch multicast here: NCCL
+        if a.tp_comm != "nvls":
+            raise
+        print(f"nvls unavailable ({e}); using nccl", file=sys.stderr)
+        tp = TensorParallel(mode="nccl", fill="rows" if world >= 8 else "columns")
+    shard(model, tp)
+    lockstep = Lockstep(control, arms)
+    try:
+        if rank == 0:
+            sched = Scheduler(model, eos=eos, interleave=0, graphs=False, lockstep=lockstep).start()
+            try:
+                Server(create_app(sched, arms, tok, dict(props, tensor_parallel=world)), a.host, a.port,
+                       log_level="info").run()
+            finally:
+                sched.stop()
+        else:
+            serve_worker(model, lockstep)
+    finally:
+        tp.close()
+        dist.destroy_process_group()
     return 0
 
 

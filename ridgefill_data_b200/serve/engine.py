@@ -10,7 +10,9 @@ runs one decode round for the other requests, so their inter-token gap during a 
 that prefill instead of all of it (the quantity the fixed-arrival mix measures). k is `interleave`, or with
 `gap_ms` it is sized to the prefill: gap_ms / (rows x the per-row, per-layer cost learned from large prefills that
 ran alone), so a short prompt runs uninterrupted and a long one yields about every gap_ms. Under
-tensor parallelism the layer outputs live in rotating collective buffers, so interleaving is off there.
+tensor parallelism the layer outputs live in rotating collective buffers, so interleaving is off there; a
+tensor-parallel model is served by this scheduler on rank 0 with `lockstep` (serve/lockstep.py), which has every
+other rank make the same model calls.
 
 Events are plain dicts handed to the request's `emit` callback from the worker thread, in the field layout of the
 llama.cpp server's `/completion` stream (kept alike so the 27B kit's clients read them unchanged):
@@ -33,6 +35,22 @@ import torch
 from ..engine import decode as D
 from ..engine.arm import Arm
 from ..engine.prefill import finish, run_lower
+
+
+def prefill_request(model, ids, arm, n_predict, tick=None):
+    """The model work of one request's prefill (every rank of a lockstep group runs it alike): (logits row of the
+    first token [V], cache, prompt rows filled from the maps)."""
+    quality = arm.meta.get("quality")
+    if quality is not None:
+        from ..engine.quality import prefill_quality
+        logits, cache, P, rows = prefill_quality(model, ids, arm, quality, keep=1, reserve=n_predict + 64, tick=tick)
+        return logits[-1], cache, int(P) - len(rows)
+    if arm.fill == "exact" or arm.split is None:
+        hs, cache = run_lower(model, ids, [model.n_layers], tick=tick, reserve=n_predict + 64)
+        return model.logits(hs[model.n_layers][-1:])[-1], cache, 0
+    hs, lower = run_lower(model, ids, [arm.split], tick=tick, reserve=n_predict + 64, maps=arm.projector)
+    logits, cache, P = finish(model, ids, hs[arm.split], lower, arm, keep=1, tick=tick)
+    return logits[-1], cache, int(P)
 
 
 @dataclass
@@ -59,8 +77,11 @@ class Request:
 
 class Scheduler:
     def __init__(self, model, eos=(), interleave=4, max_active=64, max_batch=32, sync=None, gap_ms=0.0,
-                 sample_rows=4096, graphs=True, graph_min_tokens=8):
+                 sample_rows=4096, graphs=True, graph_min_tokens=8, lockstep=None):
         self.model = model
+        # lockstep: a serve.lockstep.Lockstep when the model is sharded over ranks (this scheduler runs on rank 0
+        # and every model call is mirrored on the others)
+        self.lockstep = lockstep
         self.eos = frozenset(int(e) for e in eos)
         self.interleave = int(interleave)
         # gap_ms > 0: the decode-round period of a prefill follows its size, so that the running streams wait about
@@ -72,7 +93,7 @@ class Scheduler:
         self._row_layer_ms = None
         # decode rounds as CUDA-graph replays (engine/decode_graph.py) while the set of running requests stays the
         # same; a new graph is captured when it changes and every request has graph_min_tokens or more to go
-        self.graphs = bool(graphs) and model.device.type == "cuda"
+        self.graphs = bool(graphs) and model.device.type == "cuda" and lockstep is None
         self.graph_min_tokens = int(graph_min_tokens)
         self._graph = None
         self._graph_key = None
@@ -148,6 +169,8 @@ class Scheduler:
             elif not started:
                 self._wake.wait(0.05)
                 self._wake.clear()
+        if self.lockstep is not None:
+            self.lockstep.command("stop")
 
     def period_for(self, rows):
         """Prefill layers between decode rounds for a prompt of `rows` tokens."""
@@ -157,7 +180,7 @@ class Scheduler:
 
     def _tick_for(self, owner):
         """tick(i) for the prefill of `owner`: a decode round of the running streams every period_for(rows) layers."""
-        if self.interleave <= 0 or getattr(self.model, "tp", None) is not None:
+        if self.interleave <= 0 or getattr(self.model, "tp", None) is not None or self.lockstep is not None:
             return None
         count = itertools.count(1)
         period = self.period_for(int(owner.ids.numel()))
@@ -184,30 +207,25 @@ class Scheduler:
         pool = getattr(model, "kv_pool", None)
         if pool is not None:
             pool.owner = req.rid                       # pages taken during this prefill belong to the request
+        err, sent = None, False
         try:
-            ids = req.ids.to(model.device)
-            quality = arm.meta.get("quality")
-            if quality is not None:
-                from ..engine.quality import prefill_quality
-                logits, cache, P, rows = prefill_quality(model, ids, arm, quality, keep=1,
-                                                         reserve=req.n_predict + 64, tick=tick)
-                req.filled, hs = int(P) - len(rows), None
-            elif arm.fill == "exact" or arm.split is None:
-                hs, cache = run_lower(model, ids, [model.n_layers], tick=tick, reserve=req.n_predict + 64)
-                logits = model.logits(hs[model.n_layers][-1:])
-                req.filled = 0
-            else:
-                hs, lower = run_lower(model, ids, [arm.split], tick=tick, reserve=req.n_predict + 64,
-                                      maps=arm.projector)
-                logits, cache, P = finish(model, ids, hs[arm.split], lower, arm, keep=1, tick=tick)
-                req.filled = int(P)
-            del hs
-            tok = int(D.check_finite(logits[-1], f"{req.rid} first token").argmax())
+            if self.lockstep is not None:
+                key = self.lockstep.key_of(arm)        # before the command: an unknown arm reaches no rank
+                self.lockstep.command("prefill", req.rid, req.ids, req.n_predict, key)
+                sent = True
+            row, cache, req.filled = prefill_request(model, req.ids.to(model.device), arm, req.n_predict, tick)
+            tok = int(D.check_finite(row, f"{req.rid} first token").argmax())
         except Exception as e:                         # report, drop the request, keep serving
+            err = e
+        if sent and not self.lockstep.agree(err is None) and err is None:
+            err = RuntimeError("the prefill failed on another rank")
+        if err is not None:
             self.stats["errors"] += 1
             if pool is not None:
                 pool.release_owner(req.rid)
-            self._emit(req, {"error": f"{type(e).__name__}: {e}", "stop": True})
+            if sent:
+                self.lockstep.command("release", req.rid)
+            self._emit(req, {"error": f"{type(err).__name__}: {err}", "stop": True})
             return
         now = time.perf_counter()
         req.cache, req.position, req.t_first, req.t_last = cache, n, now, now
@@ -287,6 +305,9 @@ class Scheduler:
         toks = {}
         for j in range(0, len(plain), self.max_batch):
             grp = plain[j:j + self.max_batch]
+            if self.lockstep is not None:
+                self.lockstep.command("decode", [r.rid for r in grp], [r.tok for r in grp], [r.position for r in grp])
+            err = None
             try:
                 g = self._graph_for(grp) if len(plain) <= self.max_batch else None
                 if g is not None:
@@ -296,17 +317,25 @@ class Scheduler:
                     logits = self.model.decode_batch([r.tok for r in grp], [r.position for r in grp],
                                                      [r.cache for r in grp])
                 self.stats["decode_batches"] += 1
-                for r, row in zip(grp, logits):
-                    toks[id(r)] = row
             except Exception as e:          # a failed batch may have appended to some caches: end its requests
-                for r in grp:
-                    toks[id(r)] = e
+                err = e
+            if self.lockstep is not None and not self.lockstep.agree(err is None) and err is None:
+                err = RuntimeError("the decode batch failed on another rank")
+            for j, r in enumerate(grp):
+                toks[id(r)] = err if err is not None else logits[j]
         for r in reqs:
             if r.arm.fill == "swiftkv_native":
+                if self.lockstep is not None:
+                    self.lockstep.command("step", r.rid, r.tok, r.position, self.lockstep.key_of(r.arm))
+                err = None
                 try:
                     toks[id(r)] = D.step(self.model, r.tok, r.position, r.cache, r.arm)[-1]
                 except Exception as e:
-                    toks[id(r)] = e
+                    err = e
+                if self.lockstep is not None and not self.lockstep.agree(err is None) and err is None:
+                    err = RuntimeError("the decode step failed on another rank")
+                if err is not None:
+                    toks[id(r)] = err
         keep = []
         for req in reqs:
             row = toks[id(req)]
@@ -337,6 +366,8 @@ class Scheduler:
             pool.release(req.cache)
             pool.release_owner(req.rid)
         req.cache = None
+        if self.lockstep is not None:
+            self.lockstep.command("release", req.rid)
 
     def _final(self, req):
         n = int(req.ids.numel())
