@@ -9,12 +9,19 @@ POST /completion  {"prompt": [ids] | "text", "n_predict": 16, "stream": false, "
   stream=true  -> text/event-stream, one `data: {event}` per token and the final event (see serve/engine.py).
 OpenAI-compatible (the API the c5 kit's client and the LongBench v2 runner speak):
   GET  /v1/models
-  POST /v1/completions       {"prompt": "text" | [ids], "max_tokens", "stream", "stop", "ridgefill_mode"}
+  POST /v1/completions       {"prompt": "text" | [ids], "max_tokens", "stream", "stop", "ridgefill_mode",
+                              "prompt_logprobs": k (vLLM's field: the log-prob and rank of every prompt token given
+                              its prefix, plus the k most likely tokens), "vllm_xargs": {"dyluhn_kva": "0" | "1",
+                              "dyluhn_kva_tail": T} (the c5 kit's per-request RidgeFill switch: off / on)}
   POST /v1/chat/completions  {"messages": [...], "max_tokens", "stream", "stop", "ridgefill_mode"} (the tokenizer's
                              chat template renders the prompt)
   Responses carry choices[0].text / .message.content, finish_reason ("stop" | "length") and usage token counts;
   streams are chunk objects ending with `data: [DONE]`. Greedy decoding only. Text is detokenized incrementally
   (the decoded prefix grows; a trailing partial character is held back), so multi-byte pieces stream correctly.
+  prompt_logprobs: choices[0].prompt_logprobs holds one entry per prompt token, the first None, the others
+  {str(id): {"logprob", "rank", "decoded_token"}} (and the k alternatives). Only rows that run through every layer
+  have logits: under RidgeFill those are the exact tail, so the entries of the filled prefix carry "logprob": null
+  (as do positions before the last MAX_SCORED_ROWS); an exact request scores every position.
 """
 from __future__ import annotations
 
@@ -89,10 +96,58 @@ def _greedy_only(body):
 
 
 def _mode(body, arms):
-    mode = body.get("ridgefill_mode", "on" if body.get("ridgefill", True) else "off")
+    xargs = body.get("vllm_xargs") or {}
+    if not isinstance(xargs, dict):
+        raise BadRequest("vllm_xargs: an object")
+    default = "on" if body.get("ridgefill", True) else "off"
+    if "dyluhn_kva" in xargs:                           # the c5 kit's switch: "1" RidgeFill, "0" exact
+        default = "on" if str(xargs["dyluhn_kva"]) == "1" else "off"
+    mode = body.get("ridgefill_mode", default)
     if mode not in arms:
         raise BadRequest(f"ridgefill_mode {mode!r}: one of {sorted(arms)}")
+    if "dyluhn_kva_tail" in xargs and mode != "off":
+        tail = getattr(arms[mode], "tail", None)
+        if tail is None or int(xargs["dyluhn_kva_tail"]) != int(tail):
+            raise BadRequest(f"dyluhn_kva_tail {xargs['dyluhn_kva_tail']}: this server's RidgeFill tail is {tail}")
+    if float(body.get("repetition_penalty", 1.0) or 1.0) != 1.0:
+        raise BadRequest("repetition_penalty: only 1.0 (greedy decoding) is served")
     return arms[mode]
+
+
+def _prompt_logprobs(body):
+    """-1 when the request asks for no prompt log-probs, else the number of alternatives per position (<= 20)."""
+    v = body.get("prompt_logprobs")
+    if v is None or v is False:
+        return -1
+    try:
+        k = int(v)
+    except (TypeError, ValueError):
+        raise BadRequest("prompt_logprobs: an integer")
+    if not 0 <= k <= 20:
+        raise BadRequest("prompt_logprobs: 0 to 20 alternatives")
+    return k
+
+
+def prompt_logprob_entries(ids, scores, tokenizer=None):
+    """vLLM's prompt_logprobs list from the scheduler's (first scored position, [(logprob, rank, alternatives)])."""
+    ids = [int(t) for t in ids]
+    first, vals = scores
+
+    def piece(t):                                       # JSON-safe text (a lone surrogate becomes U+FFFD)
+        if tokenizer is None:
+            return None
+        return tokenizer.decode([t]).encode("utf-8", "replace").decode("utf-8")
+    out = [None]
+    for i in range(1, len(ids)):
+        t = ids[i]
+        if i < first:
+            out.append({str(t): dict(logprob=None, rank=None, decoded_token=piece(t))})
+            continue
+        lp, rank, alts = vals[i - first]
+        e = {str(a): dict(logprob=float(alp), rank=r + 1, decoded_token=piece(a)) for r, (a, alp) in enumerate(alts)}
+        e[str(t)] = dict(logprob=float(lp), rank=int(rank), decoded_token=piece(t))
+        out.append(e)
+    return out
 
 
 def _stops(body):
@@ -119,10 +174,10 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
         return JSONResponse({"error": {"code": code, "message": msg, "type": "invalid_request_error"}},
                             status_code=code)
 
-    def submit(ids, n_predict, arm, ignore_eos=False):
+    def submit(ids, n_predict, arm, ignore_eos=False, prompt_logprobs=-1):
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
-        req = Request(ids=ids, n_predict=n_predict, arm=arm, ignore_eos=ignore_eos,
+        req = Request(ids=ids, n_predict=n_predict, arm=arm, ignore_eos=ignore_eos, prompt_logprobs=prompt_logprobs,
                       emit=lambda ev: loop.call_soon_threadsafe(q.put_nowait, ev))
         scheduler.submit(req)
         return req, q
@@ -133,8 +188,9 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
         if n_predict < 1:
             raise BadRequest("max_tokens must be at least 1")
         stops = _stops(body)
+        plp = _prompt_logprobs(body) if kind == "text" else -1
         try:
-            req, q = submit(ids, n_predict, arm)
+            req, q = submit(ids, n_predict, arm, prompt_logprobs=plp)
         except ValueError as e:
             raise BadRequest(str(e))
         rid = ("chatcmpl-" if kind == "chat" else "cmpl-") + uuid.uuid4().hex[:24]
@@ -182,6 +238,10 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
             n_out = final.get("tokens_predicted", 0) if final else 0
             return dict(prompt_tokens=int(ids.numel()), completion_tokens=n_out, total_tokens=int(ids.numel()) + n_out)
 
+        def add_prompt_logprobs(choice, final):
+            if plp >= 0 and final is not None and "prompt_scores" in final:
+                choice["prompt_logprobs"] = prompt_logprob_entries(ids, final["prompt_scores"], tokenizer)
+
         if body.get("stream"):
             async def events():
                 first = True
@@ -191,6 +251,7 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
                             c = chunk(delta, finish, first)
                             if finish:
                                 c["usage"] = usage(final)
+                                add_prompt_logprobs(c["choices"][0], final)
                             yield "data: " + json.dumps(c) + "\n\n"
                             first = False
                 except RuntimeError as e:
@@ -207,6 +268,7 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
         text = "".join(out)
         choice = (dict(index=0, message=dict(role="assistant", content=text), finish_reason=finish)
                   if kind == "chat" else dict(index=0, text=text, finish_reason=finish, logprobs=None))
+        add_prompt_logprobs(choice, final)
         return dict(id=rid, object=obj, created=created, model=model_name, choices=[choice], usage=usage(final))
 
     @app.get("/v1/models")

@@ -37,20 +37,51 @@ from ..engine.arm import Arm
 from ..engine.prefill import finish, run_lower
 
 
-def prefill_request(model, ids, arm, n_predict, tick=None):
-    """The model work of one request's prefill (every rank of a lockstep group runs it alike): (logits row of the
-    first token [V], cache, prompt rows filled from the maps)."""
+MAX_SCORED_ROWS = 4096      # prompt positions a request can have scored (prompt_logprobs): the last ones
+
+
+def prefill_request(model, ids, arm, n_predict, tick=None, keep=1):
+    """The model work of one request's prefill (every rank of a lockstep group runs it alike): (logits [k, V] of the
+    last k <= keep prompt rows, the last one giving the first token; cache; prompt rows filled from the maps). A
+    RidgeFill arm has logits only for its tail rows (the rows run through every layer), so k is at most the tail."""
     quality = arm.meta.get("quality")
+    n = int(ids.numel())
     if quality is not None:
         from ..engine.quality import prefill_quality
-        logits, cache, P, rows = prefill_quality(model, ids, arm, quality, keep=1, reserve=n_predict + 64, tick=tick)
-        return logits[-1], cache, int(P) - len(rows)
+        if n >= quality.min_prompt and arm.split is not None:
+            keep = max(1, min(keep, n - arm.prefix_len(n)))
+        logits, cache, P, rows = prefill_quality(model, ids, arm, quality, keep=keep, reserve=n_predict + 64,
+                                                 tick=tick)
+        return logits, cache, int(P) - len(rows)
     if arm.fill == "exact" or arm.split is None:
         hs, cache = run_lower(model, ids, [model.n_layers], tick=tick, reserve=n_predict + 64)
-        return model.logits(hs[model.n_layers][-1:])[-1], cache, 0
+        return model.logits(hs[model.n_layers][-keep:]), cache, 0
+    keep = max(1, min(keep, n - arm.prefix_len(n)))
     hs, lower = run_lower(model, ids, [arm.split], tick=tick, reserve=n_predict + 64, maps=arm.projector)
-    logits, cache, P = finish(model, ids, hs[arm.split], lower, arm, keep=1, tick=tick)
-    return logits[-1], cache, int(P)
+    logits, cache, P = finish(model, ids, hs[arm.split], lower, arm, keep=keep, tick=tick)
+    return logits, cache, int(P)
+
+
+def score_prompt(logits, ids, top=0, chunk=256):
+    """Teacher-forced scores of the prompt positions that `logits` (the last k rows' logits) predict: row j scores
+    prompt token n - k + 1 + j. Returns (first scored position, [(logprob, rank, [(id, logprob)] * top)]); rank is
+    1 + the number of tokens the row gives a higher log-prob (the vLLM prompt_logprobs fields)."""
+    n, k = int(ids.numel()), int(logits.shape[0])
+    m = k - 1
+    out = []
+    tgt_all = ids[n - m:].to(logits.device)
+    for c0 in range(0, m, chunk):
+        lp = logits[c0:min(m, c0 + chunk)].float().log_softmax(-1)
+        tgt = tgt_all[c0:c0 + lp.shape[0]]
+        tl = lp.gather(1, tgt[:, None])[:, 0]
+        rank = (lp > tl[:, None]).sum(-1) + 1
+        alts = lp.topk(top, -1) if top > 0 else None
+        tl, rank = tl.tolist(), rank.tolist()
+        av = (alts.values.tolist(), alts.indices.tolist()) if alts is not None else None
+        for j in range(lp.shape[0]):
+            out.append((tl[j], int(rank[j]),
+                        list(zip(av[1][j], av[0][j])) if av is not None else []))
+    return n - m, out
 
 
 @dataclass
@@ -73,6 +104,8 @@ class Request:
     t_last: float = 0.0
     filled: int = 0
     cancelled: bool = False
+    prompt_logprobs: int = -1               # >= 0: score the prompt (that many top alternatives per position)
+    prompt_scores: object = None            # (first scored position, [(logprob, rank, alternatives)])
 
 
 class Scheduler:
@@ -208,13 +241,18 @@ class Scheduler:
         if pool is not None:
             pool.owner = req.rid                       # pages taken during this prefill belong to the request
         err, sent = None, False
+        keep = 1 if req.prompt_logprobs < 0 else min(n, MAX_SCORED_ROWS + 1)
         try:
             if self.lockstep is not None:
                 key = self.lockstep.key_of(arm)        # before the command: an unknown arm reaches no rank
-                self.lockstep.command("prefill", req.rid, req.ids, req.n_predict, key)
+                self.lockstep.command("prefill", req.rid, req.ids, req.n_predict, key, keep)
                 sent = True
-            row, cache, req.filled = prefill_request(model, req.ids.to(model.device), arm, req.n_predict, tick)
-            tok = int(D.check_finite(row, f"{req.rid} first token").argmax())
+            logits, cache, req.filled = prefill_request(model, req.ids.to(model.device), arm, req.n_predict, tick,
+                                                        keep=keep)
+            tok = int(D.check_finite(logits[-1], f"{req.rid} first token").argmax())
+            if req.prompt_logprobs >= 0:
+                req.prompt_scores = score_prompt(logits, req.ids, req.prompt_logprobs)
+            del logits
         except Exception as e:                         # report, drop the request, keep serving
             err = e
         if sent and not self.lockstep.agree(err is None) and err is None:
@@ -389,9 +427,11 @@ class Scheduler:
         self._release(req)
         with self._lock:
             self.stats["completed"] += 1
-        self._emit(req, {"tokens": [], "content": "", "stop": True, "stop_type": stop_type,
-                         "tokens_predicted": pred, "tokens_evaluated": n, "truncated": False, "id": req.rid,
-                         "timings": timings})
+        final = {"tokens": [], "content": "", "stop": True, "stop_type": stop_type, "tokens_predicted": pred,
+                 "tokens_evaluated": n, "truncated": False, "id": req.rid, "timings": timings}
+        if req.prompt_scores is not None:
+            final["prompt_scores"] = req.prompt_scores
+        self._emit(req, final)
 
     # ---- metrics (Prometheus text exposition)
     def metrics_text(self):

@@ -12,7 +12,7 @@ group's timeout ends the job (the host-side failure detection of parallel/health
 where they are made; a worker keeps them by request id.
 
 Commands, all from the scheduler's one worker thread:
-  ("prefill", rid, ids, n_predict, arm_key)   then agree
+  ("prefill", rid, ids, n_predict, arm_key, keep)   then agree   (keep: prompt rows whose logits are computed)
   ("decode", [rid], [tok], [position])        then agree
   ("step", rid, tok, position, arm_key)       then agree   (SwiftKV-native requests)
   ("release", rid)
@@ -87,10 +87,10 @@ def serve_worker(model, lockstep, log=None):
         try:
             with torch.no_grad():
                 if op == "prefill":
-                    _, rid, ids, n_predict, key = cmd
+                    _, rid, ids, n_predict, key, keep = cmd
                     if pool is not None:
                         pool.owner = rid
-                    _, cache, _ = prefill_request(model, ids.to(model.device), arms[key], n_predict)
+                    _, cache, _ = prefill_request(model, ids.to(model.device), arms[key], n_predict, keep=keep)
                     caches[rid] = cache
                 elif op == "decode":
                     _, rids, toks, positions = cmd

@@ -326,3 +326,39 @@ def test_scheduler_graph_policy_with_a_stand_in_graph(setup, monkeypatch):
     monkeypatch.setattr(DGM, "DecodeGraph", Broken)
     sched_b, toks_b = run(True)
     assert toks_b == toks_e and sched_b.graphs is False and sched_b.stats["graph_captures"] == 0
+
+
+def test_prompt_logprobs_and_the_c5_switch(text_server):
+    """vLLM's prompt_logprobs on /v1/completions: an exact request scores every position (against the model's own
+    teacher-forced log-softmax), a RidgeFill request scores its exact tail and leaves the filled prefix null; the
+    c5 kit's vllm_xargs switch picks the mode, and a tail other than the server's is refused."""
+    url, model, arms, tok = text_server
+    g = torch.Generator().manual_seed(21)
+    ids = torch.randint(20, CFG.vocab, (48,), generator=g)
+    body = dict(prompt=ids.tolist(), max_tokens=2, temperature=0, prompt_logprobs=2, cache_salt="x",
+                repetition_penalty=1.0, skip_special_tokens=True)
+    for kva, arm in (("0", arms["off"]), ("1", arms["on"])):
+        r = C.post_json(url, "/v1/completions", dict(body, vllm_xargs=dict(dyluhn_kva=kva, dyluhn_kva_tail=TAIL)))
+        entries = r["choices"][0]["prompt_logprobs"]
+        assert len(entries) == ids.numel() == r["usage"]["prompt_tokens"] and entries[0] is None
+        n = ids.numel()
+        k = n if arm is arms["off"] else n - arm.prefix_len(n)
+        logits, _, _ = prefill(model, ids, arm, keep=k)
+        lp = logits[:-1].double().log_softmax(-1)
+        lp32 = logits[:-1].float().log_softmax(-1)            # the server ranks in fp32
+        first = n - (k - 1)
+        for i in range(1, n):
+            e = entries[i][str(int(ids[i]))]
+            if i < first:
+                assert e["logprob"] is None
+                continue
+            row = lp[i - first]
+            assert abs(e["logprob"] - float(row[ids[i]])) < 1e-4
+            r32 = lp32[i - first]
+            assert e["rank"] == int((r32 > r32[ids[i]]).sum()) + 1
+            assert len(entries[i]) >= 2 and len(entries[i]) <= 3           # the prompt token and 2 alternatives
+        assert (first == 1) == (arm is arms["off"])
+    with pytest.raises(Exception, match="400"):
+        C.post_json(url, "/v1/completions", dict(body, vllm_xargs=dict(dyluhn_kva="1", dyluhn_kva_tail=TAIL + 1)))
+    with pytest.raises(Exception, match="400"):
+        C.post_json(url, "/v1/completions", dict(body, prompt_logprobs=99))
