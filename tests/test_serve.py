@@ -362,3 +362,32 @@ def test_prompt_logprobs_and_the_c5_switch(text_server):
         C.post_json(url, "/v1/completions", dict(body, vllm_xargs=dict(dyluhn_kva="1", dyluhn_kva_tail=TAIL + 1)))
     with pytest.raises(Exception, match="400"):
         C.post_json(url, "/v1/completions", dict(body, prompt_logprobs=99))
+
+
+def test_locked_set_client_over_the_openai_api(text_server, tmp_path):
+    """serve/sets.py (the c5 kit client's role) against the server: the ppl continuation NLL equals the model's own
+    teacher-forced NLL for RidgeFill and exact requests, a RULER-style prompt gets the greedy completion and its
+    score, speed rounds time the arm and the exact path, and samples resume from their sidecars."""
+    from ridgefill_data_b200.serve import sets as SE
+    url, model, arms, tok = text_server
+    g = torch.Generator().manual_seed(23)
+    ids = torch.randint(20, CFG.vocab, (48,), generator=g)
+    doc = dict(name="d0", ids=ids.tolist(), cont_len=10, novel=[j % 3 != 0 for j in range(10)])
+    for kva, arm in ((1, arms["on"]), (0, arms["off"])):
+        rec = SE.run_ppl(SE.Endpoint(url, kva=kva, tail=TAIL), doc)
+        logits, _, _ = prefill(model, ids, arm, keep=11)
+        lp = logits[:-1].double().log_softmax(-1)
+        want = [-float(lp[j, ids[38 + j]]) for j in range(10)]
+        assert rec["cont_len"] == 10 and rec["n_novel"] == 6
+        assert max(abs(a - b) for a, b in zip(rec["token_nll"], want)) < 1e-4
+        assert abs(rec["nll"] - sum(want) / 10) < 1e-4
+    ep = SE.Endpoint(url, kva=1, tail=TAIL)
+    q = dict(name="r0", set="ruler", ids=ids[:30].tolist(), max_new=4, metric="string_match_all", refs=["zz"])
+    rec = SE.run_ruler(ep, q)
+    assert rec["text"] == tok.decode(_expected(model, arms["on"], ids[:30], 4), skip_special_tokens=True)
+    assert rec["score"] in (0.0, 1.0) and rec["metric"] == "string_match_all"
+    rows = SE.run_speed(ep, ids.tolist(), [20, 40], runs=2)
+    assert [r["length"] for r in rows] == [20, 40]
+    assert all(len(r["ttft_s"]["arm"]) == len(r["ttft_s"]["exact"]) == 2 and r["speedup_median"] > 0 for r in rows)
+    assert SE.save(tmp_path, "ppl", "d0", dict(x=1)) and SE.done(tmp_path, "ppl", "d0")
+    assert not SE.save(tmp_path, "ppl", "d0", dict(x=2))
