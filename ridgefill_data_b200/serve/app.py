@@ -15,7 +15,8 @@ OpenAI-compatible (the API the c5 kit's client and the LongBench v2 runner speak
                               "dyluhn_kva_tail": T} (the c5 kit's per-request RidgeFill switch: off / on)}
   POST /v1/chat/completions  {"messages": [...], "max_tokens", "stream", "stop", "ridgefill_mode"} (the tokenizer's
                              chat template renders the prompt)
-  Responses carry choices[0].text / .message.content, finish_reason ("stop" | "length") and usage token counts;
+  Responses carry choices[0].text / .message.content, finish_reason ("stop" | "length") and usage token counts
+  (plus prompt_filled_tokens, the prompt rows approximated from the maps: the request's real tail is the rest);
   streams are chunk objects ending with `data: [DONE]`. Greedy decoding only. Text is detokenized incrementally
   (the decoded prefix grows; a trailing partial character is held back), so multi-byte pieces stream correctly.
   prompt_logprobs: choices[0].prompt_logprobs holds one entry per prompt token, the first None, the others
@@ -236,7 +237,10 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
 
         def usage(final):
             n_out = final.get("tokens_predicted", 0) if final else 0
-            return dict(prompt_tokens=int(ids.numel()), completion_tokens=n_out, total_tokens=int(ids.numel()) + n_out)
+            filled = int(final.get("timings", {}).get("prompt_filled_n", 0)) if final else 0
+            # prompt_filled_tokens: prompt rows approximated from the maps (the real tail is prompt_tokens minus it)
+            return dict(prompt_tokens=int(ids.numel()), completion_tokens=n_out, total_tokens=int(ids.numel()) + n_out,
+                        prompt_filled_tokens=filled)
 
         def add_prompt_logprobs(choice, final):
             if plp >= 0 and final is not None and "prompt_scores" in final:

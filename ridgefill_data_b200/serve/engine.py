@@ -30,12 +30,16 @@ import threading
 import time
 from dataclasses import dataclass, field
 
+import logging
+
 import torch
 
 from ..engine import decode as D
 from ..engine.arm import Arm
 from ..engine.prefill import finish, run_lower
 
+
+_log = logging.getLogger("ridgefill_data_b200.serve")
 
 MAX_SCORED_ROWS = 4096      # prompt positions a request can have scored (prompt_logprobs): the last ones
 
@@ -424,6 +428,9 @@ class Scheduler:
         if req.filled:
             timings["ridgefill"] = dict(n_filled=req.filled, split=arm.split, tail=arm.tail, fill=arm.fill,
                                         n_cached_exact_prefix=0)
+            # the real tail of every request, one log line each (the record a protocol audit reads)
+            _log.info("request %s: %d of %d prompt tokens approximated from layer %s", req.rid, req.filled, n,
+                      arm.split)
         self._release(req)
         with self._lock:
             self.stats["completed"] += 1

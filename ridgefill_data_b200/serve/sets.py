@@ -103,7 +103,13 @@ def run_ppl(ep, doc, kva=None):
     novel = [x for x, m in zip(nll, doc.get("novel") or [True] * len(nll)) if m]
     return {"name": doc["name"], "set": "ppl", "n_prompt": len(ids), "cont_len": doc["cont_len"],
             "nll": sum(nll) / len(nll), "nll_novel": sum(novel) / len(novel) if novel else None,
-            "n_novel": len(novel), "token_nll": nll, "wall_s": wall}
+            "n_novel": len(novel), "token_nll": nll, "wall_s": wall, **_tail(reply, len(ids))}
+
+
+def _tail(reply, n):
+    """The request's real tail, as the server reports it (usage.prompt_filled_tokens; None when it does not)."""
+    filled = reply.get("usage", {}).get("prompt_filled_tokens")
+    return {"filled": filled, "tail": None if filled is None else n - int(filled)}
 
 
 def run_ruler(ep, q, kva=None, score=None):
@@ -114,7 +120,8 @@ def run_ruler(ep, q, kva=None, score=None):
     reply = ep.post(ep.body(q["ids"], q["max_new"], kva=kva))
     text = reply["choices"][0]["text"]
     rec = {"name": q["name"], "set": "ruler", "n_prompt": len(q["ids"]), "text": text,
-           "finish_reason": reply["choices"][0].get("finish_reason"), "wall_s": time.perf_counter() - t0}
+           "finish_reason": reply["choices"][0].get("finish_reason"), "wall_s": time.perf_counter() - t0,
+           **_tail(reply, len(q["ids"]))}
     rec.update(score(q, text))
     return rec
 

@@ -231,7 +231,8 @@ def test_openai_endpoints(text_server):
     want = tok.decode(_expected(model, arms["on"], ids, 8), skip_special_tokens=True)
     r = C.post_json(url, "/v1/completions", dict(model="tiny", prompt=prompt, max_tokens=8, temperature=0))
     assert r["object"] == "text_completion" and r["choices"][0]["text"] == want
-    assert r["usage"] == dict(prompt_tokens=ids.numel(), completion_tokens=8, total_tokens=ids.numel() + 8)
+    assert r["usage"] == dict(prompt_tokens=ids.numel(), completion_tokens=8, total_tokens=ids.numel() + 8,
+                              prompt_filled_tokens=arms["on"].prefix_len(ids.numel()))
     assert r["choices"][0]["finish_reason"] == "length"
     chunks = _sse(url, "/v1/completions", dict(prompt=prompt, max_tokens=8))
     assert chunks[-1] == "[DONE]"
@@ -379,6 +380,7 @@ def test_locked_set_client_over_the_openai_api(text_server, tmp_path):
         lp = logits[:-1].double().log_softmax(-1)
         want = [-float(lp[j, ids[38 + j]]) for j in range(10)]
         assert rec["cont_len"] == 10 and rec["n_novel"] == 6
+        assert rec["tail"] == (48 - arm.prefix_len(48) if kva else 48)
         assert max(abs(a - b) for a, b in zip(rec["token_nll"], want)) < 1e-4
         assert abs(rec["nll"] - sum(want) / 10) < 1e-4
     ep = SE.Endpoint(url, kva=1, tail=TAIL)
