@@ -162,3 +162,30 @@ def test_weighted_capture_and_leverage(model):
     x = torch.randn(5, model.hidden)
     lev = IM.log_leverage(x, mean, L)
     assert lev.shape == (5,) and torch.isfinite(lev).all()
+
+
+def test_impact_is_bounded_by_error_times_sensitivity(model):
+    """The ImpactBound statements (code/lean/kva_lean/KvaLean/ImpactBound.lean) on this framework's impact: per row
+    |impact_j| <= |g_j| |delta_j| (Cauchy-Schwarz); with rows S kept exact, |sum over the others| <= e sum_{j not in S}
+    |g_j| for e the largest error; and the S holding the largest gradient norms leaves the smallest outside mass."""
+    split, P = 2, 32
+    ids, h, rows, tgt = _setup(model)
+    true, _ = IM.exact_late(model, h, split, P, rows + P, tgt)
+    kv, gdn = IM.fill_late(model, split, P, lambda i: h[:P])
+    res, _ = IM.impact(model, split, h[P:], P, kv, true, gdn, rows, tgt)
+    d2 = torch.zeros(P, dtype=torch.float64)
+    for i, (k, v) in kv.items():
+        for fill, exact in ((k, true[i][0]), (v, true[i][1])):
+            d2 += (exact.float() - fill.float()).square().sum((0, 2)).double()
+    delta, g, imp = d2.sqrt(), res["grad_norm"].double(), res["impact"].double()
+    assert (imp.abs() <= g * delta * (1 + 1e-5) + 1e-9).all()
+    e = float(delta.max())
+    gen = torch.Generator().manual_seed(3)
+    for m in (0, 4, 16):
+        top = set(torch.topk(g, m).indices.tolist()) if m else set()
+        outside = [j for j in range(P) if j not in top]
+        assert abs(float(imp[outside].sum())) <= e * float(g[outside].sum()) * (1 + 1e-5) + 1e-9
+        for _ in range(20):                              # no other set of m rows leaves less sensitivity outside
+            other = set(torch.randperm(P, generator=gen)[:m].tolist())
+            rest = [j for j in range(P) if j not in other]
+            assert float(g[outside].sum()) <= float(g[rest].sum()) + 1e-12
