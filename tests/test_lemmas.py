@@ -10,6 +10,9 @@ checks of the statements, not proofs.
   4  uniform logit shift                softmax mass of a set never falls when its logits rise
   5  attention influence                ops.oracle.attend_at: changing one value row moves each query's output by
                                         exactly that row's attention weight times the change; later rows none
+  6  attention key sensitivity          ops.oracle.attend: moving one key row by delta changes each weight by at
+                                        most a_ij0 (exp|eps_i| - 1), eps_i = scale <q_i, delta>, and each output by
+                                        at most a_ij0 (exp|eps_i| |dv| + 2 M (exp|eps_i| - 1)) with the value moved too
   9  QK-norm invariance                 ops.oracle.rms_norm (eps 0) ignores a positive scale of its input
   10 speedup with exact rows            CostModel.bypass: every exact row costs, the speedup falls with the rows
   11 count-matched random control       engine.select.random_rows: exactly k distinct rows, uniform over many prompts
@@ -124,6 +127,35 @@ def test_attention_value_influence_is_the_weight():
     a = torch.softmax(s, -1)
     torch.testing.assert_close(moved, a[:, j:j + 1] * dv[None, :], rtol=1e-5, atol=1e-6)   # fp32 scores
     assert float(moved[:j].abs().max()) == 0.0                        # earlier queries never see row j
+
+
+@FAST
+@given(st.integers(0, 2 ** 31 - 1), st.floats(0.01, 2.0))
+def test_attention_key_sensitivity_is_bounded_by_the_weight(seed, size):
+    g = torch.Generator().manual_seed(seed)
+    n, d, j = 10, 8, 4
+    q, k, v = (torch.randn(1, n, d, generator=g, dtype=torch.float64) for _ in range(3))
+    scale = d ** -0.5
+    dk = torch.randn(d, generator=g, dtype=torch.float64) * size
+    dv = torch.randn(d, generator=g, dtype=torch.float64) * size
+    causal = torch.ones(n, n, dtype=torch.bool).triu(1)
+
+    def weights(kk):
+        return torch.softmax(((q[0] @ kk[0].T) * scale).masked_fill(causal, float("-inf")), -1)
+    k2, v2 = k.clone(), v.clone()
+    k2[0, j] += dk
+    v2[0, j] += dv
+    a, a2 = weights(k), weights(k2)
+    eps = ((q[0] @ dk) * scale).abs()
+    grow = torch.expm1(eps)
+    tol = 1e-5                                                          # attend's scores are fp32
+    assert ((a2 - a).abs() <= a[:, j:j + 1] * grow[:, None] + tol).all()
+    M = float(v[0].norm(dim=-1).max())
+    key_only = (O.attend(q, k2, v, scale) - O.attend(q, k, v, scale)).norm(dim=-1)     # [n] (rows, features)
+    assert (key_only <= 2 * M * a[:, j] * grow + tol).all()
+    both = (O.attend(q, k2, v2, scale) - O.attend(q, k, v, scale)).norm(dim=-1)
+    assert (both <= a[:, j] * (eps.exp() * dv.norm() + 2 * M * grow) + tol).all()
+    assert float(both[:j].max()) == 0.0                                 # earlier queries never see row j
 
 
 @FAST
