@@ -12,6 +12,8 @@ Sets (prompts from eval/locked.py, sent as token ids):
   speed  time to the first streamed token (max_tokens 1) of prefixes of one document at --speed-lengths: one warm-up,
          then --speed-runs rounds; with --kva 1 each round runs the arm and the same server's exact path
          (dyluhn_kva 0) back to back.
+  control  the positive control of a RidgeFill run: the first --control-docs ppl documents with dyluhn_kva 0 (no
+         row approximated, the same server), to compare with an exact run.
 The per-request switch is the c5 kit's `vllm_xargs` {"dyluhn_kva": "0" | "1", "dyluhn_kva_tail": T}, which this
 framework's server reads too, so the same client drives either server. Each sample is one JSON file
 <out>/<set>/<name>.json with a sha256 sidecar, written atomically; a sample whose file and sidecar agree is skipped
@@ -179,6 +181,7 @@ def main(argv=None):
     ap.add_argument("--ruler-lengths", default="8192,16384,32768")
     ap.add_argument("--speed-lengths", default="9216,16384,32768")
     ap.add_argument("--speed-runs", type=int, default=3)
+    ap.add_argument("--control-docs", type=int, default=4)
     ap.add_argument("--out", required=True)
     a = ap.parse_args(argv)
     from ..eval import locked as LK
@@ -188,7 +191,7 @@ def main(argv=None):
     ep = Endpoint(a.url, a.served_model, a.kva, a.tail)
     sets = [s for s in a.sets.split(",") if s]
     summary = {}
-    if "ppl" in sets or "speed" in sets:
+    if "ppl" in sets or "speed" in sets or "control" in sets:
         docs, _ = LK.longppl_docs(tok, man, a.model, max_len=a.ppl_max_len, root=a.locked_root)
     if "ppl" in sets:
         recs = []
@@ -199,6 +202,15 @@ def main(argv=None):
             save(a.out, "ppl", d["name"], rec)
             recs.append(rec)
         summary["ppl"] = {"documents": len(recs), "nll_mean": sum(r["nll"] for r in recs) / max(1, len(recs))}
+    if "control" in sets:
+        recs = []
+        for d in docs[:a.control_docs]:
+            if done(a.out, "control", d["name"]):
+                continue
+            rec = run_ppl(ep, d, kva=0)
+            save(a.out, "control", d["name"], rec)
+            recs.append(rec)
+        summary["control"] = {"documents": len(recs), "nll_mean": sum(r["nll"] for r in recs) / max(1, len(recs))}
     if "ruler" in sets:
         lengths = [int(x) for x in a.ruler_lengths.split(",") if x]
         prompts_, _ = LK.ruler_prompts(tok, "raw", man, lengths=lengths, root=a.locked_root)
