@@ -82,7 +82,8 @@ class Detok:
         if self.tok is None:
             return ""
         self.ids += list(ids)
-        text = self.tok.decode(self.ids, skip_special_tokens=True)
+        # JSON-safe text: a lone surrogate (a tokenizer that maps ids to raw code points) becomes "?"
+        text = self.tok.decode(self.ids, skip_special_tokens=True).encode("utf-8", "replace").decode("utf-8")
         if text.endswith("\ufffd"):
             return ""
         delta = text[len(self.sent):] if text.startswith(self.sent) else text

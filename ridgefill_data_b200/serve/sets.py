@@ -179,6 +179,7 @@ def main(argv=None):
     ap.add_argument("--locked-root")
     ap.add_argument("--ppl-max-len", type=int, default=32768)
     ap.add_argument("--ruler-lengths", default="8192,16384,32768")
+    ap.add_argument("--ruler-tasks", default="", help="comma-separated RULER tasks (default: every locked task)")
     ap.add_argument("--speed-lengths", default="9216,16384,32768")
     ap.add_argument("--speed-runs", type=int, default=3)
     ap.add_argument("--control-docs", type=int, default=4)
@@ -213,7 +214,8 @@ def main(argv=None):
         summary["control"] = {"documents": len(recs), "nll_mean": sum(r["nll"] for r in recs) / max(1, len(recs))}
     if "ruler" in sets:
         lengths = [int(x) for x in a.ruler_lengths.split(",") if x]
-        prompts_, _ = LK.ruler_prompts(tok, "raw", man, lengths=lengths, root=a.locked_root)
+        tasks = [t for t in a.ruler_tasks.split(",") if t] or None
+        prompts_, _ = LK.ruler_prompts(tok, "raw", man, tasks=tasks, lengths=lengths, root=a.locked_root)
         recs = []
         for q in prompts_:
             if done(a.out, "ruler", q["name"]):

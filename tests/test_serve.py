@@ -393,3 +393,27 @@ def test_locked_set_client_over_the_openai_api(text_server, tmp_path):
     assert all(len(r["ttft_s"]["arm"]) == len(r["ttft_s"]["exact"]) == 2 and r["speedup_median"] > 0 for r in rows)
     assert SE.save(tmp_path, "ppl", "d0", dict(x=1)) and SE.done(tmp_path, "ppl", "d0")
     assert not SE.save(tmp_path, "ppl", "d0", dict(x=2))
+
+
+def test_locked_set_client_cli_writes_and_resumes(text_server, tmp_path, monkeypatch):
+    """`python -m ridgefill_data_b200.serve.sets` on a small locked set (the fixture of tests/test_eval_sets.py):
+    ppl, RULER and control samples written with sidecars; a second run finds them finished and writes nothing."""
+    from test_eval_sets import _write_set
+    from ridgefill_data_b200.serve import sets as SE
+    url, model, arms, tok = text_server
+    root = tmp_path / "locked"
+    _write_set(root)
+    monkeypatch.setenv("RF_LOCKED_DIR", str(root))
+    monkeypatch.setenv("RF_DERIVED_DIR", str(tmp_path / "derived"))
+    out = tmp_path / "out"
+    argv = ["--url", url, "--kva", "0", "--tokenizer", "char", "--model", "m", "--sets", "ppl,ruler,control",
+            "--ruler-lengths", "8192", "--ruler-tasks", "niah_single_1", "--control-docs", "1", "--out", str(out)]
+    assert SE.main(argv) == 0
+    ppl = json.loads((out / "ppl" / "lp-doc_4096_0.json").read_text())
+    assert ppl["cont_len"] == 200 and ppl["tail"] == ppl["n_prompt"] and ppl["nll"] > 0
+    ruler = sorted((out / "ruler").glob("*.json"))
+    assert len(ruler) == 3 and all(0.0 <= json.loads(f.read_text())["score"] <= 1.0 for f in ruler)
+    assert (out / "control" / "lp-doc_4096_0.json.sha256").exists()
+    stamps = {f: f.stat().st_mtime_ns for f in out.rglob("*.json")}
+    assert SE.main(argv) == 0
+    assert {f: f.stat().st_mtime_ns for f in out.rglob("*.json")} == stamps
