@@ -187,6 +187,66 @@ def fit_bench(args):
         dist.destroy_process_group()
 
 
+def decode_bench(args):
+    """bench.py --decode 1,3,8: the greedy decode step of R sequences on one GPU, as the server runs it (one CUDA graph
+    of the device-position step, engine/decode_graph.py), after a prefill of --decode-context tokens each; device
+    time per step with CUDA events, 3 warm-up steps, then --steps timed, the RidgeFill 16K step untouched. One JSON
+    line per R (tokens/s = R x steps per second), with the weight-read floor of the step (the model's bytes over the
+    measured copy bandwidth)."""
+    import torch
+    from ridgefill_data_b200.engine.decode_graph import DecodeGraph
+    from ridgefill_data_b200.engine.prefill import run_lower
+    from ridgefill_data_b200.models.base import from_config
+    from ridgefill_data_b200.models.config import PRESETS
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    cfg = PRESETS[args.model]
+    model = from_config(cfg, seed=0, device=device, backend="b200", std=0.02)
+    rs = sorted({int(r) for r in args.decode.split(",") if r})
+    g = torch.Generator().manual_seed(0)
+    caches, toks = [], []
+    with torch.no_grad():
+        for _ in range(max(rs)):
+            ids = torch.randint(0, cfg.vocab, (args.decode_context,), generator=g).to(device)
+            caches.append(run_lower(model, ids, [model.n_layers], reserve=args.steps + 64)[1])
+            toks.append(int(ids[-1]))
+    torch.cuda.synchronize()
+    tensors = [t for w in model.W for t in w.values() if torch.is_tensor(t) and t.is_cuda]
+    if torch.is_tensor(getattr(model, "lm_head", None)):
+        tensors.append(model.lm_head)
+    seen, weight_bytes = set(), 0          # every weight read once per step (views of one packed tensor counted once)
+    for t in tensors:
+        st = t.untyped_storage()
+        if st.data_ptr() not in seen:
+            seen.add(st.data_ptr())
+            weight_bytes += st.nbytes()
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    for R in rs:
+        with torch.no_grad():
+            dg = DecodeGraph(model, caches[:R], headroom=args.steps + 8)
+            for _ in range(3):
+                dg.step(toks[:R])
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                dg.step(toks[:R])
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            del dg
+        print(json.dumps(dict(metric="greedy decode tokens/s (CUDA-graph step)", value=round(R * 1e3 / ms, 1),
+                              unit="tokens/s", ms_per_step=round(ms, 3), sequences=R, steps=args.steps, warmup=3,
+                              n_gpus=1, dtype="bf16", data="synthetic (seeded ids; random-init weights)",
+                              config=dict(model=args.model, context=args.decode_context),
+                              weight_floor_ms=round(weight_bytes / (peaks.get("hbm_gbs", 6540.5) * 1e6), 2))),
+              flush=True)
+
+
 def build_engine(args, device):
     from ridgefill_data_b200.engine.arm import Arm
     from ridgefill_data_b200.models.base import from_config
@@ -232,6 +292,9 @@ def main():
                          "--map-slots device buffers (copies overlap the lower layers)")
     ap.add_argument("--map-slots", type=int, default=8)
     ap.add_argument("--fit", action="store_true", help="time the ridge fit instead of the prefill (see fit_bench)")
+    ap.add_argument("--decode", default="", help="time the decode step of these numbers of sequences instead of the "
+                                                 "prefill, e.g. 1,3,8 (see decode_bench)")
+    ap.add_argument("--decode-context", type=int, default=1024, help="prompt tokens of each decoding sequence")
     ap.add_argument("--fit-rows", type=int, default=839652)
     ap.add_argument("--fit-doc", type=int, default=8192, help="calibration document length (tokens)")
     ap.add_argument("--fit-splits", default="16,24,32")
@@ -260,6 +323,8 @@ def main():
         return reference_arm(args)
     if args.fit:
         return fit_bench(args)
+    if args.decode:
+        return decode_bench(args)
 
     import torch
     import torch.distributed as dist
