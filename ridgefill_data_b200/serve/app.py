@@ -249,7 +249,7 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
 
         if body.get("stream"):
             async def events():
-                first = True
+                first, done = True, False
                 try:
                     async for delta, finish, final in pieces():
                         if delta or first or finish:
@@ -259,8 +259,13 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
                                 add_prompt_logprobs(c["choices"][0], final)
                             yield "data: " + json.dumps(c) + "\n\n"
                             first = False
+                    done = True
                 except RuntimeError as e:
+                    done = True
                     yield "data: " + json.dumps({"error": {"message": str(e)}}) + "\n\n"
+                finally:              # the client went away mid-stream: the scheduler ends the request next round
+                    if not done:
+                        req.cancelled = True
                 yield "data: [DONE]\n\n"
             return StreamingResponse(events(), media_type="text/event-stream")
         out, finish, final = [], None, None
@@ -341,11 +346,17 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
             return JSONResponse({"error": {"code": 400, "message": str(e)}}, status_code=400)
         if body.get("stream"):
             async def events():
-                while True:
-                    ev = await q.get()
-                    yield "data: " + json.dumps(ev) + "\n\n"
-                    if ev.get("stop"):
-                        break
+                done = False
+                try:
+                    while True:
+                        ev = await q.get()
+                        yield "data: " + json.dumps(ev) + "\n\n"
+                        if ev.get("stop"):
+                            done = True
+                            break
+                finally:              # the client went away mid-stream: the scheduler ends the request next round
+                    if not done:
+                        req.cancelled = True
             return StreamingResponse(events(), media_type="text/event-stream")
         toks, text = [], []
         while True:

@@ -147,7 +147,8 @@ class Scheduler:
         self.sync = sync if sync is not None else (torch.cuda.synchronize if model.device.type == "cuda"
                                                   else (lambda: None))
         self.stats = dict(requests=0, completed=0, errors=0, prompt_tokens=0, predicted_tokens=0,
-                          filled_tokens=0, interleaved_rounds=0, decode_batches=0, graph_captures=0, graph_steps=0)
+                          filled_tokens=0, interleaved_rounds=0, decode_batches=0, graph_captures=0, graph_steps=0,
+                          cancelled=0)
         self.ttft_ms, self.prompt_ms = [], []
         self._lock = threading.Lock()
 
@@ -197,6 +198,10 @@ class Scheduler:
                 try:
                     req = self.waiting.get_nowait()
                 except queue.Empty:
+                    req = None
+                if req is not None and req.cancelled:   # its client left while it waited: never prefilled
+                    with self._lock:
+                        self.stats["cancelled"] += 1
                     req = None
                 if req is not None:
                     started = True
@@ -434,6 +439,8 @@ class Scheduler:
         self._release(req)
         with self._lock:
             self.stats["completed"] += 1
+            if req.cancelled:
+                self.stats["cancelled"] += 1
         final = {"tokens": [], "content": "", "stop": True, "stop_type": stop_type, "tokens_predicted": pred,
                  "tokens_evaluated": n, "truncated": False, "id": req.rid, "timings": timings}
         if req.prompt_scores is not None:

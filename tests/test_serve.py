@@ -417,3 +417,38 @@ def test_locked_set_client_cli_writes_and_resumes(text_server, tmp_path, monkeyp
     stamps = {f: f.stat().st_mtime_ns for f in out.rglob("*.json")}
     assert SE.main(argv) == 0
     assert {f: f.stat().st_mtime_ns for f in out.rglob("*.json")} == stamps
+
+
+def test_a_stream_whose_client_leaves_is_ended(server):
+    """A streamed request whose client closes the connection after its first token is ended by the scheduler at
+    its next decode round (its cache released, counted as cancelled) instead of decoding to its limit."""
+    import http.client
+    import time
+    url, model, arms = server
+    host, port = url.split("//")[1].split(":")
+    before = _metric(url, "ridgefill_cancelled_total")
+    ids = uniform_prompt(40, CFG.vocab, seed=31)
+    conn = http.client.HTTPConnection(host, int(port), timeout=60)
+    conn.request("POST", "/completion", body=json.dumps(dict(prompt=ids.tolist(), n_predict=100000, ignore_eos=True,
+                                                             stream=True)),
+                 headers={"Content-Type": "application/json"})
+    r = conn.getresponse()
+    line = b""
+    while not line.startswith(b"data:"):
+        line = r.fp.readline().strip()
+    conn.sock.close()                                    # the client leaves after its first token
+    conn.close()
+    t0 = time.time()
+    while time.time() - t0 < 30:
+        if C.get_json(url, "/health")["active"] == 0 and _metric(url, "ridgefill_cancelled_total") > before:
+            break
+        time.sleep(0.05)
+    assert C.get_json(url, "/health")["active"] == 0
+    assert _metric(url, "ridgefill_cancelled_total") == before + 1
+
+
+def _metric(url, name):
+    for line in urllib.request.urlopen(url + "/metrics").read().decode().splitlines():
+        if line.startswith(name + " "):
+            return float(line.split()[1])
+    return 0.0
