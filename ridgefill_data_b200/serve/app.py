@@ -24,7 +24,6 @@ OpenAI-compatible (the API the c5 kit's client and the LongBench v2 runner speak
   have logits: under RidgeFill those are the exact tail, so the entries of the filled prefix carry "logprob": null
   (as do positions before the last MAX_SCORED_ROWS); an exact request scores every position.
 """
-from __future__ import annotations
 
 import asyncio
 import json
@@ -36,6 +35,30 @@ from .engine import Request
 
 class BadRequest(ValueError):
     pass
+
+
+class ClientGone(Exception):
+    """The HTTP client disconnected while its non-streamed request was running."""
+
+
+async def _next_event(q, http_req=None, poll_s=0.5):
+    """The request's next event; with the HTTP request, at least every poll_s (also while events keep arriving)
+    checks that its client is still connected."""
+    if http_req is None:
+        return await q.get()
+    loop = asyncio.get_running_loop()
+    last = getattr(http_req.state, "rf_checked", None)
+    if last is None:
+        last = http_req.state.rf_checked = loop.time()
+    while True:
+        if loop.time() - last >= poll_s:
+            last = http_req.state.rf_checked = loop.time()
+            if await http_req.is_disconnected():
+                raise ClientGone()
+        try:
+            return await asyncio.wait_for(q.get(), max(1e-3, poll_s - (loop.time() - last)))
+        except asyncio.TimeoutError:
+            pass
 
 
 def parse_body(body, arms, tokenizer=None):
@@ -167,6 +190,7 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
     import uuid
 
     from fastapi import FastAPI
+    from fastapi import Request as HTTPRequest
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
     app = FastAPI(title="ridgefill-b200")
@@ -184,7 +208,7 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
         scheduler.submit(req)
         return req, q
 
-    async def openai_run(ids, body, arm, kind):
+    async def openai_run(ids, body, arm, kind, http_req=None):
         """Shared core of /v1/completions and /v1/chat/completions."""
         n_predict = int(body.get("max_tokens") or body.get("max_completion_tokens") or 16)
         if n_predict < 1:
@@ -215,7 +239,7 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
             """(text delta, finish_reason or None, final event or None) as tokens arrive; applies stop strings."""
             text, emitted = "", 0
             while True:
-                ev = await q.get()
+                ev = await _next_event(q, None if body.get("stream") else http_req)
                 if "error" in ev:
                     raise RuntimeError(ev["error"])
                 if ev.get("stop"):
@@ -275,6 +299,9 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
                 finish, final = f or finish, fin or final
         except RuntimeError as e:
             return bad(str(e), 500)
+        except ClientGone:                  # nobody reads the reply: end the request at the next decode round
+            req.cancelled = True
+            return bad("client disconnected", 499)
         text = "".join(out)
         choice = (dict(index=0, message=dict(role="assistant", content=text), finish_reason=finish)
                   if kind == "chat" else dict(index=0, text=text, finish_reason=finish, logprobs=None))
@@ -286,7 +313,7 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
         return dict(object="list", data=[dict(id=model_name, object="model", owned_by="ridgefill-b200")])
 
     @app.post("/v1/completions")
-    async def v1_completions(body: dict):
+    async def v1_completions(body: dict, http_req: HTTPRequest):
         try:
             _greedy_only(body)
             arm = _mode(body, arms)
@@ -294,12 +321,12 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
             if isinstance(prompt, list) and len(prompt) == 1 and isinstance(prompt[0], str):
                 prompt = prompt[0]
             ids, _, _, _ = parse_body(dict(prompt=prompt, n_predict=1, ridgefill_mode="x"), {"x": arm}, tokenizer)
-            return await openai_run(ids, body, arm, "text")
+            return await openai_run(ids, body, arm, "text", http_req)
         except BadRequest as e:
             return bad(str(e))
 
     @app.post("/v1/chat/completions")
-    async def v1_chat(body: dict):
+    async def v1_chat(body: dict, http_req: HTTPRequest):
         try:
             _greedy_only(body)
             arm = _mode(body, arms)
@@ -313,7 +340,7 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
             ids = torch.tensor(encode(tokenizer, rendered), dtype=torch.long)
             if ids.numel() == 0:
                 raise BadRequest("the rendered chat prompt encodes to no tokens")
-            return await openai_run(ids, body, arm, "chat")
+            return await openai_run(ids, body, arm, "chat", http_req)
         except BadRequest as e:
             return bad(str(e))
 
@@ -330,7 +357,7 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
         return PlainTextResponse(scheduler.metrics_text(), media_type="text/plain; version=0.0.4")
 
     @app.post("/completion")
-    async def completion(body: dict):
+    async def completion(body: dict, http_req: HTTPRequest):
         try:
             ids, n_predict, arm, ignore_eos = parse_body(body, arms, tokenizer)
         except BadRequest as e:
@@ -360,7 +387,11 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
             return StreamingResponse(events(), media_type="text/event-stream")
         toks, text = [], []
         while True:
-            ev = await q.get()
+            try:
+                ev = await _next_event(q, http_req)
+            except ClientGone:              # nobody reads the reply: end the request at the next decode round
+                req.cancelled = True
+                return JSONResponse({"error": {"code": 499, "message": "client disconnected"}}, status_code=499)
             if "error" in ev:
                 return JSONResponse({"error": {"code": 500, "message": ev["error"]}}, status_code=500)
             if ev.get("stop"):

@@ -447,6 +447,31 @@ def test_a_stream_whose_client_leaves_is_ended(server):
     assert _metric(url, "ridgefill_cancelled_total") == before + 1
 
 
+def test_a_non_streamed_request_whose_client_leaves_is_ended(server):
+    """The same for a non-streamed request: the server notices the closed connection while it waits and ends it."""
+    import http.client
+    import time
+    url, model, arms = server
+    host, port = url.split("//")[1].split(":")
+    before = _metric(url, "ridgefill_cancelled_total")
+    ids = uniform_prompt(40, CFG.vocab, seed=32)
+    conn = http.client.HTTPConnection(host, int(port), timeout=60)
+    conn.request("POST", "/completion", body=json.dumps(dict(prompt=ids.tolist(), n_predict=100000,
+                                                             ignore_eos=True)),
+                 headers={"Content-Type": "application/json"})
+    t0 = time.time()
+    while C.get_json(url, "/health")["active"] == 0 and time.time() - t0 < 30:
+        time.sleep(0.02)                                 # decoding has started
+    conn.sock.close()
+    conn.close()
+    while time.time() - t0 < 30:
+        if C.get_json(url, "/health")["active"] == 0 and _metric(url, "ridgefill_cancelled_total") > before:
+            break
+        time.sleep(0.05)
+    assert C.get_json(url, "/health")["active"] == 0
+    assert _metric(url, "ridgefill_cancelled_total") == before + 1
+
+
 def _metric(url, name):
     for line in urllib.request.urlopen(url + "/metrics").read().decode().splitlines():
         if line.startswith(name + " "):
