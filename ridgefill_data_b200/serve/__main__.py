@@ -98,6 +98,8 @@ def main(argv=None):
                          "decode-round period follows its size (0: every --interleave layers)")
     ap.add_argument("--tp-comm", default="nvls", choices=("nccl", "fused", "nvls"),
                     help="tensor parallel (under torchrun with several ranks): the all-reduce / all-gather kernels")
+    ap.add_argument("--max-waiting", type=int, default=0,
+                    help="refuse new requests with HTTP 503 while this many wait for a prefill (0: no limit)")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8080)
     a = ap.parse_args(argv)
@@ -107,7 +109,7 @@ def main(argv=None):
     from .engine import Scheduler
     model, arms, tok, eos, props = build(a)
     sched = Scheduler(model, eos=eos, interleave=a.interleave, gap_ms=a.decode_gap_ms,
-                      graphs=bool(a.decode_graphs)).start()
+                      graphs=bool(a.decode_graphs), max_waiting=a.max_waiting).start()
     try:
         Server(create_app(sched, arms, tok, props), a.host, a.port, log_level="info").run()
     finally:
@@ -145,7 +147,8 @@ def main_tp(a):
     lockstep = Lockstep(control, arms)
     try:
         if rank == 0:
-            sched = Scheduler(model, eos=eos, interleave=0, graphs=False, lockstep=lockstep).start()
+            sched = Scheduler(model, eos=eos, interleave=0, graphs=False, lockstep=lockstep,
+                              max_waiting=a.max_waiting).start()
             try:
                 Server(create_app(sched, arms, tok, dict(props, tensor_parallel=world)), a.host, a.port,
                        log_level="info").run()

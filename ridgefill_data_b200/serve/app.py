@@ -30,7 +30,7 @@ import json
 
 import torch
 
-from .engine import Request
+from .engine import Request, ServerBusy
 
 
 class BadRequest(ValueError):
@@ -217,6 +217,8 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
         plp = _prompt_logprobs(body) if kind == "text" else -1
         try:
             req, q = submit(ids, n_predict, arm, prompt_logprobs=plp)
+        except ServerBusy as e:
+            return bad(str(e), 503)
         except ValueError as e:
             raise BadRequest(str(e))
         rid = ("chatcmpl-" if kind == "chat" else "cmpl-") + uuid.uuid4().hex[:24]
@@ -369,6 +371,8 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
                       emit=lambda ev: loop.call_soon_threadsafe(q.put_nowait, ev))
         try:
             scheduler.submit(req)
+        except ServerBusy as e:
+            return JSONResponse({"error": {"code": 503, "message": str(e)}}, status_code=503)
         except ValueError as e:
             return JSONResponse({"error": {"code": 400, "message": str(e)}}, status_code=400)
         if body.get("stream"):

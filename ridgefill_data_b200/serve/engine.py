@@ -88,6 +88,10 @@ def score_prompt(logits, ids, top=0, chunk=256):
     return n - m, out
 
 
+class ServerBusy(RuntimeError):
+    """The waiting queue is full (max_waiting): the client should retry later."""
+
+
 @dataclass
 class Request:
     ids: torch.Tensor                       # [n] int64 prompt ids (host)
@@ -114,7 +118,7 @@ class Request:
 
 class Scheduler:
     def __init__(self, model, eos=(), interleave=4, max_active=64, max_batch=32, sync=None, gap_ms=0.0,
-                 sample_rows=4096, graphs=True, graph_min_tokens=8, lockstep=None):
+                 sample_rows=4096, graphs=True, graph_min_tokens=8, lockstep=None, max_waiting=0):
         self.model = model
         # lockstep: a serve.lockstep.Lockstep when the model is sharded over ranks (this scheduler runs on rank 0
         # and every model call is mirrored on the others)
@@ -137,6 +141,7 @@ class Scheduler:
         self._graph_pool = None
         self._seen_key = None        # the previous round's set: a graph is captured once a set repeats
         self.max_active = int(max_active)
+        self.max_waiting = int(max_waiting)      # > 0: requests refused (ServerBusy) while this many wait
         self.max_batch = int(max_batch)
         self.waiting = queue.Queue()
         self.active = []
@@ -148,7 +153,7 @@ class Scheduler:
                                                   else (lambda: None))
         self.stats = dict(requests=0, completed=0, errors=0, prompt_tokens=0, predicted_tokens=0,
                           filled_tokens=0, interleaved_rounds=0, decode_batches=0, graph_captures=0, graph_steps=0,
-                          cancelled=0)
+                          cancelled=0, refused_busy=0)
         self.ttft_ms, self.prompt_ms = [], []
         self._lock = threading.Lock()
 
@@ -178,6 +183,10 @@ class Scheduler:
         vocab = getattr(getattr(self.model, "cfg", None), "vocab", None)
         if vocab and (int(req.ids.min()) < 0 or int(req.ids.max()) >= vocab):
             raise ValueError(f"prompt ids outside the vocabulary [0, {vocab})")
+        if self.max_waiting > 0 and self.waiting.qsize() >= self.max_waiting:
+            with self._lock:
+                self.stats["refused_busy"] += 1
+            raise ServerBusy(f"{self.waiting.qsize()} requests are waiting (the server's limit); retry later")
         req.rid = req.rid or f"req-{next(self._ids)}"
         req.t_submit = time.perf_counter()
         with self._lock:

@@ -128,6 +128,21 @@ def test_eos_and_bad_requests(setup):
         sched.stop()
 
 
+def test_a_full_waiting_queue_refuses_with_busy(setup):
+    """max_waiting: with that many requests waiting for a prefill, submit refuses (ServerBusy, HTTP 503 in the app);
+    a stopped scheduler's queue stays full, so the refusal is deterministic here."""
+    from ridgefill_data_b200.serve.engine import ServerBusy
+    model, arms = setup
+    sched = Scheduler(model, max_waiting=2)              # not started: nothing leaves the queue
+    ids = uniform_prompt(20, CFG.vocab, seed=9)
+    for _ in range(2):
+        sched.submit(Request(ids=ids, n_predict=1, arm=arms["off"], emit=print))
+    with pytest.raises(ServerBusy):
+        sched.submit(Request(ids=ids, n_predict=1, arm=arms["off"], emit=print))
+    assert sched.stats["refused_busy"] == 1 and sched.load["waiting"] == 2
+    assert "ridgefill_refused_busy_total 1" in sched.metrics_text()
+
+
 @pytest.fixture(scope="module")
 def server(setup):
     model, arms = setup
