@@ -100,6 +100,9 @@ def main(argv=None):
                     help="tensor parallel (under torchrun with several ranks): the all-reduce / all-gather kernels")
     ap.add_argument("--max-waiting", type=int, default=0,
                     help="refuse new requests with HTTP 503 while this many wait for a prefill (0: no limit)")
+    ap.add_argument("--api-key", default=os.environ.get("RF_API_KEY"),
+                    help="require `Authorization: Bearer KEY` on every endpoint but /health and /metrics "
+                         "(default: $RF_API_KEY; unset: open)")
     ap.add_argument("--host", default="127.0.0.1")
     ap.add_argument("--port", type=int, default=8080)
     a = ap.parse_args(argv)
@@ -111,7 +114,7 @@ def main(argv=None):
     sched = Scheduler(model, eos=eos, interleave=a.interleave, gap_ms=a.decode_gap_ms,
                       graphs=bool(a.decode_graphs), max_waiting=a.max_waiting).start()
     try:
-        Server(create_app(sched, arms, tok, props), a.host, a.port, log_level="info").run()
+        Server(create_app(sched, arms, tok, props, api_key=a.api_key), a.host, a.port, log_level="info").run()
     finally:
         sched.stop()
     return 0
@@ -150,8 +153,8 @@ def main_tp(a):
             sched = Scheduler(model, eos=eos, interleave=0, graphs=False, lockstep=lockstep,
                               max_waiting=a.max_waiting).start()
             try:
-                Server(create_app(sched, arms, tok, dict(props, tensor_parallel=world)), a.host, a.port,
-                       log_level="info").run()
+                Server(create_app(sched, arms, tok, dict(props, tensor_parallel=world), api_key=a.api_key), a.host,
+                       a.port, log_level="info").run()
             finally:
                 sched.stop()
         else:

@@ -185,7 +185,10 @@ def _stops(body):
     return st
 
 
-def create_app(scheduler, arms, tokenizer=None, props=None):
+def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
+    """The FastAPI app. api_key: every endpoint but /health and /metrics then needs `Authorization: Bearer <key>`
+    (or `x-api-key: <key>`), as vLLM's and llama.cpp's servers do with their --api-key."""
+    import hmac
     import time
     import uuid
 
@@ -194,6 +197,17 @@ def create_app(scheduler, arms, tokenizer=None, props=None):
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
     app = FastAPI(title="ridgefill-b200")
+
+    if api_key:
+        @app.middleware("http")
+        async def check_key(request, call_next):
+            if request.url.path not in ("/health", "/metrics"):
+                auth = request.headers.get("authorization", "")
+                given = auth[7:] if auth.lower().startswith("bearer ") else request.headers.get("x-api-key", "")
+                if not hmac.compare_digest(given.encode(), str(api_key).encode()):
+                    return JSONResponse({"error": {"code": 401, "message": "invalid or missing API key",
+                                                   "type": "invalid_request_error"}}, status_code=401)
+            return await call_next(request)
     model_name = str((props or {}).get("model", "ridgefill"))
 
     def bad(msg, code=400):

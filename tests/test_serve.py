@@ -492,3 +492,31 @@ def _metric(url, name):
         if line.startswith(name + " "):
             return float(line.split()[1])
     return 0.0
+
+
+def test_api_key_guards_every_endpoint_but_health(setup):
+    """--api-key: requests without the key get 401, with it (Bearer or x-api-key) they are served; /health and
+    /metrics stay open for probes."""
+    model, arms = setup
+    sched = Scheduler(model, interleave=2).start()
+    srv = Server(create_app(sched, arms, props=dict(vocab=CFG.vocab), api_key="s3cret"), port=0).start()
+    url = f"http://127.0.0.1:{srv.port}"
+    try:
+        body = json.dumps(dict(prompt=uniform_prompt(20, CFG.vocab, seed=3).tolist(), n_predict=2)).encode()
+
+        def post(headers):
+            req = urllib.request.Request(url + "/completion", data=body,
+                                         headers=dict({"Content-Type": "application/json"}, **headers))
+            with urllib.request.urlopen(req, timeout=60) as r:
+                return json.load(r)
+        for bad in ({}, {"Authorization": "Bearer wrong"}, {"x-api-key": "s3cre"}):
+            with pytest.raises(urllib.error.HTTPError) as e:
+                post(bad)
+            assert e.value.code == 401
+        assert post({"Authorization": "Bearer s3cret"})["tokens_predicted"] == 2
+        assert post({"x-api-key": "s3cret"})["stop"]
+        assert C.get_json(url, "/health")["status"] == "ok"
+        assert "ridgefill_requests_total" in urllib.request.urlopen(url + "/metrics").read().decode()
+    finally:
+        srv.stop()
+        sched.stop()
