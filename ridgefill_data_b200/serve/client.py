@@ -15,6 +15,7 @@ Only the standard library is used on the client side (urllib + threads), so it r
 from __future__ import annotations
 
 import json
+import os
 import threading
 import time
 import urllib.request
@@ -23,8 +24,17 @@ import numpy as np
 
 
 # ------------------------------------------------------------------------------------------------ transport
+def headers():
+    """JSON content type, plus `Authorization: Bearer $RF_API_KEY` when the server was started with a key."""
+    h = {"Content-Type": "application/json"}
+    key = os.environ.get("RF_API_KEY")
+    if key:
+        h["Authorization"] = f"Bearer {key}"
+    return h
+
+
 def post_json(url, path, body, timeout=600):
-    req = urllib.request.Request(url + path, data=json.dumps(body).encode(), headers={"Content-Type": "application/json"})
+    req = urllib.request.Request(url + path, data=json.dumps(body).encode(), headers=headers())
     with urllib.request.urlopen(req, timeout=timeout) as r:
         return json.load(r)
 
@@ -38,8 +48,7 @@ def stream(url, body, epoch=None, timeout=600):
     """[{'t': seconds since epoch, 'data': event}] of one streamed completion, and the send time."""
     epoch = time.monotonic() if epoch is None else epoch
     body = dict(body, stream=True)
-    req = urllib.request.Request(url + "/completion", data=json.dumps(body).encode(),
-                                 headers={"Content-Type": "application/json"})
+    req = urllib.request.Request(url + "/completion", data=json.dumps(body).encode(), headers=headers())
     sent = time.monotonic() - epoch
     events = []
     with urllib.request.urlopen(req, timeout=timeout) as r:

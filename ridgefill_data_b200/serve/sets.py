@@ -26,7 +26,7 @@ import time
 import urllib.request
 from pathlib import Path
 
-from .client import post_json
+from .client import headers, post_json
 
 
 class Endpoint:
@@ -53,7 +53,7 @@ class Endpoint:
     def first_token_s(self, body):
         """Seconds from sending a streamed request to its first chunk with text (the whole reply drained)."""
         req = urllib.request.Request(self.url + "/v1/completions", data=json.dumps(dict(body, stream=True)).encode(),
-                                     headers={"Content-Type": "application/json"})
+                                     headers=headers())
         t0 = time.perf_counter()
         first = None
         with urllib.request.urlopen(req, timeout=self.timeout) as r:
