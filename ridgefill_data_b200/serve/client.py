@@ -2,6 +2,9 @@
 
 * `timing`: TTFT of distinct prompts on a warm server: one short warm-up request, then each prompt once, with the
   client-side TTFT (send -> first token event) next to the server's own prompt time.
+* `load`: an open-loop load test: requests arrive as a Poisson process at a given rate for a given time, each with
+  a prompt length drawn from a range; the summary gives request and token throughput, TTFT and inter-token gaps
+  (p50 / p90 / p99), and the requests the server refused as busy (HTTP 503) or failed.
 * `mix`: a fixed-arrival concurrency mix. Background requests start decoding; at a planned time an injector sends a
   long prompt; every request's stream is recorded with arrival-relative timestamps. The summary gives the injector's
   TTFT and the background streams' inter-token gaps before, during and after the injector's prefill: what a long
@@ -203,11 +206,73 @@ def summarize(results):
         coalesced_tokens=sum(r["coalesced_tokens"] for r in results))
 
 
+# ------------------------------------------------------------------------------------------------ load
+def make_load(rate, duration_s, vocab, min_len=512, max_len=4096, predict=32, seed=0):
+    """Poisson arrivals at `rate` requests per second over duration_s, prompt lengths uniform in [min_len,
+    max_len], seeded uniform ids."""
+    g = np.random.default_rng(seed)
+    plan, t = [], float(g.exponential(1.0 / rate))
+    while t < duration_s:
+        n = int(g.integers(min_len, max_len + 1))
+        plan.append(dict(id=f"r{len(plan)}", arrival_s=t, predict=predict, ids=g.integers(0, vocab, n).tolist()))
+        t += float(g.exponential(1.0 / rate))
+    return plan
+
+
+def run_load(url, plan, mode="on", timeout=900):
+    """Send every planned request at its arrival time (streamed), return (per-request results, summary)."""
+    import urllib.error
+    out, refused, failed, threads = [], [], [], []
+    lock = threading.Lock()
+    epoch = time.monotonic() + 0.5
+
+    def one(item):
+        body = dict(prompt=item["ids"], n_predict=item["predict"], ignore_eos=True, temperature=0, top_k=1,
+                    ridgefill_mode=mode)
+        time.sleep(max(0.0, epoch + item["arrival_s"] - time.monotonic()))
+        try:
+            events, sent = stream(url, body, epoch, timeout)
+            m = token_metrics(events, item["predict"])
+            m.update(id=item["id"], n_prompt=len(item["ids"]), predict=item["predict"], sent=sent,
+                     ttft_s=m["first"] - sent)
+            with lock:
+                out.append(m)
+        except urllib.error.HTTPError as e:
+            with lock:
+                (refused if e.code == 503 else failed).append(dict(id=item["id"], code=e.code))
+        except Exception as e:
+            with lock:
+                failed.append(dict(id=item["id"], error=repr(e)))
+
+    for item in plan:
+        th = threading.Thread(target=one, args=(item,), daemon=True)
+        threads.append(th)
+        th.start()
+    for th in threads:
+        th.join(timeout)
+    return out, summarize_load(out, plan, refused, failed)
+
+
+def summarize_load(results, plan, refused=(), failed=()):
+    if results:
+        wall = max(r["last"] for r in results) - min(r["sent"] for r in results)
+    else:
+        wall = 0.0
+    tokens = sum(r["predict"] for r in results)
+    return dict(requests=len(plan), completed=len(results), refused_busy=len(refused), failed=len(failed),
+                offered_rate_rps=len(plan) / max(1e-9, plan[-1]["arrival_s"]) if plan else 0.0,
+                throughput_rps=len(results) / wall if wall > 0 else None,
+                throughput_tokens_per_s=tokens / wall if wall > 0 else None,
+                prompt_tokens_per_s=sum(r["n_prompt"] for r in results) / wall if wall > 0 else None,
+                ttft_s=distribution([r["ttft_s"] for r in results]),
+                itl_ms=distribution([g["ms"] for r in results for g in r["gaps"]]), workload_s=wall)
+
+
 def main(argv=None):
     import argparse
     ap = argparse.ArgumentParser(description="timing and concurrency-mix clients of the completion server")
     sub = ap.add_subparsers(dest="cmd", required=True)
-    for name in ("timing", "mix"):
+    for name in ("timing", "mix", "load"):
         p = sub.add_parser(name)
         p.add_argument("--url", default="http://127.0.0.1:8080")
         p.add_argument("--mode", default="on", help="the prompt's (injector's) ridgefill_mode")
@@ -224,11 +289,20 @@ def main(argv=None):
     m.add_argument("--injector-predict", type=int, default=8)
     m.add_argument("--inject-at", type=float, default=1.0)
     m.add_argument("--background-mode", default="off")
+    ld = sub.choices["load"]
+    ld.add_argument("--rate", type=float, default=1.0, help="requests per second (Poisson arrivals)")
+    ld.add_argument("--duration", type=float, default=60.0, help="seconds of arrivals")
+    ld.add_argument("--min-len", type=int, default=512)
+    ld.add_argument("--max-len", type=int, default=16384)
+    ld.add_argument("--predict", type=int, default=32)
     a = ap.parse_args(argv)
     vocab = int(get_json(a.url, "/props").get("vocab", 32000))
     g = np.random.default_rng(a.seed)
     if a.cmd == "timing":
         res = timing(a.url, [g.integers(0, vocab, a.length).tolist() for _ in range(a.prompts)], a.mode)
+    elif a.cmd == "load":
+        plan = make_load(a.rate, a.duration, vocab, a.min_len, a.max_len, a.predict, seed=a.seed)
+        _, res = run_load(a.url, plan, a.mode)
     else:
         plan = make_schedule(a.concurrency, vocab, a.background_len, a.background_predict, a.injector_len,
                              a.injector_predict, a.inject_at, seed=a.seed)

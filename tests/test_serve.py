@@ -184,6 +184,19 @@ def test_timing_and_mix_clients(server):
     json.dumps(summary)
 
 
+def test_open_loop_load_client(server):
+    """The Poisson load client: every planned request completes with its tokens, the summary's counts add up, and a
+    plan is the same for the same seed."""
+    url, _, _ = server
+    plan = C.make_load(rate=20.0, duration_s=0.5, vocab=CFG.vocab, min_len=16, max_len=48, predict=4, seed=3)
+    assert plan == C.make_load(rate=20.0, duration_s=0.5, vocab=CFG.vocab, min_len=16, max_len=48, predict=4, seed=3)
+    assert len(plan) >= 2 and all(16 <= len(p["ids"]) <= 48 for p in plan)
+    results, summary = C.run_load(url, plan, mode="on")
+    assert summary["completed"] == len(results) == len(plan) and summary["failed"] == summary["refused_busy"] == 0
+    assert summary["itl_ms"]["n"] == 3 * len(plan) and summary["throughput_tokens_per_s"] > 0
+    json.dumps(summary)
+
+
 def test_token_metrics_checks():
     ev = [dict(t=0.1, data=dict(tokens=[5], tokens_predicted=1)), dict(t=0.3, data=dict(tokens=[6, 7],
                                                                                           tokens_predicted=3)),
