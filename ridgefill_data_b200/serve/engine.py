@@ -24,13 +24,13 @@ llama.cpp server's `/completion` stream (kept alike so the 27B kit's clients rea
 """
 from __future__ import annotations
 
+import collections
 import itertools
+import logging
 import queue
 import threading
 import time
 from dataclasses import dataclass, field
-
-import logging
 
 import torch
 
@@ -41,6 +41,7 @@ from ..engine.prefill import finish, run_lower
 
 _log = logging.getLogger("ridgefill_data_b200.serve")
 
+LATENCY_WINDOW = 10000      # latency samples kept per /metrics summary
 MAX_SCORED_ROWS = 4096      # prompt positions a request can have scored (prompt_logprobs): the last ones
 
 
@@ -154,7 +155,10 @@ class Scheduler:
         self.stats = dict(requests=0, completed=0, errors=0, prompt_tokens=0, predicted_tokens=0,
                           filled_tokens=0, interleaved_rounds=0, decode_batches=0, graph_captures=0, graph_steps=0,
                           cancelled=0, refused_busy=0)
-        self.ttft_ms, self.prompt_ms = [], []
+        # latency samples for /metrics: quantiles over the last LATENCY_WINDOW, count and sum over all time
+        self.ttft_ms, self.prompt_ms, self.decode_round_ms = (collections.deque(maxlen=LATENCY_WINDOW)
+                                                              for _ in range(3))
+        self._lat_total = {k: [0, 0.0] for k in ("ttft_ms", "prompt_ms", "decode_round_ms")}
         self._lock = threading.Lock()
 
     # ---- control
@@ -285,11 +289,12 @@ class Scheduler:
             return
         now = time.perf_counter()
         req.cache, req.position, req.t_first, req.t_last = cache, n, now, now
-        self.prompt_ms.append(1e3 * (now - req.t_prefill0))
+        prompt_ms = 1e3 * (now - req.t_prefill0)
+        self._observe("prompt_ms", prompt_ms)
         if self.stats["interleaved_rounds"] == rounds0 and n >= self.sample_rows:   # a clean per-row cost sample
-            x = self.prompt_ms[-1] / (n * max(1, getattr(model, "n_layers", 1)))
+            x = prompt_ms / (n * max(1, getattr(model, "n_layers", 1)))
             self._row_layer_ms = x if self._row_layer_ms is None else 0.7 * self._row_layer_ms + 0.3 * x
-        self.ttft_ms.append(1e3 * (now - req.t_submit))
+        self._observe("ttft_ms", 1e3 * (now - req.t_submit))
         self.stats["prompt_tokens"] += n
         self.stats["filled_tokens"] += req.filled
         self._deliver(req, tok)
@@ -318,11 +323,19 @@ class Scheduler:
         saved = pool.owner if pool is not None else None
         if pool is not None:       # pages a decode step takes are released with the cache that holds them
             pool.owner = "decode"
+        t0 = time.perf_counter()
         try:
             self._decode_round_inner()
         finally:
             if pool is not None:
                 pool.owner = saved
+        self._observe("decode_round_ms", 1e3 * (time.perf_counter() - t0))
+
+    def _observe(self, name, ms):
+        getattr(self, name).append(ms)
+        tot = self._lat_total[name]
+        tot[0] += 1
+        tot[1] += ms
 
     def _graph_for(self, grp):
         """The decode graph of this group of requests (reused, or captured now), or None for an eager round."""
@@ -472,11 +485,12 @@ class Scheduler:
         pool = getattr(self.model, "kv_pool", None)
         if pool is not None:
             lines += ["# TYPE ridgefill_kv_pages_free gauge", f"ridgefill_kv_pages_free {pool.free_pages()}"]
-        for name, xs in (("ridgefill_ttft_ms", self.ttft_ms), ("ridgefill_prompt_ms", self.prompt_ms)):
-            xs = sorted(xs)
+        for key in ("ttft_ms", "prompt_ms", "decode_round_ms"):
+            name, xs = f"ridgefill_{key}", sorted(getattr(self, key))
             lines.append(f"# TYPE {name} summary")
             for q in (0.5, 0.9, 0.99):
                 v = xs[min(len(xs) - 1, int(q * len(xs)))] if xs else float("nan")
                 lines.append(f'{name}{{quantile="{q}"}} {v:.3f}')
-            lines += [f"{name}_count {len(xs)}", f"{name}_sum {sum(xs):.3f}"]
+            count, total = self._lat_total[key]
+            lines += [f"{name}_count {count}", f"{name}_sum {total:.3f}"]
         return "\n".join(lines) + "\n"

@@ -170,6 +170,7 @@ def test_http_completion(server):
         assert e.value.code == 400
     text = urllib.request.urlopen(url + "/metrics").read().decode()
     assert "ridgefill_requests_total" in text and 'ridgefill_ttft_ms{quantile="0.5"}' in text
+    assert "ridgefill_decode_round_ms_count" in text
 
 
 def test_timing_and_mix_clients(server):
