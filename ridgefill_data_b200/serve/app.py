@@ -153,6 +153,50 @@ def _prompt_logprobs(body):
     return k
 
 
+def _legacy_logprobs(body):
+    """OpenAI's completions `logprobs` (alternatives per position, 0-5 there; up to 20 here), or None."""
+    v = body.get("logprobs")
+    if v is None or v is False:
+        return None
+    if v is True:
+        return 0
+    try:
+        k = int(v)
+    except (TypeError, ValueError):
+        raise BadRequest("logprobs: an integer")
+    if not 0 <= k <= 20:
+        raise BadRequest("logprobs: 0 to 20 alternatives")
+    return k
+
+
+def legacy_logprobs(ids, scores, top, tokenizer=None):
+    """OpenAI's legacy completions logprobs of the echoed prompt: tokens, token_logprobs (None for the first position
+    and for positions without logits), top_logprobs and text_offset."""
+    ids = [int(t) for t in ids]
+    first, vals = scores
+
+    def piece(t):
+        if tokenizer is None:
+            return str(t)
+        return tokenizer.decode([t]).encode("utf-8", "replace").decode("utf-8")
+    tokens = [piece(t) for t in ids]
+    lps, tops, offsets, at = [None], [None], [], 0
+    for tok in tokens:
+        offsets.append(at)
+        at += len(tok)
+    for i in range(1, len(ids)):
+        if i < first:
+            lps.append(None)
+            tops.append(None)
+            continue
+        lp, _, alts = vals[i - first]
+        lps.append(float(lp))
+        d = {piece(a): float(alp) for a, alp in alts[:top]}
+        d[tokens[i]] = float(lp)
+        tops.append(d)
+    return dict(tokens=tokens, token_logprobs=lps, top_logprobs=tops, text_offset=offsets)
+
+
 def prompt_logprob_entries(ids, scores, tokenizer=None):
     """vLLM's prompt_logprobs list from the scheduler's (first scored position, [(logprob, rank, alternatives)])."""
     ids = [int(t) for t in ids]
@@ -224,11 +268,18 @@ def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
 
     async def openai_run(ids, body, arm, kind, http_req=None):
         """Shared core of /v1/completions and /v1/chat/completions."""
-        n_predict = int(body.get("max_tokens") or body.get("max_completion_tokens") or 16)
-        if n_predict < 1:
-            raise BadRequest("max_tokens must be at least 1")
+        mt = body.get("max_tokens", body.get("max_completion_tokens"))
+        n_predict = 16 if mt is None else int(mt)
         stops = _stops(body)
         plp = _prompt_logprobs(body) if kind == "text" else -1
+        echo = bool(body.get("echo")) and kind == "text"
+        legacy = _legacy_logprobs(body) if kind == "text" else None
+        if echo and body.get("stream"):
+            raise BadRequest("echo is served on non-streamed requests only")
+        if echo and legacy is not None:                # OpenAI's echo + logprobs: score the prompt as well
+            plp = max(plp, legacy)
+        if n_predict < 1 and not (n_predict == 0 and plp >= 0):
+            raise BadRequest("max_tokens must be at least 1 (0 only with echo + logprobs or prompt_logprobs)")
         try:
             req, q = submit(ids, n_predict, arm, prompt_logprobs=plp)
         except ServerBusy as e:
@@ -284,8 +335,12 @@ def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
                         prompt_filled_tokens=filled)
 
         def add_prompt_logprobs(choice, final):
-            if plp >= 0 and final is not None and "prompt_scores" in final:
+            if plp < 0 or final is None or "prompt_scores" not in final:
+                return
+            if _prompt_logprobs(body) >= 0:
                 choice["prompt_logprobs"] = prompt_logprob_entries(ids, final["prompt_scores"], tokenizer)
+            if echo and legacy is not None:
+                choice["logprobs"] = legacy_logprobs(ids, final["prompt_scores"], legacy, tokenizer)
 
         if body.get("stream"):
             async def events():
@@ -319,6 +374,9 @@ def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
             req.cancelled = True
             return bad("client disconnected", 499)
         text = "".join(out)
+        if echo:
+            prompt_text = tokenizer.decode(ids.tolist(), skip_special_tokens=False) if tokenizer is not None else ""
+            text = prompt_text.encode("utf-8", "replace").decode("utf-8") + text
         choice = (dict(index=0, message=dict(role="assistant", content=text), finish_reason=finish)
                   if kind == "chat" else dict(index=0, text=text, finish_reason=finish, logprobs=None))
         add_prompt_logprobs(choice, final)

@@ -176,8 +176,8 @@ class Scheduler:
             self._thread = None
 
     def submit(self, req: Request):
-        if req.n_predict < 1:
-            raise ValueError("n_predict must be at least 1")
+        if req.n_predict < 1 and not (req.n_predict == 0 and req.prompt_logprobs >= 0):
+            raise ValueError("n_predict must be at least 1 (0 only for a request that scores its prompt)")
         if req.ids.dim() != 1 or req.ids.numel() == 0:
             raise ValueError("the prompt must be a non-empty 1-D id sequence")
         limit = getattr(self.model, "max_positions", None)
@@ -297,6 +297,9 @@ class Scheduler:
         self._observe("ttft_ms", 1e3 * (now - req.t_submit))
         self.stats["prompt_tokens"] += n
         self.stats["filled_tokens"] += req.filled
+        if req.n_predict == 0:                         # a scoring request: the prompt's log-probs, no token
+            self._final(req)
+            return
         self._deliver(req, tok)
         if not self._done(req):
             self.active.append(req)

@@ -534,3 +534,28 @@ def test_api_key_guards_every_endpoint_but_health(setup):
     finally:
         srv.stop()
         sched.stop()
+
+
+def test_echo_logprobs_scoring_request(text_server):
+    """OpenAI's echo + logprobs with max_tokens 0 (what evaluation harnesses send for log-likelihoods): no token is
+    generated, the text is the prompt, and the legacy logprobs block holds every prompt token's teacher-forced
+    log-prob with its top alternatives."""
+    url, model, arms, tok = text_server
+    g = torch.Generator().manual_seed(41)
+    ids = torch.randint(20, CFG.vocab, (40,), generator=g)
+    r = C.post_json(url, "/v1/completions", dict(prompt=ids.tolist(), max_tokens=0, echo=True, logprobs=2,
+                                                 ridgefill_mode="off"))
+    ch = r["choices"][0]
+    assert r["usage"]["completion_tokens"] == 0 and ch["finish_reason"] == "length"
+    assert ch["text"] == tok.decode(ids.tolist(), skip_special_tokens=False).encode("utf-8", "replace").decode()
+    lp = ch["logprobs"]
+    assert len(lp["tokens"]) == len(lp["token_logprobs"]) == len(lp["top_logprobs"]) == 40
+    assert lp["token_logprobs"][0] is None and lp["top_logprobs"][0] is None
+    logits, _, _ = prefill(model, ids, arms["off"], keep=40)
+    ref = logits[:-1].double().log_softmax(-1)
+    for i in range(1, 40):
+        assert abs(lp["token_logprobs"][i] - float(ref[i - 1, ids[i]])) < 1e-4
+        assert lp["tokens"][i] in lp["top_logprobs"][i] and 1 <= len(lp["top_logprobs"][i]) <= 3
+    with pytest.raises(urllib.error.HTTPError) as e:
+        C.post_json(url, "/v1/completions", dict(prompt=ids.tolist(), max_tokens=0))
+    assert e.value.code == 400
