@@ -12,7 +12,9 @@ OpenAI-compatible (the API the c5 kit's client and the LongBench v2 runner speak
   POST /v1/completions       {"prompt": "text" | [ids], "max_tokens", "stream", "stop", "ridgefill_mode",
                               "prompt_logprobs": k (vLLM's field: the log-prob and rank of every prompt token given
                               its prefix, plus the k most likely tokens), "vllm_xargs": {"dyluhn_kva": "0" | "1",
-                              "dyluhn_kva_tail": T} (the c5 kit's per-request RidgeFill switch: off / on)}
+                              "dyluhn_kva_tail": T} (the c5 kit's per-request RidgeFill switch: off / on),
+                              "echo" + "logprobs": k (OpenAI's legacy log-probs of the echoed prompt; with
+                              max_tokens 0 a scoring request, as evaluation harnesses send for log-likelihoods)}
   POST /v1/chat/completions  {"messages": [...], "max_tokens", "stream", "stop", "ridgefill_mode"} (the tokenizer's
                              chat template renders the prompt)
   Responses carry choices[0].text / .message.content, finish_reason ("stop" | "length") and usage token counts
