@@ -2,6 +2,7 @@
 `/completion` (kept alike so the 27B kit's clients and schedules run unchanged), plus `/health`, `/props` and a
 Prometheus `/metrics`.
 
+POST /tokenize, /detokenize  text <-> ids with the server's tokenizer (llama.cpp's and vLLM's field names)
 POST /completion  {"prompt": [ids] | "text", "n_predict": 16, "stream": false, "ridgefill_mode": "on" | "off"
                    (or "ridgefill": bool), "ignore_eos": false, ...}; other llama.cpp sampling fields (temperature 0,
                    top_k 1, seed, cache_prompt false, id_slot) are accepted and must mean greedy decoding.
@@ -419,6 +420,32 @@ def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
             return await openai_run(ids, body, arm, "chat", http_req)
         except BadRequest as e:
             return bad(str(e))
+
+    @app.post("/tokenize")
+    def tokenize(body: dict):
+        """llama.cpp's {"content": text} or vLLM's {"prompt": text} -> {"tokens": [ids], "count": n}."""
+        text = body.get("content", body.get("prompt"))
+        if tokenizer is None:
+            return bad("tokenizing needs the server's --tokenizer")
+        if not isinstance(text, str):
+            return bad("content: a string")
+        from ..eval.text import encode
+        ids = encode(tokenizer, text)
+        if body.get("add_special", body.get("add_special_tokens", False)):
+            from ..eval.text import bos_ids
+            ids = bos_ids(tokenizer) + ids
+        return dict(tokens=ids, count=len(ids))
+
+    @app.post("/detokenize")
+    def detokenize(body: dict):
+        """{"tokens": [ids]} -> {"content": text, "prompt": text}."""
+        ids = body.get("tokens")
+        if tokenizer is None:
+            return bad("detokenizing needs the server's --tokenizer")
+        if not isinstance(ids, list) or not all(isinstance(t, int) for t in ids):
+            return bad("tokens: a list of token ids")
+        text = tokenizer.decode(ids, skip_special_tokens=False).encode("utf-8", "replace").decode("utf-8")
+        return dict(content=text, prompt=text)
 
     @app.get("/health")
     def health():

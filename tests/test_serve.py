@@ -559,3 +559,14 @@ def test_echo_logprobs_scoring_request(text_server):
     with pytest.raises(urllib.error.HTTPError) as e:
         C.post_json(url, "/v1/completions", dict(prompt=ids.tolist(), max_tokens=0))
     assert e.value.code == 400
+
+
+def test_tokenize_and_detokenize(text_server):
+    url, model, arms, tok = text_server
+    r = C.post_json(url, "/tokenize", dict(content="amber cloud"))
+    assert r["count"] == len(r["tokens"]) == len("amber cloud")
+    assert C.post_json(url, "/detokenize", dict(tokens=r["tokens"]))["content"] == "amber cloud"
+    assert C.post_json(url, "/tokenize", dict(prompt="ab", add_special=True))["tokens"][0] == tok.bos_token_id
+    with pytest.raises(urllib.error.HTTPError) as e:
+        C.post_json(url, "/detokenize", dict(tokens="x"))
+    assert e.value.code == 400
