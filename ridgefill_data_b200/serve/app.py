@@ -121,6 +121,11 @@ def _greedy_only(body):
     if float(body.get("temperature", 0) or 0) != 0 or int(body.get("top_k", 1) or 1) not in (1, -1) \
             or float(body.get("top_p", 1) or 1) != 1:
         raise BadRequest("only greedy decoding (temperature 0) is served")
+    if int(body.get("n", 1) or 1) != 1 or int(body.get("best_of", 1) or 1) != 1:
+        raise BadRequest("n / best_of: one greedy completion per request")
+    if float(body.get("presence_penalty", 0) or 0) != 0 or float(body.get("frequency_penalty", 0) or 0) != 0 \
+            or body.get("logit_bias"):
+        raise BadRequest("presence / frequency penalties and logit_bias are not served (greedy decoding)")
 
 
 def _mode(body, arms):

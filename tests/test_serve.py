@@ -556,9 +556,11 @@ def test_echo_logprobs_scoring_request(text_server):
     for i in range(1, 40):
         assert abs(lp["token_logprobs"][i] - float(ref[i - 1, ids[i]])) < 1e-4
         assert lp["tokens"][i] in lp["top_logprobs"][i] and 1 <= len(lp["top_logprobs"][i]) <= 3
-    with pytest.raises(urllib.error.HTTPError) as e:
-        C.post_json(url, "/v1/completions", dict(prompt=ids.tolist(), max_tokens=0))
-    assert e.value.code == 400
+    for bad in (dict(max_tokens=0), dict(max_tokens=2, n=2), dict(max_tokens=2, presence_penalty=0.5),
+                dict(max_tokens=2, logit_bias={"5": 1.0}), dict(max_tokens=0, echo=True, logprobs=1, stream=True)):
+        with pytest.raises(urllib.error.HTTPError) as e:
+            C.post_json(url, "/v1/completions", dict(bad, prompt=ids.tolist()))
+        assert e.value.code == 400
 
 
 def test_tokenize_and_detokenize(text_server):
