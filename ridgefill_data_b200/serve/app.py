@@ -10,7 +10,8 @@ POST /completion  {"prompt": [ids] | "text", "n_predict": 16, "stream": false, "
   stream=true  -> text/event-stream, one `data: {event}` per token and the final event (see serve/engine.py).
 OpenAI-compatible (the API the c5 kit's client and the LongBench v2 runner speak):
   GET  /v1/models
-  POST /v1/completions       {"prompt": "text" | [ids], "max_tokens", "stream", "stop", "ridgefill_mode",
+  POST /v1/completions       {"prompt": "text" | [ids] | a list of those (one choice each, non-streamed),
+                              "max_tokens", "stream", "stop", "ridgefill_mode",
                               "prompt_logprobs": k (vLLM's field: the log-prob and rank of every prompt token given
                               its prefix, plus the k most likely tokens), "vllm_xargs": {"dyluhn_kva": "0" | "1",
                               "dyluhn_kva_tail": T} (the c5 kit's per-request RidgeFill switch: off / on),
@@ -390,6 +391,25 @@ def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
         add_prompt_logprobs(choice, final)
         return dict(id=rid, object=obj, created=created, model=model_name, choices=[choice], usage=usage(final))
 
+    async def batch_run(prompts, body, arm, http_req):
+        """A list of prompts (texts or id lists): one request each, all submitted at once (the scheduler batches
+        their decode rounds), answered as one reply with choices in prompt order and summed usage."""
+        if body.get("stream"):
+            raise BadRequest("a list of prompts is served without stream")
+        all_ids = [parse_body(dict(prompt=p, n_predict=1, ridgefill_mode="x"), {"x": arm}, tokenizer)[0]
+                   for p in prompts]
+        results = await asyncio.gather(*(openai_run(ids, body, arm, "text", http_req) for ids in all_ids))
+        for r in results:
+            if not isinstance(r, dict):                 # an error reply of one prompt answers for the batch
+                return r
+        choices = []
+        for i, r in enumerate(results):
+            c = r["choices"][0]
+            c["index"] = i
+            choices.append(c)
+        usage = {k: sum(r["usage"][k] for r in results) for k in results[0]["usage"]}
+        return dict(results[0], choices=choices, usage=usage)
+
     @app.get("/v1/models")
     def models():
         return dict(object="list", data=[dict(id=model_name, object="model", owned_by="ridgefill-b200")])
@@ -400,8 +420,10 @@ def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
             _greedy_only(body)
             arm = _mode(body, arms)
             prompt = body.get("prompt")
-            if isinstance(prompt, list) and len(prompt) == 1 and isinstance(prompt[0], str):
+            if isinstance(prompt, list) and len(prompt) == 1 and isinstance(prompt[0], (str, list)):
                 prompt = prompt[0]
+            if isinstance(prompt, list) and prompt and all(isinstance(p, (str, list)) for p in prompt):
+                return await batch_run(prompt, body, arm, http_req)
             ids, _, _, _ = parse_body(dict(prompt=prompt, n_predict=1, ridgefill_mode="x"), {"x": arm}, tokenizer)
             return await openai_run(ids, body, arm, "text", http_req)
         except BadRequest as e:

@@ -572,3 +572,20 @@ def test_tokenize_and_detokenize(text_server):
     with pytest.raises(urllib.error.HTTPError) as e:
         C.post_json(url, "/detokenize", dict(tokens="x"))
     assert e.value.code == 400
+
+
+def test_a_list_of_prompts_is_one_reply(text_server):
+    """/v1/completions with several prompts (texts or id lists), as evaluation harnesses batch them: one choice per
+    prompt in order, each equal to that prompt's own request, and the usage summed."""
+    url, model, arms, tok = text_server
+    g = torch.Generator().manual_seed(43)
+    prompts = [torch.randint(20, CFG.vocab, (n,), generator=g).tolist() for n in (24, 31, 40)]
+    r = C.post_json(url, "/v1/completions", dict(prompt=prompts, max_tokens=3, ridgefill_mode="off"))
+    assert [c["index"] for c in r["choices"]] == [0, 1, 2]
+    for p, c in zip(prompts, r["choices"]):
+        one = C.post_json(url, "/v1/completions", dict(prompt=p, max_tokens=3, ridgefill_mode="off"))
+        assert c["text"] == one["choices"][0]["text"]
+    assert r["usage"]["prompt_tokens"] == 24 + 31 + 40 and r["usage"]["completion_tokens"] == 9
+    scored = C.post_json(url, "/v1/completions", dict(prompt=prompts[:2], max_tokens=0, echo=True, logprobs=0,
+                                                      ridgefill_mode="off"))
+    assert [len(c["logprobs"]["token_logprobs"]) for c in scored["choices"]] == [24, 31]
