@@ -178,9 +178,10 @@ def _legacy_logprobs(body):
     return k
 
 
-def legacy_logprobs(ids, scores, top, tokenizer=None):
-    """OpenAI's legacy completions logprobs of the echoed prompt: tokens, token_logprobs (None for the first position
-    and for positions without logits), top_logprobs and text_offset."""
+def legacy_logprobs(ids, scores, top, tokenizer=None, next_score=None):
+    """OpenAI's legacy completions logprobs of the echoed prompt (and of the generated token, next_score, when there
+    is one): tokens, token_logprobs (None for the first position and for positions without logits), top_logprobs and
+    text_offset."""
     ids = [int(t) for t in ids]
     first, vals = scores
 
@@ -202,6 +203,14 @@ def legacy_logprobs(ids, scores, top, tokenizer=None):
         lps.append(float(lp))
         d = {piece(a): float(alp) for a, alp in alts[:top]}
         d[tokens[i]] = float(lp)
+        tops.append(d)
+    if next_score is not None:
+        tok, lp, alts = next_score
+        offsets.append(at)
+        tokens.append(piece(tok))
+        lps.append(float(lp))
+        d = {piece(a): float(alp) for a, alp in alts[:top]}
+        d[tokens[-1]] = float(lp)
         tops.append(d)
     return dict(tokens=tokens, token_logprobs=lps, top_logprobs=tops, text_offset=offsets)
 
@@ -289,6 +298,8 @@ def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
             plp = max(plp, legacy)
         if n_predict < 1 and not (n_predict == 0 and plp >= 0):
             raise BadRequest("max_tokens must be at least 1 (0 only with echo + logprobs or prompt_logprobs)")
+        if echo and legacy is not None and n_predict > 1:
+            raise BadRequest("echo + logprobs: max_tokens 0 or 1 (log-probs of the prompt and the first token)")
         try:
             req, q = submit(ids, n_predict, arm, prompt_logprobs=plp)
         except ServerBusy as e:
@@ -349,7 +360,8 @@ def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
             if _prompt_logprobs(body) >= 0:
                 choice["prompt_logprobs"] = prompt_logprob_entries(ids, final["prompt_scores"], tokenizer)
             if echo and legacy is not None:
-                choice["logprobs"] = legacy_logprobs(ids, final["prompt_scores"], legacy, tokenizer)
+                choice["logprobs"] = legacy_logprobs(ids, final["prompt_scores"], legacy, tokenizer,
+                                                     final.get("next_score"))
 
         if body.get("stream"):
             async def events():

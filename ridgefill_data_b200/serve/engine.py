@@ -89,6 +89,15 @@ def score_prompt(logits, ids, top=0, chunk=256):
     return n - m, out
 
 
+def score_next(logits, top=0):
+    """(greedy token, its log-prob, [(id, logprob)] * top) of the last row: the first generated token's score."""
+    lp = logits[-1].float().log_softmax(-1)
+    tok = int(lp.argmax())
+    alts = lp.topk(top) if top > 0 else None
+    return (tok, float(lp[tok]),
+            list(zip(alts.indices.tolist(), alts.values.tolist())) if alts is not None else [])
+
+
 class ServerBusy(RuntimeError):
     """The waiting queue is full (max_waiting): the client should retry later."""
 
@@ -115,6 +124,7 @@ class Request:
     cancelled: bool = False
     prompt_logprobs: int = -1               # >= 0: score the prompt (that many top alternatives per position)
     prompt_scores: object = None            # (first scored position, [(logprob, rank, alternatives)])
+    next_score: object = None               # (first generated token, its logprob, alternatives) when scored
 
 
 class Scheduler:
@@ -274,6 +284,7 @@ class Scheduler:
             tok = int(D.check_finite(logits[-1], f"{req.rid} first token").argmax())
             if req.prompt_logprobs >= 0:
                 req.prompt_scores = score_prompt(logits, req.ids, req.prompt_logprobs)
+                req.next_score = score_next(logits, req.prompt_logprobs)
             del logits
         except Exception as e:                         # report, drop the request, keep serving
             err = e
@@ -470,6 +481,8 @@ class Scheduler:
                  "tokens_evaluated": n, "truncated": False, "id": req.rid, "timings": timings}
         if req.prompt_scores is not None:
             final["prompt_scores"] = req.prompt_scores
+            if req.produced:
+                final["next_score"] = req.next_score
         self._emit(req, final)
 
     # ---- metrics (Prometheus text exposition)

@@ -589,3 +589,28 @@ def test_a_list_of_prompts_is_one_reply(text_server):
     scored = C.post_json(url, "/v1/completions", dict(prompt=prompts[:2], max_tokens=0, echo=True, logprobs=0,
                                                       ridgefill_mode="off"))
     assert [len(c["logprobs"]["token_logprobs"]) for c in scored["choices"]] == [24, 31]
+
+
+def test_log_likelihood_request_as_evaluation_harnesses_send_it(text_server):
+    """The log-likelihood request of OpenAI-API evaluation harnesses: echo, logprobs 1, max_tokens 1; the block
+    covers the prompt and the one generated token, so summing token_logprobs[ctxlen:-1] gives the continuation's
+    log-likelihood, and the continuation is greedy exactly when each token's log-prob is its row's largest."""
+    url, model, arms, tok = text_server
+    g = torch.Generator().manual_seed(47)
+    ids = torch.randint(20, CFG.vocab, (36,), generator=g)
+    ctxlen = 30
+    r = C.post_json(url, "/v1/completions", dict(prompt=ids.tolist(), max_tokens=1, echo=True, logprobs=1,
+                                                 temperature=0, seed=1234, ridgefill_mode="off"))
+    lp = r["choices"][0]["logprobs"]
+    assert len(lp["token_logprobs"]) == 37                       # the prompt and the generated token
+    logits, _, _ = prefill(model, ids, arms["off"], keep=36)
+    ref = logits.double().log_softmax(-1)
+    want = sum(float(ref[i - 1, ids[i]]) for i in range(ctxlen, 36))
+    assert abs(sum(lp["token_logprobs"][ctxlen:-1]) - want) < 1e-3
+    greedy = all(int(ref[i - 1].argmax()) == int(ids[i]) for i in range(ctxlen, 36))
+    is_greedy = all(t == max(top.values()) for t, top in zip(lp["token_logprobs"][ctxlen:-1],
+                                                             lp["top_logprobs"][ctxlen:-1]))
+    assert is_greedy == greedy
+    assert lp["token_logprobs"][-1] == max(lp["top_logprobs"][-1].values())    # the generated token is greedy
+    with pytest.raises(urllib.error.HTTPError):
+        C.post_json(url, "/v1/completions", dict(prompt=ids.tolist(), max_tokens=2, echo=True, logprobs=1))
