@@ -98,3 +98,27 @@ def test_decode_kernel_shape_predicates():
     assert gdn_decode_supported(128, 128, 4)
     assert not gdn_decode_supported(64, 64, 4)
     assert not gdn_decode_supported(128, 128, 1)
+
+
+def test_decode_kernel_routing_rules():
+    """Which decode rows take the batched kernels (models/b200.py): the GDN step needs one GPU, head dims 128 and
+    fp32 contiguous states a prefill made; the attention needs one GPU and a supported head shape."""
+    from types import SimpleNamespace
+
+    import torch
+
+    from ridgefill_data_b200.models.b200 import _B200
+    cfg = SimpleNamespace(gdn_dk=128, gdn_dv=128, conv_k=4, rot_dim=64)
+    m = SimpleNamespace(cfg=cfg, tp=None, nk=2, nv=6, conv_dim=2 * 2 * 128 + 6 * 128, head_dim=256, n_heads=24,
+                        n_kv=4)
+    ok = dict(conv=torch.zeros(3, m.conv_dim, dtype=torch.bfloat16), rec=torch.zeros(6, 128, 128))
+    assert _B200._gdn_decode_ok(m, [ok, ok])
+    assert not _B200._gdn_decode_ok(m, [ok, dict(ok, rec=ok["rec"].half())])          # fp32 states only
+    assert not _B200._gdn_decode_ok(m, [dict(ok, conv=None)])                          # no prefill yet
+    assert not _B200._gdn_decode_ok(m, [dict(ok, rec=ok["rec"].transpose(1, 2))])      # contiguous states
+    assert not _B200._gdn_decode_ok(SimpleNamespace(**dict(vars(m), tp=object())), [ok])   # TP ranks
+    assert not _B200._gdn_decode_ok(SimpleNamespace(**dict(vars(m), cfg=SimpleNamespace(**dict(vars(cfg),
+                                                                                         gdn_dk=64)))), [ok])
+    assert _B200._attn_decode_ok(m)
+    assert not _B200._attn_decode_ok(SimpleNamespace(**dict(vars(m), tp=object())))
+    assert not _B200._attn_decode_ok(SimpleNamespace(**dict(vars(m), n_heads=12)))    # 3 query heads per KV head
