@@ -78,6 +78,11 @@ def _rank(rank, world, port, out):
             streams.append((evs, done))
         for _, done in streams:
             done.wait(60)
+        scored, sdone = [], threading.Event()            # a scoring request: prompt log-probs, no token
+        sched.submit(Request(ids=uniform_prompt(30, CFG.vocab, seed=8), n_predict=0, arm=arms["off"],
+                             prompt_logprobs=1, emit=lambda ev: (scored.append(ev), sdone.set() if ev.get("stop")
+                                                                 else None)))
+        sdone.wait(60)
         evs, done = [], threading.Event()
         sched.submit(Request(ids=uniform_prompt(20, CFG.vocab, seed=9), n_predict=2, arm=Arm("exact"),
                              emit=lambda ev: (evs.append(ev), done.set() if ev.get("stop") else None), ignore_eos=True))
@@ -85,7 +90,8 @@ def _rank(rank, world, port, out):
         refused = evs[-1].get("error") if evs else None
         sched.stop()
         toks = [[ev["tokens"][0] for ev in e if ev.get("tokens")] for e, _ in streams]
-        out.put((0, dict(toks=toks, log=sent, calls=len(calls), refused=refused)))
+        first, vals = scored[-1]["prompt_scores"]
+        out.put((0, dict(toks=toks, log=sent, calls=len(calls), refused=refused, scored=(first, len(vals)))))
     else:
         log = []
         serve_worker(model, ls, log=log)
@@ -113,6 +119,7 @@ def test_lockstep_serving_mirrors_every_model_call():
     assert res[1]["log"] == res[0]["log"]
     assert res[0]["log"][-1] == ("stop", None)
     ops = [op for op, _ in res[0]["log"]]
-    assert ops.count("prefill") == len(JOBS) and ops.count("release") == len(JOBS) and "decode" in ops
+    assert ops.count("prefill") == len(JOBS) + 1 and ops.count("release") == len(JOBS) + 1 and "decode" in ops
+    assert res[0]["scored"] == (1, 29)                   # every position after the first, exact
     assert res[0]["calls"] == res[1]["calls"] > 0                 # every model call met its peer's collective
     assert res[0]["refused"] and "not one of the server's arms" in res[0]["refused"]
