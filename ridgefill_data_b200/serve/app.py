@@ -488,6 +488,8 @@ def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
 
     @app.get("/health")
     def health():
+        if getattr(scheduler, "failed", None):            # out of service: a load balancer should drop us
+            return JSONResponse({"status": "error", "error": scheduler.failed, **scheduler.load}, status_code=503)
         return {"status": "ok", **scheduler.load}
 
     @app.get("/props")

@@ -153,6 +153,7 @@ class Scheduler:
         self._seen_key = None        # the previous round's set: a graph is captured once a set repeats
         self.max_active = int(max_active)
         self.max_waiting = int(max_waiting)      # > 0: requests refused (ServerBusy) while this many wait
+        self.failed = None                       # why the worker stopped serving (a broken lockstep group)
         self.max_batch = int(max_batch)
         self.waiting = queue.Queue()
         self.active = []
@@ -197,6 +198,8 @@ class Scheduler:
         vocab = getattr(getattr(self.model, "cfg", None), "vocab", None)
         if vocab and (int(req.ids.min()) < 0 or int(req.ids.max()) >= vocab):
             raise ValueError(f"prompt ids outside the vocabulary [0, {vocab})")
+        if self.failed is not None:
+            raise ServerBusy(f"the server stopped: {self.failed}")
         if self.max_waiting > 0 and self.waiting.qsize() >= self.max_waiting:
             with self._lock:
                 self.stats["refused_busy"] += 1
@@ -215,6 +218,30 @@ class Scheduler:
 
     # ---- worker
     def _loop(self):
+        try:
+            self._serve()
+        except Exception as e:          # a broken lockstep group (a rank gone): fail every request, serve no more
+            self._fail(e)
+            return
+        if self.lockstep is not None:
+            self.lockstep.command("stop")
+
+    def _fail(self, err):
+        self.failed = f"{type(err).__name__}: {err}"
+        _log.error("scheduler stopped: %s", self.failed)
+        reqs = list(self.active)
+        self.active = []
+        while True:
+            try:
+                reqs.append(self.waiting.get_nowait())
+            except queue.Empty:
+                break
+        for req in reqs:
+            with self._lock:
+                self.stats["errors"] += 1
+            self._emit(req, {"error": f"the server stopped: {self.failed}", "stop": True})
+
+    def _serve(self):
         while not self._stop.is_set():
             started = False
             if len(self.active) < self.max_active:
@@ -234,8 +261,6 @@ class Scheduler:
             elif not started:
                 self._wake.wait(0.05)
                 self._wake.clear()
-        if self.lockstep is not None:
-            self.lockstep.command("stop")
 
     def period_for(self, rows):
         """Prefill layers between decode rounds for a prompt of `rows` tokens."""

@@ -614,3 +614,43 @@ def test_log_likelihood_request_as_evaluation_harnesses_send_it(text_server):
     assert lp["token_logprobs"][-1] == max(lp["top_logprobs"][-1].values())    # the generated token is greedy
     with pytest.raises(urllib.error.HTTPError):
         C.post_json(url, "/v1/completions", dict(prompt=ids.tolist(), max_tokens=2, echo=True, logprobs=1))
+
+
+def test_a_broken_lockstep_group_fails_requests_and_health(setup):
+    """When the lockstep group breaks (a collective raises: a rank is gone), the scheduler fails the running and
+    waiting requests with an error, refuses new ones, and /health answers 503."""
+    from ridgefill_data_b200.serve.engine import ServerBusy
+
+    class Broken:
+        arms = None
+
+        def __init__(self, arms):
+            self.arms = arms
+
+        def key_of(self, arm):
+            return next(k for k, a in self.arms.items() if a is arm)
+
+        def command(self, *cmd):
+            if cmd[0] == "decode":
+                raise RuntimeError("gloo: connection closed by peer")
+
+        def agree(self, ok):
+            return ok
+    model, arms = setup
+    sched = Scheduler(model, lockstep=Broken(arms)).start()
+    srv = Server(create_app(sched, arms, props=dict(vocab=CFG.vocab)), port=0).start()
+    url = f"http://127.0.0.1:{srv.port}"
+    try:
+        evs, done = [], threading.Event()
+        sched.submit(Request(ids=uniform_prompt(20, CFG.vocab, seed=5), n_predict=5, arm=arms["off"],
+                             emit=lambda e: (evs.append(e), e.get("stop") and done.set())))
+        assert done.wait(60) and "error" in evs[-1] and "gloo" in evs[-1]["error"]
+        assert sched.failed is not None
+        with pytest.raises(ServerBusy):
+            sched.submit(Request(ids=uniform_prompt(20, CFG.vocab, seed=6), n_predict=1, arm=arms["off"], emit=print))
+        with pytest.raises(urllib.error.HTTPError) as e:
+            C.get_json(url, "/health")
+        assert e.value.code == 503
+    finally:
+        srv.stop()
+        sched.stop()
