@@ -154,6 +154,7 @@ class Scheduler:
         self.max_active = int(max_active)
         self.max_waiting = int(max_waiting)      # > 0: requests refused (ServerBusy) while this many wait
         self.failed = None                       # why the worker stopped serving (a broken lockstep group)
+        self._held = None                        # the queue's head while the K/V pool cannot hold it yet
         self.max_batch = int(max_batch)
         self.waiting = queue.Queue()
         self.active = []
@@ -214,7 +215,7 @@ class Scheduler:
 
     @property
     def load(self):
-        return dict(waiting=self.waiting.qsize(), active=len(self.active))
+        return dict(waiting=self.waiting.qsize() + (self._held is not None), active=len(self.active))
 
     # ---- worker
     def _loop(self):
@@ -229,8 +230,8 @@ class Scheduler:
     def _fail(self, err):
         self.failed = f"{type(err).__name__}: {err}"
         _log.error("scheduler stopped: %s", self.failed)
-        reqs = list(self.active)
-        self.active = []
+        reqs = list(self.active) + ([self._held] if self._held is not None else [])
+        self.active, self._held = [], None
         while True:
             try:
                 reqs.append(self.waiting.get_nowait())
@@ -241,18 +242,57 @@ class Scheduler:
                 self.stats["errors"] += 1
             self._emit(req, {"error": f"the server stopped: {self.failed}", "stop": True})
 
+    def _admission(self, req):
+        """"ok" when the paged K/V pool (if any) can hold the request's rows for its whole life on top of what the
+        running requests will still take, "wait" when it can once some of them end, "never" when the pool is too
+        small for it."""
+        pool = getattr(self.model, "kv_pool", None)
+        if pool is None:
+            return "ok"
+        ps, layer = pool.page_size, pool.layers[0]
+        need = -(-(int(req.ids.numel()) + req.n_predict) // ps)
+        if need > pool.pages:
+            return "never"
+        growth = 0                     # pages the running requests will still take as they decode
+        for r in self.active:
+            final = -(-(r.position + max(0, r.n_predict - len(r.produced))) // ps)
+            have = len((r.cache[layer] if r.cache else {}).get("pages", []))
+            growth += max(0, final - have)
+        return "ok" if pool.free_pages(layer) - growth >= need else "wait"
+
+    def _next_request(self):
+        """The request to prefill now, or None: the queue's head unless the K/V pool cannot hold it yet (it then
+        stays at the head, ahead of later arrivals, until running requests end)."""
+        req = self._held
+        self._held = None
+        if req is None:
+            try:
+                req = self.waiting.get_nowait()
+            except queue.Empty:
+                return None
+        if req.cancelled:                            # its client left while it waited: never prefilled
+            with self._lock:
+                self.stats["cancelled"] += 1
+            return None
+        verdict = self._admission(req)
+        if verdict == "wait" and self.active:
+            self._held = req
+            return None
+        if verdict != "ok":
+            pool = self.model.kv_pool
+            with self._lock:
+                self.stats["errors"] += 1
+            why = (f"more K/V pages than the pool's {pool.pages} x {pool.page_size} rows" if verdict == "never" else
+                   "more K/V pages than the pool has free with nothing else running")
+            self._emit(req, {"error": f"the prompt and its tokens need {why}", "stop": True})
+            return None
+        return req
+
     def _serve(self):
         while not self._stop.is_set():
             started = False
             if len(self.active) < self.max_active:
-                try:
-                    req = self.waiting.get_nowait()
-                except queue.Empty:
-                    req = None
-                if req is not None and req.cancelled:   # its client left while it waited: never prefilled
-                    with self._lock:
-                        self.stats["cancelled"] += 1
-                    req = None
+                req = self._next_request()
                 if req is not None:
                     started = True
                     self._prefill(req)

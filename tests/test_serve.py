@@ -654,3 +654,34 @@ def test_a_broken_lockstep_group_fails_requests_and_health(setup):
     finally:
         srv.stop()
         sched.stop()
+
+
+def test_kv_pool_admission_holds_a_request_until_pages_free(setup):
+    """With a paged K/V pool, a request whose rows (prompt + tokens) would not fit beside the running requests'
+    remaining growth waits at the head of the queue and starts once they end; one larger than the pool is refused.
+    (A stand-in pool: the torch model keeps its own caches, so the free count stays what the pool reports.)"""
+    from types import SimpleNamespace
+    model, arms = setup
+    pool = SimpleNamespace(page_size=16, pages=6, layers=[0], free_pages=lambda layer=None: 5, owner=None,
+                           release=lambda cache: None, release_owner=lambda owner: None)
+    model.kv_pool = pool
+    try:
+        sched = Scheduler(model, interleave=0).start()
+        runs = []
+        for j, (n, pred) in enumerate(((40, 8), (36, 8), (200, 4))):     # 3 pages, 3 pages, 13 pages
+            evs, done = [], threading.Event()
+            sched.submit(Request(ids=uniform_prompt(n, CFG.vocab, seed=50 + j), n_predict=pred, arm=arms["off"],
+                                 ignore_eos=True, emit=lambda e, evs=evs, done=done: (evs.append(e),
+                                                                                      e.get("stop") and done.set())))
+            runs.append((evs, done))
+        for _, done in runs:
+            assert done.wait(60)
+        first, second, big = (evs[-1] for evs, _ in runs)
+        assert first["tokens_predicted"] == second["tokens_predicted"] == 8
+        assert "pool" in big["error"]
+        # the second waited for the whole first request (its prefill and its 8 tokens) before its own prefill
+        lived = first["timings"]["prompt_ms"] + first["timings"]["predicted_ms"]
+        assert second["timings"]["queue_ms"] >= 0.9 * lived
+        sched.stop()
+    finally:
+        model.kv_pool = None
