@@ -276,10 +276,11 @@ def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
         return JSONResponse({"error": {"code": code, "message": msg, "type": "invalid_request_error"}},
                             status_code=code)
 
-    def submit(ids, n_predict, arm, ignore_eos=False, prompt_logprobs=-1):
+    def submit(ids, n_predict, arm, ignore_eos=False, prompt_logprobs=-1, stop_ids=()):
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
         req = Request(ids=ids, n_predict=n_predict, arm=arm, ignore_eos=ignore_eos, prompt_logprobs=prompt_logprobs,
+                      stop_ids=frozenset(int(t) for t in stop_ids),
                       emit=lambda ev: loop.call_soon_threadsafe(q.put_nowait, ev))
         scheduler.submit(req)
         return req, q
@@ -300,8 +301,11 @@ def create_app(scheduler, arms, tokenizer=None, props=None, api_key=None):
             raise BadRequest("max_tokens must be at least 1 (0 only with echo + logprobs or prompt_logprobs)")
         if echo and legacy is not None and n_predict > 1:
             raise BadRequest("echo + logprobs: max_tokens 0 or 1 (log-probs of the prompt and the first token)")
+        stop_ids = body.get("stop_token_ids") or []
+        if not isinstance(stop_ids, list) or not all(isinstance(t, int) for t in stop_ids):
+            raise BadRequest("stop_token_ids: a list of token ids")
         try:
-            req, q = submit(ids, n_predict, arm, prompt_logprobs=plp)
+            req, q = submit(ids, n_predict, arm, prompt_logprobs=plp, stop_ids=stop_ids)
         except ServerBusy as e:
             return bad(str(e), 503)
         except ValueError as e:

@@ -123,6 +123,7 @@ class Request:
     filled: int = 0
     cancelled: bool = False
     prompt_logprobs: int = -1               # >= 0: score the prompt (that many top alternatives per position)
+    stop_ids: frozenset = frozenset()       # token ids that end this request (beside the server's eos ids)
     prompt_scores: object = None            # (first scored position, [(logprob, rank, alternatives)])
     next_score: object = None               # (first generated token, its logprob, alternatives) when scored
 
@@ -391,7 +392,7 @@ class Scheduler:
 
     def _done(self, req):
         return (req.cancelled or len(req.produced) >= req.n_predict
-                or (not req.ignore_eos and req.tok in self.eos))
+                or (not req.ignore_eos and req.tok in self.eos) or req.tok in req.stop_ids)
 
     @torch.no_grad()
     def _decode_round(self):
@@ -522,7 +523,7 @@ class Scheduler:
         prompt_ms = 1e3 * (req.t_first - req.t_prefill0)
         pred = len(req.produced)
         pred_ms = 1e3 * (req.t_last - req.t_first)
-        stop_type = "eos" if (req.tok in self.eos and not req.ignore_eos) else "limit"
+        stop_type = ("eos" if (req.tok in self.eos and not req.ignore_eos) or req.tok in req.stop_ids else "limit")
         arm = req.arm
         timings = dict(prompt_n=n, prompt_ms=round(prompt_ms, 3),
                        prompt_per_second=round(n / max(prompt_ms, 1e-9) * 1e3, 3),

@@ -685,3 +685,14 @@ def test_kv_pool_admission_holds_a_request_until_pages_free(setup):
         sched.stop()
     finally:
         model.kv_pool = None
+
+
+def test_stop_token_ids_end_a_completion(text_server):
+    """vLLM's stop_token_ids: the completion ends at the first generated id in the list (finish_reason "stop")."""
+    url, model, arms, tok = text_server
+    ids = uniform_prompt(30, CFG.vocab, seed=61)
+    want = _expected(model, arms["off"], ids, 6)
+    r = C.post_json(url, "/v1/completions", dict(prompt=ids.tolist(), max_tokens=6, ridgefill_mode="off",
+                                                 stop_token_ids=[want[2]]))
+    assert r["usage"]["completion_tokens"] == want.index(want[2]) + 1
+    assert r["choices"][0]["finish_reason"] == "stop"
